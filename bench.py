@@ -1,0 +1,469 @@
+"""Benchmark of the B200 featurization hot path (BASELINE.json metric: featurization fwd+bwd Msamples/s at 65536
+rays; one sample = one interval x one of the 6 hexagonal multisamples).
+
+A step is one training iteration's featurization of config 2 (paper shape): the forward of the two proposal levels
+(64 intervals per ray, fused density MLP, fp32 features) and of the NeRF level (32 intervals, packed bf16 features and
+NeRF-input tail), then the NeRF-level backward (bf16 upstream gradients -> fp32/fp16 grid gradients) and the two
+proposal-level backwards (MLP recomputation, grid and MLP parameter gradients), in the order of the reference's
+Renderer.render_rays_training / Trainer.compute_gradients. Inputs are seeded synthetic data of config 2's shapes (the
+reference's Mip-NeRF 360 scenes are not available). With --gpus N (one process per GPU, torchrun), every rank
+featurizes its own 65536 rays (weak scaling) and the grid and MLP gradients are all-reduced over NCCL, the
+data-parallel exchange of a training step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / 'fused-zipnerf_b200'))
+
+import torch  # noqa: E402
+
+N_MULTISAMPLES = 6
+METRIC = 'featurization fwd+bwd Msamples/s at 65536 rays'
+UNIT = 'Msamples/s'
+GRAD_SCALE = 1048576.0
+
+
+def algorithmic_bytes(kind: str, n_levels: int, n_features: int, n_out: int, n_fp32_levels: int = 0) -> int:
+    """Algorithmic HBM bytes per interval of each kernel: every one of the 48 corner lookups (6 multisamples x 8
+    corners, before merging) of every level reads (or atomically updates) one table row, plus the interval's own
+    inputs and outputs."""
+    row = 4 * n_features
+    if kind == 'forward_proposal':
+        return 48 * row * n_levels + 4 + 4 + 4 * n_out                # gathers, tdist, raw density, fp32 features
+    if kind == 'forward_nerf':
+        return 48 * row * n_levels + 4 + 2 * ((n_out + 7) // 8 * 8) + 2 * 32  # gathers, tdist, bf16 features, input tail
+    if kind == 'backward_nerf':
+        return 2 * n_out + 4 + 48 * (row * n_fp32_levels + 2 * n_features * (n_levels - n_fp32_levels))
+    if kind == 'backward_proposal':
+        return 4 * n_out + 4 + 4 + 48 * row * n_levels
+    raise ValueError(kind)
+
+
+def measured_peaks() -> dict:
+    path = REPO / 'MEASURED_PEAKS.json'
+    if path.exists():
+        return json.loads(path.read_text()) | {'source': 'measured'}
+    return {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0, 'source': 'fallback'}
+
+
+def profiled_traffic() -> dict:
+    """DRAM bytes per launch of each kernel from the committed ncu summary (profiles/traffic.txt: 'kernel bytes')."""
+    path = REPO / 'profiles' / 'traffic.txt'
+    out = {}
+    if path.exists():
+        for line in path.read_text().splitlines():
+            parts = line.split()
+            if len(parts) == 2 and not line.startswith('#'):
+                out[parts[0]] = float(parts[1])
+    return out
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+
+    FIELDS = ['clocks.sm', 'clocks.max.sm', 'power.draw', 'clocks_event_reasons.active', 'clocks_event_reasons.hw_slowdown',
+              'clocks_event_reasons.hw_thermal_slowdown', 'clocks_event_reasons.sw_thermal_slowdown', 'clocks_event_reasons.sw_power_cap']
+
+    def __init__(self, device_index: int) -> None:
+        self.device_index = device_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.device_index}', f'--query-gpu={",".join(self.FIELDS)}',
+                                          '--format=csv,noheader,nounits', '-lms', '200'], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc) -> None:
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, sm_max, reasons = [], [], set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(',')]
+            if len(parts) != len(self.FIELDS):
+                continue
+            try:
+                sm.append(float(parts[0]))
+                sm_max.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, value in zip(names, parts[4:]):
+                if value.lower().startswith('active'):
+                    reasons.add(name)
+        if not sm:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': [], 'samples': 0}
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': max(sm_max), 'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+class Step:
+    """One featurization fwd+bwd step of a config 2 workload on one GPU, through the PyTorch binding (the
+    reference's API). Buffers are allocated once; inputs can be refreshed from pinned host copies (e2e)."""
+
+    def __init__(self, workload, device) -> None:
+        import ZipNeRFCudaBackend as backend
+        from zipnerf_b200 import workloads as wl_mod
+        self.device = device
+        self.wl = workload.to(device)
+        wl = self.wl
+        self.props, self.nerf = wl.levels[:-1], wl.levels[-1]
+        self.featurizers = [backend.Featurizer(l.level, l.sizes, l.entries, l.n_features, l.mlp_width) for l in wl.levels]
+        R = wl.n_rays
+        g = torch.Generator(device='cpu').manual_seed(1234)
+        self.empty = torch.empty(0, device=device)
+        self.prop_out, self.prop_grads = [], []
+        for lvl, f in zip(self.props, self.featurizers):
+            n = R * lvl.n_intervals
+            self.prop_out.append({'raw': torch.empty(R, lvl.n_intervals, device=device),
+                                  'features': torch.empty(n, lvl.n_output_features, device=device),
+                                  'grad_raw': (torch.randn(R, lvl.n_intervals, generator=g) * 1e-3).to(device)})
+            W = lvl.mlp_width
+            self.prop_grads.append({'table': torch.zeros(lvl.table.numel(), device=device), 'w0': torch.zeros(W, lvl.n_output_features, device=device),
+                                    'b0': torch.zeros(W, device=device), 'w1': torch.zeros(W, device=device), 'b1': torch.zeros(1, device=device)})
+        n = R * self.nerf.n_intervals
+        width = wl_mod.nerf_feature_width(self.nerf.n_output_features)
+        fn = self.featurizers[-1]
+        split = fn.n_fp32_grad_rows
+        F = self.nerf.n_features
+        self.nerf_out = {'features': torch.empty(n, width, device=device, dtype=torch.bfloat16),
+                         'inputs': torch.zeros(n, wl_mod.NERF_INPUTS_WIDTH, device=device, dtype=torch.bfloat16),
+                         'grad': (torch.randn(n, width, generator=g) * 1e-6).bfloat16().to(device)}
+        self.nerf_grads = {'g32': torch.zeros(split * F, device=device),
+                           'g16': torch.zeros((sum(self.nerf.entries) - split) * F, device=device, dtype=torch.float16)}
+        self.samples_per_step = wl.n_intervals_total * N_MULTISAMPLES
+        self.kernel_names = ['forward_proposal', 'forward_proposal', 'forward_nerf', 'backward_nerf', 'backward_proposal', 'backward_proposal']
+        self.launches_per_step = len(self.kernel_names)
+
+    def grad_buffers(self) -> list:
+        out = [self.nerf_grads['g32'], self.nerf_grads['g16']]
+        for grads in self.prop_grads:
+            out += [grads['table'], grads['w0'], grads['b0'], grads['w1'], grads['b1']]
+        return out
+
+    def input_buffers(self) -> list:
+        wl = self.wl
+        out = [wl.origins, wl.directions, wl.radii, wl.encoded_directions, self.nerf_out['grad']]
+        for lvl, po in zip(wl.levels, self.prop_out + [None]):
+            out.append(lvl.tdist)
+            if po is not None:
+                out.append(po['grad_raw'])
+        return out
+
+    def run(self, events=None) -> None:
+        """One step; events (list of (start, end) CUDA event pairs per kernel) are recorded if given."""
+        wl, seed, e = self.wl, self.wl.pattern_seed, self.empty
+        rays = (wl.origins, wl.directions, wl.radii)
+        k = 0
+
+        def mark(i, which):
+            if events is not None:
+                events[i][which].record()
+
+        for lvl, f, po in zip(self.props, self.featurizers, self.prop_out):
+            mark(k, 0)
+            f.forward(*rays, lvl.tdist, seed, False, lvl.table, lvl.scale_magnitudes, *lvl.mlp, po['raw'], po['features'], e, e, e)
+            mark(k, 1)
+            k += 1
+        nerf, fn = self.nerf, self.featurizers[-1]
+        mark(k, 0)
+        fn.forward(*rays, nerf.tdist, seed, False, nerf.table, nerf.scale_magnitudes, e, e, e, e, e, e, self.nerf_out['features'],
+                   wl.encoded_directions, self.nerf_out['inputs'])
+        mark(k, 1)
+        k += 1
+        mark(k, 0)
+        fn.backward(*rays, nerf.tdist, seed, self.nerf_out['grad'][:, :fn.n_output_features], self.nerf_grads['g32'], self.nerf_grads['g16'])
+        mark(k, 1)
+        k += 1
+        for lvl, f, po, pg in zip(self.props, self.featurizers, self.prop_out, self.prop_grads):
+            mark(k, 0)
+            f.backward_mlp(*rays, lvl.tdist, seed, po['features'], po['grad_raw'], *lvl.mlp[:3], pg['table'], pg['w0'], pg['b0'], pg['w1'], pg['b1'])
+            mark(k, 1)
+            k += 1
+
+    def kernel_bytes(self) -> list:
+        out = []
+        for lvl in self.props:
+            out.append(algorithmic_bytes('forward_proposal', lvl.n_levels, lvl.n_features, lvl.n_output_features) * self.wl.n_rays * lvl.n_intervals)
+        nerf, fn = self.nerf, self.featurizers[-1]
+        n_fp32 = sum(1 for e in nerf.entries if e < (1 << 20))
+        n = self.wl.n_rays * nerf.n_intervals
+        out.append(algorithmic_bytes('forward_nerf', nerf.n_levels, nerf.n_features, nerf.n_output_features) * n)
+        out.append(algorithmic_bytes('backward_nerf', nerf.n_levels, nerf.n_features, nerf.n_output_features, n_fp32) * n)
+        for lvl in self.props:
+            out.append(algorithmic_bytes('backward_proposal', lvl.n_levels, lvl.n_features, lvl.n_output_features) * self.wl.n_rays * lvl.n_intervals)
+        return out
+
+
+def init_distributed(n_gpus: int):
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    if world != n_gpus and world > 1:
+        raise SystemExit(f'--gpus {n_gpus} but WORLD_SIZE={world}')
+    return world, rank, local
+
+
+class CpuBaseline:
+    """The reference's own featurization code compiled for the host (oracle/_ref, where built), else the C oracle,
+    on a bounded ray sample of config 2 (fwd+bwd of all three levels, gradient buffers allocated up front)."""
+
+    def __init__(self, n_rays: int, threads: int) -> None:
+        self.n_rays, self.threads = n_rays, threads
+        self.prepared = None
+
+    def run(self, repeats: int = 1) -> dict:
+        """Times `repeats` passes; samples/s scaled to Msamples/s."""
+        if self.prepared is None:
+            self.prepared = _prepare_cpu_baseline(self.n_rays)
+        return _time_cpu_baseline(self.prepared, self.n_rays, self.threads, repeats)
+
+
+def _prepare_cpu_baseline(n_rays: int):
+    import numpy as np
+    from oracle.zf_oracle import GridSpec, Oracle, RefCpu
+    from zipnerf_b200 import workloads
+    kind = 'reference' if RefCpu.available() else 'port'
+    checker = RefCpu() if kind == 'reference' else Oracle()
+    wl = workloads.config2(n_rays=n_rays, seed=1)
+    rays = [x.numpy() for x in (wl.origins, wl.directions, wl.radii)]
+    g = np.random.default_rng(0)
+    levels = []
+    for lvl in wl.levels:
+        grid = GridSpec(lvl.level, lvl.sizes, lvl.entries, lvl.n_features, lvl.mlp_width)
+        n = n_rays * lvl.n_intervals
+        entry = {'grid': grid, 'tdist': lvl.tdist.numpy(), 'table': lvl.table.numpy(), 'mags': lvl.scale_magnitudes.numpy()}
+        if lvl.mlp_width > 0:
+            W, n_out = lvl.mlp_width, lvl.n_output_features
+            entry['mlp'] = [m.numpy() for m in lvl.mlp]
+            entry['grad_raw'] = (g.standard_normal((n_rays, lvl.n_intervals)) * 1e-3).astype(np.float32)
+            entry['grads'] = {'grad_table': np.zeros(grid.n_rows, np.float32), 'grad_w0': np.zeros((W, n_out), np.float32),
+                              'grad_b0': np.zeros(W, np.float32), 'grad_w1': np.zeros(W, np.float32), 'grad_b1': np.zeros(1, np.float32)}
+        else:
+            entry['width'] = (lvl.n_output_features + 7) // 8 * 8
+            entry['grad'] = (torch.randn(n, entry['width']) * 1e-6).bfloat16().view(torch.int16).numpy().view(np.uint16).copy()
+            entry['g32'] = np.zeros(grid.n_fp32_grad_rows * grid.n_features, np.float32)
+            entry['g16'] = np.zeros((grid.n_rows - grid.n_fp32_grad_rows) * grid.n_features, np.uint16)
+        levels.append(entry)
+    enc = wl.encoded_directions.view(torch.int16).numpy().view(np.uint16).copy()
+    return kind, checker, wl, rays, levels, enc
+
+
+def _time_cpu_baseline(prepared, n_rays: int, threads: int, repeats: int) -> dict:
+    kind, checker, wl, rays, levels, enc = prepared
+    n_threads = threads if kind == 'reference' else 1
+    start = time.perf_counter()
+    for _ in range(repeats):
+        for e in levels:
+            if 'mlp' in e:
+                out = checker.forward(e['grid'], *rays, e['tdist'], wl.pattern_seed, e['table'], e['mags'], mlp=e['mlp'], raw_density=True,
+                                      features_float=True, n_threads=n_threads)
+                checker.backward_mlp(e['grid'], *rays, e['tdist'], wl.pattern_seed, out['features_float'], e['grad_raw'], *e['mlp'][:3],
+                                     n_threads=n_threads, out=e['grads'])
+            else:
+                checker.forward(e['grid'], *rays, e['tdist'], wl.pattern_seed, e['table'], e['mags'], features_bf16_width=e['width'],
+                                encoded_directions=enc, nerf_inputs_width=96, n_threads=n_threads)
+                checker.backward(e['grid'], *rays, e['tdist'], wl.pattern_seed, e['grad'], e['g32'], e['g16'], n_threads=n_threads)
+    elapsed = time.perf_counter() - start
+    samples = n_rays * sum(l.n_intervals for l in wl.levels) * N_MULTISAMPLES * repeats
+    return {'value': samples / elapsed / 1e6, 'unit': UNIT, 'cores': n_threads, 'kind': kind,
+            'sample': f'{n_rays} rays of config 2 x (64 + 64 + 32) intervals x 6 multisamples, fwd+bwd of all three levels, '
+                      f'{repeats} pass(es): {samples} samples in {elapsed:.2f} s'}
+
+
+def run_reference_arm(args) -> None:
+    world, rank, _ = init_distributed(args.gpus)
+    if rank != 0:
+        return
+    from oracle.zf_oracle import build, n_threads_default
+    build()
+    baseline = CpuBaseline(args.reference_rays, n_threads_default())
+    values = []
+    for _ in range(args.warmup):
+        baseline.run()
+    for _ in range(args.steps):
+        values.append(baseline.run())
+    value = statistics.median(v['value'] for v in values)
+    base = values[0]
+    print(json.dumps({'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': args.gpus, 'steps': args.steps,
+                      'warmup': args.warmup, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+                      'data': 'synthetic', 'config': {'workload': 'config2 (paper-shape training-step featurization), bounded ray sample on the host cores',
+                                                      'rays': args.reference_rays},
+                      'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': base['cores'], 'kind': base['kind'], 'sample': base['sample']},
+                      'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}))
+
+
+def run_b200(args) -> None:
+    import torch.distributed as dist
+    from zipnerf_b200 import workloads
+    world, rank, local = init_distributed(args.gpus)
+    torch.cuda.set_device(local)
+    device = torch.device('cuda', local)
+    if world > 1:
+        import datetime
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120), device_id=device)
+    step = Step(workloads.config2(n_rays=args.rays, seed=1 + rank), device)
+    grads = step.grad_buffers()
+
+    def exchange():
+        if world > 1:
+            for buffer in grads:
+                dist.all_reduce(buffer)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step.run()
+        exchange()
+    barrier()
+    n_k = step.launches_per_step
+    events = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(n_k)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    visible = os.environ.get('CUDA_VISIBLE_DEVICES')
+    physical = int(visible.split(',')[local]) if visible and visible.split(',')[local].strip().isdigit() else local
+    with ClockSampler(physical) as clocks:
+        barrier()
+        start.record()
+        for i in range(args.steps):
+            step.run(events[i])
+            exchange()
+        end.record()
+        barrier()
+    elapsed_ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = t.item()
+    ms_per_step = elapsed_ms / args.steps
+    value = step.samples_per_step * world * args.steps / (elapsed_ms / 1e3) / 1e6
+    # per-kernel durations and the roofline of the dominant kernel
+    kernel_ms: dict[str, list] = {}
+    for i in range(args.steps):
+        for name, (a, b) in zip(step.kernel_names, events[i]):
+            kernel_ms.setdefault(name, []).append(a.elapsed_time(b))
+    bytes_per = {}
+    for name, nbytes in zip(step.kernel_names, step.kernel_bytes()):
+        bytes_per.setdefault(name, []).append(nbytes)
+    peaks = measured_peaks()
+    traffic = profiled_traffic()
+    kernels = {}
+    for name, times in kernel_ms.items():
+        launches_per_step = len(bytes_per[name])
+        avg_ms = sum(times) / len(times)
+        algo = sum(bytes_per[name]) / launches_per_step
+        kernels[name] = {'launches': len(times), 'avg_ms': avg_ms, 'share': sum(times) / sum(sum(v) for v in kernel_ms.values()),
+                         'algorithmic_bytes': algo, 'achieved_gbs': algo / (avg_ms * 1e-3) / 1e9}
+    dominant = max(kernels, key=lambda k: kernels[k]['avg_ms'] * kernels[k]['launches'])
+    dk = kernels[dominant]
+    roofline = {'bound': 'hbm', 'kernel': dominant, 'achieved': dk['achieved_gbs'], 'peak': peaks['hbm_gbs'], 'unit': 'GB/s',
+                'frac': dk['achieved_gbs'] / peaks['hbm_gbs'], 'peak_source': peaks['source'],
+                'traffic': traffic.get(dominant)}
+    result = {'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
+              'ms_per_step': ms_per_step, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+              'data': 'synthetic (seeded config 2 shapes; Mip-NeRF 360 unavailable)',
+              'config': {'workload': 'config2: 65536 rays x (64 + 64 + 32) intervals x 6 multisamples, fwd+bwd of 2 proposal levels (10x1 features, '
+                                     'table 2^21, 16->512, fused MLP 64) and the NeRF level (10x4 features, table 2^21, 16->8192)',
+                         'rays_per_gpu': args.rays, 'samples_per_step_per_gpu': step.samples_per_step,
+                         'parallelism': f'dp{world} (rays sharded, gradients all-reduced)' if world > 1 else 'single GPU',
+                         'l2': 'inputs larger than L2 (step working set ~1.8 GB > 126 MB)'},
+              'roofline': roofline, 'kernels': kernels, 'gpu_launches': step.launches_per_step * args.steps, 'clocks': clocks.summary()}
+    if not args.skip_e2e:
+        result['e2e'] = measure_e2e(step, args, world, exchange, barrier)
+    if rank == 0 and not args.skip_cpu_baseline and world == 1:
+        from oracle.zf_oracle import build, n_threads_default
+        build()
+        result['cpu_baseline'] = CpuBaseline(args.reference_rays, n_threads_default()).run(repeats=3)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result))
+
+
+def measure_e2e(step: Step, args, world: int, exchange, barrier) -> dict:
+    """The metric through the public API with host buffers: every step copies its inputs (rays, interval endpoints,
+    encoded directions, upstream gradients) from pinned host memory and reads back the MLP bias gradients."""
+    inputs = step.input_buffers()
+    host = [t.cpu().pin_memory() for t in inputs]
+    result_dev = [g['b1'] for g in step.prop_grads]
+    result_host = torch.empty(len(result_dev), pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    d2h = result_host.numel() * result_host.element_size()
+
+    def one():
+        for d, h in zip(inputs, host):
+            d.copy_(h, non_blocking=True)
+        step.run()
+        exchange()
+        result_host.copy_(torch.cat(result_dev), non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        one()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        one()
+    end.record()
+    barrier()
+    elapsed = start.elapsed_time(end)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([elapsed], device=step.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = t.item()
+    return {'value': step.samples_per_step * world * args.steps / (elapsed / 1e3) / 1e6, 'unit': UNIT, 'h2d_bytes_per_step': h2d,
+            'd2h_bytes_per_step': d2h, 'api': 'ZipNeRFCudaBackend._C.Featurizer'}
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument('--gpus', type=int, default=1)
+    parser.add_argument('--steps', type=int, default=20)
+    parser.add_argument('--warmup', type=int, default=3)
+    parser.add_argument('--impl', choices=['b200', 'reference'], default='b200')
+    parser.add_argument('--rays', type=int, default=65536)
+    parser.add_argument('--reference-rays', type=int, default=4096, help='ray sample of the CPU reference / baseline')
+    parser.add_argument('--skip-e2e', action='store_true')
+    parser.add_argument('--skip-cpu-baseline', action='store_true')
+    args = parser.parse_args()
+    args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps
+    if args.impl == 'reference':
+        run_reference_arm(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == '__main__':
+    main()

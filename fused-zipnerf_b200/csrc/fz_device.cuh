@@ -1,0 +1,244 @@
+// fz_device.cuh -- device-side math of the multisampled hash-grid featurization (sm_100a).
+//
+// Per interval of a ray this places six hexagonal multisamples in the conical frustum, contracts them into [0,1]^3,
+// derives per-level erf downweighting from the multisample radius, and visits the trilinear corners of every grid
+// level, with multisamples that fall into the same cell merged into one group of eight corners. The expressions follow
+// the reference's featurize_common.cuh operation for operation (same operand order, same fast-math intrinsics), so
+// the cell indices, hash rows and weights are bit-identical to the reference kernels:
+//   interval setup          featurize_common.cuh:56-98
+//   multisample/contraction featurize_common.cuh:101-117
+//   level weighting (erf)   featurize_common.cuh:45-47, 202-204
+//   corner visit + merging  featurize_common.cuh:123-173
+//   counter-based RNG       common/include/random.cuh:15-29
+// Kernels are compiled with --use_fast_math, like the reference's runtime compilation (rtc_kernel.cu:49).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace zf {
+
+constexpr int kMaxLevels = 16;
+constexpr int kMaxFeatures = 4;
+constexpr uint32_t kMultisamples = 6;
+constexpr float kGridBboxSize = 4.0f;  // grids cover the contracted space [-2, 2]^3
+constexpr float kMultisampleScale = 0.5f;
+constexpr uint32_t kHashPrimeY = 19349663u;
+constexpr uint32_t kHashPrimeZ = 83492791u;
+constexpr float kTiny = 1.17549435e-38f;
+constexpr float kPreconditionScaling = 10.0f;
+constexpr float kFeatureScale = kPreconditionScaling / kMultisamples;
+constexpr unsigned long long kPatternStreamBase = 16ull;
+
+// Grid layout of one featurizer, passed to every kernel by value (kernel parameters live in the constant bank, and
+// with the level loops unrolled every access is a constant-offset read).
+struct GridParams {
+    uint32_t n_levels;
+    uint32_t n_features;
+    uint32_t size[kMaxLevels];
+    uint32_t entries[kMaxLevels];
+    uint32_t offset[kMaxLevels + 1];
+    uint32_t hashed_mask;  // bit l: level l is hashed (size^3 > entries)
+    uint32_t pow2_mask;    // bit l: entries of level l is a power of two (hash modulo is a mask)
+    uint32_t n_fp32_levels;  // leading levels whose backward gradient is fp32
+    unsigned long long pattern_stream;
+};
+
+// Per-ray inputs shared by all kernels.
+struct RayInputs {
+    const float* origins;     // [n_rays, 3]
+    const float* directions;  // [n_rays, 3]
+    const float* radii;       // [n_rays]
+    const float* tdist;       // [n_rays, n_intervals + 1]
+    long long pattern_seed;   // < 0: deterministic alternating patterns
+    uint32_t n_intervals;
+    uint32_t n_samples;       // n_rays * n_intervals
+};
+
+// ---------------------------------------------------------------------------------------------------------------------
+// small vector helpers (the same operand order as the reference's featurize_common.cuh:38-43)
+
+__device__ __forceinline__ float3 add3(const float3& a, const float3& b) { return make_float3(a.x + b.x, a.y + b.y, a.z + b.z); }
+__device__ __forceinline__ float3 mul3(const float a, const float3& b) { return make_float3(a * b.x, a * b.y, a * b.z); }
+__device__ __forceinline__ float dot3(const float3& a, const float3& b) { return a.x * b.x + a.y * b.y + a.z * b.z; }
+__device__ __forceinline__ float3 cross3(const float3& a, const float3& b) {
+    return make_float3(a.y * b.z - a.z * b.y, a.z * b.x - a.x * b.z, a.x * b.y - a.y * b.x);
+}
+__device__ __forceinline__ float3 normalize3(const float3& a) { return mul3(rsqrtf(dot3(a, a)), a); }
+
+// ---------------------------------------------------------------------------------------------------------------------
+// counter-based random numbers: splitmix64 of (seed, stream, index)
+
+__device__ __forceinline__ unsigned long long splitmix64(unsigned long long x) {
+    x += 0x9e3779b97f4a7c15ull;
+    x = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ull;
+    x = (x ^ (x >> 27)) * 0x94d049bb133111ebull;
+    return x ^ (x >> 31);
+}
+
+__device__ __forceinline__ float rng_uniform(const unsigned long long seed, const unsigned long long stream, const unsigned long long index) {
+    const unsigned long long h = splitmix64(splitmix64(seed ^ (stream << 56)) ^ index);
+    return static_cast<float>(h >> 40) * (1.0f / 16777216.0f);
+}
+
+// erf approximation sign(x) sqrt(1 - exp(-4 x^2 / pi))
+__device__ __forceinline__ float approx_erf(const float x) {
+    return copysignf(sqrtf(-expm1f(-(4.0f / 3.14159265358979f) * x * x)), x);
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// conical frustum of one interval
+
+struct Frustum {
+    float3 origin, direction, axis1, axis2;
+    float radius, t0, ratio, base, root, rotation;
+    bool flip;
+};
+
+__device__ __forceinline__ float3 load_float3(const float* p, const uint32_t i) {
+    return make_float3(__ldg(p + 3 * i), __ldg(p + 3 * i + 1), __ldg(p + 3 * i + 2));
+}
+
+__device__ __forceinline__ Frustum setup_frustum(const RayInputs& in, const unsigned long long pattern_stream, const uint32_t sample) {
+    Frustum fr;
+    const uint32_t ray = sample / in.n_intervals;
+    const uint32_t interval = sample - ray * in.n_intervals;
+    fr.origin = load_float3(in.origins, ray);
+    fr.direction = load_float3(in.directions, ray);
+    fr.radius = __ldg(in.radii + ray);
+    const float3 d = fr.direction;
+    float3 c = cross3(d, make_float3(0.0f, 0.0f, 1.0f));
+    constexpr float eps = 1.1920929e-07f;
+    if (fabsf(c.x) < eps && fabsf(c.y) < eps && fabsf(c.z) < eps) c = cross3(d, make_float3(1.0f, 1.0f, 1.0f));
+    fr.axis1 = normalize3(c);
+    fr.axis2 = normalize3(cross3(d, c));
+    const float* t = in.tdist + static_cast<size_t>(ray) * (in.n_intervals + 1) + interval;
+    const float t0 = __ldg(t), t1 = __ldg(t + 1);
+    const float s = 0.5f * (t0 + t1);
+    const float h = 0.5f * (t1 - t0);
+    const float denominator = h * h + 3.0f * s * s;
+    fr.t0 = t0;
+    fr.ratio = fabsf(denominator) < kTiny ? 0.0f : h / denominator;
+    fr.base = t1 * t1 + 2.0f * s * s;
+    const float q = h * h - s * s;
+    fr.root = sqrtf(fmaxf(q * q + 4.0f * s * s * s * s, 0.0f));
+    if (in.pattern_seed >= 0) {
+        const unsigned long long seed = static_cast<unsigned long long>(in.pattern_seed);
+        fr.flip = rng_uniform(seed, pattern_stream, 2ull * sample) < 0.5f;
+        fr.rotation = 2.0f * 3.14159265358979f * rng_uniform(seed, pattern_stream, 2ull * sample + 1);
+    }
+    else {
+        fr.flip = interval % 2 == 1;
+        fr.rotation = fr.flip ? 3.14159265358979f / 6.0f : 0.0f;
+    }
+    return fr;
+}
+
+// contracted position of multisample j in [0,1]^3 and its radius in the same units; contracted = |p|^2 > 1
+__device__ __forceinline__ void multisample(const Frustum& fr, const uint32_t j, float3& x, float& scale, bool* contracted = nullptr) {
+    constexpr float pattern[kMultisamples] = {0.0f, 2.0f, 4.0f, 3.0f, 5.0f, 1.0f};
+    const float theta = (3.14159265358979f / 3.0f) * pattern[fr.flip ? kMultisamples - 1 - j : j] + fr.rotation;
+    const float cz = fr.t0 + fr.ratio * (fr.base + (3.0f / sqrtf(7.0f)) * (j * 0.4f - 1.0f) * fr.root);
+    const float perp = sqrtf(0.5f) * fr.radius * cz;
+    float sin_theta, cos_theta;
+    sincosf(theta, &sin_theta, &cos_theta);
+    const float3 p = add3(add3(add3(fr.origin, mul3(perp * cos_theta, fr.axis1)), mul3(perp * sin_theta, fr.axis2)), mul3(cz, fr.direction));
+    const float dot_p = dot3(p, p);
+    if (contracted != nullptr) *contracted = dot_p > 1.0f;
+    const float norm_sq = fmaxf(dot_p, 1.0f);
+    const float norm = sqrtf(norm_sq);
+    const float isoscale = expf((2.0f / 3.0f) * logf(2.0f * norm - 1.0f) - logf(norm_sq));
+    const float contraction = (2.0f * norm - 1.0f) / norm_sq;
+    x = add3(mul3(1.0f / kGridBboxSize, mul3(contraction, p)), make_float3(0.5f, 0.5f, 0.5f));
+    scale = kMultisampleScale * perp * isoscale * (1.0f / kGridBboxSize);
+}
+
+__device__ __forceinline__ float level_weighting(const uint32_t size, const float scale) {
+    return approx_erf(1.0f / (sqrtf(8.0f) * scale * size));
+}
+
+// table row of a corner (level offset included); weight is zeroed for corners outside a dense level
+__device__ __forceinline__ uint32_t corner_row(const GridParams& gp, const uint32_t level, const int ix, const int iy, const int iz, float& weight) {
+    uint32_t index;
+    if (gp.hashed_mask & (1u << level)) {
+        const uint32_t h = static_cast<uint32_t>(ix) ^ (static_cast<uint32_t>(iy) * kHashPrimeY) ^ (static_cast<uint32_t>(iz) * kHashPrimeZ);
+        index = (gp.pow2_mask & (1u << level)) ? (h & (gp.entries[level] - 1u)) : (h % gp.entries[level]);
+    }
+    else {
+        const int n = static_cast<int>(gp.size[level]);
+        const bool valid = ix >= 0 && ix < n && iy >= 0 && iy < n && iz >= 0 && iz < n;
+        if (!valid) weight = 0.0f;
+        index = valid ? static_cast<uint32_t>(ix + n * (iy + n * iz)) : 0u;
+    }
+    return gp.offset[level] + index;
+}
+
+// Visits the merged corner groups of one level: visitor(row, weight) for the 8 corners of every group, groups in
+// the order of their first multisample, corners in the order (x, y, z) bit 2, 1, 0.
+template <typename Visitor>
+__device__ __forceinline__ void visit_level(const GridParams& gp, const uint32_t level, const float3* x, const float* weighting, Visitor& visitor) {
+    const uint32_t size = gp.size[level];
+    int cells[kMultisamples][3];
+    float fractions[kMultisamples][3];
+    #pragma unroll
+    for (uint32_t j = 0; j < kMultisamples; j++) {
+        const float p[3] = {x[j].x * size - 0.5f, x[j].y * size - 0.5f, x[j].z * size - 0.5f};
+        #pragma unroll
+        for (uint32_t d = 0; d < 3; d++) {
+            const float floored = floorf(p[d]);
+            cells[j][d] = static_cast<int>(floored);
+            fractions[j][d] = p[d] - floored;
+        }
+    }
+    uint32_t merged = 0;
+    #pragma unroll
+    for (uint32_t j = 0; j < kMultisamples; j++) {
+        if (merged & (1u << j)) continue;
+        float corner_weights[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        #pragma unroll
+        for (uint32_t k = j; k < kMultisamples; k++) {
+            if (cells[k][0] != cells[j][0] || cells[k][1] != cells[j][1] || cells[k][2] != cells[j][2]) continue;
+            merged |= 1u << k;
+            #pragma unroll
+            for (uint32_t corner = 0; corner < 8; corner++) {
+                const float wx = corner & 4u ? fractions[k][0] : 1.0f - fractions[k][0];
+                const float wy = corner & 2u ? fractions[k][1] : 1.0f - fractions[k][1];
+                const float wz = corner & 1u ? fractions[k][2] : 1.0f - fractions[k][2];
+                corner_weights[corner] += weighting[k] * (wx * wy * wz);
+            }
+        }
+        #pragma unroll
+        for (uint32_t corner = 0; corner < 8; corner++) {
+            float weight = corner_weights[corner];
+            const uint32_t row = corner_row(gp, level, cells[j][0] + static_cast<int>((corner >> 2) & 1u),
+                                            cells[j][1] + static_cast<int>((corner >> 1) & 1u), cells[j][2] + static_cast<int>(corner & 1u), weight);
+            visitor(row, weight);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// numeric conversions (round to nearest even, as the reference's cvt.rn)
+
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(const float v) {
+    uint16_t r;
+    asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(r) : "f"(v));
+    return r;
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(const uint16_t v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
+
+// packs (lo, hi) into one f16x2 word, lo at the lower address
+__device__ __forceinline__ uint32_t pack_half2(const float lo, const float hi) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+__device__ __forceinline__ uint16_t f32_to_half_bits(const float v) {
+    uint16_t r;
+    asm("cvt.rn.f16.f32 %0, %1;" : "=h"(r) : "f"(v));
+    return r;
+}
+
+}  // namespace zf

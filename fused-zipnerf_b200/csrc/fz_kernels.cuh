@@ -1,0 +1,555 @@
+// fz_kernels.cuh -- featurization kernels: forward (optionally with the fused density MLP), NeRF-level backward, and
+// proposal-level backward with the MLP recomputation.
+//
+// The reference compiles one kernel per grid at runtime with the layout, level count and feature count as constants
+// (featurizer.cu:157-184). Here kernels are compiled ahead of time for sm_100a, templated only on the features per level
+// F (and, with the MLP, on the MLP input width rounded up to a multiple of 8); the level loop runs over the layout in
+// the kernel parameters, with one level's multisample / corner / gather body unrolled. Per-thread feature rows are
+// staged in shared memory, so outputs leave the SM as coalesced warp-wide stores.
+#pragma once
+
+#include "fz_device.cuh"
+
+namespace zf {
+
+constexpr int kBlock = 128;
+constexpr int kWarps = kBlock / 32;
+
+// odd row stride (in floats) of per-thread rows in shared memory: lanes writing the same column hit distinct banks
+__host__ __device__ constexpr int staged_stride(const int n_out) { return n_out | 1; }
+
+// ---------------------------------------------------------------------------------------------------------------------
+// forward
+
+struct ForwardArgs {
+    RayInputs in;
+    const float* table;             // [rows, F]
+    const float* scale_magnitudes;  // [L]
+    const float* w0;                // [W, n_out]
+    const float* b0;                // [W]
+    const float* w1;                // [W]
+    const float* b1;                // [1]
+    int mlp_width;
+    float* raw_density;             // [n_samples] or null (requires the MLP)
+    float* features_float;          // [n_samples, n_out] or null
+    uint16_t* features_bf16;        // [n_samples, features_bf16_width] or null
+    int features_bf16_width;
+    const uint16_t* encoded_directions;  // [n_rays, encoded_width]
+    uint16_t* nerf_inputs;          // [n_samples, nerf_inputs_width] or null (last encoded_width columns written)
+    int nerf_inputs_width;
+    int encoded_width;
+    uint32_t interleave_rays;       // 0: consecutive threads take consecutive samples; else the same interval of this many rays
+    bool bf16_pairs;                // features_bf16 allows 4-byte (pair) stores: even width, 4-byte aligned
+    bool inputs_vectors;            // nerf_inputs / encoded_directions allow 16-byte copies
+};
+
+template <int F>
+struct GatherRows {
+    const float* table;
+    float value[F];
+
+    __device__ __forceinline__ void operator()(const uint32_t row, const float weight) {
+        if (weight == 0.0f) return;
+        if constexpr (F == 4) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(table) + row);
+            value[0] += weight * t.x;
+            value[1] += weight * t.y;
+            value[2] += weight * t.z;
+            value[3] += weight * t.w;
+        }
+        else if constexpr (F == 2) {
+            const float2 t = __ldg(reinterpret_cast<const float2*>(table) + row);
+            value[0] += weight * t.x;
+            value[1] += weight * t.y;
+        }
+        else {
+            #pragma unroll
+            for (int f = 0; f < F; f++) value[f] += weight * __ldg(table + row * F + f);
+        }
+    }
+};
+
+// sample of a thread: consecutive samples, or (interleave) the same interval of up to R consecutive rays per warp run
+// (featurize_forward.cu:49-58)
+__device__ __forceinline__ uint32_t thread_sample(const uint32_t t, const RayInputs& in, const uint32_t interleave_rays) {
+    if (interleave_rays == 0) return t;
+    const uint32_t n = in.n_intervals;
+    const uint32_t group = t / (interleave_rays * n), offset = t % (interleave_rays * n);
+    const uint32_t group_rays = min(interleave_rays, in.n_samples / n - interleave_rays * group);
+    return (interleave_rays * group + offset % group_rays) * n + offset / group_rays;
+}
+
+__device__ __forceinline__ void multisamples(const Frustum& fr, float3 (&x)[kMultisamples], float (&scale)[kMultisamples]) {
+    #pragma unroll
+    for (uint32_t j = 0; j < kMultisamples; j++) multisample(fr, j, x[j], scale[j]);
+}
+
+// all level features of one interval into a shared-memory row: row[l (F + 1) + f] grid features (averaged over the
+// multisamples and preconditioned), row[l (F + 1) + F] the scale feature (featurize_common.cuh:207-227)
+template <int F>
+__device__ __forceinline__ void featurize_to_row(const GridParams& gp, const Frustum& fr, const float* __restrict__ table,
+                                                 const float* __restrict__ scale_magnitudes, float* row) {
+    float3 x[kMultisamples];
+    float scale[kMultisamples];
+    multisamples(fr, x, scale);
+    #pragma unroll 1
+    for (uint32_t level = 0; level < gp.n_levels; level++) {
+        float weighting[kMultisamples];
+        float scale_feature = 0.0f;
+        #pragma unroll
+        for (uint32_t j = 0; j < kMultisamples; j++) {
+            weighting[j] = level_weighting(gp.size[level], scale[j]);
+            scale_feature += 2.0f * weighting[j] - 1.0f;
+        }
+        GatherRows<F> gather{table, {}};
+        #pragma unroll
+        for (int f = 0; f < F; f++) gather.value[f] = 0.0f;
+        visit_level(gp, level, x, weighting, gather);
+        #pragma unroll
+        for (int f = 0; f < F; f++) row[level * (F + 1) + f] = kFeatureScale * gather.value[f];
+        row[level * (F + 1) + F] = kFeatureScale * scale_feature * __ldg(scale_magnitudes + level);
+    }
+}
+
+// warp-cooperative copy of the warp's staged rows to row-major global outputs (rows of samples s_sample[...])
+__device__ __forceinline__ void store_rows_float(const float* s_rows, const int stride, const uint32_t* s_sample, const int n_rows, const int n_out,
+                                                 float* __restrict__ out, const int lane) {
+    const int n = n_rows * n_out;
+    for (int e = lane; e < n; e += 32) {
+        const int r = e / n_out, c = e - r * n_out;
+        out[static_cast<size_t>(s_sample[r]) * n_out + c] = s_rows[r * stride + c];
+    }
+}
+
+__device__ __forceinline__ void store_rows_bf16(const float* s_rows, const int stride, const uint32_t* s_sample, const int n_rows, const int n_out,
+                                                uint16_t* __restrict__ out, const int width, const bool pairs, const int lane) {
+    if (pairs) {
+        const int half = width / 2;
+        const int n = n_rows * half;
+        for (int e = lane; e < n; e += 32) {
+            const int r = e / half, p = e - r * half;
+            const int c = 2 * p;
+            const uint32_t lo = c < n_out ? f32_to_bf16_bits(s_rows[r * stride + c]) : 0u;
+            const uint32_t hi = c + 1 < n_out ? f32_to_bf16_bits(s_rows[r * stride + c + 1]) : 0u;
+            reinterpret_cast<uint32_t*>(out + static_cast<size_t>(s_sample[r]) * width)[p] = lo | (hi << 16);
+        }
+    }
+    else {
+        const int n = n_rows * width;
+        for (int e = lane; e < n; e += 32) {
+            const int r = e / width, c = e - r * width;
+            out[static_cast<size_t>(s_sample[r]) * width + c] = c < n_out ? f32_to_bf16_bits(s_rows[r * stride + c]) : static_cast<uint16_t>(0);
+        }
+    }
+}
+
+// the encoded view direction in the last columns of the NeRF MLP inputs, its last column the bias lane (bf16 1.0)
+// (featurize_forward.cu:86-92)
+template <typename Args>
+__device__ __forceinline__ void store_inputs_tail(const Args& a, const uint32_t* s_sample, const int n_rows, const int lane) {
+    const int E = a.encoded_width;
+    if (a.inputs_vectors) {
+        const int nv = E / 8;
+        const int n = n_rows * nv;
+        for (int e = lane; e < n; e += 32) {
+            const int r = e / nv, v = e - r * nv;
+            const uint32_t sample = s_sample[r];
+            const uint4* src = reinterpret_cast<const uint4*>(a.encoded_directions + static_cast<size_t>(sample / a.in.n_intervals) * E);
+            uint4 value = __ldg(src + v);
+            if (v == nv - 1) value.w = (value.w & 0x0000FFFFu) | 0x3f800000u;
+            reinterpret_cast<uint4*>(a.nerf_inputs + static_cast<size_t>(sample + 1) * a.nerf_inputs_width - E)[v] = value;
+        }
+    }
+    else {
+        const int n = n_rows * E;
+        for (int e = lane; e < n; e += 32) {
+            const int r = e / E, c = e - r * E;
+            const uint32_t sample = s_sample[r];
+            const uint16_t value = c == E - 1 ? static_cast<uint16_t>(0x3f80) : a.encoded_directions[static_cast<size_t>(sample / a.in.n_intervals) * E + c];
+            a.nerf_inputs[static_cast<size_t>(sample + 1) * a.nerf_inputs_width - E + c] = value;
+        }
+    }
+}
+
+// Forward. NOUT_PAD == 0: no MLP; otherwise the fused density MLP n_out -> W (ReLU) -> 1 runs for raw_density, with
+// the features in registers (NOUT_PAD >= n_out) and the reference's accumulation order (featurize_forward.cu:65-73).
+template <int F, int NOUT_PAD>
+__global__ void __launch_bounds__(kBlock) fz_forward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ ForwardArgs a) {
+    const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
+    const int stride = staged_stride(n_out);
+    extern __shared__ __align__(16) float smem[];
+    uint32_t* s_sample = reinterpret_cast<uint32_t*>(smem);   // [kBlock]
+    float* s_rows = smem + kBlock;                             // [kBlock, stride]
+    float* s_w0 = smem + (kBlock + kBlock * stride + 3) / 4 * 4;  // [W, NOUT_PAD] (MLP only; 16-byte aligned)
+    float* s_b0 = s_w0 + a.mlp_width * NOUT_PAD;               // [W]
+    float* s_w1 = s_b0 + a.mlp_width;                          // [W]
+    if constexpr (NOUT_PAD > 0) {
+        for (int i = threadIdx.x; i < a.mlp_width * NOUT_PAD; i += kBlock) {
+            const int j = i / NOUT_PAD, c = i - j * NOUT_PAD;
+            s_w0[i] = c < n_out ? __ldg(a.w0 + j * n_out + c) : 0.0f;
+        }
+        for (int i = threadIdx.x; i < a.mlp_width; i += kBlock) {
+            s_b0[i] = __ldg(a.b0 + i);
+            s_w1[i] = __ldg(a.w1 + i);
+        }
+        __syncthreads();
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t warp_first = blockIdx.x * kBlock + warp * 32;
+    if (warp_first >= a.in.n_samples) return;
+    const int n_rows = min(32, static_cast<int>(a.in.n_samples - warp_first));
+    const bool active = lane < n_rows;
+    const uint32_t sample = active ? thread_sample(warp_first + lane, a.in, a.interleave_rays) : 0u;
+    float* row = s_rows + threadIdx.x * stride;
+    s_sample[threadIdx.x] = sample;
+    if (active) {
+        const Frustum fr = setup_frustum(a.in, gp.pattern_stream, sample);
+        featurize_to_row<F>(gp, fr, a.table, a.scale_magnitudes, row);
+    }
+    if constexpr (NOUT_PAD > 0) {
+        if (active) {
+            float f[NOUT_PAD];
+            #pragma unroll
+            for (int i = 0; i < NOUT_PAD; i++) f[i] = i < n_out ? row[i] : 0.0f;
+            float raw = __ldg(a.b1);
+            for (int j = 0; j < a.mlp_width; j++) {
+                float pre = s_b0[j];
+                const float4* w = reinterpret_cast<const float4*>(s_w0 + j * NOUT_PAD);
+                #pragma unroll
+                for (int q = 0; q < NOUT_PAD / 4; q++) {
+                    const float4 wq = w[q];
+                    if (4 * q < n_out) pre += wq.x * f[4 * q];
+                    if (4 * q + 1 < n_out) pre += wq.y * f[4 * q + 1];
+                    if (4 * q + 2 < n_out) pre += wq.z * f[4 * q + 2];
+                    if (4 * q + 3 < n_out) pre += wq.w * f[4 * q + 3];
+                }
+                raw += s_w1[j] * fmaxf(pre, 0.0f);
+            }
+            a.raw_density[sample] = raw;
+        }
+    }
+    __syncwarp();
+    const float* warp_rows = s_rows + warp * 32 * stride;
+    const uint32_t* warp_samples = s_sample + warp * 32;
+    if (a.features_float != nullptr) store_rows_float(warp_rows, stride, warp_samples, n_rows, n_out, a.features_float, lane);
+    if (a.features_bf16 != nullptr) store_rows_bf16(warp_rows, stride, warp_samples, n_rows, n_out, a.features_bf16, a.features_bf16_width, a.bf16_pairs, lane);
+    if (a.nerf_inputs != nullptr) store_inputs_tail(a, warp_samples, n_rows, lane);
+}
+
+// dynamic shared memory of fz_forward_kernel in floats (the MLP weights start 16-byte aligned)
+__host__ __device__ constexpr int forward_smem_floats(const int n_out, const int nout_pad, const int width) {
+    return ((kBlock + kBlock * staged_stride(n_out) + 3) / 4) * 4 + (nout_pad > 0 ? width * nout_pad + 2 * width : 0);
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// row gradient atomics (featurize_common.cuh:230-268)
+
+template <int F>
+__device__ __forceinline__ void add_row_f32(float* __restrict__ grad_table, const uint32_t row, const float weight, const float* g) {
+    float* p = grad_table + static_cast<size_t>(row) * F;
+    if constexpr (F == 4) {
+        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" :: "l"(p), "f"(weight * g[0]), "f"(weight * g[1]),
+                     "f"(weight * g[2]), "f"(weight * g[3]) : "memory");
+    }
+    else {
+        #pragma unroll
+        for (int f = 0; f < F; f++) {
+            if (g[f] != 0.0f) atomicAdd(p + f, weight * g[f]);
+        }
+    }
+}
+
+template <int F>
+__device__ __forceinline__ void add_row_f16(uint16_t* __restrict__ grad_table, const uint32_t row, const float weight, const float* g) {
+    uint16_t* p = grad_table + static_cast<size_t>(row) * F;
+    if constexpr (F == 4) {
+        const uint32_t p0 = pack_half2(weight * g[0], weight * g[1]);
+        const uint32_t p1 = pack_half2(weight * g[2], weight * g[3]);
+        asm volatile("red.global.add.noftz.v2.f16x2 [%0], {%1, %2};" :: "l"(p), "r"(p0), "r"(p1) : "memory");
+    }
+    else if constexpr (F % 2 == 0) {
+        #pragma unroll
+        for (int q = 0; q < F / 2; q++) {
+            const uint32_t pair = pack_half2(weight * g[2 * q], weight * g[2 * q + 1]);
+            asm volatile("red.global.add.noftz.f16x2 [%0], %1;" :: "l"(p + 2 * q), "r"(pair) : "memory");
+        }
+    }
+    else {
+        #pragma unroll
+        for (int f = 0; f < F; f++) {
+            if (g[f] != 0.0f) asm volatile("red.global.add.noftz.f16 [%0], %1;" :: "l"(p + f), "h"(f32_to_half_bits(weight * g[f])) : "memory");
+        }
+    }
+}
+
+// scatters one interval's feature gradient (g_row[l (F + 1) + f]; scale features carry none) into the grid gradient:
+// levels below n_fp32 into grad_table (fp32), the others into grad_table_half (fp16, rows re-based at the first fp16
+// level) (featurize_common.cuh:273-291)
+template <int F>
+__device__ __forceinline__ void scatter_row(const GridParams& gp, const Frustum& fr, const float* g_row, const uint32_t n_fp32,
+                                            float* __restrict__ grad_table, uint16_t* __restrict__ grad_table_half) {
+    float3 x[kMultisamples];
+    float scale[kMultisamples];
+    multisamples(fr, x, scale);
+    const uint32_t half_base = gp.offset[min(n_fp32, gp.n_levels)];
+    #pragma unroll 1
+    for (uint32_t level = 0; level < gp.n_levels; level++) {
+        float weighting[kMultisamples];
+        #pragma unroll
+        for (uint32_t j = 0; j < kMultisamples; j++) weighting[j] = level_weighting(gp.size[level], scale[j]);
+        float g[F];
+        #pragma unroll
+        for (int f = 0; f < F; f++) g[f] = g_row[level * (F + 1) + f];
+        if (level < n_fp32) {
+            auto visitor = [&](const uint32_t row, const float weight) {
+                if (weight != 0.0f) add_row_f32<F>(grad_table, row, weight, g);
+            };
+            visit_level(gp, level, x, weighting, visitor);
+        }
+        else {
+            auto visitor = [&](const uint32_t row, const float weight) {
+                if (weight != 0.0f) add_row_f16<F>(grad_table_half, row - half_base, weight, g);
+            };
+            visit_level(gp, level, x, weighting, visitor);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// NeRF-level backward: bf16 feature gradients -> grid gradient scaled by grad_scale (featurize_backward.cu:19-26)
+
+struct BackwardArgs {
+    RayInputs in;
+    const uint16_t* grad_features;  // bf16 [n_samples, >= n_out], row stride grad_stride
+    long long grad_stride;
+    float grad_scale;
+    float* grad_table;              // fp32 [n_fp32_rows, F]
+    uint16_t* grad_table_half;      // fp16 [rows - n_fp32_rows, F]
+};
+
+template <int F>
+__global__ void __launch_bounds__(kBlock) fz_backward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardArgs a) {
+    const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
+    const int stride = staged_stride(n_out);
+    extern __shared__ __align__(16) float smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t warp_first = blockIdx.x * kBlock + warp * 32;
+    if (warp_first >= a.in.n_samples) return;
+    const int n_rows = min(32, static_cast<int>(a.in.n_samples - warp_first));
+    float* warp_rows = smem + warp * 32 * stride;
+    // coalesced load of the warp's gradient rows, scaled as the reference (feature_scale * grad_scale * g)
+    const int n = n_rows * n_out;
+    for (int e = lane; e < n; e += 32) {
+        const int r = e / n_out, c = e - r * n_out;
+        const uint16_t bits = __ldg(a.grad_features + static_cast<size_t>(warp_first + r) * a.grad_stride + c);
+        warp_rows[r * stride + c] = kFeatureScale * a.grad_scale * bf16_bits_to_f32(bits);
+    }
+    __syncwarp();
+    if (lane >= n_rows) return;
+    const uint32_t sample = warp_first + lane;
+    const Frustum fr = setup_frustum(a.in, gp.pattern_stream, sample);
+    scatter_row<F>(gp, fr, warp_rows + lane * stride, gp.n_fp32_levels, a.grad_table, a.grad_table_half);
+}
+
+__host__ __device__ constexpr int backward_smem_floats(const int n_out) { return kBlock * staged_stride(n_out); }
+
+// ---------------------------------------------------------------------------------------------------------------------
+// proposal-level backward: recompute the fused MLP from the stored fp32 features, scatter the input gradient into the
+// fp32 grid gradient, and reduce the MLP parameter gradients (featurize_backward_mlp.cu:79-147)
+//
+// with a_j = [pre_j > 0] g: grad_w0[j][i] = w1_j sum a_j f_i, grad_b0[j] = w1_j sum a_j, grad_w1[j] = sum g relu(pre_j),
+// grad_b1 = sum g
+
+struct BackwardMlpArgs {
+    RayInputs in;
+    const float* features;          // [n_samples, n_out]
+    const float* grad_raw_density;  // [n_samples]
+    const float* w0;                // [W, n_out]
+    const float* b0;                // [W]
+    const float* w1;                // [W]
+    int mlp_width;
+    float* grad_table;              // [rows, F]
+    float* grad_w0;
+    float* grad_b0;
+    float* grad_w1;
+    float* grad_b1;
+};
+
+// dynamic shared memory of fz_backward_mlp_kernel in floats
+__host__ __device__ constexpr int backward_mlp_smem_floats(const int n_out, const int nout_pad, const int width) {
+    return width * nout_pad + 2 * width                // weights (w0 rows padded to nout_pad)
+        + (width * n_out + 2 * width + 1)              // per-block parameter gradient sums
+        + kBlock * (width + staged_stride(n_out) + 1); // per-step pre-activations, feature rows, raw density gradients
+}
+
+template <int F, int NOUT_PAD>
+__global__ void __launch_bounds__(kBlock) fz_backward_mlp_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardMlpArgs a) {
+    const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
+    const int stride = staged_stride(n_out);
+    const int W = a.mlp_width;
+    const int n_w0 = W * n_out;
+    const int n_params = n_w0 + 2 * W + 1;
+    extern __shared__ __align__(16) float smem[];
+    float* s_w0 = smem;                        // [W, NOUT_PAD]
+    float* s_b0 = s_w0 + W * NOUT_PAD;
+    float* s_w1 = s_b0 + W;
+    float* s_acc = s_w1 + W;                   // [n_params]
+    float* s_pre = s_acc + n_params;           // [kBlock, W]
+    float* s_rows = s_pre + kBlock * W;        // [kBlock, stride]: the scaled feature gradient, then the features
+    float* s_g = s_rows + kBlock * stride;     // [kBlock]
+    for (int i = threadIdx.x; i < W * NOUT_PAD; i += kBlock) {
+        const int j = i / NOUT_PAD, c = i - j * NOUT_PAD;
+        s_w0[i] = c < n_out ? __ldg(a.w0 + j * n_out + c) : 0.0f;
+    }
+    for (int i = threadIdx.x; i < W; i += kBlock) {
+        s_b0[i] = __ldg(a.b0 + i);
+        s_w1[i] = __ldg(a.w1 + i);
+    }
+    for (int i = threadIdx.x; i < n_params; i += kBlock) s_acc[i] = 0.0f;
+    __syncthreads();
+    float* row = s_rows + threadIdx.x * stride;
+
+    // block-uniform loop bound, so every thread reaches the barriers
+    for (uint32_t base = blockIdx.x * kBlock; base < a.in.n_samples; base += gridDim.x * kBlock) {
+        const uint32_t sample = base + threadIdx.x;
+        const bool active = sample < a.in.n_samples;
+        float f[NOUT_PAD];
+        #pragma unroll
+        for (int i = 0; i < NOUT_PAD; i++) f[i] = active && i < n_out ? __ldg(a.features + static_cast<size_t>(sample) * n_out + i) : 0.0f;
+        const float g = active ? __ldg(a.grad_raw_density + sample) : 0.0f;
+        float grad_f[NOUT_PAD];
+        #pragma unroll
+        for (int i = 0; i < NOUT_PAD; i++) grad_f[i] = 0.0f;
+        for (int j = 0; j < W; j++) {
+            float pre = s_b0[j];
+            const float4* w = reinterpret_cast<const float4*>(s_w0 + j * NOUT_PAD);
+            #pragma unroll
+            for (int q = 0; q < NOUT_PAD / 4; q++) {
+                const float4 wq = w[q];
+                if (4 * q < n_out) pre += wq.x * f[4 * q];
+                if (4 * q + 1 < n_out) pre += wq.y * f[4 * q + 1];
+                if (4 * q + 2 < n_out) pre += wq.z * f[4 * q + 2];
+                if (4 * q + 3 < n_out) pre += wq.w * f[4 * q + 3];
+            }
+            s_pre[threadIdx.x * W + j] = pre;
+            if (pre > 0.0f) {
+                const float grad_pre = g * s_w1[j];
+                #pragma unroll
+                for (int q = 0; q < NOUT_PAD / 4; q++) {
+                    const float4 wq = w[q];
+                    grad_f[4 * q] += grad_pre * wq.x;
+                    grad_f[4 * q + 1] += grad_pre * wq.y;
+                    grad_f[4 * q + 2] += grad_pre * wq.z;
+                    grad_f[4 * q + 3] += grad_pre * wq.w;
+                }
+            }
+        }
+        s_g[threadIdx.x] = g;
+        // the scatter reads the scaled feature gradient from the thread's row; the parameter reduction then needs the
+        // features, which replace it afterwards
+        #pragma unroll
+        for (int i = 0; i < NOUT_PAD; i++) {
+            if (i < n_out) row[i] = grad_f[i] * kFeatureScale;
+        }
+        if (active && g != 0.0f) {
+            const Frustum fr = setup_frustum(a.in, gp.pattern_stream, sample);
+            scatter_row<F>(gp, fr, row, gp.n_levels, a.grad_table, nullptr);
+        }
+        #pragma unroll
+        for (int i = 0; i < NOUT_PAD; i++) {
+            if (i < n_out) row[i] = f[i];
+        }
+        __syncthreads();
+        for (int q = threadIdx.x; q < n_params; q += kBlock) {
+            float sum = 0.0f;
+            if (q < n_w0) {
+                const int j = q / n_out, i = q - j * n_out;
+                for (int s = 0; s < kBlock; s++) {
+                    if (s_pre[s * W + j] > 0.0f) sum += s_g[s] * s_rows[s * stride + i];
+                }
+            }
+            else if (q < n_w0 + W) {
+                const int j = q - n_w0;
+                for (int s = 0; s < kBlock; s++) {
+                    if (s_pre[s * W + j] > 0.0f) sum += s_g[s];
+                }
+            }
+            else if (q < n_w0 + 2 * W) {
+                const int j = q - n_w0 - W;
+                for (int s = 0; s < kBlock; s++) sum += s_g[s] * fmaxf(s_pre[s * W + j], 0.0f);
+            }
+            else {
+                for (int s = 0; s < kBlock; s++) sum += s_g[s];
+            }
+            s_acc[q] += sum;
+        }
+        __syncthreads();
+    }
+
+    for (int q = threadIdx.x; q < n_params; q += kBlock) {
+        const float acc = s_acc[q];
+        if (acc == 0.0f) continue;
+        if (q < n_w0) atomicAdd(a.grad_w0 + q, s_w1[q / n_out] * acc);
+        else if (q < n_w0 + W) atomicAdd(a.grad_b0 + (q - n_w0), s_w1[q - n_w0] * acc);
+        else if (q < n_w0 + 2 * W) atomicAdd(a.grad_w1 + (q - n_w0 - W), acc);
+        else atomicAdd(a.grad_b1, acc);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// debug: intermediate values of single intervals (positions, contraction flags, merged corner rows and weights)
+
+struct DebugArgs {
+    RayInputs in;
+    const uint32_t* samples;  // [n_debug] sample indices
+    uint32_t n_debug;
+    float* x;                 // [n_debug, 6, 3]
+    float* scale;             // [n_debug, 6]
+    int32_t* contracted;      // [n_debug, 6]
+    int32_t* n_groups;        // [n_debug, L]
+    uint32_t* rows;           // [n_debug, L, 6, 8]
+    float* weights;           // [n_debug, L, 6, 8]
+};
+
+// (a template only so that the header defines no non-inline kernel; instantiated once, as fz_debug_kernel<0>)
+template <int kUnused>
+__global__ void fz_debug_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ DebugArgs a) {
+    const uint32_t d = blockIdx.x * blockDim.x + threadIdx.x;
+    if (d >= a.n_debug) return;
+    const uint32_t sample = a.samples[d];
+    const uint32_t L = gp.n_levels;
+    const Frustum fr = setup_frustum(a.in, gp.pattern_stream, sample);
+    float3 x[kMultisamples];
+    float scale[kMultisamples];
+    #pragma unroll
+    for (uint32_t j = 0; j < kMultisamples; j++) {
+        bool contracted;
+        multisample(fr, j, x[j], scale[j], &contracted);
+        a.x[(d * kMultisamples + j) * 3] = x[j].x;
+        a.x[(d * kMultisamples + j) * 3 + 1] = x[j].y;
+        a.x[(d * kMultisamples + j) * 3 + 2] = x[j].z;
+        a.scale[d * kMultisamples + j] = scale[j];
+        a.contracted[d * kMultisamples + j] = contracted;
+    }
+    #pragma unroll 1
+    for (uint32_t level = 0; level < L; level++) {
+        float weighting[kMultisamples];
+        #pragma unroll
+        for (uint32_t j = 0; j < kMultisamples; j++) weighting[j] = level_weighting(gp.size[level], scale[j]);
+        uint32_t n = 0;
+        const size_t base = (static_cast<size_t>(d) * L + level) * kMultisamples * 8;
+        auto visitor = [&](const uint32_t row, const float weight) {
+            a.rows[base + n] = row;
+            a.weights[base + n] = weight;
+            n++;
+        };
+        visit_level(gp, level, x, weighting, visitor);
+        for (uint32_t k = n; k < kMultisamples * 8; k++) {
+            a.rows[base + k] = 0u;
+            a.weights[base + k] = 0.0f;
+        }
+        a.n_groups[d * L + level] = static_cast<int32_t>(n / 8);
+    }
+}
+
+}  // namespace zf

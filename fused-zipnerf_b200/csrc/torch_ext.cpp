@@ -1,0 +1,263 @@
+// torch_ext.cpp -- the PyTorch binding ZipNeRFCudaBackend._C over the C ABI (include/zf_featurize.h).
+//
+// Mirrors the featurization part of the reference module (torch_bindings/bindings.cu:14-22): the attributes
+// grid_max_value and nerf_grid_grad_scale, set_rtc_dirs, and the class Featurizer with its constructor,
+// n_fp32_grad_rows, forward, backward and backward_mlp, with the reference's argument order and meaning
+// (featurizer.h:25-82), its tensor checks (featurizer.cu:127-138, 207-233, 276-283, 318-331) and its error text
+// (RuntimeError "ZipNeRF: ..."). Launches go to the current CUDA stream. An empty tensor skips an output, as in the
+// reference. All computation happens in libzf_featurize.so; this file only converts tensors to pointers.
+#include "zf_featurize.h"
+
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/csrc/utils/pybind.h>
+
+#include <pybind11/stl.h>
+
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace {
+
+void check_status(const int status) {
+    if (status != ZF_OK) throw std::runtime_error(zf_last_error());
+}
+
+void check_input(const at::Tensor& tensor, const char* name, const at::ScalarType dtype) {
+    if (!tensor.is_cuda() || !tensor.is_contiguous() || tensor.scalar_type() != dtype) {
+        throw std::runtime_error(std::string("ZipNeRF: ") + name + " must be a contiguous cuda tensor of the expected type");
+    }
+}
+
+// row-strided 2D tensors (e.g., column slices of a larger buffer)
+void check_rows(const at::Tensor& tensor, const char* name, const at::ScalarType dtype, const int64_t n_rows, const int64_t n_columns) {
+    if (!tensor.is_cuda() || tensor.scalar_type() != dtype || tensor.dim() != 2 || tensor.size(0) != n_rows || tensor.size(1) < n_columns || tensor.stride(1) != 1) {
+        throw std::runtime_error(std::string("ZipNeRF: ") + name + " has an invalid layout");
+    }
+}
+
+template <typename T>
+T* optional_ptr(const at::Tensor& tensor) {
+    return tensor.numel() > 0 ? reinterpret_cast<T*>(tensor.data_ptr()) : nullptr;
+}
+
+cudaStream_t current_stream() { return c10::cuda::getCurrentCUDAStream().stream(); }
+
+class Featurizer {
+public:
+    Featurizer(const int level, const std::vector<int64_t>& level_sizes, const std::vector<int64_t>& level_entries, const int n_features, const int mlp_width) {
+        if (level_sizes.size() != level_entries.size()) throw std::runtime_error("ZipNeRF: level_sizes and level_entries differ in length");
+        check_status(zf_featurizer_create(level, level_sizes.data(), level_entries.data(), static_cast<int>(level_sizes.size()), n_features, mlp_width, &m_featurizer));
+        m_n_features = n_features;
+        m_mlp_width = mlp_width;
+    }
+
+    ~Featurizer() { zf_featurizer_destroy(m_featurizer); }
+
+    Featurizer(const Featurizer&) = delete;
+    Featurizer& operator=(const Featurizer&) = delete;
+
+    int n_output_features() const { return zf_featurizer_n_output_features(m_featurizer); }
+    int64_t n_fp32_grad_rows() const { return zf_featurizer_n_fp32_grad_rows(m_featurizer); }
+
+    void forward(const at::Tensor& origins, const at::Tensor& directions, const at::Tensor& radii, const at::Tensor& tdist,
+                 const int64_t pattern_seed, const bool interleave, const at::Tensor& table, const at::Tensor& scale_magnitudes,
+                 const at::Tensor& w0, const at::Tensor& b0, const at::Tensor& w1, const at::Tensor& b1, at::Tensor& raw_density,
+                 at::Tensor& features_float, at::Tensor& features_bf16, const at::Tensor& encoded_directions, at::Tensor& nerf_inputs) {
+        zf_forward_args a{};
+        fill_rays(origins, directions, radii, tdist, pattern_seed, a.rays);
+        const int64_t n_samples = a.rays.n_rays * a.rays.n_intervals;
+        check_input(table, "table", at::kFloat);
+        check_input(scale_magnitudes, "scale_magnitudes", at::kFloat);
+        if (scale_magnitudes.numel() < static_cast<int64_t>(zf_featurizer_n_output_features(m_featurizer) / (m_n_features + 1))) {
+            throw std::runtime_error("ZipNeRF: invalid scale_magnitudes");
+        }
+        a.interleave = interleave ? 1 : 0;
+        a.table = table.data_ptr<float>();
+        a.table_rows = table.numel() / m_n_features;
+        if (table.numel() != zf_featurizer_n_rows(m_featurizer) * m_n_features) throw std::runtime_error("ZipNeRF: invalid table");
+        a.scale_magnitudes = scale_magnitudes.data_ptr<float>();
+        if (raw_density.numel() > 0) {
+            check_input(raw_density, "raw_density", at::kFloat);
+            if (raw_density.numel() != n_samples) throw std::runtime_error("ZipNeRF: invalid raw_density");
+            check_input(w0, "w0", at::kFloat);
+            if (m_mlp_width == 0 || w0.numel() != static_cast<int64_t>(m_mlp_width) * n_output_features()) throw std::runtime_error("ZipNeRF: invalid proposal mlp weights");
+            check_input(b0, "b0", at::kFloat);
+            check_input(w1, "w1", at::kFloat);
+            check_input(b1, "b1", at::kFloat);
+            if (b0.numel() != m_mlp_width || w1.numel() != m_mlp_width || b1.numel() < 1) throw std::runtime_error("ZipNeRF: invalid proposal mlp weights");
+            a.w0 = w0.data_ptr<float>();
+            a.b0 = b0.data_ptr<float>();
+            a.w1 = w1.data_ptr<float>();
+            a.b1 = b1.data_ptr<float>();
+            a.w0_numel = w0.numel();
+            a.raw_density = raw_density.data_ptr<float>();
+        }
+        if (features_float.numel() > 0) {
+            check_input(features_float, "features_float", at::kFloat);
+            if (features_float.numel() != n_samples * n_output_features()) throw std::runtime_error("ZipNeRF: invalid features_float");
+            a.features_float = features_float.data_ptr<float>();
+        }
+        if (features_bf16.numel() > 0) {
+            check_input(features_bf16, "features_bf16", at::kBFloat16);
+            if (features_bf16.dim() != 2 || features_bf16.size(0) != n_samples || features_bf16.size(1) < n_output_features()) {
+                throw std::runtime_error("ZipNeRF: invalid features_bf16");
+            }
+            a.features_bf16 = reinterpret_cast<uint16_t*>(features_bf16.data_ptr());
+            a.features_bf16_width = features_bf16.size(1);
+        }
+        if (nerf_inputs.numel() > 0) {
+            check_input(nerf_inputs, "nerf_inputs", at::kBFloat16);
+            check_input(encoded_directions, "encoded_directions", at::kBFloat16);
+            if (nerf_inputs.dim() != 2 || encoded_directions.dim() != 2 || nerf_inputs.size(0) != n_samples || nerf_inputs.size(1) < encoded_directions.size(1) ||
+                encoded_directions.size(0) != a.rays.n_rays) {
+                throw std::runtime_error("ZipNeRF: invalid nerf_inputs");
+            }
+            a.nerf_inputs = reinterpret_cast<uint16_t*>(nerf_inputs.data_ptr());
+            a.nerf_inputs_width = nerf_inputs.size(1);
+            a.encoded_directions = reinterpret_cast<const uint16_t*>(encoded_directions.data_ptr());
+            a.encoded_width = encoded_directions.size(1);
+        }
+        if (n_samples == 0) return;
+        const c10::cuda::CUDAGuard guard(origins.device());
+        check_status(zf_featurize_forward(m_featurizer, &a, current_stream()));
+    }
+
+    void backward(const at::Tensor& origins, const at::Tensor& directions, const at::Tensor& radii, const at::Tensor& tdist, const int64_t pattern_seed,
+                  const at::Tensor& grad_features, at::Tensor& grad_table, at::Tensor& grad_table_half) {
+        check_input(grad_table, "grad_table", at::kFloat);
+        check_input(grad_table_half, "grad_table_half", at::kHalf);
+        const int64_t split = n_fp32_grad_rows();
+        const int64_t rows = zf_featurizer_n_rows(m_featurizer);
+        if (grad_table.numel() != split * m_n_features || grad_table_half.numel() != (rows - split) * m_n_features) {
+            throw std::runtime_error("ZipNeRF: invalid grid gradient split");
+        }
+        zf_backward_args a{};
+        fill_rays(origins, directions, radii, tdist, pattern_seed, a.rays);
+        const int64_t n_samples = a.rays.n_rays * a.rays.n_intervals;
+        check_rows(grad_features, "grad_features", at::kBFloat16, n_samples, n_output_features());
+        if (n_samples == 0) return;
+        a.grad_features = reinterpret_cast<const uint16_t*>(grad_features.data_ptr());
+        a.grad_features_cols = grad_features.size(1);
+        a.grad_features_stride = grad_features.stride(0);
+        a.grad_table = optional_ptr<float>(grad_table);
+        a.grad_table_numel = grad_table.numel();
+        a.grad_table_half = optional_ptr<uint16_t>(grad_table_half);
+        a.grad_table_half_numel = grad_table_half.numel();
+        const c10::cuda::CUDAGuard guard(origins.device());
+        check_status(zf_featurize_backward(m_featurizer, &a, current_stream()));
+    }
+
+    void backward_mlp(const at::Tensor& origins, const at::Tensor& directions, const at::Tensor& radii, const at::Tensor& tdist, const int64_t pattern_seed,
+                      const at::Tensor& features, const at::Tensor& grad_raw_density, const at::Tensor& w0, const at::Tensor& b0, const at::Tensor& w1,
+                      at::Tensor& grad_table, at::Tensor& grad_w0, at::Tensor& grad_b0, at::Tensor& grad_w1, at::Tensor& grad_b1) {
+        zf_backward_mlp_args a{};
+        fill_rays(origins, directions, radii, tdist, pattern_seed, a.rays);
+        const int64_t n_samples = a.rays.n_rays * a.rays.n_intervals;
+        check_input(features, "features", at::kFloat);
+        check_input(grad_raw_density, "grad_raw_density", at::kFloat);
+        if (features.numel() != n_samples * n_output_features() || grad_raw_density.numel() != n_samples) throw std::runtime_error("ZipNeRF: invalid backward_mlp inputs");
+        check_input(w0, "w0", at::kFloat);
+        check_input(b0, "b0", at::kFloat);
+        check_input(w1, "w1", at::kFloat);
+        check_input(grad_table, "grad_table", at::kFloat);
+        check_input(grad_w0, "grad_w0", at::kFloat);
+        check_input(grad_b0, "grad_b0", at::kFloat);
+        check_input(grad_w1, "grad_w1", at::kFloat);
+        check_input(grad_b1, "grad_b1", at::kFloat);
+        if (m_mlp_width == 0 || w0.numel() != static_cast<int64_t>(m_mlp_width) * n_output_features() || grad_w0.numel() != w0.numel()) {
+            throw std::runtime_error("ZipNeRF: invalid proposal mlp weights");
+        }
+        if (b0.numel() != m_mlp_width || w1.numel() != m_mlp_width || grad_b0.numel() != m_mlp_width || grad_w1.numel() != m_mlp_width || grad_b1.numel() < 1) {
+            throw std::runtime_error("ZipNeRF: invalid proposal mlp weights");
+        }
+        if (n_samples == 0) return;
+        a.features = features.data_ptr<float>();
+        a.features_numel = features.numel();
+        a.grad_raw_density = grad_raw_density.data_ptr<float>();
+        a.grad_raw_density_numel = grad_raw_density.numel();
+        a.w0 = w0.data_ptr<float>();
+        a.b0 = b0.data_ptr<float>();
+        a.w1 = w1.data_ptr<float>();
+        a.w0_numel = w0.numel();
+        a.grad_table = grad_table.data_ptr<float>();
+        a.grad_table_numel = grad_table.numel();
+        a.grad_w0 = grad_w0.data_ptr<float>();
+        a.grad_w0_numel = grad_w0.numel();
+        a.grad_b0 = grad_b0.data_ptr<float>();
+        a.grad_w1 = grad_w1.data_ptr<float>();
+        a.grad_b1 = grad_b1.data_ptr<float>();
+        const c10::cuda::CUDAGuard guard(origins.device());
+        check_status(zf_featurize_backward_mlp(m_featurizer, &a, current_stream()));
+    }
+
+    // intermediate values of the given samples (no counterpart in the reference): a dict of x [n, 6, 3],
+    // scale [n, 6], contracted [n, 6], n_groups [n, L], rows [n, L, 6, 8] (int64), weights [n, L, 6, 8]
+    pybind11::dict debug(const at::Tensor& origins, const at::Tensor& directions, const at::Tensor& radii, const at::Tensor& tdist,
+                         const int64_t pattern_seed, const at::Tensor& samples) {
+        zf_rays rays{};
+        fill_rays(origins, directions, radii, tdist, pattern_seed, rays);
+        check_input(samples, "samples", at::kInt);
+        const int64_t n = samples.numel();
+        const int L = n_output_features() / (m_n_features + 1);
+        const auto opts = origins.options();
+        at::Tensor x = at::zeros({n, 6, 3}, opts), scale = at::zeros({n, 6}, opts), weights = at::zeros({n, L, 6, 8}, opts);
+        at::Tensor contracted = at::zeros({n, 6}, opts.dtype(at::kInt)), n_groups = at::zeros({n, L}, opts.dtype(at::kInt)), rows = at::zeros({n, L, 6, 8}, opts.dtype(at::kInt));
+        const c10::cuda::CUDAGuard guard(origins.device());
+        check_status(zf_featurize_debug(m_featurizer, &rays, reinterpret_cast<const uint32_t*>(samples.data_ptr()), n, x.data_ptr<float>(), scale.data_ptr<float>(),
+                                        contracted.data_ptr<int32_t>(), n_groups.data_ptr<int32_t>(), reinterpret_cast<uint32_t*>(rows.data_ptr()),
+                                        weights.data_ptr<float>(), current_stream()));
+        pybind11::dict out;
+        out["x"] = x;
+        out["scale"] = scale;
+        out["contracted"] = contracted;
+        out["n_groups"] = n_groups;
+        out["rows"] = rows.to(at::kLong).bitwise_and(0xFFFFFFFFLL);
+        out["weights"] = weights;
+        return out;
+    }
+
+private:
+    void fill_rays(const at::Tensor& origins, const at::Tensor& directions, const at::Tensor& radii, const at::Tensor& tdist, const int64_t pattern_seed, zf_rays& rays) const {
+        check_input(origins, "origins", at::kFloat);
+        check_input(directions, "directions", at::kFloat);
+        check_input(radii, "radii", at::kFloat);
+        check_input(tdist, "tdist", at::kFloat);
+        if (tdist.dim() != 2 || tdist.size(1) < 2) throw std::runtime_error("ZipNeRF: invalid tdist");
+        const int64_t n_rays = tdist.size(0);
+        if (origins.numel() != 3 * n_rays || directions.numel() != 3 * n_rays || radii.numel() != n_rays) throw std::runtime_error("ZipNeRF: invalid rays");
+        rays.origins = origins.data_ptr<float>();
+        rays.directions = directions.data_ptr<float>();
+        rays.radii = radii.data_ptr<float>();
+        rays.tdist = tdist.data_ptr<float>();
+        rays.n_rays = n_rays;
+        rays.n_intervals = tdist.size(1) - 1;
+        rays.pattern_seed = pattern_seed;
+    }
+
+    zf_featurizer* m_featurizer = nullptr;
+    int m_n_features = 0;
+    int m_mlp_width = 0;
+};
+
+// the reference compiles its featurization kernels at runtime from a source directory into a cache directory
+// (featurizer.cu:112-117); these kernels are compiled ahead of time, so the directories are accepted and unused
+void set_rtc_dirs(const std::string&, const std::string&) {}
+
+}  // namespace
+
+PYBIND11_MODULE(_C, m) {
+    m.attr("grid_max_value") = zf_grid_max_value();
+    m.attr("nerf_grid_grad_scale") = zf_nerf_grid_grad_scale();
+    m.def("set_rtc_dirs", &set_rtc_dirs);
+    pybind11::class_<Featurizer>(m, "Featurizer")
+        .def(pybind11::init<int, const std::vector<int64_t>&, const std::vector<int64_t>&, int, int>())
+        .def_property_readonly("n_fp32_grad_rows", &Featurizer::n_fp32_grad_rows)
+        .def_property_readonly("n_output_features", &Featurizer::n_output_features)
+        .def("forward", &Featurizer::forward)
+        .def("backward", &Featurizer::backward)
+        .def("backward_mlp", &Featurizer::backward_mlp)
+        .def("debug", &Featurizer::debug);
+}

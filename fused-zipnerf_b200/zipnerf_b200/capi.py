@@ -1,0 +1,167 @@
+"""ctypes binding of the C ABI in include/zf_featurize.h (libzf_featurize.so).
+
+This is the binding a non-PyTorch host would write against the library (INTEGRATION.md shows it beside the other
+language stubs). ``CFeaturizer`` adds a thin convenience layer that takes PyTorch CUDA tensors and passes their device
+pointers; the computation happens in the library. No CPU fallback exists: calls fail with ``ZfError`` when the
+library reports an error, and loading fails when the library is not built.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIBRARY = Path(__file__).resolve().parent.parent / 'ZipNeRFCudaBackend' / 'libzf_featurize.so'
+
+ZF_OK, ZF_ERROR_INVALID_ARGUMENT, ZF_ERROR_UNSUPPORTED, ZF_ERROR_CUDA = 0, 1, 2, 3
+
+EXPORTED = ['zf_featurizer_create', 'zf_featurizer_destroy', 'zf_featurizer_n_output_features', 'zf_featurizer_n_fp32_grad_rows',
+            'zf_featurizer_n_rows', 'zf_featurize_forward', 'zf_featurize_backward', 'zf_featurize_backward_mlp', 'zf_featurize_debug',
+            'zf_last_error', 'zf_grid_max_value', 'zf_nerf_grid_grad_scale']
+
+_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+
+
+class zf_rays(ctypes.Structure):
+    _fields_ = [('origins', _p), ('directions', _p), ('radii', _p), ('tdist', _p), ('n_rays', _i64), ('n_intervals', _i64),
+                ('pattern_seed', _i64)]
+
+
+class zf_forward_args(ctypes.Structure):
+    _fields_ = [('rays', zf_rays), ('interleave', ctypes.c_int), ('table', _p), ('table_rows', _i64), ('scale_magnitudes', _p),
+                ('w0', _p), ('b0', _p), ('w1', _p), ('b1', _p), ('w0_numel', _i64), ('raw_density', _p), ('features_float', _p),
+                ('features_bf16', _p), ('features_bf16_width', _i64), ('encoded_directions', _p), ('encoded_width', _i64),
+                ('nerf_inputs', _p), ('nerf_inputs_width', _i64)]
+
+
+class zf_backward_args(ctypes.Structure):
+    _fields_ = [('rays', zf_rays), ('grad_features', _p), ('grad_features_cols', _i64), ('grad_features_stride', _i64),
+                ('grad_table', _p), ('grad_table_numel', _i64), ('grad_table_half', _p), ('grad_table_half_numel', _i64)]
+
+
+class zf_backward_mlp_args(ctypes.Structure):
+    _fields_ = [('rays', zf_rays), ('features', _p), ('features_numel', _i64), ('grad_raw_density', _p),
+                ('grad_raw_density_numel', _i64), ('w0', _p), ('b0', _p), ('w1', _p), ('w0_numel', _i64), ('grad_table', _p),
+                ('grad_table_numel', _i64), ('grad_w0', _p), ('grad_w0_numel', _i64), ('grad_b0', _p), ('grad_w1', _p), ('grad_b1', _p)]
+
+
+class ZfError(RuntimeError):
+    def __init__(self, code: int, message: str) -> None:
+        super().__init__(message)
+        self.code = code
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads libzf_featurize.so (once) and declares the signatures of include/zf_featurize.h."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIBRARY.exists():
+        raise FileNotFoundError(f'{LIBRARY} is not built (python fused-zipnerf_b200/build.py)')
+    lib = ctypes.CDLL(str(LIBRARY))
+    lib.zf_featurizer_create.argtypes = [ctypes.c_int, ctypes.POINTER(_i64), ctypes.POINTER(_i64), ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_int, ctypes.POINTER(_p)]
+    lib.zf_featurizer_create.restype = ctypes.c_int
+    lib.zf_featurizer_destroy.argtypes = [_p]
+    lib.zf_featurizer_destroy.restype = None
+    lib.zf_featurizer_n_output_features.argtypes = [_p]
+    lib.zf_featurizer_n_output_features.restype = ctypes.c_int
+    lib.zf_featurizer_n_fp32_grad_rows.argtypes = [_p]
+    lib.zf_featurizer_n_fp32_grad_rows.restype = _i64
+    lib.zf_featurizer_n_rows.argtypes = [_p]
+    lib.zf_featurizer_n_rows.restype = _i64
+    lib.zf_featurize_forward.argtypes = [_p, ctypes.POINTER(zf_forward_args), _p]
+    lib.zf_featurize_backward.argtypes = [_p, ctypes.POINTER(zf_backward_args), _p]
+    lib.zf_featurize_backward_mlp.argtypes = [_p, ctypes.POINTER(zf_backward_mlp_args), _p]
+    lib.zf_featurize_debug.argtypes = [_p, ctypes.POINTER(zf_rays), _p, _i64, _p, _p, _p, _p, _p, _p, _p]
+    for name in ['zf_featurize_forward', 'zf_featurize_backward', 'zf_featurize_backward_mlp', 'zf_featurize_debug']:
+        getattr(lib, name).restype = ctypes.c_int
+    lib.zf_last_error.argtypes = []
+    lib.zf_last_error.restype = ctypes.c_char_p
+    lib.zf_grid_max_value.restype = ctypes.c_double
+    lib.zf_nerf_grid_grad_scale.restype = ctypes.c_double
+    _lib = lib
+    return lib
+
+
+def check(code: int) -> None:
+    if code != ZF_OK:
+        raise ZfError(code, load().zf_last_error().decode())
+
+
+def _ptr(tensor) -> int | None:
+    return None if tensor is None or tensor.numel() == 0 else tensor.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return stream if isinstance(stream, int) else stream.cuda_stream
+
+
+class CFeaturizer:
+    """A zf_featurizer handle with tensor-level calls (device pointers of contiguous CUDA tensors)."""
+
+    def __init__(self, level: int, sizes, entries, n_features: int, mlp_width: int) -> None:
+        lib = load()
+        n = len(sizes)
+        handle = _p()
+        check(lib.zf_featurizer_create(level, (_i64 * n)(*sizes), (_i64 * n)(*entries), n, n_features, mlp_width, ctypes.byref(handle)))
+        self.handle = handle
+        self.n_features, self.mlp_width = n_features, mlp_width
+        self.n_output_features = lib.zf_featurizer_n_output_features(handle)
+        self.n_fp32_grad_rows = lib.zf_featurizer_n_fp32_grad_rows(handle)
+        self.n_rows = lib.zf_featurizer_n_rows(handle)
+
+    def __del__(self) -> None:
+        if getattr(self, 'handle', None) and _lib is not None:
+            _lib.zf_featurizer_destroy(self.handle)
+            self.handle = None
+
+    @staticmethod
+    def rays(origins, directions, radii, tdist, pattern_seed: int) -> zf_rays:
+        return zf_rays(_ptr(origins), _ptr(directions), _ptr(radii), _ptr(tdist), tdist.shape[0], tdist.shape[1] - 1, pattern_seed)
+
+    def forward(self, origins, directions, radii, tdist, pattern_seed, interleave, table, scale_magnitudes, w0=None, b0=None, w1=None,
+                b1=None, raw_density=None, features_float=None, features_bf16=None, encoded_directions=None, nerf_inputs=None,
+                stream=None) -> None:
+        a = zf_forward_args(self.rays(origins, directions, radii, tdist, pattern_seed), int(bool(interleave)), _ptr(table),
+                            table.numel() // self.n_features, _ptr(scale_magnitudes), _ptr(w0), _ptr(b0), _ptr(w1), _ptr(b1),
+                            w0.numel() if w0 is not None else 0, _ptr(raw_density), _ptr(features_float), _ptr(features_bf16),
+                            features_bf16.shape[1] if features_bf16 is not None and features_bf16.numel() else 0,
+                            _ptr(encoded_directions), encoded_directions.shape[1] if encoded_directions is not None else 0,
+                            _ptr(nerf_inputs), nerf_inputs.shape[1] if nerf_inputs is not None and nerf_inputs.numel() else 0)
+        check(load().zf_featurize_forward(self.handle, ctypes.byref(a), _stream(stream)))
+
+    def backward(self, origins, directions, radii, tdist, pattern_seed, grad_features, grad_table, grad_table_half, stream=None) -> None:
+        a = zf_backward_args(self.rays(origins, directions, radii, tdist, pattern_seed), _ptr(grad_features), grad_features.shape[1],
+                             grad_features.stride(0), _ptr(grad_table), grad_table.numel(), _ptr(grad_table_half), grad_table_half.numel())
+        check(load().zf_featurize_backward(self.handle, ctypes.byref(a), _stream(stream)))
+
+    def backward_mlp(self, origins, directions, radii, tdist, pattern_seed, features, grad_raw_density, w0, b0, w1, grad_table,
+                     grad_w0, grad_b0, grad_w1, grad_b1, stream=None) -> None:
+        a = zf_backward_mlp_args(self.rays(origins, directions, radii, tdist, pattern_seed), _ptr(features), features.numel(),
+                                 _ptr(grad_raw_density), grad_raw_density.numel(), _ptr(w0), _ptr(b0), _ptr(w1), w0.numel(),
+                                 _ptr(grad_table), grad_table.numel(), _ptr(grad_w0), grad_w0.numel(), _ptr(grad_b0), _ptr(grad_w1),
+                                 _ptr(grad_b1))
+        check(load().zf_featurize_backward_mlp(self.handle, ctypes.byref(a), _stream(stream)))
+
+    def debug(self, origins, directions, radii, tdist, pattern_seed, samples, stream=None) -> dict:
+        """Intermediate values of the given samples (int32 CUDA tensor): x, scale, contracted, n_groups, rows, weights."""
+        import torch
+        n = samples.numel()
+        L = self.n_output_features // (self.n_features + 1)
+        dev = samples.device
+        out = {'x': torch.zeros(n, 6, 3, device=dev), 'scale': torch.zeros(n, 6, device=dev),
+               'contracted': torch.zeros(n, 6, dtype=torch.int32, device=dev), 'n_groups': torch.zeros(n, L, dtype=torch.int32, device=dev),
+               'rows': torch.zeros(n, L, 6, 8, dtype=torch.int32, device=dev), 'weights': torch.zeros(n, L, 6, 8, device=dev)}
+        rays = self.rays(origins, directions, radii, tdist, pattern_seed)
+        check(load().zf_featurize_debug(self.handle, ctypes.byref(rays), _ptr(samples), n, _ptr(out['x']), _ptr(out['scale']),
+                                        _ptr(out['contracted']), _ptr(out['n_groups']), _ptr(out['rows']), _ptr(out['weights']),
+                                        _stream(stream)))
+        out['rows'] = out['rows'].to(torch.int64) & 0xFFFFFFFF
+        return out
