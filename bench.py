@@ -403,7 +403,7 @@ def run_b200(args) -> None:
     if rank == 0 and not args.skip_cpu_baseline and world == 1:
         from oracle.zf_oracle import build, n_threads_default
         build()
-        result['cpu_baseline'] = CpuBaseline(args.reference_rays, n_threads_default()).run(repeats=3)
+        result['cpu_baseline'] = CpuBaseline(args.reference_rays, n_threads_default()).run(repeats=args.reference_repeats)
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
@@ -454,7 +454,8 @@ def main() -> None:
     parser.add_argument('--warmup', type=int, default=3)
     parser.add_argument('--impl', choices=['b200', 'reference'], default='b200')
     parser.add_argument('--rays', type=int, default=65536)
-    parser.add_argument('--reference-rays', type=int, default=4096, help='ray sample of the CPU reference / baseline')
+    parser.add_argument('--reference-rays', type=int, default=16384, help='ray sample of the CPU reference / baseline')
+    parser.add_argument('--reference-repeats', type=int, default=5, help='passes over the ray sample timed for cpu_baseline')
     parser.add_argument('--skip-e2e', action='store_true')
     parser.add_argument('--skip-cpu-baseline', action='store_true')
     args = parser.parse_args()

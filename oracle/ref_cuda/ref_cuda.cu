@@ -1,0 +1,152 @@
+// ref_cuda.cu -- host launchers around the reference's own featurization kernels (TEST INFRASTRUCTURE ONLY).
+//
+// The reference compiles its featurization kernels at runtime with NVRTC (--use_fast_math, featurizer.cu:157-184,
+// rtc_kernel.cu:36-102), prepending a generated preamble of the grid layout. oracle/ref_cuda/build.py writes that
+// preamble for one layout (ZF_REF_PREAMBLE) and compiles this file with nvcc for sm_100a into
+// oracle/_ref/cuda/libzfref_<variant>.so. The kernels are the reference's, included from the sources where they lie;
+// the launchers restate the reference's host code (featurizer.cu:188-355: launch shapes, the packed-bf16 choice, the
+// backward_mlp grid and shared memory), and ref_debug adds a kernel built from the reference's device functions that
+// exports the intermediate values the reference kernels keep in registers. The GPU parity tests compare the product
+// kernels with these bit for bit, and tests/bench_vs_reference_cuda.py times both.
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include ZF_REF_PREAMBLE
+#include "random.cuh"
+#include "featurize_common.cuh"
+#if JIT_MLP_WIDTH > 0
+#include "featurize_forward.cu"
+#include "featurize_backward_mlp.cu"
+#else
+#include "featurize_forward.cu"
+#include "featurize_forward_bf16.cu"
+#include "featurize_backward.cu"
+#endif
+
+#define REF_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+constexpr int launch_block = 128;           // featurizer.h:14
+constexpr int backward_mlp_blocks_per_sm = 8;  // featurizer.h:15
+unsigned n_blocks(const int64_t n) { return static_cast<unsigned>((n + launch_block - 1) / launch_block); }
+bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+}
+
+// featurizer.cu:188-264 (arguments as the reference passes them; null pointers for skipped outputs)
+REF_API int ref_forward(const float* origins, const float* directions, const float* radii, const float* tdist, int64_t n_rays, int64_t n_intervals,
+                        long long pattern_seed, int interleave, const float* table, const float* scale_magnitudes, const float* w0, const float* b0,
+                        const float* w1, const float* b1, float* raw_density, float* features_float, uint16_t* features_bf16, int features_bf16_width,
+                        const uint16_t* encoded_directions, int encoded_width, uint16_t* nerf_inputs, int nerf_inputs_width, cudaStream_t stream) {
+    const int64_t n_samples = n_rays * n_intervals;
+    if (n_samples == 0) return 0;
+#if JIT_MLP_WIDTH > 0
+    featurize_forward<<<n_blocks(n_samples), launch_block, 0, stream>>>(
+        reinterpret_cast<const float3*>(origins), reinterpret_cast<const float3*>(directions), radii, tdist, pattern_seed, interleave != 0, table,
+        scale_magnitudes, raw_density ? w0 : nullptr, raw_density ? b0 : nullptr, raw_density ? w1 : nullptr, raw_density ? b1 : nullptr, raw_density,
+        features_float, features_bf16, features_bf16 ? features_bf16_width : 0, nerf_inputs ? encoded_directions : nullptr, nerf_inputs,
+        nerf_inputs ? nerf_inputs_width : 0, nerf_inputs ? encoded_width : 0, static_cast<uint32_t>(n_samples), static_cast<uint32_t>(n_intervals));
+#else
+    const bool packed = features_float == nullptr && features_bf16 != nullptr && features_bf16_width % 8 == 0 && aligned16(features_bf16) &&
+        (nerf_inputs == nullptr || (nerf_inputs_width % 8 == 0 && encoded_width % 8 == 0 && aligned16(nerf_inputs) && aligned16(encoded_directions)));
+    auto kernel = packed ? featurize_forward_bf16 : featurize_forward;
+    kernel<<<n_blocks(n_samples), launch_block, 0, stream>>>(
+        reinterpret_cast<const float3*>(origins), reinterpret_cast<const float3*>(directions), radii, tdist, pattern_seed, interleave != 0, table,
+        scale_magnitudes, nullptr, nullptr, nullptr, nullptr, raw_density, features_float, features_bf16, features_bf16 ? features_bf16_width : 0,
+        nerf_inputs ? encoded_directions : nullptr, nerf_inputs, nerf_inputs ? nerf_inputs_width : 0, nerf_inputs ? encoded_width : 0,
+        static_cast<uint32_t>(n_samples), static_cast<uint32_t>(n_intervals));
+#endif
+    return static_cast<int>(cudaGetLastError());
+}
+
+// featurizer.cu:266-299
+REF_API int ref_backward(const float* origins, const float* directions, const float* radii, const float* tdist, int64_t n_rays, int64_t n_intervals,
+                         long long pattern_seed, const uint16_t* grad_features, int grad_stride, float* grad_table, uint16_t* grad_table_half,
+                         cudaStream_t stream) {
+#if JIT_MLP_WIDTH > 0
+    return -1;
+#else
+    const int64_t n_samples = n_rays * n_intervals;
+    if (n_samples == 0) return 0;
+    featurize_backward<<<n_blocks(n_samples), launch_block, 0, stream>>>(
+        reinterpret_cast<const float3*>(origins), reinterpret_cast<const float3*>(directions), radii, tdist, pattern_seed, grad_features, grad_stride,
+        1048576.0f, grad_table, grad_table_half, static_cast<uint32_t>(n_samples), static_cast<uint32_t>(n_intervals));
+    return static_cast<int>(cudaGetLastError());
+#endif
+}
+
+// featurizer.cu:301-355
+REF_API int ref_backward_mlp(const float* origins, const float* directions, const float* radii, const float* tdist, int64_t n_rays, int64_t n_intervals,
+                             long long pattern_seed, const float* features, const float* grad_raw_density, const float* w0, const float* b0,
+                             const float* w1, float* grad_table, float* grad_w0, float* grad_b0, float* grad_w1, float* grad_b1, cudaStream_t stream) {
+#if JIT_MLP_WIDTH > 0
+    const int64_t n_samples = n_rays * n_intervals;
+    if (n_samples == 0) return 0;
+    int device, n_sms;
+    cudaGetDevice(&device);
+    cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, device);
+    const unsigned blocks = std::min(n_blocks(n_samples), static_cast<unsigned>(n_sms * backward_mlp_blocks_per_sm));
+    const unsigned shmem = launch_block * (JIT_MLP_WIDTH + zipnerf::n_output_features + 1) * sizeof(float);
+    featurize_backward_mlp<<<blocks, launch_block, shmem, stream>>>(
+        reinterpret_cast<const float3*>(origins), reinterpret_cast<const float3*>(directions), radii, tdist, pattern_seed, features, grad_raw_density,
+        w0, b0, w1, grad_table, grad_w0, grad_b0, grad_w1, grad_b1, static_cast<uint32_t>(n_samples), static_cast<uint32_t>(n_intervals));
+    return static_cast<int>(cudaGetLastError());
+#else
+    return -1;
+#endif
+}
+
+// intermediate values of the listed samples from the reference's device functions (no counterpart kernel in the
+// reference): x [n, 6, 3], scale [n, 6], n_groups [n, L], rows / weights [n, L, 6, 8] in visit order
+__global__ void ref_debug_kernel(const float3* origins, const float3* directions, const float* radii, const float* tdist, long long pattern_seed,
+                                 uint32_t n_intervals, const uint32_t* samples, uint32_t n_debug, float* x_out, float* scale_out, int32_t* n_groups,
+                                 uint32_t* rows, float* weights) {
+    using namespace zipnerf;
+    const uint32_t d = blockIdx.x * blockDim.x + threadIdx.x;
+    if (d >= n_debug) return;
+    const RayInterval interval = setup_interval(origins, directions, radii, tdist, pattern_seed, samples[d], n_intervals);
+    float3 x[n_multisamples];
+    float scale[n_multisamples];
+    for (uint32_t j = 0; j < n_multisamples; j++) {
+        multisample(interval, j, x[j], scale[j]);
+        x_out[(d * n_multisamples + j) * 3] = x[j].x;
+        x_out[(d * n_multisamples + j) * 3 + 1] = x[j].y;
+        x_out[(d * n_multisamples + j) * 3 + 2] = x[j].z;
+        scale_out[d * n_multisamples + j] = scale[j];
+    }
+    #pragma unroll
+    for (uint32_t level = 0; level < JIT_N_LEVELS; level++) {
+        float weighting[n_multisamples];
+        for (uint32_t j = 0; j < n_multisamples; j++) weighting[j] = level_weighting(level, scale[j]);
+        uint32_t n = 0;
+        const size_t base = (static_cast<size_t>(d) * JIT_N_LEVELS + level) * n_multisamples * 8;
+        auto visitor = [&](const uint32_t row, const float weight) {
+            rows[base + n] = row;
+            weights[base + n] = weight;
+            n++;
+        };
+        visit_level_corners(level, x, weighting, visitor);
+        for (uint32_t k = n; k < n_multisamples * 8; k++) {
+            rows[base + k] = 0u;
+            weights[base + k] = 0.0f;
+        }
+        n_groups[d * JIT_N_LEVELS + level] = static_cast<int32_t>(n / 8);
+    }
+}
+
+REF_API int ref_debug(const float* origins, const float* directions, const float* radii, const float* tdist, int64_t n_intervals, long long pattern_seed,
+                      const uint32_t* samples, int64_t n_debug, float* x, float* scale, int32_t* n_groups, uint32_t* rows, float* weights,
+                      cudaStream_t stream) {
+    if (n_debug == 0) return 0;
+    ref_debug_kernel<<<static_cast<unsigned>((n_debug + 63) / 64), 64, 0, stream>>>(
+        reinterpret_cast<const float3*>(origins), reinterpret_cast<const float3*>(directions), radii, tdist, pattern_seed,
+        static_cast<uint32_t>(n_intervals), samples, static_cast<uint32_t>(n_debug), x, scale, n_groups, rows, weights);
+    return static_cast<int>(cudaGetLastError());
+}
+
+REF_API int ref_layout(int* n_levels, int* n_features, int* mlp_width, int* n_fp32_grad_levels) {
+    *n_levels = JIT_N_LEVELS;
+    *n_features = JIT_N_FEATURES;
+    *mlp_width = JIT_MLP_WIDTH;
+    *n_fp32_grad_levels = JIT_N_FP32_GRAD_LEVELS;
+    return 0;
+}
