@@ -31,6 +31,8 @@ MAX_LEVELS, MAX_FEATURES = 16, 4
 NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')
 NVCC_FLAGS = ['-gencode', 'arch=compute_100a,code=sm_100a', '-O3', '--use_fast_math', '-lineinfo', '-std=c++17',
               '-Xcompiler', '-fPIC', '-Xcompiler', '-fvisibility=hidden', f'-I{INCLUDE}', f'-I{CSRC}']
+# extra nvcc flags for tuning builds (e.g. ZF_NVCC_EXTRA="-DZF_MIN_BLOCKS=6")
+NVCC_FLAGS += os.environ.get('ZF_NVCC_EXTRA', '').split()
 
 
 def _headers() -> list[Path]:

@@ -174,44 +174,56 @@ __device__ __forceinline__ uint32_t corner_row(const GridParams& gp, const uint3
 }
 
 // Visits the merged corner groups of one level: visitor(row, weight) for the 8 corners of every group, groups in
-// the order of their first multisample, corners in the order (x, y, z) bit 2, 1, 0.
+// the order of their first multisample, corners in the order (x, y, z) bit 2, 1, 0. Multisamples in the same cell
+// form one group whose corner weights are summed in multisample order, exactly as featurize_common.cuh:137-172 does;
+// here each lane loops over its own groups (lowest unvisited multisample first), so a warp issues the corner work of
+// max(groups) groups instead of all 21 (leader, member) pairs of the fully unrolled merge.
 template <typename Visitor>
 __device__ __forceinline__ void visit_level(const GridParams& gp, const uint32_t level, const float3* x, const float* weighting, Visitor& visitor) {
     const uint32_t size = gp.size[level];
-    int cells[kMultisamples][3];
-    float fractions[kMultisamples][3];
+    int cx[kMultisamples], cy[kMultisamples], cz[kMultisamples];
+    float fx[kMultisamples], fy[kMultisamples], fz[kMultisamples];
     #pragma unroll
     for (uint32_t j = 0; j < kMultisamples; j++) {
-        const float p[3] = {x[j].x * size - 0.5f, x[j].y * size - 0.5f, x[j].z * size - 0.5f};
-        #pragma unroll
-        for (uint32_t d = 0; d < 3; d++) {
-            const float floored = floorf(p[d]);
-            cells[j][d] = static_cast<int>(floored);
-            fractions[j][d] = p[d] - floored;
-        }
+        const float px = x[j].x * size - 0.5f, py = x[j].y * size - 0.5f, pz = x[j].z * size - 0.5f;
+        const float gx = floorf(px), gy = floorf(py), gz = floorf(pz);
+        cx[j] = static_cast<int>(gx);
+        cy[j] = static_cast<int>(gy);
+        cz[j] = static_cast<int>(gz);
+        fx[j] = px - gx;
+        fy[j] = py - gy;
+        fz[j] = pz - gz;
     }
-    uint32_t merged = 0;
-    #pragma unroll
-    for (uint32_t j = 0; j < kMultisamples; j++) {
-        if (merged & (1u << j)) continue;
+    uint32_t remaining = (1u << kMultisamples) - 1u;
+    while (remaining != 0u) {
+        const uint32_t leader = __ffs(remaining) - 1u;
+        int lx = cx[0], ly = cy[0], lz = cz[0];
+        #pragma unroll
+        for (uint32_t j = 1; j < kMultisamples; j++) {
+            if (leader == j) {
+                lx = cx[j];
+                ly = cy[j];
+                lz = cz[j];
+            }
+        }
         float corner_weights[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
         #pragma unroll
-        for (uint32_t k = j; k < kMultisamples; k++) {
-            if (cells[k][0] != cells[j][0] || cells[k][1] != cells[j][1] || cells[k][2] != cells[j][2]) continue;
-            merged |= 1u << k;
+        for (uint32_t k = 0; k < kMultisamples; k++) {
+            if (!((remaining >> k) & 1u) || cx[k] != lx || cy[k] != ly || cz[k] != lz) continue;
+            remaining &= ~(1u << k);
             #pragma unroll
             for (uint32_t corner = 0; corner < 8; corner++) {
-                const float wx = corner & 4u ? fractions[k][0] : 1.0f - fractions[k][0];
-                const float wy = corner & 2u ? fractions[k][1] : 1.0f - fractions[k][1];
-                const float wz = corner & 1u ? fractions[k][2] : 1.0f - fractions[k][2];
+                const float wx = corner & 4u ? fx[k] : 1.0f - fx[k];
+                const float wy = corner & 2u ? fy[k] : 1.0f - fy[k];
+                const float wz = corner & 1u ? fz[k] : 1.0f - fz[k];
                 corner_weights[corner] += weighting[k] * (wx * wy * wz);
             }
         }
         #pragma unroll
         for (uint32_t corner = 0; corner < 8; corner++) {
             float weight = corner_weights[corner];
-            const uint32_t row = corner_row(gp, level, cells[j][0] + static_cast<int>((corner >> 2) & 1u),
-                                            cells[j][1] + static_cast<int>((corner >> 1) & 1u), cells[j][2] + static_cast<int>(corner & 1u), weight);
+            const uint32_t row = corner_row(gp, level, lx + static_cast<int>((corner >> 2) & 1u), ly + static_cast<int>((corner >> 1) & 1u),
+                                            lz + static_cast<int>(corner & 1u), weight);
             visitor(row, weight);
         }
     }

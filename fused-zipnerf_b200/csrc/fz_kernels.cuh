@@ -13,6 +13,9 @@
 namespace zf {
 
 constexpr int kBlock = 128;
+#ifndef ZF_MIN_BLOCKS
+#define ZF_MIN_BLOCKS 1  // minimum resident blocks per SM the register allocation must allow (__launch_bounds__)
+#endif
 constexpr int kWarps = kBlock / 32;
 
 // odd row stride (in floats) of per-thread rows in shared memory: lanes writing the same column hit distinct banks
@@ -174,7 +177,7 @@ __device__ __forceinline__ void store_inputs_tail(const Args& a, const uint32_t*
 // Forward. NOUT_PAD == 0: no MLP; otherwise the fused density MLP n_out -> W (ReLU) -> 1 runs for raw_density, with
 // the features in registers (NOUT_PAD >= n_out) and the reference's accumulation order (featurize_forward.cu:65-73).
 template <int F, int NOUT_PAD>
-__global__ void __launch_bounds__(kBlock) fz_forward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ ForwardArgs a) {
+__global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS) fz_forward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ ForwardArgs a) {
     const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
     const int stride = staged_stride(n_out);
     extern __shared__ __align__(16) float smem[];
@@ -328,7 +331,7 @@ struct BackwardArgs {
 };
 
 template <int F>
-__global__ void __launch_bounds__(kBlock) fz_backward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardArgs a) {
+__global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS) fz_backward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardArgs a) {
     const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
     const int stride = staged_stride(n_out);
     extern __shared__ __align__(16) float smem[];
@@ -379,14 +382,15 @@ struct BackwardMlpArgs {
 __host__ __device__ constexpr int backward_mlp_smem_floats(const int n_out, const int nout_pad, const int width) {
     return width * nout_pad + 2 * width                // weights (w0 rows padded to nout_pad)
         + (width * n_out + 2 * width + 1)              // per-block parameter gradient sums
-        + kBlock * (width + staged_stride(n_out) + 1); // per-step pre-activations, feature rows, raw density gradients
+        + kBlock * ((width | 1) + staged_stride(n_out) + 1); // per-step pre-activations, feature rows, raw density gradients
 }
 
 template <int F, int NOUT_PAD>
-__global__ void __launch_bounds__(kBlock) fz_backward_mlp_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardMlpArgs a) {
+__global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS) fz_backward_mlp_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardMlpArgs a) {
     const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
     const int stride = staged_stride(n_out);
     const int W = a.mlp_width;
+    const int pre_stride = W | 1;              // odd: lanes writing their own rows hit distinct banks
     const int n_w0 = W * n_out;
     const int n_params = n_w0 + 2 * W + 1;
     extern __shared__ __align__(16) float smem[];
@@ -394,8 +398,8 @@ __global__ void __launch_bounds__(kBlock) fz_backward_mlp_kernel(const __grid_co
     float* s_b0 = s_w0 + W * NOUT_PAD;
     float* s_w1 = s_b0 + W;
     float* s_acc = s_w1 + W;                   // [n_params]
-    float* s_pre = s_acc + n_params;           // [kBlock, W]
-    float* s_rows = s_pre + kBlock * W;        // [kBlock, stride]: the scaled feature gradient, then the features
+    float* s_pre = s_acc + n_params;           // [kBlock, pre_stride]
+    float* s_rows = s_pre + kBlock * pre_stride;  // [kBlock, stride]: the scaled feature gradient, then the features
     float* s_g = s_rows + kBlock * stride;     // [kBlock]
     for (int i = threadIdx.x; i < W * NOUT_PAD; i += kBlock) {
         const int j = i / NOUT_PAD, c = i - j * NOUT_PAD;
@@ -431,7 +435,7 @@ __global__ void __launch_bounds__(kBlock) fz_backward_mlp_kernel(const __grid_co
                 if (4 * q + 2 < n_out) pre += wq.z * f[4 * q + 2];
                 if (4 * q + 3 < n_out) pre += wq.w * f[4 * q + 3];
             }
-            s_pre[threadIdx.x * W + j] = pre;
+            s_pre[threadIdx.x * pre_stride + j] = pre;
             if (pre > 0.0f) {
                 const float grad_pre = g * s_w1[j];
                 #pragma unroll
@@ -465,18 +469,18 @@ __global__ void __launch_bounds__(kBlock) fz_backward_mlp_kernel(const __grid_co
             if (q < n_w0) {
                 const int j = q / n_out, i = q - j * n_out;
                 for (int s = 0; s < kBlock; s++) {
-                    if (s_pre[s * W + j] > 0.0f) sum += s_g[s] * s_rows[s * stride + i];
+                    if (s_pre[s * pre_stride + j] > 0.0f) sum += s_g[s] * s_rows[s * stride + i];
                 }
             }
             else if (q < n_w0 + W) {
                 const int j = q - n_w0;
                 for (int s = 0; s < kBlock; s++) {
-                    if (s_pre[s * W + j] > 0.0f) sum += s_g[s];
+                    if (s_pre[s * pre_stride + j] > 0.0f) sum += s_g[s];
                 }
             }
             else if (q < n_w0 + 2 * W) {
                 const int j = q - n_w0 - W;
-                for (int s = 0; s < kBlock; s++) sum += s_g[s] * fmaxf(s_pre[s * W + j], 0.0f);
+                for (int s = 0; s < kBlock; s++) sum += s_g[s] * fmaxf(s_pre[s * pre_stride + j], 0.0f);
             }
             else {
                 for (int s = 0; s < kBlock; s++) sum += s_g[s];
