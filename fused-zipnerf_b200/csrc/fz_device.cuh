@@ -177,7 +177,9 @@ __device__ __forceinline__ uint32_t corner_row(const GridParams& gp, const uint3
 // the order of their first multisample, corners in the order (x, y, z) bit 2, 1, 0. Multisamples in the same cell
 // form one group whose corner weights are summed in multisample order, exactly as featurize_common.cuh:137-172 does;
 // here each lane loops over its own groups (lowest unvisited multisample first), so a warp issues the corner work of
-// max(groups) groups instead of all 21 (leader, member) pairs of the fully unrolled merge.
+// max(groups) groups instead of all 21 (leader, member) pairs of the fully unrolled merge. The roundings are explicit
+// (a fused multiply-add of the weighting into the sum of (wx wy) wz products), which reproduces the reference
+// kernels' corner weights bit for bit independently of how the surrounding code is scheduled.
 template <typename Visitor>
 __device__ __forceinline__ void visit_level(const GridParams& gp, const uint32_t level, const float3* x, const float* weighting, Visitor& visitor) {
     const uint32_t size = gp.size[level];
@@ -216,7 +218,7 @@ __device__ __forceinline__ void visit_level(const GridParams& gp, const uint32_t
                 const float wx = corner & 4u ? fx[k] : 1.0f - fx[k];
                 const float wy = corner & 2u ? fy[k] : 1.0f - fy[k];
                 const float wz = corner & 1u ? fz[k] : 1.0f - fz[k];
-                corner_weights[corner] += weighting[k] * (wx * wy * wz);
+                corner_weights[corner] = __fmaf_rn(weighting[k], __fmul_rn(__fmul_rn(wx, wy), wz), corner_weights[corner]);
             }
         }
         #pragma unroll

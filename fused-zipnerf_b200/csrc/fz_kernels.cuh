@@ -13,8 +13,16 @@
 namespace zf {
 
 constexpr int kBlock = 128;
-#ifndef ZF_MIN_BLOCKS
-#define ZF_MIN_BLOCKS 1  // minimum resident blocks per SM the register allocation must allow (__launch_bounds__)
+// minimum resident blocks per SM each kernel's register allocation must allow (__launch_bounds__): the forward is
+// latency bound on its gathers and gains from occupancy; the backwards keep their registers (atomics, MLP)
+#ifndef ZF_MIN_BLOCKS_FORWARD
+#define ZF_MIN_BLOCKS_FORWARD 6
+#endif
+#ifndef ZF_MIN_BLOCKS_BACKWARD
+#define ZF_MIN_BLOCKS_BACKWARD 1
+#endif
+#ifndef ZF_MIN_BLOCKS_BACKWARD_MLP
+#define ZF_MIN_BLOCKS_BACKWARD_MLP 1
 #endif
 constexpr int kWarps = kBlock / 32;
 
@@ -53,21 +61,22 @@ struct GatherRows {
 
     __device__ __forceinline__ void operator()(const uint32_t row, const float weight) {
         if (weight == 0.0f) return;
+        // fused multiply-adds, as the reference's feature gather (featurize_common.cuh:179-198)
         if constexpr (F == 4) {
             const float4 t = __ldg(reinterpret_cast<const float4*>(table) + row);
-            value[0] += weight * t.x;
-            value[1] += weight * t.y;
-            value[2] += weight * t.z;
-            value[3] += weight * t.w;
+            value[0] = __fmaf_rn(weight, t.x, value[0]);
+            value[1] = __fmaf_rn(weight, t.y, value[1]);
+            value[2] = __fmaf_rn(weight, t.z, value[2]);
+            value[3] = __fmaf_rn(weight, t.w, value[3]);
         }
         else if constexpr (F == 2) {
             const float2 t = __ldg(reinterpret_cast<const float2*>(table) + row);
-            value[0] += weight * t.x;
-            value[1] += weight * t.y;
+            value[0] = __fmaf_rn(weight, t.x, value[0]);
+            value[1] = __fmaf_rn(weight, t.y, value[1]);
         }
         else {
             #pragma unroll
-            for (int f = 0; f < F; f++) value[f] += weight * __ldg(table + row * F + f);
+            for (int f = 0; f < F; f++) value[f] = __fmaf_rn(weight, __ldg(table + row * F + f), value[f]);
         }
     }
 };
@@ -177,7 +186,7 @@ __device__ __forceinline__ void store_inputs_tail(const Args& a, const uint32_t*
 // Forward. NOUT_PAD == 0: no MLP; otherwise the fused density MLP n_out -> W (ReLU) -> 1 runs for raw_density, with
 // the features in registers (NOUT_PAD >= n_out) and the reference's accumulation order (featurize_forward.cu:65-73).
 template <int F, int NOUT_PAD>
-__global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS) fz_forward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ ForwardArgs a) {
+__global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_FORWARD) fz_forward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ ForwardArgs a) {
     const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
     const int stride = staged_stride(n_out);
     extern __shared__ __align__(16) float smem[];
@@ -221,12 +230,12 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS) fz_forward_kernel(const
                 #pragma unroll
                 for (int q = 0; q < NOUT_PAD / 4; q++) {
                     const float4 wq = w[q];
-                    if (4 * q < n_out) pre += wq.x * f[4 * q];
-                    if (4 * q + 1 < n_out) pre += wq.y * f[4 * q + 1];
-                    if (4 * q + 2 < n_out) pre += wq.z * f[4 * q + 2];
-                    if (4 * q + 3 < n_out) pre += wq.w * f[4 * q + 3];
+                    if (4 * q < n_out) pre = __fmaf_rn(wq.x, f[4 * q], pre);
+                    if (4 * q + 1 < n_out) pre = __fmaf_rn(wq.y, f[4 * q + 1], pre);
+                    if (4 * q + 2 < n_out) pre = __fmaf_rn(wq.z, f[4 * q + 2], pre);
+                    if (4 * q + 3 < n_out) pre = __fmaf_rn(wq.w, f[4 * q + 3], pre);
                 }
-                raw += s_w1[j] * fmaxf(pre, 0.0f);
+                raw = __fmaf_rn(s_w1[j], fmaxf(pre, 0.0f), raw);
             }
             a.raw_density[sample] = raw;
         }
@@ -285,11 +294,11 @@ __device__ __forceinline__ void add_row_f16(uint16_t* __restrict__ grad_table, c
     }
 }
 
-// scatters one interval's feature gradient (g_row[l (F + 1) + f]; scale features carry none) into the grid gradient:
-// levels below n_fp32 into grad_table (fp32), the others into grad_table_half (fp16, rows re-based at the first fp16
-// level) (featurize_common.cuh:273-291)
+// scatters one interval's feature gradient (g_row[(l (F + 1) + f) g_stride]; scale features carry none) into the grid
+// gradient: levels below n_fp32 into grad_table (fp32), the others into grad_table_half (fp16, rows re-based at the
+// first fp16 level) (featurize_common.cuh:273-291)
 template <int F>
-__device__ __forceinline__ void scatter_row(const GridParams& gp, const Frustum& fr, const float* g_row, const uint32_t n_fp32,
+__device__ __forceinline__ void scatter_row(const GridParams& gp, const Frustum& fr, const float* g_row, const int g_stride, const uint32_t n_fp32,
                                             float* __restrict__ grad_table, uint16_t* __restrict__ grad_table_half) {
     float3 x[kMultisamples];
     float scale[kMultisamples];
@@ -302,7 +311,7 @@ __device__ __forceinline__ void scatter_row(const GridParams& gp, const Frustum&
         for (uint32_t j = 0; j < kMultisamples; j++) weighting[j] = level_weighting(gp.size[level], scale[j]);
         float g[F];
         #pragma unroll
-        for (int f = 0; f < F; f++) g[f] = g_row[level * (F + 1) + f];
+        for (int f = 0; f < F; f++) g[f] = g_row[(level * (F + 1) + f) * g_stride];
         if (level < n_fp32) {
             auto visitor = [&](const uint32_t row, const float weight) {
                 if (weight != 0.0f) add_row_f32<F>(grad_table, row, weight, g);
@@ -331,7 +340,7 @@ struct BackwardArgs {
 };
 
 template <int F>
-__global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS) fz_backward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardArgs a) {
+__global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardArgs a) {
     const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
     const int stride = staged_stride(n_out);
     extern __shared__ __align__(16) float smem[];
@@ -351,7 +360,7 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS) fz_backward_kernel(cons
     if (lane >= n_rows) return;
     const uint32_t sample = warp_first + lane;
     const Frustum fr = setup_frustum(a.in, gp.pattern_stream, sample);
-    scatter_row<F>(gp, fr, warp_rows + lane * stride, gp.n_fp32_levels, a.grad_table, a.grad_table_half);
+    scatter_row<F>(gp, fr, warp_rows + lane * stride, 1, gp.n_fp32_levels, a.grad_table, a.grad_table_half);
 }
 
 __host__ __device__ constexpr int backward_smem_floats(const int n_out) { return kBlock * staged_stride(n_out); }
@@ -378,29 +387,33 @@ struct BackwardMlpArgs {
     float* grad_b1;
 };
 
-// dynamic shared memory of fz_backward_mlp_kernel in floats
+// Shared memory of fz_backward_mlp_kernel in floats. Per-sample columns ([row][sample], row stride kBlock + 1) make
+// both the per-thread writes of phase 1 and the tile reads of phase 2 bank-conflict free.
+__host__ __device__ constexpr int column_stride() { return kBlock + 1; }
 __host__ __device__ constexpr int backward_mlp_smem_floats(const int n_out, const int nout_pad, const int width) {
-    return width * nout_pad + 2 * width                // weights (w0 rows padded to nout_pad)
-        + (width * n_out + 2 * width + 1)              // per-block parameter gradient sums
-        + kBlock * ((width | 1) + staged_stride(n_out) + 1); // per-step pre-activations, feature rows, raw density gradients
+    return width * nout_pad + 2 * width                       // weights (w0 rows padded to nout_pad), b0, w1
+        + (width * n_out + 2 * width + 1)                     // parameter gradient sums of the block
+        + ((width + 3) / 4 * 4) * column_stride()             // pre-activations [j][sample]
+        + nout_pad * column_stride()                          // feature gradient, then features [i][sample]
+        + kBlock;                                             // raw density gradients
 }
 
 template <int F, int NOUT_PAD>
-__global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS) fz_backward_mlp_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardMlpArgs a) {
+__global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_backward_mlp_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardMlpArgs a) {
+    constexpr int cs = column_stride();
     const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
-    const int stride = staged_stride(n_out);
     const int W = a.mlp_width;
-    const int pre_stride = W | 1;              // odd: lanes writing their own rows hit distinct banks
+    const int w_pad = (W + 3) / 4 * 4;
     const int n_w0 = W * n_out;
     const int n_params = n_w0 + 2 * W + 1;
     extern __shared__ __align__(16) float smem[];
     float* s_w0 = smem;                        // [W, NOUT_PAD]
     float* s_b0 = s_w0 + W * NOUT_PAD;
     float* s_w1 = s_b0 + W;
-    float* s_acc = s_w1 + W;                   // [n_params]
-    float* s_pre = s_acc + n_params;           // [kBlock, pre_stride]
-    float* s_rows = s_pre + kBlock * pre_stride;  // [kBlock, stride]: the scaled feature gradient, then the features
-    float* s_g = s_rows + kBlock * stride;     // [kBlock]
+    float* s_acc = s_w1 + W;                   // [n_params] (the reference's output order: w0, b0, w1, b1)
+    float* s_pre = s_acc + n_params;           // [w_pad][cs]
+    float* s_col = s_pre + w_pad * cs;         // [NOUT_PAD][cs]
+    float* s_g = s_col + NOUT_PAD * cs;        // [kBlock]
     for (int i = threadIdx.x; i < W * NOUT_PAD; i += kBlock) {
         const int j = i / NOUT_PAD, c = i - j * NOUT_PAD;
         s_w0[i] = c < n_out ? __ldg(a.w0 + j * n_out + c) : 0.0f;
@@ -410,11 +423,16 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS) fz_backward_mlp_kernel(
         s_w1[i] = __ldg(a.w1 + i);
     }
     for (int i = threadIdx.x; i < n_params; i += kBlock) s_acc[i] = 0.0f;
+    // padding rows of the pre-activations stay non-positive (they select no gradient)
+    for (int i = threadIdx.x; i < (w_pad - W) * cs; i += kBlock) s_pre[W * cs + i] = 0.0f;
     __syncthreads();
-    float* row = s_rows + threadIdx.x * stride;
+    const int n_tiles = (w_pad / 4) * (NOUT_PAD / 4);
+    const int n_items = n_tiles + 2 * W + 1;
 
     // block-uniform loop bound, so every thread reaches the barriers
     for (uint32_t base = blockIdx.x * kBlock; base < a.in.n_samples; base += gridDim.x * kBlock) {
+        // phase 1, one sample per thread: MLP recomputation (featurize_backward_mlp.cu:82-99), the input gradient, and
+        // its scatter into the grid gradient
         const uint32_t sample = base + threadIdx.x;
         const bool active = sample < a.in.n_samples;
         float f[NOUT_PAD];
@@ -430,66 +448,94 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS) fz_backward_mlp_kernel(
             #pragma unroll
             for (int q = 0; q < NOUT_PAD / 4; q++) {
                 const float4 wq = w[q];
-                if (4 * q < n_out) pre += wq.x * f[4 * q];
-                if (4 * q + 1 < n_out) pre += wq.y * f[4 * q + 1];
-                if (4 * q + 2 < n_out) pre += wq.z * f[4 * q + 2];
-                if (4 * q + 3 < n_out) pre += wq.w * f[4 * q + 3];
+                if (4 * q < n_out) pre = __fmaf_rn(wq.x, f[4 * q], pre);
+                if (4 * q + 1 < n_out) pre = __fmaf_rn(wq.y, f[4 * q + 1], pre);
+                if (4 * q + 2 < n_out) pre = __fmaf_rn(wq.z, f[4 * q + 2], pre);
+                if (4 * q + 3 < n_out) pre = __fmaf_rn(wq.w, f[4 * q + 3], pre);
             }
-            s_pre[threadIdx.x * pre_stride + j] = pre;
+            s_pre[j * cs + threadIdx.x] = pre;
             if (pre > 0.0f) {
-                const float grad_pre = g * s_w1[j];
+                const float grad_pre = __fmul_rn(g, s_w1[j]);
                 #pragma unroll
                 for (int q = 0; q < NOUT_PAD / 4; q++) {
                     const float4 wq = w[q];
-                    grad_f[4 * q] += grad_pre * wq.x;
-                    grad_f[4 * q + 1] += grad_pre * wq.y;
-                    grad_f[4 * q + 2] += grad_pre * wq.z;
-                    grad_f[4 * q + 3] += grad_pre * wq.w;
+                    grad_f[4 * q] = __fmaf_rn(grad_pre, wq.x, grad_f[4 * q]);
+                    grad_f[4 * q + 1] = __fmaf_rn(grad_pre, wq.y, grad_f[4 * q + 1]);
+                    grad_f[4 * q + 2] = __fmaf_rn(grad_pre, wq.z, grad_f[4 * q + 2]);
+                    grad_f[4 * q + 3] = __fmaf_rn(grad_pre, wq.w, grad_f[4 * q + 3]);
                 }
             }
         }
         s_g[threadIdx.x] = g;
-        // the scatter reads the scaled feature gradient from the thread's row; the parameter reduction then needs the
-        // features, which replace it afterwards
-        #pragma unroll
-        for (int i = 0; i < NOUT_PAD; i++) {
-            if (i < n_out) row[i] = grad_f[i] * kFeatureScale;
-        }
+        float* column = s_col + threadIdx.x;
         if (active && g != 0.0f) {
+            #pragma unroll
+            for (int i = 0; i < NOUT_PAD; i++) {
+                if (i < n_out) column[i * cs] = __fmul_rn(grad_f[i], kFeatureScale);
+            }
             const Frustum fr = setup_frustum(a.in, gp.pattern_stream, sample);
-            scatter_row<F>(gp, fr, row, gp.n_levels, a.grad_table, nullptr);
+            scatter_row<F>(gp, fr, column, cs, gp.n_levels, a.grad_table, nullptr);
         }
         #pragma unroll
-        for (int i = 0; i < NOUT_PAD; i++) {
-            if (i < n_out) row[i] = f[i];
-        }
+        for (int i = 0; i < NOUT_PAD; i++) column[i * cs] = f[i];
         __syncthreads();
-        for (int q = threadIdx.x; q < n_params; q += kBlock) {
-            float sum = 0.0f;
-            if (q < n_w0) {
-                const int j = q / n_out, i = q - j * n_out;
+
+        // phase 2: the block's parameter gradient sums over its samples, in sample order per output (as the reference's
+        // featurize_backward_mlp.cu:110-135): 4 x 4 tiles of grad_w0 (a register-blocked outer product of
+        // [pre > 0] g with the features), then grad_b0, grad_w1 and grad_b1
+        for (int item = threadIdx.x; item < n_items; item += kBlock) {
+            if (item < n_tiles) {
+                const int j0 = (item / (NOUT_PAD / 4)) * 4, i0 = (item % (NOUT_PAD / 4)) * 4;
+                float sum[4][4] = {};
                 for (int s = 0; s < kBlock; s++) {
-                    if (s_pre[s * pre_stride + j] > 0.0f) sum += s_g[s] * s_rows[s * stride + i];
+                    const float gs = s_g[s];
+                    float av[4], fv[4];
+                    #pragma unroll
+                    for (int r = 0; r < 4; r++) {
+                        av[r] = s_pre[(j0 + r) * cs + s] > 0.0f ? gs : 0.0f;
+                        fv[r] = s_col[(i0 + r) * cs + s];
+                    }
+                    #pragma unroll
+                    for (int r = 0; r < 4; r++) {
+                        #pragma unroll
+                        for (int c = 0; c < 4; c++) {
+                            if (av[r] != 0.0f) sum[r][c] = __fmaf_rn(av[r], fv[c], sum[r][c]);
+                        }
+                    }
                 }
-            }
-            else if (q < n_w0 + W) {
-                const int j = q - n_w0;
-                for (int s = 0; s < kBlock; s++) {
-                    if (s_pre[s * pre_stride + j] > 0.0f) sum += s_g[s];
+                #pragma unroll
+                for (int r = 0; r < 4; r++) {
+                    #pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const int j = j0 + r, i = i0 + c;
+                        if (j < W && i < n_out) s_acc[j * n_out + i] += sum[r][c];
+                    }
                 }
-            }
-            else if (q < n_w0 + 2 * W) {
-                const int j = q - n_w0 - W;
-                for (int s = 0; s < kBlock; s++) sum += s_g[s] * fmaxf(s_pre[s * pre_stride + j], 0.0f);
             }
             else {
-                for (int s = 0; s < kBlock; s++) sum += s_g[s];
+                const int q = item - n_tiles;
+                float sum = 0.0f;
+                if (q < W) {
+                    for (int s = 0; s < kBlock; s++) {
+                        if (s_pre[q * cs + s] > 0.0f) sum = __fadd_rn(sum, s_g[s]);
+                    }
+                    s_acc[n_w0 + q] += sum;
+                }
+                else if (q < 2 * W) {
+                    const int j = q - W;
+                    for (int s = 0; s < kBlock; s++) sum = __fmaf_rn(s_g[s], fmaxf(s_pre[j * cs + s], 0.0f), sum);
+                    s_acc[n_w0 + W + j] += sum;
+                }
+                else {
+                    for (int s = 0; s < kBlock; s++) sum = __fadd_rn(sum, s_g[s]);
+                    s_acc[n_w0 + 2 * W] += sum;
+                }
             }
-            s_acc[q] += sum;
         }
         __syncthreads();
     }
 
+    // one atomic per parameter and block, with w1 applied late (featurize_backward_mlp.cu:139-147)
     for (int q = threadIdx.x; q < n_params; q += kBlock) {
         const float acc = s_acc[q];
         if (acc == 0.0f) continue;
