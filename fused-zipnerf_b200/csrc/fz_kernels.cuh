@@ -18,11 +18,14 @@ constexpr int kBlock = 128;
 #ifndef ZF_MIN_BLOCKS_FORWARD
 #define ZF_MIN_BLOCKS_FORWARD 6
 #endif
+#ifndef ZF_MIN_BLOCKS_FORWARD_MLP
+#define ZF_MIN_BLOCKS_FORWARD_MLP 7
+#endif
 #ifndef ZF_MIN_BLOCKS_BACKWARD
 #define ZF_MIN_BLOCKS_BACKWARD 1
 #endif
 #ifndef ZF_MIN_BLOCKS_BACKWARD_MLP
-#define ZF_MIN_BLOCKS_BACKWARD_MLP 1
+#define ZF_MIN_BLOCKS_BACKWARD_MLP 2
 #endif
 constexpr int kWarps = kBlock / 32;
 
@@ -186,7 +189,7 @@ __device__ __forceinline__ void store_inputs_tail(const Args& a, const uint32_t*
 // Forward. NOUT_PAD == 0: no MLP; otherwise the fused density MLP n_out -> W (ReLU) -> 1 runs for raw_density, with
 // the features in registers (NOUT_PAD >= n_out) and the reference's accumulation order (featurize_forward.cu:65-73).
 template <int F, int NOUT_PAD>
-__global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_FORWARD) fz_forward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ ForwardArgs a) {
+__global__ void __launch_bounds__(kBlock, NOUT_PAD > 0 ? ZF_MIN_BLOCKS_FORWARD_MLP : ZF_MIN_BLOCKS_FORWARD) fz_forward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ ForwardArgs a) {
     const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
     const int stride = staged_stride(n_out);
     extern __shared__ __align__(16) float smem[];
