@@ -57,33 +57,6 @@ struct ForwardArgs {
     bool inputs_vectors;            // nerf_inputs / encoded_directions allow 16-byte copies
 };
 
-template <int F>
-struct GatherRows {
-    const float* table;
-    float value[F];
-
-    __device__ __forceinline__ void operator()(const uint32_t row, const float weight) {
-        if (weight == 0.0f) return;
-        // fused multiply-adds, as the reference's feature gather (featurize_common.cuh:179-198)
-        if constexpr (F == 4) {
-            const float4 t = __ldg(reinterpret_cast<const float4*>(table) + row);
-            value[0] = __fmaf_rn(weight, t.x, value[0]);
-            value[1] = __fmaf_rn(weight, t.y, value[1]);
-            value[2] = __fmaf_rn(weight, t.z, value[2]);
-            value[3] = __fmaf_rn(weight, t.w, value[3]);
-        }
-        else if constexpr (F == 2) {
-            const float2 t = __ldg(reinterpret_cast<const float2*>(table) + row);
-            value[0] = __fmaf_rn(weight, t.x, value[0]);
-            value[1] = __fmaf_rn(weight, t.y, value[1]);
-        }
-        else {
-            #pragma unroll
-            for (int f = 0; f < F; f++) value[f] = __fmaf_rn(weight, __ldg(table + row * F + f), value[f]);
-        }
-    }
-};
-
 // sample of a thread: consecutive samples, or (interleave) the same interval of up to R consecutive rays per warp run
 // (featurize_forward.cu:49-58)
 __device__ __forceinline__ uint32_t thread_sample(const uint32_t t, const RayInputs& in, const uint32_t interleave_rays) {
@@ -99,40 +72,115 @@ __device__ __forceinline__ void multisamples(const Frustum& fr, float3 (&x)[kMul
     for (uint32_t j = 0; j < kMultisamples; j++) multisample(fr, j, x[j], scale[j]);
 }
 
-// all level features of one interval into a shared-memory row: row[l (F + 1) + f] grid features (averaged over the
-// multisamples and preconditioned), row[l (F + 1) + F] the scale feature (featurize_common.cuh:207-227)
+template <int F>
+__device__ __forceinline__ void load_group(const float* __restrict__ table, const uint32_t (&rows)[8], const float (&weights)[8], float (&values)[8][F]) {
+    #pragma unroll
+    for (int c = 0; c < 8; c++) {
+        if constexpr (F == 4) {
+            float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (weights[c] != 0.0f) t = __ldg(reinterpret_cast<const float4*>(table) + rows[c]);
+            values[c][0] = t.x;
+            values[c][1] = t.y;
+            values[c][2] = t.z;
+            values[c][3] = t.w;
+        }
+        else if constexpr (F == 2) {
+            float2 t = make_float2(0.0f, 0.0f);
+            if (weights[c] != 0.0f) t = __ldg(reinterpret_cast<const float2*>(table) + rows[c]);
+            values[c][0] = t.x;
+            values[c][1] = t.y;
+        }
+        else {
+            #pragma unroll
+            for (int f = 0; f < F; f++) values[c][f] = weights[c] != 0.0f ? __ldg(table + rows[c] * F + f) : 0.0f;
+        }
+    }
+}
+
+// All level features of one interval into a shared-memory row: row[l (F + 1) + f] grid features (averaged over the
+// multisamples and preconditioned), row[l (F + 1) + F] the scale feature (featurize_common.cuh:207-227).
+//
+// The corner groups of all levels form one stream that is software pipelined: the gathers of the next group are
+// issued before the current group's values are accumulated, so every group's table latency overlaps the preparation
+// of the following group (cells, erf weights and corner rows of the next level included). The accumulation order is
+// the reference's: groups of a level in order, corners in order, zero-weight corners skipped, fused multiply-adds.
 template <int F>
 __device__ __forceinline__ void featurize_to_row(const GridParams& gp, const Frustum& fr, const float* __restrict__ table,
                                                  const float* __restrict__ scale_magnitudes, float* row) {
     float3 x[kMultisamples];
     float scale[kMultisamples];
     multisamples(fr, x, scale);
-    #pragma unroll 1
-    for (uint32_t level = 0; level < gp.n_levels; level++) {
-        float weighting[kMultisamples];
-        float scale_feature = 0.0f;
-        #pragma unroll
-        for (uint32_t j = 0; j < kMultisamples; j++) {
-            weighting[j] = level_weighting(gp.size[level], scale[j]);
-            scale_feature += 2.0f * weighting[j] - 1.0f;
+    const uint32_t n_levels = gp.n_levels;
+    LevelCells lc;
+    uint32_t level_next = 0, remaining = (1u << kMultisamples) - 1u;
+    {
+        const float sf = level_cells(gp, 0, x, scale, lc);
+        row[F] = kFeatureScale * sf * __ldg(scale_magnitudes);
+    }
+    uint32_t rows[8];
+    float weights[8], values[8][F];
+    next_group(gp, 0, lc, remaining, rows, weights);
+    load_group<F>(table, rows, weights, values);
+    uint32_t level = 0;
+    bool last = remaining == 0u;
+    float acc[F];
+    #pragma unroll
+    for (int f = 0; f < F; f++) acc[f] = 0.0f;
+    while (true) {
+        // prepare and issue the next group (possibly the first of the next level)
+        if (remaining == 0u) {
+            level_next++;
+            if (level_next < n_levels) {
+                const float sf = level_cells(gp, level_next, x, scale, lc);
+                row[level_next * (F + 1) + F] = kFeatureScale * sf * __ldg(scale_magnitudes + level_next);
+                remaining = (1u << kMultisamples) - 1u;
+            }
         }
-        GatherRows<F> gather{table, {}};
+        const bool has_next = level_next < n_levels;
+        uint32_t next_rows[8];
+        float next_weights[8], next_values[8][F];
+        bool next_last = true;
+        if (has_next) {
+            next_group(gp, level_next, lc, remaining, next_rows, next_weights);
+            next_last = remaining == 0u;
+            load_group<F>(table, next_rows, next_weights, next_values);
+        }
+        // accumulate the current group
         #pragma unroll
-        for (int f = 0; f < F; f++) gather.value[f] = 0.0f;
-        visit_level(gp, level, x, weighting, gather);
+        for (int c = 0; c < 8; c++) {
+            if (weights[c] != 0.0f) {
+                #pragma unroll
+                for (int f = 0; f < F; f++) acc[f] = __fmaf_rn(weights[c], values[c][f], acc[f]);
+            }
+        }
+        if (last) {
+            #pragma unroll
+            for (int f = 0; f < F; f++) {
+                row[level * (F + 1) + f] = kFeatureScale * acc[f];
+                acc[f] = 0.0f;
+            }
+        }
+        if (!has_next) break;
+        level = level_next;
+        last = next_last;
         #pragma unroll
-        for (int f = 0; f < F; f++) row[level * (F + 1) + f] = kFeatureScale * gather.value[f];
-        row[level * (F + 1) + F] = kFeatureScale * scale_feature * __ldg(scale_magnitudes + level);
+        for (int c = 0; c < 8; c++) {
+            weights[c] = next_weights[c];
+            #pragma unroll
+            for (int f = 0; f < F; f++) values[c][f] = next_values[c][f];
+        }
     }
 }
 
-// warp-cooperative copy of the warp's staged rows to row-major global outputs (rows of samples s_sample[...])
+// warp-cooperative copy of the warp's staged rows to row-major global outputs (rows of samples s_sample[...]); the
+// outputs are written once and read by a later kernel, so they are stored with the evict-first (streaming) policy
+// and do not push the grid tables out of L2
 __device__ __forceinline__ void store_rows_float(const float* s_rows, const int stride, const uint32_t* s_sample, const int n_rows, const int n_out,
                                                  float* __restrict__ out, const int lane) {
     const int n = n_rows * n_out;
     for (int e = lane; e < n; e += 32) {
         const int r = e / n_out, c = e - r * n_out;
-        out[static_cast<size_t>(s_sample[r]) * n_out + c] = s_rows[r * stride + c];
+        __stcs(out + static_cast<size_t>(s_sample[r]) * n_out + c, s_rows[r * stride + c]);
     }
 }
 
@@ -146,14 +194,14 @@ __device__ __forceinline__ void store_rows_bf16(const float* s_rows, const int s
             const int c = 2 * p;
             const uint32_t lo = c < n_out ? f32_to_bf16_bits(s_rows[r * stride + c]) : 0u;
             const uint32_t hi = c + 1 < n_out ? f32_to_bf16_bits(s_rows[r * stride + c + 1]) : 0u;
-            reinterpret_cast<uint32_t*>(out + static_cast<size_t>(s_sample[r]) * width)[p] = lo | (hi << 16);
+            __stcs(reinterpret_cast<unsigned int*>(out + static_cast<size_t>(s_sample[r]) * width) + p, lo | (hi << 16));
         }
     }
     else {
         const int n = n_rows * width;
         for (int e = lane; e < n; e += 32) {
             const int r = e / width, c = e - r * width;
-            out[static_cast<size_t>(s_sample[r]) * width + c] = c < n_out ? f32_to_bf16_bits(s_rows[r * stride + c]) : static_cast<uint16_t>(0);
+            __stcs(out + static_cast<size_t>(s_sample[r]) * width + c, c < n_out ? f32_to_bf16_bits(s_rows[r * stride + c]) : static_cast<unsigned short>(0));
         }
     }
 }
@@ -172,7 +220,7 @@ __device__ __forceinline__ void store_inputs_tail(const Args& a, const uint32_t*
             const uint4* src = reinterpret_cast<const uint4*>(a.encoded_directions + static_cast<size_t>(sample / a.in.n_intervals) * E);
             uint4 value = __ldg(src + v);
             if (v == nv - 1) value.w = (value.w & 0x0000FFFFu) | 0x3f800000u;
-            reinterpret_cast<uint4*>(a.nerf_inputs + static_cast<size_t>(sample + 1) * a.nerf_inputs_width - E)[v] = value;
+            __stcs(reinterpret_cast<uint4*>(a.nerf_inputs + static_cast<size_t>(sample + 1) * a.nerf_inputs_width - E) + v, value);
         }
     }
     else {
@@ -181,7 +229,7 @@ __device__ __forceinline__ void store_inputs_tail(const Args& a, const uint32_t*
             const int r = e / E, c = e - r * E;
             const uint32_t sample = s_sample[r];
             const uint16_t value = c == E - 1 ? static_cast<uint16_t>(0x3f80) : a.encoded_directions[static_cast<size_t>(sample / a.in.n_intervals) * E + c];
-            a.nerf_inputs[static_cast<size_t>(sample + 1) * a.nerf_inputs_width - E + c] = value;
+            __stcs(a.nerf_inputs + static_cast<size_t>(sample + 1) * a.nerf_inputs_width - E + c, value);
         }
     }
 }
@@ -240,7 +288,7 @@ __global__ void __launch_bounds__(kBlock, NOUT_PAD > 0 ? ZF_MIN_BLOCKS_FORWARD_M
                 }
                 raw = __fmaf_rn(s_w1[j], fmaxf(pre, 0.0f), raw);
             }
-            a.raw_density[sample] = raw;
+            __stcs(a.raw_density + sample, raw);
         }
     }
     __syncwarp();
@@ -309,9 +357,6 @@ __device__ __forceinline__ void scatter_row(const GridParams& gp, const Frustum&
     const uint32_t half_base = gp.offset[min(n_fp32, gp.n_levels)];
     #pragma unroll 1
     for (uint32_t level = 0; level < gp.n_levels; level++) {
-        float weighting[kMultisamples];
-        #pragma unroll
-        for (uint32_t j = 0; j < kMultisamples; j++) weighting[j] = level_weighting(gp.size[level], scale[j]);
         float g[F];
         #pragma unroll
         for (int f = 0; f < F; f++) g[f] = g_row[(level * (F + 1) + f) * g_stride];
@@ -319,13 +364,13 @@ __device__ __forceinline__ void scatter_row(const GridParams& gp, const Frustum&
             auto visitor = [&](const uint32_t row, const float weight) {
                 if (weight != 0.0f) add_row_f32<F>(grad_table, row, weight, g);
             };
-            visit_level(gp, level, x, weighting, visitor);
+            visit_level(gp, level, x, scale, visitor);
         }
         else {
             auto visitor = [&](const uint32_t row, const float weight) {
                 if (weight != 0.0f) add_row_f16<F>(grad_table_half, row - half_base, weight, g);
             };
-            visit_level(gp, level, x, weighting, visitor);
+            visit_level(gp, level, x, scale, visitor);
         }
     }
 }
@@ -356,7 +401,7 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_ke
     const int n = n_rows * n_out;
     for (int e = lane; e < n; e += 32) {
         const int r = e / n_out, c = e - r * n_out;
-        const uint16_t bits = __ldg(a.grad_features + static_cast<size_t>(warp_first + r) * a.grad_stride + c);
+        const uint16_t bits = __ldcs(a.grad_features + static_cast<size_t>(warp_first + r) * a.grad_stride + c);
         warp_rows[r * stride + c] = kFeatureScale * a.grad_scale * bf16_bits_to_f32(bits);
     }
     __syncwarp();
@@ -440,8 +485,8 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_backwar
         const bool active = sample < a.in.n_samples;
         float f[NOUT_PAD];
         #pragma unroll
-        for (int i = 0; i < NOUT_PAD; i++) f[i] = active && i < n_out ? __ldg(a.features + static_cast<size_t>(sample) * n_out + i) : 0.0f;
-        const float g = active ? __ldg(a.grad_raw_density + sample) : 0.0f;
+        for (int i = 0; i < NOUT_PAD; i++) f[i] = active && i < n_out ? __ldcs(a.features + static_cast<size_t>(sample) * n_out + i) : 0.0f;
+        const float g = active ? __ldcs(a.grad_raw_density + sample) : 0.0f;
         float grad_f[NOUT_PAD];
         #pragma unroll
         for (int i = 0; i < NOUT_PAD; i++) grad_f[i] = 0.0f;
@@ -586,9 +631,6 @@ __global__ void fz_debug_kernel(const __grid_constant__ GridParams gp, const __g
     }
     #pragma unroll 1
     for (uint32_t level = 0; level < L; level++) {
-        float weighting[kMultisamples];
-        #pragma unroll
-        for (uint32_t j = 0; j < kMultisamples; j++) weighting[j] = level_weighting(gp.size[level], scale[j]);
         uint32_t n = 0;
         const size_t base = (static_cast<size_t>(d) * L + level) * kMultisamples * 8;
         auto visitor = [&](const uint32_t row, const float weight) {
@@ -596,7 +638,7 @@ __global__ void fz_debug_kernel(const __grid_constant__ GridParams gp, const __g
             a.weights[base + n] = weight;
             n++;
         };
-        visit_level(gp, level, x, weighting, visitor);
+        visit_level(gp, level, x, scale, visitor);
         for (uint32_t k = n; k < kMultisamples * 8; k++) {
             a.rows[base + k] = 0u;
             a.weights[base + k] = 0.0f;
