@@ -173,86 +173,61 @@ __device__ __forceinline__ uint32_t corner_row(const GridParams& gp, const uint3
     return gp.offset[level] + index;
 }
 
-// Cells, fractional positions and erf downweighting of the six multisamples at one level.
-struct LevelCells {
+// Visits the merged corner groups of one level: visitor(row, weight) for the 8 corners of every group, groups in
+// the order of their first multisample, corners in the order (x, y, z) bit 2, 1, 0. Multisamples in the same cell
+// form one group whose corner weights are summed in multisample order, exactly as featurize_common.cuh:137-172 does;
+// here each lane loops over its own groups (lowest unvisited multisample first), so a warp issues the corner work of
+// max(groups) groups instead of all 21 (leader, member) pairs of the fully unrolled merge. The roundings are explicit
+// (a fused multiply-add of the weighting into the sum of (wx wy) wz products), which reproduces the reference
+// kernels' corner weights bit for bit independently of how the surrounding code is scheduled.
+template <typename Visitor>
+__device__ __forceinline__ void visit_level(const GridParams& gp, const uint32_t level, const float3* x, const float* weighting, Visitor& visitor) {
+    const uint32_t size = gp.size[level];
     int cx[kMultisamples], cy[kMultisamples], cz[kMultisamples];
     float fx[kMultisamples], fy[kMultisamples], fz[kMultisamples];
-    float weighting[kMultisamples];
-};
-
-// fills the cells of `level`; returns the level's scale feature sum (sum over multisamples of 2 w - 1,
-// featurize_common.cuh:214-220)
-__device__ __forceinline__ float level_cells(const GridParams& gp, const uint32_t level, const float3* x, const float* scale, LevelCells& lc) {
-    const uint32_t size = gp.size[level];
-    float scale_feature = 0.0f;
     #pragma unroll
     for (uint32_t j = 0; j < kMultisamples; j++) {
-        lc.weighting[j] = level_weighting(size, scale[j]);
-        scale_feature += 2.0f * lc.weighting[j] - 1.0f;
         const float px = x[j].x * size - 0.5f, py = x[j].y * size - 0.5f, pz = x[j].z * size - 0.5f;
         const float gx = floorf(px), gy = floorf(py), gz = floorf(pz);
-        lc.cx[j] = static_cast<int>(gx);
-        lc.cy[j] = static_cast<int>(gy);
-        lc.cz[j] = static_cast<int>(gz);
-        lc.fx[j] = px - gx;
-        lc.fy[j] = py - gy;
-        lc.fz[j] = pz - gz;
+        cx[j] = static_cast<int>(gx);
+        cy[j] = static_cast<int>(gy);
+        cz[j] = static_cast<int>(gz);
+        fx[j] = px - gx;
+        fy[j] = py - gy;
+        fz[j] = pz - gz;
     }
-    return scale_feature;
-}
-
-// Pops the next merged corner group of a level: the group of the lowest multisample still in `remaining` (the
-// multisamples in its cell are removed from it). Writes the 8 corner rows (level offset included) and weights in the
-// order (x, y, z) bit 2, 1, 0. The corner weights sum the group's multisamples in order, as featurize_common.cuh:137-172
-// does; the roundings are explicit (a fused multiply-add of the weighting into the sum of (wx wy) wz products), which
-// reproduces the reference kernels' weights bit for bit however the surrounding code is scheduled.
-__device__ __forceinline__ void next_group(const GridParams& gp, const uint32_t level, const LevelCells& lc, uint32_t& remaining, uint32_t (&rows)[8],
-                                           float (&weights)[8]) {
-    const uint32_t leader = __ffs(remaining) - 1u;
-    int lx = lc.cx[0], ly = lc.cy[0], lz = lc.cz[0];
-    #pragma unroll
-    for (uint32_t j = 1; j < kMultisamples; j++) {
-        if (leader == j) {
-            lx = lc.cx[j];
-            ly = lc.cy[j];
-            lz = lc.cz[j];
-        }
-    }
-    #pragma unroll
-    for (uint32_t corner = 0; corner < 8; corner++) weights[corner] = 0.0f;
-    #pragma unroll
-    for (uint32_t k = 0; k < kMultisamples; k++) {
-        if (!((remaining >> k) & 1u) || lc.cx[k] != lx || lc.cy[k] != ly || lc.cz[k] != lz) continue;
-        remaining &= ~(1u << k);
-        #pragma unroll
-        for (uint32_t corner = 0; corner < 8; corner++) {
-            const float wx = corner & 4u ? lc.fx[k] : 1.0f - lc.fx[k];
-            const float wy = corner & 2u ? lc.fy[k] : 1.0f - lc.fy[k];
-            const float wz = corner & 1u ? lc.fz[k] : 1.0f - lc.fz[k];
-            weights[corner] = __fmaf_rn(lc.weighting[k], __fmul_rn(__fmul_rn(wx, wy), wz), weights[corner]);
-        }
-    }
-    #pragma unroll
-    for (uint32_t corner = 0; corner < 8; corner++) {
-        rows[corner] = corner_row(gp, level, lx + static_cast<int>((corner >> 2) & 1u), ly + static_cast<int>((corner >> 1) & 1u),
-                                  lz + static_cast<int>(corner & 1u), weights[corner]);
-    }
-}
-
-// Visits the merged corner groups of one level: visitor(row, weight) for the 8 corners of every group, groups in the
-// order of their first multisample. Each lane loops over its own groups, so a warp issues the corner work of
-// max(groups) groups instead of all 21 (leader, member) pairs of the reference's fully unrolled merge.
-template <typename Visitor>
-__device__ __forceinline__ void visit_level(const GridParams& gp, const uint32_t level, const float3* x, const float* scale, Visitor& visitor) {
-    LevelCells lc;
-    level_cells(gp, level, x, scale, lc);
     uint32_t remaining = (1u << kMultisamples) - 1u;
     while (remaining != 0u) {
-        uint32_t rows[8];
-        float weights[8];
-        next_group(gp, level, lc, remaining, rows, weights);
+        const uint32_t leader = __ffs(remaining) - 1u;
+        int lx = cx[0], ly = cy[0], lz = cz[0];
         #pragma unroll
-        for (uint32_t corner = 0; corner < 8; corner++) visitor(rows[corner], weights[corner]);
+        for (uint32_t j = 1; j < kMultisamples; j++) {
+            if (leader == j) {
+                lx = cx[j];
+                ly = cy[j];
+                lz = cz[j];
+            }
+        }
+        float corner_weights[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        #pragma unroll
+        for (uint32_t k = 0; k < kMultisamples; k++) {
+            if (!((remaining >> k) & 1u) || cx[k] != lx || cy[k] != ly || cz[k] != lz) continue;
+            remaining &= ~(1u << k);
+            #pragma unroll
+            for (uint32_t corner = 0; corner < 8; corner++) {
+                const float wx = corner & 4u ? fx[k] : 1.0f - fx[k];
+                const float wy = corner & 2u ? fy[k] : 1.0f - fy[k];
+                const float wz = corner & 1u ? fz[k] : 1.0f - fz[k];
+                corner_weights[corner] = __fmaf_rn(weighting[k], __fmul_rn(__fmul_rn(wx, wy), wz), corner_weights[corner]);
+            }
+        }
+        #pragma unroll
+        for (uint32_t corner = 0; corner < 8; corner++) {
+            float weight = corner_weights[corner];
+            const uint32_t row = corner_row(gp, level, lx + static_cast<int>((corner >> 2) & 1u), ly + static_cast<int>((corner >> 1) & 1u),
+                                            lz + static_cast<int>(corner & 1u), weight);
+            visitor(row, weight);
+        }
     }
 }
 

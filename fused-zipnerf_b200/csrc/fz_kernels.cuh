@@ -57,6 +57,33 @@ struct ForwardArgs {
     bool inputs_vectors;            // nerf_inputs / encoded_directions allow 16-byte copies
 };
 
+template <int F>
+struct GatherRows {
+    const float* table;
+    float value[F];
+
+    __device__ __forceinline__ void operator()(const uint32_t row, const float weight) {
+        if (weight == 0.0f) return;
+        // fused multiply-adds, as the reference's feature gather (featurize_common.cuh:179-198)
+        if constexpr (F == 4) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(table) + row);
+            value[0] = __fmaf_rn(weight, t.x, value[0]);
+            value[1] = __fmaf_rn(weight, t.y, value[1]);
+            value[2] = __fmaf_rn(weight, t.z, value[2]);
+            value[3] = __fmaf_rn(weight, t.w, value[3]);
+        }
+        else if constexpr (F == 2) {
+            const float2 t = __ldg(reinterpret_cast<const float2*>(table) + row);
+            value[0] = __fmaf_rn(weight, t.x, value[0]);
+            value[1] = __fmaf_rn(weight, t.y, value[1]);
+        }
+        else {
+            #pragma unroll
+            for (int f = 0; f < F; f++) value[f] = __fmaf_rn(weight, __ldg(table + row * F + f), value[f]);
+        }
+    }
+};
+
 // sample of a thread: consecutive samples, or (interleave) the same interval of up to R consecutive rays per warp run
 // (featurize_forward.cu:49-58)
 __device__ __forceinline__ uint32_t thread_sample(const uint32_t t, const RayInputs& in, const uint32_t interleave_rays) {
@@ -72,103 +99,30 @@ __device__ __forceinline__ void multisamples(const Frustum& fr, float3 (&x)[kMul
     for (uint32_t j = 0; j < kMultisamples; j++) multisample(fr, j, x[j], scale[j]);
 }
 
-template <int F>
-__device__ __forceinline__ void load_group(const float* __restrict__ table, const uint32_t (&rows)[8], const float (&weights)[8], float (&values)[8][F]) {
-    #pragma unroll
-    for (int c = 0; c < 8; c++) {
-        if constexpr (F == 4) {
-            float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (weights[c] != 0.0f) t = __ldg(reinterpret_cast<const float4*>(table) + rows[c]);
-            values[c][0] = t.x;
-            values[c][1] = t.y;
-            values[c][2] = t.z;
-            values[c][3] = t.w;
-        }
-        else if constexpr (F == 2) {
-            float2 t = make_float2(0.0f, 0.0f);
-            if (weights[c] != 0.0f) t = __ldg(reinterpret_cast<const float2*>(table) + rows[c]);
-            values[c][0] = t.x;
-            values[c][1] = t.y;
-        }
-        else {
-            #pragma unroll
-            for (int f = 0; f < F; f++) values[c][f] = weights[c] != 0.0f ? __ldg(table + rows[c] * F + f) : 0.0f;
-        }
-    }
-}
-
-// All level features of one interval into a shared-memory row: row[l (F + 1) + f] grid features (averaged over the
-// multisamples and preconditioned), row[l (F + 1) + F] the scale feature (featurize_common.cuh:207-227).
-//
-// The corner groups of all levels form one stream that is software pipelined: the gathers of the next group are
-// issued before the current group's values are accumulated, so every group's table latency overlaps the preparation
-// of the following group (cells, erf weights and corner rows of the next level included). The accumulation order is
-// the reference's: groups of a level in order, corners in order, zero-weight corners skipped, fused multiply-adds.
+// all level features of one interval into a shared-memory row: row[l (F + 1) + f] grid features (averaged over the
+// multisamples and preconditioned), row[l (F + 1) + F] the scale feature (featurize_common.cuh:207-227)
 template <int F>
 __device__ __forceinline__ void featurize_to_row(const GridParams& gp, const Frustum& fr, const float* __restrict__ table,
                                                  const float* __restrict__ scale_magnitudes, float* row) {
     float3 x[kMultisamples];
     float scale[kMultisamples];
     multisamples(fr, x, scale);
-    const uint32_t n_levels = gp.n_levels;
-    LevelCells lc;
-    uint32_t level_next = 0, remaining = (1u << kMultisamples) - 1u;
-    {
-        const float sf = level_cells(gp, 0, x, scale, lc);
-        row[F] = kFeatureScale * sf * __ldg(scale_magnitudes);
-    }
-    uint32_t rows[8];
-    float weights[8], values[8][F];
-    next_group(gp, 0, lc, remaining, rows, weights);
-    load_group<F>(table, rows, weights, values);
-    uint32_t level = 0;
-    bool last = remaining == 0u;
-    float acc[F];
-    #pragma unroll
-    for (int f = 0; f < F; f++) acc[f] = 0.0f;
-    while (true) {
-        // prepare and issue the next group (possibly the first of the next level)
-        if (remaining == 0u) {
-            level_next++;
-            if (level_next < n_levels) {
-                const float sf = level_cells(gp, level_next, x, scale, lc);
-                row[level_next * (F + 1) + F] = kFeatureScale * sf * __ldg(scale_magnitudes + level_next);
-                remaining = (1u << kMultisamples) - 1u;
-            }
-        }
-        const bool has_next = level_next < n_levels;
-        uint32_t next_rows[8];
-        float next_weights[8], next_values[8][F];
-        bool next_last = true;
-        if (has_next) {
-            next_group(gp, level_next, lc, remaining, next_rows, next_weights);
-            next_last = remaining == 0u;
-            load_group<F>(table, next_rows, next_weights, next_values);
-        }
-        // accumulate the current group
+    #pragma unroll 1
+    for (uint32_t level = 0; level < gp.n_levels; level++) {
+        float weighting[kMultisamples];
+        float scale_feature = 0.0f;
         #pragma unroll
-        for (int c = 0; c < 8; c++) {
-            if (weights[c] != 0.0f) {
-                #pragma unroll
-                for (int f = 0; f < F; f++) acc[f] = __fmaf_rn(weights[c], values[c][f], acc[f]);
-            }
+        for (uint32_t j = 0; j < kMultisamples; j++) {
+            weighting[j] = level_weighting(gp.size[level], scale[j]);
+            scale_feature += 2.0f * weighting[j] - 1.0f;
         }
-        if (last) {
-            #pragma unroll
-            for (int f = 0; f < F; f++) {
-                row[level * (F + 1) + f] = kFeatureScale * acc[f];
-                acc[f] = 0.0f;
-            }
-        }
-        if (!has_next) break;
-        level = level_next;
-        last = next_last;
+        GatherRows<F> gather{table, {}};
         #pragma unroll
-        for (int c = 0; c < 8; c++) {
-            weights[c] = next_weights[c];
-            #pragma unroll
-            for (int f = 0; f < F; f++) values[c][f] = next_values[c][f];
-        }
+        for (int f = 0; f < F; f++) gather.value[f] = 0.0f;
+        visit_level(gp, level, x, weighting, gather);
+        #pragma unroll
+        for (int f = 0; f < F; f++) row[level * (F + 1) + f] = kFeatureScale * gather.value[f];
+        row[level * (F + 1) + F] = kFeatureScale * scale_feature * __ldg(scale_magnitudes + level);
     }
 }
 
@@ -357,6 +311,9 @@ __device__ __forceinline__ void scatter_row(const GridParams& gp, const Frustum&
     const uint32_t half_base = gp.offset[min(n_fp32, gp.n_levels)];
     #pragma unroll 1
     for (uint32_t level = 0; level < gp.n_levels; level++) {
+        float weighting[kMultisamples];
+        #pragma unroll
+        for (uint32_t j = 0; j < kMultisamples; j++) weighting[j] = level_weighting(gp.size[level], scale[j]);
         float g[F];
         #pragma unroll
         for (int f = 0; f < F; f++) g[f] = g_row[(level * (F + 1) + f) * g_stride];
@@ -364,13 +321,13 @@ __device__ __forceinline__ void scatter_row(const GridParams& gp, const Frustum&
             auto visitor = [&](const uint32_t row, const float weight) {
                 if (weight != 0.0f) add_row_f32<F>(grad_table, row, weight, g);
             };
-            visit_level(gp, level, x, scale, visitor);
+            visit_level(gp, level, x, weighting, visitor);
         }
         else {
             auto visitor = [&](const uint32_t row, const float weight) {
                 if (weight != 0.0f) add_row_f16<F>(grad_table_half, row - half_base, weight, g);
             };
-            visit_level(gp, level, x, scale, visitor);
+            visit_level(gp, level, x, weighting, visitor);
         }
     }
 }
@@ -631,6 +588,9 @@ __global__ void fz_debug_kernel(const __grid_constant__ GridParams gp, const __g
     }
     #pragma unroll 1
     for (uint32_t level = 0; level < L; level++) {
+        float weighting[kMultisamples];
+        #pragma unroll
+        for (uint32_t j = 0; j < kMultisamples; j++) weighting[j] = level_weighting(gp.size[level], scale[j]);
         uint32_t n = 0;
         const size_t base = (static_cast<size_t>(d) * L + level) * kMultisamples * 8;
         auto visitor = [&](const uint32_t row, const float weight) {
@@ -638,7 +598,7 @@ __global__ void fz_debug_kernel(const __grid_constant__ GridParams gp, const __g
             a.weights[base + n] = weight;
             n++;
         };
-        visit_level(gp, level, x, scale, visitor);
+        visit_level(gp, level, x, weighting, visitor);
         for (uint32_t k = n; k < kMultisamples * 8; k++) {
             a.rows[base + k] = 0u;
             a.weights[base + k] = 0.0f;
