@@ -21,6 +21,7 @@ ZF_DECLARE_KSET(1) ZF_DECLARE_KSET(2) ZF_DECLARE_KSET(3) ZF_DECLARE_KSET(4)
 ZF_FOR_EACH_MLP(ZF_DECLARE_MLP_KSET)
 #undef ZF_DECLARE_MLP_KSET
 extern "C" void (*const zf_debug_kernel)(zf::GridParams, zf::DebugArgs) __attribute__((weak));
+extern "C" void (*const zf_check_erf_kernel)(uint32_t, uint32_t, unsigned long long*, uint32_t*) __attribute__((weak));
 
 namespace {
 
@@ -340,6 +341,20 @@ int zf_featurize_debug(zf_featurizer* f, const zf_rays* rays, const uint32_t* sa
     if (error != cudaSuccess) return cuda_fail(error, "featurize_debug launch");
     return ZF_OK;
 }
+
+int zf_check_erf_saturation(const uint32_t first_bits, const uint32_t last_bits, unsigned long long* n_not_one, uint32_t* max_bits, cudaStream_t stream) {
+    if (&zf_check_erf_kernel == nullptr) return fail(ZF_ERROR_UNSUPPORTED, "the erf check is not compiled into this build");
+    if (n_not_one == nullptr || max_bits == nullptr || last_bits < first_bits) return fail(ZF_ERROR_INVALID_ARGUMENT, "invalid erf check arguments");
+    const uint32_t count = last_bits - first_bits + 1u;
+    void (*kernel)(uint32_t, uint32_t, unsigned long long*, uint32_t*) = zf_check_erf_kernel;
+    uint32_t first = first_bits, n = count;
+    void* params[] = {&first, &n, &n_not_one, &max_bits};
+    const cudaError_t error = cudaLaunchKernel(reinterpret_cast<const void*>(kernel), dim3(148 * 16), dim3(256), params, 0, stream);
+    if (error != cudaSuccess) return cuda_fail(error, "erf check launch");
+    return ZF_OK;
+}
+
+float zf_erf_saturation_threshold(void) { return zf::kErfSaturation; }
 
 const char* zf_last_error(void) { return last_error.c_str(); }
 

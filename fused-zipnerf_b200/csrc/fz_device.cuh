@@ -153,8 +153,19 @@ __device__ __forceinline__ void multisample(const Frustum& fr, const uint32_t j,
     scale = kMultisampleScale * perp * isoscale * (1.0f / kGridBboxSize);
 }
 
+// Arguments from which approx_erf is exactly 1.0f in this build: expm1f of the argument's square term is exactly -1
+// and the square root of 1 is 1. zf_check_erf_saturation verifies that claim over every float in [threshold, +inf)
+// on the device (the GPU tests run it); below the threshold the erf is evaluated as the reference does.
+#ifndef ZF_ERF_SATURATION
+#define ZF_ERF_SATURATION 4.0f
+#endif
+constexpr float kErfSaturation = ZF_ERF_SATURATION;
+
 __device__ __forceinline__ float level_weighting(const uint32_t size, const float scale) {
-    return approx_erf(1.0f / (sqrtf(8.0f) * scale * size));
+    const float x = 1.0f / (sqrtf(8.0f) * scale * size);
+    // coarse levels of small multisamples (the common case) saturate: skip the expm1f / sqrtf of approx_erf
+    if (x >= kErfSaturation) return 1.0f;
+    return approx_erf(x);
 }
 
 // table row of a corner (level offset included); weight is zeroed for corners outside a dense level

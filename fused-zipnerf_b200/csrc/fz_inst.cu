@@ -15,6 +15,7 @@ extern "C" const zf::KernelSet ZF_KSET_NAME(ZF_INST_F) = {
 };
 #if ZF_INST_F == 1
 extern "C" void (*const zf_debug_kernel)(zf::GridParams, zf::DebugArgs) = zf::fz_debug_kernel<0>;
+extern "C" void (*const zf_check_erf_kernel)(uint32_t, uint32_t, unsigned long long*, uint32_t*) = zf::fz_check_erf_kernel<0>;
 #endif
 #else
 extern "C" const zf::MlpKernelSet ZF_MLP_KSET_NAME(ZF_INST_F, ZF_INST_PAD) = {

@@ -126,35 +126,48 @@ __device__ __forceinline__ void featurize_to_row(const GridParams& gp, const Fru
     }
 }
 
+// (row, column) of the elements e = lane, lane + 32, ... of a row-major [rows, cols] block, advanced without a
+// division per element
+struct LaneWalk {
+    int r, c, dr, dc, cols;
+    __device__ __forceinline__ LaneWalk(const int lane, const int n_cols) : cols(n_cols) {
+        r = lane / n_cols;
+        c = lane - r * n_cols;
+        dr = 32 / n_cols;
+        dc = 32 - dr * n_cols;
+    }
+    __device__ __forceinline__ void next() {
+        r += dr;
+        c += dc;
+        if (c >= cols) {
+            c -= cols;
+            r++;
+        }
+    }
+};
+
 // warp-cooperative copy of the warp's staged rows to row-major global outputs (rows of samples s_sample[...]); the
 // outputs are written once and read by a later kernel, so they are stored with the evict-first (streaming) policy
 // and do not push the grid tables out of L2
 __device__ __forceinline__ void store_rows_float(const float* s_rows, const int stride, const uint32_t* s_sample, const int n_rows, const int n_out,
                                                  float* __restrict__ out, const int lane) {
-    const int n = n_rows * n_out;
-    for (int e = lane; e < n; e += 32) {
-        const int r = e / n_out, c = e - r * n_out;
-        __stcs(out + static_cast<size_t>(s_sample[r]) * n_out + c, s_rows[r * stride + c]);
-    }
+    LaneWalk w(lane, n_out);
+    for (; w.r < n_rows; w.next()) __stcs(out + static_cast<size_t>(s_sample[w.r]) * n_out + w.c, s_rows[w.r * stride + w.c]);
 }
 
 __device__ __forceinline__ void store_rows_bf16(const float* s_rows, const int stride, const uint32_t* s_sample, const int n_rows, const int n_out,
                                                 uint16_t* __restrict__ out, const int width, const bool pairs, const int lane) {
     if (pairs) {
-        const int half = width / 2;
-        const int n = n_rows * half;
-        for (int e = lane; e < n; e += 32) {
-            const int r = e / half, p = e - r * half;
-            const int c = 2 * p;
+        for (LaneWalk w(lane, width / 2); w.r < n_rows; w.next()) {
+            const int r = w.r, p = w.c, c = 2 * p;
             const uint32_t lo = c < n_out ? f32_to_bf16_bits(s_rows[r * stride + c]) : 0u;
             const uint32_t hi = c + 1 < n_out ? f32_to_bf16_bits(s_rows[r * stride + c + 1]) : 0u;
             __stcs(reinterpret_cast<unsigned int*>(out + static_cast<size_t>(s_sample[r]) * width) + p, lo | (hi << 16));
         }
     }
     else {
-        const int n = n_rows * width;
-        for (int e = lane; e < n; e += 32) {
-            const int r = e / width, c = e - r * width;
+        for (LaneWalk w(lane, width); w.r < n_rows; w.next()) {
+            const int r = w.r, c = w.c;
             __stcs(out + static_cast<size_t>(s_sample[r]) * width + c, c < n_out ? f32_to_bf16_bits(s_rows[r * stride + c]) : static_cast<unsigned short>(0));
         }
     }
@@ -167,9 +180,8 @@ __device__ __forceinline__ void store_inputs_tail(const Args& a, const uint32_t*
     const int E = a.encoded_width;
     if (a.inputs_vectors) {
         const int nv = E / 8;
-        const int n = n_rows * nv;
-        for (int e = lane; e < n; e += 32) {
-            const int r = e / nv, v = e - r * nv;
+        for (LaneWalk w(lane, nv); w.r < n_rows; w.next()) {
+            const int r = w.r, v = w.c;
             const uint32_t sample = s_sample[r];
             const uint4* src = reinterpret_cast<const uint4*>(a.encoded_directions + static_cast<size_t>(sample / a.in.n_intervals) * E);
             uint4 value = __ldg(src + v);
@@ -178,9 +190,8 @@ __device__ __forceinline__ void store_inputs_tail(const Args& a, const uint32_t*
         }
     }
     else {
-        const int n = n_rows * E;
-        for (int e = lane; e < n; e += 32) {
-            const int r = e / E, c = e - r * E;
+        for (LaneWalk w(lane, E); w.r < n_rows; w.next()) {
+            const int r = w.r, c = w.c;
             const uint32_t sample = s_sample[r];
             const uint16_t value = c == E - 1 ? static_cast<uint16_t>(0x3f80) : a.encoded_directions[static_cast<size_t>(sample / a.in.n_intervals) * E + c];
             __stcs(a.nerf_inputs + static_cast<size_t>(sample + 1) * a.nerf_inputs_width - E + c, value);
@@ -355,9 +366,8 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_ke
     const int n_rows = min(32, static_cast<int>(a.in.n_samples - warp_first));
     float* warp_rows = smem + warp * 32 * stride;
     // coalesced load of the warp's gradient rows, scaled as the reference (feature_scale * grad_scale * g)
-    const int n = n_rows * n_out;
-    for (int e = lane; e < n; e += 32) {
-        const int r = e / n_out, c = e - r * n_out;
+    for (LaneWalk w(lane, n_out); w.r < n_rows; w.next()) {
+        const int r = w.r, c = w.c;
         const uint16_t bits = __ldcs(a.grad_features + static_cast<size_t>(warp_first + r) * a.grad_stride + c);
         warp_rows[r * stride + c] = kFeatureScale * a.grad_scale * bf16_bits_to_f32(bits);
     }
@@ -548,6 +558,27 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_backwar
         else if (q < n_w0 + W) atomicAdd(a.grad_b0 + (q - n_w0), s_w1[q - n_w0] * acc);
         else if (q < n_w0 + 2 * W) atomicAdd(a.grad_w1 + (q - n_w0 - W), acc);
         else atomicAdd(a.grad_b1, acc);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// numerics self-check: approx_erf over a range of float bit patterns; counts the arguments whose value is not exactly
+// 1.0f and records the largest such bit pattern (atomicMax on the bits orders non-negative floats)
+
+template <int kUnused>
+__global__ void fz_check_erf_kernel(const uint32_t first_bits, const uint32_t count, unsigned long long* n_not_one, uint32_t* max_bits) {
+    unsigned long long local = 0;
+    uint32_t local_max = 0;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) {
+        const uint32_t bits = first_bits + i;
+        if (approx_erf(__uint_as_float(bits)) != 1.0f) {
+            local++;
+            local_max = max(local_max, bits);
+        }
+    }
+    if (local != 0) {
+        atomicAdd(n_not_one, local);
+        atomicMax(max_bits, local_max);
     }
 }
 

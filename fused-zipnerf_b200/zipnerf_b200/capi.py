@@ -16,7 +16,7 @@ ZF_OK, ZF_ERROR_INVALID_ARGUMENT, ZF_ERROR_UNSUPPORTED, ZF_ERROR_CUDA = 0, 1, 2,
 
 EXPORTED = ['zf_featurizer_create', 'zf_featurizer_destroy', 'zf_featurizer_n_output_features', 'zf_featurizer_n_fp32_grad_rows',
             'zf_featurizer_n_rows', 'zf_featurize_forward', 'zf_featurize_backward', 'zf_featurize_backward_mlp', 'zf_featurize_debug',
-            'zf_last_error', 'zf_grid_max_value', 'zf_nerf_grid_grad_scale']
+            'zf_check_erf_saturation', 'zf_erf_saturation_threshold', 'zf_last_error', 'zf_grid_max_value', 'zf_nerf_grid_grad_scale']
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -79,6 +79,10 @@ def load() -> ctypes.CDLL:
     lib.zf_featurize_debug.argtypes = [_p, ctypes.POINTER(zf_rays), _p, _i64, _p, _p, _p, _p, _p, _p, _p]
     for name in ['zf_featurize_forward', 'zf_featurize_backward', 'zf_featurize_backward_mlp', 'zf_featurize_debug']:
         getattr(lib, name).restype = ctypes.c_int
+    lib.zf_check_erf_saturation.argtypes = [ctypes.c_uint32, ctypes.c_uint32, _p, _p, _p]
+    lib.zf_check_erf_saturation.restype = ctypes.c_int
+    lib.zf_erf_saturation_threshold.argtypes = []
+    lib.zf_erf_saturation_threshold.restype = ctypes.c_float
     lib.zf_last_error.argtypes = []
     lib.zf_last_error.restype = ctypes.c_char_p
     lib.zf_grid_max_value.restype = ctypes.c_double
@@ -101,6 +105,21 @@ def _stream(stream) -> int | None:
         import torch
         return torch.cuda.current_stream().cuda_stream
     return stream if isinstance(stream, int) else stream.cuda_stream
+
+
+def check_erf_saturation(first: float, last: float = float('inf')) -> tuple[int, float]:
+    """Runs zf_check_erf_saturation over the floats in [first, last] (non-negative): returns the number of arguments
+    whose erf downweighting is not exactly 1.0f and the largest of them (0.0 if none)."""
+    import numpy as np
+    import torch
+    lib = load()
+    lo = int(np.float32(first).view(np.uint32))
+    hi = int(np.float32(last).view(np.uint32))
+    count = torch.zeros(1, dtype=torch.int64, device='cuda')
+    max_bits = torch.zeros(1, dtype=torch.int32, device='cuda')
+    check(lib.zf_check_erf_saturation(lo, hi, count.data_ptr(), max_bits.data_ptr(), _stream(None)))
+    bits = np.array([max_bits.item()], np.int32).view(np.float32)[0]
+    return int(count.item()), float(bits)
 
 
 class CFeaturizer:

@@ -145,6 +145,15 @@ ZF_API int zf_featurize_debug(zf_featurizer* featurizer, const zf_rays* rays, co
                        float* x, float* scale, int32_t* contracted, int32_t* n_groups, uint32_t* rows, float* weights,
                        struct CUstream_st* stream);
 
+/* Numerics self-check of this build (no counterpart in the reference). The per-level erf downweighting
+ * sign(x) sqrt(1 - exp(-4 x^2 / pi)) of featurize_common.cuh:45-47 is evaluated for every float whose bit pattern lies in
+ * [first_bits, last_bits]; *n_not_one (device, zeroed by the caller) counts the arguments whose result is not exactly
+ * 1.0f and *max_bits (device, zeroed by the caller) receives the largest such bit pattern. The kernels skip the erf for
+ * arguments >= zf_erf_saturation_threshold(); the check over [threshold, +inf) must count 0 on every device. */
+ZF_API int zf_check_erf_saturation(uint32_t first_bits, uint32_t last_bits, unsigned long long* n_not_one, uint32_t* max_bits,
+                                   struct CUstream_st* stream);
+ZF_API float zf_erf_saturation_threshold(void);
+
 /* Message of the calling thread's last failed call ("" if none). */
 ZF_API const char* zf_last_error(void);
 

@@ -261,3 +261,15 @@ def test_unsupported_layouts_fail_loudly(capi, backend, cuda_device):
         capi.CFeaturizer(0, [16] * 17, [4096] * 17, 1, 0)
     with pytest.raises(RuntimeError, match='ZipNeRF: grid table too large'):
         backend.Featurizer(0, [2048, 2048], [2 ** 31, 2 ** 31], 4, 0)
+
+
+def test_erf_saturation_is_exact(capi, cuda_device):
+    """The kernels skip the erf downweighting for arguments >= the build's threshold and use exactly 1.0f: this holds
+    only if the fast-math erf of the reference's formula (featurize_common.cuh:45-47) is exactly 1.0f for every float
+    argument from the threshold to +inf, which is checked exhaustively on the device."""
+    threshold = capi.load().zf_erf_saturation_threshold()
+    n_not_one, largest = capi.check_erf_saturation(threshold)
+    assert n_not_one == 0, f'{n_not_one} arguments >= {threshold} give an erf below 1 (largest {largest})'
+    # and below the threshold the erf is not constant 1 (the early-out changes nothing there)
+    n_below, _ = capi.check_erf_saturation(0.0, 1.0)
+    assert n_below > 0
