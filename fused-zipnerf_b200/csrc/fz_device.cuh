@@ -157,7 +157,7 @@ __device__ __forceinline__ void multisample(const Frustum& fr, const uint32_t j,
 // and the square root of 1 is 1. zf_check_erf_saturation verifies that claim over every float in [threshold, +inf)
 // on the device (the GPU tests run it); below the threshold the erf is evaluated as the reference does.
 #ifndef ZF_ERF_SATURATION
-#define ZF_ERF_SATURATION 4.0f
+#define ZF_ERF_SATURATION 3.66f
 #endif
 constexpr float kErfSaturation = ZF_ERF_SATURATION;
 
@@ -209,27 +209,50 @@ __device__ __forceinline__ void visit_level(const GridParams& gp, const uint32_t
     }
     uint32_t remaining = (1u << kMultisamples) - 1u;
     while (remaining != 0u) {
+        // the group of the lowest unvisited multisample (its leader): the leader's values by selection
         const uint32_t leader = __ffs(remaining) - 1u;
         int lx = cx[0], ly = cy[0], lz = cz[0];
+        float lfx = fx[0], lfy = fy[0], lfz = fz[0], lw = weighting[0];
         #pragma unroll
         for (uint32_t j = 1; j < kMultisamples; j++) {
             if (leader == j) {
                 lx = cx[j];
                 ly = cy[j];
                 lz = cz[j];
+                lfx = fx[j];
+                lfy = fy[j];
+                lfz = fz[j];
+                lw = weighting[j];
             }
         }
-        float corner_weights[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        uint32_t members = 0u;
         #pragma unroll
         for (uint32_t k = 0; k < kMultisamples; k++) {
-            if (!((remaining >> k) & 1u) || cx[k] != lx || cy[k] != ly || cz[k] != lz) continue;
-            remaining &= ~(1u << k);
+            if (((remaining >> k) & 1u) && cx[k] == lx && cy[k] == ly && cz[k] == lz) members |= 1u << k;
+        }
+        remaining &= ~members;
+        // corner weights: the leader's trilinear weights, then the other members' in multisample order (most groups of
+        // the fine levels are single multisamples, which skip the member loop)
+        float corner_weights[8];
+        #pragma unroll
+        for (uint32_t corner = 0; corner < 8; corner++) {
+            const float wx = corner & 4u ? lfx : 1.0f - lfx;
+            const float wy = corner & 2u ? lfy : 1.0f - lfy;
+            const float wz = corner & 1u ? lfz : 1.0f - lfz;
+            corner_weights[corner] = __fmaf_rn(lw, __fmul_rn(__fmul_rn(wx, wy), wz), 0.0f);
+        }
+        const uint32_t others = members & ~(1u << leader);
+        if (others != 0u) {
             #pragma unroll
-            for (uint32_t corner = 0; corner < 8; corner++) {
-                const float wx = corner & 4u ? fx[k] : 1.0f - fx[k];
-                const float wy = corner & 2u ? fy[k] : 1.0f - fy[k];
-                const float wz = corner & 1u ? fz[k] : 1.0f - fz[k];
-                corner_weights[corner] = __fmaf_rn(weighting[k], __fmul_rn(__fmul_rn(wx, wy), wz), corner_weights[corner]);
+            for (uint32_t k = 1; k < kMultisamples; k++) {
+                if (!((others >> k) & 1u)) continue;
+                #pragma unroll
+                for (uint32_t corner = 0; corner < 8; corner++) {
+                    const float wx = corner & 4u ? fx[k] : 1.0f - fx[k];
+                    const float wy = corner & 2u ? fy[k] : 1.0f - fy[k];
+                    const float wz = corner & 1u ? fz[k] : 1.0f - fz[k];
+                    corner_weights[corner] = __fmaf_rn(weighting[k], __fmul_rn(__fmul_rn(wx, wy), wz), corner_weights[corner]);
+                }
             }
         }
         #pragma unroll
