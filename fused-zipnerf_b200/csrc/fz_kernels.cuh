@@ -22,10 +22,10 @@ constexpr int kBlock = 128;
 #define ZF_MIN_BLOCKS_FORWARD_MLP 7
 #endif
 #ifndef ZF_MIN_BLOCKS_BACKWARD
-#define ZF_MIN_BLOCKS_BACKWARD 1
+#define ZF_MIN_BLOCKS_BACKWARD 4
 #endif
 #ifndef ZF_MIN_BLOCKS_BACKWARD_MLP
-#define ZF_MIN_BLOCKS_BACKWARD_MLP 2
+#define ZF_MIN_BLOCKS_BACKWARD_MLP 3
 #endif
 constexpr int kWarps = kBlock / 32;
 
