@@ -271,12 +271,19 @@ int zf_featurize_backward(zf_featurizer* f, const zf_backward_args* a, cudaStrea
     k.grad_features = a->grad_features;
     k.grad_stride = a->grad_features_stride;
     k.grad_scale = static_cast<float>(kNerfGridGradScale);
+    k.n_fp32_levels = static_cast<uint32_t>(f->n_fp32_grad_levels);
     k.grad_table = a->grad_table;
     k.grad_table_half = a->grad_table_half;
     const size_t smem = static_cast<size_t>(zf::backward_smem_floats(f->n_output_features())) * sizeof(float);
     const cudaError_t error = launch(f->kernels->backward, n_blocks(k.in.n_samples), smem, stream, f->params, k);
     if (error != cudaSuccess) return cuda_fail(error, "featurize_backward launch");
     return ZF_OK;
+}
+
+int64_t zf_featurize_backward_mlp_workspace_size(const zf_featurizer* f, const int64_t n_samples) {
+    if (f == nullptr || n_samples < 0) return 0;
+    // the scaled feature gradient of every sample, between the MLP and the scatter kernels
+    return n_samples * f->n_output_features() * static_cast<int64_t>(sizeof(float));
 }
 
 int zf_featurize_backward_mlp(zf_featurizer* f, const zf_backward_mlp_args* a, cudaStream_t stream) {
@@ -296,21 +303,52 @@ int zf_featurize_backward_mlp(zf_featurizer* f, const zf_backward_mlp_args* a, c
         a->grad_w1 == nullptr || a->grad_b1 == nullptr || (n_samples > 0 && (a->features == nullptr || a->grad_raw_density == nullptr))) {
         return fail(ZF_ERROR_INVALID_ARGUMENT, "backward_mlp tensors must be given");
     }
+    const int64_t workspace_bytes = zf_featurize_backward_mlp_workspace_size(f, n_samples);
+    if (a->workspace != nullptr && (a->workspace_bytes < workspace_bytes || !aligned(a->workspace, 16))) {
+        return fail(ZF_ERROR_INVALID_ARGUMENT, "workspace too small or not 16-byte aligned");
+    }
     if (n_samples == 0) return ZF_OK;
-    const size_t smem = static_cast<size_t>(zf::backward_mlp_smem_floats(n_out, zf::mlp_pad(n_out), f->mlp_width)) * sizeof(float);
+    float* rows = static_cast<float*>(a->workspace);
+    if (rows == nullptr) {
+        const cudaError_t error = cudaMallocAsync(reinterpret_cast<void**>(&rows), static_cast<size_t>(workspace_bytes), stream);
+        if (error != cudaSuccess) return cuda_fail(error, "backward_mlp workspace allocation");
+    }
     k.features = a->features;
     k.grad_raw_density = a->grad_raw_density;
     k.w0 = a->w0;
     k.b0 = a->b0;
     k.w1 = a->w1;
     k.mlp_width = f->mlp_width;
-    k.grad_table = a->grad_table;
+    k.grad_rows = rows;
     k.grad_w0 = a->grad_w0;
     k.grad_b0 = a->grad_b0;
     k.grad_w1 = a->grad_w1;
     k.grad_b1 = a->grad_b1;
-    const unsigned blocks = std::min<unsigned>(n_blocks(n_samples), static_cast<unsigned>(f->n_sms * kBackwardMlpBlocksPerSm));
-    const cudaError_t error = launch(f->mlp_kernels->backward_mlp, blocks, smem, stream, f->params, k);
+    // one resident wave of the MLP kernel (its per-block parameter sums end in one atomic per parameter and block)
+    const size_t smem = static_cast<size_t>(zf::backward_mlp_smem_floats(n_out, zf::mlp_pad(n_out), f->mlp_width)) * sizeof(float);
+    cudaError_t error = ensure_smem(reinterpret_cast<const void*>(f->mlp_kernels->backward_mlp), smem);
+    int resident = 0;
+    if (error == cudaSuccess) error = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, reinterpret_cast<const void*>(f->mlp_kernels->backward_mlp), zf::kBlock, smem);
+    if (error == cudaSuccess) {
+        const unsigned blocks = std::min<unsigned>(n_blocks(n_samples), static_cast<unsigned>(f->n_sms * std::max(resident, 1)));
+        error = launch(f->mlp_kernels->backward_mlp, blocks, smem, stream, f->params, k);
+    }
+    if (error == cudaSuccess) {
+        // the scatter of the scaled feature gradients into the fp32 grid gradient (all levels), skipping samples with a
+        // zero raw density gradient (featurize_backward_mlp.cu:103-108)
+        zf::BackwardArgs s{};
+        s.in = k.in;
+        s.grad_rows = rows;
+        s.skip_if_zero = a->grad_raw_density;
+        s.n_fp32_levels = static_cast<uint32_t>(f->n_levels);
+        s.grad_table = a->grad_table;
+        const size_t scatter_smem = static_cast<size_t>(zf::backward_smem_floats(n_out)) * sizeof(float);
+        error = launch(f->kernels->backward, n_blocks(n_samples), scatter_smem, stream, f->params, s);
+    }
+    if (a->workspace == nullptr) {
+        const cudaError_t free_error = cudaFreeAsync(rows, stream);
+        if (error == cudaSuccess) error = free_error;
+    }
     if (error != cudaSuccess) return cuda_fail(error, "featurize_backward_mlp launch");
     return ZF_OK;
 }

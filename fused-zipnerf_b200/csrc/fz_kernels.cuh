@@ -126,15 +126,15 @@ __device__ __forceinline__ void featurize_to_row(const GridParams& gp, const Fru
     }
 }
 
-// (row, column) of the elements e = lane, lane + 32, ... of a row-major [rows, cols] block, advanced without a
-// division per element
+// (row, column) of the elements e = first, first + step, ... of a row-major [rows, cols] block (step 32: a warp's
+// lanes, kBlock: a block's threads), advanced without a division per element
 struct LaneWalk {
     int r, c, dr, dc, cols;
-    __device__ __forceinline__ LaneWalk(const int lane, const int n_cols) : cols(n_cols) {
-        r = lane / n_cols;
-        c = lane - r * n_cols;
-        dr = 32 / n_cols;
-        dc = 32 - dr * n_cols;
+    __device__ __forceinline__ LaneWalk(const int first, const int n_cols, const int step = 32) : cols(n_cols) {
+        r = first / n_cols;
+        c = first - r * n_cols;
+        dr = step / n_cols;
+        dc = step - dr * n_cols;
     }
     __device__ __forceinline__ void next() {
         r += dr;
@@ -348,9 +348,12 @@ __device__ __forceinline__ void scatter_row(const GridParams& gp, const Frustum&
 
 struct BackwardArgs {
     RayInputs in;
-    const uint16_t* grad_features;  // bf16 [n_samples, >= n_out], row stride grad_stride
+    const uint16_t* grad_features;  // bf16 [n_samples, >= n_out], row stride grad_stride (NeRF level)
     long long grad_stride;
     float grad_scale;
+    const float* grad_rows;         // or: fp32 [n_samples, n_out] feature gradients, already scaled (proposal levels)
+    const float* skip_if_zero;      // optional [n_samples]: samples whose value is 0 are not scattered
+    uint32_t n_fp32_levels;         // leading levels scattered into grad_table (fp32), the rest into grad_table_half
     float* grad_table;              // fp32 [n_fp32_rows, F]
     uint16_t* grad_table_half;      // fp16 [rows - n_fp32_rows, F]
 };
@@ -365,24 +368,33 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_ke
     if (warp_first >= a.in.n_samples) return;
     const int n_rows = min(32, static_cast<int>(a.in.n_samples - warp_first));
     float* warp_rows = smem + warp * 32 * stride;
-    // coalesced load of the warp's gradient rows, scaled as the reference (feature_scale * grad_scale * g)
-    for (LaneWalk w(lane, n_out); w.r < n_rows; w.next()) {
-        const int r = w.r, c = w.c;
-        const uint16_t bits = __ldcs(a.grad_features + static_cast<size_t>(warp_first + r) * a.grad_stride + c);
-        warp_rows[r * stride + c] = kFeatureScale * a.grad_scale * bf16_bits_to_f32(bits);
+    // coalesced load of the warp's gradient rows
+    if (a.grad_rows != nullptr) {
+        for (LaneWalk w(lane, n_out); w.r < n_rows; w.next()) {
+            warp_rows[w.r * stride + w.c] = __ldcs(a.grad_rows + static_cast<size_t>(warp_first + w.r) * n_out + w.c);
+        }
+    }
+    else {
+        // bf16 feature gradients, scaled as the reference (feature_scale * grad_scale * g, featurize_backward.cu:24)
+        for (LaneWalk w(lane, n_out); w.r < n_rows; w.next()) {
+            const uint16_t bits = __ldcs(a.grad_features + static_cast<size_t>(warp_first + w.r) * a.grad_stride + w.c);
+            warp_rows[w.r * stride + w.c] = kFeatureScale * a.grad_scale * bf16_bits_to_f32(bits);
+        }
     }
     __syncwarp();
     if (lane >= n_rows) return;
     const uint32_t sample = warp_first + lane;
+    if (a.skip_if_zero != nullptr && __ldcs(a.skip_if_zero + sample) == 0.0f) return;
     const Frustum fr = setup_frustum(a.in, gp.pattern_stream, sample);
-    scatter_row<F>(gp, fr, warp_rows + lane * stride, 1, gp.n_fp32_levels, a.grad_table, a.grad_table_half);
+    scatter_row<F>(gp, fr, warp_rows + lane * stride, 1, a.n_fp32_levels, a.grad_table, a.grad_table_half);
 }
 
 __host__ __device__ constexpr int backward_smem_floats(const int n_out) { return kBlock * staged_stride(n_out); }
 
 // ---------------------------------------------------------------------------------------------------------------------
-// proposal-level backward: recompute the fused MLP from the stored fp32 features, scatter the input gradient into the
-// fp32 grid gradient, and reduce the MLP parameter gradients (featurize_backward_mlp.cu:79-147)
+// proposal-level backward, MLP part (featurize_backward_mlp.cu:79-147 without the scatter): recomputes the fused MLP
+// from the stored fp32 features, writes the scaled input gradient of every sample to grad_rows (the scatter kernel
+// adds it to the grid gradient), and reduces the MLP parameter gradients
 //
 // with a_j = [pre_j > 0] g: grad_w0[j][i] = w1_j sum a_j f_i, grad_b0[j] = w1_j sum a_j, grad_w1[j] = sum g relu(pre_j),
 // grad_b1 = sum g
@@ -395,7 +407,7 @@ struct BackwardMlpArgs {
     const float* b0;                // [W]
     const float* w1;                // [W]
     int mlp_width;
-    float* grad_table;              // [rows, F]
+    float* grad_rows;               // out: [n_samples, n_out] feature gradients times feature_scale
     float* grad_w0;
     float* grad_b0;
     float* grad_w1;
@@ -409,7 +421,7 @@ __host__ __device__ constexpr int backward_mlp_smem_floats(const int n_out, cons
     return width * nout_pad + 2 * width                       // weights (w0 rows padded to nout_pad), b0, w1
         + (width * n_out + 2 * width + 1)                     // parameter gradient sums of the block
         + ((width + 3) / 4 * 4) * column_stride()             // pre-activations [j][sample]
-        + nout_pad * column_stride()                          // feature gradient, then features [i][sample]
+        + 2 * nout_pad * column_stride()                      // features and feature gradients [i][sample]
         + kBlock;                                             // raw density gradients
 }
 
@@ -427,8 +439,9 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_backwar
     float* s_w1 = s_b0 + W;
     float* s_acc = s_w1 + W;                   // [n_params] (the reference's output order: w0, b0, w1, b1)
     float* s_pre = s_acc + n_params;           // [w_pad][cs]
-    float* s_col = s_pre + w_pad * cs;         // [NOUT_PAD][cs]
-    float* s_g = s_col + NOUT_PAD * cs;        // [kBlock]
+    float* s_col = s_pre + w_pad * cs;         // [NOUT_PAD][cs] features
+    float* s_gcol = s_col + NOUT_PAD * cs;     // [NOUT_PAD][cs] scaled feature gradients
+    float* s_g = s_gcol + NOUT_PAD * cs;       // [kBlock]
     for (int i = threadIdx.x; i < W * NOUT_PAD; i += kBlock) {
         const int j = i / NOUT_PAD, c = i - j * NOUT_PAD;
         s_w0[i] = c < n_out ? __ldg(a.w0 + j * n_out + c) : 0.0f;
@@ -446,8 +459,7 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_backwar
 
     // block-uniform loop bound, so every thread reaches the barriers
     for (uint32_t base = blockIdx.x * kBlock; base < a.in.n_samples; base += gridDim.x * kBlock) {
-        // phase 1, one sample per thread: MLP recomputation (featurize_backward_mlp.cu:82-99), the input gradient, and
-        // its scatter into the grid gradient
+        // phase 1, one sample per thread: MLP recomputation and its input gradient (featurize_backward_mlp.cu:82-105)
         const uint32_t sample = base + threadIdx.x;
         const bool active = sample < a.in.n_samples;
         float f[NOUT_PAD];
@@ -482,18 +494,18 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_backwar
             }
         }
         s_g[threadIdx.x] = g;
-        float* column = s_col + threadIdx.x;
-        if (active && g != 0.0f) {
-            #pragma unroll
-            for (int i = 0; i < NOUT_PAD; i++) {
-                if (i < n_out) column[i * cs] = __fmul_rn(grad_f[i], kFeatureScale);
-            }
-            const Frustum fr = setup_frustum(a.in, gp.pattern_stream, sample);
-            scatter_row<F>(gp, fr, column, cs, gp.n_levels, a.grad_table, nullptr);
-        }
         #pragma unroll
-        for (int i = 0; i < NOUT_PAD; i++) column[i * cs] = f[i];
+        for (int i = 0; i < NOUT_PAD; i++) {
+            s_col[i * cs + threadIdx.x] = f[i];
+            s_gcol[i * cs + threadIdx.x] = __fmul_rn(grad_f[i], kFeatureScale);
+        }
         __syncthreads();
+
+        // the block's scaled feature gradients to grad_rows, coalesced (rows of consecutive samples are contiguous)
+        const int n_rows = min(kBlock, static_cast<int>(a.in.n_samples - base));
+        for (LaneWalk w(threadIdx.x, n_out, kBlock); w.r < n_rows; w.next()) {
+            __stcs(a.grad_rows + (static_cast<size_t>(base) + w.r) * n_out + w.c, s_gcol[w.c * cs + w.r]);
+        }
 
         // phase 2: the block's parameter gradient sums over its samples, in sample order per output (as the reference's
         // featurize_backward_mlp.cu:110-135): 4 x 4 tiles of grad_w0 (a register-blocked outer product of

@@ -190,6 +190,12 @@ public:
         a.grad_w1 = grad_w1.data_ptr<float>();
         a.grad_b1 = grad_b1.data_ptr<float>();
         const c10::cuda::CUDAGuard guard(origins.device());
+        // the workspace between the MLP and the scatter kernels comes from PyTorch's caching allocator (stream-ordered on
+        // the current stream, returned to the cache when this call's tensor goes out of scope)
+        const int64_t workspace_bytes = zf_featurize_backward_mlp_workspace_size(m_featurizer, n_samples);
+        at::Tensor workspace = at::empty({workspace_bytes}, origins.options().dtype(at::kByte));
+        a.workspace = workspace.data_ptr();
+        a.workspace_bytes = workspace_bytes;
         check_status(zf_featurize_backward_mlp(m_featurizer, &a, current_stream()));
     }
 

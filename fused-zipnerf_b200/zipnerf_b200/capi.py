@@ -15,7 +15,8 @@ LIBRARY = Path(__file__).resolve().parent.parent / 'ZipNeRFCudaBackend' / 'libzf
 ZF_OK, ZF_ERROR_INVALID_ARGUMENT, ZF_ERROR_UNSUPPORTED, ZF_ERROR_CUDA = 0, 1, 2, 3
 
 EXPORTED = ['zf_featurizer_create', 'zf_featurizer_destroy', 'zf_featurizer_n_output_features', 'zf_featurizer_n_fp32_grad_rows',
-            'zf_featurizer_n_rows', 'zf_featurize_forward', 'zf_featurize_backward', 'zf_featurize_backward_mlp', 'zf_featurize_debug',
+            'zf_featurizer_n_rows', 'zf_featurize_forward', 'zf_featurize_backward', 'zf_featurize_backward_mlp',
+            'zf_featurize_backward_mlp_workspace_size', 'zf_featurize_debug',
             'zf_check_erf_saturation', 'zf_erf_saturation_threshold', 'zf_last_error', 'zf_grid_max_value', 'zf_nerf_grid_grad_scale']
 
 _p = ctypes.c_void_p
@@ -42,7 +43,8 @@ class zf_backward_args(ctypes.Structure):
 class zf_backward_mlp_args(ctypes.Structure):
     _fields_ = [('rays', zf_rays), ('features', _p), ('features_numel', _i64), ('grad_raw_density', _p),
                 ('grad_raw_density_numel', _i64), ('w0', _p), ('b0', _p), ('w1', _p), ('w0_numel', _i64), ('grad_table', _p),
-                ('grad_table_numel', _i64), ('grad_w0', _p), ('grad_w0_numel', _i64), ('grad_b0', _p), ('grad_w1', _p), ('grad_b1', _p)]
+                ('grad_table_numel', _i64), ('grad_w0', _p), ('grad_w0_numel', _i64), ('grad_b0', _p), ('grad_w1', _p), ('grad_b1', _p),
+                ('workspace', _p), ('workspace_bytes', _i64)]
 
 
 class ZfError(RuntimeError):
@@ -76,6 +78,8 @@ def load() -> ctypes.CDLL:
     lib.zf_featurize_forward.argtypes = [_p, ctypes.POINTER(zf_forward_args), _p]
     lib.zf_featurize_backward.argtypes = [_p, ctypes.POINTER(zf_backward_args), _p]
     lib.zf_featurize_backward_mlp.argtypes = [_p, ctypes.POINTER(zf_backward_mlp_args), _p]
+    lib.zf_featurize_backward_mlp_workspace_size.argtypes = [_p, _i64]
+    lib.zf_featurize_backward_mlp_workspace_size.restype = _i64
     lib.zf_featurize_debug.argtypes = [_p, ctypes.POINTER(zf_rays), _p, _i64, _p, _p, _p, _p, _p, _p, _p]
     for name in ['zf_featurize_forward', 'zf_featurize_backward', 'zf_featurize_backward_mlp', 'zf_featurize_debug']:
         getattr(lib, name).restype = ctypes.c_int
@@ -162,12 +166,16 @@ class CFeaturizer:
         check(load().zf_featurize_backward(self.handle, ctypes.byref(a), _stream(stream)))
 
     def backward_mlp(self, origins, directions, radii, tdist, pattern_seed, features, grad_raw_density, w0, b0, w1, grad_table,
-                     grad_w0, grad_b0, grad_w1, grad_b1, stream=None) -> None:
+                     grad_w0, grad_b0, grad_w1, grad_b1, workspace=None, stream=None) -> None:
+        """workspace: optional uint8 CUDA tensor of workspace_size(n_samples) bytes (None: allocated per call)."""
         a = zf_backward_mlp_args(self.rays(origins, directions, radii, tdist, pattern_seed), _ptr(features), features.numel(),
                                  _ptr(grad_raw_density), grad_raw_density.numel(), _ptr(w0), _ptr(b0), _ptr(w1), w0.numel(),
                                  _ptr(grad_table), grad_table.numel(), _ptr(grad_w0), grad_w0.numel(), _ptr(grad_b0), _ptr(grad_w1),
-                                 _ptr(grad_b1))
+                                 _ptr(grad_b1), _ptr(workspace), workspace.numel() if workspace is not None else 0)
         check(load().zf_featurize_backward_mlp(self.handle, ctypes.byref(a), _stream(stream)))
+
+    def workspace_size(self, n_samples: int) -> int:
+        return load().zf_featurize_backward_mlp_workspace_size(self.handle, n_samples)
 
     def debug(self, origins, directions, radii, tdist, pattern_seed, samples, stream=None) -> dict:
         """Intermediate values of the given samples (int32 CUDA tensor): x, scale, contracted, n_groups, rows, weights."""

@@ -110,6 +110,10 @@ typedef struct zf_backward_mlp_args {
     float* grad_b0;                      /* [mlp_width] */
     float* grad_w1;                      /* [mlp_width] */
     float* grad_b1;                      /* [1] */
+    void* workspace;                     /* optional device scratch (16-byte aligned) of at least
+                                            zf_featurize_backward_mlp_workspace_size() bytes; NULL: the call allocates it
+                                            from the stream-ordered pool (cudaMallocAsync) and frees it after use */
+    int64_t workspace_bytes;
 } zf_backward_mlp_args;
 
 /* Creates a featurizer for one sampling level (Featurizer ctor, featurizer.h:25 / featurizer.cu:145-155) on the
@@ -133,8 +137,12 @@ ZF_API int64_t zf_featurizer_n_rows(const zf_featurizer* featurizer);
 ZF_API int zf_featurize_forward(zf_featurizer* featurizer, const zf_forward_args* args, struct CUstream_st* stream);
 /* Featurizer::backward (featurizer.cu:266-299) */
 ZF_API int zf_featurize_backward(zf_featurizer* featurizer, const zf_backward_args* args, struct CUstream_st* stream);
-/* Featurizer::backward_mlp (featurizer.cu:301-355) */
+/* Featurizer::backward_mlp (featurizer.cu:301-355). Runs as two kernels: the MLP recomputation with the parameter
+ * gradient reduction, which writes each sample's feature gradient to the workspace, and the scatter of those into
+ * grad_table. */
 ZF_API int zf_featurize_backward_mlp(zf_featurizer* featurizer, const zf_backward_mlp_args* args, struct CUstream_st* stream);
+/* workspace bytes of zf_featurize_backward_mlp for n_samples intervals (n_samples * n_output_features floats) */
+ZF_API int64_t zf_featurize_backward_mlp_workspace_size(const zf_featurizer* featurizer, int64_t n_samples);
 
 /* Intermediate values of the listed samples, for exact checks of sample placement, contraction and hashing. No
  * counterpart in the reference (whose kernels keep these in registers). Outputs (device memory, n = n_debug):
