@@ -394,6 +394,70 @@ int zf_check_erf_saturation(const uint32_t first_bits, const uint32_t last_bits,
 
 float zf_erf_saturation_threshold(void) { return zf::kErfSaturation; }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------------------------------
+// Allocation-free variant of the proposal-level backward, for hosts that must not allocate device memory while they run:
+// a host that plans a fixed device-memory budget up front, or a plugin inside a framework that owns every device
+// allocation and does not let its plugins call cudaMalloc / cudaMallocAsync, and that cannot hand this library a
+// workspace either. Its workspace is this file-scope device array instead: every GPU that loads the library holds it
+// (kStaticWorkspaceBytes) until the process exits, and every call on a device shares it.
+
+namespace {
+
+constexpr size_t kStaticWorkspaceBytes = size_t(32) << 20;  // 32 MiB: n_samples * n_output_features * 4 bytes at most
+constexpr int kMaxDevices = 64;
+
+}  // namespace
+
+static __device__ __align__(256) unsigned char zf_static_workspace[kStaticWorkspaceBytes];
+
+namespace {
+
+// device address of zf_static_workspace on the current device, looked up once per device with that device current
+int static_workspace_address(void** address) {
+    static std::mutex mutex;
+    static void* addresses[kMaxDevices] = {};
+    int device = 0;
+    cudaError_t error = cudaGetDevice(&device);
+    if (error != cudaSuccess) return cuda_fail(error, "cudaGetDevice");
+    if (device < 0 || device >= kMaxDevices) return fail(ZF_ERROR_UNSUPPORTED, "device index beyond the static workspace table");
+    std::lock_guard<std::mutex> lock(mutex);
+    if (addresses[device] == nullptr) {
+        void* ptr = nullptr;
+        error = cudaGetSymbolAddress(&ptr, zf_static_workspace);
+        if (error != cudaSuccess) return cuda_fail(error, "cudaGetSymbolAddress of the static workspace");
+        addresses[device] = ptr;
+    }
+    *address = addresses[device];
+    return ZF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int zf_featurize_backward_mlp_no_alloc(zf_featurizer* f, const zf_backward_mlp_args* a, cudaStream_t stream) {
+    if (f == nullptr || a == nullptr) return fail(ZF_ERROR_INVALID_ARGUMENT, "featurizer and arguments must not be null");
+    if (a->rays.n_rays < 0 || a->rays.n_intervals < 1) return fail(ZF_ERROR_INVALID_ARGUMENT, "tdist must have at least two columns");
+    const int64_t n_samples = a->rays.n_rays * a->rays.n_intervals;
+    const int64_t needed = zf_featurize_backward_mlp_workspace_size(f, n_samples);
+    if (needed > static_cast<int64_t>(kStaticWorkspaceBytes)) {
+        const int64_t limit = static_cast<int64_t>(kStaticWorkspaceBytes) / (f->n_output_features() * static_cast<int64_t>(sizeof(float)));
+        return fail(ZF_ERROR_INVALID_ARGUMENT, "backward_mlp without allocation supports at most " + std::to_string(limit) +
+                    " samples of this featurizer (a static 32 MiB workspace); got " + std::to_string(n_samples));
+    }
+    void* workspace = nullptr;
+    const int rc = static_workspace_address(&workspace);
+    if (rc != ZF_OK) return rc;
+    // the MLP kernel writes every workspace row before the scatter kernel reads it, so nothing needs clearing
+    zf_backward_mlp_args args = *a;
+    args.workspace = workspace;
+    args.workspace_bytes = static_cast<int64_t>(kStaticWorkspaceBytes);
+    return zf_featurize_backward_mlp(f, &args, stream);
+}
+
+
 const char* zf_last_error(void) { return last_error.c_str(); }
 
 double zf_grid_max_value(void) { return kGridMaxValue; }

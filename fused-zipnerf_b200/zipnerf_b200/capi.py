@@ -1,8 +1,8 @@
 """ctypes binding of the C ABI in include/zf_featurize.h (libzf_featurize.so).
 
-This is the binding a non-PyTorch host would write against the library (INTEGRATION.md shows it beside the other
-language stubs). ``CFeaturizer`` adds a thin convenience layer that takes PyTorch CUDA tensors and passes their device
-pointers; the computation happens in the library. No CPU fallback exists: calls fail with ``ZfError`` when the
+This is the binding a Python host without the PyTorch extension would write against the library. ``CFeaturizer``
+adds a thin convenience layer that takes PyTorch CUDA tensors and passes their device pointers; the computation
+happens in the library. No CPU fallback exists: calls fail with ``ZfError`` when the
 library reports an error, and loading fails when the library is not built.
 """
 from __future__ import annotations
@@ -16,7 +16,7 @@ ZF_OK, ZF_ERROR_INVALID_ARGUMENT, ZF_ERROR_UNSUPPORTED, ZF_ERROR_CUDA = 0, 1, 2,
 
 EXPORTED = ['zf_featurizer_create', 'zf_featurizer_destroy', 'zf_featurizer_n_output_features', 'zf_featurizer_n_fp32_grad_rows',
             'zf_featurizer_n_rows', 'zf_featurize_forward', 'zf_featurize_backward', 'zf_featurize_backward_mlp',
-            'zf_featurize_backward_mlp_workspace_size', 'zf_featurize_debug',
+            'zf_featurize_backward_mlp_workspace_size', 'zf_featurize_backward_mlp_no_alloc', 'zf_featurize_debug',
             'zf_check_erf_saturation', 'zf_erf_saturation_threshold', 'zf_last_error', 'zf_grid_max_value', 'zf_nerf_grid_grad_scale']
 
 _p = ctypes.c_void_p
@@ -78,6 +78,8 @@ def load() -> ctypes.CDLL:
     lib.zf_featurize_forward.argtypes = [_p, ctypes.POINTER(zf_forward_args), _p]
     lib.zf_featurize_backward.argtypes = [_p, ctypes.POINTER(zf_backward_args), _p]
     lib.zf_featurize_backward_mlp.argtypes = [_p, ctypes.POINTER(zf_backward_mlp_args), _p]
+    lib.zf_featurize_backward_mlp_no_alloc.argtypes = [_p, ctypes.POINTER(zf_backward_mlp_args), _p]
+    lib.zf_featurize_backward_mlp_no_alloc.restype = ctypes.c_int
     lib.zf_featurize_backward_mlp_workspace_size.argtypes = [_p, _i64]
     lib.zf_featurize_backward_mlp_workspace_size.restype = _i64
     lib.zf_featurize_debug.argtypes = [_p, ctypes.POINTER(zf_rays), _p, _i64, _p, _p, _p, _p, _p, _p, _p]
@@ -173,6 +175,15 @@ class CFeaturizer:
                                  _ptr(grad_table), grad_table.numel(), _ptr(grad_w0), grad_w0.numel(), _ptr(grad_b0), _ptr(grad_w1),
                                  _ptr(grad_b1), _ptr(workspace), workspace.numel() if workspace is not None else 0)
         check(load().zf_featurize_backward_mlp(self.handle, ctypes.byref(a), _stream(stream)))
+
+    def backward_mlp_no_alloc(self, origins, directions, radii, tdist, pattern_seed, features, grad_raw_density, w0, b0, w1, grad_table,
+                              grad_w0, grad_b0, grad_w1, grad_b1, stream=None) -> None:
+        """backward_mlp through zf_featurize_backward_mlp_no_alloc (the library's static workspace; no allocation)."""
+        a = zf_backward_mlp_args(self.rays(origins, directions, radii, tdist, pattern_seed), _ptr(features), features.numel(),
+                                 _ptr(grad_raw_density), grad_raw_density.numel(), _ptr(w0), _ptr(b0), _ptr(w1), w0.numel(),
+                                 _ptr(grad_table), grad_table.numel(), _ptr(grad_w0), grad_w0.numel(), _ptr(grad_b0), _ptr(grad_w1),
+                                 _ptr(grad_b1), None, 0)
+        check(load().zf_featurize_backward_mlp_no_alloc(self.handle, ctypes.byref(a), _stream(stream)))
 
     def workspace_size(self, n_samples: int) -> int:
         return load().zf_featurize_backward_mlp_workspace_size(self.handle, n_samples)

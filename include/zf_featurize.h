@@ -143,6 +143,16 @@ ZF_API int zf_featurize_backward(zf_featurizer* featurizer, const zf_backward_ar
 ZF_API int zf_featurize_backward_mlp(zf_featurizer* featurizer, const zf_backward_mlp_args* args, struct CUstream_st* stream);
 /* workspace bytes of zf_featurize_backward_mlp for n_samples intervals (n_samples * n_output_features floats) */
 ZF_API int64_t zf_featurize_backward_mlp_workspace_size(const zf_featurizer* featurizer, int64_t n_samples);
+/* zf_featurize_backward_mlp without any device allocation. No counterpart in the reference. For callers that must not
+ * allocate device memory while they run (a host with a fixed device-memory budget, or a plugin whose framework owns
+ * every device allocation) and cannot pass a workspace: the workspace is a static 32 MiB device array of this library,
+ * held by every GPU that loads it until the process exits, so a call takes at most
+ * 32 MiB / (4 * n_output_features) samples (419430 at 20 output features) and larger calls fail with
+ * ZF_ERROR_INVALID_ARGUMENT. args->workspace is ignored. The first call on a device looks up the array's address on that
+ * device (make it before any stream capture). All calls share the array: calls whose kernels overlap on the GPU (other
+ * streams, other threads) race and must be serialized by the caller. The array keeps the last call's contents; every
+ * call overwrites what it reads, so nothing needs clearing. */
+ZF_API int zf_featurize_backward_mlp_no_alloc(zf_featurizer* featurizer, const zf_backward_mlp_args* args, struct CUstream_st* stream);
 
 /* Intermediate values of the listed samples, for exact checks of sample placement, contraction and hashing. No
  * counterpart in the reference (whose kernels keep these in registers). Outputs (device memory, n = n_debug):
