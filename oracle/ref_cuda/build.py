@@ -4,8 +4,8 @@ For each layout variant below this writes the preamble that the reference's host
 compilation (featurizer.cu:157-184: JIT_* constants and the per-level layout functions; written here by this script
 from the layout, not copied) and compiles oracle/ref_cuda/ref_cuda.cu with the reference's kernel sources included
 from where they lie, with the reference's compile options (--use_fast_math, rtc_kernel.cu:49), for sm_100a, into
-oracle/_ref/cuda/libzfref_<variant>.so. Needs the reference sources (REFERENCE_ROOT, default /root/reference); the
-built libraries travel to the GPU box with the rest of oracle/_ref.
+oracle/_ref/cuda/libzfref_<variant>.so. Needs the reference sources (their root in the REFERENCE_ROOT environment
+variable when not at the default mount); the built libraries are shipped with the rest of oracle/_ref.
 
     python oracle/ref_cuda/build.py [--jobs N]
 """
@@ -49,7 +49,8 @@ def variants() -> dict:
 
 
 def preamble(level, sizes, entries, n_features, mlp_width) -> str:
-    """The JIT preamble of featurizer.cu:157-184 for one layout (integer typedefs come from <cstdint> here)."""
+    """The JIT preamble of featurizer.cu:157-184 for one layout (integer typedefs come from <cstdint> here; the switches'
+    unreachable default case falls through to the final return instead of stopping the kernel)."""
     n_levels = len(sizes)
     offsets = [0]
     for e in entries:
@@ -66,7 +67,7 @@ def preamble(level, sizes, entries, n_features, mlp_width) -> str:
         lines.append('    switch (level) {')
         for i, v in enumerate(values):
             lines.append(f'        case {i}: return {v};')
-        lines.append('        default: __trap();')
+        lines.append('        default: break;')  # unreachable (every level index is below JIT_N_LEVELS)
         lines.append('    }')
         lines.append('    return 0;')
         lines.append('}')
