@@ -129,14 +129,18 @@ class Step:
     """One featurization fwd+bwd step of a config 2 workload on one GPU, through the PyTorch binding (the
     reference's API). Buffers are allocated once; inputs can be refreshed from pinned host copies (e2e)."""
 
-    def __init__(self, workload, device) -> None:
+    def __init__(self, workload, device, rank: int = 0) -> None:
         import ZipNeRFCudaBackend as backend
+        from zipnerf_b200 import sharding
         from zipnerf_b200 import workloads as wl_mod
         self.device = device
         self.wl = workload.to(device)
         wl = self.wl
         self.props, self.nerf = wl.levels[:-1], wl.levels[-1]
         self.featurizers = [backend.Featurizer(l.level, l.sizes, l.entries, l.n_features, l.mlp_width) for l in wl.levels]
+        # this rank's rays follow the previous ranks' in the global batch (pattern random numbers of the whole batch)
+        for lvl, f in zip(wl.levels, self.featurizers):
+            f.sample_offset = sharding.sample_offset(rank * wl.n_rays, lvl.n_intervals)
         R = wl.n_rays
         g = torch.Generator(device='cpu').manual_seed(1234)
         self.empty = torch.empty(0, device=device)
@@ -330,13 +334,13 @@ def run_b200(args) -> None:
     if world > 1:
         import datetime
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120), device_id=device)
-    step = Step(workloads.config2(n_rays=args.rays, seed=1 + rank), device)
+    step = Step(workloads.config2(n_rays=args.rays, seed=1 + rank), device, rank)
     grads = step.grad_buffers()
 
     def exchange():
         if world > 1:
-            for buffer in grads:
-                dist.all_reduce(buffer)
+            from zipnerf_b200 import sharding
+            sharding.allreduce_gradients(grads)
 
     def barrier():
         if world > 1:

@@ -136,7 +136,9 @@ int check_rays(const zf_rays* rays, zf::RayInputs& in) {
     in.directions = rays->directions;
     in.radii = rays->radii;
     in.tdist = rays->tdist;
+    if (rays->sample_offset < 0) return fail(ZF_ERROR_INVALID_ARGUMENT, "sample_offset must not be negative");
     in.pattern_seed = rays->pattern_seed;
+    in.sample_offset = static_cast<unsigned long long>(rays->sample_offset);
     in.n_intervals = static_cast<uint32_t>(rays->n_intervals);
     in.n_samples = static_cast<uint32_t>(n_samples);
     return ZF_OK;

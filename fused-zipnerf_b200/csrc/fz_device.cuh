@@ -51,6 +51,7 @@ struct RayInputs {
     const float* radii;       // [n_rays]
     const float* tdist;       // [n_rays, n_intervals + 1]
     long long pattern_seed;   // < 0: deterministic alternating patterns
+    unsigned long long sample_offset;  // added to the sample index of the pattern random numbers (batch shards)
     uint32_t n_intervals;
     uint32_t n_samples;       // n_rays * n_intervals
 };
@@ -124,8 +125,9 @@ __device__ __forceinline__ Frustum setup_frustum(const RayInputs& in, const unsi
     fr.root = sqrtf(fmaxf(q * q + 4.0f * s * s * s * s, 0.0f));
     if (in.pattern_seed >= 0) {
         const unsigned long long seed = static_cast<unsigned long long>(in.pattern_seed);
-        fr.flip = rng_uniform(seed, pattern_stream, 2ull * sample) < 0.5f;
-        fr.rotation = 2.0f * 3.14159265358979f * rng_uniform(seed, pattern_stream, 2ull * sample + 1);
+        const unsigned long long index = in.sample_offset + sample;
+        fr.flip = rng_uniform(seed, pattern_stream, 2ull * index) < 0.5f;
+        fr.rotation = 2.0f * 3.14159265358979f * rng_uniform(seed, pattern_stream, 2ull * index + 1);
     }
     else {
         fr.flip = interval % 2 == 1;

@@ -241,9 +241,22 @@ private:
         rays.n_rays = n_rays;
         rays.n_intervals = tdist.size(1) - 1;
         rays.pattern_seed = pattern_seed;
+        rays.sample_offset = m_sample_offset;
     }
 
+public:
+    // batch index of the first sample of this featurizer's calls, for the pattern random numbers (0: the reference's
+    // behaviour; a data-parallel shard sets the index of its first sample in the global batch)
+    int64_t sample_offset() const { return m_sample_offset; }
+    void set_sample_offset(const int64_t offset) {
+        if (offset < 0) throw std::runtime_error("ZipNeRF: sample_offset must not be negative");
+        m_sample_offset = offset;
+    }
+
+private:
+
     zf_featurizer* m_featurizer = nullptr;
+    int64_t m_sample_offset = 0;
     int m_n_features = 0;
     int m_mlp_width = 0;
 };
@@ -262,6 +275,7 @@ PYBIND11_MODULE(_C, m) {
         .def(pybind11::init<int, const std::vector<int64_t>&, const std::vector<int64_t>&, int, int>())
         .def_property_readonly("n_fp32_grad_rows", &Featurizer::n_fp32_grad_rows)
         .def_property_readonly("n_output_features", &Featurizer::n_output_features)
+        .def_property("sample_offset", &Featurizer::sample_offset, &Featurizer::set_sample_offset)
         .def("forward", &Featurizer::forward)
         .def("backward", &Featurizer::backward)
         .def("backward_mlp", &Featurizer::backward_mlp)

@@ -25,7 +25,7 @@ _i64 = ctypes.c_int64
 
 class zf_rays(ctypes.Structure):
     _fields_ = [('origins', _p), ('directions', _p), ('radii', _p), ('tdist', _p), ('n_rays', _i64), ('n_intervals', _i64),
-                ('pattern_seed', _i64)]
+                ('pattern_seed', _i64), ('sample_offset', _i64)]
 
 
 class zf_forward_args(ctypes.Structure):
@@ -138,6 +138,7 @@ class CFeaturizer:
         check(lib.zf_featurizer_create(level, (_i64 * n)(*sizes), (_i64 * n)(*entries), n, n_features, mlp_width, ctypes.byref(handle)))
         self.handle = handle
         self.n_features, self.mlp_width = n_features, mlp_width
+        self.sample_offset = 0  # batch index of the first sample (pattern random numbers of a shard)
         self.n_output_features = lib.zf_featurizer_n_output_features(handle)
         self.n_fp32_grad_rows = lib.zf_featurizer_n_fp32_grad_rows(handle)
         self.n_rows = lib.zf_featurizer_n_rows(handle)
@@ -147,9 +148,9 @@ class CFeaturizer:
             _lib.zf_featurizer_destroy(self.handle)
             self.handle = None
 
-    @staticmethod
-    def rays(origins, directions, radii, tdist, pattern_seed: int) -> zf_rays:
-        return zf_rays(_ptr(origins), _ptr(directions), _ptr(radii), _ptr(tdist), tdist.shape[0], tdist.shape[1] - 1, pattern_seed)
+    def rays(self, origins, directions, radii, tdist, pattern_seed: int) -> zf_rays:
+        return zf_rays(_ptr(origins), _ptr(directions), _ptr(radii), _ptr(tdist), tdist.shape[0], tdist.shape[1] - 1, pattern_seed,
+                       self.sample_offset)
 
     def forward(self, origins, directions, radii, tdist, pattern_seed, interleave, table, scale_magnitudes, w0=None, b0=None, w1=None,
                 b1=None, raw_density=None, features_float=None, features_bf16=None, encoded_directions=None, nerf_inputs=None,

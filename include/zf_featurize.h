@@ -42,7 +42,9 @@ typedef struct zf_featurizer zf_featurizer;
 
 /* Rays and interval endpoints of one call (the first five tensor arguments of Featurizer::forward/backward/backward_mlp,
  * featurizer.h:36-40). pattern_seed >= 0 draws random multisample pattern flips and rotations from the counter-based
- * stream 16 + level (random.cuh:12); pattern_seed < 0 alternates flips with a pi/6 rotation. */
+ * stream 16 + level (random.cuh:12) at index sample_offset + sample; pattern_seed < 0 alternates flips with a pi/6
+ * rotation. sample_offset is 0 for the reference's behaviour; a shard of a larger batch passes the batch index of its
+ * first sample, so that the shards together draw exactly the patterns of the whole batch. */
 typedef struct zf_rays {
     const float* origins;
     const float* directions;
@@ -51,6 +53,7 @@ typedef struct zf_rays {
     int64_t n_rays;
     int64_t n_intervals;
     int64_t pattern_seed;
+    int64_t sample_offset;
 } zf_rays;
 
 /* Arguments of zf_featurize_forward (Featurizer::forward, featurizer.h:35-52). A NULL output is skipped, as an empty

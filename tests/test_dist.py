@@ -1,0 +1,84 @@
+"""Data-parallel host logic on two gloo ranks (CPU): ray shards partition the batch, the gradient all-reduce averages
+fp32 and fp16 buffers without fp16 overflow, and the featurization gradients of two ray shards (CPU oracle, one per
+rank) sum to the gradients of the whole batch."""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from zipnerf_b200 import sharding
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(('127.0.0.1', 0))
+        return s.getsockname()[1]
+
+
+def test_shard_ranges_partition_the_batch():
+    for n in [0, 1, 7, 65536, 65537]:
+        for world in [1, 2, 3, 8]:
+            covered = []
+            for rank in range(world):
+                start, count = sharding.shard_range(n, world, rank)
+                covered.extend(range(start, start + count))
+            assert covered == list(range(n))
+    with pytest.raises(ValueError):
+        sharding.shard_range(10, 2, 2)
+    assert sharding.sample_offset(3, 64) == 192
+
+
+def _worker(rank: int, world: int, port: int, queue) -> None:
+    os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port))
+    import datetime
+    dist.init_process_group('gloo', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        # averaging: fp16 values whose sum would overflow (2 x 40000 > 65504)
+        half = torch.full((4,), 40000.0, dtype=torch.float16)
+        single = torch.full((3,), float(rank + 1))
+        sharding.allreduce_gradients([half, single])
+        # featurization gradients of this rank's ray shard with the CPU oracle
+        import zf_testdata as td
+        from oracle.zf_oracle import GridSpec, Oracle
+        case = td.grids_case(4, 33, 5, -1)
+        grid = GridSpec(case['level'], case['sizes'], case['entries'], 4, 0)
+        start, count = sharding.shard_range(33, world, rank)
+        rays = [np.ascontiguousarray(case[k][start:start + count]) for k in ('origins', 'directions', 'radii', 'tdist')]
+        n = case['tdist'].shape[1] - 1
+        grad = np.ascontiguousarray(case['grad_features'][start * n:(start + count) * n])
+        g32, g16 = Oracle().backward(grid, *rays, case['seed'], grad)
+        g32 = torch.from_numpy(g32.copy())
+        sharding.allreduce_gradients([g32], average=False)
+        queue.put((rank, half.tolist(), single.tolist(), g32.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gradient_exchange():
+    ctx = mp.get_context('spawn')
+    queue = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_worker, args=(rank, 2, port, queue)) for rank in range(2)]
+    for p in procs:
+        p.start()
+    results = [queue.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    import zf_testdata as td
+    from oracle.zf_oracle import GridSpec, Oracle
+    case = td.grids_case(4, 33, 5, -1)
+    grid = GridSpec(case['level'], case['sizes'], case['entries'], 4, 0)
+    full32, _ = Oracle().backward(grid, *(case[k] for k in ('origins', 'directions', 'radii', 'tdist')), case['seed'],
+                                  np.ascontiguousarray(case['grad_features']))
+    for rank, half, single, g32 in results:
+        assert half == [40000.0] * 4, 'fp16 average overflowed'
+        assert single == [1.5] * 3
+        # the shards' summed gradients are the whole batch's, up to fp32 summation order
+        np.testing.assert_allclose(g32, full32, rtol=0, atol=1e-5 * float(np.abs(full32).max()))

@@ -273,3 +273,26 @@ def test_erf_saturation_is_exact(capi, cuda_device):
     # and below the threshold the erf is not constant 1 (the early-out changes nothing there)
     n_below, _ = capi.check_erf_saturation(0.0, 1.0)
     assert n_below > 0
+
+
+@pytest.mark.parametrize('name', ['config2prop_R24_P0', 'grids_F4_R33_I5_S37'])
+def test_ray_shards_reproduce_the_whole_batch(capi, cuda_device, name):
+    """Two ray shards with their sample offsets draw the random multisample patterns of the whole batch: the forward
+    outputs of the shards are bit-identical to the whole batch's rows."""
+    from zipnerf_b200 import sharding
+    case = CASES[name]
+    assert case['seed'] >= 0
+    whole = run_forward(capi.CFeaturizer(case['level'], case['sizes'], case['entries'], case['n_features'], case['mlp_width']), case, cuda_device)
+    R, n = case['tdist'].shape[0], case['tdist'].shape[1] - 1
+    for rank in range(2):
+        start, count = sharding.shard_range(R, 2, rank)
+        shard = dict(case)
+        for key in ('origins', 'directions', 'radii', 'tdist', 'encoded'):
+            if key in case:
+                shard[key] = np.ascontiguousarray(case[key][start:start + count])
+        f = capi.CFeaturizer(case['level'], case['sizes'], case['entries'], case['n_features'], case['mlp_width'])
+        f.sample_offset = sharding.sample_offset(start, n)
+        out = run_forward(f, shard, cuda_device)
+        for key in out:
+            expected = whole[key].reshape(R, n, -1)[start:start + count].reshape(out[key].shape)
+            np.testing.assert_array_equal(out[key], expected, err_msg=f'{key} of shard {rank}')
