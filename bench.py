@@ -317,12 +317,12 @@ def run_reference_arm(args) -> None:
         values.append(baseline.run())
     value = statistics.median(v['value'] for v in values)
     base = values[0]
-    print(json.dumps({'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': args.gpus, 'steps': args.steps,
+    emit({'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': args.gpus, 'steps': args.steps,
                       'warmup': args.warmup, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
                       'data': 'synthetic', 'config': {'workload': 'config2 (paper-shape training-step featurization), bounded ray sample on the host cores',
                                                       'rays': args.reference_rays},
                       'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': base['cores'], 'kind': base['kind'], 'sample': base['sample']},
-                      'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}))
+                      'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}})
 
 
 def run_b200(args) -> None:
@@ -412,7 +412,7 @@ def run_b200(args) -> None:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(result))
+        emit(result)
 
 
 def measure_e2e(step: Step, args, world: int, exchange, barrier) -> dict:
@@ -451,7 +451,22 @@ def measure_e2e(step: Step, args, world: int, exchange, barrier) -> dict:
             'd2h_bytes_per_step': d2h, 'api': 'ZipNeRFCudaBackend._C.Featurizer'}
 
 
+_RESULT_FD = None
+
+
+def emit(result: dict) -> None:
+    """Writes the one JSON line to the process's original standard output."""
+    line = (json.dumps(result) + '\n').encode()
+    os.write(_RESULT_FD if _RESULT_FD is not None else 1, line)
+
+
 def main() -> None:
+    global _RESULT_FD
+    # everything else written to standard output (library banners, e.g. NCCL's version line) goes to standard error,
+    # so that standard output carries exactly the result line
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument('--gpus', type=int, default=1)
     parser.add_argument('--steps', type=int, default=20)
