@@ -166,6 +166,49 @@ def config2(n_rays: int = 65536, seed: int = 1, samples=(64, 64, 32)) -> Workloa
     return Workload('config2', origins, directions, radii, encoded, levels, pattern_seed=seed)
 
 
+def morton_order(width: int, height: int) -> torch.Tensor:
+    """Pixel indices of a width x height image in Morton (Z) order (Renderer.pixel_order, Renderer.py:120-130)."""
+    def spread(v: torch.Tensor) -> torch.Tensor:
+        for shift, mask in ((8, 0x00FF00FF), (4, 0x0F0F0F0F), (2, 0x33333333), (1, 0x55555555)):
+            v = (v | (v << shift)) & mask
+        return v
+    y, x = torch.meshgrid(torch.arange(height), torch.arange(width), indexing='ij')
+    return (spread(x) | (spread(y) << 1)).flatten().argsort()
+
+
+def config3(n_rays: int | None = None, seed: int = 3, width: int = 1296, height: int = 840, focal: float = 1100.0,
+            samples=(64, 64, 32)) -> Workload:
+    """Inference render of one frame: a pinhole camera (focal length in pixels) on a radius-4 sphere looking at the
+    origin, rays of the pixels in Morton order (the first n_rays of them, all by default), deterministic patterns
+    (pattern seed -1), interval endpoints from the random piecewise-constant resampling as in config 2. Grids as in
+    config 2."""
+    g = torch.Generator().manual_seed(seed)
+    eye = torch.nn.functional.normalize(torch.randn(3, generator=g), dim=0) * 4.0
+    forward = torch.nn.functional.normalize(-eye, dim=0)
+    up = torch.tensor([0.0, 0.0, 1.0])
+    right = torch.nn.functional.normalize(torch.linalg.cross(forward, up), dim=0)
+    true_up = torch.linalg.cross(right, forward)
+    order = morton_order(width, height)
+    if n_rays is not None:
+        order = order[:n_rays]
+    px, py = (order % width).float() + 0.5, (order // width).float() + 0.5
+    local = torch.stack([(px - width / 2) / focal, -(py - height / 2) / focal, torch.ones_like(px)], dim=1)
+    directions = local[:, 0:1] * right + local[:, 1:2] * true_up + local[:, 2:3] * forward
+    R = order.numel()
+    origins = eye.expand(R, 3).contiguous()
+    radii = torch.full((R,), (2.0 / focal) / math.sqrt(12.0))  # pixel_radius: (1/fx + 1/fy) / sqrt(12) (utils.py:14-16)
+    encoded = torch.randn(R, ENCODED_WIDTH, generator=g).bfloat16()
+    levels = []
+    for level, n in enumerate(samples[:-1]):
+        sizes, entries = grid_layout(10, 21, 16, 512)
+        table, mags = _grid_params(sizes, entries, 1, g)
+        levels.append(Level(level, sizes, entries, 1, 64, resampled_tdist(R, n, g), table, mags, _proposal_mlp(len(sizes) * 2, 64, g)))
+    sizes, entries = grid_layout(10, 21, 16, 8192)
+    table, mags = _grid_params(sizes, entries, 4, g)
+    levels.append(Level(len(samples) - 1, sizes, entries, 4, 0, resampled_tdist(R, samples[-1], g), table, mags))
+    return Workload('config3', origins, directions.contiguous(), radii, encoded, levels, pattern_seed=-1)
+
+
 def config5(n_rays: int = 65536, seed: int = 5, n_intervals: int = 160) -> Workload:
     """Atomic-contention stress: origins within a 0.05-radius ball, directions within a 5 degree cone, one NeRF level
     of 12 x 4 features, table 2^22, resolutions 16 -> 16384."""

@@ -154,3 +154,70 @@ def test_backward_mlp_matches_reference_kernels(capi, cuda_device, name):
     torch.cuda.synchronize()
     for i, key in enumerate(['grid', 'w0', 'b0', 'w1', 'b1']):
         noise_limited_close(results[0][i], results[1][i], results[2][i], False, f'grad {key}')
+
+
+def workload_tensors(wl, lvl):
+    return (wl.origins, wl.directions, wl.radii, lvl.tdist)
+
+
+@needs_reference
+def test_inference_render_bit_exact_with_reference_kernels(capi, cuda_device):
+    """Config 3 (inference render): Morton-ordered pinhole rays of a 1296 x 840 frame (its first 16384 pixels),
+    deterministic patterns, the interleaved thread mapping, forward only: raw densities of both proposal levels and the
+    NeRF level's packed bf16 features and inputs equal the reference kernels' bit for bit."""
+    from zipnerf_b200 import workloads
+    wl = workloads.config3(n_rays=16384).to(cuda_device)
+    R = wl.n_rays
+    for lvl, variant in zip(wl.levels, ['config2_prop0', 'config2_prop1', 'config2_nerf']):
+        ref = RefCuda(variant)
+        ours = capi.CFeaturizer(lvl.level, lvl.sizes, lvl.entries, lvl.n_features, lvl.mlp_width)
+        outs = []
+        for f in (ours, ref):
+            if lvl.mlp_width:
+                raw = torch.full((R, lvl.n_intervals), float('nan'), device=cuda_device)
+                f.forward(*workload_tensors(wl, lvl), -1, True, lvl.table, lvl.scale_magnitudes, *lvl.mlp, raw_density=raw)
+                outs.append([raw])
+            else:
+                n = R * lvl.n_intervals
+                bf16 = torch.full((n, 56), -1.0, device=cuda_device, dtype=torch.bfloat16)
+                inputs = torch.zeros(n, 96, device=cuda_device, dtype=torch.bfloat16)
+                f.forward(*workload_tensors(wl, lvl), -1, True, lvl.table, lvl.scale_magnitudes, features_bf16=bf16,
+                          encoded_directions=wl.encoded_directions, nerf_inputs=inputs)
+                outs.append([bf16, inputs])
+        torch.cuda.synchronize()
+        for a, b in zip(*outs):
+            np.testing.assert_array_equal(as_bits(a), as_bits(b), err_msg=f'level {lvl.level}')
+
+
+@needs_reference
+def test_contention_stress_matches_reference_kernels(capi, cuda_device):
+    """Config 5 (atomic contention): rays from a 0.05-radius ball within a 5 degree cone, 160 intervals, 12 x 4
+    features, table 2^22; forward bit-exact, fp32 (levels 0-2) and fp16 (levels 3-11) gradients within the
+    reference's own repeat noise, although coarse rows receive thousands of contributions."""
+    from zipnerf_b200 import workloads
+    wl = workloads.config5(n_rays=1024).to(cuda_device)
+    lvl = wl.levels[0]
+    ref = RefCuda('config5')
+    ours = capi.CFeaturizer(lvl.level, lvl.sizes, lvl.entries, lvl.n_features, lvl.mlp_width)
+    n = wl.n_rays * lvl.n_intervals
+    feats = []
+    for f in (ours, ref):
+        out = torch.full((n, lvl.n_output_features), float('nan'), device=cuda_device)
+        f.forward(*workload_tensors(wl, lvl), wl.pattern_seed, False, lvl.table, lvl.scale_magnitudes, features_float=out)
+        feats.append(out)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(as_bits(feats[0]), as_bits(feats[1]))
+    g = torch.Generator().manual_seed(55)
+    grad = (torch.randn(n, 64, generator=g) * 1e-6).bfloat16().to(cuda_device)[:, :lvl.n_output_features]
+    split, rows = ours.n_fp32_grad_rows, ours.n_rows
+    results = []
+    for f in (ours, ref, ref):
+        g32 = torch.zeros(split * 4, device=cuda_device)
+        g16 = torch.zeros((rows - split) * 4, device=cuda_device, dtype=torch.float16)
+        f.backward(*workload_tensors(wl, lvl), wl.pattern_seed, grad, g32, g16)
+        results.append((g32, g16))
+    torch.cuda.synchronize()
+    (a32, a16), (b32, b16), (r32, r16) = results
+    assert b32.abs().max().item() > 0 and b16.float().abs().max().item() > 0
+    noise_limited_close(a32, b32, r32, False, 'fp32 grid gradient')
+    noise_limited_close(a16.float(), b16.float(), r16.float(), True, 'fp16 grid gradient')
