@@ -193,6 +193,14 @@ __device__ __forceinline__ uint32_t corner_row(const GridParams& gp, const uint3
 // max(groups) groups instead of all 21 (leader, member) pairs of the fully unrolled merge. The roundings are explicit
 // (a fused multiply-add of the weighting into the sum of (wx wy) wz products), which reproduces the reference
 // kernels' corner weights bit for bit independently of how the surrounding code is scheduled.
+// cell and fractional position of a contracted coordinate on a level of the given size (featurize_common.cuh:127-131)
+__device__ __forceinline__ void level_cell(const float x, const uint32_t size, int& cell, float& frac) {
+    const float p = x * size - 0.5f;
+    const float g = floorf(p);
+    cell = static_cast<int>(g);
+    frac = p - g;
+}
+
 template <typename Visitor>
 __device__ __forceinline__ void visit_level(const GridParams& gp, const uint32_t level, const float3* x, const float* weighting, Visitor& visitor) {
     const uint32_t size = gp.size[level];
@@ -200,14 +208,9 @@ __device__ __forceinline__ void visit_level(const GridParams& gp, const uint32_t
     float fx[kMultisamples], fy[kMultisamples], fz[kMultisamples];
     #pragma unroll
     for (uint32_t j = 0; j < kMultisamples; j++) {
-        const float px = x[j].x * size - 0.5f, py = x[j].y * size - 0.5f, pz = x[j].z * size - 0.5f;
-        const float gx = floorf(px), gy = floorf(py), gz = floorf(pz);
-        cx[j] = static_cast<int>(gx);
-        cy[j] = static_cast<int>(gy);
-        cz[j] = static_cast<int>(gz);
-        fx[j] = px - gx;
-        fy[j] = py - gy;
-        fz[j] = pz - gz;
+        level_cell(x[j].x, size, cx[j], fx[j]);
+        level_cell(x[j].y, size, cy[j], fy[j]);
+        level_cell(x[j].z, size, cz[j], fz[j]);
     }
     uint32_t remaining = (1u << kMultisamples) - 1u;
     while (remaining != 0u) {

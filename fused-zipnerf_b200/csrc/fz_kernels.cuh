@@ -310,36 +310,149 @@ __device__ __forceinline__ void add_row_f16(uint16_t* __restrict__ grad_table, c
     }
 }
 
-// scatters one interval's feature gradient (g_row[(l (F + 1) + f) g_stride]; scale features carry none) into the grid
-// gradient: levels below n_fp32 into grad_table (fp32), the others into grad_table_half (fp16, rows re-based at the
-// first fp16 level) (featurize_common.cuh:273-291)
-template <int F>
-__device__ __forceinline__ void scatter_row(const GridParams& gp, const Frustum& fr, const float* g_row, const int g_stride, const uint32_t n_fp32,
-                                            float* __restrict__ grad_table, uint16_t* __restrict__ grad_table_half) {
-    float3 x[kMultisamples];
-    float scale[kMultisamples];
-    multisamples(fr, x, scale);
-    const uint32_t half_base = gp.offset[min(n_fp32, gp.n_levels)];
-    #pragma unroll 1
-    for (uint32_t level = 0; level < gp.n_levels; level++) {
-        float weighting[kMultisamples];
+// ---------------------------------------------------------------------------------------------------------------------
+// warp-cooperative gradient scatter (featurize_common.cuh:123-173, 273-291)
+//
+// The corner work of an interval is one task per merged corner group, 1 to 6 per level. A lane that loops over its own
+// groups keeps the warp busy for the largest group count of its 32 intervals (coarse levels: one group for most
+// intervals, several for a few). Here every lane publishes its multisample records of the level to shared memory and
+// appends its groups to the warp's task list; the warp then works through the list 32 tasks at a time, each lane
+// taking whichever group comes next. The atomics are order-free; the merged corner weights are formed exactly as in
+// visit_level (the leader's weights, then the other members' in multisample order).
+
+// per-warp shared memory of the cooperative scatter. Records of lane l, multisample j at [l kRecordStride + j]: with
+// stride 7 the 16-byte records of 8 consecutive lanes fall into distinct bank quads
+constexpr int kRecordStride = 7;
+struct ScatterWarpSmem {
+    float4 frac[32 * kRecordStride];   // (fx, fy, fz, weighting) of every multisample
+    int4 cell[32 * kRecordStride];     // (cx, cy, cz, member mask) of every group leader
+    uint8_t task[32 * kMultisamples];  // one byte per group: owner lane | leader multisample << 5
+};
+static_assert(sizeof(ScatterWarpSmem) % 16 == 0, "records stay 16-byte aligned per warp");
+
+// writes one interval's multisample records of a level; returns the mask of group leaders (the lowest multisample of
+// every set of multisamples that share a cell)
+__device__ __forceinline__ uint32_t publish_level(const GridParams& gp, const uint32_t level, const float3* x, const float* scale,
+                                                  ScatterWarpSmem& ws, const int lane) {
+    const uint32_t size = gp.size[level];
+    int cx[kMultisamples], cy[kMultisamples], cz[kMultisamples];
+    #pragma unroll
+    for (uint32_t j = 0; j < kMultisamples; j++) {
+        float fx, fy, fz;
+        level_cell(x[j].x, size, cx[j], fx);
+        level_cell(x[j].y, size, cy[j], fy);
+        level_cell(x[j].z, size, cz[j], fz);
+        ws.frac[lane * kRecordStride + j] = make_float4(fx, fy, fz, level_weighting(size, scale[j]));
+    }
+    uint32_t members[kMultisamples];
+    uint32_t followers = 0u;
+    #pragma unroll
+    for (uint32_t j = 0; j < kMultisamples; j++) members[j] = 1u << j;
+    #pragma unroll
+    for (uint32_t j = 0; j < kMultisamples; j++) {
         #pragma unroll
-        for (uint32_t j = 0; j < kMultisamples; j++) weighting[j] = level_weighting(gp.size[level], scale[j]);
+        for (uint32_t k = j + 1; k < kMultisamples; k++) {
+            if (cx[j] == cx[k] && cy[j] == cy[k] && cz[j] == cz[k]) {
+                members[j] |= 1u << k;
+                followers |= 1u << k;
+            }
+        }
+    }
+    const uint32_t leaders = ((1u << kMultisamples) - 1u) & ~followers;
+    #pragma unroll
+    for (uint32_t j = 0; j < kMultisamples; j++) {
+        if ((leaders >> j) & 1u) ws.cell[lane * kRecordStride + j] = make_int4(cx[j], cy[j], cz[j], static_cast<int>(members[j]));
+    }
+    return leaders;
+}
+
+// works through the warp's task list of one level: merged corner weights of each group, its 8 rows, and the atomics of
+// the owner's gradient (fp32 table, or fp16 table with rows re-based at row_base)
+template <int F, bool HALF>
+__device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32_t level, const ScatterWarpSmem& ws, const uint32_t n_tasks,
+                                              const int lane, const float* warp_rows, const int stride, float* __restrict__ grad_table,
+                                              uint16_t* __restrict__ grad_table_half, const uint32_t row_base) {
+    for (uint32_t t = lane; t < n_tasks; t += 32) {
+        const uint32_t task = ws.task[t];
+        const uint32_t owner = task & 31u, leader = task >> 5;
+        const float4 q = ws.frac[owner * kRecordStride + leader];
+        const int4 c = ws.cell[owner * kRecordStride + leader];
+        float corner_weights[8];
+        #pragma unroll
+        for (uint32_t corner = 0; corner < 8; corner++) {
+            const float wx = corner & 4u ? q.x : 1.0f - q.x;
+            const float wy = corner & 2u ? q.y : 1.0f - q.y;
+            const float wz = corner & 1u ? q.z : 1.0f - q.z;
+            corner_weights[corner] = __fmaf_rn(q.w, __fmul_rn(__fmul_rn(wx, wy), wz), 0.0f);
+        }
+        uint32_t others = static_cast<uint32_t>(c.w) & ~(1u << leader);
+        while (others != 0u) {
+            const uint32_t m = __ffs(others) - 1u;
+            others &= others - 1u;
+            const float4 qm = ws.frac[owner * kRecordStride + m];
+            #pragma unroll
+            for (uint32_t corner = 0; corner < 8; corner++) {
+                const float wx = corner & 4u ? qm.x : 1.0f - qm.x;
+                const float wy = corner & 2u ? qm.y : 1.0f - qm.y;
+                const float wz = corner & 1u ? qm.z : 1.0f - qm.z;
+                corner_weights[corner] = __fmaf_rn(qm.w, __fmul_rn(__fmul_rn(wx, wy), wz), corner_weights[corner]);
+            }
+        }
         float g[F];
         #pragma unroll
-        for (int f = 0; f < F; f++) g[f] = g_row[(level * (F + 1) + f) * g_stride];
-        if (level < n_fp32) {
-            auto visitor = [&](const uint32_t row, const float weight) {
-                if (weight != 0.0f) add_row_f32<F>(grad_table, row, weight, g);
-            };
-            visit_level(gp, level, x, weighting, visitor);
+        for (int f = 0; f < F; f++) g[f] = warp_rows[owner * stride + level * (F + 1) + f];
+        #pragma unroll
+        for (uint32_t corner = 0; corner < 8; corner++) {
+            float weight = corner_weights[corner];
+            const uint32_t row = corner_row(gp, level, c.x + static_cast<int>((corner >> 2) & 1u), c.y + static_cast<int>((corner >> 1) & 1u),
+                                            c.z + static_cast<int>(corner & 1u), weight);
+            if (weight == 0.0f) continue;
+            if constexpr (HALF) add_row_f16<F>(grad_table_half, row - row_base, weight, g);
+            else add_row_f32<F>(grad_table, row, weight, g);
         }
-        else {
-            auto visitor = [&](const uint32_t row, const float weight) {
-                if (weight != 0.0f) add_row_f16<F>(grad_table_half, row - half_base, weight, g);
-            };
-            visit_level(gp, level, x, weighting, visitor);
+    }
+}
+
+// scatters the feature gradients of a warp's intervals (row of lane l at warp_rows[l stride], column l (F + 1) + f;
+// scale features carry none) into the grid gradient: levels below n_fp32 into grad_table (fp32), the others into
+// grad_table_half (fp16, rows re-based at the first fp16 level). Inactive lanes and all-zero level gradients add no
+// tasks. Every lane of the warp must call this.
+template <int F>
+__device__ __forceinline__ void scatter_warp(const GridParams& gp, const Frustum& fr, const bool active, const float* warp_rows, const int stride,
+                                             const int lane, const uint32_t n_fp32, float* __restrict__ grad_table,
+                                             uint16_t* __restrict__ grad_table_half, ScatterWarpSmem& ws) {
+    float3 x[kMultisamples];
+    float scale[kMultisamples];
+    if (active) multisamples(fr, x, scale);
+    const uint32_t half_base = gp.offset[min(n_fp32, gp.n_levels)];
+    const float* g_row = warp_rows + lane * stride;
+    const uint32_t lanes_below = (1u << lane) - 1u;
+    #pragma unroll 1
+    for (uint32_t level = 0; level < gp.n_levels; level++) {
+        uint32_t leaders = 0u;
+        if (active) {
+            bool any = false;
+            #pragma unroll
+            for (int f = 0; f < F; f++) any |= g_row[level * (F + 1) + f] != 0.0f;
+            if (any) leaders = publish_level(gp, level, x, scale, ws, lane);
         }
+        // this lane's first task slot (exclusive prefix of the 0..6 group counts, one ballot per count bit) and the total
+        const uint32_t n = __popc(leaders);
+        uint32_t first = 0u, n_tasks = 0u;
+        #pragma unroll
+        for (int b = 0; b < 3; b++) {
+            const uint32_t bits = __ballot_sync(0xFFFFFFFFu, (n >> b) & 1u);
+            first += static_cast<uint32_t>(__popc(bits & lanes_below)) << b;
+            n_tasks += static_cast<uint32_t>(__popc(bits)) << b;
+        }
+        #pragma unroll
+        for (uint32_t j = 0; j < kMultisamples; j++) {
+            if ((leaders >> j) & 1u) ws.task[first + __popc(leaders & ((1u << j) - 1u))] = static_cast<uint8_t>(lane | (j << 5));
+        }
+        __syncwarp();
+        if (level < n_fp32) scatter_tasks<F, false>(gp, level, ws, n_tasks, lane, warp_rows, stride, grad_table, grad_table_half, 0u);
+        else scatter_tasks<F, true>(gp, level, ws, n_tasks, lane, warp_rows, stride, grad_table, grad_table_half, half_base);
+        __syncwarp();
     }
 }
 
@@ -382,14 +495,19 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_ke
         }
     }
     __syncwarp();
-    if (lane >= n_rows) return;
     const uint32_t sample = warp_first + lane;
-    if (a.skip_if_zero != nullptr && __ldcs(a.skip_if_zero + sample) == 0.0f) return;
-    const Frustum fr = setup_frustum(a.in, gp.pattern_stream, sample);
-    scatter_row<F>(gp, fr, warp_rows + lane * stride, 1, a.n_fp32_levels, a.grad_table, a.grad_table_half);
+    bool active = lane < n_rows;
+    if (active && a.skip_if_zero != nullptr && __ldcs(a.skip_if_zero + sample) == 0.0f) active = false;
+    Frustum fr;
+    if (active) fr = setup_frustum(a.in, gp.pattern_stream, sample);
+    ScatterWarpSmem& ws = reinterpret_cast<ScatterWarpSmem*>(smem + kBlock * stride)[warp];
+    scatter_warp<F>(gp, fr, active, warp_rows, stride, lane, a.n_fp32_levels, a.grad_table, a.grad_table_half, ws);
 }
 
-__host__ __device__ constexpr int backward_smem_floats(const int n_out) { return kBlock * staged_stride(n_out); }
+// dynamic shared memory of fz_backward_kernel in floats: staged gradient rows, then the warps' scatter records
+__host__ __device__ constexpr int backward_smem_floats(const int n_out) {
+    return kBlock * staged_stride(n_out) + kWarps * static_cast<int>(sizeof(ScatterWarpSmem) / sizeof(float));
+}
 
 // ---------------------------------------------------------------------------------------------------------------------
 // proposal-level backward, MLP part (featurize_backward_mlp.cu:79-147 without the scatter): recomputes the fused MLP
