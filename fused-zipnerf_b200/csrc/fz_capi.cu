@@ -115,6 +115,9 @@ struct zf_featurizer {
     zf::GridParams params{};
     const zf::KernelSet* kernels = nullptr;
     const zf::MlpKernelSet* mlp_kernels = nullptr;  // null without an MLP
+    // stream-ordered pool of the proposal backward's workspace when the caller passes none; it keeps its memory after
+    // a call (no release threshold), so repeated calls neither map nor unmap device memory
+    cudaMemPool_t workspace_pool = nullptr;
 
     int n_output_features() const { return n_levels * (n_features + 1); }
     int64_t n_rows() const { return offsets[n_levels]; }
@@ -189,7 +192,7 @@ int zf_featurizer_create(const int level, const int64_t* level_sizes, const int6
     if (mlp_width > 0) {
         f.mlp_kernels = mlp_kernel_set(n_features, zf::mlp_pad(f.n_output_features()));
         if (f.mlp_kernels == nullptr) return fail(ZF_ERROR_UNSUPPORTED, "this mlp input width is not compiled into this build");
-        const size_t fwd = static_cast<size_t>(zf::forward_smem_floats(f.n_output_features(), zf::mlp_pad(f.n_output_features()), mlp_width)) * sizeof(float);
+        const size_t fwd = static_cast<size_t>(zf::forward_smem_floats(f.n_output_features(), f.n_features, zf::mlp_pad(f.n_output_features()), mlp_width)) * sizeof(float);
         const size_t bwd = static_cast<size_t>(zf::backward_mlp_smem_floats(f.n_output_features(), zf::mlp_pad(f.n_output_features()), mlp_width)) * sizeof(float);
         if (std::max(fwd, bwd) > 227 * 1024) return fail(ZF_ERROR_UNSUPPORTED, "mlp_width too large for the kernels' shared memory");
     }
@@ -197,11 +200,30 @@ int zf_featurizer_create(const int level, const int64_t* level_sizes, const int6
     if (error != cudaSuccess) return cuda_fail(error, "cudaGetDevice");
     error = cudaDeviceGetAttribute(&f.n_sms, cudaDevAttrMultiProcessorCount, f.device);
     if (error != cudaSuccess) return cuda_fail(error, "cudaDeviceGetAttribute");
+    if (mlp_width > 0) {
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = f.device;
+        error = cudaMemPoolCreate(&f.workspace_pool, &props);
+        if (error != cudaSuccess) return cuda_fail(error, "workspace pool creation");
+        uint64_t keep = UINT64_MAX;
+        error = cudaMemPoolSetAttribute(f.workspace_pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        if (error != cudaSuccess) {
+            cudaMemPoolDestroy(f.workspace_pool);
+            return cuda_fail(error, "workspace pool release threshold");
+        }
+    }
     *out = new zf_featurizer(f);
     return ZF_OK;
 }
 
-void zf_featurizer_destroy(zf_featurizer* featurizer) { delete featurizer; }
+void zf_featurizer_destroy(zf_featurizer* featurizer) {
+    if (featurizer == nullptr) return;
+    // memory still in use by queued work is released when that work completes
+    if (featurizer->workspace_pool != nullptr) cudaMemPoolDestroy(featurizer->workspace_pool);
+    delete featurizer;
+}
 
 int zf_featurizer_n_output_features(const zf_featurizer* featurizer) { return featurizer ? featurizer->n_output_features() : 0; }
 
@@ -249,7 +271,7 @@ int zf_featurize_forward(zf_featurizer* f, const zf_forward_args* a, cudaStream_
     k.inputs_vectors = a->nerf_inputs != nullptr && a->nerf_inputs_width % 8 == 0 && a->encoded_width % 8 == 0 && aligned(a->nerf_inputs, 16) && aligned(a->encoded_directions, 16);
     k.interleave_rays = a->interleave ? 32u : 0u;
     const int pad = mlp ? zf::mlp_pad(n_out) : 0;
-    const size_t smem = static_cast<size_t>(zf::forward_smem_floats(n_out, pad, k.mlp_width)) * sizeof(float);
+    const size_t smem = static_cast<size_t>(zf::forward_smem_floats(n_out, f->n_features, pad, k.mlp_width)) * sizeof(float);
     const cudaError_t error = launch(mlp ? f->mlp_kernels->forward : f->kernels->forward, n_blocks(n_samples), smem, stream, f->params, k);
     if (error != cudaSuccess) return cuda_fail(error, "featurize_forward launch");
     return ZF_OK;
@@ -312,7 +334,7 @@ int zf_featurize_backward_mlp(zf_featurizer* f, const zf_backward_mlp_args* a, c
     if (n_samples == 0) return ZF_OK;
     float* rows = static_cast<float*>(a->workspace);
     if (rows == nullptr) {
-        const cudaError_t error = cudaMallocAsync(reinterpret_cast<void**>(&rows), static_cast<size_t>(workspace_bytes), stream);
+        const cudaError_t error = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&rows), static_cast<size_t>(workspace_bytes), f->workspace_pool, stream);
         if (error != cudaSuccess) return cuda_fail(error, "backward_mlp workspace allocation");
     }
     k.features = a->features;

@@ -21,6 +21,10 @@ constexpr int kBlock = 128;
 #ifndef ZF_MIN_BLOCKS_FORWARD_MLP
 #define ZF_MIN_BLOCKS_FORWARD_MLP 7
 #endif
+// the cooperative forward (1-2 features per level) is held to 4 blocks per SM by its shared memory
+#ifndef ZF_MIN_BLOCKS_FORWARD_COOP
+#define ZF_MIN_BLOCKS_FORWARD_COOP 4
+#endif
 #ifndef ZF_MIN_BLOCKS_BACKWARD
 #define ZF_MIN_BLOCKS_BACKWARD 4
 #endif
@@ -97,6 +101,240 @@ __device__ __forceinline__ uint32_t thread_sample(const uint32_t t, const RayInp
 __device__ __forceinline__ void multisamples(const Frustum& fr, float3 (&x)[kMultisamples], float (&scale)[kMultisamples]) {
     #pragma unroll
     for (uint32_t j = 0; j < kMultisamples; j++) multisample(fr, j, x[j], scale[j]);
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// warp-cooperative corner groups (featurize_common.cuh:123-198)
+//
+// The corner work of an interval is one task per merged corner group, 1 to 6 per level. A lane that loops over its own
+// groups keeps the warp busy for the largest group count of its 32 intervals (coarse levels: one group for most
+// intervals, several for a few), and pays for selecting its group's leader out of registers. Here every lane publishes
+// its multisample records of the level to shared memory and lists its groups in the warp's task list; the warp then
+// works through the list 32 tasks at a time, each lane taking whichever group comes next. The merged corner weights
+// are formed exactly as in visit_level (the leader's weights, then the other members' in multisample order). Tasks are
+// listed group-index-major (every lane's first group, then every lane's second group, ...), so a lane's groups come in
+// its own order, which the forward's accumulation needs.
+
+// Records of lane l, multisample j at [l kRecordStride + j]: with stride 7 the 16-byte records of 8 consecutive lanes
+// fall into distinct bank quads.
+constexpr int kRecordStride = 7;
+struct GroupRecords {
+    float4 frac[32 * kRecordStride];   // (fx, fy, fz, weighting) of every multisample
+    int4 cell[32 * kRecordStride];     // (cx, cy, cz, member mask) of every group leader
+    uint8_t task[32 * kMultisamples];  // one byte per group: owner lane | leader multisample << 5
+};
+static_assert(sizeof(GroupRecords) % 16 == 0, "records stay 16-byte aligned per warp");
+
+// writes one interval's multisample records of a level; returns the mask of group leaders (the lowest multisample of
+// every set of multisamples that share a cell)
+__device__ __forceinline__ uint32_t publish_level(const uint32_t size, const float3* x, const float* weighting, GroupRecords& gr, const int lane) {
+    int cx[kMultisamples], cy[kMultisamples], cz[kMultisamples];
+    #pragma unroll
+    for (uint32_t j = 0; j < kMultisamples; j++) {
+        float fx, fy, fz;
+        level_cell(x[j].x, size, cx[j], fx);
+        level_cell(x[j].y, size, cy[j], fy);
+        level_cell(x[j].z, size, cz[j], fz);
+        gr.frac[lane * kRecordStride + j] = make_float4(fx, fy, fz, weighting[j]);
+    }
+    uint32_t members[kMultisamples];
+    uint32_t followers = 0u;
+    #pragma unroll
+    for (uint32_t j = 0; j < kMultisamples; j++) members[j] = 1u << j;
+    #pragma unroll
+    for (uint32_t j = 0; j < kMultisamples; j++) {
+        #pragma unroll
+        for (uint32_t k = j + 1; k < kMultisamples; k++) {
+            if (cx[j] == cx[k] && cy[j] == cy[k] && cz[j] == cz[k]) {
+                members[j] |= 1u << k;
+                followers |= 1u << k;
+            }
+        }
+    }
+    const uint32_t leaders = ((1u << kMultisamples) - 1u) & ~followers;
+    #pragma unroll
+    for (uint32_t j = 0; j < kMultisamples; j++) {
+        if ((leaders >> j) & 1u) gr.cell[lane * kRecordStride + j] = make_int4(cx[j], cy[j], cz[j], static_cast<int>(members[j]));
+    }
+    return leaders;
+}
+
+// lists the groups of every lane, group-index-major; slot[i] = the task index of this lane's i-th group (for i below
+// its group count). Returns the warp's task count. Every lane of the warp must call this.
+__device__ __forceinline__ uint32_t list_tasks(const uint32_t leaders, const int lane, GroupRecords& gr, uint32_t (&slot)[kMultisamples]) {
+    const uint32_t lanes_below = (1u << lane) - 1u;
+    const uint32_t n = __popc(leaders);
+    uint32_t base = 0u, rest = leaders;
+    #pragma unroll
+    for (uint32_t i = 0; i < kMultisamples; i++) {
+        const uint32_t mask = __ballot_sync(0xFFFFFFFFu, n > i);
+        slot[i] = base + __popc(mask & lanes_below);
+        if (n > i) {
+            gr.task[slot[i]] = static_cast<uint8_t>(lane | ((__ffs(rest) - 1) << 5));
+            rest &= rest - 1u;
+        }
+        base += __popc(mask);
+    }
+    return base;
+}
+
+// lists the groups of every lane, lane-major (a lane's groups next to each other: the lanes of a round then touch the
+// corners of fewer distinct intervals at a time, so fewer of a warp's atomics hit the same row). Returns the warp's
+// task count. Every lane of the warp must call this.
+__device__ __forceinline__ uint32_t list_tasks_by_lane(const uint32_t leaders, const int lane, GroupRecords& gr) {
+    const uint32_t lanes_below = (1u << lane) - 1u;
+    const uint32_t n = __popc(leaders);
+    // this lane's first slot: exclusive prefix of the 0..6 group counts, one ballot per count bit
+    uint32_t first = 0u, n_tasks = 0u;
+    #pragma unroll
+    for (int b = 0; b < 3; b++) {
+        const uint32_t bits = __ballot_sync(0xFFFFFFFFu, (n >> b) & 1u);
+        first += static_cast<uint32_t>(__popc(bits & lanes_below)) << b;
+        n_tasks += static_cast<uint32_t>(__popc(bits)) << b;
+    }
+    #pragma unroll
+    for (uint32_t j = 0; j < kMultisamples; j++) {
+        if ((leaders >> j) & 1u) gr.task[first + __popc(leaders & ((1u << j) - 1u))] = static_cast<uint8_t>(lane | (j << 5));
+    }
+    return n_tasks;
+}
+
+// merged corner weights and cell of task t's group
+__device__ __forceinline__ void task_group(const GroupRecords& gr, const uint32_t t, float (&corner_weights)[8], int4& cell, uint32_t& owner) {
+    const uint32_t task = gr.task[t];
+    owner = task & 31u;
+    const uint32_t leader = task >> 5;
+    const float4 q = gr.frac[owner * kRecordStride + leader];
+    cell = gr.cell[owner * kRecordStride + leader];
+    #pragma unroll
+    for (uint32_t corner = 0; corner < 8; corner++) {
+        const float wx = corner & 4u ? q.x : 1.0f - q.x;
+        const float wy = corner & 2u ? q.y : 1.0f - q.y;
+        const float wz = corner & 1u ? q.z : 1.0f - q.z;
+        corner_weights[corner] = __fmaf_rn(q.w, __fmul_rn(__fmul_rn(wx, wy), wz), 0.0f);
+    }
+    uint32_t others = static_cast<uint32_t>(cell.w) & ~(1u << leader);
+    while (others != 0u) {
+        const uint32_t m = __ffs(others) - 1u;
+        others &= others - 1u;
+        const float4 qm = gr.frac[owner * kRecordStride + m];
+        #pragma unroll
+        for (uint32_t corner = 0; corner < 8; corner++) {
+            const float wx = corner & 4u ? qm.x : 1.0f - qm.x;
+            const float wy = corner & 2u ? qm.y : 1.0f - qm.y;
+            const float wz = corner & 1u ? qm.z : 1.0f - qm.z;
+            corner_weights[corner] = __fmaf_rn(qm.w, __fmul_rn(__fmul_rn(wx, wy), wz), corner_weights[corner]);
+        }
+    }
+}
+
+__device__ __forceinline__ int corner_offset(const uint32_t corner, const int axis_bit) { return static_cast<int>((corner >> axis_bit) & 1u); }
+
+template <int F>
+__device__ __forceinline__ void load_row(const float* __restrict__ table, const uint32_t row, float (&v)[F]) {
+    if constexpr (F == 4) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(table) + row);
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    }
+    else if constexpr (F == 2) {
+        const float2 t = __ldg(reinterpret_cast<const float2*>(table) + row);
+        v[0] = t.x; v[1] = t.y;
+    }
+    else {
+        #pragma unroll
+        for (int f = 0; f < F; f++) v[f] = __ldg(table + static_cast<size_t>(row) * F + f);
+    }
+}
+
+// floats per warp of the forward's per-round gather results: (weight, F values) of 8 corners for 32 tasks
+template <int F>
+__host__ __device__ constexpr int gather_result_floats() { return 32 * 8 * (F + 1); }
+
+// The forward gathers cooperatively for 1-2 features per level. With more, the per-warp records and results take the
+// shared memory that the latency-bound gathers of wide hashed tables need for resident warps (measured on the B200 for
+// 4 features: 2 instead of 6 blocks per SM, 2.3x slower), and each lane loops over its own groups (visit_level).
+__host__ __device__ constexpr bool cooperative_forward(const int n_features) { return n_features <= 2; }
+
+// all level features of a warp's intervals into their shared-memory rows (lane l's row: row[l (F + 1) + f] grid
+// features, row[l (F + 1) + F] the scale feature; featurize_common.cuh:174-227). A round's tasks gather their 8 corner
+// rows into s_result (component-major, lane-minor); then every owner accumulates its tasks of the round, in its own
+// group order, corner by corner, with the fused multiply-adds of the reference's gather, so the features are the
+// reference's bit for bit. Every lane of the warp must call this; inactive lanes add no tasks and write no row.
+template <int F>
+__device__ __forceinline__ void featurize_warp(const GridParams& gp, const Frustum& fr, const bool active, const float* __restrict__ table,
+                                               const float* __restrict__ scale_magnitudes, float* row, const int lane, GroupRecords& gr,
+                                               float* s_result) {
+    float3 x[kMultisamples];
+    float scale[kMultisamples];
+    if (active) multisamples(fr, x, scale);
+    #pragma unroll 1
+    for (uint32_t level = 0; level < gp.n_levels; level++) {
+        const uint32_t size = gp.size[level];
+        float scale_feature = 0.0f;
+        uint32_t leaders = 0u;
+        if (active) {
+            float weighting[kMultisamples];
+            #pragma unroll
+            for (uint32_t j = 0; j < kMultisamples; j++) {
+                weighting[j] = level_weighting(size, scale[j]);
+                scale_feature += 2.0f * weighting[j] - 1.0f;
+            }
+            leaders = publish_level(size, x, weighting, gr, lane);
+        }
+        uint32_t slot[kMultisamples];
+        const uint32_t n_tasks = list_tasks(leaders, lane, gr, slot);
+        const uint32_t n_groups = __popc(leaders);
+        __syncwarp();
+        float value[F];
+        #pragma unroll
+        for (int f = 0; f < F; f++) value[f] = 0.0f;
+        for (uint32_t first = 0; first < n_tasks; first += 32) {
+            const uint32_t t = first + lane;
+            if (t < n_tasks) {
+                float w[8];
+                int4 c;
+                uint32_t owner;
+                task_group(gr, t, w, c, owner);
+                float v[8][F];
+                #pragma unroll
+                for (uint32_t corner = 0; corner < 8; corner++) {
+                    const uint32_t r = corner_row(gp, level, c.x + corner_offset(corner, 2), c.y + corner_offset(corner, 1), c.z + corner_offset(corner, 0), w[corner]);
+                    if (w[corner] != 0.0f) load_row<F>(table, r, v[corner]);
+                    else {
+                        #pragma unroll
+                        for (int f = 0; f < F; f++) v[corner][f] = 0.0f;
+                    }
+                }
+                #pragma unroll
+                for (uint32_t corner = 0; corner < 8; corner++) {
+                    s_result[(corner * (F + 1)) * 32 + lane] = w[corner];
+                    #pragma unroll
+                    for (int f = 0; f < F; f++) s_result[(corner * (F + 1) + 1 + f) * 32 + lane] = v[corner][f];
+                }
+            }
+            __syncwarp();
+            #pragma unroll
+            for (uint32_t i = 0; i < kMultisamples; i++) {
+                const uint32_t src = slot[i] - first;
+                if (i < n_groups && src < 32u) {
+                    #pragma unroll
+                    for (uint32_t corner = 0; corner < 8; corner++) {
+                        const float weight = s_result[(corner * (F + 1)) * 32 + src];
+                        if (weight != 0.0f) {
+                            #pragma unroll
+                            for (int f = 0; f < F; f++) value[f] = __fmaf_rn(weight, s_result[(corner * (F + 1) + 1 + f) * 32 + src], value[f]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+        }
+        if (active) {
+            #pragma unroll
+            for (int f = 0; f < F; f++) row[level * (F + 1) + f] = kFeatureScale * value[f];
+            row[level * (F + 1) + F] = kFeatureScale * scale_feature * __ldg(scale_magnitudes + level);
+        }
+    }
 }
 
 // all level features of one interval into a shared-memory row: row[l (F + 1) + f] grid features (averaged over the
@@ -202,7 +440,7 @@ __device__ __forceinline__ void store_inputs_tail(const Args& a, const uint32_t*
 // Forward. NOUT_PAD == 0: no MLP; otherwise the fused density MLP n_out -> W (ReLU) -> 1 runs for raw_density, with
 // the features in registers (NOUT_PAD >= n_out) and the reference's accumulation order (featurize_forward.cu:65-73).
 template <int F, int NOUT_PAD>
-__global__ void __launch_bounds__(kBlock, NOUT_PAD > 0 ? ZF_MIN_BLOCKS_FORWARD_MLP : ZF_MIN_BLOCKS_FORWARD) fz_forward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ ForwardArgs a) {
+__global__ void __launch_bounds__(kBlock, cooperative_forward(F) ? ZF_MIN_BLOCKS_FORWARD_COOP : (NOUT_PAD > 0 ? ZF_MIN_BLOCKS_FORWARD_MLP : ZF_MIN_BLOCKS_FORWARD)) fz_forward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ ForwardArgs a) {
     const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
     const int stride = staged_stride(n_out);
     extern __shared__ __align__(16) float smem[];
@@ -211,6 +449,9 @@ __global__ void __launch_bounds__(kBlock, NOUT_PAD > 0 ? ZF_MIN_BLOCKS_FORWARD_M
     float* s_w0 = smem + (kBlock + kBlock * stride + 3) / 4 * 4;  // [W, NOUT_PAD] (MLP only; 16-byte aligned)
     float* s_b0 = s_w0 + a.mlp_width * NOUT_PAD;               // [W]
     float* s_w1 = s_b0 + a.mlp_width;                          // [W]
+    // the warps' group records and gather results (cooperative forward; 16-byte aligned)
+    GroupRecords* s_groups = reinterpret_cast<GroupRecords*>(s_w0 + (NOUT_PAD > 0 ? (a.mlp_width * NOUT_PAD + 2 * a.mlp_width + 3) / 4 * 4 : 0));
+    float* s_results = reinterpret_cast<float*>(s_groups + kWarps);  // [kWarps, gather_result_floats<F>()]
     if constexpr (NOUT_PAD > 0) {
         for (int i = threadIdx.x; i < a.mlp_width * NOUT_PAD; i += kBlock) {
             const int j = i / NOUT_PAD, c = i - j * NOUT_PAD;
@@ -230,7 +471,12 @@ __global__ void __launch_bounds__(kBlock, NOUT_PAD > 0 ? ZF_MIN_BLOCKS_FORWARD_M
     const uint32_t sample = active ? thread_sample(warp_first + lane, a.in, a.interleave_rays) : 0u;
     float* row = s_rows + threadIdx.x * stride;
     s_sample[threadIdx.x] = sample;
-    if (active) {
+    if constexpr (cooperative_forward(F)) {
+        Frustum fr;
+        if (active) fr = setup_frustum(a.in, gp.pattern_stream, sample);
+        featurize_warp<F>(gp, fr, active, a.table, a.scale_magnitudes, row, lane, s_groups[warp], s_results + warp * gather_result_floats<F>());
+    }
+    else if (active) {
         const Frustum fr = setup_frustum(a.in, gp.pattern_stream, sample);
         featurize_to_row<F>(gp, fr, a.table, a.scale_magnitudes, row);
     }
@@ -264,9 +510,11 @@ __global__ void __launch_bounds__(kBlock, NOUT_PAD > 0 ? ZF_MIN_BLOCKS_FORWARD_M
     if (a.nerf_inputs != nullptr) store_inputs_tail(a, warp_samples, n_rows, lane);
 }
 
-// dynamic shared memory of fz_forward_kernel in floats (the MLP weights start 16-byte aligned)
-__host__ __device__ constexpr int forward_smem_floats(const int n_out, const int nout_pad, const int width) {
-    return ((kBlock + kBlock * staged_stride(n_out) + 3) / 4) * 4 + (nout_pad > 0 ? width * nout_pad + 2 * width : 0);
+// dynamic shared memory of fz_forward_kernel in floats: sample indices, staged rows, MLP weights, the warps' group
+// records and gather results (the last three 16-byte aligned)
+__host__ __device__ constexpr int forward_smem_floats(const int n_out, const int n_features, const int nout_pad, const int width) {
+    return ((kBlock + kBlock * staged_stride(n_out) + 3) / 4) * 4 + (nout_pad > 0 ? (width * nout_pad + 2 * width + 3) / 4 * 4 : 0) +
+           (cooperative_forward(n_features) ? kWarps * (static_cast<int>(sizeof(GroupRecords) / sizeof(float)) + 32 * 8 * (n_features + 1)) : 0);
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
@@ -311,101 +559,27 @@ __device__ __forceinline__ void add_row_f16(uint16_t* __restrict__ grad_table, c
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
-// warp-cooperative gradient scatter (featurize_common.cuh:123-173, 273-291)
-//
-// The corner work of an interval is one task per merged corner group, 1 to 6 per level. A lane that loops over its own
-// groups keeps the warp busy for the largest group count of its 32 intervals (coarse levels: one group for most
-// intervals, several for a few). Here every lane publishes its multisample records of the level to shared memory and
-// appends its groups to the warp's task list; the warp then works through the list 32 tasks at a time, each lane
-// taking whichever group comes next. The atomics are order-free; the merged corner weights are formed exactly as in
-// visit_level (the leader's weights, then the other members' in multisample order).
-
-// per-warp shared memory of the cooperative scatter. Records of lane l, multisample j at [l kRecordStride + j]: with
-// stride 7 the 16-byte records of 8 consecutive lanes fall into distinct bank quads
-constexpr int kRecordStride = 7;
-struct ScatterWarpSmem {
-    float4 frac[32 * kRecordStride];   // (fx, fy, fz, weighting) of every multisample
-    int4 cell[32 * kRecordStride];     // (cx, cy, cz, member mask) of every group leader
-    uint8_t task[32 * kMultisamples];  // one byte per group: owner lane | leader multisample << 5
-};
-static_assert(sizeof(ScatterWarpSmem) % 16 == 0, "records stay 16-byte aligned per warp");
-
-// writes one interval's multisample records of a level; returns the mask of group leaders (the lowest multisample of
-// every set of multisamples that share a cell)
-__device__ __forceinline__ uint32_t publish_level(const GridParams& gp, const uint32_t level, const float3* x, const float* scale,
-                                                  ScatterWarpSmem& ws, const int lane) {
-    const uint32_t size = gp.size[level];
-    int cx[kMultisamples], cy[kMultisamples], cz[kMultisamples];
-    #pragma unroll
-    for (uint32_t j = 0; j < kMultisamples; j++) {
-        float fx, fy, fz;
-        level_cell(x[j].x, size, cx[j], fx);
-        level_cell(x[j].y, size, cy[j], fy);
-        level_cell(x[j].z, size, cz[j], fz);
-        ws.frac[lane * kRecordStride + j] = make_float4(fx, fy, fz, level_weighting(size, scale[j]));
-    }
-    uint32_t members[kMultisamples];
-    uint32_t followers = 0u;
-    #pragma unroll
-    for (uint32_t j = 0; j < kMultisamples; j++) members[j] = 1u << j;
-    #pragma unroll
-    for (uint32_t j = 0; j < kMultisamples; j++) {
-        #pragma unroll
-        for (uint32_t k = j + 1; k < kMultisamples; k++) {
-            if (cx[j] == cx[k] && cy[j] == cy[k] && cz[j] == cz[k]) {
-                members[j] |= 1u << k;
-                followers |= 1u << k;
-            }
-        }
-    }
-    const uint32_t leaders = ((1u << kMultisamples) - 1u) & ~followers;
-    #pragma unroll
-    for (uint32_t j = 0; j < kMultisamples; j++) {
-        if ((leaders >> j) & 1u) ws.cell[lane * kRecordStride + j] = make_int4(cx[j], cy[j], cz[j], static_cast<int>(members[j]));
-    }
-    return leaders;
-}
+// warp-cooperative gradient scatter (featurize_common.cuh:123-173, 273-291): the corner groups of a warp's intervals as
+// one task list (above); the atomics are order-free
 
 // works through the warp's task list of one level: merged corner weights of each group, its 8 rows, and the atomics of
 // the owner's gradient (fp32 table, or fp16 table with rows re-based at row_base)
 template <int F, bool HALF>
-__device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32_t level, const ScatterWarpSmem& ws, const uint32_t n_tasks,
+__device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32_t level, const GroupRecords& gr, const uint32_t n_tasks,
                                               const int lane, const float* warp_rows, const int stride, float* __restrict__ grad_table,
                                               uint16_t* __restrict__ grad_table_half, const uint32_t row_base) {
     for (uint32_t t = lane; t < n_tasks; t += 32) {
-        const uint32_t task = ws.task[t];
-        const uint32_t owner = task & 31u, leader = task >> 5;
-        const float4 q = ws.frac[owner * kRecordStride + leader];
-        const int4 c = ws.cell[owner * kRecordStride + leader];
         float corner_weights[8];
-        #pragma unroll
-        for (uint32_t corner = 0; corner < 8; corner++) {
-            const float wx = corner & 4u ? q.x : 1.0f - q.x;
-            const float wy = corner & 2u ? q.y : 1.0f - q.y;
-            const float wz = corner & 1u ? q.z : 1.0f - q.z;
-            corner_weights[corner] = __fmaf_rn(q.w, __fmul_rn(__fmul_rn(wx, wy), wz), 0.0f);
-        }
-        uint32_t others = static_cast<uint32_t>(c.w) & ~(1u << leader);
-        while (others != 0u) {
-            const uint32_t m = __ffs(others) - 1u;
-            others &= others - 1u;
-            const float4 qm = ws.frac[owner * kRecordStride + m];
-            #pragma unroll
-            for (uint32_t corner = 0; corner < 8; corner++) {
-                const float wx = corner & 4u ? qm.x : 1.0f - qm.x;
-                const float wy = corner & 2u ? qm.y : 1.0f - qm.y;
-                const float wz = corner & 1u ? qm.z : 1.0f - qm.z;
-                corner_weights[corner] = __fmaf_rn(qm.w, __fmul_rn(__fmul_rn(wx, wy), wz), corner_weights[corner]);
-            }
-        }
+        int4 c;
+        uint32_t owner;
+        task_group(gr, t, corner_weights, c, owner);
         float g[F];
         #pragma unroll
         for (int f = 0; f < F; f++) g[f] = warp_rows[owner * stride + level * (F + 1) + f];
         #pragma unroll
         for (uint32_t corner = 0; corner < 8; corner++) {
             float weight = corner_weights[corner];
-            const uint32_t row = corner_row(gp, level, c.x + static_cast<int>((corner >> 2) & 1u), c.y + static_cast<int>((corner >> 1) & 1u),
-                                            c.z + static_cast<int>(corner & 1u), weight);
+            const uint32_t row = corner_row(gp, level, c.x + corner_offset(corner, 2), c.y + corner_offset(corner, 1), c.z + corner_offset(corner, 0), weight);
             if (weight == 0.0f) continue;
             if constexpr (HALF) add_row_f16<F>(grad_table_half, row - row_base, weight, g);
             else add_row_f32<F>(grad_table, row, weight, g);
@@ -420,38 +594,31 @@ __device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32
 template <int F>
 __device__ __forceinline__ void scatter_warp(const GridParams& gp, const Frustum& fr, const bool active, const float* warp_rows, const int stride,
                                              const int lane, const uint32_t n_fp32, float* __restrict__ grad_table,
-                                             uint16_t* __restrict__ grad_table_half, ScatterWarpSmem& ws) {
+                                             uint16_t* __restrict__ grad_table_half, GroupRecords& gr) {
     float3 x[kMultisamples];
     float scale[kMultisamples];
     if (active) multisamples(fr, x, scale);
     const uint32_t half_base = gp.offset[min(n_fp32, gp.n_levels)];
     const float* g_row = warp_rows + lane * stride;
-    const uint32_t lanes_below = (1u << lane) - 1u;
     #pragma unroll 1
     for (uint32_t level = 0; level < gp.n_levels; level++) {
+        const uint32_t size = gp.size[level];
         uint32_t leaders = 0u;
         if (active) {
             bool any = false;
             #pragma unroll
             for (int f = 0; f < F; f++) any |= g_row[level * (F + 1) + f] != 0.0f;
-            if (any) leaders = publish_level(gp, level, x, scale, ws, lane);
+            if (any) {
+                float weighting[kMultisamples];
+                #pragma unroll
+                for (uint32_t j = 0; j < kMultisamples; j++) weighting[j] = level_weighting(size, scale[j]);
+                leaders = publish_level(size, x, weighting, gr, lane);
+            }
         }
-        // this lane's first task slot (exclusive prefix of the 0..6 group counts, one ballot per count bit) and the total
-        const uint32_t n = __popc(leaders);
-        uint32_t first = 0u, n_tasks = 0u;
-        #pragma unroll
-        for (int b = 0; b < 3; b++) {
-            const uint32_t bits = __ballot_sync(0xFFFFFFFFu, (n >> b) & 1u);
-            first += static_cast<uint32_t>(__popc(bits & lanes_below)) << b;
-            n_tasks += static_cast<uint32_t>(__popc(bits)) << b;
-        }
-        #pragma unroll
-        for (uint32_t j = 0; j < kMultisamples; j++) {
-            if ((leaders >> j) & 1u) ws.task[first + __popc(leaders & ((1u << j) - 1u))] = static_cast<uint8_t>(lane | (j << 5));
-        }
+        const uint32_t n_tasks = list_tasks_by_lane(leaders, lane, gr);
         __syncwarp();
-        if (level < n_fp32) scatter_tasks<F, false>(gp, level, ws, n_tasks, lane, warp_rows, stride, grad_table, grad_table_half, 0u);
-        else scatter_tasks<F, true>(gp, level, ws, n_tasks, lane, warp_rows, stride, grad_table, grad_table_half, half_base);
+        if (level < n_fp32) scatter_tasks<F, false>(gp, level, gr, n_tasks, lane, warp_rows, stride, grad_table, grad_table_half, 0u);
+        else scatter_tasks<F, true>(gp, level, gr, n_tasks, lane, warp_rows, stride, grad_table, grad_table_half, half_base);
         __syncwarp();
     }
 }
@@ -500,13 +667,13 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_ke
     if (active && a.skip_if_zero != nullptr && __ldcs(a.skip_if_zero + sample) == 0.0f) active = false;
     Frustum fr;
     if (active) fr = setup_frustum(a.in, gp.pattern_stream, sample);
-    ScatterWarpSmem& ws = reinterpret_cast<ScatterWarpSmem*>(smem + kBlock * stride)[warp];
-    scatter_warp<F>(gp, fr, active, warp_rows, stride, lane, a.n_fp32_levels, a.grad_table, a.grad_table_half, ws);
+    GroupRecords& gr = reinterpret_cast<GroupRecords*>(smem + kBlock * stride)[warp];
+    scatter_warp<F>(gp, fr, active, warp_rows, stride, lane, a.n_fp32_levels, a.grad_table, a.grad_table_half, gr);
 }
 
 // dynamic shared memory of fz_backward_kernel in floats: staged gradient rows, then the warps' scatter records
 __host__ __device__ constexpr int backward_smem_floats(const int n_out) {
-    return kBlock * staged_stride(n_out) + kWarps * static_cast<int>(sizeof(ScatterWarpSmem) / sizeof(float));
+    return kBlock * staged_stride(n_out) + kWarps * static_cast<int>(sizeof(GroupRecords) / sizeof(float));
 }
 
 // ---------------------------------------------------------------------------------------------------------------------

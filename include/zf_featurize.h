@@ -114,8 +114,9 @@ typedef struct zf_backward_mlp_args {
     float* grad_w1;                      /* [mlp_width] */
     float* grad_b1;                      /* [1] */
     void* workspace;                     /* optional device scratch (16-byte aligned) of at least
-                                            zf_featurize_backward_mlp_workspace_size() bytes; NULL: the call allocates it
-                                            from the stream-ordered pool (cudaMallocAsync) and frees it after use */
+                                            zf_featurize_backward_mlp_workspace_size() bytes; NULL: the call takes it
+                                            from the featurizer's own stream-ordered memory pool, which keeps the
+                                            largest workspace used reserved until zf_featurizer_destroy */
     int64_t workspace_bytes;
 } zf_backward_mlp_args;
 
