@@ -562,27 +562,89 @@ __device__ __forceinline__ void add_row_f16(uint16_t* __restrict__ grad_table, c
 // warp-cooperative gradient scatter (featurize_common.cuh:123-173, 273-291): the corner groups of a warp's intervals as
 // one task list (above); the atomics are order-free
 
+// Runs of tasks with the same cell in consecutive lanes are common on coarse levels, where neighbouring intervals of a
+// ray share cells; one atomic per run and corner instead of per lane keeps the L2 atomic units from serialising on a few
+// hot rows (how much that costs otherwise depends on where the table's rows fall among the L2 slices: up to 1.2 ms per
+// proposal backward at 65,536 rays on a B200). A round takes this path when at least kMinRunLanes of its 32 lanes
+// continue a run (swept 4-28: fewer pays the scan on rounds that gain little, more leaves hot rows unmerged).
+constexpr int kMinRunLanes = 24;
+
+// inclusive sums of v over the lanes from run_start to this lane (a segmented scan)
+template <int F>
+__device__ __forceinline__ void sum_run(float (&v)[F], const int lane, const int run_start) {
+    #pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        #pragma unroll
+        for (int f = 0; f < F; f++) {
+            const float y = __shfl_up_sync(0xFFFFFFFFu, v[f], d);
+            if (lane - d >= run_start) v[f] += y;
+        }
+    }
+}
+
 // works through the warp's task list of one level: merged corner weights of each group, its 8 rows, and the atomics of
-// the owner's gradient (fp32 table, or fp16 table with rows re-based at row_base)
+// the owner's gradient (fp32 table, or fp16 table with rows re-based at row_base). fp32 contributions of runs of equal
+// cells are summed over the run first; fp16 contributions are always rounded and added one by one, as the reference
+// does.
 template <int F, bool HALF>
 __device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32_t level, const GroupRecords& gr, const uint32_t n_tasks,
                                               const int lane, const float* warp_rows, const int stride, float* __restrict__ grad_table,
                                               uint16_t* __restrict__ grad_table_half, const uint32_t row_base) {
-    for (uint32_t t = lane; t < n_tasks; t += 32) {
-        float corner_weights[8];
-        int4 c;
-        uint32_t owner;
-        task_group(gr, t, corner_weights, c, owner);
+    for (uint32_t first = 0; first < n_tasks; first += 32) {
+        const bool valid = first + lane < n_tasks;
+        float weights[8];
+        uint32_t rows[8];
         float g[F];
-        #pragma unroll
-        for (int f = 0; f < F; f++) g[f] = warp_rows[owner * stride + level * (F + 1) + f];
-        #pragma unroll
-        for (uint32_t corner = 0; corner < 8; corner++) {
-            float weight = corner_weights[corner];
-            const uint32_t row = corner_row(gp, level, c.x + corner_offset(corner, 2), c.y + corner_offset(corner, 1), c.z + corner_offset(corner, 0), weight);
-            if (weight == 0.0f) continue;
-            if constexpr (HALF) add_row_f16<F>(grad_table_half, row - row_base, weight, g);
-            else add_row_f32<F>(grad_table, row, weight, g);
+        int4 c = make_int4(0, 0, 0, 0);
+        if (valid) {
+            uint32_t owner;
+            task_group(gr, first + lane, weights, c, owner);
+            #pragma unroll
+            for (int f = 0; f < F; f++) g[f] = warp_rows[owner * stride + level * (F + 1) + f];
+            #pragma unroll
+            for (uint32_t corner = 0; corner < 8; corner++) {
+                rows[corner] = corner_row(gp, level, c.x + corner_offset(corner, 2), c.y + corner_offset(corner, 1), c.z + corner_offset(corner, 0), weights[corner]);
+            }
+        }
+        else {
+            #pragma unroll
+            for (uint32_t corner = 0; corner < 8; corner++) {
+                weights[corner] = 0.0f;
+                rows[corner] = 0u;
+            }
+            #pragma unroll
+            for (int f = 0; f < F; f++) g[f] = 0.0f;
+        }
+        if constexpr (!HALF) {
+            // lanes that continue the run of the lane before them (same cell; every lane takes part in the shuffles)
+            const int lx = __shfl_up_sync(0xFFFFFFFFu, c.x, 1), ly = __shfl_up_sync(0xFFFFFFFFu, c.y, 1), lz = __shfl_up_sync(0xFFFFFFFFu, c.z, 1);
+            const bool continues = valid && lane > 0 && lx == c.x && ly == c.y && lz == c.z;
+            const uint32_t continuing = __ballot_sync(0xFFFFFFFFu, continues);
+            if (__popc(continuing) >= kMinRunLanes) {
+                const uint32_t heads = ~continuing;
+                const int run_start = 31 - __clz(heads & (0xFFFFFFFFu >> (31 - lane)));
+                const bool run_end = lane == 31 || !((continuing >> (lane + 1)) & 1u);
+                #pragma unroll
+                for (uint32_t corner = 0; corner < 8; corner++) {
+                    float v[F];
+                    #pragma unroll
+                    for (int f = 0; f < F; f++) v[f] = weights[corner] != 0.0f ? weights[corner] * g[f] : 0.0f;
+                    sum_run<F>(v, lane, run_start);
+                    bool any = false;
+                    #pragma unroll
+                    for (int f = 0; f < F; f++) any |= v[f] != 0.0f;
+                    if (valid && run_end && any) add_row_f32<F>(grad_table, rows[corner], 1.0f, v);
+                }
+                continue;
+            }
+        }
+        if (valid) {
+            #pragma unroll
+            for (uint32_t corner = 0; corner < 8; corner++) {
+                if (weights[corner] == 0.0f) continue;
+                if constexpr (HALF) add_row_f16<F>(grad_table_half, rows[corner] - row_base, weights[corner], g);
+                else add_row_f32<F>(grad_table, rows[corner], weights[corner], g);
+            }
         }
     }
 }
