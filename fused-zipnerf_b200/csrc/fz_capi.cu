@@ -90,11 +90,11 @@ cudaError_t ensure_smem(const void* kernel, const size_t bytes) {
 
 template <typename Args>
 cudaError_t launch(void (*kernel)(zf::GridParams, Args), const unsigned grid, const size_t smem, cudaStream_t stream,
-                   const zf::GridParams& gp, const Args& args) {
+                   const zf::GridParams& gp, const Args& args, const int block = zf::kBlock) {
     cudaError_t error = ensure_smem(reinterpret_cast<const void*>(kernel), smem);
     if (error != cudaSuccess) return error;
     void* params[] = {const_cast<zf::GridParams*>(&gp), const_cast<Args*>(&args)};
-    return cudaLaunchKernel(reinterpret_cast<const void*>(kernel), dim3(grid), dim3(zf::kBlock), params, smem, stream);
+    return cudaLaunchKernel(reinterpret_cast<const void*>(kernel), dim3(grid), dim3(block), params, smem, stream);
 }
 
 unsigned n_blocks(const int64_t n) { return static_cast<unsigned>((n + zf::kBlock - 1) / zf::kBlock); }
@@ -352,10 +352,11 @@ int zf_featurize_backward_mlp(zf_featurizer* f, const zf_backward_mlp_args* a, c
     const size_t smem = static_cast<size_t>(zf::backward_mlp_smem_floats(n_out, zf::mlp_pad(n_out), f->mlp_width)) * sizeof(float);
     cudaError_t error = ensure_smem(reinterpret_cast<const void*>(f->mlp_kernels->backward_mlp), smem);
     int resident = 0;
-    if (error == cudaSuccess) error = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, reinterpret_cast<const void*>(f->mlp_kernels->backward_mlp), zf::kBlock, smem);
+    if (error == cudaSuccess) error = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, reinterpret_cast<const void*>(f->mlp_kernels->backward_mlp), zf::kMlpBlock, smem);
     if (error == cudaSuccess) {
-        const unsigned blocks = std::min<unsigned>(n_blocks(n_samples), static_cast<unsigned>(f->n_sms * std::max(resident, 1)));
-        error = launch(f->mlp_kernels->backward_mlp, blocks, smem, stream, f->params, k);
+        const unsigned mlp_blocks = static_cast<unsigned>((n_samples + zf::kMlpBlock - 1) / zf::kMlpBlock);
+        const unsigned blocks = std::min<unsigned>(mlp_blocks, static_cast<unsigned>(f->n_sms * std::max(resident, 1)));
+        error = launch(f->mlp_kernels->backward_mlp, blocks, smem, stream, f->params, k, zf::kMlpBlock);
     }
     if (error == cudaSuccess) {
         // the scatter of the scaled feature gradients into the fp32 grid gradient (all levels), skipping samples with a

@@ -29,7 +29,7 @@ constexpr int kBlock = 128;
 #define ZF_MIN_BLOCKS_BACKWARD 4
 #endif
 #ifndef ZF_MIN_BLOCKS_BACKWARD_MLP
-#define ZF_MIN_BLOCKS_BACKWARD_MLP 3
+#define ZF_MIN_BLOCKS_BACKWARD_MLP 2
 #endif
 constexpr int kWarps = kBlock / 32;
 
@@ -761,156 +761,189 @@ struct BackwardMlpArgs {
     float* grad_b1;
 };
 
-// Shared memory of fz_backward_mlp_kernel in floats. Per-sample columns ([row][sample], row stride kBlock + 1) make
-// both the per-thread writes of phase 1 and the tile reads of phase 2 bank-conflict free.
-__host__ __device__ constexpr int column_stride() { return kBlock + 1; }
+// The kernel runs warps independently: each takes 32 samples at a time (a chunk) through
+//   phase 1 (lane = sample): the MLP recomputation in the forward's accumulation order (the same ReLU mask as the
+//           forward), its input gradient (written to grad_rows) and the pre-activations (to shared memory), then
+//   phase 2 (lane = 4 x 4 tiles of grad_w0, and the scalar sums): the chunk's sums in sample order, added to the block's
+//           sums with shared-memory atomics.
+// Chunk rows in shared memory have a stride of an odd number of 16-byte words, so the lanes' 16-byte stores of phase 1
+// are bank-conflict free, and phase 2 reads one row (broadcast) per sample.
+#ifndef ZF_MLP_WARPS
+#define ZF_MLP_WARPS 8
+#endif
+constexpr int kMlpWarps = ZF_MLP_WARPS;
+constexpr int kMlpBlock = 32 * kMlpWarps;
+__host__ __device__ constexpr int odd_quads(const int n) { return (n / 4) % 2 == 1 ? n : n + 4; }
+__host__ __device__ constexpr int mlp_rows_pad(const int width) { return (width + 3) / 4 * 4; }
+__host__ __device__ constexpr int mlp_block_floats(const int n_out, const int nout_pad, const int width) {
+    return mlp_rows_pad(width) * nout_pad + 2 * mlp_rows_pad(width)  // weights (w0 rows padded to nout_pad), b0, w1
+        + (width * n_out + 2 * width + 1 + 3) / 4 * 4;                // the block's parameter gradient sums
+}
+__host__ __device__ constexpr int mlp_warp_floats(const int nout_pad, const int width) {
+    return 32 * odd_quads(mlp_rows_pad(width)) + 32 * odd_quads(nout_pad) + 32;  // pre-activations, features, upstream gradient
+}
 __host__ __device__ constexpr int backward_mlp_smem_floats(const int n_out, const int nout_pad, const int width) {
-    return width * nout_pad + 2 * width                       // weights (w0 rows padded to nout_pad), b0, w1
-        + (width * n_out + 2 * width + 1)                     // parameter gradient sums of the block
-        + ((width + 3) / 4 * 4) * column_stride()             // pre-activations [j][sample]
-        + 2 * nout_pad * column_stride()                      // features and feature gradients [i][sample]
-        + kBlock;                                             // raw density gradients
+    return mlp_block_floats(n_out, nout_pad, width) + kMlpWarps * mlp_warp_floats(nout_pad, width);
 }
 
 template <int F, int NOUT_PAD>
-__global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_backward_mlp_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardMlpArgs a) {
-    constexpr int cs = column_stride();
+__global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_backward_mlp_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardMlpArgs a) {
     const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
     const int W = a.mlp_width;
-    const int w_pad = (W + 3) / 4 * 4;
+    const int w_pad = mlp_rows_pad(W);
     const int n_w0 = W * n_out;
     const int n_params = n_w0 + 2 * W + 1;
+    const int ps = odd_quads(w_pad), fs = odd_quads(NOUT_PAD);
     extern __shared__ __align__(16) float smem[];
-    float* s_w0 = smem;                        // [W, NOUT_PAD]
-    float* s_b0 = s_w0 + W * NOUT_PAD;
-    float* s_w1 = s_b0 + W;
-    float* s_acc = s_w1 + W;                   // [n_params] (the reference's output order: w0, b0, w1, b1)
-    float* s_pre = s_acc + n_params;           // [w_pad][cs]
-    float* s_col = s_pre + w_pad * cs;         // [NOUT_PAD][cs] features
-    float* s_gcol = s_col + NOUT_PAD * cs;     // [NOUT_PAD][cs] scaled feature gradients
-    float* s_g = s_gcol + NOUT_PAD * cs;       // [kBlock]
-    for (int i = threadIdx.x; i < W * NOUT_PAD; i += kBlock) {
+    float* s_w0 = smem;                        // [w_pad, NOUT_PAD]
+    float* s_b0 = s_w0 + w_pad * NOUT_PAD;     // [w_pad]
+    float* s_w1 = s_b0 + w_pad;                // [w_pad]
+    float* s_acc = s_w1 + w_pad;               // [n_params] (the reference's output order: w0, b0, w1, b1)
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float* s_pre = smem + mlp_block_floats(n_out, NOUT_PAD, W) + warp * mlp_warp_floats(NOUT_PAD, W);  // [32, ps]
+    float* s_feat = s_pre + 32 * ps;           // [32, fs]
+    float* s_g = s_feat + 32 * fs;             // [32]
+    // padding rows (j >= W) and columns (i >= n_out) are zero: their pre-activations are 0 and select no gradient
+    for (int i = threadIdx.x; i < w_pad * NOUT_PAD; i += kMlpBlock) {
         const int j = i / NOUT_PAD, c = i - j * NOUT_PAD;
-        s_w0[i] = c < n_out ? __ldg(a.w0 + j * n_out + c) : 0.0f;
+        s_w0[i] = j < W && c < n_out ? __ldg(a.w0 + j * n_out + c) : 0.0f;
     }
-    for (int i = threadIdx.x; i < W; i += kBlock) {
-        s_b0[i] = __ldg(a.b0 + i);
-        s_w1[i] = __ldg(a.w1 + i);
+    for (int i = threadIdx.x; i < w_pad; i += kMlpBlock) {
+        s_b0[i] = i < W ? __ldg(a.b0 + i) : 0.0f;
+        s_w1[i] = i < W ? __ldg(a.w1 + i) : 0.0f;
     }
-    for (int i = threadIdx.x; i < n_params; i += kBlock) s_acc[i] = 0.0f;
-    // padding rows of the pre-activations stay non-positive (they select no gradient)
-    for (int i = threadIdx.x; i < (w_pad - W) * cs; i += kBlock) s_pre[W * cs + i] = 0.0f;
+    for (int i = threadIdx.x; i < n_params; i += kMlpBlock) s_acc[i] = 0.0f;
+    for (int i = lane; i < 32 * fs; i += 32) s_feat[i] = 0.0f;
     __syncthreads();
     const int n_tiles = (w_pad / 4) * (NOUT_PAD / 4);
-    const int n_items = n_tiles + 2 * W + 1;
+    const int n_scalars = 2 * W + 1;
+    const bool vector_rows = n_out % 4 == 0;
 
-    // block-uniform loop bound, so every thread reaches the barriers
-    for (uint32_t base = blockIdx.x * kBlock; base < a.in.n_samples; base += gridDim.x * kBlock) {
-        // phase 1, one sample per thread: MLP recomputation and its input gradient (featurize_backward_mlp.cu:82-105)
-        const uint32_t sample = base + threadIdx.x;
-        const bool active = sample < a.in.n_samples;
-        float f[NOUT_PAD];
-        #pragma unroll
-        for (int i = 0; i < NOUT_PAD; i++) f[i] = active && i < n_out ? __ldcs(a.features + static_cast<size_t>(sample) * n_out + i) : 0.0f;
-        const float g = active ? __ldcs(a.grad_raw_density + sample) : 0.0f;
-        float grad_f[NOUT_PAD];
-        #pragma unroll
-        for (int i = 0; i < NOUT_PAD; i++) grad_f[i] = 0.0f;
-        for (int j = 0; j < W; j++) {
-            float pre = s_b0[j];
-            const float4* w = reinterpret_cast<const float4*>(s_w0 + j * NOUT_PAD);
+    // warp-uniform loop bound
+    for (uint32_t base = (blockIdx.x * kMlpWarps + warp) * 32u; base < a.in.n_samples; base += gridDim.x * kMlpBlock) {
+        const int n_rows = min(32, static_cast<int>(a.in.n_samples - base));
+        // the chunk's features (coalesced) and upstream gradients
+        for (LaneWalk w(lane, n_out); w.r < n_rows; w.next()) s_feat[w.r * fs + w.c] = __ldcs(a.features + static_cast<size_t>(base + w.r) * n_out + w.c);
+        s_g[lane] = lane < n_rows ? __ldcs(a.grad_raw_density + base + lane) : 0.0f;
+        __syncwarp();
+
+        // phase 1, one sample per lane: MLP recomputation and its input gradient (featurize_backward_mlp.cu:82-105)
+        {
+            float f[NOUT_PAD];
             #pragma unroll
             for (int q = 0; q < NOUT_PAD / 4; q++) {
-                const float4 wq = w[q];
-                if (4 * q < n_out) pre = __fmaf_rn(wq.x, f[4 * q], pre);
-                if (4 * q + 1 < n_out) pre = __fmaf_rn(wq.y, f[4 * q + 1], pre);
-                if (4 * q + 2 < n_out) pre = __fmaf_rn(wq.z, f[4 * q + 2], pre);
-                if (4 * q + 3 < n_out) pre = __fmaf_rn(wq.w, f[4 * q + 3], pre);
+                const float4 v = *reinterpret_cast<const float4*>(s_feat + lane * fs + 4 * q);
+                f[4 * q] = v.x;
+                f[4 * q + 1] = v.y;
+                f[4 * q + 2] = v.z;
+                f[4 * q + 3] = v.w;
             }
-            s_pre[j * cs + threadIdx.x] = pre;
-            if (pre > 0.0f) {
-                const float grad_pre = __fmul_rn(g, s_w1[j]);
+            const float g = s_g[lane];
+            float grad_f[NOUT_PAD];
+            #pragma unroll
+            for (int i = 0; i < NOUT_PAD; i++) grad_f[i] = 0.0f;
+            for (int j0 = 0; j0 < w_pad; j0 += 4) {
+                float pre[4];
                 #pragma unroll
-                for (int q = 0; q < NOUT_PAD / 4; q++) {
-                    const float4 wq = w[q];
-                    grad_f[4 * q] = __fmaf_rn(grad_pre, wq.x, grad_f[4 * q]);
-                    grad_f[4 * q + 1] = __fmaf_rn(grad_pre, wq.y, grad_f[4 * q + 1]);
-                    grad_f[4 * q + 2] = __fmaf_rn(grad_pre, wq.z, grad_f[4 * q + 2]);
-                    grad_f[4 * q + 3] = __fmaf_rn(grad_pre, wq.w, grad_f[4 * q + 3]);
-                }
-            }
-        }
-        s_g[threadIdx.x] = g;
-        #pragma unroll
-        for (int i = 0; i < NOUT_PAD; i++) {
-            s_col[i * cs + threadIdx.x] = f[i];
-            s_gcol[i * cs + threadIdx.x] = __fmul_rn(grad_f[i], kFeatureScale);
-        }
-        __syncthreads();
-
-        // the block's scaled feature gradients to grad_rows, coalesced (rows of consecutive samples are contiguous)
-        const int n_rows = min(kBlock, static_cast<int>(a.in.n_samples - base));
-        for (LaneWalk w(threadIdx.x, n_out, kBlock); w.r < n_rows; w.next()) {
-            __stcs(a.grad_rows + (static_cast<size_t>(base) + w.r) * n_out + w.c, s_gcol[w.c * cs + w.r]);
-        }
-
-        // phase 2: the block's parameter gradient sums over its samples, in sample order per output (as the reference's
-        // featurize_backward_mlp.cu:110-135): 4 x 4 tiles of grad_w0 (a register-blocked outer product of
-        // [pre > 0] g with the features), then grad_b0, grad_w1 and grad_b1
-        for (int item = threadIdx.x; item < n_items; item += kBlock) {
-            if (item < n_tiles) {
-                const int j0 = (item / (NOUT_PAD / 4)) * 4, i0 = (item % (NOUT_PAD / 4)) * 4;
-                float sum[4][4] = {};
-                for (int s = 0; s < kBlock; s++) {
-                    const float gs = s_g[s];
-                    float av[4], fv[4];
+                for (int r = 0; r < 4; r++) {
+                    const float4* w = reinterpret_cast<const float4*>(s_w0 + (j0 + r) * NOUT_PAD);
+                    float p = s_b0[j0 + r];
                     #pragma unroll
-                    for (int r = 0; r < 4; r++) {
-                        av[r] = s_pre[(j0 + r) * cs + s] > 0.0f ? gs : 0.0f;
-                        fv[r] = s_col[(i0 + r) * cs + s];
+                    for (int q = 0; q < NOUT_PAD / 4; q++) {
+                        const float4 wq = w[q];
+                        if (4 * q < n_out) p = __fmaf_rn(wq.x, f[4 * q], p);
+                        if (4 * q + 1 < n_out) p = __fmaf_rn(wq.y, f[4 * q + 1], p);
+                        if (4 * q + 2 < n_out) p = __fmaf_rn(wq.z, f[4 * q + 2], p);
+                        if (4 * q + 3 < n_out) p = __fmaf_rn(wq.w, f[4 * q + 3], p);
                     }
-                    #pragma unroll
-                    for (int r = 0; r < 4; r++) {
+                    pre[r] = p;
+                    if (p > 0.0f) {
+                        const float grad_pre = __fmul_rn(g, s_w1[j0 + r]);
                         #pragma unroll
-                        for (int c = 0; c < 4; c++) {
-                            if (av[r] != 0.0f) sum[r][c] = __fmaf_rn(av[r], fv[c], sum[r][c]);
+                        for (int q = 0; q < NOUT_PAD / 4; q++) {
+                            const float4 wq = w[q];
+                            grad_f[4 * q] = __fmaf_rn(grad_pre, wq.x, grad_f[4 * q]);
+                            grad_f[4 * q + 1] = __fmaf_rn(grad_pre, wq.y, grad_f[4 * q + 1]);
+                            grad_f[4 * q + 2] = __fmaf_rn(grad_pre, wq.z, grad_f[4 * q + 2]);
+                            grad_f[4 * q + 3] = __fmaf_rn(grad_pre, wq.w, grad_f[4 * q + 3]);
                         }
                     }
                 }
+                *reinterpret_cast<float4*>(s_pre + lane * ps + j0) = make_float4(pre[0], pre[1], pre[2], pre[3]);
+            }
+            // this sample's scaled feature gradient to grad_rows (read by the scatter kernel)
+            if (lane < n_rows) {
+                float* out = a.grad_rows + static_cast<size_t>(base + lane) * n_out;
+                if (vector_rows) {
+                    #pragma unroll
+                    for (int q = 0; q < NOUT_PAD / 4; q++) {
+                        if (4 * q < n_out) {
+                            __stcs(reinterpret_cast<float4*>(out) + q, make_float4(__fmul_rn(grad_f[4 * q], kFeatureScale), __fmul_rn(grad_f[4 * q + 1], kFeatureScale),
+                                                                                  __fmul_rn(grad_f[4 * q + 2], kFeatureScale), __fmul_rn(grad_f[4 * q + 3], kFeatureScale)));
+                        }
+                    }
+                }
+                else {
+                    #pragma unroll
+                    for (int i = 0; i < NOUT_PAD; i++) {
+                        if (i < n_out) __stcs(out + i, __fmul_rn(grad_f[i], kFeatureScale));
+                    }
+                }
+            }
+        }
+        __syncwarp();
+
+        // phase 2: the chunk's parameter gradient sums in sample order per output (as the reference's
+        // featurize_backward_mlp.cu:110-135): 4 x 4 tiles of grad_w0 (a register-blocked outer product of [pre > 0] g
+        // with the features), then grad_b0, grad_w1 and grad_b1
+        for (int tile = lane; tile < n_tiles; tile += 32) {
+            const int j0 = (tile / (NOUT_PAD / 4)) * 4, i0 = (tile % (NOUT_PAD / 4)) * 4;
+            float sum[4][4] = {};
+            for (int s = 0; s < n_rows; s++) {
+                const float4 p = *reinterpret_cast<const float4*>(s_pre + s * ps + j0);
+                const float4 fv = *reinterpret_cast<const float4*>(s_feat + s * fs + i0);
+                const float gs = s_g[s];
+                const float av[4] = {p.x > 0.0f ? gs : 0.0f, p.y > 0.0f ? gs : 0.0f, p.z > 0.0f ? gs : 0.0f, p.w > 0.0f ? gs : 0.0f};
+                const float fc[4] = {fv.x, fv.y, fv.z, fv.w};
                 #pragma unroll
                 for (int r = 0; r < 4; r++) {
                     #pragma unroll
                     for (int c = 0; c < 4; c++) {
-                        const int j = j0 + r, i = i0 + c;
-                        if (j < W && i < n_out) s_acc[j * n_out + i] += sum[r][c];
+                        if (av[r] != 0.0f) sum[r][c] = __fmaf_rn(av[r], fc[c], sum[r][c]);
                     }
                 }
             }
-            else {
-                const int q = item - n_tiles;
-                float sum = 0.0f;
-                if (q < W) {
-                    for (int s = 0; s < kBlock; s++) {
-                        if (s_pre[q * cs + s] > 0.0f) sum = __fadd_rn(sum, s_g[s]);
-                    }
-                    s_acc[n_w0 + q] += sum;
-                }
-                else if (q < 2 * W) {
-                    const int j = q - W;
-                    for (int s = 0; s < kBlock; s++) sum = __fmaf_rn(s_g[s], fmaxf(s_pre[j * cs + s], 0.0f), sum);
-                    s_acc[n_w0 + W + j] += sum;
-                }
-                else {
-                    for (int s = 0; s < kBlock; s++) sum = __fadd_rn(sum, s_g[s]);
-                    s_acc[n_w0 + 2 * W] += sum;
+            #pragma unroll
+            for (int r = 0; r < 4; r++) {
+                #pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    const int j = j0 + r, i = i0 + c;
+                    if (j < W && i < n_out && sum[r][c] != 0.0f) atomicAdd(s_acc + j * n_out + i, sum[r][c]);
                 }
             }
         }
-        __syncthreads();
+        for (int q = lane; q < n_scalars; q += 32) {
+            float sum = 0.0f;
+            if (q < W) {
+                for (int s = 0; s < n_rows; s++) {
+                    if (s_pre[s * ps + q] > 0.0f) sum = __fadd_rn(sum, s_g[s]);
+                }
+            }
+            else if (q < 2 * W) {
+                const int j = q - W;
+                for (int s = 0; s < n_rows; s++) sum = __fmaf_rn(s_g[s], fmaxf(s_pre[s * ps + j], 0.0f), sum);
+            }
+            else {
+                for (int s = 0; s < n_rows; s++) sum = __fadd_rn(sum, s_g[s]);
+            }
+            if (sum != 0.0f) atomicAdd(s_acc + n_w0 + q, sum);
+        }
+        __syncwarp();
     }
+    __syncthreads();
 
     // one atomic per parameter and block, with w1 applied late (featurize_backward_mlp.cu:139-147)
-    for (int q = threadIdx.x; q < n_params; q += kBlock) {
+    for (int q = threadIdx.x; q < n_params; q += kMlpBlock) {
         const float acc = s_acc[q];
         if (acc == 0.0f) continue;
         if (q < n_w0) atomicAdd(a.grad_w0 + q, s_w1[q / n_out] * acc);
