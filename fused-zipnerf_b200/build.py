@@ -63,7 +63,7 @@ def build_library(jobs: int | None = None, force: bool = False, subset: set | No
     wanted = []
     for features in range(1, MAX_FEATURES + 1):
         # pad 0: the kernels without MLP; pads: the MLP kernels of padded input widths up to 16 (F + 1)
-        for pad in [0] + list(range(8, 16 * (features + 1) + 1, 8)):
+        for pad in [0] + list(range(4, 16 * (features + 1) + 1, 4)):
             if subset is not None and (features, pad) not in subset and (features, 0) not in subset:
                 continue
             obj = BUILD / f'fz_inst_F{features}_P{pad}.o'

@@ -3,7 +3,7 @@
 //
 // The reference compiles one kernel per grid at runtime with the layout, level count and feature count as constants
 // (featurizer.cu:157-184). Here kernels are compiled ahead of time for sm_100a, templated only on the features per level
-// F (and, with the MLP, on the MLP input width rounded up to a multiple of 8); the level loop runs over the layout in
+// F (and, with the MLP, on the MLP input width rounded up to a multiple of 4); the level loop runs over the layout in
 // the kernel parameters, with one level's multisample / corner / gather body unrolled. Per-thread feature rows are
 // staged in shared memory, so outputs leave the SM as coalesced warp-wide stores.
 #pragma once
@@ -764,7 +764,7 @@ struct BackwardMlpArgs {
 // The kernel runs warps independently: each takes 32 samples at a time (a chunk) through
 //   phase 1 (lane = sample): the MLP recomputation in the forward's accumulation order (the same ReLU mask as the
 //           forward), its input gradient (written to grad_rows) and the pre-activations (to shared memory), then
-//   phase 2 (lane = 4 x 4 tiles of grad_w0, and the scalar sums): the chunk's sums in sample order, added to the block's
+//   phase 2 (lane = 4-row tiles of grad_w0, and the scalar sums): the chunk's sums in sample order, added to the block's
 //           sums with shared-memory atomics.
 // Chunk rows in shared memory have a stride of an odd number of 16-byte words, so the lanes' 16-byte stores of phase 1
 // are bank-conflict free, and phase 2 reads one row (broadcast) per sample.
@@ -815,7 +815,11 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
     for (int i = threadIdx.x; i < n_params; i += kMlpBlock) s_acc[i] = 0.0f;
     for (int i = lane; i < 32 * fs; i += 32) s_feat[i] = 0.0f;
     __syncthreads();
-    const int n_tiles = (w_pad / 4) * (NOUT_PAD / 4);
+    // grad_w0 tiles of 4 rows x TI columns: half the padded inputs up to 24 (a 64-wide MLP then gives every lane one
+    // tile), else 4
+    constexpr int TI = NOUT_PAD <= 24 ? NOUT_PAD / 2 : 4;
+    constexpr int n_itiles = NOUT_PAD / TI;
+    const int n_tiles = (w_pad / 4) * n_itiles;
     const int n_scalars = 2 * W + 1;
     const bool vector_rows = n_out % 4 == 0;
 
@@ -847,14 +851,16 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
                 #pragma unroll
                 for (int r = 0; r < 4; r++) {
                     const float4* w = reinterpret_cast<const float4*>(s_w0 + (j0 + r) * NOUT_PAD);
+                    // the forward's accumulation order; the padding columns (zero weight, zero feature) add +0, which
+                    // changes at most the sign of a zero and so neither the ReLU mask nor relu(pre)
                     float p = s_b0[j0 + r];
                     #pragma unroll
                     for (int q = 0; q < NOUT_PAD / 4; q++) {
                         const float4 wq = w[q];
-                        if (4 * q < n_out) p = __fmaf_rn(wq.x, f[4 * q], p);
-                        if (4 * q + 1 < n_out) p = __fmaf_rn(wq.y, f[4 * q + 1], p);
-                        if (4 * q + 2 < n_out) p = __fmaf_rn(wq.z, f[4 * q + 2], p);
-                        if (4 * q + 3 < n_out) p = __fmaf_rn(wq.w, f[4 * q + 3], p);
+                        p = __fmaf_rn(wq.x, f[4 * q], p);
+                        p = __fmaf_rn(wq.y, f[4 * q + 1], p);
+                        p = __fmaf_rn(wq.z, f[4 * q + 2], p);
+                        p = __fmaf_rn(wq.w, f[4 * q + 3], p);
                     }
                     pre[r] = p;
                     if (p > 0.0f) {
@@ -894,29 +900,32 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
         __syncwarp();
 
         // phase 2: the chunk's parameter gradient sums in sample order per output (as the reference's
-        // featurize_backward_mlp.cu:110-135): 4 x 4 tiles of grad_w0 (a register-blocked outer product of [pre > 0] g
-        // with the features), then grad_b0, grad_w1 and grad_b1
+        // featurize_backward_mlp.cu:110-135): tiles of 4 x TI of grad_w0 (a register-blocked outer product of
+        // [pre > 0] g with the features), then grad_b0, grad_w1 and grad_b1
         for (int tile = lane; tile < n_tiles; tile += 32) {
-            const int j0 = (tile / (NOUT_PAD / 4)) * 4, i0 = (tile % (NOUT_PAD / 4)) * 4;
-            float sum[4][4] = {};
+            const int j0 = (tile / n_itiles) * 4, i0 = (tile % n_itiles) * TI;
+            float sum[4][TI] = {};
             for (int s = 0; s < n_rows; s++) {
                 const float4 p = *reinterpret_cast<const float4*>(s_pre + s * ps + j0);
-                const float4 fv = *reinterpret_cast<const float4*>(s_feat + s * fs + i0);
+                float fc[TI];
+                #pragma unroll
+                for (int c = 0; c < TI; c += 2) {
+                    const float2 v = *reinterpret_cast<const float2*>(s_feat + s * fs + i0 + c);
+                    fc[c] = v.x;
+                    fc[c + 1] = v.y;
+                }
                 const float gs = s_g[s];
                 const float av[4] = {p.x > 0.0f ? gs : 0.0f, p.y > 0.0f ? gs : 0.0f, p.z > 0.0f ? gs : 0.0f, p.w > 0.0f ? gs : 0.0f};
-                const float fc[4] = {fv.x, fv.y, fv.z, fv.w};
                 #pragma unroll
                 for (int r = 0; r < 4; r++) {
                     #pragma unroll
-                    for (int c = 0; c < 4; c++) {
-                        if (av[r] != 0.0f) sum[r][c] = __fmaf_rn(av[r], fc[c], sum[r][c]);
-                    }
+                    for (int c = 0; c < TI; c++) sum[r][c] = __fmaf_rn(av[r], fc[c], sum[r][c]);
                 }
             }
             #pragma unroll
             for (int r = 0; r < 4; r++) {
                 #pragma unroll
-                for (int c = 0; c < 4; c++) {
+                for (int c = 0; c < TI; c++) {
                     const int j = j0 + r, i = i0 + c;
                     if (j < W && i < n_out && sum[r][c] != 0.0f) atomicAdd(s_acc + j * n_out + i, sum[r][c]);
                 }
