@@ -16,7 +16,7 @@ constexpr int kBlock = 128;
 // minimum resident blocks per SM each kernel's register allocation must allow (__launch_bounds__): the forward is
 // latency bound on its gathers and gains from occupancy; the backwards keep their registers (atomics, MLP)
 #ifndef ZF_MIN_BLOCKS_FORWARD
-#define ZF_MIN_BLOCKS_FORWARD 6
+#define ZF_MIN_BLOCKS_FORWARD 7
 #endif
 #ifndef ZF_MIN_BLOCKS_FORWARD_MLP
 #define ZF_MIN_BLOCKS_FORWARD_MLP 7
@@ -57,6 +57,8 @@ struct ForwardArgs {
     int nerf_inputs_width;
     int encoded_width;
     uint32_t interleave_rays;       // 0: consecutive threads take consecutive samples; else the same interval of this many rays
+    uint32_t level_begin;           // the levels of this launch (a pass; without the MLP a forward may take several)
+    uint32_t level_end;
     bool bf16_pairs;                // features_bf16 allows 4-byte (pair) stores: even width, 4-byte aligned
     bool inputs_vectors;            // nerf_inputs / encoded_directions allow 16-byte copies
 };
@@ -263,12 +265,12 @@ __host__ __device__ constexpr bool cooperative_forward(const int n_features) { r
 template <int F>
 __device__ __forceinline__ void featurize_warp(const GridParams& gp, const Frustum& fr, const bool active, const float* __restrict__ table,
                                                const float* __restrict__ scale_magnitudes, float* row, const int lane, GroupRecords& gr,
-                                               float* s_result) {
+                                               float* s_result, const uint32_t level_begin, const uint32_t level_end) {
     float3 x[kMultisamples];
     float scale[kMultisamples];
     if (active) multisamples(fr, x, scale);
     #pragma unroll 1
-    for (uint32_t level = 0; level < gp.n_levels; level++) {
+    for (uint32_t level = level_begin; level < level_end; level++) {
         const uint32_t size = gp.size[level];
         float scale_feature = 0.0f;
         uint32_t leaders = 0u;
@@ -341,12 +343,13 @@ __device__ __forceinline__ void featurize_warp(const GridParams& gp, const Frust
 // multisamples and preconditioned), row[l (F + 1) + F] the scale feature (featurize_common.cuh:207-227)
 template <int F>
 __device__ __forceinline__ void featurize_to_row(const GridParams& gp, const Frustum& fr, const float* __restrict__ table,
-                                                 const float* __restrict__ scale_magnitudes, float* row) {
+                                                 const float* __restrict__ scale_magnitudes, float* row, const uint32_t level_begin,
+                                                 const uint32_t level_end) {
     float3 x[kMultisamples];
     float scale[kMultisamples];
     multisamples(fr, x, scale);
     #pragma unroll 1
-    for (uint32_t level = 0; level < gp.n_levels; level++) {
+    for (uint32_t level = level_begin; level < level_end; level++) {
         float weighting[kMultisamples];
         float scale_feature = 0.0f;
         #pragma unroll
@@ -387,26 +390,33 @@ struct LaneWalk {
 // warp-cooperative copy of the warp's staged rows to row-major global outputs (rows of samples s_sample[...]); the
 // outputs are written once and read by a later kernel, so they are stored with the evict-first (streaming) policy
 // and do not push the grid tables out of L2
+// (columns [c0, c1) of the rows: a pass writes the columns of its levels; columns at or past n_out are zero padding)
 __device__ __forceinline__ void store_rows_float(const float* s_rows, const int stride, const uint32_t* s_sample, const int n_rows, const int n_out,
-                                                 float* __restrict__ out, const int lane) {
-    LaneWalk w(lane, n_out);
-    for (; w.r < n_rows; w.next()) __stcs(out + static_cast<size_t>(s_sample[w.r]) * n_out + w.c, s_rows[w.r * stride + w.c]);
+                                                 const int c0, const int c1, float* __restrict__ out, const int lane) {
+    for (LaneWalk w(lane, c1 - c0); w.r < n_rows; w.next()) {
+        const int c = c0 + w.c;
+        __stcs(out + static_cast<size_t>(s_sample[w.r]) * n_out + c, s_rows[w.r * stride + c]);
+    }
 }
 
 __device__ __forceinline__ void store_rows_bf16(const float* s_rows, const int stride, const uint32_t* s_sample, const int n_rows, const int n_out,
-                                                uint16_t* __restrict__ out, const int width, const bool pairs, const int lane) {
+                                                const int c0, const int c1, uint16_t* __restrict__ out, const int width, const bool pairs, const int lane) {
+    auto bits = [&](const int r, const int c) -> uint32_t { return c < n_out ? f32_to_bf16_bits(s_rows[r * stride + c]) : 0u; };
     if (pairs) {
-        for (LaneWalk w(lane, width / 2); w.r < n_rows; w.next()) {
-            const int r = w.r, p = w.c, c = 2 * p;
-            const uint32_t lo = c < n_out ? f32_to_bf16_bits(s_rows[r * stride + c]) : 0u;
-            const uint32_t hi = c + 1 < n_out ? f32_to_bf16_bits(s_rows[r * stride + c + 1]) : 0u;
-            __stcs(reinterpret_cast<unsigned int*>(out + static_cast<size_t>(s_sample[r]) * width) + p, lo | (hi << 16));
+        // 4-byte column pairs; a pair half outside [c0, c1) belongs to another pass and is not written
+        const int p0 = c0 / 2;
+        for (LaneWalk w(lane, (c1 + 1) / 2 - p0); w.r < n_rows; w.next()) {
+            const int r = w.r, c = 2 * (p0 + w.c);
+            uint16_t* row = out + static_cast<size_t>(s_sample[r]) * width;
+            if (c >= c0 && c + 1 < c1) __stcs(reinterpret_cast<unsigned int*>(row + c), bits(r, c) | (bits(r, c + 1) << 16));
+            else if (c >= c0) __stcs(row + c, static_cast<unsigned short>(bits(r, c)));
+            else __stcs(row + c + 1, static_cast<unsigned short>(bits(r, c + 1)));
         }
     }
     else {
-        for (LaneWalk w(lane, width); w.r < n_rows; w.next()) {
-            const int r = w.r, c = w.c;
-            __stcs(out + static_cast<size_t>(s_sample[r]) * width + c, c < n_out ? f32_to_bf16_bits(s_rows[r * stride + c]) : static_cast<unsigned short>(0));
+        for (LaneWalk w(lane, c1 - c0); w.r < n_rows; w.next()) {
+            const int c = c0 + w.c;
+            __stcs(out + static_cast<size_t>(s_sample[w.r]) * width + c, static_cast<unsigned short>(bits(w.r, c)));
         }
     }
 }
@@ -474,11 +484,12 @@ __global__ void __launch_bounds__(kBlock, cooperative_forward(F) ? ZF_MIN_BLOCKS
     if constexpr (cooperative_forward(F)) {
         Frustum fr;
         if (active) fr = setup_frustum(a.in, gp.pattern_stream, sample);
-        featurize_warp<F>(gp, fr, active, a.table, a.scale_magnitudes, row, lane, s_groups[warp], s_results + warp * gather_result_floats<F>());
+        featurize_warp<F>(gp, fr, active, a.table, a.scale_magnitudes, row, lane, s_groups[warp], s_results + warp * gather_result_floats<F>(),
+                          a.level_begin, a.level_end);
     }
     else if (active) {
         const Frustum fr = setup_frustum(a.in, gp.pattern_stream, sample);
-        featurize_to_row<F>(gp, fr, a.table, a.scale_magnitudes, row);
+        featurize_to_row<F>(gp, fr, a.table, a.scale_magnitudes, row, a.level_begin, a.level_end);
     }
     if constexpr (NOUT_PAD > 0) {
         if (active) {
@@ -505,9 +516,15 @@ __global__ void __launch_bounds__(kBlock, cooperative_forward(F) ? ZF_MIN_BLOCKS
     __syncwarp();
     const float* warp_rows = s_rows + warp * 32 * stride;
     const uint32_t* warp_samples = s_sample + warp * 32;
-    if (a.features_float != nullptr) store_rows_float(warp_rows, stride, warp_samples, n_rows, n_out, a.features_float, lane);
-    if (a.features_bf16 != nullptr) store_rows_bf16(warp_rows, stride, warp_samples, n_rows, n_out, a.features_bf16, a.features_bf16_width, a.bf16_pairs, lane);
-    if (a.nerf_inputs != nullptr) store_inputs_tail(a, warp_samples, n_rows, lane);
+    // this pass's columns; the last pass also writes the zero padding of the bf16 rows and the NeRF-input tail
+    const bool last_pass = a.level_end == gp.n_levels;
+    const int c0 = static_cast<int>(a.level_begin) * (F + 1), c1 = static_cast<int>(a.level_end) * (F + 1);
+    if (a.features_float != nullptr) store_rows_float(warp_rows, stride, warp_samples, n_rows, n_out, c0, c1, a.features_float, lane);
+    if (a.features_bf16 != nullptr) {
+        store_rows_bf16(warp_rows, stride, warp_samples, n_rows, n_out, c0, last_pass ? static_cast<int>(a.features_bf16_width) : c1, a.features_bf16,
+                        a.features_bf16_width, a.bf16_pairs, lane);
+    }
+    if (a.nerf_inputs != nullptr && last_pass) store_inputs_tail(a, warp_samples, n_rows, lane);
 }
 
 // dynamic shared memory of fz_forward_kernel in floats: sample indices, staged rows, MLP weights, the warps' group
@@ -587,9 +604,9 @@ __device__ __forceinline__ void sum_run(float (&v)[F], const int lane, const int
 // cells are summed over the run first; fp16 contributions are always rounded and added one by one, as the reference
 // does.
 template <int F, bool HALF>
-__device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32_t level, const GroupRecords& gr, const uint32_t n_tasks,
-                                              const int lane, const float* warp_rows, const int stride, float* __restrict__ grad_table,
-                                              uint16_t* __restrict__ grad_table_half, const uint32_t row_base) {
+__device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32_t level, const uint32_t level_begin, const GroupRecords& gr,
+                                              const uint32_t n_tasks, const int lane, const float* warp_rows, const int stride,
+                                              float* __restrict__ grad_table, uint16_t* __restrict__ grad_table_half, const uint32_t row_base) {
     for (uint32_t first = 0; first < n_tasks; first += 32) {
         const bool valid = first + lane < n_tasks;
         float weights[8];
@@ -600,7 +617,7 @@ __device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32
             uint32_t owner;
             task_group(gr, first + lane, weights, c, owner);
             #pragma unroll
-            for (int f = 0; f < F; f++) g[f] = warp_rows[owner * stride + level * (F + 1) + f];
+            for (int f = 0; f < F; f++) g[f] = warp_rows[owner * stride + (level - level_begin) * (F + 1) + f];
             #pragma unroll
             for (uint32_t corner = 0; corner < 8; corner++) {
                 rows[corner] = corner_row(gp, level, c.x + corner_offset(corner, 2), c.y + corner_offset(corner, 1), c.z + corner_offset(corner, 0), weights[corner]);
@@ -649,27 +666,28 @@ __device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32
     }
 }
 
-// scatters the feature gradients of a warp's intervals (row of lane l at warp_rows[l stride], column l (F + 1) + f;
-// scale features carry none) into the grid gradient: levels below n_fp32 into grad_table (fp32), the others into
-// grad_table_half (fp16, rows re-based at the first fp16 level). Inactive lanes and all-zero level gradients add no
-// tasks. Every lane of the warp must call this.
+// scatters the feature gradients of levels [level_begin, level_end) of a warp's intervals (row of lane l at
+// warp_rows[l stride], column (level - level_begin) (F + 1) + f; scale features carry none) into the grid gradient:
+// levels below n_fp32 into grad_table (fp32), the others into grad_table_half (fp16, rows re-based at the first fp16
+// level). Inactive lanes and all-zero level gradients add no tasks. Every lane of the warp must call this.
 template <int F>
 __device__ __forceinline__ void scatter_warp(const GridParams& gp, const Frustum& fr, const bool active, const float* warp_rows, const int stride,
                                              const int lane, const uint32_t n_fp32, float* __restrict__ grad_table,
-                                             uint16_t* __restrict__ grad_table_half, GroupRecords& gr) {
+                                             uint16_t* __restrict__ grad_table_half, GroupRecords& gr, const uint32_t level_begin,
+                                             const uint32_t level_end) {
     float3 x[kMultisamples];
     float scale[kMultisamples];
     if (active) multisamples(fr, x, scale);
     const uint32_t half_base = gp.offset[min(n_fp32, gp.n_levels)];
     const float* g_row = warp_rows + lane * stride;
     #pragma unroll 1
-    for (uint32_t level = 0; level < gp.n_levels; level++) {
+    for (uint32_t level = level_begin; level < level_end; level++) {
         const uint32_t size = gp.size[level];
         uint32_t leaders = 0u;
         if (active) {
             bool any = false;
             #pragma unroll
-            for (int f = 0; f < F; f++) any |= g_row[level * (F + 1) + f] != 0.0f;
+            for (int f = 0; f < F; f++) any |= g_row[(level - level_begin) * (F + 1) + f] != 0.0f;
             if (any) {
                 float weighting[kMultisamples];
                 #pragma unroll
@@ -679,8 +697,8 @@ __device__ __forceinline__ void scatter_warp(const GridParams& gp, const Frustum
         }
         const uint32_t n_tasks = list_tasks_by_lane(leaders, lane, gr);
         __syncwarp();
-        if (level < n_fp32) scatter_tasks<F, false>(gp, level, gr, n_tasks, lane, warp_rows, stride, grad_table, grad_table_half, 0u);
-        else scatter_tasks<F, true>(gp, level, gr, n_tasks, lane, warp_rows, stride, grad_table, grad_table_half, half_base);
+        if (level < n_fp32) scatter_tasks<F, false>(gp, level, level_begin, gr, n_tasks, lane, warp_rows, stride, grad_table, grad_table_half, 0u);
+        else scatter_tasks<F, true>(gp, level, level_begin, gr, n_tasks, lane, warp_rows, stride, grad_table, grad_table_half, half_base);
         __syncwarp();
     }
 }
@@ -698,12 +716,16 @@ struct BackwardArgs {
     uint32_t n_fp32_levels;         // leading levels scattered into grad_table (fp32), the rest into grad_table_half
     float* grad_table;              // fp32 [n_fp32_rows, F]
     uint16_t* grad_table_half;      // fp16 [rows - n_fp32_rows, F]
+    uint32_t level_begin;           // the levels of this launch (a pass)
+    uint32_t level_end;
 };
 
 template <int F>
 __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardArgs a) {
     const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
-    const int stride = staged_stride(n_out);
+    // the columns of this pass's levels
+    const int c0 = static_cast<int>(a.level_begin) * (F + 1), n_cols = static_cast<int>(a.level_end - a.level_begin) * (F + 1);
+    const int stride = staged_stride(n_cols);
     extern __shared__ __align__(16) float smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t warp_first = blockIdx.x * kBlock + warp * 32;
@@ -712,14 +734,14 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_ke
     float* warp_rows = smem + warp * 32 * stride;
     // coalesced load of the warp's gradient rows
     if (a.grad_rows != nullptr) {
-        for (LaneWalk w(lane, n_out); w.r < n_rows; w.next()) {
-            warp_rows[w.r * stride + w.c] = __ldcs(a.grad_rows + static_cast<size_t>(warp_first + w.r) * n_out + w.c);
+        for (LaneWalk w(lane, n_cols); w.r < n_rows; w.next()) {
+            warp_rows[w.r * stride + w.c] = __ldcs(a.grad_rows + static_cast<size_t>(warp_first + w.r) * n_out + c0 + w.c);
         }
     }
     else {
         // bf16 feature gradients, scaled as the reference (feature_scale * grad_scale * g, featurize_backward.cu:24)
-        for (LaneWalk w(lane, n_out); w.r < n_rows; w.next()) {
-            const uint16_t bits = __ldcs(a.grad_features + static_cast<size_t>(warp_first + w.r) * a.grad_stride + w.c);
+        for (LaneWalk w(lane, n_cols); w.r < n_rows; w.next()) {
+            const uint16_t bits = __ldcs(a.grad_features + static_cast<size_t>(warp_first + w.r) * a.grad_stride + c0 + w.c);
             warp_rows[w.r * stride + w.c] = kFeatureScale * a.grad_scale * bf16_bits_to_f32(bits);
         }
     }
@@ -729,8 +751,9 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_ke
     if (active && a.skip_if_zero != nullptr && __ldcs(a.skip_if_zero + sample) == 0.0f) active = false;
     Frustum fr;
     if (active) fr = setup_frustum(a.in, gp.pattern_stream, sample);
-    GroupRecords& gr = reinterpret_cast<GroupRecords*>(smem + kBlock * stride)[warp];
-    scatter_warp<F>(gp, fr, active, warp_rows, stride, lane, a.n_fp32_levels, a.grad_table, a.grad_table_half, gr);
+    // (the records follow the rows of a full-width pass, the allocated size)
+    GroupRecords& gr = reinterpret_cast<GroupRecords*>(smem + kBlock * staged_stride(n_out))[warp];
+    scatter_warp<F>(gp, fr, active, warp_rows, stride, lane, a.n_fp32_levels, a.grad_table, a.grad_table_half, gr, a.level_begin, a.level_end);
 }
 
 // dynamic shared memory of fz_backward_kernel in floats: staged gradient rows, then the warps' scatter records
