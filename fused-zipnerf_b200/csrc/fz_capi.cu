@@ -205,6 +205,10 @@ int zf_featurizer_create(const int level, const int64_t* level_sizes, const int6
             return fail(ZF_ERROR_INVALID_ARGUMENT, "invalid level size or entries");
         }
         const int64_t size = level_sizes[l];
+        // the cooperative forward of 1-2 features per level packs cell coordinates into 16 bits
+        if (zf::cooperative_forward(n_features) && size > static_cast<int64_t>(zf::kMaxPackedSize)) {
+            return fail(ZF_ERROR_UNSUPPORTED, "level sizes above 65534 are not supported with 1-2 features per level");
+        }
         const bool hashed = size * size * size > level_entries[l];
         if (!hashed && size * size * size > static_cast<int64_t>(INT32_MAX)) return fail(ZF_ERROR_INVALID_ARGUMENT, "dense level too large");
         f.offsets[l + 1] = f.offsets[l] + level_entries[l];

@@ -21,9 +21,9 @@ constexpr int kBlock = 128;
 #ifndef ZF_MIN_BLOCKS_FORWARD_MLP
 #define ZF_MIN_BLOCKS_FORWARD_MLP 7
 #endif
-// the cooperative forward (1-2 features per level) is held to 4 blocks per SM by its shared memory
+// the cooperative forward (1-2 features per level) is held to 5 blocks per SM by its shared memory
 #ifndef ZF_MIN_BLOCKS_FORWARD_COOP
-#define ZF_MIN_BLOCKS_FORWARD_COOP 4
+#define ZF_MIN_BLOCKS_FORWARD_COOP 5
 #endif
 #ifndef ZF_MIN_BLOCKS_BACKWARD
 #define ZF_MIN_BLOCKS_BACKWARD 4
@@ -117,19 +117,46 @@ __device__ __forceinline__ void multisamples(const Frustum& fr, float3 (&x)[kMul
 // listed group-index-major (every lane's first group, then every lane's second group, ...), so a lane's groups come in
 // its own order, which the forward's accumulation needs.
 
-// Records of lane l, multisample j at [l kRecordStride + j]: with stride 7 the 16-byte records of 8 consecutive lanes
-// fall into distinct bank quads.
+// Per-warp records of the current level. Lane-major records (the scatter's lane-major task lists, where neighbouring
+// lanes read one lane's groups) sit at [l 7 + j]: with stride 7 the 16-byte records of 8 consecutive lanes fall into
+// distinct bank quads. Multisample-major records (the forward's group-major task lists, where neighbouring lanes read
+// different lanes' records) sit at [j 32 + l], with the cell packed into 16-bit fields (exact for cells in [-1, 65534],
+// i.e. level sizes up to kMaxPackedSize), which keeps the forward's shared memory within 5 blocks per SM.
 constexpr int kRecordStride = 7;
-struct GroupRecords {
+constexpr uint32_t kMaxPackedSize = 65534;
+struct LaneMajorRecords {
     float4 frac[32 * kRecordStride];   // (fx, fy, fz, weighting) of every multisample
     int4 cell[32 * kRecordStride];     // (cx, cy, cz, member mask) of every group leader
     uint8_t task[32 * kMultisamples];  // one byte per group: owner lane | leader multisample << 5
+
+    static __device__ __forceinline__ int at(const uint32_t lane, const uint32_t j) { return static_cast<int>(lane * kRecordStride + j); }
+    __device__ __forceinline__ void put_cell(const int i, const int cx, const int cy, const int cz, const uint32_t members) {
+        cell[i] = make_int4(cx, cy, cz, static_cast<int>(members));
+    }
+    __device__ __forceinline__ int4 get_cell(const int i) const { return cell[i]; }
 };
-static_assert(sizeof(GroupRecords) % 16 == 0, "records stay 16-byte aligned per warp");
+struct PackedRecords {
+    float4 frac[kMultisamples * 32];   // (fx, fy, fz, weighting) of every multisample
+    uint2 cell[kMultisamples * 32];    // (cx + 1 | (cy + 1) << 16, cz + 1 | member mask << 16) of every group leader
+    uint8_t task[32 * kMultisamples];  // one byte per group: owner lane | leader multisample << 5
+
+    static __device__ __forceinline__ int at(const uint32_t lane, const uint32_t j) { return static_cast<int>(j * 32 + lane); }
+    __device__ __forceinline__ void put_cell(const int i, const int cx, const int cy, const int cz, const uint32_t members) {
+        cell[i] = make_uint2((static_cast<uint32_t>(cx + 1) & 0xFFFFu) | (static_cast<uint32_t>(cy + 1) << 16),
+                             (static_cast<uint32_t>(cz + 1) & 0xFFFFu) | (members << 16));
+    }
+    __device__ __forceinline__ int4 get_cell(const int i) const {
+        const uint2 c = cell[i];
+        return make_int4(static_cast<int>(c.x & 0xFFFFu) - 1, static_cast<int>(c.x >> 16) - 1, static_cast<int>(c.y & 0xFFFFu) - 1,
+                         static_cast<int>(c.y >> 16));
+    }
+};
+static_assert(sizeof(LaneMajorRecords) % 16 == 0 && sizeof(PackedRecords) % 16 == 0, "records stay 16-byte aligned per warp");
 
 // writes one interval's multisample records of a level; returns the mask of group leaders (the lowest multisample of
 // every set of multisamples that share a cell)
-__device__ __forceinline__ uint32_t publish_level(const uint32_t size, const float3* x, const float* weighting, GroupRecords& gr, const int lane) {
+template <typename Records>
+__device__ __forceinline__ uint32_t publish_level(const uint32_t size, const float3* x, const float* weighting, Records& gr, const int lane) {
     int cx[kMultisamples], cy[kMultisamples], cz[kMultisamples];
     #pragma unroll
     for (uint32_t j = 0; j < kMultisamples; j++) {
@@ -137,7 +164,7 @@ __device__ __forceinline__ uint32_t publish_level(const uint32_t size, const flo
         level_cell(x[j].x, size, cx[j], fx);
         level_cell(x[j].y, size, cy[j], fy);
         level_cell(x[j].z, size, cz[j], fz);
-        gr.frac[lane * kRecordStride + j] = make_float4(fx, fy, fz, weighting[j]);
+        gr.frac[Records::at(lane, j)] = make_float4(fx, fy, fz, weighting[j]);
     }
     uint32_t members[kMultisamples];
     uint32_t followers = 0u;
@@ -156,14 +183,15 @@ __device__ __forceinline__ uint32_t publish_level(const uint32_t size, const flo
     const uint32_t leaders = ((1u << kMultisamples) - 1u) & ~followers;
     #pragma unroll
     for (uint32_t j = 0; j < kMultisamples; j++) {
-        if ((leaders >> j) & 1u) gr.cell[lane * kRecordStride + j] = make_int4(cx[j], cy[j], cz[j], static_cast<int>(members[j]));
+        if ((leaders >> j) & 1u) gr.put_cell(Records::at(lane, j), cx[j], cy[j], cz[j], members[j]);
     }
     return leaders;
 }
 
 // lists the groups of every lane, group-index-major; slot[i] = the task index of this lane's i-th group (for i below
 // its group count). Returns the warp's task count. Every lane of the warp must call this.
-__device__ __forceinline__ uint32_t list_tasks(const uint32_t leaders, const int lane, GroupRecords& gr, uint32_t (&slot)[kMultisamples]) {
+template <typename Records>
+__device__ __forceinline__ uint32_t list_tasks(const uint32_t leaders, const int lane, Records& gr, uint32_t (&slot)[kMultisamples]) {
     const uint32_t lanes_below = (1u << lane) - 1u;
     const uint32_t n = __popc(leaders);
     uint32_t base = 0u, rest = leaders;
@@ -183,7 +211,8 @@ __device__ __forceinline__ uint32_t list_tasks(const uint32_t leaders, const int
 // lists the groups of every lane, lane-major (a lane's groups next to each other: the lanes of a round then touch the
 // corners of fewer distinct intervals at a time, so fewer of a warp's atomics hit the same row). Returns the warp's
 // task count. Every lane of the warp must call this.
-__device__ __forceinline__ uint32_t list_tasks_by_lane(const uint32_t leaders, const int lane, GroupRecords& gr) {
+template <typename Records>
+__device__ __forceinline__ uint32_t list_tasks_by_lane(const uint32_t leaders, const int lane, Records& gr) {
     const uint32_t lanes_below = (1u << lane) - 1u;
     const uint32_t n = __popc(leaders);
     // this lane's first slot: exclusive prefix of the 0..6 group counts, one ballot per count bit
@@ -202,12 +231,13 @@ __device__ __forceinline__ uint32_t list_tasks_by_lane(const uint32_t leaders, c
 }
 
 // merged corner weights and cell of task t's group
-__device__ __forceinline__ void task_group(const GroupRecords& gr, const uint32_t t, float (&corner_weights)[8], int4& cell, uint32_t& owner) {
+template <typename Records>
+__device__ __forceinline__ void task_group(const Records& gr, const uint32_t t, float (&corner_weights)[8], int4& cell, uint32_t& owner) {
     const uint32_t task = gr.task[t];
     owner = task & 31u;
     const uint32_t leader = task >> 5;
-    const float4 q = gr.frac[owner * kRecordStride + leader];
-    cell = gr.cell[owner * kRecordStride + leader];
+    const float4 q = gr.frac[Records::at(owner, leader)];
+    cell = gr.get_cell(Records::at(owner, leader));
     #pragma unroll
     for (uint32_t corner = 0; corner < 8; corner++) {
         const float wx = corner & 4u ? q.x : 1.0f - q.x;
@@ -219,7 +249,7 @@ __device__ __forceinline__ void task_group(const GroupRecords& gr, const uint32_
     while (others != 0u) {
         const uint32_t m = __ffs(others) - 1u;
         others &= others - 1u;
-        const float4 qm = gr.frac[owner * kRecordStride + m];
+        const float4 qm = gr.frac[Records::at(owner, m)];
         #pragma unroll
         for (uint32_t corner = 0; corner < 8; corner++) {
             const float wx = corner & 4u ? qm.x : 1.0f - qm.x;
@@ -264,7 +294,7 @@ __host__ __device__ constexpr bool cooperative_forward(const int n_features) { r
 // reference's bit for bit. Every lane of the warp must call this; inactive lanes add no tasks and write no row.
 template <int F>
 __device__ __forceinline__ void featurize_warp(const GridParams& gp, const Frustum& fr, const bool active, const float* __restrict__ table,
-                                               const float* __restrict__ scale_magnitudes, float* row, const int lane, GroupRecords& gr,
+                                               const float* __restrict__ scale_magnitudes, float* row, const int lane, PackedRecords& gr,
                                                float* s_result, const uint32_t level_begin, const uint32_t level_end) {
     float3 x[kMultisamples];
     float scale[kMultisamples];
@@ -460,7 +490,7 @@ __global__ void __launch_bounds__(kBlock, cooperative_forward(F) ? ZF_MIN_BLOCKS
     float* s_b0 = s_w0 + a.mlp_width * NOUT_PAD;               // [W]
     float* s_w1 = s_b0 + a.mlp_width;                          // [W]
     // the warps' group records and gather results (cooperative forward; 16-byte aligned)
-    GroupRecords* s_groups = reinterpret_cast<GroupRecords*>(s_w0 + (NOUT_PAD > 0 ? (a.mlp_width * NOUT_PAD + 2 * a.mlp_width + 3) / 4 * 4 : 0));
+    PackedRecords* s_groups = reinterpret_cast<PackedRecords*>(s_w0 + (NOUT_PAD > 0 ? (a.mlp_width * NOUT_PAD + 2 * a.mlp_width + 3) / 4 * 4 : 0));
     float* s_results = reinterpret_cast<float*>(s_groups + kWarps);  // [kWarps, gather_result_floats<F>()]
     if constexpr (NOUT_PAD > 0) {
         for (int i = threadIdx.x; i < a.mlp_width * NOUT_PAD; i += kBlock) {
@@ -531,7 +561,7 @@ __global__ void __launch_bounds__(kBlock, cooperative_forward(F) ? ZF_MIN_BLOCKS
 // records and gather results (the last three 16-byte aligned)
 __host__ __device__ constexpr int forward_smem_floats(const int n_out, const int n_features, const int nout_pad, const int width) {
     return ((kBlock + kBlock * staged_stride(n_out) + 3) / 4) * 4 + (nout_pad > 0 ? (width * nout_pad + 2 * width + 3) / 4 * 4 : 0) +
-           (cooperative_forward(n_features) ? kWarps * (static_cast<int>(sizeof(GroupRecords) / sizeof(float)) + 32 * 8 * (n_features + 1)) : 0);
+           (cooperative_forward(n_features) ? kWarps * (static_cast<int>(sizeof(PackedRecords) / sizeof(float)) + 32 * 8 * (n_features + 1)) : 0);
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
@@ -604,7 +634,7 @@ __device__ __forceinline__ void sum_run(float (&v)[F], const int lane, const int
 // cells are summed over the run first; fp16 contributions are always rounded and added one by one, as the reference
 // does.
 template <int F, bool HALF>
-__device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32_t level, const uint32_t level_begin, const GroupRecords& gr,
+__device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32_t level, const uint32_t level_begin, const LaneMajorRecords& gr,
                                               const uint32_t n_tasks, const int lane, const float* warp_rows, const int stride,
                                               float* __restrict__ grad_table, uint16_t* __restrict__ grad_table_half, const uint32_t row_base) {
     for (uint32_t first = 0; first < n_tasks; first += 32) {
@@ -673,7 +703,7 @@ __device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32
 template <int F>
 __device__ __forceinline__ void scatter_warp(const GridParams& gp, const Frustum& fr, const bool active, const float* warp_rows, const int stride,
                                              const int lane, const uint32_t n_fp32, float* __restrict__ grad_table,
-                                             uint16_t* __restrict__ grad_table_half, GroupRecords& gr, const uint32_t level_begin,
+                                             uint16_t* __restrict__ grad_table_half, LaneMajorRecords& gr, const uint32_t level_begin,
                                              const uint32_t level_end) {
     float3 x[kMultisamples];
     float scale[kMultisamples];
@@ -752,13 +782,13 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_ke
     Frustum fr;
     if (active) fr = setup_frustum(a.in, gp.pattern_stream, sample);
     // (the records follow the rows of a full-width pass, the allocated size)
-    GroupRecords& gr = reinterpret_cast<GroupRecords*>(smem + kBlock * staged_stride(n_out))[warp];
+    LaneMajorRecords& gr = reinterpret_cast<LaneMajorRecords*>(smem + kBlock * staged_stride(n_out))[warp];
     scatter_warp<F>(gp, fr, active, warp_rows, stride, lane, a.n_fp32_levels, a.grad_table, a.grad_table_half, gr, a.level_begin, a.level_end);
 }
 
 // dynamic shared memory of fz_backward_kernel in floats: staged gradient rows, then the warps' scatter records
 __host__ __device__ constexpr int backward_smem_floats(const int n_out) {
-    return kBlock * staged_stride(n_out) + kWarps * static_cast<int>(sizeof(GroupRecords) / sizeof(float));
+    return kBlock * staged_stride(n_out) + kWarps * static_cast<int>(sizeof(LaneMajorRecords) / sizeof(float));
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
