@@ -350,7 +350,9 @@ int zf_featurize_backward(zf_featurizer* f, const zf_backward_args* a, cudaStrea
     k.n_fp32_levels = static_cast<uint32_t>(f->n_fp32_grad_levels);
     k.grad_table = a->grad_table;
     k.grad_table_half = a->grad_table_half;
-    const size_t smem = static_cast<size_t>(zf::backward_smem_floats(f->n_output_features())) * sizeof(float);
+    int max_levels = 0;
+    for (int p = 0; p < f->backward_passes.n; p++) max_levels = std::max(max_levels, f->backward_passes.begin[p + 1] - f->backward_passes.begin[p]);
+    const size_t smem = static_cast<size_t>(zf::backward_smem_floats(max_levels * (f->n_features + 1))) * sizeof(float);
     for (int p = 0; p < f->backward_passes.n; p++) {
         k.level_begin = static_cast<uint32_t>(f->backward_passes.begin[p]);
         k.level_end = static_cast<uint32_t>(f->backward_passes.begin[p + 1]);

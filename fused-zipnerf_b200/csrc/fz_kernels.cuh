@@ -26,7 +26,7 @@ constexpr int kBlock = 128;
 #define ZF_MIN_BLOCKS_FORWARD_COOP 5
 #endif
 #ifndef ZF_MIN_BLOCKS_BACKWARD
-#define ZF_MIN_BLOCKS_BACKWARD 4
+#define ZF_MIN_BLOCKS_BACKWARD 5
 #endif
 #ifndef ZF_MIN_BLOCKS_BACKWARD_MLP
 #define ZF_MIN_BLOCKS_BACKWARD_MLP 2
@@ -761,7 +761,9 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_ke
     const uint32_t warp_first = blockIdx.x * kBlock + warp * 32;
     if (warp_first >= a.in.n_samples) return;
     const int n_rows = min(32, static_cast<int>(a.in.n_samples - warp_first));
-    float* warp_rows = smem + warp * 32 * stride;
+    // the warps' group records, then the gradient rows of this pass's columns
+    LaneMajorRecords& gr = reinterpret_cast<LaneMajorRecords*>(smem)[warp];
+    float* warp_rows = smem + kWarps * static_cast<int>(sizeof(LaneMajorRecords) / sizeof(float)) + warp * 32 * stride;
     // coalesced load of the warp's gradient rows
     if (a.grad_rows != nullptr) {
         for (LaneWalk w(lane, n_cols); w.r < n_rows; w.next()) {
@@ -781,14 +783,13 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_ke
     if (active && a.skip_if_zero != nullptr && __ldcs(a.skip_if_zero + sample) == 0.0f) active = false;
     Frustum fr;
     if (active) fr = setup_frustum(a.in, gp.pattern_stream, sample);
-    // (the records follow the rows of a full-width pass, the allocated size)
-    LaneMajorRecords& gr = reinterpret_cast<LaneMajorRecords*>(smem + kBlock * staged_stride(n_out))[warp];
     scatter_warp<F>(gp, fr, active, warp_rows, stride, lane, a.n_fp32_levels, a.grad_table, a.grad_table_half, gr, a.level_begin, a.level_end);
 }
 
-// dynamic shared memory of fz_backward_kernel in floats: staged gradient rows, then the warps' scatter records
-__host__ __device__ constexpr int backward_smem_floats(const int n_out) {
-    return kBlock * staged_stride(n_out) + kWarps * static_cast<int>(sizeof(LaneMajorRecords) / sizeof(float));
+// dynamic shared memory of fz_backward_kernel in floats for passes of at most n_cols gradient columns: the warps'
+// scatter records, then the staged gradient rows
+__host__ __device__ constexpr int backward_smem_floats(const int n_cols) {
+    return kWarps * static_cast<int>(sizeof(LaneMajorRecords) / sizeof(float)) + kBlock * staged_stride(n_cols);
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
