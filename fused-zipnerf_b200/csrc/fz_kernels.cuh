@@ -819,8 +819,8 @@ struct BackwardMlpArgs {
 // The kernel runs warps independently: each takes 32 samples at a time (a chunk) through
 //   phase 1 (lane = sample): the MLP recomputation in the forward's accumulation order (the same ReLU mask as the
 //           forward), its input gradient (written to grad_rows) and the pre-activations (to shared memory), then
-//   phase 2 (lane = 4-row tiles of grad_w0, and the scalar sums): the chunk's sums in sample order, added to the block's
-//           sums with shared-memory atomics.
+//   phase 2 (lane = 4-row tiles of grad_w0, with the row sums of grad_b0 and grad_w1): the chunk's sums in sample
+//           order, added to the block's sums with shared-memory atomics.
 // Chunk rows in shared memory have a stride of an odd number of 16-byte words, so the lanes' 16-byte stores of phase 1
 // are bank-conflict free, and phase 2 reads one row (broadcast) per sample.
 #ifndef ZF_MLP_WARPS
@@ -875,7 +875,6 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
     constexpr int TI = NOUT_PAD <= 24 ? NOUT_PAD / 2 : 4;
     constexpr int n_itiles = NOUT_PAD / TI;
     const int n_tiles = (w_pad / 4) * n_itiles;
-    const int n_scalars = 2 * W + 1;
     const bool vector_rows = n_out % 4 == 0;
 
     // warp-uniform loop bound
@@ -918,16 +917,15 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
                         p = __fmaf_rn(wq.w, f[4 * q + 3], p);
                     }
                     pre[r] = p;
-                    if (p > 0.0f) {
-                        const float grad_pre = __fmul_rn(g, s_w1[j0 + r]);
-                        #pragma unroll
-                        for (int q = 0; q < NOUT_PAD / 4; q++) {
-                            const float4 wq = w[q];
-                            grad_f[4 * q] = __fmaf_rn(grad_pre, wq.x, grad_f[4 * q]);
-                            grad_f[4 * q + 1] = __fmaf_rn(grad_pre, wq.y, grad_f[4 * q + 1]);
-                            grad_f[4 * q + 2] = __fmaf_rn(grad_pre, wq.z, grad_f[4 * q + 2]);
-                            grad_f[4 * q + 3] = __fmaf_rn(grad_pre, wq.w, grad_f[4 * q + 3]);
-                        }
+                    // branch-free: a zero pre-activation gradient adds +0 (the warp has some positive lane anyway)
+                    const float grad_pre = p > 0.0f ? __fmul_rn(g, s_w1[j0 + r]) : 0.0f;
+                    #pragma unroll
+                    for (int q = 0; q < NOUT_PAD / 4; q++) {
+                        const float4 wq = w[q];
+                        grad_f[4 * q] = __fmaf_rn(grad_pre, wq.x, grad_f[4 * q]);
+                        grad_f[4 * q + 1] = __fmaf_rn(grad_pre, wq.y, grad_f[4 * q + 1]);
+                        grad_f[4 * q + 2] = __fmaf_rn(grad_pre, wq.z, grad_f[4 * q + 2]);
+                        grad_f[4 * q + 3] = __fmaf_rn(grad_pre, wq.w, grad_f[4 * q + 3]);
                     }
                 }
                 *reinterpret_cast<float4*>(s_pre + lane * ps + j0) = make_float4(pre[0], pre[1], pre[2], pre[3]);
@@ -956,10 +954,11 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
 
         // phase 2: the chunk's parameter gradient sums in sample order per output (as the reference's
         // featurize_backward_mlp.cu:110-135): tiles of 4 x TI of grad_w0 (a register-blocked outer product of
-        // [pre > 0] g with the features), then grad_b0, grad_w1 and grad_b1
+        // [pre > 0] g with the features); the tiles of the first columns also sum grad_b0 and grad_w1 of their rows
         for (int tile = lane; tile < n_tiles; tile += 32) {
             const int j0 = (tile / n_itiles) * 4, i0 = (tile % n_itiles) * TI;
             float sum[4][TI] = {};
+            float sum_b0[4] = {}, sum_w1[4] = {};
             for (int s = 0; s < n_rows; s++) {
                 const float4 p = *reinterpret_cast<const float4*>(s_pre + s * ps + j0);
                 float fc[TI];
@@ -971,36 +970,33 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
                 }
                 const float gs = s_g[s];
                 const float av[4] = {p.x > 0.0f ? gs : 0.0f, p.y > 0.0f ? gs : 0.0f, p.z > 0.0f ? gs : 0.0f, p.w > 0.0f ? gs : 0.0f};
+                const float pr[4] = {p.x, p.y, p.z, p.w};
                 #pragma unroll
                 for (int r = 0; r < 4; r++) {
                     #pragma unroll
                     for (int c = 0; c < TI; c++) sum[r][c] = __fmaf_rn(av[r], fc[c], sum[r][c]);
+                    sum_b0[r] = __fadd_rn(sum_b0[r], av[r]);
+                    sum_w1[r] = __fmaf_rn(gs, fmaxf(pr[r], 0.0f), sum_w1[r]);
                 }
             }
             #pragma unroll
             for (int r = 0; r < 4; r++) {
+                const int j = j0 + r;
                 #pragma unroll
                 for (int c = 0; c < TI; c++) {
-                    const int j = j0 + r, i = i0 + c;
+                    const int i = i0 + c;
                     if (j < W && i < n_out && sum[r][c] != 0.0f) atomicAdd(s_acc + j * n_out + i, sum[r][c]);
+                }
+                if (i0 == 0 && j < W) {
+                    if (sum_b0[r] != 0.0f) atomicAdd(s_acc + n_w0 + j, sum_b0[r]);
+                    if (sum_w1[r] != 0.0f) atomicAdd(s_acc + n_w0 + W + j, sum_w1[r]);
                 }
             }
         }
-        for (int q = lane; q < n_scalars; q += 32) {
+        if (lane == 0) {
             float sum = 0.0f;
-            if (q < W) {
-                for (int s = 0; s < n_rows; s++) {
-                    if (s_pre[s * ps + q] > 0.0f) sum = __fadd_rn(sum, s_g[s]);
-                }
-            }
-            else if (q < 2 * W) {
-                const int j = q - W;
-                for (int s = 0; s < n_rows; s++) sum = __fmaf_rn(s_g[s], fmaxf(s_pre[s * ps + j], 0.0f), sum);
-            }
-            else {
-                for (int s = 0; s < n_rows; s++) sum = __fadd_rn(sum, s_g[s]);
-            }
-            if (sum != 0.0f) atomicAdd(s_acc + n_w0 + q, sum);
+            for (int s = 0; s < n_rows; s++) sum = __fadd_rn(sum, s_g[s]);
+            if (sum != 0.0f) atomicAdd(s_acc + n_w0 + 2 * W, sum);
         }
         __syncwarp();
     }
