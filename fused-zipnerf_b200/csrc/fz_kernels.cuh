@@ -831,8 +831,8 @@ constexpr int kMlpBlock = 32 * kMlpWarps;
 __host__ __device__ constexpr int odd_quads(const int n) { return (n / 4) % 2 == 1 ? n : n + 4; }
 __host__ __device__ constexpr int mlp_rows_pad(const int width) { return (width + 3) / 4 * 4; }
 __host__ __device__ constexpr int mlp_block_floats(const int n_out, const int nout_pad, const int width) {
-    return mlp_rows_pad(width) * nout_pad + 2 * mlp_rows_pad(width)  // weights (w0 rows padded to nout_pad), b0, w1
-        + (width * n_out + 2 * width + 1 + 3) / 4 * 4;                // the block's parameter gradient sums
+    return mlp_rows_pad(width) * nout_pad + 2 * mlp_rows_pad(width)                  // weights (w0 rows padded to nout_pad), b0, w1
+        + (n_out * (mlp_rows_pad(width) + 1) + 2 * width + 1 + 3) / 4 * 4;           // the block's parameter gradient sums
 }
 __host__ __device__ constexpr int mlp_warp_floats(const int nout_pad, const int width) {
     return 32 * odd_quads(mlp_rows_pad(width)) + 32 * odd_quads(nout_pad) + 32;  // pre-activations, features, upstream gradient
@@ -853,7 +853,11 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
     float* s_w0 = smem;                        // [w_pad, NOUT_PAD]
     float* s_b0 = s_w0 + w_pad * NOUT_PAD;     // [w_pad]
     float* s_w1 = s_b0 + w_pad;                // [w_pad]
-    float* s_acc = s_w1 + w_pad;               // [n_params] (the reference's output order: w0, b0, w1, b1)
+    // the block's sums: grad_w0 column-major [n_out][w_pad + 1] (the lanes' shared-memory atomics of one tile entry
+    // then fall on distinct banks, but for pairs), then grad_b0 [W], grad_w1 [W], grad_b1
+    float* s_acc = s_w1 + w_pad;
+    const int acc_stride = w_pad + 1;
+    const int acc_b0 = n_out * acc_stride, acc_w1 = acc_b0 + W, acc_b1 = acc_w1 + W, n_acc = acc_b1 + 1;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float* s_pre = smem + mlp_block_floats(n_out, NOUT_PAD, W) + warp * mlp_warp_floats(NOUT_PAD, W);  // [32, ps]
     float* s_feat = s_pre + 32 * ps;           // [32, fs]
@@ -867,7 +871,7 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
         s_b0[i] = i < W ? __ldg(a.b0 + i) : 0.0f;
         s_w1[i] = i < W ? __ldg(a.w1 + i) : 0.0f;
     }
-    for (int i = threadIdx.x; i < n_params; i += kMlpBlock) s_acc[i] = 0.0f;
+    for (int i = threadIdx.x; i < n_acc; i += kMlpBlock) s_acc[i] = 0.0f;
     for (int i = lane; i < 32 * fs; i += 32) s_feat[i] = 0.0f;
     __syncthreads();
     // grad_w0 tiles of 4 rows x TI columns: half the padded inputs up to 24 (a 64-wide MLP then gives every lane one
@@ -883,6 +887,15 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
         // the chunk's features (coalesced) and upstream gradients
         for (LaneWalk w(lane, n_out); w.r < n_rows; w.next()) s_feat[w.r * fs + w.c] = __ldcs(a.features + static_cast<size_t>(base + w.r) * n_out + w.c);
         s_g[lane] = lane < n_rows ? __ldcs(a.grad_raw_density + base + lane) : 0.0f;
+        {
+            // L2 prefetch of this warp's next chunk (its feature rows, 128 bytes per lane, and upstream gradients)
+            const uint32_t next = base + gridDim.x * kMlpBlock;
+            if (next < a.in.n_samples) {
+                const size_t first = static_cast<size_t>(next) * n_out, end = static_cast<size_t>(min(next + 32u, a.in.n_samples)) * n_out;
+                if (first + lane * 32u < end) asm volatile("prefetch.global.L2 [%0];" :: "l"(a.features + first + lane * 32u));
+                if (lane == 0) asm volatile("prefetch.global.L2 [%0];" :: "l"(a.grad_raw_density + next));
+            }
+        }
         __syncwarp();
 
         // phase 1, one sample per lane: MLP recomputation and its input gradient (featurize_backward_mlp.cu:82-105)
@@ -985,18 +998,18 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
                 #pragma unroll
                 for (int c = 0; c < TI; c++) {
                     const int i = i0 + c;
-                    if (j < W && i < n_out && sum[r][c] != 0.0f) atomicAdd(s_acc + j * n_out + i, sum[r][c]);
+                    if (j < W && i < n_out && sum[r][c] != 0.0f) atomicAdd(s_acc + i * acc_stride + j, sum[r][c]);
                 }
                 if (i0 == 0 && j < W) {
-                    if (sum_b0[r] != 0.0f) atomicAdd(s_acc + n_w0 + j, sum_b0[r]);
-                    if (sum_w1[r] != 0.0f) atomicAdd(s_acc + n_w0 + W + j, sum_w1[r]);
+                    if (sum_b0[r] != 0.0f) atomicAdd(s_acc + acc_b0 + j, sum_b0[r]);
+                    if (sum_w1[r] != 0.0f) atomicAdd(s_acc + acc_w1 + j, sum_w1[r]);
                 }
             }
         }
         if (lane == 0) {
             float sum = 0.0f;
             for (int s = 0; s < n_rows; s++) sum = __fadd_rn(sum, s_g[s]);
-            if (sum != 0.0f) atomicAdd(s_acc + n_w0 + 2 * W, sum);
+            if (sum != 0.0f) atomicAdd(s_acc + acc_b1, sum);
         }
         __syncwarp();
     }
@@ -1004,12 +1017,20 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
 
     // one atomic per parameter and block, with w1 applied late (featurize_backward_mlp.cu:139-147)
     for (int q = threadIdx.x; q < n_params; q += kMlpBlock) {
-        const float acc = s_acc[q];
-        if (acc == 0.0f) continue;
-        if (q < n_w0) atomicAdd(a.grad_w0 + q, s_w1[q / n_out] * acc);
-        else if (q < n_w0 + W) atomicAdd(a.grad_b0 + (q - n_w0), s_w1[q - n_w0] * acc);
-        else if (q < n_w0 + 2 * W) atomicAdd(a.grad_w1 + (q - n_w0 - W), acc);
-        else atomicAdd(a.grad_b1, acc);
+        if (q < n_w0) {
+            const int j = q / n_out, i = q - j * n_out;
+            const float acc = s_acc[i * acc_stride + j];
+            if (acc != 0.0f) atomicAdd(a.grad_w0 + q, s_w1[j] * acc);
+        }
+        else if (q < n_w0 + W) {
+            const float acc = s_acc[acc_b0 + q - n_w0];
+            if (acc != 0.0f) atomicAdd(a.grad_b0 + (q - n_w0), s_w1[q - n_w0] * acc);
+        }
+        else if (q < n_w0 + 2 * W) {
+            const float acc = s_acc[acc_w1 + q - n_w0 - W];
+            if (acc != 0.0f) atomicAdd(a.grad_w1 + (q - n_w0 - W), acc);
+        }
+        else if (s_acc[acc_b1] != 0.0f) atomicAdd(a.grad_b1, s_acc[acc_b1]);
     }
 }
 
