@@ -30,8 +30,8 @@ constexpr float kPreconditionScaling = 10.0f;
 constexpr float kFeatureScale = kPreconditionScaling / kMultisamples;
 constexpr unsigned long long kPatternStreamBase = 16ull;
 
-// Grid layout of one featurizer, passed to every kernel by value (kernel parameters live in the constant bank, and
-// with the level loops unrolled every access is a constant-offset read).
+// Grid layout of one featurizer, passed to every kernel by value (kernel parameters live in the constant bank; the
+// per-level fields are read with the loop's level as an index).
 struct GridParams {
     uint32_t n_levels;
     uint32_t n_features;
@@ -170,29 +170,41 @@ __device__ __forceinline__ float level_weighting(const uint32_t size, const floa
     return approx_erf(x);
 }
 
-// table row of a corner (level offset included); weight is zeroed for corners outside a dense level
-__device__ __forceinline__ uint32_t corner_row(const GridParams& gp, const uint32_t level, const int ix, const int iy, const int iz, float& weight) {
-    uint32_t index;
+// table rows of the 8 corners of a cell (corner bits x, y, z = 4, 2, 1; level offset included) from per-axis terms:
+// hashed levels xor the coordinate terms x, y * prime_y, z * prime_z (the +1 terms by adding the prime, modulo 2^32 as
+// the product); dense levels add 1, n, n^2 to the cell's index and zero the weight of corners outside the grid
+// (featurize_common.cuh:154-171: the same integers as the reference's per-corner hash or index).
+__device__ __forceinline__ void cell_rows(const GridParams& gp, const uint32_t level, const int cx, const int cy, const int cz, uint32_t (&rows)[8],
+                                          float (&weights)[8]) {
+    const uint32_t base = gp.offset[level];
     if (gp.hashed_mask & (1u << level)) {
-        const uint32_t h = static_cast<uint32_t>(ix) ^ (static_cast<uint32_t>(iy) * kHashPrimeY) ^ (static_cast<uint32_t>(iz) * kHashPrimeZ);
-        index = (gp.pow2_mask & (1u << level)) ? (h & (gp.entries[level] - 1u)) : (h % gp.entries[level]);
+        const uint32_t hx[2] = {static_cast<uint32_t>(cx), static_cast<uint32_t>(cx) + 1u};
+        const uint32_t y0 = static_cast<uint32_t>(cy) * kHashPrimeY, z0 = static_cast<uint32_t>(cz) * kHashPrimeZ;
+        const uint32_t hy[2] = {y0, y0 + kHashPrimeY}, hz[2] = {z0, z0 + kHashPrimeZ};
+        const uint32_t entries = gp.entries[level];
+        const bool pow2 = (gp.pow2_mask >> level) & 1u;
+        #pragma unroll
+        for (uint32_t corner = 0; corner < 8; corner++) {
+            const uint32_t h = hx[(corner >> 2) & 1u] ^ hy[(corner >> 1) & 1u] ^ hz[corner & 1u];
+            rows[corner] = base + (pow2 ? (h & (entries - 1u)) : (h % entries));
+        }
     }
     else {
         const int n = static_cast<int>(gp.size[level]);
-        const bool valid = ix >= 0 && ix < n && iy >= 0 && iy < n && iz >= 0 && iz < n;
-        if (!valid) weight = 0.0f;
-        index = valid ? static_cast<uint32_t>(ix + n * (iy + n * iz)) : 0u;
+        const bool vx[2] = {cx >= 0 && cx < n, cx + 1 >= 0 && cx + 1 < n};
+        const bool vy[2] = {cy >= 0 && cy < n, cy + 1 >= 0 && cy + 1 < n};
+        const bool vz[2] = {cz >= 0 && cz < n, cz + 1 >= 0 && cz + 1 < n};
+        const int index = cx + n * (cy + n * cz);
+        #pragma unroll
+        for (uint32_t corner = 0; corner < 8; corner++) {
+            const int dx = static_cast<int>((corner >> 2) & 1u), dy = static_cast<int>((corner >> 1) & 1u), dz = static_cast<int>(corner & 1u);
+            const bool valid = vx[dx] && vy[dy] && vz[dz];
+            if (!valid) weights[corner] = 0.0f;
+            rows[corner] = base + (valid ? static_cast<uint32_t>(index + dx + n * (dy + n * dz)) : 0u);
+        }
     }
-    return gp.offset[level] + index;
 }
 
-// Visits the merged corner groups of one level: visitor(row, weight) for the 8 corners of every group, groups in
-// the order of their first multisample, corners in the order (x, y, z) bit 2, 1, 0. Multisamples in the same cell
-// form one group whose corner weights are summed in multisample order, exactly as featurize_common.cuh:137-172 does;
-// here each lane loops over its own groups (lowest unvisited multisample first), so a warp issues the corner work of
-// max(groups) groups instead of all 21 (leader, member) pairs of the fully unrolled merge. The roundings are explicit
-// (a fused multiply-add of the weighting into the sum of (wx wy) wz products), which reproduces the reference
-// kernels' corner weights bit for bit independently of how the surrounding code is scheduled.
 // cell and fractional position of a contracted coordinate on a level of the given size (featurize_common.cuh:127-131)
 __device__ __forceinline__ void level_cell(const float x, const uint32_t size, int& cell, float& frac) {
     const float p = x * size - 0.5f;
@@ -260,13 +272,10 @@ __device__ __forceinline__ void visit_level(const GridParams& gp, const uint32_t
                 }
             }
         }
+        uint32_t rows[8];
+        cell_rows(gp, level, lx, ly, lz, rows, corner_weights);
         #pragma unroll
-        for (uint32_t corner = 0; corner < 8; corner++) {
-            float weight = corner_weights[corner];
-            const uint32_t row = corner_row(gp, level, lx + static_cast<int>((corner >> 2) & 1u), ly + static_cast<int>((corner >> 1) & 1u),
-                                            lz + static_cast<int>(corner & 1u), weight);
-            visitor(row, weight);
-        }
+        for (uint32_t corner = 0; corner < 8; corner++) visitor(rows[corner], corner_weights[corner]);
     }
 }
 

@@ -261,7 +261,6 @@ __device__ __forceinline__ void task_group(const Records& gr, const uint32_t t, 
     }
 }
 
-__device__ __forceinline__ int corner_offset(const uint32_t corner, const int axis_bit) { return static_cast<int>((corner >> axis_bit) & 1u); }
 
 template <int F>
 __device__ __forceinline__ void load_row(const float* __restrict__ table, const uint32_t row, float (&v)[F]) {
@@ -329,10 +328,11 @@ __device__ __forceinline__ void featurize_warp(const GridParams& gp, const Frust
                 uint32_t owner;
                 task_group(gr, t, w, c, owner);
                 float v[8][F];
+                uint32_t rows[8];
+                cell_rows(gp, level, c.x, c.y, c.z, rows, w);
                 #pragma unroll
                 for (uint32_t corner = 0; corner < 8; corner++) {
-                    const uint32_t r = corner_row(gp, level, c.x + corner_offset(corner, 2), c.y + corner_offset(corner, 1), c.z + corner_offset(corner, 0), w[corner]);
-                    if (w[corner] != 0.0f) load_row<F>(table, r, v[corner]);
+                    if (w[corner] != 0.0f) load_row<F>(table, rows[corner], v[corner]);
                     else {
                         #pragma unroll
                         for (int f = 0; f < F; f++) v[corner][f] = 0.0f;
@@ -649,10 +649,7 @@ __device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32
             task_group(gr, first + lane, weights, c, owner);
             #pragma unroll
             for (int f = 0; f < F; f++) g[f] = warp_rows[owner * stride + (level - level_begin) * (F + 1) + f];
-            #pragma unroll
-            for (uint32_t corner = 0; corner < 8; corner++) {
-                rows[corner] = corner_row(gp, level, c.x + corner_offset(corner, 2), c.y + corner_offset(corner, 1), c.z + corner_offset(corner, 0), weights[corner]);
-            }
+            cell_rows(gp, level, c.x, c.y, c.z, rows, weights);
         }
         else {
             #pragma unroll
