@@ -17,7 +17,7 @@ constexpr int kBlock = 128;
 // B200: the kernels are latency bound and gain from resident warps up to where registers spill or shared memory runs
 // out (the cooperative forward and the scatter: shared memory for 5 blocks; the MLP kernel: 2 blocks of 256 threads)
 #ifndef ZF_MIN_BLOCKS_FORWARD
-#define ZF_MIN_BLOCKS_FORWARD 7
+#define ZF_MIN_BLOCKS_FORWARD 6
 #endif
 #ifndef ZF_MIN_BLOCKS_FORWARD_MLP
 #define ZF_MIN_BLOCKS_FORWARD_MLP 7
