@@ -615,7 +615,7 @@ __device__ __forceinline__ void add_row_f16(uint16_t* __restrict__ grad_table, c
 // hot rows (how much that costs otherwise depends on where the table's rows fall among the L2 slices: up to 1.2 ms per
 // proposal backward at 65,536 rays on a B200). A round takes this path when at least kMinRunLanes of its 32 lanes
 // continue a run (swept 4-28: fewer pays the scan on rounds that gain little, more leaves hot rows unmerged).
-constexpr int kMinRunLanes = 24;
+constexpr int kMinRunLanes = 20;
 
 // inclusive sums of v over the lanes from run_start to this lane (a segmented scan)
 template <int F>
