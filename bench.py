@@ -182,6 +182,16 @@ class Step:
                 out.append(po['grad_raw'])
         return out
 
+    def set_inputs(self, buffers: list) -> None:
+        """Points the step at another set of input tensors (the order of input_buffers)."""
+        wl = self.wl
+        it = iter(buffers)
+        wl.origins, wl.directions, wl.radii, wl.encoded_directions, self.nerf_out['grad'] = (next(it) for _ in range(5))
+        for lvl, po in zip(wl.levels, self.prop_out + [None]):
+            lvl.tdist = next(it)
+            if po is not None:
+                po['grad_raw'] = next(it)
+
     def run(self, events=None) -> None:
         """One step; events (list of (start, end) CUDA event pairs per kernel) are recorded if given."""
         wl, seed, e = self.wl, self.wl.pattern_seed, self.empty
@@ -417,30 +427,55 @@ def run_b200(args) -> None:
 
 def measure_e2e(step: Step, args, world: int, exchange, barrier) -> dict:
     """The metric through the public API with host buffers: every step copies its inputs (rays, interval endpoints,
-    encoded directions, upstream gradients) from pinned host memory and reads back the MLP bias gradients."""
-    inputs = step.input_buffers()
-    host = [t.cpu().pin_memory() for t in inputs]
+    encoded directions, upstream gradients) from pinned host memory and reads back the MLP bias gradients. As in a
+    training loop, the inputs are double-buffered: a copy stream brings step i + 1's inputs over PCIe while step i
+    computes; the copies of every timed step (the first two included) lie inside the timed region."""
+    device_sets = [step.input_buffers()]
+    device_sets.append([torch.empty_like(t) for t in device_sets[0]])
+    host = [t.cpu().pin_memory() for t in device_sets[0]]
     result_dev = [g['b1'] for g in step.prop_grads]
     result_host = torch.empty(len(result_dev), pin_memory=True)
     h2d = sum(t.numel() * t.element_size() for t in host)
     d2h = result_host.numel() * result_host.element_size()
+    compute = torch.cuda.current_stream()
+    copies = torch.cuda.Stream()
+    copied = [torch.cuda.Event(), torch.cuda.Event()]
+    released = [torch.cuda.Event(), torch.cuda.Event()]
 
-    def one():
-        for d, h in zip(inputs, host):
-            d.copy_(h, non_blocking=True)
-        step.run()
-        exchange()
-        result_host.copy_(torch.cat(result_dev), non_blocking=True)
+    def copy_inputs(k: int) -> None:
+        # into input set k, once the step that last read it has finished
+        copies.wait_event(released[k])
+        with torch.cuda.stream(copies):
+            for d, h in zip(device_sets[k], host):
+                d.copy_(h, non_blocking=True)
+        copied[k].record(copies)
 
-    for _ in range(max(1, args.warmup)):
-        one()
+    def run(n_steps: int) -> None:
+        for k in range(min(2, n_steps)):
+            copy_inputs(k)
+        for i in range(n_steps):
+            k = i % 2
+            compute.wait_event(copied[k])
+            step.set_inputs(device_sets[k])
+            step.run()
+            exchange()
+            result_host.copy_(torch.cat(result_dev), non_blocking=True)
+            released[k].record(compute)
+            if i + 2 < n_steps:
+                copy_inputs(k)
+
+    for k in range(2):
+        released[k].record(compute)
+    run(max(1, args.warmup))
     barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
-    for _ in range(args.steps):
-        one()
+    for k in range(2):
+        released[k].record(compute)  # the timed copies start after the start event
+    run(args.steps)
     end.record()
     barrier()
+    step.set_inputs(device_sets[0])
     elapsed = start.elapsed_time(end)
     if world > 1:
         import torch.distributed as dist
@@ -448,7 +483,7 @@ def measure_e2e(step: Step, args, world: int, exchange, barrier) -> dict:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed = t.item()
     return {'value': step.samples_per_step * world * args.steps / (elapsed / 1e3) / 1e6, 'unit': UNIT, 'h2d_bytes_per_step': h2d,
-            'd2h_bytes_per_step': d2h, 'api': 'ZipNeRFCudaBackend._C.Featurizer'}
+            'd2h_bytes_per_step': d2h, 'api': 'ZipNeRFCudaBackend._C.Featurizer', 'overlap': 'inputs double-buffered on a copy stream'}
 
 
 _RESULT_FD = None
