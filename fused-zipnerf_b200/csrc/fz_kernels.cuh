@@ -197,8 +197,11 @@ __device__ __forceinline__ uint32_t list_tasks(const uint32_t leaders, const int
     const uint32_t n = __popc(leaders);
     uint32_t base = 0u, rest = leaders;
     #pragma unroll
+    for (uint32_t i = 0; i < kMultisamples; i++) slot[i] = 0u;
+    #pragma unroll
     for (uint32_t i = 0; i < kMultisamples; i++) {
         const uint32_t mask = __ballot_sync(0xFFFFFFFFu, n > i);
+        if (mask == 0u) break;  // no lane has an i-th group (warp-uniform)
         slot[i] = base + __popc(mask & lanes_below);
         if (n > i) {
             gr.task[slot[i]] = static_cast<uint8_t>(lane | ((__ffs(rest) - 1) << 5));
@@ -340,9 +343,14 @@ __device__ __forceinline__ void featurize_warp(const GridParams& gp, const Frust
                 }
                 #pragma unroll
                 for (uint32_t corner = 0; corner < 8; corner++) {
-                    s_result[(corner * (F + 1)) * 32 + lane] = w[corner];
-                    #pragma unroll
-                    for (int f = 0; f < F; f++) s_result[(corner * (F + 1) + 1 + f) * 32 + lane] = v[corner][f];
+                    if constexpr (F == 1) {
+                        reinterpret_cast<float2*>(s_result)[corner * 32 + lane] = make_float2(w[corner], v[corner][0]);
+                    }
+                    else {
+                        s_result[(corner * (F + 1)) * 32 + lane] = w[corner];
+                        #pragma unroll
+                        for (int f = 0; f < F; f++) s_result[(corner * (F + 1) + 1 + f) * 32 + lane] = v[corner][f];
+                    }
                 }
             }
             __syncwarp();
@@ -352,10 +360,16 @@ __device__ __forceinline__ void featurize_warp(const GridParams& gp, const Frust
                 if (i < n_groups && src < 32u) {
                     #pragma unroll
                     for (uint32_t corner = 0; corner < 8; corner++) {
-                        const float weight = s_result[(corner * (F + 1)) * 32 + src];
-                        if (weight != 0.0f) {
-                            #pragma unroll
-                            for (int f = 0; f < F; f++) value[f] = __fmaf_rn(weight, s_result[(corner * (F + 1) + 1 + f) * 32 + src], value[f]);
+                        if constexpr (F == 1) {
+                            const float2 wv = reinterpret_cast<const float2*>(s_result)[corner * 32 + src];
+                            if (wv.x != 0.0f) value[0] = __fmaf_rn(wv.x, wv.y, value[0]);
+                        }
+                        else {
+                            const float weight = s_result[(corner * (F + 1)) * 32 + src];
+                            if (weight != 0.0f) {
+                                #pragma unroll
+                                for (int f = 0; f < F; f++) value[f] = __fmaf_rn(weight, s_result[(corner * (F + 1) + 1 + f) * 32 + src], value[f]);
+                            }
                         }
                     }
                 }
