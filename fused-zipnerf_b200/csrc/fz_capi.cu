@@ -32,13 +32,13 @@ using zf::kMaxLevels;
 // at a time, so that a pass's random row reads (forward) or gradient atomics (backward) hit the L2 instead of DRAM;
 // each pass recomputes its intervals' multisamples. The budgets are the randomly accessed bytes of one pass, measured
 // on the B200 (126 MB L2) for the NeRF grid of 10 levels, 16-8192, 2^21 rows: the forward is fastest with one 32 MB
-// table per pass (7 passes, 8 % faster than one), the backward with three 16 MB fp16 gradient slices per pass (3 % faster);
-// larger forward passes were slower than one.
+// table per pass (7 passes; two tables per pass were 13 % slower), the backward with up to four 16 MB fp16 gradient
+// slices per pass (2 passes; 32, 48 and 100 MB passes were 2-6 % slower).
 #ifndef ZF_FORWARD_PASS_BYTES
 #define ZF_FORWARD_PASS_BYTES (40ll << 20)
 #endif
 #ifndef ZF_BACKWARD_PASS_BYTES
-#define ZF_BACKWARD_PASS_BYTES (48ll << 20)
+#define ZF_BACKWARD_PASS_BYTES (64ll << 20)
 #endif
 constexpr int64_t kForwardPassBytes = ZF_FORWARD_PASS_BYTES;
 constexpr int64_t kBackwardPassBytes = ZF_BACKWARD_PASS_BYTES;
