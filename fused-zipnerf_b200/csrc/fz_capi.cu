@@ -352,7 +352,7 @@ int zf_featurize_backward(zf_featurizer* f, const zf_backward_args* a, cudaStrea
     k.grad_table_half = a->grad_table_half;
     int max_levels = 0;
     for (int p = 0; p < f->backward_passes.n; p++) max_levels = std::max(max_levels, f->backward_passes.begin[p + 1] - f->backward_passes.begin[p]);
-    const size_t smem = static_cast<size_t>(zf::backward_smem_floats(max_levels * (f->n_features + 1))) * sizeof(float);
+    const size_t smem = static_cast<size_t>(zf::backward_smem_floats(f->n_features, max_levels * (f->n_features + 1))) * sizeof(float);
     for (int p = 0; p < f->backward_passes.n; p++) {
         k.level_begin = static_cast<uint32_t>(f->backward_passes.begin[p]);
         k.level_end = static_cast<uint32_t>(f->backward_passes.begin[p + 1]);
@@ -427,7 +427,7 @@ int zf_featurize_backward_mlp(zf_featurizer* f, const zf_backward_mlp_args* a, c
         s.grad_table = a->grad_table;
         s.level_begin = 0;
         s.level_end = static_cast<uint32_t>(f->n_levels);
-        const size_t scatter_smem = static_cast<size_t>(zf::backward_smem_floats(n_out)) * sizeof(float);
+        const size_t scatter_smem = static_cast<size_t>(zf::backward_smem_floats(f->n_features, n_out)) * sizeof(float);
         error = launch(f->kernels->backward, n_blocks(n_samples), scatter_smem, stream, f->params, s);
     }
     if (a->workspace == nullptr) {

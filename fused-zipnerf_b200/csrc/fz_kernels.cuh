@@ -8,6 +8,8 @@
 // staged in shared memory, so outputs leave the SM as coalesced warp-wide stores.
 #pragma once
 
+#include <type_traits>
+
 #include "fz_device.cuh"
 
 namespace zf {
@@ -28,6 +30,9 @@ constexpr int kBlock = 128;
 #endif
 #ifndef ZF_MIN_BLOCKS_BACKWARD
 #define ZF_MIN_BLOCKS_BACKWARD 5
+#endif
+#ifndef ZF_MIN_BLOCKS_BACKWARD_PACKED
+#define ZF_MIN_BLOCKS_BACKWARD_PACKED 6
 #endif
 #ifndef ZF_MIN_BLOCKS_BACKWARD_MLP
 #define ZF_MIN_BLOCKS_BACKWARD_MLP 2
@@ -152,7 +157,28 @@ struct PackedRecords {
                          static_cast<int>(c.y >> 16));
     }
 };
-static_assert(sizeof(LaneMajorRecords) % 16 == 0 && sizeof(PackedRecords) % 16 == 0, "records stay 16-byte aligned per warp");
+// lane-major records with packed cells (the scatter of 1-2 features per level)
+struct LaneMajorPackedRecords {
+    float4 frac[32 * kRecordStride];
+    uint2 cell[32 * kRecordStride];
+    uint8_t task[32 * kMultisamples];
+
+    static __device__ __forceinline__ int at(const uint32_t lane, const uint32_t j) { return static_cast<int>(lane * kRecordStride + j); }
+    __device__ __forceinline__ void put_cell(const int i, const int cx, const int cy, const int cz, const uint32_t members) {
+        cell[i] = make_uint2((static_cast<uint32_t>(cx + 1) & 0xFFFFu) | (static_cast<uint32_t>(cy + 1) << 16),
+                             (static_cast<uint32_t>(cz + 1) & 0xFFFFu) | (members << 16));
+    }
+    __device__ __forceinline__ int4 get_cell(const int i) const {
+        const uint2 c = cell[i];
+        return make_int4(static_cast<int>(c.x & 0xFFFFu) - 1, static_cast<int>(c.x >> 16) - 1, static_cast<int>(c.y & 0xFFFFu) - 1,
+                         static_cast<int>(c.y >> 16));
+    }
+};
+static_assert(sizeof(LaneMajorRecords) % 16 == 0 && sizeof(PackedRecords) % 16 == 0 && sizeof(LaneMajorPackedRecords) % 16 == 0,
+              "records stay 16-byte aligned per warp");
+// the scatter's records: packed cells for 1-2 features per level (level sizes up to kMaxPackedSize, as the forward)
+template <int F>
+using ScatterRecords = std::conditional_t<(F <= 2), LaneMajorPackedRecords, LaneMajorRecords>;
 
 // writes one interval's multisample records of a level; returns the mask of group leaders (the lowest multisample of
 // every set of multisamples that share a cell)
@@ -649,7 +675,7 @@ __device__ __forceinline__ void sum_run(float (&v)[F], const int lane, const int
 // cells are summed over the run first; fp16 contributions are always rounded and added one by one, as the reference
 // does.
 template <int F, bool HALF>
-__device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32_t level, const uint32_t level_begin, const LaneMajorRecords& gr,
+__device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32_t level, const uint32_t level_begin, const ScatterRecords<F>& gr,
                                               const uint32_t n_tasks, const int lane, const float* warp_rows, const int stride,
                                               float* __restrict__ grad_table, uint16_t* __restrict__ grad_table_half, const uint32_t row_base) {
     for (uint32_t first = 0; first < n_tasks; first += 32) {
@@ -715,7 +741,7 @@ __device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32
 template <int F>
 __device__ __forceinline__ void scatter_warp(const GridParams& gp, const Frustum& fr, const bool active, const float* warp_rows, const int stride,
                                              const int lane, const uint32_t n_fp32, float* __restrict__ grad_table,
-                                             uint16_t* __restrict__ grad_table_half, LaneMajorRecords& gr, const uint32_t level_begin,
+                                             uint16_t* __restrict__ grad_table_half, ScatterRecords<F>& gr, const uint32_t level_begin,
                                              const uint32_t level_end) {
     float3 x[kMultisamples];
     float scale[kMultisamples];
@@ -763,7 +789,7 @@ struct BackwardArgs {
 };
 
 template <int F>
-__global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardArgs a) {
+__global__ void __launch_bounds__(kBlock, F <= 2 ? ZF_MIN_BLOCKS_BACKWARD_PACKED : ZF_MIN_BLOCKS_BACKWARD) fz_backward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardArgs a) {
     const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
     // the columns of this pass's levels
     const int c0 = static_cast<int>(a.level_begin) * (F + 1), n_cols = static_cast<int>(a.level_end - a.level_begin) * (F + 1);
@@ -774,8 +800,8 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_ke
     if (warp_first >= a.in.n_samples) return;
     const int n_rows = min(32, static_cast<int>(a.in.n_samples - warp_first));
     // the warps' group records, then the gradient rows of this pass's columns
-    LaneMajorRecords& gr = reinterpret_cast<LaneMajorRecords*>(smem)[warp];
-    float* warp_rows = smem + kWarps * static_cast<int>(sizeof(LaneMajorRecords) / sizeof(float)) + warp * 32 * stride;
+    ScatterRecords<F>& gr = reinterpret_cast<ScatterRecords<F>*>(smem)[warp];
+    float* warp_rows = smem + kWarps * static_cast<int>(sizeof(ScatterRecords<F>) / sizeof(float)) + warp * 32 * stride;
     // coalesced load of the warp's gradient rows
     if (a.grad_rows != nullptr) {
         for (LaneWalk w(lane, n_cols); w.r < n_rows; w.next()) {
@@ -800,8 +826,9 @@ __global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_ke
 
 // dynamic shared memory of fz_backward_kernel in floats for passes of at most n_cols gradient columns: the warps'
 // scatter records, then the staged gradient rows
-__host__ __device__ constexpr int backward_smem_floats(const int n_cols) {
-    return kWarps * static_cast<int>(sizeof(LaneMajorRecords) / sizeof(float)) + kBlock * staged_stride(n_cols);
+__host__ __device__ constexpr int backward_smem_floats(const int n_features, const int n_cols) {
+    return kWarps * static_cast<int>((n_features <= 2 ? sizeof(LaneMajorPackedRecords) : sizeof(LaneMajorRecords)) / sizeof(float)) +
+           kBlock * staged_stride(n_cols);
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
