@@ -167,12 +167,6 @@ class Step:
         self.kernel_names = ['forward_proposal', 'forward_proposal', 'forward_nerf', 'backward_nerf', 'backward_proposal', 'backward_proposal']
         self.launches_per_step = len(self.kernel_names)
 
-    def grad_buffers(self) -> list:
-        out = [self.nerf_grads['g32'], self.nerf_grads['g16']]
-        for grads in self.prop_grads:
-            out += [grads['table'], grads['w0'], grads['b0'], grads['w1'], grads['b1']]
-        return out
-
     def input_buffers(self) -> list:
         wl = self.wl
         out = [wl.origins, wl.directions, wl.radii, wl.encoded_directions, self.nerf_out['grad']]
@@ -192,8 +186,10 @@ class Step:
             if po is not None:
                 po['grad_raw'] = next(it)
 
-    def run(self, events=None) -> None:
-        """One step; events (list of (start, end) CUDA event pairs per kernel) are recorded if given."""
+    def run(self, events=None, after_backward=None) -> None:
+        """One step; events (list of (start, end) CUDA event pairs per kernel) are recorded if given;
+        after_backward(buffers) is called with each level's gradient buffers once its backward is enqueued (the
+        data-parallel exchange of those buffers starts there)."""
         wl, seed, e = self.wl, self.wl.pattern_seed, self.empty
         rays = (wl.origins, wl.directions, wl.radii)
         k = 0
@@ -217,11 +213,15 @@ class Step:
         fn.backward(*rays, nerf.tdist, seed, self.nerf_out['grad'][:, :fn.n_output_features], self.nerf_grads['g32'], self.nerf_grads['g16'])
         mark(k, 1)
         k += 1
+        if after_backward is not None:
+            after_backward([self.nerf_grads['g32'], self.nerf_grads['g16']])
         for lvl, f, po, pg in zip(self.props, self.featurizers, self.prop_out, self.prop_grads):
             mark(k, 0)
             f.backward_mlp(*rays, lvl.tdist, seed, po['features'], po['grad_raw'], *lvl.mlp[:3], pg['table'], pg['w0'], pg['b0'], pg['w1'], pg['b1'])
             mark(k, 1)
             k += 1
+            if after_backward is not None:
+                after_backward([pg['table'], pg['w0'], pg['b0'], pg['w1'], pg['b1']])
 
     def kernel_bytes(self) -> list:
         out = []
@@ -345,12 +345,21 @@ def run_b200(args) -> None:
         import datetime
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120), device_id=device)
     step = Step(workloads.config2(n_rays=args.rays, seed=1 + rank), device, rank)
-    grads = step.grad_buffers()
+    comm = torch.cuda.Stream() if world > 1 else None
 
-    def exchange():
+    def start_exchange(buffers):
+        # a level's gradients are final after its backward: average them on a communication stream while the next
+        # levels' backwards run (every rank issues the same collectives in the same order)
         if world > 1:
             from zipnerf_b200 import sharding
-            sharding.allreduce_gradients(grads)
+            comm.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(comm):
+                sharding.allreduce_gradients(buffers)
+
+    def exchange():
+        # the step ends when every level's exchange has finished
+        if world > 1:
+            torch.cuda.current_stream().wait_stream(comm)
 
     def barrier():
         if world > 1:
@@ -358,7 +367,7 @@ def run_b200(args) -> None:
         torch.cuda.synchronize()
 
     for _ in range(args.warmup):
-        step.run()
+        step.run(after_backward=start_exchange)
         exchange()
     barrier()
     n_k = step.launches_per_step
@@ -370,7 +379,7 @@ def run_b200(args) -> None:
         barrier()
         start.record()
         for i in range(args.steps):
-            step.run(events[i])
+            step.run(events[i], after_backward=start_exchange)
             exchange()
         end.record()
         barrier()
@@ -413,7 +422,7 @@ def run_b200(args) -> None:
                          'l2': 'inputs larger than L2 (step working set ~1.8 GB > 126 MB)'},
               'roofline': roofline, 'kernels': kernels, 'gpu_launches': step.launches_per_step * args.steps, 'clocks': clocks.summary()}
     if not args.skip_e2e:
-        result['e2e'] = measure_e2e(step, args, world, exchange, barrier)
+        result['e2e'] = measure_e2e(step, args, world, start_exchange, exchange, barrier)
     if rank == 0 and not args.skip_cpu_baseline and world == 1:
         from oracle.zf_oracle import build, n_threads_default
         build()
@@ -425,7 +434,7 @@ def run_b200(args) -> None:
         emit(result)
 
 
-def measure_e2e(step: Step, args, world: int, exchange, barrier) -> dict:
+def measure_e2e(step: Step, args, world: int, start_exchange, exchange, barrier) -> dict:
     """The metric through the public API with host buffers: every step copies its inputs (rays, interval endpoints,
     encoded directions, upstream gradients) from pinned host memory and reads back the MLP bias gradients. As in a
     training loop, the inputs are double-buffered: a copy stream brings step i + 1's inputs over PCIe while step i
@@ -457,7 +466,7 @@ def measure_e2e(step: Step, args, world: int, exchange, barrier) -> dict:
             k = i % 2
             compute.wait_event(copied[k])
             step.set_inputs(device_sets[k])
-            step.run()
+            step.run(after_backward=start_exchange)
             exchange()
             result_host.copy_(torch.cat(result_dev), non_blocking=True)
             released[k].record(compute)
