@@ -238,7 +238,7 @@ int zf_featurizer_create(const int level, const int64_t* level_sizes, const int6
     if (mlp_width > 0) {
         f.mlp_kernels = mlp_kernel_set(n_features, zf::mlp_pad(f.n_output_features()));
         if (f.mlp_kernels == nullptr) return fail(ZF_ERROR_UNSUPPORTED, "this mlp input width is not compiled into this build");
-        const size_t fwd = static_cast<size_t>(zf::forward_smem_floats(f.n_output_features(), f.n_features, zf::mlp_pad(f.n_output_features()), mlp_width)) * sizeof(float);
+        const size_t fwd = static_cast<size_t>(zf::forward_smem_floats(f.n_output_features(), f.n_features)) * sizeof(float);
         const size_t bwd = static_cast<size_t>(zf::backward_mlp_smem_floats(f.n_output_features(), zf::mlp_pad(f.n_output_features()), mlp_width)) * sizeof(float);
         if (std::max(fwd, bwd) > 227 * 1024) return fail(ZF_ERROR_UNSUPPORTED, "mlp_width too large for the kernels' shared memory");
     }
@@ -315,9 +315,9 @@ int zf_featurize_forward(zf_featurizer* f, const zf_forward_args* a, cudaStream_
     k.nerf_inputs_width = a->nerf_inputs != nullptr ? static_cast<int>(a->nerf_inputs_width) : 0;
     k.encoded_width = a->nerf_inputs != nullptr ? static_cast<int>(a->encoded_width) : 0;
     k.inputs_vectors = a->nerf_inputs != nullptr && a->nerf_inputs_width % 8 == 0 && a->encoded_width % 8 == 0 && aligned(a->nerf_inputs, 16) && aligned(a->encoded_directions, 16);
+    k.w0_vectors = mlp && n_out % 4 == 0 && aligned(a->w0, 16);
     k.interleave_rays = a->interleave ? 32u : 0u;
-    const int pad = mlp ? zf::mlp_pad(n_out) : 0;
-    const size_t smem = static_cast<size_t>(zf::forward_smem_floats(n_out, f->n_features, pad, k.mlp_width)) * sizeof(float);
+    const size_t smem = static_cast<size_t>(zf::forward_smem_floats(n_out, f->n_features)) * sizeof(float);
     // the fused MLP needs every level of an interval in one launch; without it, one launch per level pass
     const int n_passes = mlp ? 1 : f->forward_passes.n;
     for (int p = 0; p < n_passes; p++) {

@@ -24,9 +24,9 @@ constexpr int kBlock = 128;
 #ifndef ZF_MIN_BLOCKS_FORWARD_MLP
 #define ZF_MIN_BLOCKS_FORWARD_MLP 7
 #endif
-// the cooperative forward (1-2 features per level) is held to 5 blocks per SM by its shared memory
+// the cooperative forward (1-2 features per level): its shared memory allows 6 blocks per SM
 #ifndef ZF_MIN_BLOCKS_FORWARD_COOP
-#define ZF_MIN_BLOCKS_FORWARD_COOP 5
+#define ZF_MIN_BLOCKS_FORWARD_COOP 6
 #endif
 #ifndef ZF_MIN_BLOCKS_BACKWARD
 #define ZF_MIN_BLOCKS_BACKWARD 5
@@ -41,6 +41,9 @@ constexpr int kWarps = kBlock / 32;
 
 // odd row stride (in floats) of per-thread rows in shared memory: lanes writing the same column hit distinct banks
 __host__ __device__ constexpr int staged_stride(const int n_out) { return n_out | 1; }
+// n (a multiple of 4) or n + 4: an odd number of 16-byte words, so the 16-byte accesses of 8 consecutive lanes to rows
+// of this stride fall into distinct bank quads
+__host__ __device__ constexpr int odd_quads(const int n) { return (n / 4) % 2 == 1 ? n : n + 4; }
 
 // ---------------------------------------------------------------------------------------------------------------------
 // forward
@@ -67,6 +70,7 @@ struct ForwardArgs {
     uint32_t level_end;
     bool bf16_pairs;                // features_bf16 allows 4-byte (pair) stores: even width, 4-byte aligned
     bool inputs_vectors;            // nerf_inputs / encoded_directions allow 16-byte copies
+    bool w0_vectors;                // w0 rows allow 16-byte loads: 16-byte aligned, n_out a multiple of 4
 };
 
 template <int F>
@@ -518,75 +522,101 @@ __device__ __forceinline__ void store_inputs_tail(const Args& a, const uint32_t*
     }
 }
 
+// staged-row stride of the forward: the cooperative forward's rows are read as 16-byte words by its MLP (a multiple of
+// 4 with an odd word count); the per-lane forward writes its rows column by column (odd)
+__host__ __device__ constexpr int forward_row_stride(const int n_features, const int n_out) {
+    return cooperative_forward(n_features) ? odd_quads((n_out + 3) / 4 * 4) : staged_stride(n_out);
+}
+
 // Forward. NOUT_PAD == 0: no MLP; otherwise the fused density MLP n_out -> W (ReLU) -> 1 runs for raw_density, with
-// the features in registers (NOUT_PAD >= n_out) and the reference's accumulation order (featurize_forward.cu:65-73).
+// the features in registers (NOUT_PAD >= n_out) and the reference's accumulation order (featurize_forward.cu:65-73);
+// its weights are read through the L1 (every lane reads the same row).
 template <int F, int NOUT_PAD>
 __global__ void __launch_bounds__(kBlock, cooperative_forward(F) ? ZF_MIN_BLOCKS_FORWARD_COOP : (NOUT_PAD > 0 ? ZF_MIN_BLOCKS_FORWARD_MLP : ZF_MIN_BLOCKS_FORWARD)) fz_forward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ ForwardArgs a) {
     const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
-    const int stride = staged_stride(n_out);
+    const int stride = forward_row_stride(F, n_out);
     extern __shared__ __align__(16) float smem[];
-    uint32_t* s_sample = reinterpret_cast<uint32_t*>(smem);   // [kBlock]
-    float* s_rows = smem + kBlock;                             // [kBlock, stride]
-    float* s_w0 = smem + (kBlock + kBlock * stride + 3) / 4 * 4;  // [W, NOUT_PAD] (MLP only; 16-byte aligned)
-    float* s_b0 = s_w0 + a.mlp_width * NOUT_PAD;               // [W]
-    float* s_w1 = s_b0 + a.mlp_width;                          // [W]
-    // the warps' group records and gather results (cooperative forward; 16-byte aligned)
-    PackedRecords* s_groups = reinterpret_cast<PackedRecords*>(s_w0 + (NOUT_PAD > 0 ? (a.mlp_width * NOUT_PAD + 2 * a.mlp_width + 3) / 4 * 4 : 0));
+    float* s_rows = smem;                                      // [kBlock, stride]
+    // the cooperative forward: the warps' group records and gather results (16-byte aligned); the per-lane forward: the
+    // threads' sample indices
+    PackedRecords* s_groups = reinterpret_cast<PackedRecords*>(smem + kBlock * stride);
     float* s_results = reinterpret_cast<float*>(s_groups + kWarps);  // [kWarps, gather_result_floats<F>()]
-    if constexpr (NOUT_PAD > 0) {
-        for (int i = threadIdx.x; i < a.mlp_width * NOUT_PAD; i += kBlock) {
-            const int j = i / NOUT_PAD, c = i - j * NOUT_PAD;
-            s_w0[i] = c < n_out ? __ldg(a.w0 + j * n_out + c) : 0.0f;
-        }
-        for (int i = threadIdx.x; i < a.mlp_width; i += kBlock) {
-            s_b0[i] = __ldg(a.b0 + i);
-            s_w1[i] = __ldg(a.w1 + i);
-        }
-        __syncthreads();
-    }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // the warp's sample indices for the output stores (the cooperative forward keeps them in its gather results, which
+    // are free once the levels are done)
+    uint32_t* warp_samples = cooperative_forward(F) ? reinterpret_cast<uint32_t*>(s_results + warp * gather_result_floats<F>())
+                                                    : reinterpret_cast<uint32_t*>(smem + kBlock * stride) + warp * 32;
     const uint32_t warp_first = blockIdx.x * kBlock + warp * 32;
     if (warp_first >= a.in.n_samples) return;
     const int n_rows = min(32, static_cast<int>(a.in.n_samples - warp_first));
     const bool active = lane < n_rows;
     const uint32_t sample = active ? thread_sample(warp_first + lane, a.in, a.interleave_rays) : 0u;
     float* row = s_rows + threadIdx.x * stride;
-    s_sample[threadIdx.x] = sample;
     if constexpr (cooperative_forward(F)) {
         Frustum fr;
         if (active) fr = setup_frustum(a.in, gp.pattern_stream, sample);
         featurize_warp<F>(gp, fr, active, a.table, a.scale_magnitudes, row, lane, s_groups[warp], s_results + warp * gather_result_floats<F>(),
                           a.level_begin, a.level_end);
+        __syncwarp();
+        warp_samples[lane] = sample;
     }
-    else if (active) {
-        const Frustum fr = setup_frustum(a.in, gp.pattern_stream, sample);
-        featurize_to_row<F>(gp, fr, a.table, a.scale_magnitudes, row, a.level_begin, a.level_end);
+    else {
+        warp_samples[lane] = sample;
+        if (active) {
+            const Frustum fr = setup_frustum(a.in, gp.pattern_stream, sample);
+            featurize_to_row<F>(gp, fr, a.table, a.scale_magnitudes, row, a.level_begin, a.level_end);
+        }
     }
     if constexpr (NOUT_PAD > 0) {
         if (active) {
             float f[NOUT_PAD];
-            #pragma unroll
-            for (int i = 0; i < NOUT_PAD; i++) f[i] = i < n_out ? row[i] : 0.0f;
-            float raw = __ldg(a.b1);
-            for (int j = 0; j < a.mlp_width; j++) {
-                float pre = s_b0[j];
-                const float4* w = reinterpret_cast<const float4*>(s_w0 + j * NOUT_PAD);
+            if constexpr (cooperative_forward(F)) {
                 #pragma unroll
                 for (int q = 0; q < NOUT_PAD / 4; q++) {
-                    const float4 wq = w[q];
-                    if (4 * q < n_out) pre = __fmaf_rn(wq.x, f[4 * q], pre);
-                    if (4 * q + 1 < n_out) pre = __fmaf_rn(wq.y, f[4 * q + 1], pre);
-                    if (4 * q + 2 < n_out) pre = __fmaf_rn(wq.z, f[4 * q + 2], pre);
-                    if (4 * q + 3 < n_out) pre = __fmaf_rn(wq.w, f[4 * q + 3], pre);
+                    const float4 v = reinterpret_cast<const float4*>(row)[q];
+                    f[4 * q] = v.x;
+                    f[4 * q + 1] = v.y;
+                    f[4 * q + 2] = v.z;
+                    f[4 * q + 3] = v.w;
                 }
-                raw = __fmaf_rn(s_w1[j], fmaxf(pre, 0.0f), raw);
+                #pragma unroll
+                for (int i = 0; i < NOUT_PAD; i++) f[i] = i < n_out ? f[i] : 0.0f;
+            }
+            else {
+                #pragma unroll
+                for (int i = 0; i < NOUT_PAD; i++) f[i] = i < n_out ? row[i] : 0.0f;
+            }
+            float raw = __ldg(a.b1);
+            if (a.w0_vectors) {
+                for (int j = 0; j < a.mlp_width; j++) {
+                    float pre = __ldg(a.b0 + j);
+                    const float4* w = reinterpret_cast<const float4*>(a.w0 + j * n_out);
+                    #pragma unroll
+                    for (int q = 0; q < NOUT_PAD / 4; q++) {
+                        const float4 wq = __ldg(w + q);
+                        pre = __fmaf_rn(wq.x, f[4 * q], pre);
+                        pre = __fmaf_rn(wq.y, f[4 * q + 1], pre);
+                        pre = __fmaf_rn(wq.z, f[4 * q + 2], pre);
+                        pre = __fmaf_rn(wq.w, f[4 * q + 3], pre);
+                    }
+                    raw = __fmaf_rn(__ldg(a.w1 + j), fmaxf(pre, 0.0f), raw);
+                }
+            }
+            else {
+                for (int j = 0; j < a.mlp_width; j++) {
+                    float pre = __ldg(a.b0 + j);
+                    #pragma unroll
+                    for (int i = 0; i < NOUT_PAD; i++) {
+                        if (i < n_out) pre = __fmaf_rn(__ldg(a.w0 + j * n_out + i), f[i], pre);
+                    }
+                    raw = __fmaf_rn(__ldg(a.w1 + j), fmaxf(pre, 0.0f), raw);
+                }
             }
             __stcs(a.raw_density + sample, raw);
         }
     }
     __syncwarp();
     const float* warp_rows = s_rows + warp * 32 * stride;
-    const uint32_t* warp_samples = s_sample + warp * 32;
     // this pass's columns; the last pass also writes the zero padding of the bf16 rows and the NeRF-input tail
     const bool last_pass = a.level_end == gp.n_levels;
     const int c0 = static_cast<int>(a.level_begin) * (F + 1), c1 = static_cast<int>(a.level_end) * (F + 1);
@@ -598,11 +628,11 @@ __global__ void __launch_bounds__(kBlock, cooperative_forward(F) ? ZF_MIN_BLOCKS
     if (a.nerf_inputs != nullptr && last_pass) store_inputs_tail(a, warp_samples, n_rows, lane);
 }
 
-// dynamic shared memory of fz_forward_kernel in floats: sample indices, staged rows, MLP weights, the warps' group
-// records and gather results (the last three 16-byte aligned)
-__host__ __device__ constexpr int forward_smem_floats(const int n_out, const int n_features, const int nout_pad, const int width) {
-    return ((kBlock + kBlock * staged_stride(n_out) + 3) / 4) * 4 + (nout_pad > 0 ? (width * nout_pad + 2 * width + 3) / 4 * 4 : 0) +
-           (cooperative_forward(n_features) ? kWarps * (static_cast<int>(sizeof(PackedRecords) / sizeof(float)) + 32 * 8 * (n_features + 1)) : 0);
+// dynamic shared memory of fz_forward_kernel in floats: staged rows, then the cooperative forward's group records and
+// gather results (16-byte aligned), or the per-lane forward's sample indices
+__host__ __device__ constexpr int forward_smem_floats(const int n_out, const int n_features) {
+    return kBlock * forward_row_stride(n_features, n_out) +
+           (cooperative_forward(n_features) ? kWarps * (static_cast<int>(sizeof(PackedRecords) / sizeof(float)) + 32 * 8 * (n_features + 1)) : kBlock);
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
@@ -866,7 +896,6 @@ struct BackwardMlpArgs {
 #endif
 constexpr int kMlpWarps = ZF_MLP_WARPS;
 constexpr int kMlpBlock = 32 * kMlpWarps;
-__host__ __device__ constexpr int odd_quads(const int n) { return (n / 4) % 2 == 1 ? n : n + 4; }
 __host__ __device__ constexpr int mlp_rows_pad(const int width) { return (width + 3) / 4 * 4; }
 __host__ __device__ constexpr int mlp_block_floats(const int n_out, const int nout_pad, const int width) {
     return mlp_rows_pad(width) * nout_pad + 2 * mlp_rows_pad(width)                  // weights (w0 rows padded to nout_pad), b0, w1
