@@ -180,6 +180,37 @@ def test_backward_mlp_matches_oracle(capi, cuda_device, oracle, name):
         np.testing.assert_allclose(a, b, rtol=0, atol=1e-4 * max(float(np.abs(b).max()), 1e-12), err_msg=key)
 
 
+@pytest.mark.parametrize('n_levels', [7, 8])
+def test_mlp_weight_loads_are_bit_identical(capi, cuda_device, oracle, n_levels):
+    """The fused MLP reads its weight rows as 16-byte words when w0 is 16-byte aligned and the MLP input width a multiple
+    of 4, element by element otherwise (7 levels: 14 inputs; or a w0 4 bytes off alignment). Raw density and features
+    are bit-identical either way, and match the oracle and a float64 MLP."""
+    from oracle.zf_oracle import GridSpec
+    case = td.proposals_case(n_levels, 33, 5, 37)
+    rays, table, mags = case_tensors(case, cuda_device)
+    mlp = [cuda(m, cuda_device) for m in case['mlp']]
+    storage = torch.empty(mlp[0].numel() + 1, device=cuda_device)
+    w0_offset = storage[1:].view_as(mlp[0])
+    w0_offset.copy_(mlp[0])
+    f = capi.CFeaturizer(case['level'], case['sizes'], case['entries'], 1, 64)
+    n_rays, n = case['tdist'].shape[0], case['tdist'].shape[1] - 1
+    outs = []
+    for w0 in (mlp[0], w0_offset):
+        raw = torch.full((n_rays, n), float('nan'), device=cuda_device)
+        feats = torch.full((n_rays * n, f.n_output_features), float('nan'), device=cuda_device)
+        f.forward(*rays, case['seed'], False, table, mags, w0, *mlp[1:], raw_density=raw, features_float=feats)
+        torch.cuda.synchronize()
+        outs.append((raw.cpu().numpy(), feats.cpu().numpy()))
+    np.testing.assert_array_equal(outs[0][0], outs[1][0])
+    np.testing.assert_array_equal(outs[0][1], outs[1][1])
+    grid = GridSpec(case['level'], case['sizes'], case['entries'], 1, 64)
+    gold = oracle.forward(grid, *(case[k] for k in ('origins', 'directions', 'radii', 'tdist')), case['seed'], td.table(case),
+                          td.scale_magnitudes(case), features_float=True)
+    parity.assert_features_close(outs[0][1], gold['features_float'], case['sizes'], 1, float(np.abs(td.table(case)).max()))
+    raw_ref = mlp_reference(outs[0][1], case['mlp'])
+    np.testing.assert_allclose(outs[0][0].reshape(-1), raw_ref, rtol=0, atol=1e-5 * max(float(np.abs(raw_ref).max()), 1e-6))
+
+
 @pytest.mark.parametrize('name', ['grids_F1_R65_I3_S-1', 'grids_F3_R33_I5_S37', 'proposals_L8_R129_I32_S37', 'config2nerf_R24'])
 def test_interleave_and_layouts_are_bit_identical(capi, cuda_device, name):
     """The thread mapping (interleave) and the output layout (aligned or not) never change a result bit."""
