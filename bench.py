@@ -165,7 +165,12 @@ class Step:
                            'g16': torch.zeros((sum(self.nerf.entries) - split) * F, device=device, dtype=torch.float16)}
         self.samples_per_step = wl.n_intervals_total * N_MULTISAMPLES
         self.kernel_names = ['forward_proposal', 'forward_proposal', 'forward_nerf', 'backward_nerf', 'backward_proposal', 'backward_proposal']
-        self.launches_per_step = len(self.kernel_names)
+        self.calls_per_step = len(self.kernel_names)
+        # kernel launches of the step's calls (level passes of the NeRF grid, two kernels per proposal backward)
+        from zipnerf_b200 import capi
+        counts = [capi.CFeaturizer(l.level, l.sizes, l.entries, l.n_features, l.mlp_width) for l in wl.levels]
+        self.kernel_launches_per_step = (sum(c.launches('forward_mlp') + c.launches('backward_mlp') for c in counts[:-1]) +
+                                         counts[-1].launches('forward') + counts[-1].launches('backward'))
 
     def input_buffers(self) -> list:
         wl = self.wl
@@ -313,6 +318,15 @@ def _time_cpu_baseline(prepared, n_rays: int, threads: int, repeats: int) -> dic
                       f'{repeats} pass(es): {samples} samples in {elapsed:.2f} s'}
 
 
+def bench_config(args, world: int, samples_per_step: int) -> dict:
+    """The workload of both arms' lines."""
+    return {'workload': 'config2: 65536 rays x (64 + 64 + 32) intervals x 6 multisamples, fwd+bwd of 2 proposal levels (10x1 features, '
+                        'table 2^21, 16->512, fused MLP 64) and the NeRF level (10x4 features, table 2^21, 16->8192)',
+            'rays_per_gpu': args.rays, 'samples_per_step_per_gpu': samples_per_step,
+            'parallelism': f'dp{world} (rays sharded, gradients all-reduced)' if world > 1 else 'single GPU',
+            'l2': 'inputs larger than L2 (step working set ~1.8 GB > 126 MB)'}
+
+
 def run_reference_arm(args) -> None:
     world, rank, _ = init_distributed(args.gpus)
     if rank != 0:
@@ -329,8 +343,8 @@ def run_reference_arm(args) -> None:
     base = values[0]
     emit({'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': args.gpus, 'steps': args.steps,
                       'warmup': args.warmup, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
-                      'data': 'synthetic', 'config': {'workload': 'config2 (paper-shape training-step featurization), bounded ray sample on the host cores',
-                                                      'rays': args.reference_rays},
+                      'data': 'synthetic (seeded config 2 shapes; Mip-NeRF 360 unavailable)',
+                      'config': bench_config(args, 1, args.rays * (64 + 64 + 32) * N_MULTISAMPLES),
                       'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': base['cores'], 'kind': base['kind'], 'sample': base['sample']},
                       'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}})
 
@@ -370,7 +384,7 @@ def run_b200(args) -> None:
         step.run(after_backward=start_exchange)
         exchange()
     barrier()
-    n_k = step.launches_per_step
+    n_k = step.calls_per_step
     events = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(n_k)] for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     visible = os.environ.get('CUDA_VISIBLE_DEVICES')
@@ -405,9 +419,9 @@ def run_b200(args) -> None:
         launches_per_step = len(bytes_per[name])
         avg_ms = sum(times) / len(times)
         algo = sum(bytes_per[name]) / launches_per_step
-        kernels[name] = {'launches': len(times), 'avg_ms': avg_ms, 'share': sum(times) / sum(sum(v) for v in kernel_ms.values()),
+        kernels[name] = {'calls': len(times), 'avg_ms': avg_ms, 'share': sum(times) / sum(sum(v) for v in kernel_ms.values()),
                          'algorithmic_bytes': algo, 'achieved_gbs': algo / (avg_ms * 1e-3) / 1e9}
-    dominant = max(kernels, key=lambda k: kernels[k]['avg_ms'] * kernels[k]['launches'])
+    dominant = max(kernels, key=lambda k: kernels[k]['avg_ms'] * kernels[k]['calls'])
     dk = kernels[dominant]
     roofline = {'bound': 'hbm', 'kernel': dominant, 'achieved': dk['achieved_gbs'], 'peak': peaks['hbm_gbs'], 'unit': 'GB/s',
                 'frac': dk['achieved_gbs'] / peaks['hbm_gbs'], 'peak_source': peaks['source'],
@@ -415,12 +429,8 @@ def run_b200(args) -> None:
     result = {'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
               'ms_per_step': ms_per_step, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
               'data': 'synthetic (seeded config 2 shapes; Mip-NeRF 360 unavailable)',
-              'config': {'workload': 'config2: 65536 rays x (64 + 64 + 32) intervals x 6 multisamples, fwd+bwd of 2 proposal levels (10x1 features, '
-                                     'table 2^21, 16->512, fused MLP 64) and the NeRF level (10x4 features, table 2^21, 16->8192)',
-                         'rays_per_gpu': args.rays, 'samples_per_step_per_gpu': step.samples_per_step,
-                         'parallelism': f'dp{world} (rays sharded, gradients all-reduced)' if world > 1 else 'single GPU',
-                         'l2': 'inputs larger than L2 (step working set ~1.8 GB > 126 MB)'},
-              'roofline': roofline, 'kernels': kernels, 'gpu_launches': step.launches_per_step * args.steps, 'clocks': clocks.summary()}
+              'config': bench_config(args, world, step.samples_per_step),
+              'roofline': roofline, 'kernels': kernels, 'gpu_launches': step.kernel_launches_per_step * args.steps, 'clocks': clocks.summary()}
     if not args.skip_e2e:
         result['e2e'] = measure_e2e(step, args, world, start_exchange, exchange, barrier)
     if rank == 0 and not args.skip_cpu_baseline and world == 1:

@@ -277,6 +277,17 @@ int64_t zf_featurizer_n_fp32_grad_rows(const zf_featurizer* featurizer) { return
 
 int64_t zf_featurizer_n_rows(const zf_featurizer* featurizer) { return featurizer ? featurizer->n_rows() : 0; }
 
+int zf_featurizer_launches(const zf_featurizer* featurizer, const int call) {
+    if (featurizer == nullptr) return 0;
+    switch (call) {
+        case 0: return featurizer->forward_passes.n;
+        case 1: return featurizer->mlp_width > 0 ? 1 : 0;
+        case 2: return featurizer->backward_passes.n;
+        case 3: return featurizer->mlp_width > 0 ? 2 : 0;  // the MLP kernel and the scatter
+        default: return 0;
+    }
+}
+
 int zf_featurize_forward(zf_featurizer* f, const zf_forward_args* a, cudaStream_t stream) {
     if (f == nullptr || a == nullptr) return fail(ZF_ERROR_INVALID_ARGUMENT, "featurizer and arguments must not be null");
     zf::ForwardArgs k{};

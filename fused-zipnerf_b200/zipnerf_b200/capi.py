@@ -15,7 +15,7 @@ LIBRARY = Path(__file__).resolve().parent.parent / 'ZipNeRFCudaBackend' / 'libzf
 ZF_OK, ZF_ERROR_INVALID_ARGUMENT, ZF_ERROR_UNSUPPORTED, ZF_ERROR_CUDA = 0, 1, 2, 3
 
 EXPORTED = ['zf_featurizer_create', 'zf_featurizer_destroy', 'zf_featurizer_n_output_features', 'zf_featurizer_n_fp32_grad_rows',
-            'zf_featurizer_n_rows', 'zf_featurize_forward', 'zf_featurize_backward', 'zf_featurize_backward_mlp',
+            'zf_featurizer_n_rows', 'zf_featurizer_launches', 'zf_featurize_forward', 'zf_featurize_backward', 'zf_featurize_backward_mlp',
             'zf_featurize_backward_mlp_workspace_size', 'zf_featurize_backward_mlp_no_alloc', 'zf_featurize_debug',
             'zf_check_erf_saturation', 'zf_erf_saturation_threshold', 'zf_last_error', 'zf_grid_max_value', 'zf_nerf_grid_grad_scale']
 
@@ -75,6 +75,8 @@ def load() -> ctypes.CDLL:
     lib.zf_featurizer_n_fp32_grad_rows.restype = _i64
     lib.zf_featurizer_n_rows.argtypes = [_p]
     lib.zf_featurizer_n_rows.restype = _i64
+    lib.zf_featurizer_launches.argtypes = [_p, ctypes.c_int]
+    lib.zf_featurizer_launches.restype = ctypes.c_int
     lib.zf_featurize_forward.argtypes = [_p, ctypes.POINTER(zf_forward_args), _p]
     lib.zf_featurize_backward.argtypes = [_p, ctypes.POINTER(zf_backward_args), _p]
     lib.zf_featurize_backward_mlp.argtypes = [_p, ctypes.POINTER(zf_backward_mlp_args), _p]
@@ -185,6 +187,10 @@ class CFeaturizer:
                                  _ptr(grad_table), grad_table.numel(), _ptr(grad_w0), grad_w0.numel(), _ptr(grad_b0), _ptr(grad_w1),
                                  _ptr(grad_b1), None, 0)
         check(load().zf_featurize_backward_mlp_no_alloc(self.handle, ctypes.byref(a), _stream(stream)))
+
+    def launches(self, call: str) -> int:
+        """Kernel launches of one call: 'forward', 'forward_mlp', 'backward' or 'backward_mlp'."""
+        return load().zf_featurizer_launches(self.handle, ['forward', 'forward_mlp', 'backward', 'backward_mlp'].index(call))
 
     def workspace_size(self, n_samples: int) -> int:
         return load().zf_featurize_backward_mlp_workspace_size(self.handle, n_samples)

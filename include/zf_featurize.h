@@ -136,6 +136,10 @@ ZF_API int zf_featurizer_n_output_features(const zf_featurizer* featurizer);
 ZF_API int64_t zf_featurizer_n_fp32_grad_rows(const zf_featurizer* featurizer);
 /* total table rows (sum of level_entries) */
 ZF_API int64_t zf_featurizer_n_rows(const zf_featurizer* featurizer);
+/* kernel launches of one call (no counterpart in the reference, which launches one kernel per call): call 0 =
+ * zf_featurize_forward without the MLP, 1 = with the MLP, 2 = zf_featurize_backward, 3 = zf_featurize_backward_mlp.
+ * Grids larger than the L2 run their forward and backward as level passes, one launch each; 0 for other calls. */
+ZF_API int zf_featurizer_launches(const zf_featurizer* featurizer, int call);
 
 /* Featurizer::forward (featurizer.cu:188-264) */
 ZF_API int zf_featurize_forward(zf_featurizer* featurizer, const zf_forward_args* args, struct CUstream_st* stream);
