@@ -205,10 +205,8 @@ int zf_featurizer_create(const int level, const int64_t* level_sizes, const int6
             return fail(ZF_ERROR_INVALID_ARGUMENT, "invalid level size or entries");
         }
         const int64_t size = level_sizes[l];
-        // the cooperative forward of 1-2 features per level packs cell coordinates into 16 bits
-        if (zf::cooperative_forward(n_features) && size > static_cast<int64_t>(zf::kMaxPackedSize)) {
-            return fail(ZF_ERROR_UNSUPPORTED, "level sizes above 65534 are not supported with 1-2 features per level");
-        }
+        // the kernels' group records pack cell coordinates into 16 bits
+        if (size > static_cast<int64_t>(zf::kMaxPackedSize)) return fail(ZF_ERROR_UNSUPPORTED, "level sizes above 65534 are not supported");
         const bool hashed = size * size * size > level_entries[l];
         if (!hashed && size * size * size > static_cast<int64_t>(INT32_MAX)) return fail(ZF_ERROR_INVALID_ARGUMENT, "dense level too large");
         f.offsets[l + 1] = f.offsets[l] + level_entries[l];
@@ -363,7 +361,7 @@ int zf_featurize_backward(zf_featurizer* f, const zf_backward_args* a, cudaStrea
     k.grad_table_half = a->grad_table_half;
     int max_levels = 0;
     for (int p = 0; p < f->backward_passes.n; p++) max_levels = std::max(max_levels, f->backward_passes.begin[p + 1] - f->backward_passes.begin[p]);
-    const size_t smem = static_cast<size_t>(zf::backward_smem_floats(f->n_features, max_levels * (f->n_features + 1))) * sizeof(float);
+    const size_t smem = static_cast<size_t>(zf::backward_smem_bytes(max_levels * (f->n_features + 1), 2));
     for (int p = 0; p < f->backward_passes.n; p++) {
         k.level_begin = static_cast<uint32_t>(f->backward_passes.begin[p]);
         k.level_end = static_cast<uint32_t>(f->backward_passes.begin[p + 1]);
@@ -438,7 +436,7 @@ int zf_featurize_backward_mlp(zf_featurizer* f, const zf_backward_mlp_args* a, c
         s.grad_table = a->grad_table;
         s.level_begin = 0;
         s.level_end = static_cast<uint32_t>(f->n_levels);
-        const size_t scatter_smem = static_cast<size_t>(zf::backward_smem_floats(f->n_features, n_out)) * sizeof(float);
+        const size_t scatter_smem = static_cast<size_t>(zf::backward_smem_bytes(n_out, 4));
         error = launch(f->kernels->backward, n_blocks(n_samples), scatter_smem, stream, f->params, s);
     }
     if (a->workspace == nullptr) {

@@ -29,10 +29,7 @@ constexpr int kBlock = 128;
 #define ZF_MIN_BLOCKS_FORWARD_COOP 6
 #endif
 #ifndef ZF_MIN_BLOCKS_BACKWARD
-#define ZF_MIN_BLOCKS_BACKWARD 5
-#endif
-#ifndef ZF_MIN_BLOCKS_BACKWARD_PACKED
-#define ZF_MIN_BLOCKS_BACKWARD_PACKED 6
+#define ZF_MIN_BLOCKS_BACKWARD 6
 #endif
 #ifndef ZF_MIN_BLOCKS_BACKWARD_MLP
 #define ZF_MIN_BLOCKS_BACKWARD_MLP 2
@@ -127,24 +124,13 @@ __device__ __forceinline__ void multisamples(const Frustum& fr, float3 (&x)[kMul
 // listed group-index-major (every lane's first group, then every lane's second group, ...), so a lane's groups come in
 // its own order, which the forward's accumulation needs.
 
-// Per-warp records of the current level. Lane-major records (the scatter's lane-major task lists, where neighbouring
-// lanes read one lane's groups) sit at [l 7 + j]: with stride 7 the 16-byte records of 8 consecutive lanes fall into
-// distinct bank quads. Multisample-major records (the forward's group-major task lists, where neighbouring lanes read
-// different lanes' records) sit at [j 32 + l], with the cell packed into 16-bit fields (exact for cells in [-1, 65534],
-// i.e. level sizes up to kMaxPackedSize), which keeps the forward's shared memory within 5 blocks per SM.
+// Per-warp records of the current level, cells packed into 16-bit fields (exact for cells in [-1, 65534], i.e. level
+// sizes up to kMaxPackedSize), which keeps the kernels' shared memory within 6 blocks per SM. Lane-major records (the
+// scatter's lane-major task lists, where neighbouring lanes read one lane's groups) sit at [l 7 + j]: with stride 7 the
+// 16-byte records of 8 consecutive lanes fall into distinct bank quads. Multisample-major records (the forward's
+// group-major task lists, where neighbouring lanes read different lanes' records) sit at [j 32 + l].
 constexpr int kRecordStride = 7;
 constexpr uint32_t kMaxPackedSize = 65534;
-struct LaneMajorRecords {
-    float4 frac[32 * kRecordStride];   // (fx, fy, fz, weighting) of every multisample
-    int4 cell[32 * kRecordStride];     // (cx, cy, cz, member mask) of every group leader
-    uint8_t task[32 * kMultisamples];  // one byte per group: owner lane | leader multisample << 5
-
-    static __device__ __forceinline__ int at(const uint32_t lane, const uint32_t j) { return static_cast<int>(lane * kRecordStride + j); }
-    __device__ __forceinline__ void put_cell(const int i, const int cx, const int cy, const int cz, const uint32_t members) {
-        cell[i] = make_int4(cx, cy, cz, static_cast<int>(members));
-    }
-    __device__ __forceinline__ int4 get_cell(const int i) const { return cell[i]; }
-};
 struct PackedRecords {
     float4 frac[kMultisamples * 32];   // (fx, fy, fz, weighting) of every multisample
     uint2 cell[kMultisamples * 32];    // (cx + 1 | (cy + 1) << 16, cz + 1 | member mask << 16) of every group leader
@@ -178,11 +164,23 @@ struct LaneMajorPackedRecords {
                          static_cast<int>(c.y >> 16));
     }
 };
-static_assert(sizeof(LaneMajorRecords) % 16 == 0 && sizeof(PackedRecords) % 16 == 0 && sizeof(LaneMajorPackedRecords) % 16 == 0,
-              "records stay 16-byte aligned per warp");
-// the scatter's records: packed cells for 1-2 features per level (level sizes up to kMaxPackedSize, as the forward)
-template <int F>
-using ScatterRecords = std::conditional_t<(F <= 2), LaneMajorPackedRecords, LaneMajorRecords>;
+static_assert(sizeof(PackedRecords) % 16 == 0 && sizeof(LaneMajorPackedRecords) % 16 == 0, "records stay 16-byte aligned per warp");
+// the scatter's records: lane-major with packed cells (level sizes up to kMaxPackedSize)
+using ScatterRecords = LaneMajorPackedRecords;
+
+// a warp's staged feature gradients, row r, column c: fp32 rows already scaled, or bf16 bits scaled on reading by
+// feature_scale * grad_scale (the product first, as the reference's feature_scale * grad_scale * g,
+// featurize_backward.cu:24)
+template <typename T>
+struct StagedRows {
+    const T* rows;
+    int stride;
+    float scale;
+    __device__ __forceinline__ float operator()(const uint32_t r, const int c) const {
+        if constexpr (std::is_same_v<T, float>) return rows[r * stride + c];
+        else return scale * bf16_bits_to_f32(rows[r * stride + c]);
+    }
+};
 
 // writes one interval's multisample records of a level; returns the mask of group leaders (the lowest multisample of
 // every set of multisamples that share a cell)
@@ -704,10 +702,10 @@ __device__ __forceinline__ void sum_run(float (&v)[F], const int lane, const int
 // the owner's gradient (fp32 table, or fp16 table with rows re-based at row_base). fp32 contributions of runs of equal
 // cells are summed over the run first; fp16 contributions are always rounded and added one by one, as the reference
 // does.
-template <int F, bool HALF>
-__device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32_t level, const uint32_t level_begin, const ScatterRecords<F>& gr,
-                                              const uint32_t n_tasks, const int lane, const float* warp_rows, const int stride,
-                                              float* __restrict__ grad_table, uint16_t* __restrict__ grad_table_half, const uint32_t row_base) {
+template <int F, bool HALF, typename Rows>
+__device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32_t level, const uint32_t level_begin, const ScatterRecords& gr,
+                                              const uint32_t n_tasks, const int lane, const Rows& staged, float* __restrict__ grad_table,
+                                              uint16_t* __restrict__ grad_table_half, const uint32_t row_base) {
     for (uint32_t first = 0; first < n_tasks; first += 32) {
         const bool valid = first + lane < n_tasks;
         float weights[8];
@@ -718,7 +716,7 @@ __device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32
             uint32_t owner;
             task_group(gr, first + lane, weights, c, owner);
             #pragma unroll
-            for (int f = 0; f < F; f++) g[f] = warp_rows[owner * stride + (level - level_begin) * (F + 1) + f];
+            for (int f = 0; f < F; f++) g[f] = staged(owner, static_cast<int>(level - level_begin) * (F + 1) + f);
             cell_rows(gp, level, c.x, c.y, c.z, rows, weights);
         }
         else {
@@ -768,16 +766,14 @@ __device__ __forceinline__ void scatter_tasks(const GridParams& gp, const uint32
 // warp_rows[l stride], column (level - level_begin) (F + 1) + f; scale features carry none) into the grid gradient:
 // levels below n_fp32 into grad_table (fp32), the others into grad_table_half (fp16, rows re-based at the first fp16
 // level). Inactive lanes and all-zero level gradients add no tasks. Every lane of the warp must call this.
-template <int F>
-__device__ __forceinline__ void scatter_warp(const GridParams& gp, const Frustum& fr, const bool active, const float* warp_rows, const int stride,
-                                             const int lane, const uint32_t n_fp32, float* __restrict__ grad_table,
-                                             uint16_t* __restrict__ grad_table_half, ScatterRecords<F>& gr, const uint32_t level_begin,
-                                             const uint32_t level_end) {
+template <int F, typename Rows>
+__device__ __forceinline__ void scatter_warp(const GridParams& gp, const Frustum& fr, const bool active, const Rows& staged, const int lane,
+                                             const uint32_t n_fp32, float* __restrict__ grad_table, uint16_t* __restrict__ grad_table_half,
+                                             ScatterRecords& gr, const uint32_t level_begin, const uint32_t level_end) {
     float3 x[kMultisamples];
     float scale[kMultisamples];
     if (active) multisamples(fr, x, scale);
     const uint32_t half_base = gp.offset[min(n_fp32, gp.n_levels)];
-    const float* g_row = warp_rows + lane * stride;
     #pragma unroll 1
     for (uint32_t level = level_begin; level < level_end; level++) {
         const uint32_t size = gp.size[level];
@@ -785,7 +781,7 @@ __device__ __forceinline__ void scatter_warp(const GridParams& gp, const Frustum
         if (active) {
             bool any = false;
             #pragma unroll
-            for (int f = 0; f < F; f++) any |= g_row[(level - level_begin) * (F + 1) + f] != 0.0f;
+            for (int f = 0; f < F; f++) any |= staged(static_cast<uint32_t>(lane), static_cast<int>(level - level_begin) * (F + 1) + f) != 0.0f;
             if (any) {
                 float weighting[kMultisamples];
                 #pragma unroll
@@ -795,8 +791,8 @@ __device__ __forceinline__ void scatter_warp(const GridParams& gp, const Frustum
         }
         const uint32_t n_tasks = list_tasks_by_lane(leaders, lane, gr);
         __syncwarp();
-        if (level < n_fp32) scatter_tasks<F, false>(gp, level, level_begin, gr, n_tasks, lane, warp_rows, stride, grad_table, grad_table_half, 0u);
-        else scatter_tasks<F, true>(gp, level, level_begin, gr, n_tasks, lane, warp_rows, stride, grad_table, grad_table_half, half_base);
+        if (level < n_fp32) scatter_tasks<F, false>(gp, level, level_begin, gr, n_tasks, lane, staged, grad_table, grad_table_half, 0u);
+        else scatter_tasks<F, true>(gp, level, level_begin, gr, n_tasks, lane, staged, grad_table, grad_table_half, half_base);
         __syncwarp();
     }
 }
@@ -819,7 +815,7 @@ struct BackwardArgs {
 };
 
 template <int F>
-__global__ void __launch_bounds__(kBlock, F <= 2 ? ZF_MIN_BLOCKS_BACKWARD_PACKED : ZF_MIN_BLOCKS_BACKWARD) fz_backward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardArgs a) {
+__global__ void __launch_bounds__(kBlock, ZF_MIN_BLOCKS_BACKWARD) fz_backward_kernel(const __grid_constant__ GridParams gp, const __grid_constant__ BackwardArgs a) {
     const int n_out = static_cast<int>(gp.n_levels) * (F + 1);
     // the columns of this pass's levels
     const int c0 = static_cast<int>(a.level_begin) * (F + 1), n_cols = static_cast<int>(a.level_end - a.level_begin) * (F + 1);
@@ -829,36 +825,39 @@ __global__ void __launch_bounds__(kBlock, F <= 2 ? ZF_MIN_BLOCKS_BACKWARD_PACKED
     const uint32_t warp_first = blockIdx.x * kBlock + warp * 32;
     if (warp_first >= a.in.n_samples) return;
     const int n_rows = min(32, static_cast<int>(a.in.n_samples - warp_first));
-    // the warps' group records, then the gradient rows of this pass's columns
-    ScatterRecords<F>& gr = reinterpret_cast<ScatterRecords<F>*>(smem)[warp];
-    float* warp_rows = smem + kWarps * static_cast<int>(sizeof(ScatterRecords<F>) / sizeof(float)) + warp * 32 * stride;
-    // coalesced load of the warp's gradient rows
-    if (a.grad_rows != nullptr) {
-        for (LaneWalk w(lane, n_cols); w.r < n_rows; w.next()) {
-            warp_rows[w.r * stride + w.c] = __ldcs(a.grad_rows + static_cast<size_t>(warp_first + w.r) * n_out + c0 + w.c);
-        }
-    }
-    else {
-        // bf16 feature gradients, scaled as the reference (feature_scale * grad_scale * g, featurize_backward.cu:24)
-        for (LaneWalk w(lane, n_cols); w.r < n_rows; w.next()) {
-            const uint16_t bits = __ldcs(a.grad_features + static_cast<size_t>(warp_first + w.r) * a.grad_stride + c0 + w.c);
-            warp_rows[w.r * stride + w.c] = kFeatureScale * a.grad_scale * bf16_bits_to_f32(bits);
-        }
-    }
-    __syncwarp();
+    // the warps' group records, then the gradient rows of this pass's columns (fp32 or bf16, as given)
+    ScatterRecords& gr = reinterpret_cast<ScatterRecords*>(smem)[warp];
+    unsigned char* rows_base = reinterpret_cast<unsigned char*>(smem) + kWarps * sizeof(ScatterRecords);
     const uint32_t sample = warp_first + lane;
     bool active = lane < n_rows;
     if (active && a.skip_if_zero != nullptr && __ldcs(a.skip_if_zero + sample) == 0.0f) active = false;
     Frustum fr;
     if (active) fr = setup_frustum(a.in, gp.pattern_stream, sample);
-    scatter_warp<F>(gp, fr, active, warp_rows, stride, lane, a.n_fp32_levels, a.grad_table, a.grad_table_half, gr, a.level_begin, a.level_end);
+    // coalesced load of the warp's gradient rows
+    if (a.grad_rows != nullptr) {
+        float* warp_rows = reinterpret_cast<float*>(rows_base) + warp * 32 * stride;
+        for (LaneWalk w(lane, n_cols); w.r < n_rows; w.next()) {
+            warp_rows[w.r * stride + w.c] = __ldcs(a.grad_rows + static_cast<size_t>(warp_first + w.r) * n_out + c0 + w.c);
+        }
+        __syncwarp();
+        scatter_warp<F>(gp, fr, active, StagedRows<float>{warp_rows, stride, 1.0f}, lane, a.n_fp32_levels, a.grad_table, a.grad_table_half, gr,
+                        a.level_begin, a.level_end);
+    }
+    else {
+        uint16_t* warp_rows = reinterpret_cast<uint16_t*>(rows_base) + warp * 32 * stride;
+        for (LaneWalk w(lane, n_cols); w.r < n_rows; w.next()) {
+            warp_rows[w.r * stride + w.c] = __ldcs(a.grad_features + static_cast<size_t>(warp_first + w.r) * a.grad_stride + c0 + w.c);
+        }
+        __syncwarp();
+        scatter_warp<F>(gp, fr, active, StagedRows<uint16_t>{warp_rows, stride, kFeatureScale * a.grad_scale}, lane, a.n_fp32_levels, a.grad_table,
+                        a.grad_table_half, gr, a.level_begin, a.level_end);
+    }
 }
 
-// dynamic shared memory of fz_backward_kernel in floats for passes of at most n_cols gradient columns: the warps'
-// scatter records, then the staged gradient rows
-__host__ __device__ constexpr int backward_smem_floats(const int n_features, const int n_cols) {
-    return kWarps * static_cast<int>((n_features <= 2 ? sizeof(LaneMajorPackedRecords) : sizeof(LaneMajorRecords)) / sizeof(float)) +
-           kBlock * staged_stride(n_cols);
+// dynamic shared memory of fz_backward_kernel in bytes for passes of at most n_cols gradient columns of row_bytes each
+// (4: fp32 rows, 2: bf16 rows): the warps' scatter records, then the staged gradient rows
+__host__ __device__ constexpr int backward_smem_bytes(const int n_cols, const int row_bytes) {
+    return kWarps * static_cast<int>(sizeof(ScatterRecords)) + kBlock * staged_stride(n_cols) * row_bytes;
 }
 
 // ---------------------------------------------------------------------------------------------------------------------

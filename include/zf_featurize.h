@@ -124,7 +124,7 @@ typedef struct zf_backward_mlp_args {
  * current CUDA device. level selects the pattern stream; level_sizes / level_entries give each grid level's
  * resolution and table entries (a level is hashed when size^3 > entries; its rows follow the previous levels').
  * Supported here: 1 <= n_levels <= 16, 1 <= n_features <= 4, 0 <= mlp_width (0: no fused MLP), rows * n_features
- * <= 2^32 - 1, level sizes <= 2^20 (<= 65534 with 1-2 features per level). */
+ * <= 2^32 - 1, level sizes <= 65534 (the kernels pack cell coordinates into 16 bits). */
 ZF_API int zf_featurizer_create(int level, const int64_t* level_sizes, const int64_t* level_entries, int n_levels,
                          int n_features, int mlp_width, zf_featurizer** out);
 ZF_API void zf_featurizer_destroy(zf_featurizer* featurizer);

@@ -54,10 +54,11 @@ def test_create_validates_layout_before_touching_a_device():
     big = (ctypes.c_int64 * 2)(1 << 31, 1 << 31)
     assert lib.zf_featurizer_create(0, (ctypes.c_int64 * 2)(2048, 2048), big, 2, 4, 0, ctypes.byref(handle)) == capi.ZF_ERROR_INVALID_ARGUMENT
     assert b'32-bit indexing' in lib.zf_last_error()
-    # 1-2 features per level: cell coordinates are packed into 16 bits
+    # cell coordinates are packed into 16 bits
     wide = (ctypes.c_int64 * 1)(70000)
-    assert lib.zf_featurizer_create(0, wide, (ctypes.c_int64 * 1)(1 << 20), 1, 2, 0, ctypes.byref(handle)) == capi.ZF_ERROR_UNSUPPORTED
-    assert b'65534' in lib.zf_last_error()
+    for n_features in (2, 4):
+        assert lib.zf_featurizer_create(0, wide, (ctypes.c_int64 * 1)(1 << 20), 1, n_features, 0, ctypes.byref(handle)) == capi.ZF_ERROR_UNSUPPORTED
+        assert b'65534' in lib.zf_last_error()
     assert lib.zf_featurize_forward(None, None, None) == capi.ZF_ERROR_INVALID_ARGUMENT
     assert lib.zf_featurizer_n_output_features(None) == 0
 
