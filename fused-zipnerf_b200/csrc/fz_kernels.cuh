@@ -17,7 +17,8 @@ namespace zf {
 constexpr int kBlock = 128;
 // minimum resident blocks per SM each kernel's register allocation must allow (__launch_bounds__), from sweeps on the
 // B200: the kernels are latency bound and gain from resident warps up to where registers spill or shared memory runs
-// out (the cooperative forward and the scatter: shared memory for 5 blocks; the MLP kernel: 2 blocks of 256 threads)
+// out (the cooperative forward and the scatter: shared memory for 6 blocks; the MLP kernel: 2 blocks of 256 threads;
+// the per-lane forward of 3-4 features: 6, 7 with its MLP)
 #ifndef ZF_MIN_BLOCKS_FORWARD
 #define ZF_MIN_BLOCKS_FORWARD 6
 #endif
