@@ -12,7 +12,8 @@ data-parallel exchange of a training step.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-Prints one JSON line on rank 0.
+Prints one JSON line on rank 0. On one GPU the line also carries "rows": the sampling and Adam kernels of the same
+training step (composite-and-resample, ray generation, the Adam step), each timed alone against the HBM roofline.
 """
 from __future__ import annotations
 
@@ -433,6 +434,8 @@ def run_b200(args) -> None:
               'roofline': roofline, 'kernels': kernels, 'gpu_launches': step.kernel_launches_per_step * args.steps, 'clocks': clocks.summary()}
     if not args.skip_e2e:
         result['e2e'] = measure_e2e(step, args, world, start_exchange, exchange, barrier)
+    if rank == 0 and not args.skip_rows and world == 1:
+        result['rows'] = measure_rows(device)
     if rank == 0 and not args.skip_cpu_baseline and world == 1:
         from oracle.zf_oracle import build, n_threads_default
         build()
@@ -442,6 +445,60 @@ def run_b200(args) -> None:
         dist.destroy_process_group()
     if rank == 0:
         emit(result)
+
+
+def measure_rows(device, iters: int = 10) -> dict:
+    """The per-step kernels around the featurization, each timed alone through the C ABI on config-2-sized inputs after
+    an L2 flush (zipnerf_b200/rows.py): the two composite-and-resample calls of a training step (proposal level 0 -> 64
+    intervals, level 1 -> 32), the training rays of a step drawn from a 185-view pool, and the Adam step over the
+    reference model's optimizer buffers (77.5 M parameters). Achieved bandwidth = algorithmic bytes / median time,
+    against the measured HBM peak."""
+    import ctypes
+    import ZipNeRFCudaBackend as backend
+    from zipnerf_b200 import capi, rows
+    lib = capi.load()
+    peaks = measured_peaks()
+    timer = rows.LaunchTimer(device)
+    stream = torch.cuda.current_stream().cuda_stream
+    R = rows.N_RAYS
+    warp = capi.make_ray_warp(rows.WARP)
+
+    def entry(ms_list, nbytes, config):
+        ms = sum(ms_list)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        return {'config': config, 'ms': ms, 'calls_ms': ms_list, 'algorithmic_bytes': nbytes, 'achieved_gbs': gbs, 'peak': peaks['hbm_gbs'],
+                'frac': gbs / peaks['hbm_gbs']}
+
+    out = {}
+    inp = rows.resample_inputs(R, 64, device)
+    calls, nbytes = [], 0
+    for m, level in ((64, 1), (32, 2)):
+        s_next, t_next, weights = torch.empty(R, m + 1, device=device), torch.empty(R, m + 1, device=device), torch.empty(R, 64, device=device)
+        a = capi.zf_resample_args(inp['raw_density'].data_ptr(), inp['sdist'].data_ptr(), inp['tdist'].data_ptr(), inp['directions'].data_ptr(), R,
+                                  64, 0.5, m, 1234, level, warp, weights.data_ptr(), s_next.data_ptr(), t_next.data_ptr())
+        calls.append(timer(lambda a=a: capi.check(lib.zf_composite_and_resample(ctypes.byref(a), stream)), iters))
+        nbytes += R * rows.resample_bytes(64, m)
+    out['composite_and_resample'] = entry(calls, nbytes, f'{R} rays: 64 -> 64 and 64 -> 32 intervals (training, jittered)')
+    pool = rows.ray_pool(device)
+    width = capi.direction_block_width(4)
+    o = [torch.empty(R, 3, device=device) for _ in range(3)]
+    radii, encoded = torch.empty(R, device=device), torch.empty(R, width, dtype=torch.bfloat16, device=device)
+    sd, td = torch.empty(R, 65, device=device), torch.empty(R, 65, device=device)
+    ga = capi.zf_generate_rays_args(77, R, pool['view_offsets'].data_ptr(), pool['view_cameras'].numel(), pool['view_cameras'].data_ptr(),
+                                    pool['camera_offsets'].data_ptr(), pool['local_directions'].data_ptr(), pool['c2w'].data_ptr(),
+                                    pool['camera_radii'].data_ptr(), pool['pool_rgb'].data_ptr(), pool['pool_rgb'].shape[0], 4, 64, warp,
+                                    o[0].data_ptr(), o[1].data_ptr(), radii.data_ptr(), o[2].data_ptr(), encoded.data_ptr(), sd.data_ptr(), td.data_ptr())
+    ms = timer(lambda: capi.check(lib.zf_generate_rays(ctypes.byref(ga), stream)), iters)
+    out['generate_rays'] = entry([ms], R * rows.new_rays_bytes(64, width), f'{R} rays from 185 views of 1296 x 840 pixels, 64 first-level intervals')
+    del pool
+    layout, params, grads, n_levels = rows.adam_inputs(device)
+    mags = torch.zeros(n_levels, device=device)
+    opt = backend.Adam(params, grads, [b['scale'] for b in layout], [b['offsets'] for b in layout], 0.1, 1e-5, 0.9, 0.99, 1e-15, mags)
+    ms = timer(lambda: opt.step(1e-3), iters)
+    n_params = sum(b['numel'] for b in layout)
+    out['adam'] = entry([ms], rows.adam_bytes(layout), f'{n_params} parameters in {len(layout)} buffers ({n_levels} grid levels, '
+                        'NeRF grid levels 3-9 with fp16 gradients)')
+    return out
 
 
 def measure_e2e(step: Step, args, world: int, start_exchange, exchange, barrier) -> dict:
@@ -531,6 +588,7 @@ def main() -> None:
     parser.add_argument('--reference-repeats', type=int, default=5, help='passes over the ray sample timed for cpu_baseline')
     parser.add_argument('--skip-e2e', action='store_true')
     parser.add_argument('--skip-cpu-baseline', action='store_true')
+    parser.add_argument('--skip-rows', action='store_true', help='skip the timing of the sampling and Adam kernels')
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps
     if args.impl == 'reference':

@@ -3,7 +3,8 @@
     python fused-zipnerf_b200/build.py [--jobs N] [--force]
 
 Outputs (next to the Python package that loads them, so they travel with the source tree):
-  ZipNeRFCudaBackend/libzf_featurize.so  -- the sm_100a kernels and the C ABI of include/zf_featurize.h
+  ZipNeRFCudaBackend/libzf_featurize.so  -- the sm_100a kernels and the C ABI of include/zf_featurize.h,
+                                            include/zf_sampling.h and include/zf_optim.h
   ZipNeRFCudaBackend/_C.<abi>.so         -- the PyTorch binding (ZipNeRFCudaBackend._C)
 
 Kernels are compiled ahead of time for sm_100a only (nvcc -gencode arch=compute_100a,code=sm_100a), one object per
@@ -70,16 +71,19 @@ def build_library(jobs: int | None = None, force: bool = False, subset: set | No
             wanted.append(obj)
             if force or _stale(obj, [inst, *deps]):
                 steps.append([NVCC, *NVCC_FLAGS, f'-DZF_INST_F={features}', f'-DZF_INST_PAD={pad}', '-c', str(inst), '-o', str(obj)])
-    capi = CSRC / 'fz_capi.cu'
-    capi_obj = BUILD / 'fz_capi.o'
-    if force or _stale(capi_obj, [capi, *deps]):
-        steps.append([NVCC, *NVCC_FLAGS, '-c', str(capi), '-o', str(capi_obj)])
+    # the C ABI translation units: featurizer objects, the sampling kernels, the Adam step
+    abi_objects = []
+    for name in ['fz_capi', 'fz_sampling', 'fz_optim']:
+        source, obj = CSRC / f'{name}.cu', BUILD / f'{name}.o'
+        abi_objects.append(obj)
+        if force or _stale(obj, [source, *deps]):
+            steps.append([NVCC, *NVCC_FLAGS, '-c', str(source), '-o', str(obj)])
     # the largest instantiations first, so the parallel build ends evenly
     steps.sort(key=lambda cmd: -int(next((a.split('=')[1] for a in cmd if a.startswith('-DZF_INST_PAD=')), '999')))
     with concurrent.futures.ThreadPoolExecutor(max_workers=jobs or os.cpu_count() or 4) as pool:
         for future in [pool.submit(_run, cmd) for cmd in steps]:
             future.result()
-    objects = wanted + [capi_obj]
+    objects = wanted + abi_objects
     if force or steps or _stale(LIBRARY, objects) or subset is not None:
         _run([NVCC, '-gencode', 'arch=compute_100a,code=sm_100a', '-shared', '-o', str(LIBRARY), *map(str, objects)])
     return LIBRARY
@@ -93,7 +97,7 @@ def build_torch_extension(force: bool = False) -> Path:
     suffix = sysconfig.get_config_var('EXT_SUFFIX') or '.so'
     target = PACKAGE / f'_C{suffix}'
     source = CSRC / 'torch_ext.cpp'
-    if not force and not _stale(target, [source, LIBRARY, INCLUDE / 'zf_featurize.h']):
+    if not force and not _stale(target, [source, LIBRARY, *sorted(INCLUDE.glob('*.h'))]):
         return target
     includes = cpp_extension.include_paths(device_type='cuda')
     python_include = sysconfig.get_paths()['include']

@@ -3,6 +3,7 @@
 // kernel selection from the ahead-of-time table, and launches on the caller's stream.
 #include "zf_featurize.h"
 #include "fz_kernel_set.h"
+#include "fz_status.h"
 
 #include <cuda_runtime.h>
 
@@ -135,6 +136,13 @@ unsigned n_blocks(const int64_t n) { return static_cast<unsigned>((n + zf::kBloc
 bool aligned(const void* p, const size_t bytes) { return reinterpret_cast<uintptr_t>(p) % bytes == 0; }
 
 }  // namespace
+
+namespace zf {
+
+int set_error(const int code, const std::string& message) { return fail(code, message); }
+int set_cuda_error(const cudaError_t error, const char* what) { return cuda_fail(error, what); }
+
+}  // namespace zf
 
 struct zf_featurizer {
     int level = 0;

@@ -1,12 +1,19 @@
-// torch_ext.cpp -- the PyTorch binding ZipNeRFCudaBackend._C over the C ABI (include/zf_featurize.h).
+// torch_ext.cpp -- the PyTorch binding ZipNeRFCudaBackend._C over the C ABI (include/zf_featurize.h, zf_sampling.h,
+// zf_optim.h).
 //
-// Mirrors the featurization part of the reference module (torch_bindings/bindings.cu:14-22): the attributes
-// grid_max_value and nerf_grid_grad_scale, set_rtc_dirs, and the class Featurizer with its constructor,
-// n_fp32_grad_rows, forward, backward and backward_mlp, with the reference's argument order and meaning
-// (featurizer.h:25-82), its tensor checks (featurizer.cu:127-138, 207-233, 276-283, 318-331) and its error text
-// (RuntimeError "ZipNeRF: ..."). Launches go to the current CUDA stream. An empty tensor skips an output, as in the
-// reference. All computation happens in libzf_featurize.so; this file only converts tensors to pointers.
+// Mirrors the reference module (torch_bindings/bindings.cu:14-43) except its NeRF MLP and its final-level
+// compositing / loss kernels: the attributes grid_max_value and nerf_grid_grad_scale, set_rtc_dirs, the class
+// Featurizer with its constructor, n_fp32_grad_rows, forward, backward and backward_mlp (featurizer.h:25-82), the
+// sampling functions generate_rays, view_rays, initialize_rays, sample_uniforms and composite_and_resample
+// (sampling_api.h:10-58), and the class Adam with step and regularization (optimizer_api.h:14-40), with the
+// reference's argument order and meaning, its tensor checks (featurizer.cu:127-138, 207-233, 276-283, 318-331;
+// sampling_api.cu:426-578; optimizer_api.cu:123-158) and its error text (RuntimeError "ZipNeRF: ..."). Launches go to
+// the current CUDA stream. An empty tensor skips a featurizer output, as in the reference. All computation happens in
+// libzf_featurize.so; this file only converts tensors to pointers and allocates the outputs the reference's wrappers
+// return.
 #include "zf_featurize.h"
+#include "zf_optim.h"
+#include "zf_sampling.h"
 
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -17,6 +24,7 @@
 
 #include <stdexcept>
 #include <string>
+#include <tuple>
 #include <vector>
 
 namespace {
@@ -265,6 +273,237 @@ private:
 // (featurizer.cu:112-117); these kernels are compiled ahead of time, so the directories are accepted and unused
 void set_rtc_dirs(const std::string&, const std::string&) {}
 
+// ---------------------------------------------------------------------------------------------------------------------
+// sampling (sampling_api.h:10-58, sampling_api.cu:426-578): the reference's wrappers allocate and return the outputs
+
+zf_ray_warp make_ray_warp(const std::vector<double>& values) {
+    if (values.size() != 7) throw std::runtime_error("ZipNeRF: invalid ray warp");
+    return {static_cast<float>(values[0]), static_cast<float>(values[1]), static_cast<float>(values[2]), static_cast<float>(values[3]),
+            static_cast<float>(values[4]), static_cast<float>(values[5]), static_cast<float>(values[6])};
+}
+
+void check_n_intervals(const int64_t n) {
+    if (n < 2 || n > 64) throw std::runtime_error("ZipNeRF: unsupported number of samples per level");
+}
+
+uint16_t* bf16_ptr(const at::Tensor& tensor) { return reinterpret_cast<uint16_t*>(tensor.data_ptr()); }
+
+std::vector<at::Tensor> generate_rays(const int64_t seed, const int n_rays, const at::Tensor& view_offsets, const at::Tensor& view_cameras,
+                                      const at::Tensor& camera_offsets, const at::Tensor& local_directions, const at::Tensor& c2w,
+                                      const at::Tensor& camera_radii, const at::Tensor& pool_rgb, const int direction_degree, const int n_samples,
+                                      const std::vector<double>& ray_warp) {
+    check_input(view_offsets, "view_offsets", at::kLong);
+    check_input(view_cameras, "view_cameras", at::kInt);
+    check_input(camera_offsets, "camera_offsets", at::kLong);
+    check_input(local_directions, "local_directions", at::kFloat);
+    check_input(c2w, "c2w", at::kFloat);
+    check_input(camera_radii, "camera_radii", at::kFloat);
+    check_input(pool_rgb, "pool_rgb", at::kByte);
+    check_n_intervals(n_samples);
+    const zf_ray_warp warp = make_ray_warp(ray_warp);
+    const int64_t n_views = view_cameras.size(0);
+    if (n_rays < 0 || view_offsets.numel() != n_views + 1 || c2w.numel() != 12 * n_views) throw std::runtime_error("ZipNeRF: invalid ray pool");
+    const auto options = local_directions.options();
+    at::Tensor origins = at::empty({n_rays, 3}, options), directions = at::empty({n_rays, 3}, options), radii = at::empty({n_rays}, options);
+    at::Tensor rgb = at::empty({n_rays, 3}, options);
+    at::Tensor encoded = at::empty({n_rays, zf_direction_block_width(direction_degree)}, options.dtype(at::kBFloat16));
+    at::Tensor sdist = at::empty({n_rays, n_samples + 1}, options), tdist = at::empty({n_rays, n_samples + 1}, options);
+    zf_generate_rays_args a{};
+    a.seed = seed;
+    a.n_rays = n_rays;
+    a.view_offsets = view_offsets.data_ptr<int64_t>();
+    a.n_views = static_cast<int>(n_views);
+    a.view_cameras = view_cameras.data_ptr<int32_t>();
+    a.camera_offsets = camera_offsets.data_ptr<int64_t>();
+    a.local_directions = local_directions.data_ptr<float>();
+    a.c2w = c2w.data_ptr<float>();
+    a.camera_radii = camera_radii.data_ptr<float>();
+    a.pool_rgb = pool_rgb.data_ptr<uint8_t>();
+    a.n_pixels = pool_rgb.size(0);
+    a.direction_degree = direction_degree;
+    a.n_samples = n_samples;
+    a.warp = warp;
+    a.origins = origins.data_ptr<float>();
+    a.directions = directions.data_ptr<float>();
+    a.radii = radii.data_ptr<float>();
+    a.rgb = rgb.data_ptr<float>();
+    a.encoded_directions = bf16_ptr(encoded);
+    a.sdist = sdist.data_ptr<float>();
+    a.tdist = tdist.data_ptr<float>();
+    const c10::cuda::CUDAGuard guard(local_directions.device());
+    check_status(zf_generate_rays(&a, current_stream()));
+    return {origins, directions, radii, rgb, encoded, sdist, tdist};
+}
+
+std::vector<at::Tensor> view_rays(const at::Tensor& pixel_indices, const at::Tensor& local_directions, const at::Tensor& c2w, const double radius,
+                                  const int direction_degree, const int n_samples, const std::vector<double>& ray_warp) {
+    check_input(pixel_indices, "pixel_indices", at::kLong);
+    check_input(local_directions, "local_directions", at::kFloat);
+    check_input(c2w, "c2w", at::kFloat);
+    if (c2w.numel() != 12) throw std::runtime_error("ZipNeRF: c2w must be a 3x4 matrix");
+    check_n_intervals(n_samples);
+    const zf_ray_warp warp = make_ray_warp(ray_warp);
+    const int64_t n_rays = pixel_indices.numel();
+    const auto options = local_directions.options();
+    at::Tensor origins = at::empty({n_rays, 3}, options), directions = at::empty({n_rays, 3}, options), radii = at::empty({n_rays}, options);
+    at::Tensor encoded = at::empty({n_rays, zf_direction_block_width(direction_degree)}, options.dtype(at::kBFloat16));
+    at::Tensor sdist = at::empty({n_rays, n_samples + 1}, options), tdist = at::empty({n_rays, n_samples + 1}, options);
+    zf_view_rays_args a{};
+    a.pixel_indices = pixel_indices.data_ptr<int64_t>();
+    a.n_rays = n_rays;
+    a.local_directions = local_directions.data_ptr<float>();
+    a.c2w = c2w.data_ptr<float>();
+    a.radius = static_cast<float>(radius);
+    a.direction_degree = direction_degree;
+    a.n_samples = n_samples;
+    a.warp = warp;
+    a.origins = origins.data_ptr<float>();
+    a.directions = directions.data_ptr<float>();
+    a.radii = radii.data_ptr<float>();
+    a.encoded_directions = bf16_ptr(encoded);
+    a.sdist = sdist.data_ptr<float>();
+    a.tdist = tdist.data_ptr<float>();
+    const c10::cuda::CUDAGuard guard(local_directions.device());
+    check_status(zf_view_rays(&a, current_stream()));
+    return {origins, directions, radii, encoded, sdist, tdist};
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> initialize_rays(const int64_t seed, const at::Tensor& directions, const int direction_degree,
+                                                               const int n_samples, const std::vector<double>& ray_warp) {
+    check_input(directions, "directions", at::kFloat);
+    check_n_intervals(n_samples);
+    const zf_ray_warp warp = make_ray_warp(ray_warp);
+    const int64_t n_rays = directions.size(0);
+    if (directions.numel() != 3 * n_rays) throw std::runtime_error("ZipNeRF: invalid rays");
+    const auto options = directions.options();
+    at::Tensor encoded = at::empty({n_rays, zf_direction_block_width(direction_degree)}, options.dtype(at::kBFloat16));
+    at::Tensor sdist = at::empty({n_rays, n_samples + 1}, options), tdist = at::empty({n_rays, n_samples + 1}, options);
+    zf_initialize_rays_args a{};
+    a.seed = seed;
+    a.directions = directions.data_ptr<float>();
+    a.n_rays = n_rays;
+    a.direction_degree = direction_degree;
+    a.n_samples = n_samples;
+    a.warp = warp;
+    a.encoded_directions = bf16_ptr(encoded);
+    a.sdist = sdist.data_ptr<float>();
+    a.tdist = tdist.data_ptr<float>();
+    const c10::cuda::CUDAGuard guard(directions.device());
+    check_status(zf_initialize_rays(&a, current_stream()));
+    return {encoded, sdist, tdist};
+}
+
+at::Tensor sample_uniforms(const int64_t seed, const int64_t stream, const int64_t n) {
+    if (n < 0) throw std::runtime_error("ZipNeRF: invalid number of uniforms");
+    at::Tensor values = at::empty({n}, at::TensorOptions().dtype(at::kFloat).device(at::kCUDA));
+    const c10::cuda::CUDAGuard guard(values.device());
+    check_status(zf_sample_uniforms(seed, stream, n, values.data_ptr<float>(), current_stream()));
+    return values;
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> composite_and_resample(const at::Tensor& raw_density, const at::Tensor& sdist, const at::Tensor& tdist,
+                                                                      const at::Tensor& directions, const double anneal, const int n_samples,
+                                                                      const int64_t seed, const int next_level, const std::vector<double>& ray_warp) {
+    check_input(raw_density, "raw_density", at::kFloat);
+    check_input(sdist, "sdist", at::kFloat);
+    check_input(tdist, "tdist", at::kFloat);
+    check_input(directions, "directions", at::kFloat);
+    check_n_intervals(n_samples);
+    if (raw_density.dim() != 2) throw std::runtime_error("ZipNeRF: invalid raw_density");
+    const int64_t n_rays = raw_density.size(0), n_intervals = raw_density.size(1);
+    check_n_intervals(n_intervals);
+    if (sdist.numel() != n_rays * (n_intervals + 1) || tdist.numel() != n_rays * (n_intervals + 1) || directions.numel() != 3 * n_rays) {
+        throw std::runtime_error("ZipNeRF: invalid composite_and_resample inputs");
+    }
+    const zf_ray_warp warp = make_ray_warp(ray_warp);
+    at::Tensor weights = at::empty_like(raw_density);
+    at::Tensor sdist_next = at::empty({n_rays, n_samples + 1}, raw_density.options()), tdist_next = at::empty({n_rays, n_samples + 1}, raw_density.options());
+    zf_resample_args a{};
+    a.raw_density = raw_density.data_ptr<float>();
+    a.sdist = sdist.data_ptr<float>();
+    a.tdist = tdist.data_ptr<float>();
+    a.directions = directions.data_ptr<float>();
+    a.n_rays = n_rays;
+    a.n_intervals = static_cast<int>(n_intervals);
+    a.anneal = static_cast<float>(anneal);
+    a.n_samples = n_samples;
+    a.seed = seed;
+    a.next_level = next_level;
+    a.warp = warp;
+    a.weights = weights.data_ptr<float>();
+    a.sdist_next = sdist_next.data_ptr<float>();
+    a.tdist_next = tdist_next.data_ptr<float>();
+    const c10::cuda::CUDAGuard guard(raw_density.device());
+    check_status(zf_composite_and_resample(&a, current_stream()));
+    return {weights, sdist_next, tdist_next};
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// Adam (optimizer_api.h:14-40, optimizer_api.cu:123-221): the tensor checks and messages of the reference; the object
+// keeps the tensors it updates alive
+
+void check_adam_buffer(const at::Tensor& tensor, const char* name, const bool allow_half) {
+    const bool valid_type = tensor.scalar_type() == at::kFloat || (allow_half && tensor.scalar_type() == at::kHalf);
+    if (!tensor.is_cuda() || !tensor.is_contiguous() || !valid_type || tensor.numel() % 4 != 0) {
+        throw std::runtime_error(std::string("ZipNeRF: ") + name + " must be a contiguous float (or half) cuda tensor with a multiple of four elements");
+    }
+}
+
+class Adam {
+public:
+    Adam(const std::vector<at::Tensor>& params, const std::vector<at::Tensor>& grads, const std::vector<double>& grad_scales,
+         const std::vector<std::vector<int64_t>>& level_offsets, const double reg_weight, const double max_value, const double beta1,
+         const double beta2, const double eps, const at::Tensor& magnitudes)
+        : m_params(params), m_grads(grads), m_magnitudes(magnitudes) {
+        const size_t n = params.size();
+        if (n == 0 || n > 8 || grads.size() != n || grad_scales.size() != n || level_offsets.size() != n) {
+            throw std::runtime_error("ZipNeRF: invalid optimizer buffers");
+        }
+        std::vector<zf_adam_buffer> buffers(n);
+        for (size_t b = 0; b < n; b++) {
+            check_adam_buffer(params[b], "param", false);
+            check_adam_buffer(grads[b], "grad", true);
+            if (grads[b].numel() != params[b].numel()) throw std::runtime_error("ZipNeRF: optimizer gradient size mismatch");
+            buffers[b] = {params[b].data_ptr<float>(), grads[b].data_ptr(), grads[b].scalar_type() == at::kHalf ? 1 : 0, params[b].numel(),
+                          grad_scales[b], level_offsets[b].data(), static_cast<int>(level_offsets[b].size())};
+        }
+        if (!magnitudes.is_cuda() || !magnitudes.is_contiguous() || magnitudes.scalar_type() != at::kFloat) {
+            throw std::runtime_error("ZipNeRF: magnitudes must be a contiguous float cuda tensor with one entry per level");
+        }
+        m_regularization = at::zeros({}, params.front().options());
+        const c10::cuda::CUDAGuard guard(params.front().device());
+        check_status(zf_adam_create(buffers.data(), static_cast<int>(n), reg_weight, max_value, beta1, beta2, eps, m_magnitudes.data_ptr<float>(),
+                                    m_magnitudes.numel(), m_regularization.data_ptr<float>(), &m_adam));
+    }
+
+    ~Adam() { zf_adam_destroy(m_adam); }
+
+    Adam(const Adam&) = delete;
+    Adam& operator=(const Adam&) = delete;
+
+    void step(const double lr) {
+        const c10::cuda::CUDAGuard guard(m_params.front().device());
+        check_status(zf_adam_step(m_adam, lr, current_stream()));
+    }
+
+    at::Tensor regularization() const { return m_regularization; }
+
+    // copies of one buffer's moments (no counterpart in the reference, whose moments are private)
+    std::tuple<at::Tensor, at::Tensor> state(const int buffer) const {
+        float* exp_avg = nullptr;
+        float* exp_avg_sq = nullptr;
+        int64_t steps = 0;
+        check_status(zf_adam_state(m_adam, buffer, &exp_avg, &exp_avg_sq, &steps));
+        const at::Tensor& param = m_params[buffer];
+        return {at::from_blob(exp_avg, {param.numel()}, param.options()).clone(), at::from_blob(exp_avg_sq, {param.numel()}, param.options()).clone()};
+    }
+
+private:
+    std::vector<at::Tensor> m_params, m_grads;
+    at::Tensor m_magnitudes, m_regularization;
+    zf_adam* m_adam = nullptr;
+};
+
 }  // namespace
 
 PYBIND11_MODULE(_C, m) {
@@ -280,4 +519,15 @@ PYBIND11_MODULE(_C, m) {
         .def("backward", &Featurizer::backward)
         .def("backward_mlp", &Featurizer::backward_mlp)
         .def("debug", &Featurizer::debug);
+    pybind11::class_<Adam>(m, "Adam")
+        .def(pybind11::init<const std::vector<at::Tensor>&, const std::vector<at::Tensor>&, const std::vector<double>&,
+                            const std::vector<std::vector<int64_t>>&, double, double, double, double, double, const at::Tensor&>())
+        .def("step", &Adam::step)
+        .def("regularization", &Adam::regularization)
+        .def("state", &Adam::state);
+    m.def("generate_rays", &generate_rays);
+    m.def("view_rays", &view_rays);
+    m.def("initialize_rays", &initialize_rays);
+    m.def("sample_uniforms", &sample_uniforms);
+    m.def("composite_and_resample", &composite_and_resample);
 }

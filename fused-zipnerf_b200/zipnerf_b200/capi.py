@@ -1,4 +1,4 @@
-"""ctypes binding of the C ABI in include/zf_featurize.h (libzf_featurize.so).
+"""ctypes binding of the C ABI in include/zf_featurize.h, zf_sampling.h and zf_optim.h (libzf_featurize.so).
 
 This is the binding a Python host without the PyTorch extension would write against the library. ``CFeaturizer``
 adds a thin convenience layer that takes PyTorch CUDA tensors and passes their device pointers; the computation
@@ -17,7 +17,9 @@ ZF_OK, ZF_ERROR_INVALID_ARGUMENT, ZF_ERROR_UNSUPPORTED, ZF_ERROR_CUDA = 0, 1, 2,
 EXPORTED = ['zf_featurizer_create', 'zf_featurizer_destroy', 'zf_featurizer_n_output_features', 'zf_featurizer_n_fp32_grad_rows',
             'zf_featurizer_n_rows', 'zf_featurizer_launches', 'zf_featurize_forward', 'zf_featurize_backward', 'zf_featurize_backward_mlp',
             'zf_featurize_backward_mlp_workspace_size', 'zf_featurize_backward_mlp_no_alloc', 'zf_featurize_debug',
-            'zf_check_erf_saturation', 'zf_erf_saturation_threshold', 'zf_last_error', 'zf_grid_max_value', 'zf_nerf_grid_grad_scale']
+            'zf_check_erf_saturation', 'zf_erf_saturation_threshold', 'zf_last_error', 'zf_grid_max_value', 'zf_nerf_grid_grad_scale',
+            'zf_direction_block_width', 'zf_initialize_rays', 'zf_view_rays', 'zf_generate_rays', 'zf_sample_uniforms',
+            'zf_composite_and_resample', 'zf_adam_create', 'zf_adam_destroy', 'zf_adam_step', 'zf_adam_state']
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -45,6 +47,39 @@ class zf_backward_mlp_args(ctypes.Structure):
                 ('grad_raw_density_numel', _i64), ('w0', _p), ('b0', _p), ('w1', _p), ('w0_numel', _i64), ('grad_table', _p),
                 ('grad_table_numel', _i64), ('grad_w0', _p), ('grad_w0_numel', _i64), ('grad_b0', _p), ('grad_w1', _p), ('grad_b1', _p),
                 ('workspace', _p), ('workspace_bytes', _i64)]
+
+
+class zf_ray_warp(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_float) for name in ('near', 'far', 'fn_near', 'fn_far', 'power', 'premult', 'y_max')]
+
+
+class zf_initialize_rays_args(ctypes.Structure):
+    _fields_ = [('seed', _i64), ('directions', _p), ('n_rays', _i64), ('direction_degree', ctypes.c_int), ('n_samples', ctypes.c_int),
+                ('warp', zf_ray_warp), ('encoded_directions', _p), ('sdist', _p), ('tdist', _p)]
+
+
+class zf_view_rays_args(ctypes.Structure):
+    _fields_ = [('pixel_indices', _p), ('n_rays', _i64), ('local_directions', _p), ('c2w', _p), ('radius', ctypes.c_float),
+                ('direction_degree', ctypes.c_int), ('n_samples', ctypes.c_int), ('warp', zf_ray_warp), ('origins', _p), ('directions', _p),
+                ('radii', _p), ('encoded_directions', _p), ('sdist', _p), ('tdist', _p)]
+
+
+class zf_generate_rays_args(ctypes.Structure):
+    _fields_ = [('seed', _i64), ('n_rays', _i64), ('view_offsets', _p), ('n_views', ctypes.c_int), ('view_cameras', _p), ('camera_offsets', _p),
+                ('local_directions', _p), ('c2w', _p), ('camera_radii', _p), ('pool_rgb', _p), ('n_pixels', _i64),
+                ('direction_degree', ctypes.c_int), ('n_samples', ctypes.c_int), ('warp', zf_ray_warp), ('origins', _p), ('directions', _p),
+                ('radii', _p), ('rgb', _p), ('encoded_directions', _p), ('sdist', _p), ('tdist', _p)]
+
+
+class zf_resample_args(ctypes.Structure):
+    _fields_ = [('raw_density', _p), ('sdist', _p), ('tdist', _p), ('directions', _p), ('n_rays', _i64), ('n_intervals', ctypes.c_int),
+                ('anneal', ctypes.c_float), ('n_samples', ctypes.c_int), ('seed', _i64), ('next_level', ctypes.c_int), ('warp', zf_ray_warp),
+                ('weights', _p), ('sdist_next', _p), ('tdist_next', _p)]
+
+
+class zf_adam_buffer(ctypes.Structure):
+    _fields_ = [('param', _p), ('grad', _p), ('grad_half', ctypes.c_int), ('numel', _i64), ('grad_scale', ctypes.c_double),
+                ('level_offsets', ctypes.POINTER(_i64)), ('n_level_offsets', ctypes.c_int)]
 
 
 class ZfError(RuntimeError):
@@ -95,6 +130,26 @@ def load() -> ctypes.CDLL:
     lib.zf_last_error.restype = ctypes.c_char_p
     lib.zf_grid_max_value.restype = ctypes.c_double
     lib.zf_nerf_grid_grad_scale.restype = ctypes.c_double
+    # zf_sampling.h
+    lib.zf_direction_block_width.argtypes = [ctypes.c_int]
+    lib.zf_direction_block_width.restype = _i64
+    lib.zf_initialize_rays.argtypes = [ctypes.POINTER(zf_initialize_rays_args), _p]
+    lib.zf_view_rays.argtypes = [ctypes.POINTER(zf_view_rays_args), _p]
+    lib.zf_generate_rays.argtypes = [ctypes.POINTER(zf_generate_rays_args), _p]
+    lib.zf_sample_uniforms.argtypes = [_i64, _i64, _i64, _p, _p]
+    lib.zf_composite_and_resample.argtypes = [ctypes.POINTER(zf_resample_args), _p]
+    for name in ['zf_initialize_rays', 'zf_view_rays', 'zf_generate_rays', 'zf_sample_uniforms', 'zf_composite_and_resample']:
+        getattr(lib, name).restype = ctypes.c_int
+    # zf_optim.h
+    lib.zf_adam_create.argtypes = [ctypes.POINTER(zf_adam_buffer), ctypes.c_int, ctypes.c_double, ctypes.c_double, ctypes.c_double,
+                                   ctypes.c_double, ctypes.c_double, _p, _i64, _p, ctypes.POINTER(_p)]
+    lib.zf_adam_create.restype = ctypes.c_int
+    lib.zf_adam_destroy.argtypes = [_p]
+    lib.zf_adam_destroy.restype = None
+    lib.zf_adam_step.argtypes = [_p, ctypes.c_double, _p]
+    lib.zf_adam_step.restype = ctypes.c_int
+    lib.zf_adam_state.argtypes = [_p, ctypes.c_int, ctypes.POINTER(_p), ctypes.POINTER(_p), ctypes.POINTER(_i64)]
+    lib.zf_adam_state.restype = ctypes.c_int
     _lib = lib
     return lib
 
@@ -210,3 +265,128 @@ class CFeaturizer:
                                         _stream(stream)))
         out['rows'] = out['rows'].to(torch.int64) & 0xFFFFFFFF
         return out
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# sampling and Adam through the C ABI, on PyTorch CUDA tensors (outputs allocated here, as the reference's wrappers do)
+
+def make_ray_warp(values) -> zf_ray_warp:
+    """The seven ray-warp constants of utils.ray_warp (near, far, fn(near), fn(far), power, premult, y_max)."""
+    if len(values) != 7:
+        raise ValueError('a ray warp has seven constants')
+    return zf_ray_warp(*[float(v) for v in values])
+
+
+def direction_block_width(degree: int) -> int:
+    return load().zf_direction_block_width(degree)
+
+
+def initialize_rays(seed: int, directions, degree: int, n_samples: int, warp, stream=None):
+    """zf_initialize_rays: (encoded_directions bf16 [R, W], sdist [R, n + 1], tdist [R, n + 1])."""
+    import torch
+    n_rays = directions.shape[0]
+    dev = directions.device
+    encoded = torch.empty(n_rays, direction_block_width(degree), dtype=torch.bfloat16, device=dev)
+    sdist = torch.empty(n_rays, n_samples + 1, device=dev)
+    tdist = torch.empty(n_rays, n_samples + 1, device=dev)
+    a = zf_initialize_rays_args(seed, _ptr(directions), n_rays, degree, n_samples, make_ray_warp(warp), _ptr(encoded), _ptr(sdist), _ptr(tdist))
+    check(load().zf_initialize_rays(ctypes.byref(a), _stream(stream)))
+    return encoded, sdist, tdist
+
+
+def view_rays(pixel_indices, local_directions, c2w, radius: float, degree: int, n_samples: int, warp, stream=None):
+    """zf_view_rays: (origins, directions, radii, encoded_directions, sdist, tdist)."""
+    import torch
+    n_rays = pixel_indices.numel()
+    dev = local_directions.device
+    origins, directions = torch.empty(n_rays, 3, device=dev), torch.empty(n_rays, 3, device=dev)
+    radii = torch.empty(n_rays, device=dev)
+    encoded = torch.empty(n_rays, direction_block_width(degree), dtype=torch.bfloat16, device=dev)
+    sdist, tdist = torch.empty(n_rays, n_samples + 1, device=dev), torch.empty(n_rays, n_samples + 1, device=dev)
+    a = zf_view_rays_args(_ptr(pixel_indices), n_rays, _ptr(local_directions), _ptr(c2w), radius, degree, n_samples, make_ray_warp(warp),
+                          _ptr(origins), _ptr(directions), _ptr(radii), _ptr(encoded), _ptr(sdist), _ptr(tdist))
+    check(load().zf_view_rays(ctypes.byref(a), _stream(stream)))
+    return origins, directions, radii, encoded, sdist, tdist
+
+
+def generate_rays(seed: int, n_rays: int, view_offsets, view_cameras, camera_offsets, local_directions, c2w, camera_radii, pool_rgb,
+                  degree: int, n_samples: int, warp, stream=None):
+    """zf_generate_rays: (origins, directions, radii, rgb, encoded_directions, sdist, tdist)."""
+    import torch
+    dev = local_directions.device
+    origins, directions, rgb = (torch.empty(n_rays, 3, device=dev) for _ in range(3))
+    radii = torch.empty(n_rays, device=dev)
+    encoded = torch.empty(n_rays, direction_block_width(degree), dtype=torch.bfloat16, device=dev)
+    sdist, tdist = torch.empty(n_rays, n_samples + 1, device=dev), torch.empty(n_rays, n_samples + 1, device=dev)
+    a = zf_generate_rays_args(seed, n_rays, _ptr(view_offsets), view_cameras.numel(), _ptr(view_cameras), _ptr(camera_offsets),
+                              _ptr(local_directions), _ptr(c2w), _ptr(camera_radii), _ptr(pool_rgb), pool_rgb.shape[0], degree, n_samples,
+                              make_ray_warp(warp), _ptr(origins), _ptr(directions), _ptr(radii), _ptr(rgb), _ptr(encoded), _ptr(sdist), _ptr(tdist))
+    check(load().zf_generate_rays(ctypes.byref(a), _stream(stream)))
+    return origins, directions, radii, rgb, encoded, sdist, tdist
+
+
+def sample_uniforms(seed: int, stream_index: int, n: int, device='cuda', stream=None):
+    import torch
+    values = torch.empty(n, device=device)
+    check(load().zf_sample_uniforms(seed, stream_index, n, _ptr(values), _stream(stream)))
+    return values
+
+
+def composite_and_resample(raw_density, sdist, tdist, directions, anneal: float, n_samples: int, seed: int, next_level: int, warp,
+                           with_weights: bool = True, stream=None):
+    """zf_composite_and_resample: (weights [R, n] or None, sdist_next [R, m + 1], tdist_next [R, m + 1])."""
+    import torch
+    n_rays, n_intervals = raw_density.shape
+    dev = raw_density.device
+    weights = torch.empty_like(raw_density) if with_weights else None
+    sdist_next, tdist_next = torch.empty(n_rays, n_samples + 1, device=dev), torch.empty(n_rays, n_samples + 1, device=dev)
+    a = zf_resample_args(_ptr(raw_density), _ptr(sdist), _ptr(tdist), _ptr(directions), n_rays, n_intervals, anneal, n_samples, seed,
+                         next_level, make_ray_warp(warp), _ptr(weights), _ptr(sdist_next), _ptr(tdist_next))
+    check(load().zf_composite_and_resample(ctypes.byref(a), _stream(stream)))
+    return weights, sdist_next, tdist_next
+
+
+class CAdam:
+    """A zf_adam over PyTorch CUDA tensors (params float32; grads float32 or float16), with the reference Adam's
+    arguments (optimizer_api.h:14-24); keeps the tensors alive."""
+
+    def __init__(self, params, grads, grad_scales, level_offsets, reg_weight, max_value, beta1, beta2, eps, magnitudes) -> None:
+        import torch
+        lib = load()
+        self.tensors = (list(params), list(grads), magnitudes)
+        self.regularization = torch.zeros((), device=params[0].device)
+        self._offsets = [(_i64 * len(o))(*o) for o in level_offsets]
+        buffers = (zf_adam_buffer * len(params))(*[
+            zf_adam_buffer(p.data_ptr(), g.data_ptr(), 1 if g.dtype == torch.float16 else 0, p.numel(), s, self._offsets[i], len(level_offsets[i]))
+            for i, (p, g, s) in enumerate(zip(params, grads, grad_scales))])
+        handle = _p()
+        check(lib.zf_adam_create(buffers, len(params), reg_weight, max_value, beta1, beta2, eps, _ptr(magnitudes), magnitudes.numel(),
+                                 self.regularization.data_ptr(), ctypes.byref(handle)))
+        self.handle = handle
+
+    def __del__(self) -> None:
+        if getattr(self, 'handle', None):
+            load().zf_adam_destroy(self.handle)
+            self.handle = None
+
+    def step(self, lr: float, stream=None) -> None:
+        check(load().zf_adam_step(self.handle, lr, _stream(stream)))
+
+    def state(self, buffer: int):
+        """(exp_avg, exp_avg_sq, steps): copies of one buffer's moments and the steps taken."""
+        import torch
+        m, v, steps = _p(), _p(), _i64()
+        check(load().zf_adam_state(self.handle, buffer, ctypes.byref(m), ctypes.byref(v), ctypes.byref(steps)))
+        n = self.tensors[0][buffer].numel()
+        device = self.tensors[0][buffer].device
+        return _device_floats(m.value, n, device).clone(), _device_floats(v.value, n, device).clone(), steps.value
+
+
+def _device_floats(address: int, n: int, device):
+    """A float32 tensor view of n floats of device memory at address (not owned)."""
+    import torch
+
+    class _View:
+        __cuda_array_interface__ = {'shape': (n,), 'typestr': '<f4', 'data': (address, False), 'version': 3}
+
+    return torch.as_tensor(_View(), device=device)

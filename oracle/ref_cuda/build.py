@@ -1,10 +1,11 @@
-"""Compiles the reference's featurization kernels ahead of time for the GPU checks (TEST INFRASTRUCTURE ONLY).
+"""Compiles the reference's CUDA kernels ahead of time for the GPU checks (TEST INFRASTRUCTURE ONLY).
 
 For each layout variant below this writes the preamble that the reference's host code generates before runtime
 compilation (featurizer.cu:157-184: JIT_* constants and the per-level layout functions; written here by this script
 from the layout, not copied) and compiles oracle/ref_cuda/ref_cuda.cu with the reference's kernel sources included
 from where they lie, with the reference's compile options (--use_fast_math, rtc_kernel.cu:49), for sm_100a, into
-oracle/_ref/cuda/libzfref_<variant>.so. Needs the reference sources (their root in the REFERENCE_ROOT environment
+oracle/_ref/cuda/libzfref_<variant>.so. It also compiles the reference's sampling and Adam kernels with the launchers of
+oracle/ref_cuda/ref_sampling.cu into oracle/_ref/cuda/libzfref_sampling.so. Needs the reference sources (their root in the REFERENCE_ROOT environment
 variable when not at the default mount); the built libraries are shipped with the rest of oracle/_ref.
 
     python oracle/ref_cuda/build.py [--jobs N]
@@ -99,6 +100,26 @@ def build_variant(name: str, layout) -> Path:
     return target
 
 
+def build_sampling() -> Path:
+    """The reference's sampling and Adam kernels (sampling_api.cu, optimizer_api.cu) with the launchers of
+    ref_sampling.cu, against the placeholder torch headers of torch_stub/, with the reference's nvcc options
+    (setup.py:28-34) for sm_100a -> libzfref_sampling.so."""
+    target = OUT / 'libzfref_sampling.so'
+    sources = ([HERE / 'ref_sampling.cu'] + sorted((HERE / 'torch_stub').rglob('*.h')) + sorted((BACKEND / 'sampling').rglob('*'))
+               + sorted((BACKEND / 'optimizer').rglob('*')) + sorted((BACKEND / 'common' / 'include').glob('*')))
+    if target.exists() and all(s.stat().st_mtime <= target.stat().st_mtime for s in sources if s.is_file()):
+        return target
+    cmd = [NVCC, '-gencode', 'arch=compute_100a,code=sm_100a', '-O3', '--use_fast_math', '-std=c++17', '--expt-relaxed-constexpr', '-lineinfo',
+           '-shared', '-Xcompiler', '-fPIC', '-Xcompiler', '-fvisibility=hidden', f'-I{HERE / "torch_stub"}',
+           *[f'-I{BACKEND / sub}' for sub in ('sampling/include', 'sampling/src', 'optimizer/include', 'optimizer/src', 'common/include')],
+           str(HERE / 'ref_sampling.cu'), '-o', str(target)]
+    result = subprocess.run(cmd, capture_output=True, text=True)
+    if result.returncode != 0:
+        sys.stderr.write(result.stdout + result.stderr)
+        raise RuntimeError('compiling the reference sampling kernels failed')
+    return target
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument('--jobs', type=int, default=os.cpu_count())
@@ -108,11 +129,12 @@ def main() -> None:
     OUT.mkdir(parents=True, exist_ok=True)
     layouts = variants()
     with concurrent.futures.ThreadPoolExecutor(max_workers=args.jobs) as pool:
-        for future in [pool.submit(build_variant, name, layout) for name, layout in layouts.items()]:
+        futures = [pool.submit(build_variant, name, layout) for name, layout in layouts.items()] + [pool.submit(build_sampling)]
+        for future in futures:
             future.result()
     (OUT / 'variants.json').write_text(json.dumps({name: dict(zip(['level', 'sizes', 'entries', 'n_features', 'mlp_width'], layout))
                                                    for name, layout in layouts.items()}, indent=1))
-    print(f'built {len(layouts)} reference kernel variants into {OUT}')
+    print(f'built {len(layouts)} reference featurization variants and the sampling kernels into {OUT}')
 
 
 if __name__ == '__main__':

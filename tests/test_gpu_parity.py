@@ -180,6 +180,19 @@ def test_backward_mlp_matches_oracle(capi, cuda_device, oracle, name):
         np.testing.assert_allclose(a, b, rtol=0, atol=1e-4 * max(float(np.abs(b).max()), 1e-12), err_msg=key)
 
 
+def test_level_passes_of_the_benchmark_grids(capi, cuda_device):
+    """Grids larger than the L2 run their forward and backward as level passes (config 2's NeRF grid: 7 forward passes
+    of one 32 MB hashed table, 2 backward passes); the proposal grids fit and take one launch, their backward two (the
+    MLP kernel and the scatter)."""
+    from zipnerf_b200 import workloads
+    wl = workloads.config2(n_rays=32)
+    prop, nerf = wl.levels[0], wl.levels[2]
+    fp = capi.CFeaturizer(prop.level, prop.sizes, prop.entries, prop.n_features, prop.mlp_width)
+    fn = capi.CFeaturizer(nerf.level, nerf.sizes, nerf.entries, nerf.n_features, nerf.mlp_width)
+    assert [fp.launches(c) for c in ('forward', 'forward_mlp', 'backward', 'backward_mlp')] == [1, 1, 1, 2]
+    assert [fn.launches(c) for c in ('forward', 'forward_mlp', 'backward', 'backward_mlp')] == [7, 0, 2, 0]
+
+
 @pytest.mark.parametrize('n_levels', [7, 8])
 def test_mlp_weight_loads_are_bit_identical(capi, cuda_device, oracle, n_levels):
     """The fused MLP reads its weight rows as 16-byte words when w0 is 16-byte aligned and the MLP input width a multiple

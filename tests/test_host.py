@@ -1,6 +1,6 @@
-"""Host-side checks that need no GPU: the C-ABI library loads and exports every function include/zf_featurize.h
-declares, its constants and argument validation behave like the reference's, the PyTorch binding imports with the
-reference's module surface, and the workload generators produce the benchmark shapes."""
+"""Host-side checks that need no GPU: the C-ABI library loads and exports every function include/*.h declares, its
+constants and argument validation behave like the reference's, the PyTorch binding imports with the reference's
+module surface, and the workload generators produce the benchmark shapes."""
 from __future__ import annotations
 
 import ctypes
@@ -11,11 +11,11 @@ import pytest
 import torch
 
 REPO = Path(__file__).resolve().parent.parent
-HEADER = REPO / 'include' / 'zf_featurize.h'
+HEADERS = sorted((REPO / 'include').glob('*.h'))
 
 
 def declared_functions() -> list[str]:
-    text = HEADER.read_text()
+    text = '\n'.join(h.read_text() for h in HEADERS)
     return sorted(set(re.findall(r'ZF_API\s+[\w\s\*]+?\b(zf_\w+)\s*\(', text)))
 
 
@@ -24,13 +24,17 @@ def test_header_declares_the_reference_entry_points():
     for name in ['zf_featurizer_create', 'zf_featurizer_destroy', 'zf_featurizer_n_fp32_grad_rows', 'zf_featurize_forward',
                  'zf_featurize_backward', 'zf_featurize_backward_mlp', 'zf_last_error']:
         assert name in names
+    # sampling_api.h:10-58 and optimizer_api.h:14-40
+    for name in ['zf_generate_rays', 'zf_view_rays', 'zf_initialize_rays', 'zf_sample_uniforms', 'zf_composite_and_resample',
+                 'zf_adam_create', 'zf_adam_step', 'zf_adam_destroy']:
+        assert name in names
 
 
 def test_library_exports_every_declared_function():
     from zipnerf_b200 import capi
     lib = capi.load()
     for name in declared_functions():
-        assert hasattr(lib, name), f'{name} is declared in zf_featurize.h but not exported'
+        assert hasattr(lib, name), f'{name} is declared in include/ but not exported'
     assert sorted(capi.EXPORTED) == declared_functions()
 
 
@@ -63,6 +67,41 @@ def test_create_validates_layout_before_touching_a_device():
     assert lib.zf_featurizer_n_output_features(None) == 0
 
 
+def test_sampling_and_adam_validate_before_touching_a_device():
+    """The checks of sampling_api.cu:443-445 and optimizer_api.cu:123-155 come before any launch or allocation."""
+    from zipnerf_b200 import capi
+    lib = capi.load()
+    assert lib.zf_direction_block_width(4) == 32 and lib.zf_direction_block_width(0) == 8
+    warp = capi.make_ray_warp([0.2, 1000.0, 0.0, 1.0, -1.5, 2.0, 1.6])
+    for n_intervals, n_samples in [(64, 1), (64, 65), (1, 64), (65, 64)]:
+        a = capi.zf_resample_args(None, None, None, None, 4, n_intervals, 1.0, n_samples, 0, 1, warp, None, None, None)
+        assert lib.zf_composite_and_resample(ctypes.byref(a), None) == capi.ZF_ERROR_UNSUPPORTED
+        assert b'unsupported number of samples per level' in lib.zf_last_error()
+    empty = capi.zf_resample_args(None, None, None, None, 0, 64, 1.0, 64, 0, 1, warp, None, None, None)
+    assert lib.zf_composite_and_resample(ctypes.byref(empty), None) == capi.ZF_OK  # nothing to launch
+    init = capi.zf_initialize_rays_args(0, None, 0, 4, 64, warp, None, None, None)
+    assert lib.zf_initialize_rays(ctypes.byref(init), None) == capi.ZF_OK
+    init.n_rays = 3
+    assert lib.zf_initialize_rays(ctypes.byref(init), None) == capi.ZF_ERROR_INVALID_ARGUMENT
+    assert lib.zf_sample_uniforms(1, 2, 0, None, None) == capi.ZF_OK
+    assert lib.zf_sample_uniforms(1, 2, 5, None, None) == capi.ZF_ERROR_INVALID_ARGUMENT
+    handle = ctypes.c_void_p()
+    fake = 1 << 20  # never dereferenced: creation fails in validation
+    offsets = (ctypes.c_int64 * 3)(0, 6, 16)
+    buf = capi.zf_adam_buffer(fake, fake, 0, 16, 1.0, offsets, 3)
+    assert lib.zf_adam_create(ctypes.byref(buf), 1, 0.1, 1e-5, 0.9, 0.99, 1e-15, fake, 2, fake, ctypes.byref(handle)) == capi.ZF_ERROR_INVALID_ARGUMENT
+    assert b'invalid level offsets' in lib.zf_last_error()
+    buf.level_offsets, buf.n_level_offsets = (ctypes.c_int64 * 3)(0, 8, 12), 3
+    assert lib.zf_adam_create(ctypes.byref(buf), 1, 0.1, 1e-5, 0.9, 0.99, 1e-15, fake, 2, fake, ctypes.byref(handle)) == capi.ZF_ERROR_INVALID_ARGUMENT
+    assert b'level offsets must cover the buffer' in lib.zf_last_error()
+    buf.level_offsets, buf.n_level_offsets = (ctypes.c_int64 * 3)(0, 8, 16), 3
+    assert lib.zf_adam_create(ctypes.byref(buf), 1, 0.1, 1e-5, 0.9, 0.99, 1e-15, fake, 1, fake, ctypes.byref(handle)) == capi.ZF_ERROR_INVALID_ARGUMENT
+    assert b'one entry per level' in lib.zf_last_error()
+    assert lib.zf_adam_create(ctypes.byref(buf), 9, 0.1, 1e-5, 0.9, 0.99, 1e-15, fake, 2, fake, ctypes.byref(handle)) == capi.ZF_ERROR_INVALID_ARGUMENT
+    assert b'invalid optimizer buffers' in lib.zf_last_error()
+    assert lib.zf_adam_step(None, 0.1, None) == capi.ZF_ERROR_INVALID_ARGUMENT
+
+
 @pytest.mark.skipif(torch.cuda.is_available(), reason='checks the error path of a machine without a GPU')
 def test_create_without_device_reports_cuda_error():
     from zipnerf_b200 import capi
@@ -80,6 +119,9 @@ def test_torch_binding_has_the_reference_surface():
     _C.set_rtc_dirs('/nonexistent/cache', '/nonexistent/kernels')  # accepted and unused (kernels are compiled ahead of time)
     for method in ['forward', 'backward', 'backward_mlp']:
         assert hasattr(_C.Featurizer, method)
+    for name in ['generate_rays', 'view_rays', 'initialize_rays', 'sample_uniforms', 'composite_and_resample', 'Adam']:
+        assert getattr(ZipNeRFCudaBackend, name) is getattr(_C, name) is getattr(pipeline, name)
+    assert hasattr(_C.Adam, 'step') and hasattr(_C.Adam, 'regularization')
     assert isinstance(_C.Featurizer.n_fp32_grad_rows, property)
     assert pipeline.Featurizer is _C.Featurizer
     with pytest.raises(AttributeError, match='not part of the B200 featurization backend'):
