@@ -6,6 +6,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <climits>
 #include <string>
 
@@ -44,7 +45,8 @@ int launch(void (*kernel)(Args), const unsigned grid, const unsigned block, cons
 
 int launch_new_rays(const zf::NewRaysArgs& a, cudaStream_t stream) {
     if (a.n_rays == 0) return ZF_OK;
-    return launch(zf::fz_new_rays_kernel, ray_blocks(a.n_rays), zf::kSamplingRays, sizeof(float) * zf::new_rays_smem_floats(a.n_samples), stream, a);
+    return launch(zf::fz_new_rays_kernel, ray_blocks(a.n_rays), zf::kSamplingRays, zf::new_rays_smem_bytes(a.n_samples, zf::direction_block_width(a.degree)),
+                  stream, a);
 }
 
 }  // namespace

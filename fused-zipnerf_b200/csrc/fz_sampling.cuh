@@ -55,15 +55,37 @@ __device__ __forceinline__ float activate_density(const float raw) { return expf
 // smem row stride of a block's per-ray rows: odd (a warp's column walk hits 32 distinct banks), >= cols
 __host__ __device__ constexpr int sampling_stride(const int cols) { return cols | 1; }
 
-// rows [ray0, ray0 + n_rows) of a row-major [*, cols] float matrix -> shared rows of `stride` floats; the warp copies
-// one row at a time with the lanes along its columns (coalesced)
-__device__ __forceinline__ void load_rows(const float* __restrict__ src, const int64_t ray0, const int n_rows, const int cols, float* dst, const int stride) {
+// |v| (sampling_api.cu:37)
+__device__ __forceinline__ float norm3(const float3 v) { return sqrtf(v.x * v.x + v.y * v.y + v.z * v.z); }
+
+// rows [ray0, ray0 + n_rows) of a row-major [*, cols] float matrix -> shared rows of `stride` floats, as asynchronous
+// 4-byte copies (cp.async): the warp walks the block's contiguous chunk element by element (coalesced), every copy is
+// in flight at once, and the caller waits for all of them (wait_async_rows) before the rows are read. A block's chunk
+// is a few KB, so that many copies in flight per warp is what keeps the HBM busy at this kernel's low occupancy.
+__device__ __forceinline__ void load_rows_async(const float* __restrict__ src, const int64_t ray0, const int n_rows, const int cols, float* dst,
+                                                const int stride) {
     const int lane = threadIdx.x & 31;
     const float* base = src + ray0 * cols;
-#pragma unroll 4
-    for (int r = 0; r < n_rows; r++) {
-        for (int c = lane; c < cols; c += 32) dst[r * stride + c] = __ldg(base + static_cast<int64_t>(r) * cols + c);
+    const int total = n_rows * cols;
+    const uint32_t dst_base = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+    int row = 0, col = lane;
+    while (col >= cols) {
+        col -= cols;
+        row++;
     }
+    for (int e = lane; e < total; e += 32) {
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst_base + 4u * static_cast<uint32_t>(row * stride + col)), "l"(base + e) : "memory");
+        col += 32;
+        while (col >= cols) {
+            col -= cols;
+            row++;
+        }
+    }
+}
+
+__device__ __forceinline__ void wait_async_rows() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncwarp();
 }
 
 __device__ __forceinline__ void store_rows(const float* src, const int stride, const int n_rows, const int cols, float* __restrict__ dst, const int64_t ray0) {
@@ -168,19 +190,20 @@ __global__ void __launch_bounds__(kSamplingRays) fz_composite_and_resample_kerne
     const int64_t ray0 = static_cast<int64_t>(blockIdx.x) * kSamplingRays;
     const int n_rows = static_cast<int>(min(static_cast<int64_t>(kSamplingRays), a.n_rays - ray0));
     const int n = a.n, n_out = a.n_out;
-    load_rows(a.raw_density, ray0, n_rows, n, rows_a, stride);
-    load_rows(a.sdist, ray0, n_rows, n + 1, rows_s, stride);
-    load_rows(a.tdist, ray0, n_rows, n + 1, rows_t, stride);
-    __syncwarp();
+    load_rows_async(a.raw_density, ray0, n_rows, n, rows_a, stride);
+    load_rows_async(a.sdist, ray0, n_rows, n + 1, rows_s, stride);
+    load_rows_async(a.tdist, ray0, n_rows, n + 1, rows_t, stride);
     const bool active = lane < n_rows;
     const int64_t ray = ray0 + lane;
+    float direction_norm = 0.0f;
+    if (active) direction_norm = norm3(make_float3(a.directions[3 * ray], a.directions[3 * ray + 1], a.directions[3 * ray + 2]));
+    wait_async_rows();
     float* row_a = rows_a + lane * stride;
     float* row_t = rows_t + lane * stride;
     if (active) {
         // alpha compositing (ray_ops.cuh:91-99): w_i = (1 - exp(-x_i)) exp(-sum_{j<i} x_j), x_i = sigma_i dt_i |d|
-        const float dx = a.directions[3 * ray], dy = a.directions[3 * ray + 1], dz = a.directions[3 * ray + 2];
-        const float direction_norm = sqrtf(dx * dx + dy * dy + dz * dz);
         float optical_depth = 0.0f;
+#pragma unroll 4
         for (int i = 0; i < n; i++) {
             const float x = activate_density(row_a[i]) * (row_t[i + 1] - row_t[i]) * direction_norm;
             row_a[i] = -expm1f(-x) * expf(-optical_depth);
@@ -247,35 +270,51 @@ struct NewRaysArgs {
     RayWarp warp;
 };
 
-__host__ __device__ constexpr int new_rays_smem_floats(const int n_samples) { return kSamplingRays * sampling_stride(n_samples + 1); }
-
-// world-space direction of a camera-space direction (c2w row-major 3 x 4, sampling_api.cu:65-67)
-__device__ __forceinline__ float3 world_direction(const float* m, const float lx, const float ly, const float lz) {
-    return make_float3(m[0] * lx + m[1] * ly + m[2] * lz, m[4] * lx + m[5] * ly + m[6] * lz, m[8] * lx + m[9] * ly + m[10] * lz);
+// shared memory of a block: the rays' new edges (floats), then their encodings (bf16 rows of 16-byte multiples)
+__host__ __device__ constexpr int encoded_stride(const int width) { return width + 8; }
+__host__ __device__ constexpr int new_rays_smem_bytes(const int n_samples, const int width) {
+    return 4 * kSamplingRays * sampling_stride(n_samples + 1) + 2 * kSamplingRays * encoded_stride(width);
 }
 
-// encoded direction element e of unit direction v (sampling_api.cu:45-56): v, then sin(2^k v), then cos(2^k v) for
-// octaves k and axes c (index 3 + 3 k + c), zeros beyond
-__device__ __forceinline__ float encoded_element(const float v[3], const int e, const int degree) {
-    if (e < 3) return v[e];
-    const int trig = e - 3;
-    if (trig >= 6 * degree) return 0.0f;
-    const bool cosine = trig >= 3 * degree;
-    const int kc = cosine ? trig - 3 * degree : trig;
-    const int k = kc / 3, c = kc - 3 * k;
-    float sin_value, cos_value;
-    sincosf(scalbnf(v[c], k), &sin_value, &cos_value);
-    return cosine ? cos_value : sin_value;
+// world-space direction of a camera-space direction (c2w row-major 3 x 4, sampling_api.cu:65-67)
+__device__ __forceinline__ float3 world_direction(const float* m, const float3 local) {
+    return make_float3(m[0] * local.x + m[1] * local.y + m[2] * local.z, m[4] * local.x + m[5] * local.y + m[6] * local.z,
+                       m[8] * local.x + m[9] * local.y + m[10] * local.z);
+}
+
+// the view-direction encoding of one ray into a shared row (sampling_api.cu:44-56): the unit direction v, then
+// sin(2^k v) at 3 + 3 k + c and cos(2^k v) at 3 + 3 (degree + k) + c for octaves k and axes c, zeros elsewhere
+__device__ __forceinline__ void encode_direction(const float3 d, const int degree, const int width, uint16_t* encoded) {
+    // 1 / |d| with the roundings of the reference build (its 1.0f / norm3(d) under fast math): a reciprocal square root
+    // of (x x + y y) + z z fused as written here. The compiler contracts the plain expression differently from one
+    // kernel to another (1 ulp on ~1 ray in 2000, visible in the bf16 sines); this form matched the reference kernels
+    // on every one of 170,000 directions in a black-box comparison on the B200.
+    const float inv_norm = rsqrtf(__fmaf_rn(d.z, d.z, __fmaf_rn(d.x, d.x, __fmul_rn(d.y, d.y))));
+    const float v[3] = {d.x * inv_norm, d.y * inv_norm, d.z * inv_norm};
+    for (int i = 0; i < width; i++) encoded[i] = f32_to_bf16_bits(0.0f);
+    for (int c = 0; c < 3; c++) {
+        encoded[c] = f32_to_bf16_bits(v[c]);
+        for (int k = 0; k < degree; k++) {
+            float sin_value, cos_value;
+            sincosf(scalbnf(v[c], k), &sin_value, &cos_value);
+            encoded[3 + 3 * k + c] = f32_to_bf16_bits(sin_value);
+            encoded[3 + 3 * (degree + k) + c] = f32_to_bf16_bits(cos_value);
+        }
+    }
 }
 
 __global__ void __launch_bounds__(kSamplingRays) fz_new_rays_kernel(const __grid_constant__ NewRaysArgs a) {
-    extern __shared__ float smem[];
+    extern __shared__ __align__(16) float smem[];
     const int stride = sampling_stride(a.n_samples + 1);
+    const int width = direction_block_width(a.degree);
+    const int enc_stride = encoded_stride(width);
+    uint16_t* enc_rows = reinterpret_cast<uint16_t*>(smem + kSamplingRays * stride);
     const int lane = threadIdx.x;
     const int64_t ray0 = static_cast<int64_t>(blockIdx.x) * kSamplingRays;
     const int n_rows = static_cast<int>(min(static_cast<int64_t>(kSamplingRays), a.n_rays - ray0));
     const int64_t ray = ray0 + lane;
     float* row = smem + lane * stride;
+    uint16_t* enc = enc_rows + lane * enc_stride;
     if (lane < n_rows) {
         float3 d;
         float jitter = -1.0f;
@@ -307,7 +346,7 @@ __global__ void __launch_bounds__(kSamplingRays) fz_new_rays_kernel(const __grid
                 for (int c = 0; c < 3; c++) a.rgb[3 * ray + c] = a.pool_rgb[3 * pixel + c] / 255.0f;
                 jitter = rng_uniform(seed, kStreamJitter, ray);
             }
-            d = world_direction(m, local[0], local[1], local[2]);
+            d = world_direction(m, make_float3(local[0], local[1], local[2]));
             a.origins[3 * ray] = m[3];
             a.origins[3 * ray + 1] = m[7];
             a.origins[3 * ray + 2] = m[11];
@@ -316,29 +355,20 @@ __global__ void __launch_bounds__(kSamplingRays) fz_new_rays_kernel(const __grid
             a.directions[3 * ray + 2] = d.z;
             a.radii[ray] = radius;
         }
-        // view-direction encoding of the unit direction, one 16-byte row chunk (8 values) at a time
-        const float inv_norm = 1.0f / sqrtf(d.x * d.x + d.y * d.y + d.z * d.z);
-        const float v[3] = {d.x * inv_norm, d.y * inv_norm, d.z * inv_norm};
-        const int width = direction_block_width(a.degree);
-        uint16_t* encoded = a.encoded_directions + ray * width;
-        for (int e0 = 0; e0 < width; e0 += 8) {
-            uint32_t words[4];
-            for (int q = 0; q < 4; q++) {
-                words[q] = static_cast<uint32_t>(f32_to_bf16_bits(encoded_element(v, e0 + 2 * q, a.degree)))
-                           | static_cast<uint32_t>(f32_to_bf16_bits(encoded_element(v, e0 + 2 * q + 1, a.degree))) << 16;
-            }
-            if (a.encoded_vectors) {
-                *reinterpret_cast<uint4*>(encoded + e0) = make_uint4(words[0], words[1], words[2], words[3]);
-            } else {
-                for (int q = 0; q < 4; q++) {
-                    encoded[e0 + 2 * q] = static_cast<uint16_t>(words[q] & 0xffffu);
-                    encoded[e0 + 2 * q + 1] = static_cast<uint16_t>(words[q] >> 16);
-                }
-            }
-        }
+        encode_direction(d, a.degree, width, enc);
         // the first level samples the single unit bin [0, 1] (sampling_api.cu:57-61)
         float unit_edges[2] = {0.0f, 1.0f}, unit_weight[1] = {1.0f}, work[2];
         resample_ray(unit_edges, unit_weight, 1, 1.0f, a.n_samples, jitter, work, row);
+        // the encoding row leaves as 16-byte chunks (widths are multiples of 8 values)
+        uint16_t* out = a.encoded_directions + ray * width;
+        for (int e0 = 0; e0 < width; e0 += 8) {
+            const uint4 chunk = *reinterpret_cast<const uint4*>(enc + e0);
+            if (a.encoded_vectors) {
+                *reinterpret_cast<uint4*>(out + e0) = chunk;
+            } else {
+                for (int q = 0; q < 8; q++) out[e0 + q] = enc[e0 + q];
+            }
+        }
     }
     __syncwarp();
     store_rows(smem, stride, n_rows, a.n_samples + 1, a.sdist, ray0);
