@@ -450,8 +450,8 @@ def run_b200(args) -> None:
 def measure_rows(device, iters: int = 10) -> dict:
     """The per-step kernels around the featurization, each timed alone through the C ABI on config-2-sized inputs after
     an L2 flush (zipnerf_b200/rows.py): the two composite-and-resample calls of a training step (proposal level 0 -> 64
-    intervals, level 1 -> 32), the training rays of a step drawn from a 185-view pool, and the Adam step over the
-    reference model's optimizer buffers (77.5 M parameters). Achieved bandwidth = algorithmic bytes / median time,
+    intervals, level 1 -> 32), the training rays of a step drawn from a 185-view pool, the final level's losses and
+    gradients, and the Adam step over the reference model's optimizer buffers (77.5 M parameters). Achieved bandwidth = algorithmic bytes / median time,
     against the measured HBM peak."""
     import ctypes
     import ZipNeRFCudaBackend as backend
@@ -491,6 +491,18 @@ def measure_rows(device, iters: int = 10) -> dict:
     ms = timer(lambda: capi.check(lib.zf_generate_rays(ctypes.byref(ga), stream)), iters)
     out['generate_rays'] = entry([ms], R * rows.new_rays_bytes(64, width), f'{R} rays from 185 views of 1296 x 840 pixels, 64 first-level intervals')
     del pool
+    fin = rows.final_inputs(device)
+    proposal_grads = [torch.empty_like(p['raw_density']) for p in fin['proposals']]
+    levels = (capi.zf_proposal_level * 2)(*[capi.zf_proposal_level(p['raw_density'].shape[1], p['raw_density'].data_ptr(), p['sdist'].data_ptr(),
+                                                                    p['tdist'].data_ptr(), p['weights'].data_ptr(), g.data_ptr(), p['interlevel_weight'],
+                                                                    p['interlevel_blur']) for p, g in zip(fin['proposals'], proposal_grads)])
+    out_grad, loss_sums = torch.empty_like(fin['nerf_outputs']), torch.zeros(4, device=device)
+    fa = capi.zf_train_final_args(fin['nerf_outputs'].data_ptr(), fin['sdist'].data_ptr(), fin['tdist'].data_ptr(), R, 32, levels, 2,
+                                  fin['directions'].data_ptr(), fin['seed'], fin['rgb_target'].data_ptr(), *rows.LOSS_ARGS, out_grad.data_ptr(),
+                                  loss_sums.data_ptr())
+    ms = timer(lambda: capi.check(lib.zf_train_final(ctypes.byref(fa), stream)), iters)
+    out['train_final'] = entry([ms], R * rows.final_bytes(), f'{R} rays: final level of 32 intervals, proposal levels of 64 and 64')
+    del fin, proposal_grads
     layout, params, grads, n_levels = rows.adam_inputs(device)
     mags = torch.zeros(n_levels, device=device)
     opt = backend.Adam(params, grads, [b['scale'] for b in layout], [b['offsets'] for b in layout], 0.1, 1e-5, 0.9, 0.99, 1e-15, mags)

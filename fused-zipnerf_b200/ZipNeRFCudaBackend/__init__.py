@@ -4,9 +4,9 @@ The compiled module ``ZipNeRFCudaBackend._C`` (PyTorch binding) and ``libzf_feat
 this directory; build them with ``python fused-zipnerf_b200/build.py``. The featurization entry points mirror the
 reference binding (ZipNeRFCudaBackend/ZipNeRFCudaBackend/torch_bindings/bindings.cu:14-22): ``grid_max_value``,
 ``nerf_grid_grad_scale``, ``set_rtc_dirs`` and ``Featurizer``; the sampling functions ``generate_rays``, ``view_rays``,
-``initialize_rays``, ``sample_uniforms`` and ``composite_and_resample`` (sampling_api.h:10-58); and ``Adam``
-(optimizer_api.h:14-40). The reference's NeRF MLP (``NerfMlp``, ``nerf_mlp_parameters``) and its final-level kernels
-(``train_final``, ``composite_final``) are not provided here; accessing them raises an ``AttributeError`` that says so.
+``initialize_rays``, ``sample_uniforms``, ``composite_and_resample``, ``train_final`` and ``composite_final``
+(sampling_api.h:10-90); and ``Adam`` (optimizer_api.h:14-40). The reference's NeRF MLP (``NerfMlp``,
+``nerf_mlp_parameters``) is not provided here; accessing it raises an ``AttributeError`` that says so.
 """
 from __future__ import annotations
 
@@ -30,15 +30,17 @@ view_rays = _C.view_rays
 initialize_rays = _C.initialize_rays
 sample_uniforms = _C.sample_uniforms
 composite_and_resample = _C.composite_and_resample
+train_final = _C.train_final
+composite_final = _C.composite_final
 
-_OTHER_SUBSYSTEMS = {'nerf_mlp_parameters', 'NerfMlp', 'train_final', 'composite_final'}
+_OTHER_SUBSYSTEMS = {'nerf_mlp_parameters', 'NerfMlp'}
 
 __all__ = ['grid_max_value', 'nerf_grid_grad_scale', 'Featurizer', 'set_rtc_dirs', 'Adam', 'generate_rays', 'view_rays', 'initialize_rays',
-           'sample_uniforms', 'composite_and_resample']
+           'sample_uniforms', 'composite_and_resample', 'train_final', 'composite_final']
 
 
 def __getattr__(name: str):
     if name in _OTHER_SUBSYSTEMS:
         raise AttributeError(f'ZipNeRFCudaBackend.{name} is not part of the B200 featurization backend; it belongs to the reference '
-                             f"backend's NeRF MLP / final-level compositing subsystems")
+                             f"backend's NeRF MLP subsystem")
     raise AttributeError(f'module ZipNeRFCudaBackend has no attribute {name}')

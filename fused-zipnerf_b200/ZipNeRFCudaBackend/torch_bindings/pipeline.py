@@ -1,6 +1,6 @@
 """Re-exports of the backend's entry points under the reference's module path
 (ZipNeRFCudaBackend/ZipNeRFCudaBackend/torch_bindings/pipeline.py:1-15): featurization, sampling and Adam. The
-reference's NeRF MLP and final-level kernels are not part of this backend."""
+reference's NeRF MLP is not part of this backend."""
 from ZipNeRFCudaBackend import _C
 
 grid_max_value = _C.grid_max_value
@@ -13,3 +13,5 @@ view_rays = _C.view_rays
 initialize_rays = _C.initialize_rays
 sample_uniforms = _C.sample_uniforms
 composite_and_resample = _C.composite_and_resample
+train_final = _C.train_final
+composite_final = _C.composite_final

@@ -1,6 +1,8 @@
 // fz_sampling.cu -- the C ABI of include/zf_sampling.h: argument validation (the checks of the reference's
-// sampling_api.cu:426-578 that do not concern torch dtypes or contiguity) and launches of the fz_sampling.cuh kernels.
+// sampling_api.cu:426-678 that do not concern torch dtypes or contiguity) and launches of the fz_sampling.cuh and
+// fz_final.cuh kernels.
 #include "zf_sampling.h"
+#include "fz_final.cuh"
 #include "fz_sampling.cuh"
 #include "fz_status.h"
 
@@ -191,4 +193,77 @@ int zf_composite_and_resample(const zf_resample_args* args, cudaStream_t stream)
     a.warp = ray_warp(args->warp);
     return launch(zf::fz_composite_and_resample_kernel, ray_blocks(a.n_rays), zf::kSamplingRays,
                   sizeof(float) * zf::resample_smem_floats(a.n, a.n_out), stream, a);
+}
+
+int zf_train_final(const zf_train_final_args* args, cudaStream_t stream) {
+    if (args == nullptr) return zf::set_error(ZF_ERROR_INVALID_ARGUMENT, "null arguments");
+    int status = check_n_intervals(args->n_intervals);
+    if (status == ZF_OK) status = check_rays(args->n_rays);
+    if (status != ZF_OK) return status;
+    if (args->n_proposal_levels < 0 || args->n_proposal_levels > zf::kMaxProposalLevels || (args->n_proposal_levels > 0 && args->proposals == nullptr)) {
+        return zf::set_error(ZF_ERROR_INVALID_ARGUMENT, "inconsistent proposal levels");
+    }
+    zf::TrainFinalArgs a{};
+    for (int level = 0; level < args->n_proposal_levels; level++) {
+        const zf_proposal_level& p = args->proposals[level];
+        status = check_n_intervals(p.n_intervals);
+        if (status != ZF_OK) return status;
+        if (args->n_rays > 0 && (!p.raw_density || !p.sdist || !p.tdist || !p.weights || !p.raw_density_grad)) {
+            return zf::set_error(ZF_ERROR_INVALID_ARGUMENT, "train_final: null proposal tensor");
+        }
+        a.proposals.n_intervals[level] = p.n_intervals;
+        a.proposals.raw_density[level] = p.raw_density;
+        a.proposals.sdist[level] = p.sdist;
+        a.proposals.tdist[level] = p.tdist;
+        a.proposals.weights[level] = p.weights;
+        a.proposals.raw_density_grad[level] = p.raw_density_grad;
+        a.proposals.interlevel_weight[level] = p.interlevel_weight;
+        a.proposals.interlevel_blur[level] = p.interlevel_blur;
+    }
+    a.proposals.n_levels = args->n_proposal_levels;
+    if (args->n_rays == 0) return ZF_OK;
+    if (!args->nerf_outputs || !args->sdist || !args->tdist || !args->directions || !args->rgb_target || !args->nerf_outputs_grad) {
+        return zf::set_error(ZF_ERROR_INVALID_ARGUMENT, "train_final: null tensor");
+    }
+    a.nerf_outputs = args->nerf_outputs;
+    a.sdist = args->sdist;
+    a.tdist = args->tdist;
+    a.directions = args->directions;
+    a.seed = static_cast<unsigned long long>(args->seed);
+    a.rgb_target = args->rgb_target;
+    a.nerf_outputs_grad = args->nerf_outputs_grad;
+    a.loss_sums = args->loss_sums;
+    a.n = args->n_intervals;
+    a.charbonnier_padding = args->charbonnier_padding;
+    a.distortion_weight = args->distortion_weight;
+    a.distortion_power = args->distortion_power;
+    a.distortion_premult = args->distortion_premult;
+    a.n_rays = static_cast<int>(args->n_rays);
+    a.vectors = reinterpret_cast<uintptr_t>(args->nerf_outputs) % 8 == 0 && aligned16(args->nerf_outputs_grad);
+    return launch(zf::fz_train_final_kernel, ray_blocks(args->n_rays), 32, 0, stream, a);
+}
+
+int zf_composite_final(const zf_composite_final_args* args, cudaStream_t stream) {
+    if (args == nullptr) return zf::set_error(ZF_ERROR_INVALID_ARGUMENT, "null arguments");
+    int status = check_n_intervals(args->n_intervals);
+    if (status == ZF_OK) status = check_rays(args->n_rays);
+    if (status != ZF_OK) return status;
+    if (args->n_rays == 0) return ZF_OK;
+    if (!args->nerf_outputs || !args->tdist || !args->directions || !args->background || !args->pixel_indices || !args->rgb) {
+        return zf::set_error(ZF_ERROR_INVALID_ARGUMENT, "composite_final: null tensor");
+    }
+    zf::CompositeFinalArgs a{};
+    a.nerf_outputs = args->nerf_outputs;
+    a.tdist = args->tdist;
+    a.directions = args->directions;
+    a.background = args->background;
+    a.pixel_indices = args->pixel_indices;
+    a.rgb = args->rgb;
+    a.alpha = args->alpha;
+    a.depth = args->depth;
+    a.n = args->n_intervals;
+    a.n_rays = static_cast<int>(args->n_rays);
+    a.use_median_depth = args->use_median_depth;
+    a.vectors = reinterpret_cast<uintptr_t>(args->nerf_outputs) % 8 == 0;
+    return launch(zf::fz_composite_final_kernel, ray_blocks(args->n_rays), 32, 0, stream, a);
 }

@@ -1,16 +1,15 @@
 // torch_ext.cpp -- the PyTorch binding ZipNeRFCudaBackend._C over the C ABI (include/zf_featurize.h, zf_sampling.h,
 // zf_optim.h).
 //
-// Mirrors the reference module (torch_bindings/bindings.cu:14-43) except its NeRF MLP and its final-level
-// compositing / loss kernels: the attributes grid_max_value and nerf_grid_grad_scale, set_rtc_dirs, the class
-// Featurizer with its constructor, n_fp32_grad_rows, forward, backward and backward_mlp (featurizer.h:25-82), the
-// sampling functions generate_rays, view_rays, initialize_rays, sample_uniforms and composite_and_resample
-// (sampling_api.h:10-58), and the class Adam with step and regularization (optimizer_api.h:14-40), with the
-// reference's argument order and meaning, its tensor checks (featurizer.cu:127-138, 207-233, 276-283, 318-331;
-// sampling_api.cu:426-578; optimizer_api.cu:123-158) and its error text (RuntimeError "ZipNeRF: ..."). Launches go to
-// the current CUDA stream. An empty tensor skips a featurizer output, as in the reference. All computation happens in
-// libzf_featurize.so; this file only converts tensors to pointers and allocates the outputs the reference's wrappers
-// return.
+// Mirrors the reference module (torch_bindings/bindings.cu:14-43) except its NeRF MLP: the attributes grid_max_value
+// and nerf_grid_grad_scale, set_rtc_dirs, the class Featurizer with its constructor, n_fp32_grad_rows, forward,
+// backward and backward_mlp (featurizer.h:25-82), the sampling functions generate_rays, view_rays, initialize_rays,
+// sample_uniforms, composite_and_resample, train_final and composite_final (sampling_api.h:10-90), and the class Adam
+// with step and regularization (optimizer_api.h:14-40), with the reference's argument order and meaning, its tensor
+// checks (featurizer.cu:127-138, 207-233, 276-283, 318-331; sampling_api.cu:426-678; optimizer_api.cu:123-158) and its
+// error text (RuntimeError "ZipNeRF: ..."). Launches go to the current CUDA stream. An empty tensor skips a featurizer
+// output, as in the reference. All computation happens in libzf_featurize.so; this file only converts tensors to
+// pointers and allocates the outputs the reference's wrappers return.
 #include "zf_featurize.h"
 #include "zf_optim.h"
 #include "zf_sampling.h"
@@ -438,6 +437,104 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> composite_and_resample(const at::
     return {weights, sdist_next, tdist_next};
 }
 
+std::tuple<at::Tensor, std::vector<at::Tensor>, at::Tensor> train_final(
+    const at::Tensor& nerf_outputs, const at::Tensor& sdist, const at::Tensor& tdist, const std::vector<at::Tensor>& proposal_raw_densities,
+    const std::vector<at::Tensor>& proposal_sdists, const std::vector<at::Tensor>& proposal_tdists, const std::vector<at::Tensor>& proposal_weights,
+    const at::Tensor& directions, const int64_t seed, const at::Tensor& rgb_target, const double charbonnier_padding,
+    const std::vector<double>& interlevel_weights, const std::vector<double>& interlevel_blurs, const double distortion_weight,
+    const double distortion_power, const double distortion_premult, const bool compute_loss_sums) {
+    check_input(nerf_outputs, "nerf_outputs", at::kBFloat16);
+    check_input(sdist, "sdist", at::kFloat);
+    check_input(tdist, "tdist", at::kFloat);
+    check_input(directions, "directions", at::kFloat);
+    check_input(rgb_target, "rgb_target", at::kFloat);
+    if (tdist.dim() != 2) throw std::runtime_error("ZipNeRF: invalid tdist");
+    const int64_t n_rays = tdist.size(0), n_intervals = tdist.size(1) - 1;
+    check_n_intervals(n_intervals);
+    if (nerf_outputs.numel() != n_rays * n_intervals * 8) throw std::runtime_error("ZipNeRF: invalid nerf_outputs");
+    if (sdist.numel() != tdist.numel() || directions.numel() != 3 * n_rays || rgb_target.numel() != 3 * n_rays) {
+        throw std::runtime_error("ZipNeRF: invalid train_final inputs");
+    }
+    const size_t n_levels = proposal_raw_densities.size();
+    if (n_levels > 4 || proposal_sdists.size() != n_levels || proposal_tdists.size() != n_levels || proposal_weights.size() != n_levels
+        || interlevel_weights.size() != n_levels || interlevel_blurs.size() != n_levels) {
+        throw std::runtime_error("ZipNeRF: inconsistent proposal levels");
+    }
+    std::vector<at::Tensor> grads;
+    std::vector<zf_proposal_level> levels(n_levels);
+    for (size_t level = 0; level < n_levels; level++) {
+        check_input(proposal_raw_densities[level], "proposal_raw_density", at::kFloat);
+        check_input(proposal_sdists[level], "proposal_sdist", at::kFloat);
+        check_input(proposal_tdists[level], "proposal_tdist", at::kFloat);
+        check_input(proposal_weights[level], "proposal_weights", at::kFloat);
+        const at::Tensor& raw = proposal_raw_densities[level];
+        if (raw.dim() != 2 || raw.size(0) != n_rays) throw std::runtime_error("ZipNeRF: inconsistent proposal levels");
+        const int64_t n_p = raw.size(1);
+        check_n_intervals(n_p);
+        if (proposal_sdists[level].numel() != n_rays * (n_p + 1) || proposal_tdists[level].numel() != n_rays * (n_p + 1)
+            || proposal_weights[level].numel() != n_rays * n_p) {
+            throw std::runtime_error("ZipNeRF: inconsistent proposal levels");
+        }
+        grads.push_back(at::empty_like(raw));
+        levels[level] = {static_cast<int>(n_p), raw.data_ptr<float>(), proposal_sdists[level].data_ptr<float>(), proposal_tdists[level].data_ptr<float>(),
+                         proposal_weights[level].data_ptr<float>(), grads.back().data_ptr<float>(), static_cast<float>(interlevel_weights[level]),
+                         static_cast<float>(interlevel_blurs[level])};
+    }
+    at::Tensor nerf_outputs_grad = at::empty_like(nerf_outputs);
+    at::Tensor loss_sums = compute_loss_sums ? at::zeros({4}, tdist.options()) : at::Tensor();
+    zf_train_final_args a{};
+    a.nerf_outputs = bf16_ptr(nerf_outputs);
+    a.sdist = sdist.data_ptr<float>();
+    a.tdist = tdist.data_ptr<float>();
+    a.n_rays = n_rays;
+    a.n_intervals = static_cast<int>(n_intervals);
+    a.proposals = levels.data();
+    a.n_proposal_levels = static_cast<int>(n_levels);
+    a.directions = directions.data_ptr<float>();
+    a.seed = seed;
+    a.rgb_target = rgb_target.data_ptr<float>();
+    a.charbonnier_padding = static_cast<float>(charbonnier_padding);
+    a.distortion_weight = static_cast<float>(distortion_weight);
+    a.distortion_power = static_cast<float>(distortion_power);
+    a.distortion_premult = static_cast<float>(distortion_premult);
+    a.nerf_outputs_grad = bf16_ptr(nerf_outputs_grad);
+    a.loss_sums = compute_loss_sums ? loss_sums.data_ptr<float>() : nullptr;
+    const c10::cuda::CUDAGuard guard(tdist.device());
+    check_status(zf_train_final(&a, current_stream()));
+    return {nerf_outputs_grad, grads, loss_sums};
+}
+
+void composite_final(const at::Tensor& nerf_outputs, const at::Tensor& tdist, const at::Tensor& directions, const at::Tensor& background,
+                     const at::Tensor& pixel_indices, at::Tensor& rgb, at::Tensor& alpha, at::Tensor& depth, const bool use_median_depth) {
+    check_input(nerf_outputs, "nerf_outputs", at::kBFloat16);
+    check_input(tdist, "tdist", at::kFloat);
+    check_input(directions, "directions", at::kFloat);
+    check_input(background, "background", at::kFloat);
+    check_input(pixel_indices, "pixel_indices", at::kLong);
+    check_input(rgb, "rgb", at::kFloat);
+    if (alpha.numel() > 0) check_input(alpha, "alpha", at::kFloat);
+    if (depth.numel() > 0) check_input(depth, "depth", at::kFloat);
+    if (tdist.dim() != 2) throw std::runtime_error("ZipNeRF: invalid tdist");
+    const int64_t n_rays = tdist.size(0), n_intervals = tdist.size(1) - 1;
+    check_n_intervals(n_intervals);
+    if (nerf_outputs.numel() != n_rays * n_intervals * 8 || pixel_indices.numel() != n_rays) throw std::runtime_error("ZipNeRF: invalid composite_final inputs");
+    if (directions.numel() != 3 * n_rays || background.numel() < 3) throw std::runtime_error("ZipNeRF: invalid composite_final inputs");
+    zf_composite_final_args a{};
+    a.nerf_outputs = bf16_ptr(nerf_outputs);
+    a.tdist = tdist.data_ptr<float>();
+    a.n_rays = n_rays;
+    a.n_intervals = static_cast<int>(n_intervals);
+    a.directions = directions.data_ptr<float>();
+    a.background = background.data_ptr<float>();
+    a.pixel_indices = pixel_indices.data_ptr<int64_t>();
+    a.rgb = rgb.data_ptr<float>();
+    a.alpha = optional_ptr<float>(alpha);
+    a.depth = optional_ptr<float>(depth);
+    a.use_median_depth = use_median_depth ? 1 : 0;
+    const c10::cuda::CUDAGuard guard(tdist.device());
+    check_status(zf_composite_final(&a, current_stream()));
+}
+
 // ---------------------------------------------------------------------------------------------------------------------
 // Adam (optimizer_api.h:14-40, optimizer_api.cu:123-221): the tensor checks and messages of the reference; the object
 // keeps the tensors it updates alive
@@ -530,4 +627,6 @@ PYBIND11_MODULE(_C, m) {
     m.def("initialize_rays", &initialize_rays);
     m.def("sample_uniforms", &sample_uniforms);
     m.def("composite_and_resample", &composite_and_resample);
+    m.def("train_final", &train_final);
+    m.def("composite_final", &composite_final);
 }

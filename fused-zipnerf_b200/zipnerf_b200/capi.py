@@ -19,7 +19,8 @@ EXPORTED = ['zf_featurizer_create', 'zf_featurizer_destroy', 'zf_featurizer_n_ou
             'zf_featurize_backward_mlp_workspace_size', 'zf_featurize_backward_mlp_no_alloc', 'zf_featurize_debug',
             'zf_check_erf_saturation', 'zf_erf_saturation_threshold', 'zf_last_error', 'zf_grid_max_value', 'zf_nerf_grid_grad_scale',
             'zf_direction_block_width', 'zf_initialize_rays', 'zf_view_rays', 'zf_generate_rays', 'zf_sample_uniforms',
-            'zf_composite_and_resample', 'zf_adam_create', 'zf_adam_destroy', 'zf_adam_step', 'zf_adam_state']
+            'zf_composite_and_resample', 'zf_train_final', 'zf_composite_final', 'zf_adam_create', 'zf_adam_destroy', 'zf_adam_step',
+            'zf_adam_state']
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -75,6 +76,23 @@ class zf_resample_args(ctypes.Structure):
     _fields_ = [('raw_density', _p), ('sdist', _p), ('tdist', _p), ('directions', _p), ('n_rays', _i64), ('n_intervals', ctypes.c_int),
                 ('anneal', ctypes.c_float), ('n_samples', ctypes.c_int), ('seed', _i64), ('next_level', ctypes.c_int), ('warp', zf_ray_warp),
                 ('weights', _p), ('sdist_next', _p), ('tdist_next', _p)]
+
+
+class zf_proposal_level(ctypes.Structure):
+    _fields_ = [('n_intervals', ctypes.c_int), ('raw_density', _p), ('sdist', _p), ('tdist', _p), ('weights', _p), ('raw_density_grad', _p),
+                ('interlevel_weight', ctypes.c_float), ('interlevel_blur', ctypes.c_float)]
+
+
+class zf_train_final_args(ctypes.Structure):
+    _fields_ = [('nerf_outputs', _p), ('sdist', _p), ('tdist', _p), ('n_rays', _i64), ('n_intervals', ctypes.c_int),
+                ('proposals', ctypes.POINTER(zf_proposal_level)), ('n_proposal_levels', ctypes.c_int), ('directions', _p), ('seed', _i64),
+                ('rgb_target', _p), ('charbonnier_padding', ctypes.c_float), ('distortion_weight', ctypes.c_float),
+                ('distortion_power', ctypes.c_float), ('distortion_premult', ctypes.c_float), ('nerf_outputs_grad', _p), ('loss_sums', _p)]
+
+
+class zf_composite_final_args(ctypes.Structure):
+    _fields_ = [('nerf_outputs', _p), ('tdist', _p), ('n_rays', _i64), ('n_intervals', ctypes.c_int), ('directions', _p), ('background', _p),
+                ('pixel_indices', _p), ('rgb', _p), ('alpha', _p), ('depth', _p), ('use_median_depth', ctypes.c_int)]
 
 
 class zf_adam_buffer(ctypes.Structure):
@@ -138,7 +156,10 @@ def load() -> ctypes.CDLL:
     lib.zf_generate_rays.argtypes = [ctypes.POINTER(zf_generate_rays_args), _p]
     lib.zf_sample_uniforms.argtypes = [_i64, _i64, _i64, _p, _p]
     lib.zf_composite_and_resample.argtypes = [ctypes.POINTER(zf_resample_args), _p]
-    for name in ['zf_initialize_rays', 'zf_view_rays', 'zf_generate_rays', 'zf_sample_uniforms', 'zf_composite_and_resample']:
+    lib.zf_train_final.argtypes = [ctypes.POINTER(zf_train_final_args), _p]
+    lib.zf_composite_final.argtypes = [ctypes.POINTER(zf_composite_final_args), _p]
+    for name in ['zf_initialize_rays', 'zf_view_rays', 'zf_generate_rays', 'zf_sample_uniforms', 'zf_composite_and_resample', 'zf_train_final',
+                 'zf_composite_final']:
         getattr(lib, name).restype = ctypes.c_int
     # zf_optim.h
     lib.zf_adam_create.argtypes = [ctypes.POINTER(zf_adam_buffer), ctypes.c_int, ctypes.c_double, ctypes.c_double, ctypes.c_double,
@@ -344,6 +365,34 @@ def composite_and_resample(raw_density, sdist, tdist, directions, anneal: float,
                          next_level, make_ray_warp(warp), _ptr(weights), _ptr(sdist_next), _ptr(tdist_next))
     check(load().zf_composite_and_resample(ctypes.byref(a), _stream(stream)))
     return weights, sdist_next, tdist_next
+
+
+def train_final(nerf_outputs, sdist, tdist, proposals, directions, seed: int, rgb_target, charbonnier_padding: float, distortion_weight: float,
+                distortion_power: float, distortion_premult: float, compute_loss_sums: bool = True, stream=None):
+    """zf_train_final. proposals: a list of dicts (raw_density, sdist, tdist, weights, interlevel_weight, interlevel_blur).
+    Returns (nerf_outputs_grad, [proposal raw density gradients], loss_sums or None)."""
+    import torch
+    n_rays, n1 = tdist.shape
+    grads = [torch.empty_like(p['raw_density']) for p in proposals]
+    levels = (zf_proposal_level * max(len(proposals), 1))(*[
+        zf_proposal_level(p['raw_density'].shape[1], _ptr(p['raw_density']), _ptr(p['sdist']), _ptr(p['tdist']), _ptr(p['weights']), _ptr(g),
+                          p['interlevel_weight'], p['interlevel_blur']) for p, g in zip(proposals, grads)])
+    out_grad = torch.empty_like(nerf_outputs)
+    loss_sums = torch.zeros(4, device=tdist.device) if compute_loss_sums else None
+    a = zf_train_final_args(_ptr(nerf_outputs), _ptr(sdist), _ptr(tdist), n_rays, n1 - 1, levels, len(proposals), _ptr(directions), seed,
+                            _ptr(rgb_target), charbonnier_padding, distortion_weight, distortion_power, distortion_premult, _ptr(out_grad),
+                            _ptr(loss_sums))
+    check(load().zf_train_final(ctypes.byref(a), _stream(stream)))
+    return out_grad, grads, loss_sums
+
+
+def composite_final(nerf_outputs, tdist, directions, background, pixel_indices, rgb, alpha=None, depth=None, use_median_depth: bool = False,
+                    stream=None) -> None:
+    """zf_composite_final into the given image buffers (alpha, depth optional)."""
+    n_rays, n1 = tdist.shape
+    a = zf_composite_final_args(_ptr(nerf_outputs), _ptr(tdist), n_rays, n1 - 1, _ptr(directions), _ptr(background), _ptr(pixel_indices), _ptr(rgb),
+                                _ptr(alpha), _ptr(depth), 1 if use_median_depth else 0)
+    check(load().zf_composite_final(ctypes.byref(a), _stream(stream)))
 
 
 class CAdam:

@@ -1,5 +1,6 @@
-"""Workloads of the per-step kernels around the featurization (the sampling steps and the Adam step), sized like a
-config-2 training step: 65,536 rays; proposal levels of 64 intervals feeding 64 and 32; a ray pool of 185 views of
+"""Workloads of the per-step kernels around the featurization (the sampling steps, the final level's losses and the
+Adam step), sized like a config-2 training step: 65,536 rays; proposal levels of 64 intervals feeding 64 and 32; the
+final level's 32 intervals; a ray pool of 185 views of
 1296 x 840 pixels (config 4's pool, synthetic uniform-noise colors, one pinhole camera, poses on a radius-4
 hemisphere); and the optimizer buffers of the reference model's default grids (Model.py:65-78,100-105): proposal grids
 of 6 and 8 levels x 1 feature, the NeRF grid of 10 levels x 4 features split at its fp32 / fp16 gradient levels, the
@@ -74,6 +75,34 @@ def ray_pool(device, n_views: int = 185, width: int = 1296, height: int = 840, f
 def new_rays_bytes(n_samples: int, width: int) -> int:
     """per ray: the pixel's color and camera direction read; origin, direction, radius, color, encoding, edges written"""
     return 3 + 12 + 12 + 12 + 4 + 12 + 2 * width + 8 * (n_samples + 1)
+
+
+def final_inputs(device, n_rays: int = N_RAYS, seed: int = 13) -> dict:
+    """A training step's final-level inputs: rays initialized and resampled through both proposal levels (64, 64, 32
+    intervals) by the sampling kernels, raw proposal densities N(0, 2), NeRF outputs N(0, 2) in bf16, random targets."""
+    from zipnerf_b200 import capi
+    g = torch.Generator(device=device).manual_seed(seed)
+    d = torch.nn.functional.normalize(torch.randn(n_rays, 3, generator=g, device=device), dim=1).contiguous()
+    _, s, t = capi.initialize_rays(seed, d, 4, 64, WARP)
+    proposals = []
+    for level, (n_next, blur) in enumerate(((64, 0.03), (32, 0.003)), start=1):
+        raw = torch.randn(n_rays, s.shape[1] - 1, generator=g, device=device) * 2.0
+        w, s_next, t_next = capi.composite_and_resample(raw, s, t, d, 0.5, n_next, seed, level, WARP)
+        proposals.append({'raw_density': raw, 'sdist': s, 'tdist': t, 'weights': w, 'interlevel_weight': 0.01, 'interlevel_blur': blur})
+        s, t = s_next, t_next
+    outputs = torch.randn(n_rays, 32, 8, generator=g, device=device) * 2.0
+    outputs[..., 4:] = 0.0
+    return {'nerf_outputs': outputs.to(torch.bfloat16).contiguous(), 'sdist': s, 'tdist': t, 'proposals': proposals, 'directions': d, 'seed': seed,
+            'rgb_target': torch.rand(n_rays, 3, generator=g, device=device)}
+
+
+def final_bytes(n: int = 32, proposal_intervals=(64, 64)) -> int:
+    """per ray: the NeRF outputs read (4 of 8 values per interval), their gradient rows written (8 values), edges s and
+    t, direction, target; per proposal level its raw densities, edges, weights read and its gradient written"""
+    return 8 * n + 16 * n + 8 * (n + 1) + 12 + 12 + sum(4 * m + 8 * (m + 1) + 4 * m + 4 * m for m in proposal_intervals)
+
+
+LOSS_ARGS = (0.001, 0.01, -0.25, 10000.0)  # charbonnier padding, distortion weight, power, premult (Trainer.py:24-33)
 
 
 def adam_layout() -> list[dict]:

@@ -3,9 +3,10 @@
  *
  * Replaces the producers of the featurizer's interval endpoints in Fused Zip-NeRF's ZipNeRFCudaBackend
  * (ZipNeRFCudaBackend/ZipNeRFCudaBackend/sampling/include/sampling_api.h:10-58, src/sampling_api.cu:447-578):
- * generate_rays, view_rays, initialize_rays, sample_uniforms and composite_and_resample. Conventions as
- * zf_featurize.h: plain device pointers, an int status (ZF_OK or an error code, message in zf_last_error()), no
- * exceptions, asynchronous launches on the given stream. The caller allocates every output; the reference's wrappers
+ * generate_rays, view_rays, initialize_rays, sample_uniforms and composite_and_resample; and the final level's losses
+ * and compositing around the NeRF MLP (sampling_api.h:60-90, sampling_api.cu:580-678): train_final and composite_final.
+ * Conventions as zf_featurize.h: plain device pointers, an int status (ZF_OK or an error code, message in
+ * zf_last_error()), no exceptions, asynchronous launches on the given stream. The caller allocates every output; the reference's wrappers
  * allocate them and return tensors, which the PyTorch binding does on top of these calls.
  *
  * Layouts (row-major; n = intervals of the level, n_samples = intervals of the produced level):
@@ -109,6 +110,59 @@ typedef struct zf_resample_args {
     float* tdist_next;
 } zf_resample_args;
 
+/* One proposal level of zf_train_final (the ProposalLevels of sampling_api.cu:17-27): its raw densities, interval edges
+ * and compositing weights (as composite_and_resample returned them), the gradient it receives (written, not
+ * accumulated), and its interlevel loss weight and blur half width. */
+typedef struct zf_proposal_level {
+    int n_intervals;
+    const float* raw_density;            /* [n_rays, n_intervals] */
+    const float* sdist;                  /* [n_rays, n_intervals + 1] */
+    const float* tdist;
+    const float* weights;                /* [n_rays, n_intervals] */
+    float* raw_density_grad;             /* [n_rays, n_intervals] */
+    float interlevel_weight;
+    float interlevel_blur;
+} zf_proposal_level;
+
+/* train_final_wrapper (sampling_api.cu:580-645): the training losses of a ray batch and the gradients of every level's
+ * raw outputs. nerf_outputs: bf16 [n_rays, n_intervals, 8] (raw density, rgb logits, padding) of the final level;
+ * nerf_outputs_grad: bf16 [n_rays, n_intervals, 8] (written); loss_sums: NULL or float [4] that the (data, mse,
+ * interlevel, distortion) sums are added to, divided by n_rays (the reference returns them from zeros). */
+typedef struct zf_train_final_args {
+    const uint16_t* nerf_outputs;
+    const float* sdist;
+    const float* tdist;
+    int64_t n_rays;
+    int n_intervals;
+    const zf_proposal_level* proposals;
+    int n_proposal_levels;               /* <= 4 */
+    const float* directions;
+    int64_t seed;                        /* random backgrounds: stream 1, index 3 ray + channel */
+    const float* rgb_target;             /* [n_rays, 3] */
+    float charbonnier_padding;
+    float distortion_weight;
+    float distortion_power;
+    float distortion_premult;
+    uint16_t* nerf_outputs_grad;
+    float* loss_sums;
+} zf_train_final_args;
+
+/* composite_final_wrapper (sampling_api.cu:647-678): color (over the given background), opacity and the expected
+ * log-distance (or median) depth of every ray, written to its pixel; alpha and depth may be NULL. */
+typedef struct zf_composite_final_args {
+    const uint16_t* nerf_outputs;        /* bf16 [n_rays, n_intervals, 8] */
+    const float* tdist;                  /* [n_rays, n_intervals + 1] */
+    int64_t n_rays;
+    int n_intervals;
+    const float* directions;
+    const float* background;             /* [3] */
+    const int64_t* pixel_indices;        /* [n_rays] */
+    float* rgb;                          /* [pixels, 3] */
+    float* alpha;                        /* [pixels] */
+    float* depth;                        /* [pixels] */
+    int use_median_depth;
+} zf_composite_final_args;
+
 /* width of the encoded view direction block: (3 + 6 degree + 1) rounded up to a multiple of 8 (zipnerf_config.h:18) */
 ZF_API int64_t zf_direction_block_width(int direction_degree);
 
@@ -120,6 +174,9 @@ ZF_API int zf_generate_rays(const zf_generate_rays_args* args, struct CUstream_s
 ZF_API int zf_sample_uniforms(int64_t seed, int64_t stream_index, int64_t n, float* values, struct CUstream_st* stream);
 
 ZF_API int zf_composite_and_resample(const zf_resample_args* args, struct CUstream_st* stream);
+
+ZF_API int zf_train_final(const zf_train_final_args* args, struct CUstream_st* stream);
+ZF_API int zf_composite_final(const zf_composite_final_args* args, struct CUstream_st* stream);
 
 #ifdef __cplusplus
 }

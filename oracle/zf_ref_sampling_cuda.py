@@ -1,4 +1,5 @@
-"""ctypes binding of the reference's own sampling and Adam kernels compiled for sm_100a (TEST INFRASTRUCTURE ONLY).
+"""ctypes binding of the reference's own sampling, final-level and Adam kernels compiled for sm_100a (TEST
+INFRASTRUCTURE ONLY).
 
 oracle/ref_cuda/build.py compiles B/sampling/src/sampling_api.cu and B/optimizer/src/optimizer_api.cu (unmodified, with
 the launchers of oracle/ref_cuda/ref_sampling.cu) into oracle/_ref/cuda/libzfref_sampling.so, which travels to the GPU
@@ -49,6 +50,8 @@ class RefSamplingCuda:
         lib.ref_initialize_rays.argtypes = [_i64, _p, _i32, _i32, _i32, _p, _p, _p, _p, _p]
         lib.ref_sample_uniforms.argtypes = [_i64, _i64, _i64, _p, _p]
         lib.ref_composite_and_resample.argtypes = [_p, _p, _p, _p, _i32, _i32, _f32, _i32, _i64, _i32, _p, _p, _p, _p, _p]
+        lib.ref_train_final.argtypes = [_p, _p, _p, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _f32, _f32, _f32, _f32, _p, _p, _p]
+        lib.ref_composite_final.argtypes = [_p, _p, _p, _p, _p, _i32, _i32, _p, _p, _p, _i32, _p]
         lib.ref_adam_step.argtypes = [_i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f64, _f64, _f64, _f64, _f64, _i64, _f64, _p, _p, _p, _p, _p]
         self.lib = lib
 
@@ -109,6 +112,31 @@ class RefSamplingCuda:
                                                    next_level, w.data_ptr(), _ptr(weights), _ptr(sdist_next), _ptr(tdist_next), _stream()),
                'composite_and_resample')
         return weights, sdist_next, tdist_next
+
+    def train_final(self, nerf_outputs, sdist, tdist, proposals, directions, seed, rgb_target, charbonnier_padding, distortion_weight,
+                    distortion_power, distortion_premult, compute_loss_sums=True):
+        """train_final_wrapper (sampling_api.cu:580-645); proposals: dicts of raw_density, sdist, tdist, weights,
+        interlevel_weight, interlevel_blur. Returns (nerf_outputs_grad, [proposal gradients], loss_sums or None)."""
+        import torch
+        n_rays, n1 = tdist.shape
+        k = len(proposals)
+        grads = [torch.empty_like(p['raw_density']) for p in proposals]
+        arr = lambda ctype, values: (ctype * max(k, 1))(*values)  # noqa: E731
+        out_grad = torch.empty_like(nerf_outputs)
+        loss_sums = torch.zeros(4, device=tdist.device) if compute_loss_sums else None
+        _check(self.lib.ref_train_final(
+            _ptr(nerf_outputs), _ptr(sdist), _ptr(tdist), n_rays, n1 - 1, k, arr(_i32, [p['raw_density'].shape[1] for p in proposals]),
+            arr(_p, [_ptr(p['raw_density']) for p in proposals]), arr(_p, [_ptr(p['sdist']) for p in proposals]),
+            arr(_p, [_ptr(p['tdist']) for p in proposals]), arr(_p, [_ptr(p['weights']) for p in proposals]), arr(_p, [_ptr(g) for g in grads]),
+            arr(_f32, [p['interlevel_weight'] for p in proposals]), arr(_f32, [p['interlevel_blur'] for p in proposals]), _ptr(directions), seed,
+            _ptr(rgb_target), charbonnier_padding, distortion_weight, distortion_power, distortion_premult, _ptr(out_grad), _ptr(loss_sums),
+            _stream()), 'train_final')
+        return out_grad, grads, loss_sums
+
+    def composite_final(self, nerf_outputs, tdist, directions, background, pixel_indices, rgb, alpha=None, depth=None, use_median_depth=False):
+        n_rays, n1 = tdist.shape
+        _check(self.lib.ref_composite_final(_ptr(nerf_outputs), _ptr(tdist), _ptr(directions), _ptr(background), _ptr(pixel_indices), n_rays, n1 - 1,
+                                            _ptr(rgb), _ptr(alpha), _ptr(depth), 1 if use_median_depth else 0, _stream()), 'composite_final')
 
 
 class RefAdamCuda:

@@ -1,4 +1,4 @@
-"""GPU parity of the sampling and Adam kernels: against the reference's own kernels compiled for sm_100a
+"""GPU parity of the sampling, final-level and Adam kernels: against the reference's own kernels compiled for sm_100a
 (oracle/_ref/cuda/libzfref_sampling.so, bit for bit: same per-ray arithmetic, same fast-math build), against the CPU
 restatement (oracle/zf_step_oracle.c, within the differences of the GPU's fast-math intrinsics from libm), through the
 C ABI and the PyTorch binding, with the edge cases the reference handles (empty batches, single rays, ragged warps, the
@@ -191,6 +191,100 @@ def test_sampling_edge_cases_and_errors(capi, cuda_device):
     with pytest.raises(RuntimeError, match='ZipNeRF: c2w must be a 3x4 matrix'):
         ZipNeRFCudaBackend.view_rays(torch.zeros(3, dtype=torch.int64, device=cuda_device), torch.zeros(4, 3, device=cuda_device),
                                      torch.zeros(3, 3, device=cuda_device), 0.01, 4, 64, list(sc.WARP))
+
+
+def final_case(capi, device, n_rays: int, seed: int, n_final: int = 32) -> dict:
+    """The inputs of a training step's final level: rays initialized and resampled through both proposal levels by
+    the product's own (bit-exact) sampling kernels, raw proposal densities N(0, 3), NeRF outputs N(0, 2) in bf16 with
+    a few non-finite entries (empty samples), random targets."""
+    rng = np.random.default_rng(seed)
+    d = cuda(sc.directions(rng, n_rays), device)
+    _, s, t = capi.initialize_rays(seed, d, sc.DEGREE, 64, sc.WARP)
+    proposals = []
+    for level, n_next in ((1, 64), (2, n_final)):
+        raw = cuda((rng.normal(size=(n_rays, s.shape[1] - 1)) * 3.0).astype(np.float32), device)
+        w, s_next, t_next = capi.composite_and_resample(raw, s, t, d, 0.7, n_next, seed, level, sc.WARP)
+        proposals.append({'raw_density': raw, 'sdist': s, 'tdist': t, 'weights': w, 'interlevel_weight': 0.01,
+                          'interlevel_blur': (0.03, 0.003)[level - 1]})
+        s, t = s_next, t_next
+    outputs = (rng.normal(size=(n_rays, n_final, 8)) * 2.0).astype(np.float32)
+    outputs[..., 4:] = 0.0
+    outputs[rng.uniform(size=outputs.shape) < 0.002] = np.nan
+    outputs[rng.uniform(size=outputs.shape) < 0.002] = np.inf
+    return {'nerf_outputs': cuda(outputs, device).to(torch.bfloat16).contiguous(), 'sdist': s, 'tdist': t, 'proposals': proposals, 'directions': d,
+            'seed': seed + 1000, 'rgb_target': cuda(rng.uniform(size=(n_rays, 3)).astype(np.float32), device)}
+
+
+LOSS_ARGS = (0.001, 0.01, -0.25, 10000.0)  # charbonnier padding, distortion weight, power, premult (Trainer.py:24-33)
+
+
+@pytest.mark.parametrize('n_rays', [1, 33, 300, 4096, 65536])
+def test_train_final_matches_reference_kernel(ref, capi, cuda_device, n_rays):
+    c = final_case(capi, cuda_device, n_rays, 17 + n_rays)
+    args = (c['nerf_outputs'], c['sdist'], c['tdist'], c['proposals'], c['directions'], c['seed'], c['rgb_target'], *LOSS_ARGS)
+    ours = capi.train_final(*args)
+    theirs = ref.train_final(*args)
+    assert_same_bits(ours[0], theirs[0], 'nerf_outputs_grad')
+    for level, (a, b) in enumerate(zip(ours[1], theirs[1])):
+        assert_same_bits(a, b, f'proposal {level} raw density gradient')
+    torch.testing.assert_close(ours[2], theirs[2], rtol=1e-5, atol=1e-12)  # warp sums added atomically, in varying order
+    assert torch.isfinite(ours[0].float()).all() and all(torch.isfinite(g).all() for g in ours[1])
+    import ZipNeRFCudaBackend
+    p = c['proposals']
+    grad, grads, sums = ZipNeRFCudaBackend.train_final(
+        c['nerf_outputs'], c['sdist'], c['tdist'], [x['raw_density'] for x in p], [x['sdist'] for x in p], [x['tdist'] for x in p],
+        [x['weights'] for x in p], c['directions'], c['seed'], c['rgb_target'], LOSS_ARGS[0], [x['interlevel_weight'] for x in p],
+        [x['interlevel_blur'] for x in p], *LOSS_ARGS[1:], True)
+    assert_same_bits(grad, ours[0], 'binding')
+    for a, b in zip(grads, ours[1]):
+        assert_same_bits(a, b, 'binding proposal gradient')
+    torch.testing.assert_close(sums, ours[2], rtol=1e-5, atol=1e-12)
+
+
+@pytest.mark.parametrize('use_median_depth', [False, True])
+def test_composite_final_matches_reference_kernel(ref, capi, cuda_device, use_median_depth):
+    c = final_case(capi, cuda_device, 1000, 5)
+    pixels = torch.randperm(1000, generator=torch.Generator().manual_seed(3)).to(cuda_device)
+    background = torch.tensor([0.2, 0.5, 0.9], device=cuda_device)
+    images = {}
+    for impl in ('ours', 'reference'):
+        rgb, alpha, depth = torch.full((1000, 3), -1.0, device=cuda_device), torch.full((1000,), -1.0, device=cuda_device), torch.full((1000,), -1.0, device=cuda_device)
+        fn = capi.composite_final if impl == 'ours' else ref.composite_final
+        fn(c['nerf_outputs'], c['tdist'], c['directions'], background, pixels, rgb, alpha, depth, use_median_depth=use_median_depth)
+        images[impl] = (rgb, alpha, depth)
+    for a, b, name in zip(images['ours'], images['reference'], ['rgb', 'alpha', 'depth']):
+        assert_same_bits(a, b, name)
+    assert (images['ours'][1] >= 0).all() and (images['ours'][2] > 0).all()
+    # without the optional outputs, and through the binding
+    import ZipNeRFCudaBackend
+    rgb = torch.zeros(1000, 3, device=cuda_device)
+    empty = torch.empty(0, device=cuda_device)
+    ZipNeRFCudaBackend.composite_final(c['nerf_outputs'], c['tdist'], c['directions'], background, pixels, rgb, empty, empty, use_median_depth)
+    assert_same_bits(rgb, images['ours'][0], 'binding rgb')
+
+
+def test_final_level_edge_cases_and_errors(capi, cuda_device):
+    import ZipNeRFCudaBackend
+    c = final_case(capi, cuda_device, 40, 9)
+    grad, grads, sums = capi.train_final(c['nerf_outputs'], c['sdist'], c['tdist'], c['proposals'], c['directions'], c['seed'], c['rgb_target'],
+                                         *LOSS_ARGS, compute_loss_sums=False)
+    assert sums is None and grad.shape == c['nerf_outputs'].shape
+    # no proposal levels: the data and distortion terms only
+    grad0, grads0, _ = capi.train_final(c['nerf_outputs'], c['sdist'], c['tdist'], [], c['directions'], c['seed'], c['rgb_target'], *LOSS_ARGS)
+    assert grads0 == [] and torch.equal(grad0.view(torch.int16), grad.view(torch.int16))
+    empty = capi.train_final(c['nerf_outputs'][:0], c['sdist'][:0], c['tdist'][:0], [], c['directions'][:0], 1, c['rgb_target'][:0], *LOSS_ARGS)
+    assert empty[0].numel() == 0
+    p = c['proposals']
+    lists = ([x['raw_density'] for x in p], [x['sdist'] for x in p], [x['tdist'] for x in p], [x['weights'] for x in p])
+    with pytest.raises(RuntimeError, match='ZipNeRF: inconsistent proposal levels'):
+        ZipNeRFCudaBackend.train_final(c['nerf_outputs'], c['sdist'], c['tdist'], *lists[:3], lists[3][:1], c['directions'], 1, c['rgb_target'], 0.001,
+                                       [0.01, 0.01], [0.03, 0.003], 0.01, -0.25, 1e4, True)
+    with pytest.raises(RuntimeError, match='ZipNeRF: invalid nerf_outputs'):
+        ZipNeRFCudaBackend.train_final(c['nerf_outputs'][:, :16].contiguous(), c['sdist'], c['tdist'], *lists, c['directions'], 1, c['rgb_target'], 0.001,
+                                       [0.01, 0.01], [0.03, 0.003], 0.01, -0.25, 1e4, True)
+    with pytest.raises(RuntimeError, match='ZipNeRF: nerf_outputs must be a contiguous cuda tensor'):
+        ZipNeRFCudaBackend.train_final(c['nerf_outputs'].float(), c['sdist'], c['tdist'], *lists, c['directions'], 1, c['rgb_target'], 0.001,
+                                       [0.01, 0.01], [0.03, 0.003], 0.01, -0.25, 1e4, True)
 
 
 def metric_rtol(t: np.ndarray) -> np.ndarray:

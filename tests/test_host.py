@@ -26,7 +26,7 @@ def test_header_declares_the_reference_entry_points():
         assert name in names
     # sampling_api.h:10-58 and optimizer_api.h:14-40
     for name in ['zf_generate_rays', 'zf_view_rays', 'zf_initialize_rays', 'zf_sample_uniforms', 'zf_composite_and_resample',
-                 'zf_adam_create', 'zf_adam_step', 'zf_adam_destroy']:
+                 'zf_train_final', 'zf_composite_final', 'zf_adam_create', 'zf_adam_step', 'zf_adam_destroy']:
         assert name in names
 
 
@@ -119,7 +119,8 @@ def test_torch_binding_has_the_reference_surface():
     _C.set_rtc_dirs('/nonexistent/cache', '/nonexistent/kernels')  # accepted and unused (kernels are compiled ahead of time)
     for method in ['forward', 'backward', 'backward_mlp']:
         assert hasattr(_C.Featurizer, method)
-    for name in ['generate_rays', 'view_rays', 'initialize_rays', 'sample_uniforms', 'composite_and_resample', 'Adam']:
+    for name in ['generate_rays', 'view_rays', 'initialize_rays', 'sample_uniforms', 'composite_and_resample', 'train_final', 'composite_final',
+                 'Adam']:
         assert getattr(ZipNeRFCudaBackend, name) is getattr(_C, name) is getattr(pipeline, name)
     assert hasattr(_C.Adam, 'step') and hasattr(_C.Adam, 'regularization')
     assert isinstance(_C.Featurizer.n_fp32_grad_rows, property)
