@@ -12,8 +12,10 @@ data-parallel exchange of a training step.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-Prints one JSON line on rank 0. On one GPU the line also carries "rows": the sampling and Adam kernels of the same
-training step (composite-and-resample, ray generation, the Adam step), each timed alone against the HBM roofline.
+Prints one JSON line on rank 0. The line also carries "train_step": the full training step (rays, all levels'
+featurization, resampling, the NeRF MLP, losses, backwards, the gradient all-reduce over the N GPUs and Adam) in ms,
+max over ranks; and on one GPU "rows": the sampling, final-level and Adam kernels of that step, each timed alone
+against the HBM roofline.
 """
 from __future__ import annotations
 
@@ -434,6 +436,8 @@ def run_b200(args) -> None:
               'roofline': roofline, 'kernels': kernels, 'gpu_launches': step.kernel_launches_per_step * args.steps, 'clocks': clocks.summary()}
     if not args.skip_e2e:
         result['e2e'] = measure_e2e(step, args, world, start_exchange, exchange, barrier)
+    if not args.skip_train_step:
+        result['train_step'] = measure_train_step(args, world, rank, device, barrier)
     if rank == 0 and not args.skip_rows and world == 1:
         result['rows'] = measure_rows(device)
     if rank == 0 and not args.skip_cpu_baseline and world == 1:
@@ -511,6 +515,49 @@ def measure_rows(device, iters: int = 10) -> dict:
     out['adam'] = entry([ms], rows.adam_bytes(layout), f'{n_params} parameters in {len(layout)} buffers ({n_levels} grid levels, '
                         'NeRF grid levels 3-9 with fp16 gradients)')
     return out
+
+
+def measure_train_step(args, world: int, rank: int, device, barrier, steps: int = 10) -> dict:
+    """The full training step (zipnerf_b200/train_step.py, the reference model's default grids): every rank trains on
+    its own rays (weak scaling), each gradient buffer is averaged over the ranks with NCCL on a communication stream as
+    soon as its backward has finished, and the single-launch Adam step follows. Timed on the device over `steps`
+    iterations after the warm-up, max over ranks."""
+    import torch.distributed as dist
+    from zipnerf_b200 import sharding, train_step
+    step = train_step.TrainStep(device, n_rays=args.rays, rank=rank, world=world)
+    comm = torch.cuda.Stream() if world > 1 else None
+
+    def after_backward(buffers):
+        if world > 1:
+            comm.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(comm):
+                sharding.allreduce_gradients([b for b in buffers if b is not None])
+
+    def exchange():
+        if world > 1:
+            torch.cuda.current_stream().wait_stream(comm)
+
+    for i in range(args.warmup):
+        step.run(i, after_backward=after_backward, exchange=exchange)
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        step.run(args.warmup + i, after_backward=after_backward, exchange=exchange)
+    end.record()
+    barrier()
+    elapsed_ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = t.item()
+    ms = elapsed_ms / steps
+    losses = step.loss_sums.tolist()
+    return {'ms': ms, 'steps': steps, 'rays_per_s': world * args.rays / (ms * 1e-3), 'featurized_msamples_per_s': world * step.samples_per_step / (ms * 1e-3) / 1e6,
+            'loss_sums_last_step': losses,
+            'config': f'{args.rays} rays per GPU x (64 + 64 + 32) intervals; grids of the reference model (6 and 8 levels x 1 feature, 10 x 4, '
+                      f'scale 2, 2^21); rays from a 185-view 1296 x 840 pool; gradient all-reduce over {world} GPU(s) and Adam; the NeRF MLP as '
+                      'cuBLAS bf16 GEMMs (a stand-in of the reference cuBLASLt chain)'}
 
 
 def measure_e2e(step: Step, args, world: int, start_exchange, exchange, barrier) -> dict:
@@ -601,6 +648,7 @@ def main() -> None:
     parser.add_argument('--skip-e2e', action='store_true')
     parser.add_argument('--skip-cpu-baseline', action='store_true')
     parser.add_argument('--skip-rows', action='store_true', help='skip the timing of the sampling and Adam kernels')
+    parser.add_argument('--skip-train-step', action='store_true', help='skip the timing of the full training step')
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps
     if args.impl == 'reference':

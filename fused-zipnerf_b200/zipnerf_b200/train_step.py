@@ -1,0 +1,255 @@
+"""A complete training step of Fused Zip-NeRF on this backend, in the order of the reference trainer
+(Trainer.compute_gradients / training_iteration, Trainer.py:92-141, with Renderer.render_rays_training,
+Renderer.py:44-84): training rays of random pool pixels, the two proposal levels' featurization with their fused
+density MLPs and the resampling of the next level's intervals, the NeRF level's featurization, the NeRF MLP, the
+final level's losses and gradients, the NeRF MLP backward, the grid and MLP backwards of all levels, the data-parallel
+gradient average (one NCCL all-reduce per gradient buffer, each started as soon as its buffer is final) and the
+single-launch Adam step with the grid regularizer and scale-feature magnitudes.
+
+Model: the reference model's defaults (Model.py:65-78): proposal grids of 6 and 8 levels x 1 feature and the NeRF grid
+of 10 levels x 4 features (base resolution 16, per-level scale 2, 2^21 entries), density MLPs of width 64, 64 + 64 + 32
+intervals per ray, the view-direction encoding of degree 4; the trainer's loss weights and Adam settings
+(Trainer.py:17-57). Data: a synthetic pool of 185 views of 1296 x 840 pixels (uniform-noise colors).
+
+Every kernel of the step is this backend's, except the NeRF MLP: it runs as cuBLAS bf16 GEMMs through torch (the
+layer shapes of the reference's cuBLASLt chain, nerf_mlp.cu:440-455,503-620, with elementwise ReLU and bias steps in
+torch), a stand-in of the same shape and cost, not the reference's numerics.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+N_SAMPLES = (64, 64, 32)
+GRID_LEVELS = (6, 8, 10)
+GRID_FEATURES = (1, 1, 4)
+MLP_WIDTH = 64
+DEGREE = 4
+NEAR, FAR = 0.2, 1000.0
+LOSS = {'charbonnier_padding': 0.001, 'interlevel': 0.01, 'blurs': (0.03, 0.003), 'distortion': 0.01, 'distortion_power': -0.25,
+        'distortion_premult': 10000.0, 'grid_regularization': 0.1}
+ADAM = {'beta1': 0.9, 'beta2': 0.99, 'eps': 1e-15}
+
+
+LR = {'init': 0.01, 'final': 0.001, 'delay_steps': 2500, 'delay_mult': 1e-8, 'max_steps': 25000}  # Trainer.py:17-26
+
+
+def learning_rate(step: int) -> float:
+    """The trainer's learning-rate policy (Trainer.py:22-26,58-61): the mip-NeRF schedule, a log-linear decay from
+    init to final over max_steps, scaled during the first delay_steps by a sine ramp from delay_mult to 1."""
+    t = min(max(step / LR['max_steps'], 0.0), 1.0)
+    rate = math.exp(math.log(LR['init']) * (1 - t) + math.log(LR['final']) * t)
+    ramp = min(max(step / LR['delay_steps'], 0.0), 1.0)
+    return rate * (LR['delay_mult'] + (1 - LR['delay_mult']) * math.sin(0.5 * math.pi * ramp))
+
+
+def grid_layout(n_levels: int):
+    sizes = [16 * 2 ** level for level in range(n_levels)]
+    return sizes, [min(s ** 3, 2 ** 21) for s in sizes]
+
+
+class NerfMlp:
+    """The NeRF MLP's layers as bf16 GEMMs (cuBLAS through torch): features [n, 56] -> hidden 64 (ReLU, bias) written
+    into the first 64 columns of the NeRF inputs [n, 96] (the featurizer wrote the encoded direction into the last 32);
+    inputs -> view 256 (ReLU; the bottleneck folded into the first view layer, as the reference packs it) -> 256 (ReLU,
+    bias) -> 256 (ReLU, bias) -> rgb; a skip projection of the inputs gives the raw density and the rgb skip rows.
+    Outputs [n, 8] bf16: raw density, 3 rgb logits, padding. Master parameters are one flat fp32 buffer (as the
+    reference's nerf_mlp_params), cast to bf16 once per step."""
+
+    SHAPES = [('density', (64, 56)), ('density_b', (64,)), ('combined', (256, 96)), ('skip', (8, 96)), ('view_1', (256, 256)), ('view_1_b', (256,)),
+              ('view_2', (256, 256)), ('view_2_b', (256,)), ('rgb', (8, 256))]
+
+    def __init__(self, device, generator: torch.Generator) -> None:
+        self.offsets = {}
+        n = 0
+        for name, shape in self.SHAPES:
+            self.offsets[name] = (n, shape)
+            n += math.prod(shape)
+        self.numel = (n + 3) // 4 * 4
+        self.params = torch.zeros(self.numel, device=device)
+        for name, shape in self.SHAPES:
+            if len(shape) == 2:
+                bound = math.sqrt(6.0 / shape[1])
+                self.view(self.params, name).uniform_(-bound, bound, generator=generator)
+        self.grads = torch.zeros_like(self.params)
+
+    def view(self, buffer: torch.Tensor, name: str) -> torch.Tensor:
+        offset, shape = self.offsets[name]
+        return buffer[offset:offset + math.prod(shape)].view(shape)
+
+    def forward(self, features: torch.Tensor, inputs: torch.Tensor):
+        w = {name: self.view(self.params, name).to(torch.bfloat16) for name, _ in self.SHAPES}
+        hidden = torch.relu(torch.addmm(w['density_b'], features, w['density'].t()))
+        inputs[:, :64] = hidden
+        v0 = torch.relu(inputs @ w['combined'].t())
+        outputs = inputs @ w['skip'].t()
+        v1 = torch.relu(torch.addmm(w['view_1_b'], v0, w['view_1'].t()))
+        v2 = torch.relu(torch.addmm(w['view_2_b'], v1, w['view_2'].t()))
+        outputs += v2 @ w['rgb'].t()
+        return outputs.contiguous(), (w, features, inputs, v0, v1, v2)
+
+    def backward(self, grad_outputs: torch.Tensor, context) -> torch.Tensor:
+        """Accumulates the parameter gradients (fp32) and returns the feature gradient [n, 56] bf16."""
+        w, features, inputs, v0, v1, v2 = context
+        g = self.grads
+
+        def add(name, value):
+            self.view(g, name).add_(value.float())
+
+        add('rgb', grad_outputs.t() @ v2)
+        g_v2 = (grad_outputs @ w['rgb']) * (v2 > 0)
+        add('view_2', g_v2.t() @ v1)
+        add('view_2_b', g_v2.float().sum(0))
+        g_v1 = (g_v2 @ w['view_2']) * (v1 > 0)
+        add('view_1', g_v1.t() @ v0)
+        add('view_1_b', g_v1.float().sum(0))
+        g_v0 = (g_v1 @ w['view_1']) * (v0 > 0)
+        add('combined', g_v0.t() @ inputs)
+        add('skip', grad_outputs.t() @ inputs)
+        g_hidden = (g_v0 @ w['combined'][:, :64] + grad_outputs @ w['skip'][:, :64]) * (inputs[:, :64] > 0)
+        add('density', g_hidden.t() @ features)
+        add('density_b', g_hidden.float().sum(0))
+        return (g_hidden @ w['density']).contiguous()
+
+
+@dataclass
+class Level:
+    featurizer: object
+    table: torch.Tensor
+    grad: torch.Tensor
+    grad_half: torch.Tensor | None
+    magnitudes: torch.Tensor
+
+
+class TrainStep:
+    """One rank's model, optimizer and ray pool; run() is one training iteration on n_rays rays, this rank's share of a
+    global batch of world x n_rays random rays: each rank draws its rays, jitter, backgrounds and multisample patterns
+    from the iteration's seed with the rank in bits 40-55 (the reference draws them by local ray index, so equal seeds
+    would repeat the same rays on every rank)."""
+
+    def __init__(self, device, n_rays: int = 65536, rank: int = 0, world: int = 1, seed: int = 0, pool_views: int = 185) -> None:
+        import ZipNeRFCudaBackend as backend
+        from zipnerf_b200 import rows
+        self.backend, self.device, self.n_rays, self.rank, self.world = backend, device, n_rays, rank, world
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.levels = []
+        mags = []
+        for level, (n_levels, f) in enumerate(zip(GRID_LEVELS, GRID_FEATURES)):
+            sizes, entries = grid_layout(n_levels)
+            feat = backend.Featurizer(level, sizes, entries, f, MLP_WIDTH if level < 2 else 0)
+            table = (torch.rand(sum(entries), f, generator=g, device=device) * 2 - 1) * backend.grid_max_value
+            if level < 2:
+                grad, grad_half = torch.zeros(table.numel(), device=device), None
+            else:
+                split = feat.n_fp32_grad_rows * f
+                grad, grad_half = torch.zeros(split, device=device), torch.zeros(table.numel() - split, device=device, dtype=torch.float16)
+            offsets = np.cumsum([0] + entries)
+            m = torch.stack([(backend.grid_max_value ** 2 + table[a:b].square().mean()).sqrt() for a, b in zip(offsets[:-1], offsets[1:])])
+            mags.append(m)
+            self.levels.append(Level(feat, table, grad, grad_half, m))
+        self.magnitudes = torch.cat(mags).contiguous()
+        for i, level in enumerate(self.levels):  # views into the optimizer's magnitudes
+            a = sum(len(grid_layout(n)[1]) for n in GRID_LEVELS[:i])
+            level.magnitudes = self.magnitudes[a:a + GRID_LEVELS[i]]
+        # proposal MLPs: one flat buffer (w0 [64, n_out], b0 [64], w1 [64], b1 [1] per level), padded to 4
+        self.prop_layout = []
+        n = 0
+        for level in range(2):
+            n_out = GRID_LEVELS[level] * 2
+            self.prop_layout.append((n, n_out))
+            n += 64 * n_out + 64 + 64 + 1
+        self.prop_params = torch.zeros((n + 3) // 4 * 4, device=device)
+        for level, (a, n_out) in enumerate(self.prop_layout):
+            w0, _, w1, _ = self.proposal_mlp(self.prop_params, level)
+            w0.uniform_(-math.sqrt(6 / n_out), math.sqrt(6 / n_out), generator=g)
+            w1.uniform_(-math.sqrt(6 / 64), math.sqrt(6 / 64), generator=g)
+        self.prop_grads = torch.zeros_like(self.prop_params)
+        self.nerf_mlp = NerfMlp(device, g)
+        # the optimizer over the trainer's buffers (Trainer.py:44-57)
+        nerf = self.levels[2]
+        sizes, entries = grid_layout(GRID_LEVELS[2])
+        n_fp32 = sum(1 for e in entries if e < 2 ** 20)
+        split = nerf.featurizer.n_fp32_grad_rows * 4
+        params = [self.levels[0].table.view(-1), self.levels[1].table.view(-1), nerf.table.view(-1)[:split], nerf.table.view(-1)[split:],
+                  self.prop_params, self.nerf_mlp.params]
+        grads = [self.levels[0].grad, self.levels[1].grad, nerf.grad, nerf.grad_half, self.prop_grads, self.nerf_mlp.grads]
+        scale = backend.nerf_grid_grad_scale
+        offsets = [[int(o) for o in np.cumsum([0] + grid_layout(GRID_LEVELS[0])[1])], [int(o) for o in np.cumsum([0] + grid_layout(GRID_LEVELS[1])[1])],
+                   [int(o) * 4 for o in np.cumsum([0] + entries[:n_fp32])], [int(o) * 4 for o in np.cumsum([0] + entries[n_fp32:])], [], []]
+        self.grad_buffers = grads
+        self.optimizer = backend.Adam(params, grads, [1.0, 1.0, scale, scale, 1.0, 1.0], offsets, LOSS['grid_regularization'], backend.grid_max_value,
+                                      ADAM['beta1'], ADAM['beta2'], ADAM['eps'], self.magnitudes)
+        self.pool = rows.ray_pool(device, n_views=pool_views)
+        self.warp = rows.ray_warp(NEAR, FAR)
+        self.loss_sums = None
+
+    def proposal_mlp(self, buffer: torch.Tensor, level: int):
+        a, n_out = self.prop_layout[level]
+        w0 = buffer[a:a + 64 * n_out].view(64, n_out)
+        b0 = buffer[a + 64 * n_out:a + 64 * n_out + 64]
+        w1 = buffer[a + 64 * n_out + 64:a + 64 * n_out + 128].view(1, 64)
+        b1 = buffer[a + 64 * n_out + 128:a + 64 * n_out + 129]
+        return w0, b0, w1, b1
+
+    def run(self, iteration: int, lr: float | None = None, anneal: float | None = None, after_backward=None, exchange=None) -> None:
+        """One training iteration (learning rate and resampling anneal from the trainer's schedules unless given).
+        after_backward(buffers) is called with each group of gradient buffers as soon as they are final (the NeRF grid,
+        then each proposal level with the MLP buffers last); exchange() is called before the optimizer step (the
+        data-parallel average must have finished)."""
+        if lr is None:
+            lr = learning_rate(iteration)
+        if anneal is None:  # schlick_bias(iteration / NUM_ITERATIONS, ANNEAL_SLOPE) (utils.py:30-32, Trainer.py:135-136)
+            x = iteration / LR['max_steps']
+            anneal = 10.0 * x / (9.0 * x + 1.0)
+        b = self.backend
+        R, dev = self.n_rays, self.device
+        seed = iteration + (self.rank << 40)  # below the stream bits (random.cuh:20)
+        p = self.pool
+        origins, directions, radii, rgb, encoded, sdist, tdist = b.generate_rays(
+            seed, R, p['view_offsets'], p['view_cameras'], p['camera_offsets'], p['local_directions'], p['c2w'], p['camera_radii'], p['pool_rgb'],
+            DEGREE, N_SAMPLES[0], self.warp)
+        empty = torch.empty(0, device=dev)
+        proposals = []
+        for level in range(2):
+            lv = self.levels[level]
+            n = N_SAMPLES[level]
+            raw = torch.empty(R, n, device=dev)
+            feats = torch.empty(R * n, lv.featurizer.n_output_features, device=dev)
+            lv.featurizer.forward(origins, directions, radii, tdist, seed, False, lv.table, lv.magnitudes, *self.proposal_mlp(self.prop_params, level),
+                                  raw, feats, empty, empty, empty)
+            weights, s_next, t_next = b.composite_and_resample(raw, sdist, tdist, directions, anneal, N_SAMPLES[level + 1], seed, level + 1, self.warp)
+            proposals.append({'raw': raw, 'features': feats, 'sdist': sdist, 'tdist': tdist, 'weights': weights})
+            sdist, tdist = s_next, t_next
+        nerf = self.levels[2]
+        n = N_SAMPLES[2]
+        features = torch.empty(R * n, 56, device=dev, dtype=torch.bfloat16)
+        inputs = torch.empty(R * n, 96, device=dev, dtype=torch.bfloat16)
+        nerf.featurizer.forward(origins, directions, radii, tdist, seed, False, nerf.table, nerf.magnitudes, empty, empty, empty, empty, empty, empty,
+                                features, encoded, inputs)
+        outputs, context = self.nerf_mlp.forward(features, inputs)
+        grad_outputs, proposal_grads, self.loss_sums = b.train_final(
+            outputs.view(R, n, 8), sdist, tdist, [q['raw'] for q in proposals], [q['sdist'] for q in proposals], [q['tdist'] for q in proposals],
+            [q['weights'] for q in proposals], directions, seed, rgb, LOSS['charbonnier_padding'], [LOSS['interlevel']] * 2, list(LOSS['blurs']),
+            LOSS['distortion'], LOSS['distortion_power'], LOSS['distortion_premult'], True)
+        grad_features = self.nerf_mlp.backward(grad_outputs.view(R * n, 8), context)
+        nerf.featurizer.backward(origins, directions, radii, tdist, seed, grad_features, nerf.grad, nerf.grad_half)
+        if after_backward is not None:
+            after_backward([nerf.grad, nerf.grad_half, self.nerf_mlp.grads])
+        for level in range(2):
+            lv, q = self.levels[level], proposals[level]
+            gw0, gb0, gw1, gb1 = self.proposal_mlp(self.prop_grads, level)
+            lv.featurizer.backward_mlp(origins, directions, radii, q['tdist'], seed, q['features'], proposal_grads[level],
+                                       *self.proposal_mlp(self.prop_params, level)[:3], lv.grad, gw0, gb0, gw1.view(-1), gb1)
+            if after_backward is not None:
+                after_backward([lv.grad] + ([self.prop_grads] if level == 1 else []))
+        if exchange is not None:
+            exchange()
+        self.optimizer.step(lr)
+
+    @property
+    def samples_per_step(self) -> int:
+        """featurized samples (interval x multisample) of one step: the unit of the featurization metric"""
+        return self.n_rays * sum(N_SAMPLES) * 6

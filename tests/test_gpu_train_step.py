@@ -1,0 +1,33 @@
+"""The full training step on one GPU (zipnerf_b200/train_step.py): every stage runs through this backend's kernels in
+the reference trainer's order; after each step the losses are finite, every gradient buffer has been consumed and
+zeroed by the Adam step, the parameters and scale-feature magnitudes moved, and repeated steps stay finite."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def test_training_steps_run_and_update_the_model(cuda_device):
+    from zipnerf_b200 import train_step
+    step = train_step.TrainStep(cuda_device, n_rays=4096, pool_views=3)
+    tables = [level.table.clone() for level in step.levels]
+    mlp = (step.prop_params.clone(), step.nerf_mlp.params.clone())
+    magnitudes = step.magnitudes.clone()
+    losses = []
+    for iteration in range(3):
+        step.run(iteration)
+        torch.cuda.synchronize()
+        losses.append(step.loss_sums.clone())
+        # all four terms present: data, mse, interlevel (the proposal weights against the final ones), distortion
+        assert torch.isfinite(step.loss_sums).all() and (step.loss_sums > 0).all(), step.loss_sums
+        for buffer in step.grad_buffers:
+            assert not buffer.any(), 'the Adam step zeroes every gradient buffer'
+    for before, level in zip(tables, step.levels):
+        assert torch.isfinite(level.table).all() and not torch.equal(before, level.table)
+    assert not torch.equal(mlp[0], step.prop_params) and not torch.equal(mlp[1], step.nerf_mlp.params)
+    assert torch.isfinite(step.magnitudes).all() and not torch.equal(magnitudes, step.magnitudes)
+    assert float(step.optimizer.regularization()) > 0.0
+    # the data term (charbonnier, per ray) is bounded by the colors' range
+    assert all(0.0 < float(l[0]) < 2.0 for l in losses)
