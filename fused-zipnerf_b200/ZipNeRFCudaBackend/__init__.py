@@ -32,6 +32,7 @@ sample_uniforms = _C.sample_uniforms
 composite_and_resample = _C.composite_and_resample
 train_final = _C.train_final
 composite_final = _C.composite_final
+relu_backward_ = _C.relu_backward_  # addition: the ReLU backward + bias gradient of a bf16 layer (zf_mlp.h)
 
 _OTHER_SUBSYSTEMS = {'nerf_mlp_parameters', 'NerfMlp'}
 

@@ -4,7 +4,7 @@
 
 Outputs (next to the Python package that loads them, so they travel with the source tree):
   ZipNeRFCudaBackend/libzf_featurize.so  -- the sm_100a kernels and the C ABI of include/zf_featurize.h,
-                                            include/zf_sampling.h and include/zf_optim.h
+                                            include/zf_sampling.h, include/zf_optim.h and include/zf_mlp.h
   ZipNeRFCudaBackend/_C.<abi>.so         -- the PyTorch binding (ZipNeRFCudaBackend._C)
 
 Kernels are compiled ahead of time for sm_100a only (nvcc -gencode arch=compute_100a,code=sm_100a), one object per
@@ -71,9 +71,9 @@ def build_library(jobs: int | None = None, force: bool = False, subset: set | No
             wanted.append(obj)
             if force or _stale(obj, [inst, *deps]):
                 steps.append([NVCC, *NVCC_FLAGS, f'-DZF_INST_F={features}', f'-DZF_INST_PAD={pad}', '-c', str(inst), '-o', str(obj)])
-    # the C ABI translation units: featurizer objects, the sampling kernels, the Adam step
+    # the C ABI translation units: featurizer objects, the sampling kernels, the Adam step, the MLP's ReLU backward
     abi_objects = []
-    for name in ['fz_capi', 'fz_sampling', 'fz_optim']:
+    for name in ['fz_capi', 'fz_sampling', 'fz_optim', 'fz_mlp']:
         source, obj = CSRC / f'{name}.cu', BUILD / f'{name}.o'
         abi_objects.append(obj)
         if force or _stale(obj, [source, *deps]):

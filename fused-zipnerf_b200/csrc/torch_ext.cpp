@@ -11,6 +11,7 @@
 // output, as in the reference. All computation happens in libzf_featurize.so; this file only converts tensors to
 // pointers and allocates the outputs the reference's wrappers return.
 #include "zf_featurize.h"
+#include "zf_mlp.h"
 #include "zf_optim.h"
 #include "zf_sampling.h"
 
@@ -535,6 +536,25 @@ void composite_final(const at::Tensor& nerf_outputs, const at::Tensor& tdist, co
     check_status(zf_composite_final(&a, current_stream()));
 }
 
+// the ReLU backward of a bf16 layer with its bias gradient (no counterpart in the reference module: its NeRF MLP does
+// this in cuBLASLt epilogues); grad [n, c] masked in place by activation [n, c] (row-strided), bias_grad += column sums
+void relu_backward_(at::Tensor& grad, const at::Tensor& activation, const at::Tensor& bias_grad) {
+    if (!grad.is_cuda() || grad.scalar_type() != at::kBFloat16 || grad.dim() != 2 || grad.stride(1) != 1 || !activation.is_cuda()
+        || activation.scalar_type() != at::kBFloat16 || activation.dim() != 2 || activation.stride(1) != 1 || activation.size(0) != grad.size(0)
+        || activation.size(1) != grad.size(1)) {
+        throw std::runtime_error("ZipNeRF: relu_backward_ needs matching 2D bf16 cuda tensors with unit column stride");
+    }
+    float* bias = nullptr;
+    if (bias_grad.numel() > 0) {
+        check_input(bias_grad, "bias_grad", at::kFloat);
+        if (bias_grad.numel() != grad.size(1)) throw std::runtime_error("ZipNeRF: relu_backward_ bias_grad has the wrong size");
+        bias = bias_grad.data_ptr<float>();
+    }
+    const c10::cuda::CUDAGuard guard(grad.device());
+    check_status(zf_relu_backward_bf16(bf16_ptr(grad), grad.stride(0), reinterpret_cast<const uint16_t*>(activation.data_ptr()), activation.stride(0),
+                                       grad.size(0), static_cast<int>(grad.size(1)), bias, current_stream()));
+}
+
 // ---------------------------------------------------------------------------------------------------------------------
 // Adam (optimizer_api.h:14-40, optimizer_api.cu:123-221): the tensor checks and messages of the reference; the object
 // keeps the tensors it updates alive
@@ -629,4 +649,5 @@ PYBIND11_MODULE(_C, m) {
     m.def("composite_and_resample", &composite_and_resample);
     m.def("train_final", &train_final);
     m.def("composite_final", &composite_final);
+    m.def("relu_backward_", &relu_backward_);
 }

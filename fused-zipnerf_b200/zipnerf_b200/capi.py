@@ -1,4 +1,4 @@
-"""ctypes binding of the C ABI in include/zf_featurize.h, zf_sampling.h and zf_optim.h (libzf_featurize.so).
+"""ctypes binding of the C ABI in include/zf_featurize.h, zf_sampling.h, zf_optim.h and zf_mlp.h (libzf_featurize.so).
 
 This is the binding a Python host without the PyTorch extension would write against the library. ``CFeaturizer``
 adds a thin convenience layer that takes PyTorch CUDA tensors and passes their device pointers; the computation
@@ -20,7 +20,7 @@ EXPORTED = ['zf_featurizer_create', 'zf_featurizer_destroy', 'zf_featurizer_n_ou
             'zf_check_erf_saturation', 'zf_erf_saturation_threshold', 'zf_last_error', 'zf_grid_max_value', 'zf_nerf_grid_grad_scale',
             'zf_direction_block_width', 'zf_initialize_rays', 'zf_view_rays', 'zf_generate_rays', 'zf_sample_uniforms',
             'zf_composite_and_resample', 'zf_train_final', 'zf_composite_final', 'zf_adam_create', 'zf_adam_destroy', 'zf_adam_step',
-            'zf_adam_state']
+            'zf_adam_state', 'zf_relu_backward_bf16']
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -171,6 +171,9 @@ def load() -> ctypes.CDLL:
     lib.zf_adam_step.restype = ctypes.c_int
     lib.zf_adam_state.argtypes = [_p, ctypes.c_int, ctypes.POINTER(_p), ctypes.POINTER(_p), ctypes.POINTER(_i64)]
     lib.zf_adam_state.restype = ctypes.c_int
+    # zf_mlp.h
+    lib.zf_relu_backward_bf16.argtypes = [_p, _i64, _p, _i64, _i64, ctypes.c_int, _p, _p]
+    lib.zf_relu_backward_bf16.restype = ctypes.c_int
     _lib = lib
     return lib
 

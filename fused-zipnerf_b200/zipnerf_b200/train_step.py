@@ -11,9 +11,10 @@ of 10 levels x 4 features (base resolution 16, per-level scale 2, 2^21 entries),
 intervals per ray, the view-direction encoding of degree 4; the trainer's loss weights and Adam settings
 (Trainer.py:17-57). Data: a synthetic pool of 185 views of 1296 x 840 pixels (uniform-noise colors).
 
-Every kernel of the step is this backend's, except the NeRF MLP: it runs as cuBLAS bf16 GEMMs through torch (the
-layer shapes of the reference's cuBLASLt chain, nerf_mlp.cu:440-455,503-620, with elementwise ReLU and bias steps in
-torch), a stand-in of the same shape and cost, not the reference's numerics.
+Every kernel of the step is this backend's, except the NeRF MLP's GEMMs: they run as cuBLAS / cuBLASLt bf16 GEMMs
+through torch (the layer shapes of the reference's cuBLASLt chain, nerf_mlp.cu:440-455,503-620, with the forward's bias
+and ReLU in the GEMM epilogues and the backward's ReLU masks and bias gradients in this backend's relu_backward_), a
+stand-in of the same shape and cost, not the reference's numerics.
 """
 from __future__ import annotations
 
@@ -75,44 +76,50 @@ class NerfMlp:
                 bound = math.sqrt(6.0 / shape[1])
                 self.view(self.params, name).uniform_(-bound, bound, generator=generator)
         self.grads = torch.zeros_like(self.params)
+        self.zero_bias = torch.zeros(256, device=device, dtype=torch.bfloat16)
 
     def view(self, buffer: torch.Tensor, name: str) -> torch.Tensor:
         offset, shape = self.offsets[name]
         return buffer[offset:offset + math.prod(shape)].view(shape)
 
     def forward(self, features: torch.Tensor, inputs: torch.Tensor):
+        # bias + ReLU in the GEMM epilogue (cuBLASLt through torch), as the reference's RELU_BIAS epilogues
         w = {name: self.view(self.params, name).to(torch.bfloat16) for name, _ in self.SHAPES}
-        hidden = torch.relu(torch.addmm(w['density_b'], features, w['density'].t()))
-        inputs[:, :64] = hidden
-        v0 = torch.relu(inputs @ w['combined'].t())
+        inputs[:, :64] = torch._addmm_activation(w['density_b'], features, w['density'].t())
+        v0 = torch._addmm_activation(self.zero_bias, inputs, w['combined'].t())
         outputs = inputs @ w['skip'].t()
-        v1 = torch.relu(torch.addmm(w['view_1_b'], v0, w['view_1'].t()))
-        v2 = torch.relu(torch.addmm(w['view_2_b'], v1, w['view_2'].t()))
+        v1 = torch._addmm_activation(w['view_1_b'], v0, w['view_1'].t())
+        v2 = torch._addmm_activation(w['view_2_b'], v1, w['view_2'].t())
         outputs += v2 @ w['rgb'].t()
-        return outputs.contiguous(), (w, features, inputs, v0, v1, v2)
+        return outputs, (w, features, inputs, v0, v1, v2)
 
     def backward(self, grad_outputs: torch.Tensor, context) -> torch.Tensor:
-        """Accumulates the parameter gradients (fp32) and returns the feature gradient [n, 56] bf16."""
+        """Accumulates the parameter gradients (fp32) and returns the feature gradient [n, 56] bf16. The ReLU masks and
+        bias gradients take one pass per layer (relu_backward_, this backend's kernel for the reference's DRELU_BGRAD
+        epilogues)."""
+        import ZipNeRFCudaBackend as backend
         w, features, inputs, v0, v1, v2 = context
         g = self.grads
+        empty = g[:0]
 
         def add(name, value):
             self.view(g, name).add_(value.float())
 
         add('rgb', grad_outputs.t() @ v2)
-        g_v2 = (grad_outputs @ w['rgb']) * (v2 > 0)
+        g_v2 = grad_outputs @ w['rgb']
+        backend.relu_backward_(g_v2, v2, self.view(g, 'view_2_b'))
         add('view_2', g_v2.t() @ v1)
-        add('view_2_b', g_v2.float().sum(0))
-        g_v1 = (g_v2 @ w['view_2']) * (v1 > 0)
+        g_v1 = g_v2 @ w['view_2']
+        backend.relu_backward_(g_v1, v1, self.view(g, 'view_1_b'))
         add('view_1', g_v1.t() @ v0)
-        add('view_1_b', g_v1.float().sum(0))
-        g_v0 = (g_v1 @ w['view_1']) * (v0 > 0)
+        g_v0 = g_v1 @ w['view_1']
+        backend.relu_backward_(g_v0, v0, empty)
         add('combined', g_v0.t() @ inputs)
         add('skip', grad_outputs.t() @ inputs)
-        g_hidden = (g_v0 @ w['combined'][:, :64] + grad_outputs @ w['skip'][:, :64]) * (inputs[:, :64] > 0)
+        g_hidden = torch.addmm(grad_outputs @ w['skip'][:, :64], g_v0, w['combined'][:, :64])
+        backend.relu_backward_(g_hidden, inputs[:, :64], self.view(g, 'density_b'))
         add('density', g_hidden.t() @ features)
-        add('density_b', g_hidden.float().sum(0))
-        return (g_hidden @ w['density']).contiguous()
+        return g_hidden @ w['density']
 
 
 @dataclass

@@ -1,6 +1,7 @@
 """The full training step on one GPU (zipnerf_b200/train_step.py): every stage runs through this backend's kernels in
 the reference trainer's order; after each step the losses are finite, every gradient buffer has been consumed and
-zeroed by the Adam step, the parameters and scale-feature magnitudes moved, and repeated steps stay finite."""
+zeroed by the Adam step, the parameters and scale-feature magnitudes moved, and repeated steps stay finite. Also the
+NeRF MLP's ReLU backward with bias gradient (zf_mlp.h) against plain PyTorch."""
 from __future__ import annotations
 
 import pytest
@@ -31,3 +32,26 @@ def test_training_steps_run_and_update_the_model(cuda_device):
     assert float(step.optimizer.regularization()) > 0.0
     # the data term (charbonnier, per ray) is bounded by the colors' range
     assert all(0.0 < float(l[0]) < 2.0 for l in losses)
+
+
+@pytest.mark.parametrize('cols,act_cols', [(256, 256), (64, 96), (8, 8), (24, 24)])
+def test_relu_backward_matches_torch(cuda_device, cols, act_cols):
+    """The masked gradient equals PyTorch's grad * (act > 0) exactly (NaN activations mask); the bias gradient (fp32
+    column sums, atomics) to summation order. act_cols > cols: the activation is a column slice of a wider buffer."""
+    import ZipNeRFCudaBackend as backend
+    g = torch.Generator(device=cuda_device).manual_seed(cols)
+    n = 10007
+    grad = torch.randn(n, cols, generator=g, device=cuda_device).to(torch.bfloat16)
+    act_full = torch.randn(n, act_cols, generator=g, device=cuda_device).relu().to(torch.bfloat16)
+    act_full[::97, 0] = float('nan')
+    act = act_full[:, :cols]
+    expected = torch.where(act > 0, grad, torch.zeros_like(grad))
+    bias = torch.full((cols,), 0.5, device=cuda_device)
+    out = grad.clone()
+    backend.relu_backward_(out, act, bias)
+    torch.cuda.synchronize()
+    assert torch.equal(out, expected)
+    torch.testing.assert_close(bias, 0.5 + expected.float().sum(0), rtol=1e-4, atol=1e-3)
+    out2 = grad.clone()
+    backend.relu_backward_(out2, act, torch.empty(0, device=cuda_device))
+    assert torch.equal(out2, expected)

@@ -102,6 +102,17 @@ def test_sampling_and_adam_validate_before_touching_a_device():
     assert lib.zf_adam_step(None, 0.1, None) == capi.ZF_ERROR_INVALID_ARGUMENT
 
 
+def test_relu_backward_validates_its_layout():
+    from zipnerf_b200 import capi
+    lib = capi.load()
+    fake = 1 << 20  # never dereferenced
+    for cols, grad_stride, act_stride in [(12, 16, 16), (520, 520, 520), (64, 60, 64), (64, 64, 100), (0, 8, 8)]:
+        assert lib.zf_relu_backward_bf16(fake, grad_stride, fake, act_stride, 10, cols, None, None) == capi.ZF_ERROR_INVALID_ARGUMENT
+    assert lib.zf_relu_backward_bf16(fake + 2, 64, fake, 64, 10, 64, None, None) == capi.ZF_ERROR_INVALID_ARGUMENT
+    assert b'16-byte aligned' in lib.zf_last_error()
+    assert lib.zf_relu_backward_bf16(None, 64, None, 64, 0, 64, None, None) == capi.ZF_OK  # nothing to do
+
+
 @pytest.mark.skipif(torch.cuda.is_available(), reason='checks the error path of a machine without a GPU')
 def test_create_without_device_reports_cuda_error():
     from zipnerf_b200 import capi
