@@ -44,7 +44,9 @@ ZF_API int zf_adam_create(const zf_adam_buffer* buffers, int n_buffers, double r
                           double eps, float* magnitudes, int64_t n_magnitudes, float* regularization, zf_adam** out);
 ZF_API void zf_adam_destroy(zf_adam* adam);
 
-/* Adam::step (optimizer_api.cu:160-220): the next step (counting from 1) with learning rate lr, on the stream. */
+/* Adam::step (optimizer_api.cu:160-220): the next step (counting from 1) with learning rate lr, on the stream. The
+ * steps of one object share its scratch arrays (per-block sums, a completion counter that the last block resets):
+ * enqueue them on one stream, or order them, as the reference's single-stream use does. */
 ZF_API int zf_adam_step(zf_adam* adam, double lr, struct CUstream_st* stream);
 
 /* The moments of one buffer (device float [numel] each) and the steps taken so far; no counterpart in the reference,
