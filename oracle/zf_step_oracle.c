@@ -259,3 +259,231 @@ void oracle_adam_buffer(float* params, void* grads, int grad_half, float* exp_av
         if (n_offsets > 0) level_sums[level] += (double)p * (double)p;
     }
 }
+
+/* ------------------------------------------------------------------------------------------------------------------
+ * The final level (sampling_api.cu:203-424 with ray_ops.cuh:20-24,91-166): training losses and the gradients of all
+ * levels' raw outputs, and the inference compositing. bf16 values are their 16-bit patterns. */
+#define NERF_OUTPUTS 8
+#define RGB_PADDING 0.001f
+#define MAX_PROPOSAL_LEVELS 4
+
+static float from_bf16(uint16_t bits) {
+    uint32_t word = (uint32_t)bits << 16;
+    float value;
+    memcpy(&value, &word, sizeof(value));
+    return value;
+}
+
+static float ladder(float x, float p, float premult) { /* ray_ops.cuh:20-24 */
+    float xp = fabsf(x * premult);
+    float y = fabsf(p - 1.0f) / p * (powf(xp / fabsf(p - 1.0f) + 1.0f, p) - 1.0f);
+    return copysignf(y, x);
+}
+
+static void alpha_composite(const float* density, const float* t, int n, float norm, float* w, float* x) { /* ray_ops.cuh:91-99 */
+    float depth = 0.0f;
+    for (int i = 0; i < n; i++) {
+        float xi = density[i] * (t[i + 1] - t[i]) * norm;
+        w[i] = -expm1f(-xi) * expf(-depth);
+        depth += xi;
+        x[i] = xi;
+    }
+}
+
+static void alpha_composite_backward(float* grad, const float* x, const float* w, int n) { /* ray_ops.cuh:102-117 */
+    float transmittance[MAX_INTERVALS], depth = 0.0f, suffix = 0.0f;
+    for (int i = 0; i < n; i++) {
+        depth += x[i];
+        transmittance[i] = expf(-depth);
+    }
+    for (int i = n - 1; i >= 0; i--) {
+        float g = grad[i];
+        grad[i] = g * transmittance[i] - suffix;
+        suffix += g * w[i];
+    }
+}
+
+static float up(float x) { return fabsf(x) < FLT_MIN ? FLT_MIN : nextafterf(x, INFINITY); }
+static float down(float x) { return fabsf(x) < FLT_MIN ? -FLT_MIN : nextafterf(x, -INFINITY); }
+
+/* the histogram (t, w) of n bins blurred by a box of half width h, resampled into the nq - 1 bins of tq
+ * (ray_ops.cuh:121-166) */
+static void blur_resample(const float* tq, int nq, const float* t, const float* w, int n, float h, float* out) {
+    float lo[MAX_INTERVALS + 1], hi[MAX_INTERVALS + 1], dslope[MAX_INTERVALS + 1];
+    float previous_pdf = 0.0f;
+    for (int i = 0; i <= n; i++) {
+        float dt = i < n ? t[i + 1] - t[i] : 0.0f;
+        float pdf = (i < n && dt >= FLT_MIN) ? w[i] / dt : 0.0f;
+        lo[i] = t[i] - h;
+        hi[i] = fmaxf(up(t[i]), t[i] + h);
+        dslope[i] = (pdf - previous_pdf) / (hi[i] - lo[i]);
+        previous_pdf = pdf;
+    }
+    float knots[2 * (MAX_INTERVALS + 1)], values[2 * (MAX_INTERVALS + 1)];
+    int n_knots = 2 * (n + 1), a = 0, b = 0;
+    float slope = 0.0f;
+    for (int k = 0; k < n_knots; k++) {
+        int take_lo = b > n || (a <= n && lo[a] <= hi[b]);
+        float knot = take_lo ? lo[a] : hi[b];
+        values[k] = (k == 0 || k == n_knots - 1) ? 0.0f : values[k - 1] + (knot - knots[k - 1]) * slope;
+        knots[k] = knot;
+        if (k < n_knots - 2) slope += take_lo ? dslope[a] : -dslope[b];
+        if (take_lo) a++;
+        else b++;
+    }
+    float first = knots[0], last = down(knots[n_knots - 1]), area = 0.0f, previous = 0.0f;
+    int k = 0;
+    for (int j = 0; j < nq; j++) {
+        float q = fminf(fmaxf(tq[j], first), last);
+        while (k + 2 < n_knots && knots[k + 1] <= q) {
+            area += 0.5f * (knots[k + 1] - knots[k]) * (values[k] + values[k + 1]);
+            k++;
+        }
+        float c = (values[k + 1] - values[k]) / fmaxf(FLT_EPSILON * FLT_EPSILON, 2.0f * (knots[k + 1] - knots[k]));
+        float td = q - knots[k];
+        float value = (c * td + values[k]) * td + area;
+        if (j > 0) out[j - 1] = fmaxf(value - previous, 0.0f);
+        previous = value;
+    }
+}
+
+/* densities, rgb sigmoids, optical depths and weights of one ray of the final level (sampling_api.cu:203-220) */
+static void final_level(const uint16_t* outputs, const float* t, int n, float norm, float* density, float* x, float* w, float (*sig)[3]) {
+    for (int i = 0; i < n; i++) {
+        const uint16_t* raw = outputs + NERF_OUTPUTS * i;
+        float r[4] = {from_bf16(raw[0]), from_bf16(raw[1]), from_bf16(raw[2]), from_bf16(raw[3])};
+        int valid = isfinite(r[0]) && isfinite(r[1]) && isfinite(r[2]) && isfinite(r[3]);
+        density[i] = valid ? expf(fminf(r[0] - 1.0f, 88.72283f)) : 0.0f;
+        for (int c = 0; c < 3; c++) sig[i][c] = valid ? 1.0f / (1.0f + expf(-r[c + 1])) : 0.5f;
+    }
+    alpha_composite(density, t, n, norm, w, x);
+}
+
+static float padded(float s) { return s * (1.0f + 2.0f * RGB_PADDING) - RGB_PADDING; }
+
+/* the weights' gradients -> the raw densities (sampling_api.cu:223-229) */
+static void weights_to_raw(float* grad, const float* x, const float* w, const float* density, const float* raw, const float* t, int n, float norm) {
+    alpha_composite_backward(grad, x, w, n);
+    for (int i = 0; i < n; i++) grad[i] = raw[i] - 1.0f > 88.72283f ? 0.0f : grad[i] * (t[i + 1] - t[i]) * norm * density[i];
+}
+
+/* train_final (sampling_api.cu:231-376); loss_sums (double [4]) += this batch's sums */
+void oracle_train_final(const uint16_t* outputs, const float* sdist, const float* tdist, int n_rays, int n, int n_levels, const int* n_p,
+                        const float* const* raw_p, const float* const* sdist_p, const float* const* tdist_p, const float* const* weights_p,
+                        float* const* grad_p_out, const float* interlevel_weights, const float* interlevel_blurs, const float* directions,
+                        uint64_t seed, const float* rgb_target, float padding, float distortion_weight, float distortion_power,
+                        float distortion_premult, uint16_t* outputs_grad, double* loss_sums) {
+    float inv_n_rays = 1.0f / (float)n_rays;
+    for (int r = 0; r < n_rays; r++) {
+        const float* t = tdist + (int64_t)r * (n + 1);
+        const float* s = sdist + (int64_t)r * (n + 1);
+        float norm = norm3(directions + 3 * (int64_t)r);
+        float density[MAX_INTERVALS], x[MAX_INTERVALS], w[MAX_INTERVALS], grad_w[MAX_INTERVALS], sig[MAX_INTERVALS][3];
+        final_level(outputs + (int64_t)NERF_OUTPUTS * r * n, t, n, norm, density, x, w, sig);
+        float rgb[3] = {0.0f, 0.0f, 0.0f}, acc = 0.0f;
+        for (int i = 0; i < n; i++) {
+            for (int c = 0; c < 3; c++) rgb[c] += w[i] * padded(sig[i][c]);
+            acc += w[i];
+        }
+        float bg[3], grad_rgb[3];
+        for (int c = 0; c < 3; c++) bg[c] = uniform(seed, 1, 3 * (uint64_t)r + (uint64_t)c);
+        float background_weight = fmaxf(1.0f - acc, 0.0f);
+        for (int c = 0; c < 3; c++) {
+            float residual = rgb[c] + background_weight * bg[c] - rgb_target[3 * (int64_t)r + c];
+            float q = sqrtf(residual * residual + padding * padding);
+            loss_sums[0] += q * inv_n_rays / 3.0f;
+            loss_sums[1] += residual * residual * inv_n_rays / 3.0f;
+            grad_rgb[c] = residual / q * inv_n_rays / 3.0f;
+        }
+        float grad_background = 1.0f - acc >= 0.0f ? grad_rgb[0] * bg[0] + grad_rgb[1] * bg[1] + grad_rgb[2] * bg[2] : 0.0f;
+        for (int i = 0; i < n; i++) {
+            grad_w[i] = grad_rgb[0] * padded(sig[i][0]) + grad_rgb[1] * padded(sig[i][1]) + grad_rgb[2] * padded(sig[i][2]) - grad_background;
+        }
+        /* distortion loss on the curved distances */
+        float u[MAX_INTERVALS], ds[MAX_INTERVALS], prev = ladder(t[0], distortion_power, distortion_premult), w_total = 0.0f, wu_total = 0.0f;
+        for (int i = 0; i < n; i++) {
+            float next = ladder(t[i + 1], distortion_power, distortion_premult);
+            u[i] = 0.5f * (prev + next);
+            ds[i] = next - prev;
+            prev = next;
+            w_total += w[i];
+            wu_total += w[i] * u[i];
+        }
+        float scale = distortion_weight * inv_n_rays, w_before = 0.0f, wu_before = 0.0f, loss = 0.0f;
+        for (int i = 0; i < n; i++) {
+            float w_after = w_total - w_before - w[i], wu_after = wu_total - wu_before - w[i] * u[i];
+            float inter = u[i] * w_before - wu_before + wu_after - u[i] * w_after;
+            loss += w[i] * (u[i] * w_before - wu_before) * 2.0f + w[i] * w[i] * ds[i] / 3.0f;
+            grad_w[i] += scale * (2.0f * inter + 2.0f / 3.0f * w[i] * ds[i]);
+            w_before += w[i];
+            wu_before += w[i] * u[i];
+        }
+        loss_sums[3] += scale * loss;
+        /* gradients of the raw outputs */
+        float raw[MAX_INTERVALS];
+        for (int i = 0; i < n; i++) raw[i] = from_bf16(outputs[(int64_t)NERF_OUTPUTS * ((int64_t)r * n + i)]);
+        weights_to_raw(grad_w, x, w, density, raw, t, n, norm);
+        for (int i = 0; i < n; i++) {
+            uint16_t* g = outputs_grad + (int64_t)NERF_OUTPUTS * ((int64_t)r * n + i);
+            float color_scale = w[i] * (1.0f + 2.0f * RGB_PADDING);
+            g[0] = to_bf16(grad_w[i]);
+            for (int c = 0; c < 3; c++) g[c + 1] = to_bf16(color_scale * grad_rgb[c] * sig[i][c] * (1.0f - sig[i][c]));
+            for (int c = 4; c < NERF_OUTPUTS; c++) g[c] = to_bf16(0.0f);
+        }
+        /* interlevel losses of the proposal levels */
+        for (int level = 0; level < n_levels; level++) {
+            int m = n_p[level];
+            const float* sp = sdist_p[level] + (int64_t)r * (m + 1);
+            const float* tp = tdist_p[level] + (int64_t)r * (m + 1);
+            const float* wp = weights_p[level] + (int64_t)r * m;
+            float gp[MAX_INTERVALS], rawp[MAX_INTERVALS], densityp[MAX_INTERVALS], xp[MAX_INTERVALS];
+            blur_resample(sp, m + 1, s, w, n, interlevel_blurs[level], gp);
+            float lscale = interlevel_weights[level] * inv_n_rays / (float)(m > 1 ? m : 1);
+            for (int i = 0; i < m; i++) {
+                float resid = fmaxf(gp[i] - wp[i], 0.0f), denominator = wp[i] + FLT_EPSILON;
+                loss_sums[2] += lscale * resid * resid / denominator;
+                gp[i] = lscale * (-2.0f * resid / denominator - resid * resid / (denominator * denominator));
+                rawp[i] = raw_p[level][(int64_t)r * m + i];
+                densityp[i] = expf(fminf(rawp[i] - 1.0f, 88.72283f));
+                xp[i] = densityp[i] * (tp[i + 1] - tp[i]) * norm;
+            }
+            weights_to_raw(gp, xp, wp, densityp, rawp, tp, m, norm);
+            for (int i = 0; i < m; i++) grad_p_out[level][(int64_t)r * m + i] = gp[i];
+        }
+    }
+}
+
+/* composite_final (sampling_api.cu:379-424); alpha / depth may be NULL */
+void oracle_composite_final(const uint16_t* outputs, const float* tdist, const float* directions, const float* background, const int64_t* pixels,
+                            int n_rays, int n, float* rgb, float* alpha, float* depth, int use_median_depth) {
+    for (int r = 0; r < n_rays; r++) {
+        const float* t = tdist + (int64_t)r * (n + 1);
+        float density[MAX_INTERVALS], x[MAX_INTERVALS], w[MAX_INTERVALS], sig[MAX_INTERVALS][3];
+        final_level(outputs + (int64_t)NERF_OUTPUTS * r * n, t, n, norm3(directions + 3 * (int64_t)r), density, x, w, sig);
+        float color[3] = {0.0f, 0.0f, 0.0f}, acc = 0.0f;
+        for (int i = 0; i < n; i++) {
+            for (int c = 0; c < 3; c++) color[c] += w[i] * padded(sig[i][c]);
+            acc += w[i];
+        }
+        float background_weight = fmaxf(1.0f - acc, 0.0f);
+        int64_t p = pixels[r];
+        for (int c = 0; c < 3; c++) rgb[3 * p + c] = color[c] + background_weight * background[c];
+        if (alpha) alpha[p] = acc;
+        if (!depth) continue;
+        if (use_median_depth) {
+            float target = 0.5f * acc, cw = 0.0f, median = t[n];
+            for (int i = 0; i < n; i++) {
+                cw += w[i];
+                if (w[i] > 0.0f && cw >= target) {
+                    median = t[i];
+                    break;
+                }
+            }
+            depth[p] = median;
+        } else {
+            float weighted = 0.0f;
+            for (int i = 0; i < n; i++) weighted += w[i] * logf(0.5f * (t[i] + t[i + 1]));
+            depth[p] = fminf(fmaxf(expf(weighted / fmaxf(acc, FLT_EPSILON)), t[0]), t[n]);
+        }
+    }
+}

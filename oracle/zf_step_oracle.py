@@ -1,4 +1,5 @@
-"""ctypes binding of the CPU checkers of the sampling steps and the Adam step (TEST INFRASTRUCTURE ONLY).
+"""ctypes binding of the CPU checkers of the sampling steps, the final level and the Adam step (TEST INFRASTRUCTURE
+ONLY).
 
 ``StepOracle`` wraps the C restatement (oracle/zf_step_oracle.c -> oracle/_build/libzf_step_oracle.so); ``RefSamplingCpu``
 wraps the reference's own per-ray sampling functions built for the host (oracle/ref_cpu/ref_sampling.cpp ->
@@ -46,7 +47,7 @@ def ray_warp(near: float, far: float, power: float = -1.5, premult: float = 2.0)
 
 
 class _Sampling:
-    """The five sampling entry points over one library whose functions carry the given prefix."""
+    """The sampling and final-level entry points over one library whose functions carry the given prefix."""
 
     def __init__(self, lib: ctypes.CDLL, prefix: str) -> None:
         self.lib, self.prefix = lib, prefix
@@ -58,7 +59,9 @@ class _Sampling:
         f('generate_rays').argtypes = [_i64, _i32, _p, _i32, _p, _p, _p, _p, _p, _p, _i64, _i32, _i32, _p, _p, _p, _p, _p, _p, _p, _p]
         f('sample_uniforms').argtypes = [_i64, _i64, _i64, _p]
         f('composite_and_resample').argtypes = [_p, _p, _p, _p, _i32, _i32, _f32, _i32, _i64, _i32, _p, _p, _p, _p]
-        for name in ['initialize_rays', 'view_rays', 'generate_rays', 'sample_uniforms', 'composite_and_resample']:
+        f('train_final').argtypes = [_p, _p, _p, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, ctypes.c_uint64, _p, _f32, _f32, _f32, _f32, _p, _p]
+        f('composite_final').argtypes = [_p, _p, _p, _p, _p, _i32, _i32, _p, _p, _p, _i32]
+        for name in ['initialize_rays', 'view_rays', 'generate_rays', 'sample_uniforms', 'composite_and_resample', 'train_final', 'composite_final']:
             f(name).restype = None
 
     def _f(self, name: str):
@@ -122,6 +125,42 @@ class _Sampling:
         self._f('composite_and_resample')(_ptr(raw), _ptr(s), _ptr(t), _ptr(d), n_rays, n, anneal, n_samples, seed, next_level, _ptr(_warp(warp)),
                                           _ptr(weights), _ptr(s_next), _ptr(t_next))
         return weights, s_next, t_next
+
+    def train_final(self, outputs, sdist, tdist, proposals, directions, seed: int, rgb_target, charbonnier_padding: float, distortion_weight: float,
+                    distortion_power: float, distortion_premult: float):
+        """outputs: bf16 bit patterns uint16 [R, n, 8]; proposals: dicts of raw_density, sdist, tdist, weights (numpy),
+        interlevel_weight, interlevel_blur. Returns (gradient bits uint16 [R, n, 8], [proposal gradients], loss sums
+        float64 [4])."""
+        out = np.ascontiguousarray(outputs, np.uint16)
+        s, t = np.ascontiguousarray(sdist, np.float32), np.ascontiguousarray(tdist, np.float32)
+        d, target = np.ascontiguousarray(directions, np.float32), np.ascontiguousarray(rgb_target, np.float32)
+        n_rays, n1 = t.shape
+        k = len(proposals)
+        arrays = [{key: np.ascontiguousarray(p[key], np.float32) for key in ('raw_density', 'sdist', 'tdist', 'weights')} for p in proposals]
+        grads = [np.zeros_like(a['raw_density']) for a in arrays]
+        ptrs = lambda key: (_p * max(k, 1))(*[a[key].ctypes.data for a in arrays])  # noqa: E731
+        n_p = (_i32 * max(k, 1))(*[a['raw_density'].shape[1] for a in arrays])
+        weights = np.array([p['interlevel_weight'] for p in proposals] or [0], np.float32)
+        blurs = np.array([p['interlevel_blur'] for p in proposals] or [0], np.float32)
+        grad_ptrs = (_p * max(k, 1))(*[g.ctypes.data for g in grads])
+        out_grad = np.zeros_like(out)
+        sums = np.zeros(4, np.float64)
+        self._f('train_final')(_ptr(out), _ptr(s), _ptr(t), n_rays, n1 - 1, k, n_p, ptrs('raw_density'), ptrs('sdist'), ptrs('tdist'), ptrs('weights'),
+                               grad_ptrs, _ptr(weights), _ptr(blurs), _ptr(d), seed, _ptr(target), charbonnier_padding, distortion_weight,
+                               distortion_power, distortion_premult, _ptr(out_grad), _ptr(sums))
+        return out_grad, grads, sums
+
+    def composite_final(self, outputs, tdist, directions, background, pixel_indices, n_pixels: int, use_median_depth: bool):
+        """Returns (rgb [pixels, 3], alpha [pixels], depth [pixels]); pixels that no ray writes stay -1."""
+        out = np.ascontiguousarray(outputs, np.uint16)
+        t = np.ascontiguousarray(tdist, np.float32)
+        d = np.ascontiguousarray(directions, np.float32)
+        bg = np.ascontiguousarray(background, np.float32)
+        px = np.ascontiguousarray(pixel_indices, np.int64)
+        rgb, alpha, depth = np.full((n_pixels, 3), -1, np.float32), np.full(n_pixels, -1, np.float32), np.full(n_pixels, -1, np.float32)
+        self._f('composite_final')(_ptr(out), _ptr(t), _ptr(d), _ptr(bg), _ptr(px), t.shape[0], t.shape[1] - 1, _ptr(rgb), _ptr(alpha), _ptr(depth),
+                                   int(use_median_depth))
+        return rgb, alpha, depth
 
 
 class StepOracle(_Sampling):

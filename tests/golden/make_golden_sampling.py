@@ -1,9 +1,10 @@
 """Generates tests/golden/sampling.npz: golden vectors of the sampling steps from the reference itself.
 
 The reference has no stored fixtures for its sampling kernels. These vectors are outputs of the reference's own per-ray
-sampling functions (ZipNeRFCudaBackend/ZipNeRFCudaBackend/sampling/include/ray_ops.cuh, common/include/random.cuh)
-compiled for the host by oracle/ref_cpu/ref_sampling.cpp (oracle/_ref/libzf_ref_sampling_cpu.so), on the seeded inputs
-of tests/sampling_cases.py. They pin the C restatement (oracle/zf_step_oracle.c) bit for bit.
+sampling and final-level functions (ZipNeRFCudaBackend/ZipNeRFCudaBackend/sampling/include/ray_ops.cuh,
+common/include/random.cuh) compiled for the host by oracle/ref_cpu/ref_sampling.cpp
+(oracle/_ref/libzf_ref_sampling_cpu.so), on the seeded inputs of tests/sampling_cases.py. They pin the C restatement
+(oracle/zf_step_oracle.c) bit for bit.
 
 Run where the reference sources exist (they are needed to build oracle/_ref):
     make -C oracle all ref && python tests/golden/make_golden_sampling.py
@@ -48,6 +49,16 @@ def cases(ref: RefSamplingCpu) -> dict:
     for key, value in zip(['origins', 'directions', 'radii', 'rgb', 'encoded', 'sdist', 'tdist'], gen):
         out[f'generate_{key}'] = value
     out['uniforms'] = ref.sample_uniforms(9, 2, 100)
+    # the final level on inputs from the resampling chain (computed here by the reference's own functions)
+    fin = sc.final_case(ref, 33, 4)
+    grad, proposal_grads, sums = ref.train_final(fin['nerf_outputs'], fin['sdist'], fin['tdist'], fin['proposals'], fin['directions'], fin['seed'],
+                                                 fin['rgb_target'], *sc.LOSS_ARGS)
+    out.update({'final_outputs_grad': grad, 'final_proposal0_grad': proposal_grads[0], 'final_proposal1_grad': proposal_grads[1], 'final_loss_sums': sums})
+    pixels = np.random.default_rng(7).permutation(33)
+    for median in (False, True):
+        rgb, alpha, depth = ref.composite_final(fin['nerf_outputs'], fin['tdist'], fin['directions'], np.array([0.2, 0.5, 0.9], np.float32), pixels, 33,
+                                                median)
+        out.update({f'composite_median{int(median)}_rgb': rgb, f'composite_median{int(median)}_alpha': alpha, f'composite_median{int(median)}_depth': depth})
     return out
 
 

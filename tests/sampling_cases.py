@@ -100,3 +100,30 @@ def adam_case(seed: int, level_sizes=((64, 512, 4096), (1024, 2048)), mlp: int =
         offsets.append([int(v) for v in np.cumsum([0] + list(sizes))] if sizes is not None else [])
     return {'params': params, 'grads': grads, 'grad_scales': scales, 'level_offsets': offsets, 'reg_weight': 0.1, 'max_value': 1e-5,
             'beta1': 0.9, 'beta2': 0.99, 'eps': 1e-15}
+
+
+def final_case(oracle, n_rays: int, seed: int, n_final: int = 32) -> dict:
+    """Inputs of the final level (train_final / composite_final): both proposal levels' raw densities N(0, 3), their
+    edges and compositing weights from the CPU restatement's own resampling chain (64 -> 64 -> n_final intervals),
+    NeRF outputs N(0, 2) as bf16 bit patterns with a few NaN and infinite entries (empty samples), random targets."""
+    rng = np.random.default_rng(seed)
+    d = directions(rng, n_rays)
+    _, s, t = oracle.initialize_rays(seed, d, DEGREE, 64, WARP)
+    proposals = []
+    for level, n_next in ((1, 64), (2, n_final)):
+        raw = (rng.normal(size=(n_rays, s.shape[1] - 1)) * 3.0).astype(np.float32)
+        w, s_next, t_next = oracle.composite_and_resample(raw, s, t, d, 0.7, n_next, seed, level, WARP)
+        proposals.append({'raw_density': raw, 'sdist': s, 'tdist': t, 'weights': w, 'interlevel_weight': 0.01,
+                          'interlevel_blur': (0.03, 0.003)[level - 1]})
+        s, t = s_next, t_next
+    outputs = (rng.normal(size=(n_rays, n_final, 8)) * 2.0).astype(np.float32)
+    outputs[..., 4:] = 0.0
+    outputs[rng.uniform(size=outputs.shape) < 0.002] = np.nan
+    outputs[rng.uniform(size=outputs.shape) < 0.002] = np.inf
+    bits = ((outputs.view(np.uint32) + 0x7fff + ((outputs.view(np.uint32) >> 16) & 1)) >> 16).astype(np.uint16)  # round to nearest even
+    bits[np.isnan(outputs)] = 0x7fc0
+    return {'nerf_outputs': bits, 'sdist': s, 'tdist': t, 'proposals': proposals, 'directions': d, 'seed': seed + 1000,
+            'rgb_target': rng.uniform(size=(n_rays, 3)).astype(np.float32)}
+
+
+LOSS_ARGS = (0.001, 0.01, -0.25, 10000.0)  # charbonnier padding, distortion weight, power, premult (Trainer.py:24-33)

@@ -263,6 +263,41 @@ def test_composite_final_matches_reference_kernel(ref, capi, cuda_device, use_me
     assert_same_bits(rgb, images['ours'][0], 'binding rgb')
 
 
+@pytest.mark.parametrize('n_rays,seed', [(33, 4), (300, 8)])
+def test_final_level_against_cpu_oracle(capi, step_oracle, cuda_device, n_rays, seed):
+    """Fast-math against libm: the bf16 output gradients within a bf16 step; the proposal gradients within 1e-3 relative
+    plus 1e-4 of their maximum (the interlevel term has a kink at r = 0, where a rounding moves a value between 0 and a
+    tiny gradient); loss sums within 1e-4; images within 1e-5, median depths equal except where a cumulative weight
+    lands within rounding of half the opacity (at most 0.5 % of the pixels)."""
+    c = sc.final_case(step_oracle, n_rays, seed)
+    g_ref, p_ref, l_ref = step_oracle.train_final(c['nerf_outputs'], c['sdist'], c['tdist'], c['proposals'], c['directions'], c['seed'], c['rgb_target'],
+                                                  *sc.LOSS_ARGS)
+    to = lambda x: cuda(x, cuda_device)  # noqa: E731
+    proposals = [{k: (to(v) if isinstance(v, np.ndarray) else v) for k, v in p.items()} for p in c['proposals']]
+    outputs = to(c['nerf_outputs'].view(np.int16)).view(torch.bfloat16)
+    grad, p_grads, sums = capi.train_final(outputs, to(c['sdist']), to(c['tdist']), proposals, to(c['directions']), c['seed'], to(c['rgb_target']),
+                                           *sc.LOSS_ARGS)
+    as_float = lambda e: (e.astype(np.uint32) << 16).view(np.float32)  # noqa: E731
+    got = as_float(grad.view(torch.int16).cpu().numpy().astype(np.uint16))
+    want = as_float(g_ref)
+    np.testing.assert_allclose(got, want, rtol=2 ** -7, atol=1e-6 * np.abs(want).max())
+    for a, b in zip(p_grads, p_ref):
+        np.testing.assert_allclose(a.cpu().numpy(), b, rtol=1e-3, atol=1e-4 * np.abs(b).max())
+    np.testing.assert_allclose(sums.cpu().numpy(), l_ref, rtol=1e-4)
+    pixels = np.random.default_rng(seed).permutation(n_rays)
+    background = np.array([0.2, 0.5, 0.9], np.float32)
+    for median in (False, True):
+        rgb_ref, alpha_ref, depth_ref = step_oracle.composite_final(c['nerf_outputs'], c['tdist'], c['directions'], background, pixels, n_rays, median)
+        rgb, alpha, depth = (torch.full(shape, -1.0, device=cuda_device) for shape in ((n_rays, 3), (n_rays,), (n_rays,)))
+        capi.composite_final(outputs, to(c['tdist']), to(c['directions']), to(background), to(pixels), rgb, alpha, depth, use_median_depth=median)
+        np.testing.assert_allclose(rgb.cpu().numpy(), rgb_ref, rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(alpha.cpu().numpy(), alpha_ref, rtol=1e-5, atol=1e-6)
+        if median:
+            assert np.mean(depth.cpu().numpy() != depth_ref) <= 0.005
+        else:
+            np.testing.assert_allclose(depth.cpu().numpy(), depth_ref, rtol=1e-4)
+
+
 def test_final_level_edge_cases_and_errors(capi, cuda_device):
     import ZipNeRFCudaBackend
     c = final_case(capi, cuda_device, 40, 9)

@@ -1,6 +1,6 @@
-"""The CPU checkers of the sampling steps and the Adam step: the C restatement (oracle/zf_step_oracle.c) against the
-golden vectors of the reference's own sampling functions (tests/golden/make_golden_sampling.py) and against those
-functions built for the host where they are present, the invariants of the resampled intervals, and the Adam
+"""The CPU checkers of the sampling steps, the final level and the Adam step: the C restatement
+(oracle/zf_step_oracle.c) against the golden vectors of the reference's own sampling and final-level functions
+(tests/golden/make_golden_sampling.py) and against those functions built for the host where they are present, the invariants of the resampled intervals, and the Adam
 restatement against an independent vectorized numpy restatement of optimizer_api.cu:43-53."""
 from __future__ import annotations
 
@@ -48,6 +48,26 @@ def test_restatement_matches_reference_host_build(step_oracle, n_rays, n, m, see
             pool['camera_radii'], pool['pool_rgb'], sc.DEGREE, m, sc.WARP)
     for a, b in zip(step_oracle.generate_rays(*args), ref.generate_rays(*args)):
         assert np.array_equal(a, b)
+
+
+@pytest.mark.skipif(not REF_LIB.exists(), reason='the reference host build is not present (make -C oracle ref)')
+@pytest.mark.parametrize('n_rays,seed,n_final', [(1, 3, 32), (33, 4, 32), (129, 5, 64), (64, 6, 2)])
+def test_final_level_restatement_matches_reference_host_build(step_oracle, n_rays, seed, n_final):
+    ref = RefSamplingCpu()
+    c = sc.final_case(step_oracle, n_rays, seed, n_final)
+    args = (c['nerf_outputs'], c['sdist'], c['tdist'], c['proposals'], c['directions'], c['seed'], c['rgb_target'], *sc.LOSS_ARGS)
+    (ga, pa, la), (gb, pb, lb) = step_oracle.train_final(*args), ref.train_final(*args)
+    assert np.array_equal(ga, gb) and all(np.array_equal(x.view(np.uint32), y.view(np.uint32)) for x, y in zip(pa, pb)) and np.array_equal(la, lb)
+    assert np.isfinite(la).all() and (la > 0).all()
+    # no proposal levels: the same output gradients, no interlevel term
+    g0, p0, l0 = step_oracle.train_final(*args[:3], [], *args[4:])
+    assert np.array_equal(g0, ga) and p0 == [] and l0[2] == 0.0
+    pixels = np.random.default_rng(seed).permutation(n_rays)
+    for median in (False, True):
+        a = step_oracle.composite_final(c['nerf_outputs'], c['tdist'], c['directions'], np.array([0.2, 0.5, 0.9], np.float32), pixels, n_rays, median)
+        b = ref.composite_final(c['nerf_outputs'], c['tdist'], c['directions'], np.array([0.2, 0.5, 0.9], np.float32), pixels, n_rays, median)
+        assert all(np.array_equal(x.view(np.uint32), y.view(np.uint32)) for x, y in zip(a, b))
+        assert (a[1] >= 0).all() and (a[2] >= sc.WARP[0]).all()
 
 
 @pytest.mark.parametrize('n,m,anneal,jitter_seed', [(64, 64, 1.0, 3), (64, 32, 10.0, -1), (2, 64, 0.0, 5), (64, 2, 1.0, -1)])
