@@ -1,0 +1,138 @@
+"""The NeRF MLP's fp32 parameter layout and its fold into the packed weights of the tensor-core forward
+(csrc/fz_nerf_mlp.cu, `PackedMlp`), restated from the reference: the layout of `nerf_mlp_parameters`
+(B/mlp/src/nerf_mlp.cu:440-455, the buffer Model.py:96-105 builds from it) and the fold of `pack_kernel`
+(nerf_mlp.cu:186-234).
+
+The reference network (unfolded, `unfolded_forward`):
+    h = relu(features @ density_0^T + b)               density = h @ density_1^T + b
+    bottleneck = h @ bottleneck^T + b                   (no activation)
+    v0 = relu([bottleneck | direction] @ view_0^T + b)  v1, v2 = relu(... view_1 / view_2 ...)
+    rgb = [v2 | bottleneck | direction] @ rgb^T + b
+Because the bottleneck only feeds linear maps, the fold multiplies it into the first view layer and the rgb layer's
+skip columns, and moves every bias of a layer that reads the inputs [h | direction block] into the block's last
+column (the bias lane, 1.0): the packed network (`folded_forward`) has one GEMM fewer and no bottleneck activation.
+The direction block holds 3 + 6 * degree encoded values, zero padding and the bias lane, padded to a multiple of 8.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+
+def direction_block_width(degree: int) -> int:
+    """zipnerf_config.h:18: identity, sines and cosines of 3 axes and `degree` octaves, a bias lane, padded to 8."""
+    return (3 + 6 * degree + 1 + 7) // 8 * 8
+
+
+def nerf_mlp_parameters(n_features: int, density_width: int, bottleneck_width: int, view_width: int, direction_degree: int):
+    """(name, shape, fan-in) of every tensor of the flat fp32 parameter buffer in layout order, fan-in 0 for biases;
+    input columns padded to multiples of 8, the padding columns last (nerf_mlp.cu:440-455)."""
+    n_direction = 3 + 6 * direction_degree
+    n_view_inputs = bottleneck_width + direction_block_width(direction_degree)
+    return [
+        ('density_0.weight', [density_width, (n_features + 7) // 8 * 8], n_features), ('density_0.bias', [density_width], 0),
+        ('density_1.weight', [1, density_width], density_width), ('density_1.bias', [1], 0),
+        ('bottleneck.weight', [bottleneck_width, density_width], density_width), ('bottleneck.bias', [bottleneck_width], 0),
+        ('view_0.weight', [view_width, n_view_inputs], bottleneck_width + n_direction), ('view_0.bias', [view_width], 0),
+        ('view_1.weight', [view_width, view_width], view_width), ('view_1.bias', [view_width], 0),
+        ('view_2.weight', [view_width, view_width], view_width), ('view_2.bias', [view_width], 0),
+        ('rgb.weight', [3, view_width + n_view_inputs], view_width + bottleneck_width + n_direction), ('rgb.bias', [3], 0),
+    ]
+
+
+class NerfMlpLayout:
+    """Views of the flat parameter buffer (tensors back to back in `nerf_mlp_parameters` order; the buffer is padded to
+    a multiple of 4 for the vectorized optimizer, Model.py:105). The defaults are the reference model's: 50 NeRF grid
+    features (10 levels x (4 + 1)), padded to 56 columns; widths 64 / 256 / 256; direction degree 4 (Model.py:66-77)."""
+
+    def __init__(self, n_features: int = 50, density_width: int = 64, bottleneck_width: int = 256, view_width: int = 256,
+                 direction_degree: int = 4) -> None:
+        if density_width % 8 or bottleneck_width % 8 or view_width % 8:
+            raise RuntimeError('ZipNeRF: nerf mlp widths must be multiples of 8')  # nerf_mlp.cu:458
+        self.parameters = nerf_mlp_parameters(n_features, density_width, bottleneck_width, view_width, direction_degree)
+        self.density_width, self.bottleneck_width, self.view_width = density_width, bottleneck_width, view_width
+        self.n_features = self.parameters[0][1][1]
+        self.n_direction = 3 + 6 * direction_degree
+        self.n_inputs = density_width + direction_block_width(direction_degree)
+        self.offsets, n = {}, 0
+        for name, shape, _ in self.parameters:
+            self.offsets[name] = (n, tuple(shape))
+            n += math.prod(shape)
+        self.size = n
+        self.numel = (n + 3) // 4 * 4
+
+    def view(self, buffer: torch.Tensor, name: str) -> torch.Tensor:
+        offset, shape = self.offsets[name]
+        return buffer[offset:offset + math.prod(shape)].view(shape)
+
+    def initialize(self, buffer: torch.Tensor, generator: torch.Generator) -> None:
+        """He-uniform over the first fan-in columns of each weight; the padding columns (last) and biases stay zero
+        (Model.py:59-62,110-113)."""
+        buffer.zero_()
+        for name, _, fan_in in self.parameters:
+            if fan_in > 0:
+                bound = math.sqrt(6.0 / fan_in)
+                self.view(buffer, name)[:, :fan_in].uniform_(-bound, bound, generator=generator)
+
+
+def unfolded_forward(layout: NerfMlpLayout, params: torch.Tensor, features: torch.Tensor, direction_block: torch.Tensor) -> torch.Tensor:
+    """The reference network on its fp32 parameters: [n, 8] outputs (raw density, 3 rgb logits, 4 zeros)."""
+    p = {name: layout.view(params, name) for name, _, _ in layout.parameters}
+    h = torch.relu(features @ p['density_0.weight'].t() + p['density_0.bias'])
+    density = h @ p['density_1.weight'].t() + p['density_1.bias']
+    bottleneck = h @ p['bottleneck.weight'].t() + p['bottleneck.bias']
+    view_inputs = torch.cat([bottleneck, direction_block], dim=1)
+    v0 = torch.relu(view_inputs @ p['view_0.weight'].t() + p['view_0.bias'])
+    v1 = torch.relu(v0 @ p['view_1.weight'].t() + p['view_1.bias'])
+    v2 = torch.relu(v1 @ p['view_2.weight'].t() + p['view_2.bias'])
+    rgb = torch.cat([v2, view_inputs], dim=1) @ p['rgb.weight'].t() + p['rgb.bias']
+    return torch.cat([density, rgb, torch.zeros_like(rgb[:, :1]).expand(-1, 4)], dim=1)
+
+
+def fold(layout: NerfMlpLayout, params: torch.Tensor, k_features: int = 64) -> dict:
+    """The packed network in fp32, in the kernel's shapes (`PackedMlp`): density [density_width, k_features] (features
+    zero padded to the MMA K step), combined [view_width, n_inputs], skip [16, n_inputs], view_1 / view_2, rgb
+    [16, view_width], and the fp32 biases of the density and view layers."""
+    p = {name: layout.view(params, name) for name, _, _ in layout.parameters}
+    dw, bw, vw, nd, ni = layout.density_width, layout.bottleneck_width, layout.view_width, layout.n_direction, layout.n_inputs
+    bias_lane = ni - 1
+    density = params.new_zeros(dw, k_features)
+    density[:, :layout.n_features] = p['density_0.weight']
+    view_0 = p['view_0.weight']
+    combined = params.new_zeros(vw, ni)
+    combined[:, :dw] = view_0[:, :bw] @ p['bottleneck.weight']
+    combined[:, dw:dw + nd] = view_0[:, bw:bw + nd]
+    combined[:, bias_lane] = view_0[:, :bw] @ p['bottleneck.bias'] + p['view_0.bias']
+    rgb_w = p['rgb.weight']
+    skip = params.new_zeros(16, ni)
+    skip[0, :dw] = p['density_1.weight'][0]
+    skip[0, bias_lane] = p['density_1.bias'][0]
+    skip[1:4, :dw] = rgb_w[:, vw:vw + bw] @ p['bottleneck.weight']
+    skip[1:4, dw:dw + nd] = rgb_w[:, vw + bw:vw + bw + nd]
+    skip[1:4, bias_lane] = rgb_w[:, vw:vw + bw] @ p['bottleneck.bias'] + p['rgb.bias']
+    rgb = params.new_zeros(16, vw)
+    rgb[1:4] = rgb_w[:, :vw]
+    return {'density': density, 'density_bias': p['density_0.bias'].clone(), 'combined': combined, 'skip': skip,
+            'view_1': p['view_1.weight'].clone(), 'view_1_bias': p['view_1.bias'].clone(), 'view_2': p['view_2.weight'].clone(),
+            'view_2_bias': p['view_2.bias'].clone(), 'rgb': rgb}
+
+
+def pack(layout: NerfMlpLayout, params: torch.Tensor) -> dict:
+    """`fold` with the weights rounded to bf16 (contiguous row-major, the kernel's operands) and fp32 biases."""
+    return {name: (t.contiguous() if name.endswith('_bias') else t.to(torch.bfloat16).contiguous()) for name, t in fold(layout, params).items()}
+
+
+def folded_forward(packed: dict, features: torch.Tensor, direction_block: torch.Tensor) -> torch.Tensor:
+    """The packed network's layer chain as the kernel runs it (in the packed tensors' dtype, fp32 accumulation when
+    they are fp32): [n, 8] outputs. The hidden layer h is the first columns of the inputs [h | direction block]."""
+    dtype = packed['density'].dtype
+    f = torch.nn.functional.pad(features, (0, packed['density'].shape[1] - features.shape[1])).to(dtype)
+    h = torch.relu(f @ packed['density'].t() + packed['density_bias'].to(dtype))
+    inputs = torch.cat([h, direction_block.to(dtype)], dim=1)
+    v0 = torch.relu(inputs @ packed['combined'].t())
+    out = inputs @ packed['skip'].t()
+    v1 = torch.relu(v0 @ packed['view_1'].t() + packed['view_1_bias'].to(dtype))
+    v2 = torch.relu(v1 @ packed['view_2'].t() + packed['view_2_bias'].to(dtype))
+    out = out + v2 @ packed['rgb'].t()
+    return out[:, :8]
