@@ -77,8 +77,11 @@ class NerfMlpLayout:
 
 
 def unfolded_forward(layout: NerfMlpLayout, params: torch.Tensor, features: torch.Tensor, direction_block: torch.Tensor) -> torch.Tensor:
-    """The reference network on its fp32 parameters: [n, 8] outputs (raw density, 3 rgb logits, 4 zeros)."""
+    """The reference network on its fp32 parameters: [n, 8] outputs (raw density, 3 rgb logits, 4 zeros). Only the
+    encoded values of the direction block are inputs: its padding and bias-lane columns meet the weights' padding
+    columns, which hold zeros and receive no gradient (nerf_mlp.cu:442)."""
     p = {name: layout.view(params, name) for name, _, _ in layout.parameters}
+    direction_block = torch.nn.functional.pad(direction_block[:, :layout.n_direction], (0, direction_block.shape[1] - layout.n_direction))
     h = torch.relu(features @ p['density_0.weight'].t() + p['density_0.bias'])
     density = h @ p['density_1.weight'].t() + p['density_1.bias']
     bottleneck = h @ p['bottleneck.weight'].t() + p['bottleneck.bias']
@@ -90,10 +93,12 @@ def unfolded_forward(layout: NerfMlpLayout, params: torch.Tensor, features: torc
     return torch.cat([density, rgb, torch.zeros_like(rgb[:, :1]).expand(-1, 4)], dim=1)
 
 
-def fold(layout: NerfMlpLayout, params: torch.Tensor, k_features: int = 64) -> dict:
-    """The packed network in fp32, in the kernel's shapes (`PackedMlp`): density [density_width, k_features] (features
-    zero padded to the MMA K step), combined [view_width, n_inputs], skip [16, n_inputs], view_1 / view_2, rgb
-    [16, view_width], and the fp32 biases of the density and view layers."""
+def fold(layout: NerfMlpLayout, params: torch.Tensor, k_features: int = 64, out_rows: int = 16) -> dict:
+    """The packed network in the parameters' dtype, by default in the tensor-core kernel's shapes (`PackedMlp`):
+    density [density_width, k_features] (features zero padded to the MMA K step), combined [view_width, n_inputs], skip
+    [out_rows, n_inputs], view_1 / view_2, rgb [out_rows, view_width] (out_rows >= 8: the smallest N of an M = 128 MMA
+    is 16), and the biases of the density and view layers. Differentiable: autograd of the fold is the unfold of the
+    packed weights' gradients into the parameters' (nerf_mlp.cu:236-284)."""
     p = {name: layout.view(params, name) for name, _, _ in layout.parameters}
     dw, bw, vw, nd, ni = layout.density_width, layout.bottleneck_width, layout.view_width, layout.n_direction, layout.n_inputs
     bias_lane = ni - 1
@@ -105,13 +110,13 @@ def fold(layout: NerfMlpLayout, params: torch.Tensor, k_features: int = 64) -> d
     combined[:, dw:dw + nd] = view_0[:, bw:bw + nd]
     combined[:, bias_lane] = view_0[:, :bw] @ p['bottleneck.bias'] + p['view_0.bias']
     rgb_w = p['rgb.weight']
-    skip = params.new_zeros(16, ni)
+    skip = params.new_zeros(out_rows, ni)
     skip[0, :dw] = p['density_1.weight'][0]
     skip[0, bias_lane] = p['density_1.bias'][0]
     skip[1:4, :dw] = rgb_w[:, vw:vw + bw] @ p['bottleneck.weight']
     skip[1:4, dw:dw + nd] = rgb_w[:, vw + bw:vw + bw + nd]
     skip[1:4, bias_lane] = rgb_w[:, vw:vw + bw] @ p['bottleneck.bias'] + p['rgb.bias']
-    rgb = params.new_zeros(16, vw)
+    rgb = params.new_zeros(out_rows, vw)
     rgb[1:4] = rgb_w[:, :vw]
     return {'density': density, 'density_bias': p['density_0.bias'].clone(), 'combined': combined, 'skip': skip,
             'view_1': p['view_1.weight'].clone(), 'view_1_bias': p['view_1.bias'].clone(), 'view_2': p['view_2.weight'].clone(),
@@ -136,3 +141,111 @@ def folded_forward(packed: dict, features: torch.Tensor, direction_block: torch.
     v2 = torch.relu(v1 @ packed['view_2'].t() + packed['view_2_bias'].to(dtype))
     out = out + v2 @ packed['rgb'].t()
     return out[:, :8]
+
+
+PACKED_ORDER = ('density', 'density_bias', 'combined', 'skip', 'view_1', 'view_1_bias', 'view_2', 'view_2_bias', 'rgb')
+
+
+class NerfMlp:
+    """The reference's `NerfMlp` interface (nerf_mlp.h:47-73: `n_features`, `n_inputs`, `pack`, `forward`,
+    `backward`) over the same folded bf16 layer chain as its cuBLASLt path: bf16 GEMMs with bias + ReLU epilogues
+    (cuBLASLt through torch) and this backend's ReLU backward with the bias gradient (`relu_backward_`, zf_mlp.h).
+    `pack` returns the folded weights and biases as one flat bf16 tensor; the backward's packed-weight gradients go
+    back to the fp32 parameters through autograd of the fold.
+
+    `_forward` and `_backward` hold the layer chain for any device with `relu_backward` given (the CPU tests pass a
+    torch restatement of the kernel's contract); the public methods take CUDA tensors only, as the reference's
+    checks (nerf_mlp.cu:286-290,493-496,570-574), and use the CUDA kernel."""
+
+    def __init__(self, n_features: int, density_width: int, bottleneck_width: int, view_width: int, direction_degree: int) -> None:
+        self.layout = NerfMlpLayout(n_features, density_width, bottleneck_width, view_width, direction_degree)
+        self._shapes = {name: tuple(t.shape) for name, t in fold(self.layout, torch.zeros(self.layout.numel), self.layout.n_features, 8).items()}
+        self._offsets, n = {}, 0
+        for name in PACKED_ORDER:
+            self._offsets[name] = n
+            n += math.prod(self._shapes[name])
+        self.packed_size = n
+
+    @property
+    def n_features(self) -> int:
+        return self.layout.n_features
+
+    @property
+    def n_inputs(self) -> int:
+        return self.layout.n_inputs
+
+    @staticmethod
+    def _check(tensor: torch.Tensor, name: str, dtype: torch.dtype) -> None:
+        if not tensor.is_cuda or not tensor.is_contiguous() or tensor.dtype != dtype:
+            raise RuntimeError(f'ZipNeRF: {name} must be a contiguous cuda tensor of the expected type')
+
+    def _fold(self, params: torch.Tensor) -> dict:
+        return fold(self.layout, params[:self.layout.numel], self.layout.n_features, 8)
+
+    def _pack(self, params: torch.Tensor) -> torch.Tensor:
+        if params.numel() < self.layout.size:
+            raise RuntimeError('ZipNeRF: invalid nerf mlp parameters')
+        folded = self._fold(params)
+        return torch.cat([folded[name].reshape(-1) for name in PACKED_ORDER]).to(torch.bfloat16)
+
+    def _weights(self, packed: torch.Tensor) -> dict:
+        return {name: packed[self._offsets[name]:self._offsets[name] + math.prod(self._shapes[name])].view(self._shapes[name]) for name in PACKED_ORDER}
+
+    def _forward(self, features: torch.Tensor, inputs: torch.Tensor, packed: torch.Tensor, training: bool):
+        if features.shape[1] != self.n_features or inputs.shape[1] != self.n_inputs or packed.numel() != self.packed_size:
+            raise RuntimeError('ZipNeRF: invalid nerf mlp inputs')
+        w = self._weights(packed)
+        dw = self.layout.density_width
+        zero_bias = packed.new_zeros(self.layout.view_width)
+        inputs[:, :dw] = torch._addmm_activation(w['density_bias'], features, w['density'].t())
+        v0 = torch._addmm_activation(zero_bias, inputs, w['combined'].t())
+        outputs = inputs @ w['skip'].t()
+        v1 = torch._addmm_activation(w['view_1_bias'], v0, w['view_1'].t())
+        v2 = torch._addmm_activation(w['view_2_bias'], v1, w['view_2'].t())
+        outputs += v2 @ w['rgb'].t()
+        return outputs, ([inputs, v0, v1, v2] if training else [])
+
+    def _backward(self, grad_outputs, features, packed, context, params, grad_params, relu_backward) -> torch.Tensor:
+        if len(context) != 4 or packed.numel() != self.packed_size:
+            raise RuntimeError('ZipNeRF: invalid nerf mlp backward inputs')
+        inputs, v0, v1, v2 = context
+        w = self._weights(packed)
+        dw = self.layout.density_width
+        bias_grads = {name: torch.zeros(self._shapes[name], device=packed.device) for name in ('density_bias', 'view_1_bias', 'view_2_bias')}
+        no_bias = bias_grads['density_bias'][:0]
+        g = {'rgb': grad_outputs.t().float() @ v2.float()}
+        g_v2 = grad_outputs @ w['rgb']
+        relu_backward(g_v2, v2, bias_grads['view_2_bias'])
+        g['view_2'] = g_v2.t().float() @ v1.float()
+        g_v1 = g_v2 @ w['view_2']
+        relu_backward(g_v1, v1, bias_grads['view_1_bias'])
+        g['view_1'] = g_v1.t().float() @ v0.float()
+        g_v0 = g_v1 @ w['view_1']
+        relu_backward(g_v0, v0, no_bias)
+        g['combined'] = g_v0.t().float() @ inputs.float()
+        g['skip'] = grad_outputs.t().float() @ inputs.float()
+        g_hidden = torch.addmm(grad_outputs @ w['skip'][:, :dw], g_v0, w['combined'][:, :dw])
+        relu_backward(g_hidden, inputs[:, :dw], bias_grads['density_bias'])
+        g['density'] = g_hidden.t().float() @ features.float()
+        g.update(bias_grads)
+        with torch.enable_grad():
+            p = params[:self.layout.numel].detach().float().requires_grad_()
+            folded = self._fold(p)
+            (grad,) = torch.autograd.grad([folded[name] for name in PACKED_ORDER], p, [g[name].to(p.dtype) for name in PACKED_ORDER])
+        grad_params[:self.layout.numel] += grad.to(grad_params.dtype)
+        return g_hidden @ w['density']
+
+    def pack(self, params: torch.Tensor) -> torch.Tensor:
+        self._check(params, 'params', torch.float32)
+        return self._pack(params)
+
+    def forward(self, features: torch.Tensor, inputs: torch.Tensor, packed: torch.Tensor, training: bool):
+        for tensor, name in ((features, 'features'), (inputs, 'inputs'), (packed, 'packed')):
+            self._check(tensor, name, torch.bfloat16)
+        return self._forward(features, inputs, packed, training)
+
+    def backward(self, grad_outputs, features, packed, context, params, grad_params) -> torch.Tensor:
+        import ZipNeRFCudaBackend as backend
+        self._check(params, 'params', torch.float32)
+        self._check(grad_params, 'grad_params', torch.float32)
+        return self._backward(grad_outputs, features, packed, context, params, grad_params, backend.relu_backward_)

@@ -78,6 +78,12 @@ def test_folded_network_equals_the_reference_network():
     assert expected.shape == folded.shape == (257, 8)
     assert not expected[:, 4:].any() and not folded[:, 4:].any()
     torch.testing.assert_close(folded, expected, rtol=1e-10, atol=1e-10)
+    # and so are the gradients: autograd of the fold is the unfold of the packed weights' gradients
+    grad_out = torch.randn(257, 8, generator=g, dtype=torch.float64)
+    p1, p2 = params.clone().requires_grad_(), params.clone().requires_grad_()
+    (nm.unfolded_forward(layout, p1, features, block) * grad_out).sum().backward()
+    (nm.folded_forward(nm.fold(layout, p2), features, block) * grad_out).sum().backward()
+    torch.testing.assert_close(p2.grad, p1.grad, rtol=1e-10, atol=1e-10)
     # the bias lane carries the folded biases: without it the outputs change
     no_lane = block.clone()
     no_lane[:, 31] = 0.0
@@ -113,3 +119,80 @@ def test_tensor_core_forward_compiles_for_sm100a(tmp_path):
     assert run.returncode == 0, run.stderr[-2000:]
     spills = re.findall(r'(\d+) bytes spill stores, (\d+) bytes spill loads', run.stderr)
     assert spills and all(s == ('0', '0') for s in spills), run.stderr
+
+
+def _relu_backward_double(grad: torch.Tensor, activation: torch.Tensor, bias_grad: torch.Tensor) -> None:
+    """The contract of relu_backward_ (zf_mlp.h) in torch: grad *= (activation > 0); bias_grad += the fp32 column sums
+    of the masked gradient when bias_grad is not empty. The kernel itself is checked against torch on the GPU."""
+    grad.copy_(torch.where(activation > 0, grad, torch.zeros_like(grad)))
+    if bias_grad.numel():
+        bias_grad += grad.float().sum(0)
+
+
+def test_reference_interface_forward_and_backward_match_autograd():
+    """NerfMlp's layer chain (`_forward`, `_backward`) on CPU tensors against autograd of the fold and the folded
+    chain with the same bf16 roundings (weights, activations), and against the unfolded reference network in fp32."""
+    layout, params32, g = random_model(3, torch.float32)
+    mlp = nm.NerfMlp(50, 64, 256, 256, 4)
+    n = 320
+    features32, block = inputs(layout, n, g, torch.float32)
+    features = features32.bfloat16()
+    net_inputs = torch.zeros(n, mlp.n_inputs, dtype=torch.bfloat16)
+    net_inputs[:, 64:] = block.bfloat16()
+    packed = mlp._pack(params32)
+    assert packed.dtype == torch.bfloat16 and packed.numel() == mlp.packed_size
+    outputs, context = mlp._forward(features, net_inputs, packed, True)
+    assert outputs.shape == (n, 8) and len(context) == 4 and not outputs[:, 4:].any()
+    assert mlp._forward(features, net_inputs.clone(), packed, False)[1] == []
+    grad_outputs = torch.randn(n, 8, generator=g).bfloat16()
+    grad_outputs[:, 4:] = 0
+    grad_params = torch.full_like(params32, 0.25)  # accumulates (+=)
+    grad_features = mlp._backward(grad_outputs, features, packed, context, params32, grad_params, _relu_backward_double)
+    grad_params -= 0.25
+
+    def stored(t):  # bf16 rounding that passes the gradient straight through
+        return t + (t.bfloat16().float() - t).detach()
+
+    p = params32.clone().requires_grad_()
+    x = features.float().requires_grad_()
+    w = {k: stored(v) for k, v in nm.fold(layout, p, 56, 8).items()}
+    h = stored(torch.relu(x @ w['density'].t() + w['density_bias']))
+    net_in = torch.cat([h, block.bfloat16().float()], dim=1)
+    v0 = stored(torch.relu(net_in @ w['combined'].t()))
+    v1 = stored(torch.relu(v0 @ w['view_1'].t() + w['view_1_bias']))
+    v2 = stored(torch.relu(v1 @ w['view_2'].t() + w['view_2_bias']))
+    expected = net_in @ w['skip'].t() + v2 @ w['rgb'].t()
+    torch.testing.assert_close(outputs.float(), expected, rtol=2e-2, atol=2e-2 * expected.abs().mean().item())
+    (expected * grad_outputs.float()).sum().backward()
+
+    def rel(a, b):
+        return ((a.float() - b).norm() / b.norm()).item()
+
+    errors = {name: rel(layout.view(grad_params, name), layout.view(p.grad, name)) for name, _, fan_in in layout.parameters}
+    errors['features'] = rel(grad_features, x.grad)
+    assert max(errors.values()) < 1e-2, errors
+    for name, _, fan_in in layout.parameters:  # padding columns of the parameters receive no gradient
+        if name in ('view_0.weight', 'rgb.weight'):
+            assert not layout.view(grad_params, name)[:, fan_in:].any(), name
+    # the same parameters in the unfolded reference network, fp32 throughout
+    q = params32.clone().requires_grad_()
+    reference = nm.unfolded_forward(layout, q, features.float(), block)
+    (reference * grad_outputs.float()).sum().backward()
+    # bf16 weights and activations move this chain's parameter gradients by 4-8 % from fp32 (the fold itself is exact,
+    # test_folded_network_equals_the_reference_network); outputs by 3e-3
+    assert rel(grad_params, q.grad) < 0.1 and rel(outputs, reference) < 1e-2
+
+
+def test_reference_interface_checks_its_arguments():
+    mlp = nm.NerfMlp(50, 64, 256, 256, 4)
+    assert (mlp.n_features, mlp.n_inputs) == (56, 96)
+    with pytest.raises(RuntimeError, match='ZipNeRF: params must be a contiguous cuda tensor of the expected type'):
+        mlp.pack(torch.zeros(mlp.layout.numel))  # a CPU tensor: the product path is CUDA only
+    with pytest.raises(RuntimeError, match='ZipNeRF: invalid nerf mlp parameters'):
+        mlp._pack(torch.zeros(100))
+    with pytest.raises(RuntimeError, match='ZipNeRF: invalid nerf mlp inputs'):
+        mlp._forward(torch.zeros(4, 50, dtype=torch.bfloat16), torch.zeros(4, 96, dtype=torch.bfloat16), torch.zeros(mlp.packed_size, dtype=torch.bfloat16), True)
+    with pytest.raises(RuntimeError, match='ZipNeRF: invalid nerf mlp backward inputs'):
+        mlp._backward(None, None, torch.zeros(mlp.packed_size, dtype=torch.bfloat16), [], None, None, _relu_backward_double)
+    with pytest.raises(RuntimeError, match='ZipNeRF: nerf mlp widths must be multiples of 8'):
+        nm.NerfMlp(50, 60, 256, 256, 4)
