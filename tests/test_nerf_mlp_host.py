@@ -196,3 +196,42 @@ def test_reference_interface_checks_its_arguments():
         mlp._backward(None, None, torch.zeros(mlp.packed_size, dtype=torch.bfloat16), [], None, None, _relu_backward_double)
     with pytest.raises(RuntimeError, match='ZipNeRF: nerf mlp widths must be multiples of 8'):
         nm.NerfMlp(50, 60, 256, 256, 4)
+
+
+def canonical_offset(row: int, k: int, k_total: int) -> int:
+    """csrc/fz_nerf_mlp.cu canonical_offset: the byte offset of element (row, k) of a K-major operand."""
+    return ((row >> 3) * (k_total >> 3) + (k >> 3)) * 128 + (row & 7) * 16 + (k & 7) * 2
+
+
+def mma_operand(image, start: int, leading: int, stride: int, rows: int):
+    """The [rows x 16] operand one kind::f16 MMA reads through a no-swizzle K-major descriptor: the canonical layout
+    ((8, rows / 8), (8, 2)) : ((16 B, stride), (2 B, leading)) of the tcgen05 shared-memory descriptor."""
+    import numpy as np
+    out = np.empty((rows, 16), dtype=image.dtype)
+    for r in range(rows):
+        for k in range(16):
+            address = start + 16 * (r % 8) + stride * (r // 8) + 2 * (k % 8) + leading * (k // 8)
+            out[r, k] = image[address // 2]
+    return out
+
+
+@pytest.mark.parametrize('n,k', [(64, 64), (256, 96), (16, 96), (256, 256), (16, 256)])
+def test_tensor_core_operand_layout_is_consistent(n, k):
+    """The kernel's staging (canonical_offset) and its MMA descriptors (start + 256 B per K step, leading offset 128 B,
+    stride offset k / 8 * 128 B) address the same elements: emulating the operand reads of the documented canonical
+    layout over all K steps reproduces A @ B^T for each layer shape of the kernel."""
+    import numpy as np
+    rng = np.random.default_rng(n + k)
+    a, b = rng.integers(-8, 8, size=(128, k)).astype(np.float64), rng.integers(-8, 8, size=(n, k)).astype(np.float64)
+    a_image, b_image = np.zeros(128 * k), np.zeros(n * k)
+    for r in range(128):
+        for c in range(k):
+            a_image[canonical_offset(r, c, k) // 2] = a[r, c]
+    for r in range(n):
+        for c in range(k):
+            b_image[canonical_offset(r, c, k) // 2] = b[r, c]
+    d = np.zeros((128, n))
+    for s in range(k // 16):
+        step = 2 * s * 128
+        d += mma_operand(a_image, step, 128, k // 8 * 128, 128) @ mma_operand(b_image, step, 128, k // 8 * 128, n).T
+    np.testing.assert_array_equal(d, a @ b.T)
