@@ -53,3 +53,20 @@ def test_reference_arm_under_torchrun_measures_on_rank_zero_only():
     lines = json_lines(run.stdout)
     assert len(lines) == 1, run.stdout
     check_line(lines[0], 2)
+
+
+def test_algorithmic_bytes_follow_the_roofline_accounting():
+    """Per-interval algorithmic bytes of config 2 (48 unmerged corner rows per level plus the interval's own inputs and
+    outputs): proposal 2,008 B forward and backward, NeRF 7,860 B forward and 5,096 B backward (3 fp32 and 7 fp16
+    gradient levels); 33.33 GB forward + 27.53 GB backward = 60.86 GB per 65,536-ray step."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location('bench_module', REPO / 'bench.py')
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    ab = bench.algorithmic_bytes
+    assert ab('forward_proposal', 10, 1, 20) == 2008 and ab('backward_proposal', 10, 1, 20) == 2008
+    assert ab('forward_nerf', 10, 4, 50) == 7860 and ab('backward_nerf', 10, 4, 50, 3) == 5096
+    rays = 65536
+    forward = rays * (2 * 64 * ab('forward_proposal', 10, 1, 20) + 32 * ab('forward_nerf', 10, 4, 50))
+    backward = rays * (2 * 64 * ab('backward_proposal', 10, 1, 20) + 32 * ab('backward_nerf', 10, 4, 50, 3))
+    assert round(forward / 1e9, 2) == 33.33 and round(backward / 1e9, 2) == 27.53 and round((forward + backward) / 1e9, 2) == 60.86
