@@ -3,7 +3,6 @@ golden vectors / CPU oracle, on the reference's differential-test cases and on r
 configurations. Tolerances: tests/parity.py."""
 from __future__ import annotations
 
-from pathlib import Path
 
 import numpy as np
 import pytest

@@ -9,7 +9,6 @@ import numpy as np
 import pytest
 import torch
 
-import zf_testdata as td
 from oracle.zf_ref_cuda import RefCuda, available_variants
 from test_gpu_parity import case_tensors, cuda
 from test_oracle import CASES
