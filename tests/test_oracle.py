@@ -98,7 +98,8 @@ def test_float_conversions(oracle):
     oracle.lib.zfo_float_to_bf16.restype = ctypes.c_uint16
     oracle.lib.zfo_float_to_bf16.argtypes = [ctypes.c_float]
     half = np.array([oracle.lib.zfo_float_to_half(float(v)) for v in values], np.uint16)
-    np.testing.assert_array_equal(half, values.astype(np.float16).view(np.uint16))
+    with np.errstate(over='ignore'):  # values beyond the half range round to infinity, as the oracle's conversion does
+        np.testing.assert_array_equal(half, values.astype(np.float16).view(np.uint16))
     bf16 = np.array([oracle.lib.zfo_float_to_bf16(float(v)) for v in values], np.uint16)
     np.testing.assert_array_equal(bf16, td.bf16_bits(values))
 
