@@ -1,4 +1,4 @@
-"""Data-parallel host logic on two gloo ranks (CPU): ray shards partition the batch, the gradient all-reduce averages
+"""Data-parallel host logic on two and eight gloo ranks (CPU): ray shards partition the batch, the gradient all-reduce averages
 fp32 and fp16 buffers without fp16 overflow, and the featurization gradients of two ray shards (CPU oracle, one per
 rank) sum to the gradients of the whole batch."""
 from __future__ import annotations
@@ -39,7 +39,7 @@ def _worker(rank: int, world: int, port: int, queue) -> None:
     import datetime
     dist.init_process_group('gloo', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
-        # averaging: fp16 values whose sum would overflow (2 x 40000 > 65504)
+        # averaging: fp16 values whose sum would overflow (world x 40000 > 65504)
         half = torch.full((4,), 40000.0, dtype=torch.float16)
         single = torch.full((3,), float(rank + 1))
         sharding.allreduce_gradients([half, single])
@@ -60,11 +60,13 @@ def _worker(rank: int, world: int, port: int, queue) -> None:
         dist.destroy_process_group()
 
 
-def test_two_rank_gradient_exchange():
+@pytest.mark.parametrize('world', [2, 8])
+def test_gradient_exchange(world):
+    """world 8 is the largest run of the benchmark: there the fp16 pre-division matters most (8 x 40000)."""
     ctx = mp.get_context('spawn')
     queue = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_worker, args=(rank, 2, port, queue)) for rank in range(2)]
+    procs = [ctx.Process(target=_worker, args=(rank, world, port, queue)) for rank in range(world)]
     for p in procs:
         p.start()
     results = [queue.get(timeout=120) for _ in procs]
@@ -78,7 +80,10 @@ def test_two_rank_gradient_exchange():
     full32, _ = Oracle().backward(grid, *(case[k] for k in ('origins', 'directions', 'radii', 'tdist')), case['seed'],
                                   np.ascontiguousarray(case['grad_features']))
     for rank, half, single, g32 in results:
-        assert half == [40000.0] * 4, 'fp16 average overflowed'
-        assert single == [1.5] * 3
+        # no overflow; the collective's fp16 partial sums round (spacing 32 above 32768): within one spacing per add
+        assert all(abs(h - 40000.0) <= 32.0 * (world - 1) for h in half), f'fp16 average overflowed or drifted: {half}'
+        if world == 2:
+            assert half == [40000.0] * 4  # 20000 + 20000 is exact
+        assert single == [(world + 1) / 2] * 3
         # the shards' summed gradients are the whole batch's, up to fp32 summation order
         np.testing.assert_allclose(g32, full32, rtol=0, atol=1e-5 * float(np.abs(full32).max()))
