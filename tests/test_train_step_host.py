@@ -110,3 +110,23 @@ def test_nerf_mlp_backward_is_the_chain_rule_of_its_forward(monkeypatch):
     errors['features'] = relative_error(grad_features, x.grad)
     assert max(errors.values()) < 1e-2, errors
     assert not mlp.grads[mlp.params.numel() - (mlp.numel - sum(math.prod(s) for _, s in ts.NerfMlp.SHAPES)):].any()
+
+
+def test_adam_buffers_match_the_model_layout():
+    """The benchmark's optimizer buffers (rows.adam_layout, Trainer.py:44-57) against the model's own layouts: the
+    grids of grid_layout, the proposal MLPs' flat buffer (w0 [64, levels x 2], b0, w1, b1 per level, padded to 4) and
+    the NeRF MLP's parameter table."""
+    from zipnerf_b200 import nerf_mlp, rows
+    layout = rows.adam_layout()
+    assert [b['half'] for b in layout] == [False, False, False, True, False, False]
+    for b, n_levels in zip(layout[:2], (6, 8)):
+        _, entries = ts.grid_layout(n_levels)
+        assert b['numel'] == sum(entries) and b['offsets'] == list(np.cumsum([0] + entries))
+    _, entries = ts.grid_layout(10)
+    split = sum(1 for e in entries if e < 2 ** 20)  # levels below 2^20 entries keep fp32 gradients (3 of 10)
+    assert split == 3 and layout[2]['numel'] == 4 * sum(entries[:split]) and layout[3]['numel'] == 4 * sum(entries[split:])
+    assert layout[2]['scale'] == layout[3]['scale'] == 2.0 ** 20
+    proposal = sum(64 * 2 * n + 64 + 64 + 1 for n in (6, 8))
+    assert layout[4]['numel'] == (proposal + 3) // 4 * 4 == 2052
+    assert layout[5]['numel'] == nerf_mlp.NerfMlpLayout().numel
+    assert round(sum(b['numel'] for b in layout) / 1e6, 1) == 77.5  # the parameter count of the Adam row's figures
