@@ -127,6 +127,7 @@ typedef struct zf_backward_mlp_args {
  * <= 2^32 - 1, level sizes <= 65534 (the kernels pack cell coordinates into 16 bits). */
 ZF_API int zf_featurizer_create(int level, const int64_t* level_sizes, const int64_t* level_entries, int n_levels,
                          int n_features, int mlp_width, zf_featurizer** out);
+/* releases the featurizer and its workspace pool (the end of a Featurizer's lifetime) */
 ZF_API void zf_featurizer_destroy(zf_featurizer* featurizer);
 
 /* n_levels * (n_features + 1) (Featurizer::n_output_features, featurizer.h:27) */
@@ -134,7 +135,7 @@ ZF_API int zf_featurizer_n_output_features(const zf_featurizer* featurizer);
 /* table rows of the leading levels with fewer than 2^20 entries, whose NeRF-level gradient is fp32
  * (Featurizer::n_fp32_grad_rows, featurizer.h:30) */
 ZF_API int64_t zf_featurizer_n_fp32_grad_rows(const zf_featurizer* featurizer);
-/* total table rows (sum of level_entries) */
+/* total table rows (sum of level_entries, the grid's last offset, Model.py:22); no Featurizer counterpart */
 ZF_API int64_t zf_featurizer_n_rows(const zf_featurizer* featurizer);
 /* kernel launches of one call (no counterpart in the reference, which launches one kernel per call): call 0 =
  * zf_featurize_forward without the MLP, 1 = with the MLP, 2 = zf_featurize_backward, 3 = zf_featurize_backward_mlp.
@@ -149,7 +150,8 @@ ZF_API int zf_featurize_backward(zf_featurizer* featurizer, const zf_backward_ar
  * gradient reduction, which writes each sample's feature gradient to the workspace, and the scatter of those into
  * grad_table. */
 ZF_API int zf_featurize_backward_mlp(zf_featurizer* featurizer, const zf_backward_mlp_args* args, struct CUstream_st* stream);
-/* workspace bytes of zf_featurize_backward_mlp for n_samples intervals (n_samples * n_output_features floats) */
+/* workspace bytes of zf_featurize_backward_mlp for n_samples intervals (n_samples * n_output_features floats); no
+ * reference counterpart (its backward_mlp is one kernel) */
 ZF_API int64_t zf_featurize_backward_mlp_workspace_size(const zf_featurizer* featurizer, int64_t n_samples);
 /* zf_featurize_backward_mlp without any device allocation. No counterpart in the reference. For callers that must not
  * allocate device memory while they run (a host with a fixed device-memory budget, or a plugin whose framework owns
@@ -178,6 +180,7 @@ ZF_API int zf_featurize_debug(zf_featurizer* featurizer, const zf_rays* rays, co
  * arguments >= zf_erf_saturation_threshold(); the check over [threshold, +inf) must count 0 on every device. */
 ZF_API int zf_check_erf_saturation(uint32_t first_bits, uint32_t last_bits, unsigned long long* n_not_one, uint32_t* max_bits,
                                    struct CUstream_st* stream);
+/* the smallest argument of the kernels' erf early-out; no reference counterpart */
 ZF_API float zf_erf_saturation_threshold(void);
 
 /* Message of the calling thread's last failed call ("" if none). */

@@ -42,6 +42,7 @@ typedef struct zf_adam_buffer {
  * caller and must outlive the object. */
 ZF_API int zf_adam_create(const zf_adam_buffer* buffers, int n_buffers, double reg_weight, double max_value, double beta1, double beta2,
                           double eps, float* magnitudes, int64_t n_magnitudes, float* regularization, zf_adam** out);
+/* frees the moments and scratch arrays (the end of an Adam object's lifetime) */
 ZF_API void zf_adam_destroy(zf_adam* adam);
 
 /* Adam::step (optimizer_api.cu:160-220): the next step (counting from 1) with learning rate lr, on the stream. The

@@ -166,16 +166,22 @@ typedef struct zf_composite_final_args {
 /* width of the encoded view direction block: (3 + 6 degree + 1) rounded up to a multiple of 8 (zipnerf_config.h:18) */
 ZF_API int64_t zf_direction_block_width(int direction_degree);
 
+/* initialize_rays_wrapper (sampling_api.cu:522-541) */
 ZF_API int zf_initialize_rays(const zf_initialize_rays_args* args, struct CUstream_st* stream);
+/* view_rays_wrapper (sampling_api.cu:489-520) */
 ZF_API int zf_view_rays(const zf_view_rays_args* args, struct CUstream_st* stream);
+/* generate_rays_wrapper (sampling_api.cu:446-487) */
 ZF_API int zf_generate_rays(const zf_generate_rays_args* args, struct CUstream_st* stream);
 
 /* sample_uniforms_wrapper (sampling_api.cu:541-548): values[i] = the uniform of (seed, stream_index, i), i < n */
 ZF_API int zf_sample_uniforms(int64_t seed, int64_t stream_index, int64_t n, float* values, struct CUstream_st* stream);
 
+/* composite_and_resample_wrapper (sampling_api.cu:552-581) */
 ZF_API int zf_composite_and_resample(const zf_resample_args* args, struct CUstream_st* stream);
 
+/* train_final_wrapper (sampling_api.cu:583-647) */
 ZF_API int zf_train_final(const zf_train_final_args* args, struct CUstream_st* stream);
+/* composite_final_wrapper (sampling_api.cu:649-679) */
 ZF_API int zf_composite_final(const zf_composite_final_args* args, struct CUstream_st* stream);
 
 #ifdef __cplusplus
