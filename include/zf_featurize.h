@@ -183,12 +183,14 @@ ZF_API int zf_check_erf_saturation(uint32_t first_bits, uint32_t last_bits, unsi
 /* the smallest argument of the kernels' erf early-out; no reference counterpart */
 ZF_API float zf_erf_saturation_threshold(void);
 
-/* Message of the calling thread's last failed call ("" if none). */
+/* Message of the calling thread's last failed call ("" if none): the text of the std::runtime_error the reference
+ * would have thrown (featurizer.cu:127-138). */
 ZF_API const char* zf_last_error(void);
 
 /* Module constants of the reference binding (bindings.cu:14-15): the hash grid initialization range over the
  * feature preconditioning (1e-5), and the static scale of the NeRF grid gradients (2^20). */
 ZF_API double zf_grid_max_value(void);
+/* nerf_grid_grad_scale (bindings.cu:15) */
 ZF_API double zf_nerf_grid_grad_scale(void);
 
 #ifdef __cplusplus

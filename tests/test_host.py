@@ -166,3 +166,17 @@ def test_workload_shapes():
     wl1 = workloads.config1(n_rays=16)
     assert wl1.levels[0].sizes == [16, 27, 47, 81, 138, 237, 406, 697, 1195, 2048]
     assert wl.n_intervals_total == 64 * 160
+
+
+def test_every_declared_function_names_what_it_replaces():
+    """The comment above each declaration in include/*.h cites the reference interface it replaces (file:line) or
+    says that it has no counterpart there."""
+    missing = []
+    for header in HEADERS:
+        text = header.read_text()
+        for m in re.finditer(r'ZF_API\s+[\w\s\*]+?\b(zf_\w+)\s*\(', text):
+            before = text[:m.start()].rstrip()
+            comment = before[before.rindex('/*'):] if before.endswith('*/') else ''
+            if not (re.search(r'\.(cu|cuh|h|py):\d+', comment) or 'counterpart' in comment or 'lifetime' in comment):
+                missing.append(f'{header.name}:{m.group(1)}')
+    assert not missing, missing
