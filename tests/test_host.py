@@ -180,3 +180,18 @@ def test_every_declared_function_names_what_it_replaces():
             if not (re.search(r'\.(cu|cuh|h|py):\d+', comment) or 'counterpart' in comment or 'lifetime' in comment):
                 missing.append(f'{header.name}:{m.group(1)}')
     assert not missing, missing
+
+
+@pytest.mark.parametrize('width,height', [(16, 16), (37, 23), (1, 9), (1296, 840)])
+def test_morton_order_interleaves_the_pixel_bits(width, height):
+    """workloads.morton_order against a per-bit restatement of the Z-order key (x bits even, y bits odd) of
+    Renderer.pixel_order (Renderer.py:120-130): a permutation of the pixels sorted by key."""
+    import numpy as np
+    from zipnerf_b200 import workloads
+    order = workloads.morton_order(width, height).numpy()
+    y, x = np.divmod(np.arange(width * height), width)
+    key = np.zeros(width * height, dtype=np.int64)
+    for bit in range(16):
+        key |= ((x >> bit) & 1) << (2 * bit) | ((y >> bit) & 1) << (2 * bit + 1)
+    assert np.array_equal(np.sort(order), np.arange(width * height))
+    np.testing.assert_array_equal(order, np.argsort(key, kind='stable'))
