@@ -5,8 +5,8 @@ this directory; build them with ``python fused-zipnerf_b200/build.py``. The feat
 reference binding (ZipNeRFCudaBackend/ZipNeRFCudaBackend/torch_bindings/bindings.cu:14-22): ``grid_max_value``,
 ``nerf_grid_grad_scale``, ``set_rtc_dirs`` and ``Featurizer``; the sampling functions ``generate_rays``, ``view_rays``,
 ``initialize_rays``, ``sample_uniforms``, ``composite_and_resample``, ``train_final`` and ``composite_final``
-(sampling_api.h:10-90); and ``Adam`` (optimizer_api.h:14-40). The reference's NeRF MLP (``NerfMlp``,
-``nerf_mlp_parameters``) is not provided here; accessing it raises an ``AttributeError`` that says so.
+(sampling_api.h:10-90); ``Adam`` (optimizer_api.h:14-40); and the NeRF MLP's ``NerfMlp`` and ``nerf_mlp_parameters``
+(nerf_mlp.h:31-73) with the reference's parameter layout, from ``zipnerf_b200.nerf_mlp`` in the directory above.
 """
 from __future__ import annotations
 
@@ -34,14 +34,11 @@ train_final = _C.train_final
 composite_final = _C.composite_final
 relu_backward_ = _C.relu_backward_  # addition: the ReLU backward + bias gradient of a bf16 layer (zf_mlp.h)
 
-_OTHER_SUBSYSTEMS = {'nerf_mlp_parameters', 'NerfMlp'}
+import sys as _sys  # noqa: E402
+
+if str(_HERE.parent) not in _sys.path:  # zipnerf_b200 sits beside this package
+    _sys.path.append(str(_HERE.parent))
+from zipnerf_b200.nerf_mlp import NerfMlp, nerf_mlp_parameters  # noqa: E402
 
 __all__ = ['grid_max_value', 'nerf_grid_grad_scale', 'Featurizer', 'set_rtc_dirs', 'Adam', 'generate_rays', 'view_rays', 'initialize_rays',
-           'sample_uniforms', 'composite_and_resample', 'train_final', 'composite_final']
-
-
-def __getattr__(name: str):
-    if name in _OTHER_SUBSYSTEMS:
-        raise AttributeError(f'ZipNeRFCudaBackend.{name} is not part of the B200 featurization backend; it belongs to the reference '
-                             f"backend's NeRF MLP subsystem")
-    raise AttributeError(f'module ZipNeRFCudaBackend has no attribute {name}')
+           'sample_uniforms', 'composite_and_resample', 'train_final', 'composite_final', 'nerf_mlp_parameters', 'NerfMlp']

@@ -1,6 +1,7 @@
 """Re-exports of the backend's entry points under the reference's module path
-(ZipNeRFCudaBackend/ZipNeRFCudaBackend/torch_bindings/pipeline.py:1-15): featurization, sampling and Adam. The
-reference's NeRF MLP is not part of this backend."""
+(ZipNeRFCudaBackend/ZipNeRFCudaBackend/torch_bindings/pipeline.py:1-15): featurization, sampling, Adam and the NeRF
+MLP."""
+import ZipNeRFCudaBackend as _backend
 from ZipNeRFCudaBackend import _C
 
 grid_max_value = _C.grid_max_value
@@ -15,3 +16,5 @@ sample_uniforms = _C.sample_uniforms
 composite_and_resample = _C.composite_and_resample
 train_final = _C.train_final
 composite_final = _C.composite_final
+nerf_mlp_parameters = _backend.nerf_mlp_parameters
+NerfMlp = _backend.NerfMlp

@@ -1,0 +1,77 @@
+"""The NeRF MLP with the reference's interface (`ZipNeRFCudaBackend.NerfMlp`, zipnerf_b200/nerf_mlp.py) on the GPU:
+pack, the training forward and the backward (cuBLAS bf16 GEMMs with bias + ReLU epilogues, this backend's ReLU
+backward kernel, the unfold of the packed-weight gradients) against autograd of the fold and the same layer chain
+with the same bf16 roundings (weights, activations), for the reference model's defaults (nerf_mlp.cu:440-620)."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _stored(t: torch.Tensor) -> torch.Tensor:
+    """bf16 rounding that passes the gradient straight through"""
+    return t + (t.bfloat16().float() - t).detach()
+
+
+def test_nerf_mlp_matches_autograd(cuda_device):
+    import ZipNeRFCudaBackend as backend
+    from zipnerf_b200 import nerf_mlp as nm
+    layout = nm.NerfMlpLayout()
+    gen = torch.Generator().manual_seed(3)
+    params = torch.zeros(layout.numel)
+    layout.initialize(params, gen)
+    for name, _, fan_in in layout.parameters:  # nonzero biases so that every bias fold matters
+        if fan_in == 0:
+            layout.view(params, name).uniform_(-0.3, 0.3, generator=gen)
+    n = 4096
+    features = torch.zeros(n, 56)
+    features[:, :50] = torch.randn(n, 50, generator=gen)
+    block = torch.zeros(n, 32)
+    block[:, :27] = torch.rand(n, 27, generator=gen) * 2 - 1
+    block[:, 31] = 1.0  # the bias lane
+    grad_outputs = torch.randn(n, 8, generator=gen)
+    grad_outputs[:, 4:] = 0
+    params, features = params.to(cuda_device), features.bfloat16().to(cuda_device)
+    block, grad_outputs = block.bfloat16().to(cuda_device), grad_outputs.bfloat16().to(cuda_device)
+
+    mlp = backend.NerfMlp(50, 64, 256, 256, 4)
+    assert (mlp.n_features, mlp.n_inputs) == (56, 96)
+    packed = mlp.pack(params)
+    inputs = torch.zeros(n, 96, dtype=torch.bfloat16, device=cuda_device)
+    inputs[:, 64:] = block
+    outputs, context = mlp.forward(features, inputs, packed, True)
+    grad_params = torch.zeros_like(params)
+    grad_features = mlp.backward(grad_outputs, features, packed, context, params, grad_params)
+    torch.cuda.synchronize()
+
+    p = params.clone().requires_grad_()
+    x = features.float().requires_grad_()
+    w = {k: _stored(v) for k, v in nm.fold(layout, p, 56, 8).items()}
+    h = _stored(torch.relu(x @ w['density'].t() + w['density_bias']))
+    net_in = torch.cat([h, block.float()], 1)
+    v0 = _stored(torch.relu(net_in @ w['combined'].t()))
+    v1 = _stored(torch.relu(v0 @ w['view_1'].t() + w['view_1_bias']))
+    v2 = _stored(torch.relu(v1 @ w['view_2'].t() + w['view_2_bias']))
+    expected = net_in @ w['skip'].t() + v2 @ w['rgb'].t()
+    (expected * grad_outputs.float()).sum().backward()
+
+    def rel(a, b):
+        return ((a.float() - b).norm() / b.norm()).item()
+
+    # bf16 intermediate gradients and cuBLAS accumulation order: relative errors of at most 3.4e-3 on a B200
+    errors = {name: rel(layout.view(grad_params, name), layout.view(p.grad, name)) for name, _, _ in layout.parameters}
+    errors['features'] = rel(grad_features, x.grad)
+    errors['outputs'] = rel(outputs, expected)
+    assert max(errors.values()) < 1e-2, errors
+    assert rel(inputs[:, :64], h.detach()) < 1e-2  # the hidden layer is written into the inputs
+    # inference: the same outputs, no context
+    out_inference, no_context = mlp.forward(features, inputs.clone(), packed, False)
+    assert no_context == [] and rel(out_inference, outputs.float()) < 1e-3
+
+
+def test_nerf_mlp_parameters_is_the_reference_table():
+    import ZipNeRFCudaBackend as backend
+    table = backend.nerf_mlp_parameters(50, 64, 256, 256, 4)
+    assert table[0] == ('density_0.weight', [64, 56], 50) and table[-1] == ('rgb.bias', [3], 0) and len(table) == 14

@@ -146,8 +146,11 @@ def test_torch_binding_has_the_reference_surface():
     assert hasattr(_C.Adam, 'step') and hasattr(_C.Adam, 'regularization')
     assert isinstance(_C.Featurizer.n_fp32_grad_rows, property)
     assert pipeline.Featurizer is _C.Featurizer
-    with pytest.raises(AttributeError, match='not part of the B200 featurization backend'):
-        ZipNeRFCudaBackend.NerfMlp
+    from zipnerf_b200 import nerf_mlp
+    assert ZipNeRFCudaBackend.NerfMlp is pipeline.NerfMlp is nerf_mlp.NerfMlp
+    assert ZipNeRFCudaBackend.nerf_mlp_parameters is pipeline.nerf_mlp_parameters is nerf_mlp.nerf_mlp_parameters
+    with pytest.raises(AttributeError):
+        ZipNeRFCudaBackend.not_an_entry_point
     if not torch.cuda.is_available():
         with pytest.raises(RuntimeError, match='ZipNeRF: '):
             _C.Featurizer(0, [16, 32], [4096, 32768], 1, 64)
