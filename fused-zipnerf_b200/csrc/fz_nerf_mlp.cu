@@ -62,13 +62,13 @@ enum Status : int { kOk = 0, kWaitTimeout = 1 };
 __device__ __forceinline__ uint32_t smem_address(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
 // byte offset of element (row, k) of a K-major operand with k_total columns
-__device__ __forceinline__ uint32_t canonical_offset(const int row, const int k, const int k_total) {
+__host__ __device__ __forceinline__ uint32_t canonical_offset(const int row, const int k, const int k_total) {
     return static_cast<uint32_t>(((row >> 3) * (k_total >> 3) + (k >> 3)) * 128 + (row & 7) * 16 + (k & 7) * 2);
 }
 
 // shared-memory matrix descriptor (tcgen05 format): start, leading and stride byte offsets in 16-byte units, version 1
 // in bits 46-47, base offset 0, no swizzle (layout type 0 in bits 61-63)
-__device__ __forceinline__ uint64_t smem_descriptor(const uint32_t address, const uint32_t leading_bytes, const uint32_t stride_bytes) {
+__host__ __device__ __forceinline__ uint64_t smem_descriptor(const uint32_t address, const uint32_t leading_bytes, const uint32_t stride_bytes) {
     uint64_t d = static_cast<uint64_t>((address & 0x3FFFFu) >> 4);
     d |= static_cast<uint64_t>((leading_bytes >> 4) & 0x3FFFu) << 16;
     d |= static_cast<uint64_t>((stride_bytes >> 4) & 0x3FFFu) << 32;
@@ -349,3 +349,28 @@ cudaError_t launch_forward(const uint16_t* features, const int64_t features_stri
 }
 
 }  // namespace zf::nerf_mlp
+
+// C entry of the forward for a ctypes caller: the PackedMlp pointers in struct order (density, density_bias, combined,
+// skip, view_1, view_1_bias, view_2, view_2_bias, rgb); *status (device int) is set to 1 if a wait ran out. Returns
+// the CUDA error of the launch.
+extern "C" int zf_nerf_mlp_forward_tc(const uint16_t* features, int64_t features_stride, uint16_t* inputs, int64_t inputs_stride,
+                                      const void* const* weights, uint16_t* outputs, int64_t n, int* status, cudaStream_t stream) {
+    zf::nerf_mlp::PackedMlp w;
+    w.density = static_cast<const uint16_t*>(weights[0]);
+    w.density_bias = static_cast<const float*>(weights[1]);
+    w.combined = static_cast<const uint16_t*>(weights[2]);
+    w.skip = static_cast<const uint16_t*>(weights[3]);
+    w.view_1 = static_cast<const uint16_t*>(weights[4]);
+    w.view_1_bias = static_cast<const float*>(weights[5]);
+    w.view_2 = static_cast<const uint16_t*>(weights[6]);
+    w.view_2_bias = static_cast<const float*>(weights[7]);
+    w.rgb = static_cast<const uint16_t*>(weights[8]);
+    for (int i = 0; i < 9; i++) {
+        if (reinterpret_cast<uintptr_t>(weights[i]) % 16 != 0) return static_cast<int>(cudaErrorInvalidValue);
+    }
+    if (reinterpret_cast<uintptr_t>(features) % 16 != 0 || reinterpret_cast<uintptr_t>(inputs) % 16 != 0 || reinterpret_cast<uintptr_t>(outputs) % 16 != 0
+        || features_stride % 8 != 0 || inputs_stride % 8 != 0 || features_stride < zf::nerf_mlp::kFeatures || inputs_stride < zf::nerf_mlp::kInputs) {
+        return static_cast<int>(cudaErrorInvalidValue);
+    }
+    return static_cast<int>(zf::nerf_mlp::launch_forward(features, features_stride, inputs, inputs_stride, w, outputs, n, status, stream));
+}

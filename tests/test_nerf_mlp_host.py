@@ -235,3 +235,56 @@ def test_tensor_core_operand_layout_is_consistent(n, k):
         step = 2 * s * 128
         d += mma_operand(a_image, step, 128, k // 8 * 128, 128) @ mma_operand(b_image, step, 128, k // 8 * 128, n).T
     np.testing.assert_array_equal(d, a @ b.T)
+
+
+def _cutlass_include():
+    import importlib.util
+    spec = importlib.util.find_spec('flashinfer')
+    if spec is None or spec.origin is None:
+        return None
+    path = Path(spec.origin).parent / 'data' / 'cutlass' / 'include'
+    return path if (path / 'cute' / 'arch' / 'mma_sm100_desc.hpp').exists() else None
+
+
+DESCRIPTOR_CHECK = r'''
+#include <cstdio>
+#include <cute/arch/mma_sm100_desc.hpp>
+#include <cute/numeric/numeric_types.hpp>
+#include "fz_nerf_mlp.cu"
+template <int N> int check_instr() {
+    const uint32_t theirs = uint32_t(cute::UMMA::make_instr_desc<cute::bfloat16_t, cute::bfloat16_t, float, 128, N, cute::UMMA::Major::K, cute::UMMA::Major::K>());
+    const uint32_t ours = zf::nerf_mlp::instr_descriptor(128, N);
+    if (theirs != ours) std::printf("instr N=%d: cute %08x ours %08x\n", N, theirs, ours);
+    return theirs != ours;
+}
+int main() {
+    int bad = check_instr<16>() + check_instr<64>() + check_instr<256>();
+    for (uint32_t address : {0u, 0x4000u, 0x1a300u, 0x36000u}) {
+        for (uint32_t k : {64u, 96u, 256u}) {
+            cute::UMMA::SmemDescriptor d;
+            d.version_ = 1; d.lbo_mode_ = 0; d.layout_type_ = uint8_t(cute::UMMA::LayoutType::SWIZZLE_NONE); d.base_offset_ = 0;
+            d.start_address_ = uint16_t(address >> 4); d.leading_byte_offset_ = 128 >> 4; d.stride_byte_offset_ = uint16_t(k / 8 * 128 >> 4);
+            const uint64_t ours = zf::nerf_mlp::smem_descriptor(address, 128, k / 8 * 128);
+            if (uint64_t(d) != ours) { std::printf("smem %x k=%u: cute %llx ours %llx\n", address, k, (unsigned long long)uint64_t(d), (unsigned long long)ours); bad++; }
+        }
+    }
+    std::printf("%d mismatches\n", bad);
+    return bad;
+}
+'''
+
+
+@pytest.mark.skipif(shutil.which('nvcc') is None or _cutlass_include() is None, reason='nvcc or the CUTLASS headers are absent')
+def test_tensor_core_descriptors_match_cutlass(tmp_path):
+    """The kernel's instruction descriptors (bf16 x bf16 -> fp32, M = 128, N = 16 / 64 / 256, K-major) and its
+    no-swizzle shared-memory descriptors equal the ones CUTLASS's CuTe sm100 code builds (cute/arch/mma_sm100_desc.hpp:
+    make_instr_desc, SmemDescriptor with version 1 as make_umma_desc sets it)."""
+    source = tmp_path / 'check.cu'
+    source.write_text(DESCRIPTOR_CHECK)
+    binary = tmp_path / 'check'
+    build = subprocess.run(['nvcc', '-std=c++17', '-gencode', 'arch=compute_100a,code=sm_100a', '-I', str(_cutlass_include()),
+                            '-I', str(REPO / 'fused-zipnerf_b200' / 'csrc'), str(source), '-o', str(binary)],
+                           capture_output=True, text=True, timeout=300)
+    assert build.returncode == 0, build.stderr[-3000:]
+    run = subprocess.run([str(binary)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0 and '0 mismatches' in run.stdout, run.stdout
