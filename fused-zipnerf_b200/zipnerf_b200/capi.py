@@ -20,7 +20,7 @@ EXPORTED = ['zf_featurizer_create', 'zf_featurizer_destroy', 'zf_featurizer_n_ou
             'zf_check_erf_saturation', 'zf_erf_saturation_threshold', 'zf_last_error', 'zf_grid_max_value', 'zf_nerf_grid_grad_scale',
             'zf_direction_block_width', 'zf_initialize_rays', 'zf_view_rays', 'zf_generate_rays', 'zf_sample_uniforms',
             'zf_composite_and_resample', 'zf_train_final', 'zf_composite_final', 'zf_adam_create', 'zf_adam_destroy', 'zf_adam_step',
-            'zf_adam_state', 'zf_relu_backward_bf16']
+            'zf_adam_state', 'zf_relu_backward_bf16', 'zf_nerf_mlp_forward_tc']
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -100,6 +100,10 @@ class zf_adam_buffer(ctypes.Structure):
                 ('level_offsets', ctypes.POINTER(_i64)), ('n_level_offsets', ctypes.c_int)]
 
 
+class zf_nerf_mlp_weights(ctypes.Structure):
+    _fields_ = [(name, _p) for name in ('density', 'density_bias', 'combined', 'skip', 'view_1', 'view_1_bias', 'view_2', 'view_2_bias', 'rgb')]
+
+
 class ZfError(RuntimeError):
     def __init__(self, code: int, message: str) -> None:
         super().__init__(message)
@@ -174,6 +178,8 @@ def load() -> ctypes.CDLL:
     # zf_mlp.h
     lib.zf_relu_backward_bf16.argtypes = [_p, _i64, _p, _i64, _i64, ctypes.c_int, _p, _p]
     lib.zf_relu_backward_bf16.restype = ctypes.c_int
+    lib.zf_nerf_mlp_forward_tc.argtypes = [_p, _i64, _p, _i64, _p, _p, _i64, _p, _p]
+    lib.zf_nerf_mlp_forward_tc.restype = ctypes.c_int
     _lib = lib
     return lib
 
@@ -396,6 +402,14 @@ def composite_final(nerf_outputs, tdist, directions, background, pixel_indices, 
     a = zf_composite_final_args(_ptr(nerf_outputs), _ptr(tdist), n_rays, n1 - 1, _ptr(directions), _ptr(background), _ptr(pixel_indices), _ptr(rgb),
                                 _ptr(alpha), _ptr(depth), 1 if use_median_depth else 0)
     check(load().zf_composite_final(ctypes.byref(a), _stream(stream)))
+
+
+def nerf_mlp_forward_tc(features, inputs, packed: dict, outputs, status, stream=None) -> None:
+    """zf_nerf_mlp_forward_tc: features [n, 56] and inputs [n, 96] bf16, packed as zipnerf_b200.nerf_mlp.pack gives it
+    (the kernel's shapes), outputs [n, 8] bf16, status a device int32 the kernel sets on a timed-out wait."""
+    w = zf_nerf_mlp_weights(*[packed[name].data_ptr() for name, _ in zf_nerf_mlp_weights._fields_])
+    check(load().zf_nerf_mlp_forward_tc(_ptr(features), features.stride(0), _ptr(inputs), inputs.stride(0), ctypes.byref(w), _ptr(outputs),
+                                        features.shape[0], _ptr(status), _stream(stream)))
 
 
 class CAdam:

@@ -75,3 +75,46 @@ def test_nerf_mlp_parameters_is_the_reference_table():
     import ZipNeRFCudaBackend as backend
     table = backend.nerf_mlp_parameters(50, 64, 256, 256, 4)
     assert table[0] == ('density_0.weight', [64, 56], 50) and table[-1] == ('rgb.bias', [3], 0) and len(table) == 14
+
+
+@pytest.mark.parametrize('n', [128, 4133])
+def test_tensor_core_forward_matches_the_layer_chain(cuda_device, n):
+    """zf_nerf_mlp_forward_tc (one tcgen05 kernel) against the same packed layer chain computed in fp32 from its bf16
+    operands with the kernel's roundings (bias + ReLU in fp32, then bf16): outputs within 1e-2 (1.7e-3 measured), the
+    hidden layer written into the inputs, zero padding outputs, no timed-out wait. n = 4133 leaves a ragged last tile."""
+    from zipnerf_b200 import capi, nerf_mlp as nm
+    layout = nm.NerfMlpLayout()
+    gen = torch.Generator().manual_seed(7)
+    params = torch.zeros(layout.numel)
+    layout.initialize(params, gen)
+    for name, _, fan_in in layout.parameters:
+        if fan_in == 0:
+            layout.view(params, name).uniform_(-0.3, 0.3, generator=gen)
+    packed = {k: v.to(cuda_device) for k, v in nm.pack(layout, params).items()}
+    features = torch.zeros(n, 56)
+    features[:, :50] = torch.randn(n, 50, generator=gen)
+    block = torch.zeros(n, 32)
+    block[:, :27] = torch.rand(n, 27, generator=gen) * 2 - 1
+    block[:, 31] = 1.0
+    features = features.bfloat16().to(cuda_device)
+    inputs = torch.zeros(n, 96, dtype=torch.bfloat16, device=cuda_device)
+    inputs[:, 64:] = block.bfloat16().to(cuda_device)
+    outputs = torch.full((n, 8), float('nan'), dtype=torch.bfloat16, device=cuda_device)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    capi.nerf_mlp_forward_tc(features, inputs, packed, outputs, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+
+    w = {k: v.float() for k, v in packed.items()}
+    h = torch.relu(torch.nn.functional.pad(features.float(), (0, 8)) @ w['density'].t() + w['density_bias']).bfloat16().float()
+    x = torch.cat([h, inputs[:, 64:].float()], 1)
+    v0 = torch.relu(x @ w['combined'].t()).bfloat16().float()
+    v1 = torch.relu(v0 @ w['view_1'].t() + w['view_1_bias']).bfloat16().float()
+    v2 = torch.relu(v1 @ w['view_2'].t() + w['view_2_bias']).bfloat16().float()
+    expected = (x @ w['skip'].t() + v2 @ w['rgb'].t())[:, :8]
+
+    def rel(a, b):
+        return ((a.float() - b).norm() / b.norm()).item()
+
+    assert torch.isfinite(outputs.float()).all() and not outputs[:, 4:].any()
+    assert rel(outputs, expected) < 1e-2 and rel(inputs[:, :64], h) < 1e-2

@@ -114,7 +114,7 @@ def test_packed_weights_have_the_kernel_shapes_and_padding():
 @pytest.mark.skipif(shutil.which('nvcc') is None, reason='nvcc is not on PATH')
 def test_tensor_core_forward_compiles_for_sm100a(tmp_path):
     run = subprocess.run(['nvcc', '-gencode', 'arch=compute_100a,code=sm_100a', '-O3', '--use_fast_math', '-std=c++17', '-Xptxas', '-v', '-c',
-                          str(REPO / 'fused-zipnerf_b200' / 'csrc' / 'fz_nerf_mlp.cu'), '-o', str(tmp_path / 'fz_nerf_mlp.o')],
+                          '-I', str(REPO / 'include'), str(REPO / 'fused-zipnerf_b200' / 'csrc' / 'fz_nerf_mlp.cu'), '-o', str(tmp_path / 'fz_nerf_mlp.o')],
                          capture_output=True, text=True, timeout=300)
     assert run.returncode == 0, run.stderr[-2000:]
     spills = re.findall(r'(\d+) bytes spill stores, (\d+) bytes spill loads', run.stderr)
@@ -251,6 +251,10 @@ DESCRIPTOR_CHECK = r'''
 #include <cute/arch/mma_sm100_desc.hpp>
 #include <cute/numeric/numeric_types.hpp>
 #include "fz_nerf_mlp.cu"
+namespace zf {  // the library's error recording, not linked into this check
+int set_error(int code, const std::string&) { return code; }
+int set_cuda_error(cudaError_t, const char*) { return 3; }
+}
 template <int N> int check_instr() {
     const uint32_t theirs = uint32_t(cute::UMMA::make_instr_desc<cute::bfloat16_t, cute::bfloat16_t, float, 128, N, cute::UMMA::Major::K, cute::UMMA::Major::K>());
     const uint32_t ours = zf::nerf_mlp::instr_descriptor(128, N);
@@ -283,7 +287,7 @@ def test_tensor_core_descriptors_match_cutlass(tmp_path):
     source.write_text(DESCRIPTOR_CHECK)
     binary = tmp_path / 'check'
     build = subprocess.run(['nvcc', '-std=c++17', '-gencode', 'arch=compute_100a,code=sm_100a', '-I', str(_cutlass_include()),
-                            '-I', str(REPO / 'fused-zipnerf_b200' / 'csrc'), str(source), '-o', str(binary)],
+                            '-I', str(REPO / 'fused-zipnerf_b200' / 'csrc'), '-I', str(REPO / 'include'), str(source), '-o', str(binary)],
                            capture_output=True, text=True, timeout=300)
     assert build.returncode == 0, build.stderr[-3000:]
     run = subprocess.run([str(binary)], capture_output=True, text=True, timeout=60)
