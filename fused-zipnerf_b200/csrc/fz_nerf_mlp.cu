@@ -8,9 +8,9 @@
 // The activations never leave the SM: each layer's epilogue reads its accumulator rows from tensor memory, applies
 // bias and ReLU and writes bf16 back to shared memory as the next layer's A operand.
 //
-// Status: a first version. The C entry zf_nerf_mlp_forward_tc (zf_mlp.h) launches it; it matches the same layer chain
-// computed in fp32 from the bf16 operands to 2e-3 on a B200, but each CTA stages every layer's weights with plain loads
-// and runs staging, MMAs and epilogues one after another, so it is slower than the cuBLAS chain.
+// The weights arrive already in the MMAs' shared-memory order, one bulk copy (cp.async.bulk, no multicast) per tensor
+// on a weight mbarrier; the next layer's copy is issued as soon as a layer's MMAs have finished reading the weight
+// buffer, so it lands while that layer's epilogue runs. MMAs and epilogues of one CTA still run one after another.
 //
 // Shared-memory operands use the canonical K-major layout without swizzle: 8-row x 16-byte core matrices stored
 // contiguously (128 bytes), K-adjacent core matrices 128 bytes apart (leading byte offset), 8-row groups
@@ -44,11 +44,11 @@ constexpr int kActBytes = kTileRows * kView * 2;       // 64 KB: features tile, 
 constexpr int kInBytes = kTileRows * kInputs * 2;      // 24 KB: the inputs tile
 constexpr int kWeightBytes = kView * kView * 2;        // 128 KB: one layer's weights (combined and skip together)
 constexpr int kSkipOffset = kView * kInputs * 2;       // skip weights behind the combined weights
-constexpr int kSmemBytes = kActBytes + kInBytes + kWeightBytes + 16;
+constexpr int kSmemBytes = kActBytes + kInBytes + kWeightBytes + 32;  // + the MMA and weight mbarriers, the tensor-memory slot
 static_assert(kSkipOffset + kOutputsN * kInputs * 2 <= kWeightBytes, "combined and skip weights share one buffer");
 static_assert(kSmemBytes <= 227 * 1024, "one CTA per SM");
 
-// packed weights: bf16 row-major [out x in] with zero padding, fp32 biases
+// packed weights: bf16 [out x in] with zero padding in the canonical K-major order, fp32 biases
 struct PackedMlp {
     const uint16_t* density;      // [64, 64]: features 56 -> 64 zero columns
     const float* density_bias;    // [64]
@@ -159,14 +159,17 @@ __device__ __forceinline__ uint32_t pack_bf16x2(const float lo, const float hi) 
     return out;
 }
 
-// row-major [rows x k] bf16 weights from global memory into the canonical layout, 16-byte chunks
-__device__ __forceinline__ void stage_weights(uint8_t* dst, const uint16_t* __restrict__ src, const int rows, const int k) {
-    const int chunks = rows * (k >> 3);
-    for (int q = threadIdx.x; q < chunks; q += kThreads) {
-        const int row = q / (k >> 3), c = q % (k >> 3);
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + q);
-        *reinterpret_cast<uint4*>(dst + canonical_offset(row, 8 * c, k)) = v;
-    }
+// the weight mbarrier expects `bytes` more bytes in its current phase (the arrival of its one thread)
+__device__ __forceinline__ void expect_bytes(const uint32_t bar, const uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// one bulk copy (no multicast) of a weight stored in the canonical order in global memory into shared memory, completing
+// on the weight mbarrier; addresses 16-byte aligned, bytes a multiple of 16
+__device__ __forceinline__ void bulk_copy(const uint32_t dst, const void* src, const uint32_t bytes, const uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst), "l"(src), "r"(bytes),
+                 "r"(bar)
+                 : "memory");
 }
 
 // this thread's accumulator row (columns 0 .. width - 1) + bias, ReLU, bf16 into row `row` of a K-major operand
@@ -201,14 +204,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* act = smem;
     uint8_t* in = smem + kActBytes;
     uint8_t* weights = in + kInBytes;
-    uint64_t* bar = reinterpret_cast<uint64_t*>(weights + kWeightBytes);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(weights + kWeightBytes);  // MMA completion
+    uint64_t* wbar = bar + 1;                                                // weight copies landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 2);
     const int warp = threadIdx.x / 32;
     const int row = threadIdx.x;  // accumulator row = tensor-memory lane of this thread
     const int64_t first = static_cast<int64_t>(blockIdx.x) * kTileRows;
     const int64_t sample = first + row;
     const bool valid = sample < n;
-    const uint32_t bar_address = smem_address(bar);
+    const uint32_t bar_address = smem_address(bar), wbar_address = smem_address(wbar), weights_address = smem_address(weights);
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_address(tmem_slot)), "r"(kTmemColumns));
@@ -216,7 +220,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (threadIdx.x == 0) {
         asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar_address), "r"(1));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(wbar_address), "r"(1));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        expect_bytes(wbar_address, kDensity * kFeaturesK * 2);
+        bulk_copy(weights_address, w.density, kDensity * kFeaturesK * 2, wbar_address);
     }
 
     // features (56 columns + 8 zero columns) into act, the direction block into columns 64-95 of in, density weights
@@ -232,15 +239,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (first + r < n) v = __ldg(reinterpret_cast<const uint4*>(inputs + (first + r) * inputs_stride + kDensity) + c);
         *reinterpret_cast<uint4*>(in + canonical_offset(r, kDensity + 8 * c, kInputs)) = v;
     }
-    stage_weights(weights, w.density, kDensity, kFeaturesK);
     fence_async_shared();
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
     const uint32_t tmem = *tmem_slot;
     const uint32_t tmem_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    uint32_t parity = 0;
+    uint32_t parity = 0, wparity = 0;
     bool ok = true;  // the same in every thread: each wait's outcome is combined over the block
+    ok = __syncthreads_and(wait_phase(wbar_address, wparity));
+    wparity ^= 1;
+    if (!ok) goto done;
 
     // layer 0: h = relu(features @ w_density^T + b_density)
     if (threadIdx.x == 0) {
@@ -251,18 +260,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     parity ^= 1;
     if (!ok) goto done;
     fence_after_sync();
+    if (threadIdx.x == 0) {  // the weight buffer is free: the next layer's weights arrive during this epilogue
+        expect_bytes(wbar_address, (kView + kOutputsN) * kInputs * 2);
+        bulk_copy(weights_address, w.combined, kView * kInputs * 2, wbar_address);
+        bulk_copy(weights_address + kSkipOffset, w.skip, kOutputsN * kInputs * 2, wbar_address);
+    }
     relu_epilogue<kDensity>(tmem_row, w.density_bias, in, row, kInputs, 0);
     if (valid) {  // the hidden layer is part of the inputs the backward reads
         for (int c = 0; c < kDensity / 8; c++) {
             *reinterpret_cast<uint4*>(inputs + sample * inputs_stride + 8 * c) = *reinterpret_cast<const uint4*>(in + canonical_offset(row, 8 * c, kInputs));
         }
     }
-    stage_weights(weights, w.combined, kView, kInputs);
-    stage_weights(weights + kSkipOffset, w.skip, kOutputsN, kInputs);
     fence_async_shared();
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
+    ok = __syncthreads_and(wait_phase(wbar_address, wparity));
+    wparity ^= 1;
+    if (!ok) goto done;
 
     // layer 1: v0 = relu(inputs @ w_combined^T); outputs = inputs @ w_skip^T
     if (threadIdx.x == 0) {
@@ -274,12 +289,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     parity ^= 1;
     if (!ok) goto done;
     fence_after_sync();
+    if (threadIdx.x == 0) {
+        expect_bytes(wbar_address, kView * kView * 2);
+        bulk_copy(weights_address, w.view_1, kView * kView * 2, wbar_address);
+    }
     relu_epilogue<kView>(tmem_row, nullptr, act, row, kView, 0);
-    stage_weights(weights, w.view_1, kView, kView);
     fence_async_shared();
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
+    ok = __syncthreads_and(wait_phase(wbar_address, wparity));
+    wparity ^= 1;
+    if (!ok) goto done;
 
     // layer 2: v1 = relu(v0 @ w_1^T + b_1)
     if (threadIdx.x == 0) {
@@ -290,12 +311,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     parity ^= 1;
     if (!ok) goto done;
     fence_after_sync();
+    if (threadIdx.x == 0) {
+        expect_bytes(wbar_address, kView * kView * 2);
+        bulk_copy(weights_address, w.view_2, kView * kView * 2, wbar_address);
+    }
     relu_epilogue<kView>(tmem_row, w.view_1_bias, act, row, kView, 0);
-    stage_weights(weights, w.view_2, kView, kView);
     fence_async_shared();
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
+    ok = __syncthreads_and(wait_phase(wbar_address, wparity));
+    wparity ^= 1;
+    if (!ok) goto done;
 
     // layer 3: v2 = relu(v1 @ w_2^T + b_2)
     if (threadIdx.x == 0) {
@@ -306,12 +333,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     parity ^= 1;
     if (!ok) goto done;
     fence_after_sync();
+    if (threadIdx.x == 0) {
+        expect_bytes(wbar_address, kOutputsN * kView * 2);
+        bulk_copy(weights_address, w.rgb, kOutputsN * kView * 2, wbar_address);
+    }
     relu_epilogue<kView>(tmem_row, w.view_2_bias, act, row, kView, 0);
-    stage_weights(weights, w.rgb, kOutputsN, kView);
     fence_async_shared();
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
+    ok = __syncthreads_and(wait_phase(wbar_address, wparity));
+    wparity ^= 1;
+    if (!ok) goto done;
 
     // layer 4: outputs += v2 @ w_rgb^T
     if (threadIdx.x == 0) {

@@ -123,9 +123,33 @@ def fold(layout: NerfMlpLayout, params: torch.Tensor, k_features: int = 64, out_
             'view_2_bias': p['view_2.bias'].clone(), 'rgb': rgb}
 
 
+def canonical_order(rows: int, k: int) -> torch.Tensor:
+    """Row-major element indices of a [rows x k] operand in the tensor cores' no-swizzle K-major layout: 8-row x 8-column
+    core matrices (128 bytes of bf16) stored contiguously, K-adjacent core matrices next, then the next 8 rows; the same
+    order as the kernel's canonical_offset (csrc/fz_nerf_mlp.cu), so one bulk copy lands a weight ready for the MMAs."""
+    r = torch.arange(rows).view(rows // 8, 1, 8, 1)
+    c = torch.arange(k).view(1, k // 8, 1, 8)
+    return (r * k + c).expand(rows // 8, k // 8, 8, 8).reshape(-1)
+
+
+def row_major(weight: torch.Tensor) -> torch.Tensor:
+    """The row-major [rows x k] matrix of a weight stored in `canonical_order` (the inverse permutation)."""
+    rows, k = weight.shape
+    out = torch.empty_like(weight).reshape(-1)
+    out[canonical_order(rows, k).to(weight.device)] = weight.reshape(-1)
+    return out.view(rows, k)
+
+
 def pack(layout: NerfMlpLayout, params: torch.Tensor) -> dict:
-    """`fold` with the weights rounded to bf16 (contiguous row-major, the kernel's operands) and fp32 biases."""
-    return {name: (t.contiguous() if name.endswith('_bias') else t.to(torch.bfloat16).contiguous()) for name, t in fold(layout, params).items()}
+    """`fold` with the weights rounded to bf16 and stored in the tensor cores' canonical order (`canonical_order`), and
+    fp32 biases: the operands of zf_nerf_mlp_forward_tc."""
+    out = {}
+    for name, t in fold(layout, params).items():
+        if name.endswith('_bias'):
+            out[name] = t.contiguous()
+        else:
+            out[name] = t.to(torch.bfloat16).reshape(-1)[canonical_order(*t.shape).to(t.device)].view(t.shape).contiguous()
+    return out
 
 
 def folded_forward(packed: dict, features: torch.Tensor, direction_block: torch.Tensor) -> torch.Tensor:

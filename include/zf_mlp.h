@@ -23,9 +23,11 @@ extern "C" {
 ZF_API int zf_relu_backward_bf16(uint16_t* grad, int64_t grad_stride, const uint16_t* activation, int64_t activation_stride, int64_t n_rows,
                                  int n_cols, float* bias_grad, struct CUstream_st* stream);
 
-/* Packed NeRF MLP weights of zf_nerf_mlp_forward_tc: bf16 row-major [out x in] with zero padding, fp32 biases; the
- * fold of the reference's parameters (nerf_mlp.cu:186-234: bottleneck folded into the first view layer and the rgb
- * skip columns, biases of the layers that read the inputs in their last column). All 16-byte aligned. */
+/* Packed NeRF MLP weights of zf_nerf_mlp_forward_tc: bf16 [out x in] matrices with zero padding, each stored in the
+ * tensor cores' no-swizzle K-major order (8-row x 8-column core matrices of 128 bytes, K-adjacent ones next, then the
+ * next 8 rows; zipnerf_b200.nerf_mlp.pack writes it), and fp32 biases; the fold of the reference's parameters
+ * (nerf_mlp.cu:186-234: bottleneck folded into the first view layer and the rgb skip columns, biases of the layers
+ * that read the inputs in their last column). All 16-byte aligned. */
 typedef struct zf_nerf_mlp_weights {
     const uint16_t* density;       /* [64, 64]: 56 feature columns, zero padding to the MMA K step */
     const float* density_bias;     /* [64] */

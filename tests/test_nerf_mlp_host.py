@@ -92,11 +92,16 @@ def test_folded_network_equals_the_reference_network():
 
 def test_packed_weights_have_the_kernel_shapes_and_padding():
     layout, params, g = random_model(2, torch.float32)
-    packed = nm.pack(layout, params)
+    stored = nm.pack(layout, params)
+    # the weights are stored in the tensor cores' order; row_major undoes it, and the values are the fold's in bf16
+    packed = {k: (v if k.endswith('_bias') else nm.row_major(v)) for k, v in stored.items()}
+    folded = nm.fold(layout, params)
+    for k, v in packed.items():
+        assert torch.equal(v, folded[k] if k.endswith('_bias') else folded[k].to(torch.bfloat16)), k
     shapes = {'density': (64, 64), 'density_bias': (64,), 'combined': (256, 96), 'skip': (16, 96), 'view_1': (256, 256),
               'view_1_bias': (256,), 'view_2': (256, 256), 'view_2_bias': (256,), 'rgb': (16, 256)}
     assert {k: tuple(v.shape) for k, v in packed.items()} == shapes
-    for name, t in packed.items():
+    for name, t in stored.items():
         assert t.is_contiguous() and t.dtype == (torch.float32 if name.endswith('_bias') else torch.bfloat16), name
     assert not packed['density'][:, 50:].any()  # 6 padding feature columns + 8 columns of the MMA K step
     assert not packed['combined'][:, 91:95].any()  # direction padding between the 27 encoded values and the bias lane
@@ -292,3 +297,18 @@ def test_tensor_core_descriptors_match_cutlass(tmp_path):
     assert build.returncode == 0, build.stderr[-3000:]
     run = subprocess.run([str(binary)], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0 and '0 mismatches' in run.stdout, run.stdout
+
+
+@pytest.mark.parametrize('rows,k', [(64, 64), (256, 96), (16, 96), (256, 256), (16, 256)])
+def test_packed_order_is_the_kernels_canonical_layout(rows, k):
+    """Element (r, c) of a packed weight sits at the kernel's canonical_offset(r, c, k) / 2, so a single bulk copy lands
+    it where the MMA descriptors read it; row_major inverts the order."""
+    order = nm.canonical_order(rows, k)
+    assert sorted(order.tolist()) == list(range(rows * k))
+    position = torch.empty(rows * k, dtype=torch.long)
+    position[order] = torch.arange(rows * k)
+    for r in range(rows):
+        for c in range(0, k, 3):
+            assert position[r * k + c].item() == canonical_offset(r, c, k) // 2
+    w = torch.randn(rows, k).bfloat16()
+    assert torch.equal(nm.row_major(w.reshape(-1)[order].view(rows, k)), w)
