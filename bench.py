@@ -63,16 +63,20 @@ def measured_peaks() -> dict:
     return {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0, 'source': 'fallback'}
 
 
-def profiled_traffic() -> dict:
-    """DRAM bytes per launch of each kernel from the committed ncu summary (profiles/traffic.txt: 'kernel bytes')."""
+def profiled_traffic() -> tuple[dict, str]:
+    """DRAM bytes per call of each kernel kind from the committed ncu summary (profiles/traffic.txt: 'kernel bytes'
+    lines; a '# commit' line names the source revision the capture ran). Not measured by this run: a committed figure
+    that goes stale when a kernel changes."""
     path = REPO / 'profiles' / 'traffic.txt'
-    out = {}
+    out, commit = {}, 'unknown'
     if path.exists():
         for line in path.read_text().splitlines():
             parts = line.split()
-            if len(parts) == 2 and not line.startswith('#'):
+            if line.startswith('# commit') and len(parts) >= 3:
+                commit = parts[2]
+            elif len(parts) == 2 and not line.startswith('#'):
                 out[parts[0]] = float(parts[1])
-    return out
+    return out, commit
 
 
 class ClockSampler:
@@ -245,6 +249,181 @@ class Step:
         return out
 
 
+class ReferenceStep:
+    """The same step through the reference's own featurization kernels (a BASELINE leg, like cpu_baseline: the
+    reference's four kernels compiled ahead of time from its sources by oracle/ref_cuda/build.py, launched as its
+    featurizer.cu:188-355 launches them), on the inputs of a product Step and into buffers of its own. Outside every
+    product timed region."""
+
+    VARIANTS = ('config2_prop0', 'config2_prop1', 'config2_nerf')
+
+    @staticmethod
+    def unavailable() -> str | None:
+        from oracle.zf_ref_cuda import available_variants
+        missing = [v for v in ReferenceStep.VARIANTS if v not in available_variants()]
+        return f'reference kernels not built ({", ".join(missing)}; python oracle/ref_cuda/build.py)' if missing else None
+
+    def __init__(self, step: Step) -> None:
+        from oracle.zf_ref_cuda import RefCuda
+        self.step = step
+        device, wl = step.device, step.wl
+        self.featurizers = [RefCuda(f'config2_prop{l.level}') for l in step.props] + [RefCuda('config2_nerf')]
+        self.prop_out = [{'raw': torch.empty_like(po['raw']), 'features': torch.empty_like(po['features'])} for po in step.prop_out]
+        self.prop_grads = [{k: torch.zeros_like(v) for k, v in pg.items()} for pg in step.prop_grads]
+        self.nerf_out = {'features': torch.empty_like(step.nerf_out['features']), 'inputs': torch.zeros_like(step.nerf_out['inputs'])}
+        self.nerf_grads = {k: torch.zeros_like(v) for k, v in step.nerf_grads.items()}
+        self.n_output_features = wl.levels[-1].n_output_features
+        self.kernel_names = step.kernel_names
+
+    def zero_grads(self) -> None:
+        for g in [*self.prop_grads, self.nerf_grads]:
+            for v in g.values():
+                v.zero_()
+
+    def run(self, events=None) -> None:
+        """The reference kernels of one step, in the order of Step.run (per-call CUDA events if given)."""
+        st, wl = self.step, self.step.wl
+        rays, seed = (wl.origins, wl.directions, wl.radii), wl.pattern_seed
+        k = 0
+
+        def mark(i, which):
+            if events is not None:
+                events[i][which].record()
+
+        for lvl, f, po in zip(st.props, self.featurizers, self.prop_out):
+            mark(k, 0)
+            f.forward(*rays, lvl.tdist, seed, False, lvl.table, lvl.scale_magnitudes, *lvl.mlp, raw_density=po['raw'], features_float=po['features'])
+            mark(k, 1)
+            k += 1
+        nerf, fn = st.nerf, self.featurizers[-1]
+        mark(k, 0)
+        fn.forward(*rays, nerf.tdist, seed, False, nerf.table, nerf.scale_magnitudes, features_bf16=self.nerf_out['features'],
+                   encoded_directions=wl.encoded_directions, nerf_inputs=self.nerf_out['inputs'])
+        mark(k, 1)
+        k += 1
+        mark(k, 0)
+        fn.backward(*rays, nerf.tdist, seed, st.nerf_out['grad'][:, :self.n_output_features], self.nerf_grads['g32'], self.nerf_grads['g16'])
+        mark(k, 1)
+        k += 1
+        for lvl, f, po, spo, pg in zip(st.props, self.featurizers, self.prop_out, st.prop_out, self.prop_grads):
+            mark(k, 0)
+            f.backward_mlp(*rays, lvl.tdist, seed, po['features'], spo['grad_raw'], *lvl.mlp[:3], pg['table'], pg['w0'], pg['b0'], pg['w1'], pg['b1'])
+            mark(k, 1)
+            k += 1
+
+
+def measure_reference_cuda(step: Step, args, physical: int, our_ms_per_step: float, our_kernels: dict) -> dict:
+    """The north-star comparison: the reference's own CUDA kernels on the identical config-2 step and inputs, timed on
+    this GPU right after the product's timed region, with the same protocol (CUDA events around the step on the
+    current stream, warm-up first, inputs larger than L2) and its own clock record. ratio = reference ms per step / the
+    product's ms per step (higher is better)."""
+    why = ReferenceStep.unavailable()
+    if why is not None:
+        return {'unavailable': why}
+    ref = ReferenceStep(step)
+    for _ in range(args.warmup):
+        ref.run()
+    n_k = len(ref.kernel_names)
+    events = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(n_k)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with ClockSampler(physical) as clocks:
+        start.record()
+        for i in range(args.steps):
+            ref.run(events[i])
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    per_kernel: dict[str, list] = {}
+    for i in range(args.steps):
+        for name, (a, b) in zip(ref.kernel_names, events[i]):
+            per_kernel.setdefault(name, []).append(a.elapsed_time(b))
+    kernels_ms = {name: sum(t) / len(t) for name, t in per_kernel.items()}
+    del ref
+    torch.cuda.empty_cache()
+    return {'what': "the reference's featurize_forward / featurize_forward_bf16 / featurize_backward / featurize_backward_mlp kernels, "
+                    'compiled from its sources for sm_100a with its fast-math options, launched with its launch shapes, on the same '
+                    'inputs as the product step (oracle/ref_cuda)',
+            'ms_per_step': ms, 'msamples_per_s': step.samples_per_step / (ms * 1e-3) / 1e6, 'steps': args.steps, 'warmup': args.warmup,
+            'kernels_avg_ms': kernels_ms, 'ours_ms_per_step': our_ms_per_step, 'ratio': ms / our_ms_per_step,
+            'ratio_per_kernel': {name: kernels_ms[name] / our_kernels[name]['avg_ms'] for name in kernels_ms if name in our_kernels},
+            'clocks': clocks.summary()}
+
+
+def measure_contention(args, device, physical: int) -> dict:
+    """Config 5 (atomic contention): the NeRF-level forward and backward of 65,536 rays x 160 intervals whose rays all
+    pass through a 0.05-radius ball within a 5 degree cone (coarse rows receive ~10^5 contributions per step), 12 x 4
+    features, table 2^22; the product's kernels through the PyTorch binding and, where built, the reference's kernels
+    on the same inputs. Reported per call: ms, Msamples/s and the unmerged corner contributions per second of the
+    backward (every interval's 6 x 8 x 12 corner updates)."""
+    import ZipNeRFCudaBackend as backend
+    from zipnerf_b200 import workloads as wl_mod
+    wl = wl_mod.config5(n_rays=args.rays, seed=5).to(device)
+    lvl = wl.levels[0]
+    n = wl.n_rays * lvl.n_intervals
+    width = wl_mod.nerf_feature_width(lvl.n_output_features)
+    rays = (wl.origins, wl.directions, wl.radii, lvl.tdist)
+    g = torch.Generator(device='cpu').manual_seed(55)
+    grad = (torch.randn(n, width, generator=g) * 1e-6).bfloat16().to(device)
+    feats = torch.empty(n, width, device=device, dtype=torch.bfloat16)
+    ours = backend.Featurizer(lvl.level, lvl.sizes, lvl.entries, lvl.n_features, lvl.mlp_width)
+    split = ours.n_fp32_grad_rows
+    g32 = torch.zeros(split * lvl.n_features, device=device)
+    g16 = torch.zeros((sum(lvl.entries) - split) * lvl.n_features, device=device, dtype=torch.float16)
+    e = torch.empty(0, device=device)
+    n_out = lvl.n_output_features
+
+    def our_calls():
+        return [lambda: ours.forward(*rays, wl.pattern_seed, False, lvl.table, lvl.scale_magnitudes, e, e, e, e, e, e, feats, e, e),
+                lambda: ours.backward(*rays, wl.pattern_seed, grad[:, :n_out], g32, g16)]
+
+    def ref_calls(ref):
+        return [lambda: ref.forward(*rays, wl.pattern_seed, False, lvl.table, lvl.scale_magnitudes, features_bf16=feats),
+                lambda: ref.backward(*rays, wl.pattern_seed, grad[:, :n_out], g32, g16)]
+
+    def time_calls(calls):
+        times = [[], []]
+        for i in range(args.warmup + args.steps):
+            g32.zero_()
+            g16.zero_()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in calls]
+            for (a, b), c in zip(ev, calls):
+                a.record()
+                c()
+                b.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                for t, (a, b) in zip(times, ev):
+                    t.append(a.elapsed_time(b))
+        return [statistics.median(t) for t in times]
+
+    contributions = n * N_MULTISAMPLES * 8 * lvl.n_levels
+    samples = n * N_MULTISAMPLES
+    n_fp32 = sum(1 for e in lvl.entries if e < (1 << 20))
+
+    def entry(fwd_ms, bwd_ms):
+        return {'forward_ms': fwd_ms, 'backward_ms': bwd_ms, 'forward_msamples_per_s': samples / (fwd_ms * 1e-3) / 1e6,
+                'backward_msamples_per_s': samples / (bwd_ms * 1e-3) / 1e6,
+                'backward_gcontributions_per_s': contributions / (bwd_ms * 1e-3) / 1e9}
+
+    with ClockSampler(physical) as clocks:
+        out = {'config': f'config5: {wl.n_rays} rays x {lvl.n_intervals} intervals x 6 multisamples, origins in a 0.05 ball, directions in a 5 degree '
+                         f'cone; NeRF grid 12 x 4 features, table 2^22, 16 -> 16384 (fp32 gradients on the first {n_fp32} levels, fp16 above); '
+                         'forward: packed bf16 features; backward: bf16 upstream gradients',
+               'ours': entry(*time_calls(our_calls()))}
+        from oracle.zf_ref_cuda import RefCuda, available_variants
+        if 'config5' in available_variants():
+            out['reference_cuda'] = entry(*time_calls(ref_calls(RefCuda('config5'))))
+            out['ratio_backward'] = out['reference_cuda']['backward_ms'] / out['ours']['backward_ms']
+            out['ratio_forward'] = out['reference_cuda']['forward_ms'] / out['ours']['forward_ms']
+        else:
+            out['reference_cuda'] = {'unavailable': 'reference kernel variant config5 not built'}
+    out['clocks'] = clocks.summary()
+    del wl, grad, feats, g32, g16
+    torch.cuda.empty_cache()
+    return out
+
+
 def init_distributed(n_gpus: int):
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
@@ -347,7 +526,9 @@ def run_reference_arm(args) -> None:
     emit({'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': args.gpus, 'steps': args.steps,
                       'warmup': args.warmup, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
                       'data': 'synthetic (seeded config 2 shapes; Mip-NeRF 360 unavailable)',
-                      'config': bench_config(args, 1, args.rays * (64 + 64 + 32) * N_MULTISAMPLES),
+                      'config': bench_config(args, 1, args.rays * (64 + 64 + 32) * N_MULTISAMPLES) |
+                                {'timed_sample': f'each step times {args.reference_rays} of the {args.rays} rays (all three levels, fwd+bwd) on '
+                                                 'the host cores and reports that sample\'s samples/s'},
                       'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': base['cores'], 'kind': base['kind'], 'sample': base['sample']},
                       'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}})
 
@@ -416,7 +597,7 @@ def run_b200(args) -> None:
     for name, nbytes in zip(step.kernel_names, step.kernel_bytes()):
         bytes_per.setdefault(name, []).append(nbytes)
     peaks = measured_peaks()
-    traffic = profiled_traffic()
+    traffic, traffic_commit = profiled_traffic()
     kernels = {}
     for name, times in kernel_ms.items():
         launches_per_step = len(bytes_per[name])
@@ -428,12 +609,22 @@ def run_b200(args) -> None:
     dk = kernels[dominant]
     roofline = {'bound': 'hbm', 'kernel': dominant, 'achieved': dk['achieved_gbs'], 'peak': peaks['hbm_gbs'], 'unit': 'GB/s',
                 'frac': dk['achieved_gbs'] / peaks['hbm_gbs'], 'peak_source': peaks['source'],
-                'traffic': traffic.get(dominant)}
+                'traffic': traffic.get(dominant),
+                'traffic_source': f'committed ncu capture profiles/traffic.txt (DRAM read + write bytes per call, source revision {traffic_commit}); '
+                                  'not measured by this run'}
     result = {'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
               'ms_per_step': ms_per_step, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
               'data': 'synthetic (seeded config 2 shapes; Mip-NeRF 360 unavailable)',
               'config': bench_config(args, world, step.samples_per_step),
               'roofline': roofline, 'kernels': kernels, 'gpu_launches': step.kernel_launches_per_step * args.steps, 'clocks': clocks.summary()}
+    if rank == 0 and world == 1 and not args.skip_reference_cuda:
+        # baseline legs (test infrastructure, outside the product's timed regions): the reference's own CUDA kernels on
+        # this step's inputs, and the config-5 contention case
+        result['reference_cuda'] = measure_reference_cuda(step, args, physical, ms_per_step, kernels)
+    if rank == 0 and world == 1 and not args.skip_contention:
+        result['contention'] = measure_contention(args, device, physical)
+    if rank == 0 and world == 1 and not args.skip_nerf_mlp:
+        result['nerf_mlp'] = measure_nerf_mlp(device, physical)
     if not args.skip_e2e:
         result['e2e'] = measure_e2e(step, args, world, start_exchange, exchange, barrier)
     if not args.skip_train_step:
@@ -456,64 +647,157 @@ def measure_rows(device, iters: int = 10) -> dict:
     an L2 flush (zipnerf_b200/rows.py): the two composite-and-resample calls of a training step (proposal level 0 -> 64
     intervals, level 1 -> 32), the training rays of a step drawn from a 185-view pool, the final level's losses and
     gradients, and the Adam step over the reference model's optimizer buffers (77.5 M parameters). Achieved bandwidth = algorithmic bytes / median time,
-    against the measured HBM peak."""
+    against the measured HBM peak. Where the reference's own sampling and Adam kernels are built (oracle/ref_cuda, a
+    baseline leg), each entry also carries their time on the same inputs (into outputs of their own) and the ratio."""
     import ctypes
     import ZipNeRFCudaBackend as backend
+    from oracle import zf_ref_sampling_cuda as ref_mod
     from zipnerf_b200 import capi, rows
     lib = capi.load()
+    ref = ref_mod.RefSamplingCuda() if ref_mod.available() else None
     peaks = measured_peaks()
     timer = rows.LaunchTimer(device)
     stream = torch.cuda.current_stream().cuda_stream
     R = rows.N_RAYS
     warp = capi.make_ray_warp(rows.WARP)
+    warp_host = torch.tensor(rows.WARP, dtype=torch.float32)
 
-    def entry(ms_list, nbytes, config):
+    def entry(ms_list, nbytes, config, ref_list=None):
         ms = sum(ms_list)
         gbs = nbytes / (ms * 1e-3) / 1e9
-        return {'config': config, 'ms': ms, 'calls_ms': ms_list, 'algorithmic_bytes': nbytes, 'achieved_gbs': gbs, 'peak': peaks['hbm_gbs'],
-                'frac': gbs / peaks['hbm_gbs']}
+        out = {'config': config, 'ms': ms, 'calls_ms': ms_list, 'algorithmic_bytes': nbytes, 'achieved_gbs': gbs, 'peak': peaks['hbm_gbs'],
+               'frac': gbs / peaks['hbm_gbs']}
+        if ref_list:
+            out['reference_cuda_ms'] = sum(ref_list)
+            out['ratio'] = sum(ref_list) / ms
+        return out
 
     out = {}
     inp = rows.resample_inputs(R, 64, device)
-    calls, nbytes = [], 0
+    calls, ref_calls, nbytes = [], [], 0
     for m, level in ((64, 1), (32, 2)):
         s_next, t_next, weights = torch.empty(R, m + 1, device=device), torch.empty(R, m + 1, device=device), torch.empty(R, 64, device=device)
         a = capi.zf_resample_args(inp['raw_density'].data_ptr(), inp['sdist'].data_ptr(), inp['tdist'].data_ptr(), inp['directions'].data_ptr(), R,
                                   64, 0.5, m, 1234, level, warp, weights.data_ptr(), s_next.data_ptr(), t_next.data_ptr())
         calls.append(timer(lambda a=a: capi.check(lib.zf_composite_and_resample(ctypes.byref(a), stream)), iters))
+        if ref is not None:
+            theirs = [torch.empty_like(weights), torch.empty_like(s_next), torch.empty_like(t_next)]
+            ref_calls.append(timer(lambda m=m, level=level, theirs=theirs: ref.lib.ref_composite_and_resample(
+                inp['raw_density'].data_ptr(), inp['sdist'].data_ptr(), inp['tdist'].data_ptr(), inp['directions'].data_ptr(), R, 64, 0.5, m, 1234,
+                level, warp_host.data_ptr(), *[t.data_ptr() for t in theirs], stream), iters))
         nbytes += R * rows.resample_bytes(64, m)
-    out['composite_and_resample'] = entry(calls, nbytes, f'{R} rays: 64 -> 64 and 64 -> 32 intervals (training, jittered)')
+    out['composite_and_resample'] = entry(calls, nbytes, f'{R} rays: 64 -> 64 and 64 -> 32 intervals (training, jittered)', ref_calls)
     pool = rows.ray_pool(device)
     width = capi.direction_block_width(4)
-    o = [torch.empty(R, 3, device=device) for _ in range(3)]
-    radii, encoded = torch.empty(R, device=device), torch.empty(R, width, dtype=torch.bfloat16, device=device)
-    sd, td = torch.empty(R, 65, device=device), torch.empty(R, 65, device=device)
-    ga = capi.zf_generate_rays_args(77, R, pool['view_offsets'].data_ptr(), pool['view_cameras'].numel(), pool['view_cameras'].data_ptr(),
-                                    pool['camera_offsets'].data_ptr(), pool['local_directions'].data_ptr(), pool['c2w'].data_ptr(),
-                                    pool['camera_radii'].data_ptr(), pool['pool_rgb'].data_ptr(), pool['pool_rgb'].shape[0], 4, 64, warp,
-                                    o[0].data_ptr(), o[1].data_ptr(), radii.data_ptr(), o[2].data_ptr(), encoded.data_ptr(), sd.data_ptr(), td.data_ptr())
+
+    def new_ray_outputs():
+        return ([torch.empty(R, 3, device=device) for _ in range(2)] + [torch.empty(R, device=device), torch.empty(R, 3, device=device),
+                torch.empty(R, width, dtype=torch.bfloat16, device=device), torch.empty(R, 65, device=device), torch.empty(R, 65, device=device)])
+    pool_args = (pool['view_offsets'].data_ptr(), pool['view_cameras'].numel(), pool['view_cameras'].data_ptr(), pool['camera_offsets'].data_ptr(),
+                 pool['local_directions'].data_ptr(), pool['c2w'].data_ptr(), pool['camera_radii'].data_ptr(), pool['pool_rgb'].data_ptr(),
+                 pool['pool_rgb'].shape[0])
+    ours = new_ray_outputs()
+    ga = capi.zf_generate_rays_args(77, R, *pool_args, 4, 64, warp, *[t.data_ptr() for t in ours])
     ms = timer(lambda: capi.check(lib.zf_generate_rays(ctypes.byref(ga), stream)), iters)
-    out['generate_rays'] = entry([ms], R * rows.new_rays_bytes(64, width), f'{R} rays from 185 views of 1296 x 840 pixels, 64 first-level intervals')
+    ref_ms = []
+    if ref is not None:
+        theirs = new_ray_outputs()
+        ref_ms.append(timer(lambda: ref.lib.ref_generate_rays(77, R, *pool_args, 4, 64, warp_host.data_ptr(), *[t.data_ptr() for t in theirs], stream),
+                            iters))
+    out['generate_rays'] = entry([ms], R * rows.new_rays_bytes(64, width), f'{R} rays from 185 views of 1296 x 840 pixels, 64 first-level intervals',
+                                 ref_ms)
     del pool
     fin = rows.final_inputs(device)
-    proposal_grads = [torch.empty_like(p['raw_density']) for p in fin['proposals']]
+    props = fin['proposals']
+    proposal_grads = [torch.empty_like(p['raw_density']) for p in props]
     levels = (capi.zf_proposal_level * 2)(*[capi.zf_proposal_level(p['raw_density'].shape[1], p['raw_density'].data_ptr(), p['sdist'].data_ptr(),
                                                                     p['tdist'].data_ptr(), p['weights'].data_ptr(), g.data_ptr(), p['interlevel_weight'],
-                                                                    p['interlevel_blur']) for p, g in zip(fin['proposals'], proposal_grads)])
+                                                                    p['interlevel_blur']) for p, g in zip(props, proposal_grads)])
     out_grad, loss_sums = torch.empty_like(fin['nerf_outputs']), torch.zeros(4, device=device)
     fa = capi.zf_train_final_args(fin['nerf_outputs'].data_ptr(), fin['sdist'].data_ptr(), fin['tdist'].data_ptr(), R, 32, levels, 2,
                                   fin['directions'].data_ptr(), fin['seed'], fin['rgb_target'].data_ptr(), *rows.LOSS_ARGS, out_grad.data_ptr(),
                                   loss_sums.data_ptr())
     ms = timer(lambda: capi.check(lib.zf_train_final(ctypes.byref(fa), stream)), iters)
-    out['train_final'] = entry([ms], R * rows.final_bytes(), f'{R} rays: final level of 32 intervals, proposal levels of 64 and 64')
+    ref_ms = []
+    if ref is not None:
+        ref_grads = [torch.empty_like(g) for g in proposal_grads]
+        ref_out_grad, ref_sums = torch.empty_like(out_grad), torch.zeros(4, device=device)
+
+        def arr(ctype, values):
+            return (ctype * 2)(*values)
+        ref_args = (fin['nerf_outputs'].data_ptr(), fin['sdist'].data_ptr(), fin['tdist'].data_ptr(), R, 32, 2, arr(ctypes.c_int, [64, 64]),
+                    arr(ctypes.c_void_p, [p['raw_density'].data_ptr() for p in props]), arr(ctypes.c_void_p, [p['sdist'].data_ptr() for p in props]),
+                    arr(ctypes.c_void_p, [p['tdist'].data_ptr() for p in props]), arr(ctypes.c_void_p, [p['weights'].data_ptr() for p in props]),
+                    arr(ctypes.c_void_p, [g.data_ptr() for g in ref_grads]), arr(ctypes.c_float, [p['interlevel_weight'] for p in props]),
+                    arr(ctypes.c_float, [p['interlevel_blur'] for p in props]), fin['directions'].data_ptr(), fin['seed'], fin['rgb_target'].data_ptr(),
+                    *rows.LOSS_ARGS, ref_out_grad.data_ptr(), ref_sums.data_ptr(), stream)
+        ref_ms.append(timer(lambda: ref.lib.ref_train_final(*ref_args), iters))
+    out['train_final'] = entry([ms], R * rows.final_bytes(), f'{R} rays: final level of 32 intervals, proposal levels of 64 and 64', ref_ms)
     del fin, proposal_grads
     layout, params, grads, n_levels = rows.adam_inputs(device)
     mags = torch.zeros(n_levels, device=device)
-    opt = backend.Adam(params, grads, [b['scale'] for b in layout], [b['offsets'] for b in layout], 0.1, 1e-5, 0.9, 0.99, 1e-15, mags)
+    hyper = (0.1, 1e-5, 0.9, 0.99, 1e-15)
+    scales, offsets = [b['scale'] for b in layout], [b['offsets'] for b in layout]
+    opt = backend.Adam(params, grads, scales, offsets, *hyper, mags)
     ms = timer(lambda: opt.step(1e-3), iters)
+    ref_ms = []
+    if ref is not None:
+        opt_ref = ref_mod.RefAdamCuda(ref, [p.clone() for p in params], [g.clone() for g in grads], scales, offsets, *hyper,
+                                      torch.zeros(n_levels, device=device))
+        ref_ms.append(timer(lambda: opt_ref.step(1e-3), iters))
+        del opt_ref
     n_params = sum(b['numel'] for b in layout)
     out['adam'] = entry([ms], rows.adam_bytes(layout), f'{n_params} parameters in {len(layout)} buffers ({n_levels} grid levels, '
-                        'NeRF grid levels 3-9 with fp16 gradients)')
+                        'NeRF grid levels 3-9 with fp16 gradients)', ref_ms)
+    return out
+
+
+def measure_nerf_mlp(device, physical: int, iters: int = 10, n: int = 65536 * 32) -> dict:
+    """The NeRF MLP's inference forward over one training step's NeRF level (2,097,152 samples; the reference model's
+    widths, nerf_mlp.cu:440-455): the tcgen05 kernel (zf_nerf_mlp_forward_tc through the C ABI) and the cuBLAS chain of
+    ZipNeRFCudaBackend.NerfMlp, CUDA-event means over `iters` runs after 3 warm-ups, against the measured bf16 peak
+    (burst). Inputs (336 MB) are larger than L2."""
+    import ZipNeRFCudaBackend as backend
+    from zipnerf_b200 import capi, nerf_mlp as nm
+    layout = nm.NerfMlpLayout()
+    gen = torch.Generator().manual_seed(7)
+    params = torch.zeros(layout.numel)
+    layout.initialize(params, gen)
+    features = torch.randn(n, 56, generator=gen).bfloat16().to(device)
+    inputs = torch.zeros(n, 96, dtype=torch.bfloat16, device=device)
+    inputs[:, 64:91] = (torch.rand(n, 27, generator=gen) * 2 - 1).bfloat16().to(device)
+    inputs[:, 95] = 1.0
+    outputs = torch.empty(n, 8, dtype=torch.bfloat16, device=device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    packed = {k: v.to(device) for k, v in nm.pack(layout, params).items()}
+    mlp = backend.NerfMlp(50, 64, 256, 256, 4)
+    flat = mlp.pack(params.to(device))
+    peaks = measured_peaks()
+    flop = 2 * nm.MACS_PER_SAMPLE * n
+
+    def time_ms(fn) -> float:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(iters):
+            fn()
+        end.record()
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / iters
+
+    out = {'config': f'{n} samples (65,536 rays x 32 intervals); density 64 x 56, combined 256 x 96, skip 8 x 96, view 2 x 256 x 256, rgb 8 x 256; '
+                     'bf16 operands, fp32 accumulation', 'flop_per_sample': 2 * nm.MACS_PER_SAMPLE}
+    with ClockSampler(physical) as clocks:
+        for name, fn in (('tcgen05', lambda: capi.nerf_mlp_forward_tc(features, inputs, packed, outputs, status)),
+                         ('cublas_chain', lambda: mlp.forward(features, inputs, flat, False))):
+            ms = time_ms(fn)
+            tflops = flop / (ms * 1e-3) / 1e12
+            out[name] = {'ms': ms, 'tflops': tflops, 'frac_of_bf16_peak': tflops / peaks['bf16_tflops']}
+    out['clocks'] = clocks.summary()
+    out['tcgen05_status'] = int(status.item())
+    out['ratio'] = out['cublas_chain']['ms'] / out['tcgen05']['ms']
     return out
 
 
@@ -650,6 +934,9 @@ def main() -> None:
     parser.add_argument('--skip-cpu-baseline', action='store_true')
     parser.add_argument('--skip-rows', action='store_true', help='skip the timing of the sampling and Adam kernels')
     parser.add_argument('--skip-train-step', action='store_true', help='skip the timing of the full training step')
+    parser.add_argument('--skip-reference-cuda', action='store_true', help="skip the timing of the reference's own CUDA kernels")
+    parser.add_argument('--skip-contention', action='store_true', help='skip the config-5 contention timing')
+    parser.add_argument('--skip-nerf-mlp', action='store_true', help='skip the timing of the NeRF MLP forward')
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps
     if args.impl == 'reference':

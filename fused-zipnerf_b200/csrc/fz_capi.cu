@@ -173,8 +173,11 @@ namespace {
 int check_rays(const zf_rays* rays, zf::RayInputs& in) {
     if (rays == nullptr) return fail(ZF_ERROR_INVALID_ARGUMENT, "rays must not be null");
     if (rays->n_rays < 0 || rays->n_intervals < 1) return fail(ZF_ERROR_INVALID_ARGUMENT, "tdist must have at least two columns");
+    // bounded before the product is formed, so that it cannot overflow
+    if (rays->n_intervals > static_cast<int64_t>(UINT32_MAX) || rays->n_rays > static_cast<int64_t>(UINT32_MAX) / rays->n_intervals) {
+        return fail(ZF_ERROR_INVALID_ARGUMENT, "too many samples for 32-bit indexing");
+    }
     const int64_t n_samples = rays->n_rays * rays->n_intervals;
-    if (n_samples > static_cast<int64_t>(UINT32_MAX)) return fail(ZF_ERROR_INVALID_ARGUMENT, "too many samples for 32-bit indexing");
     if (n_samples > 0 && (rays->origins == nullptr || rays->directions == nullptr || rays->radii == nullptr || rays->tdist == nullptr)) {
         return fail(ZF_ERROR_INVALID_ARGUMENT, "origins, directions, radii and tdist must be given");
     }
@@ -542,12 +545,12 @@ extern "C" {
 int zf_featurize_backward_mlp_no_alloc(zf_featurizer* f, const zf_backward_mlp_args* a, cudaStream_t stream) {
     if (f == nullptr || a == nullptr) return fail(ZF_ERROR_INVALID_ARGUMENT, "featurizer and arguments must not be null");
     if (a->rays.n_rays < 0 || a->rays.n_intervals < 1) return fail(ZF_ERROR_INVALID_ARGUMENT, "tdist must have at least two columns");
-    const int64_t n_samples = a->rays.n_rays * a->rays.n_intervals;
-    const int64_t needed = zf_featurize_backward_mlp_workspace_size(f, n_samples);
-    if (needed > static_cast<int64_t>(kStaticWorkspaceBytes)) {
-        const int64_t limit = static_cast<int64_t>(kStaticWorkspaceBytes) / (f->n_output_features() * static_cast<int64_t>(sizeof(float)));
+    // the sample limit of the static workspace, checked on the ray count before any product is formed (no overflow)
+    const int64_t limit = static_cast<int64_t>(kStaticWorkspaceBytes) / (f->n_output_features() * static_cast<int64_t>(sizeof(float)));
+    if (a->rays.n_rays > limit / a->rays.n_intervals) {
         return fail(ZF_ERROR_INVALID_ARGUMENT, "backward_mlp without allocation supports at most " + std::to_string(limit) +
-                    " samples of this featurizer (a static 32 MiB workspace); got " + std::to_string(n_samples));
+                    " samples of this featurizer (a static 32 MiB workspace); got " + std::to_string(a->rays.n_rays) + " rays x " +
+                    std::to_string(a->rays.n_intervals) + " intervals");
     }
     void* workspace = nullptr;
     const int rc = static_workspace_address(&workspace);

@@ -404,9 +404,47 @@ def composite_final(nerf_outputs, tdist, directions, background, pixel_indices, 
     check(load().zf_composite_final(ctypes.byref(a), _stream(stream)))
 
 
+# shapes and dtypes of the packed NeRF MLP tensors the tensor-core kernel reads (zf_nerf_mlp_weights)
+NERF_MLP_PACKED_SHAPES = {'density': ((64, 64), 'bfloat16'), 'density_bias': ((64,), 'float32'), 'combined': ((256, 96), 'bfloat16'),
+                          'skip': ((16, 96), 'bfloat16'), 'view_1': ((256, 256), 'bfloat16'), 'view_1_bias': ((256,), 'float32'),
+                          'view_2': ((256, 256), 'bfloat16'), 'view_2_bias': ((256,), 'float32'), 'rgb': ((16, 256), 'bfloat16')}
+
+
+def check_nerf_mlp_forward_tc(features, inputs, packed: dict, outputs, status, require_cuda: bool = True) -> None:
+    """Raises ValueError unless the tensors have the shapes, dtypes and layouts the tensor-core kernel reads and writes
+    (the C ABI sees only pointers and row strides, so a wrong shape here would make the kernel read or write out of
+    bounds): features [n, >= 56] and inputs [n, >= 96] bf16 CUDA tensors with unit column stride, outputs a contiguous
+    [n, 8] bf16 tensor, the packed weights as zipnerf_b200.nerf_mlp.pack gives them, status an int32 CUDA tensor.
+    require_cuda=False checks the shapes of CPU tensors (host tests)."""
+    import torch
+
+    def on_device(t) -> bool:
+        return t.is_cuda or not require_cuda
+    tensors = {'features': features, 'inputs': inputs, 'outputs': outputs}
+    for name, t in tensors.items():
+        if not isinstance(t, torch.Tensor) or not on_device(t) or t.dtype != torch.bfloat16 or t.dim() != 2:
+            raise ValueError(f'{name} must be a 2-d bf16 CUDA tensor')
+        if t.stride(1) != 1:
+            raise ValueError(f'{name} must have unit column stride')
+    n = features.shape[0]
+    if features.shape[1] < 56 or inputs.shape[1] < 96 or inputs.shape[0] != n:
+        raise ValueError(f'features must be [n, >= 56] and inputs [n, >= 96] with the same n (got {tuple(features.shape)}, {tuple(inputs.shape)})')
+    if tuple(outputs.shape) != (n, 8) or not outputs.is_contiguous():
+        raise ValueError(f'outputs must be a contiguous [{n}, 8] tensor (got {tuple(outputs.shape)})')
+    for name, (shape, dtype) in NERF_MLP_PACKED_SHAPES.items():
+        t = packed.get(name)
+        if not isinstance(t, torch.Tensor) or not on_device(t) or t.dtype != getattr(torch, dtype) or t.numel() != shape[0] * (shape[1] if len(shape) > 1 else 1) \
+                or not t.is_contiguous():
+            raise ValueError(f'packed[{name!r}] must be a contiguous {dtype} CUDA tensor of {shape} elements')
+    if not isinstance(status, torch.Tensor) or not on_device(status) or status.dtype != torch.int32 or status.numel() < 1:
+        raise ValueError('status must be an int32 CUDA tensor')
+
+
 def nerf_mlp_forward_tc(features, inputs, packed: dict, outputs, status, stream=None) -> None:
     """zf_nerf_mlp_forward_tc: features [n, 56] and inputs [n, 96] bf16, packed as zipnerf_b200.nerf_mlp.pack gives it
-    (the kernel's shapes), outputs [n, 8] bf16, status a device int32 the kernel sets on a timed-out wait."""
+    (the kernel's shapes), outputs [n, 8] bf16, status a device int32 the kernel sets on a timed-out wait. The
+    tensors are checked first (check_nerf_mlp_forward_tc: ValueError on a mismatch)."""
+    check_nerf_mlp_forward_tc(features, inputs, packed, outputs, status)
     w = zf_nerf_mlp_weights(*[packed[name].data_ptr() for name, _ in zf_nerf_mlp_weights._fields_])
     check(load().zf_nerf_mlp_forward_tc(_ptr(features), features.stride(0), _ptr(inputs), inputs.stride(0), ctypes.byref(w), _ptr(outputs),
                                         features.shape[0], _ptr(status), _stream(stream)))

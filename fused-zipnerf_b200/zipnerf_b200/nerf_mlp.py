@@ -20,6 +20,11 @@ import math
 import torch
 
 
+# multiply-adds per sample of the packed network at the reference model's widths: density 64 x 56, combined 256 x 96,
+# skip 8 x 96, view_1 and view_2 256 x 256, rgb 8 x 256
+MACS_PER_SAMPLE = 64 * 56 + 256 * 96 + 8 * 96 + 2 * 256 * 256 + 8 * 256
+
+
 def direction_block_width(degree: int) -> int:
     """zipnerf_config.h:18: identity, sines and cosines of 3 axes and `degree` octaves, a bias lane, padded to 8."""
     return (3 + 6 * degree + 1 + 7) // 8 * 8

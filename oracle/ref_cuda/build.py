@@ -22,7 +22,8 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE.parent / '_ref' / 'cuda'
-REFERENCE_ROOT = Path(os.environ.get('REFERENCE_ROOT', '/root/reference'))
+# the reference checkout: REFERENCE_ROOT, else a sibling directory 'reference' of this repository
+REFERENCE_ROOT = Path(os.environ.get('REFERENCE_ROOT', str(HERE.parent.parent.parent / 'reference')))
 BACKEND = REFERENCE_ROOT / 'ZipNeRFCudaBackend' / 'ZipNeRFCudaBackend'
 NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')
 MIN_HALF_GRAD_ENTRIES = 1 << 20

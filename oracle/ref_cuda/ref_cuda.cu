@@ -95,11 +95,33 @@ REF_API int ref_backward_mlp(const float* origins, const float* directions, cons
 #endif
 }
 
+// The reference keeps its contraction decision (|p|^2 > 1: the fmaxf(dot(p, p), 1) of featurize_common.cuh:111) inside
+// multisample. This restates the position p of featurize_common.cuh:103-109 with the reference's own helpers, so that the
+// flag can be exported; the contracted position formed again from that p (featurize_common.cuh:111-115) is exported as
+// x_check, and the tests require it to equal the reference's own x bit for bit, which pins the restated p to the
+// reference's.
+__device__ inline bool ref_contracted(const zipnerf::RayInterval& interval, const uint32_t j, float3& x_check) {
+    using namespace zipnerf;
+    constexpr float pattern[n_multisamples] = {0.0f, 2.0f, 4.0f, 3.0f, 5.0f, 1.0f};
+    const float theta = (3.14159265358979f / 3.0f) * pattern[interval.flip ? n_multisamples - 1 - j : j] + interval.rotation;
+    const float cz = interval.t0 + interval.ratio * (interval.base + (3.0f / sqrtf(7.0f)) * (j * 0.4f - 1.0f) * interval.root);
+    const float perp_mag = sqrtf(0.5f) * interval.radius * cz;
+    float sin_theta, cos_theta;
+    sincosf(theta, &sin_theta, &cos_theta);
+    const float3 p = interval.origin + (perp_mag * cos_theta) * interval.perp_axis1 + (perp_mag * sin_theta) * interval.perp_axis2 + cz * interval.direction;
+    const float norm_sq = fmaxf(dot(p, p), 1.0f);
+    const float norm = sqrtf(norm_sq);
+    const float contraction = (2.0f * norm - 1.0f) / norm_sq;
+    x_check = (1.0f / grid_bbox_size) * (contraction * p) + ::make_float3(0.5f, 0.5f, 0.5f);
+    return dot(p, p) > 1.0f;
+}
+
 // intermediate values of the listed samples from the reference's device functions (no counterpart kernel in the
-// reference): x [n, 6, 3], scale [n, 6], n_groups [n, L], rows / weights [n, L, 6, 8] in visit order
+// reference): x [n, 6, 3], scale [n, 6], contracted [n, 6] and x_check [n, 6, 3] (ref_contracted), n_groups [n, L],
+// rows / weights [n, L, 6, 8] in visit order
 __global__ void ref_debug_kernel(const float3* origins, const float3* directions, const float* radii, const float* tdist, long long pattern_seed,
-                                 uint32_t n_intervals, const uint32_t* samples, uint32_t n_debug, float* x_out, float* scale_out, int32_t* n_groups,
-                                 uint32_t* rows, float* weights) {
+                                 uint32_t n_intervals, const uint32_t* samples, uint32_t n_debug, float* x_out, float* scale_out, int32_t* contracted,
+                                 float* x_check, int32_t* n_groups, uint32_t* rows, float* weights) {
     using namespace zipnerf;
     const uint32_t d = blockIdx.x * blockDim.x + threadIdx.x;
     if (d >= n_debug) return;
@@ -112,6 +134,11 @@ __global__ void ref_debug_kernel(const float3* origins, const float3* directions
         x_out[(d * n_multisamples + j) * 3 + 1] = x[j].y;
         x_out[(d * n_multisamples + j) * 3 + 2] = x[j].z;
         scale_out[d * n_multisamples + j] = scale[j];
+        float3 xc;
+        contracted[d * n_multisamples + j] = ref_contracted(interval, j, xc) ? 1 : 0;
+        x_check[(d * n_multisamples + j) * 3] = xc.x;
+        x_check[(d * n_multisamples + j) * 3 + 1] = xc.y;
+        x_check[(d * n_multisamples + j) * 3 + 2] = xc.z;
     }
     #pragma unroll
     for (uint32_t level = 0; level < JIT_N_LEVELS; level++) {
@@ -134,12 +161,12 @@ __global__ void ref_debug_kernel(const float3* origins, const float3* directions
 }
 
 REF_API int ref_debug(const float* origins, const float* directions, const float* radii, const float* tdist, int64_t n_intervals, long long pattern_seed,
-                      const uint32_t* samples, int64_t n_debug, float* x, float* scale, int32_t* n_groups, uint32_t* rows, float* weights,
-                      cudaStream_t stream) {
+                      const uint32_t* samples, int64_t n_debug, float* x, float* scale, int32_t* contracted, float* x_check, int32_t* n_groups,
+                      uint32_t* rows, float* weights, cudaStream_t stream) {
     if (n_debug == 0) return 0;
     ref_debug_kernel<<<static_cast<unsigned>((n_debug + 63) / 64), 64, 0, stream>>>(
         reinterpret_cast<const float3*>(origins), reinterpret_cast<const float3*>(directions), radii, tdist, pattern_seed,
-        static_cast<uint32_t>(n_intervals), samples, static_cast<uint32_t>(n_debug), x, scale, n_groups, rows, weights);
+        static_cast<uint32_t>(n_intervals), samples, static_cast<uint32_t>(n_debug), x, scale, contracted, x_check, n_groups, rows, weights);
     return static_cast<int>(cudaGetLastError());
 }
 

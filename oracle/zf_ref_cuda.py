@@ -44,7 +44,7 @@ class RefCuda:
                                          _p, ctypes.c_int, _p, ctypes.c_int, _p]
         self.lib.ref_backward.argtypes = [_p, _p, _p, _p, _i64, _i64, ctypes.c_longlong, _p, ctypes.c_int, _p, _p, _p]
         self.lib.ref_backward_mlp.argtypes = [_p, _p, _p, _p, _i64, _i64, ctypes.c_longlong, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]
-        self.lib.ref_debug.argtypes = [_p, _p, _p, _p, _i64, ctypes.c_longlong, _p, _i64, _p, _p, _p, _p, _p, _p]
+        self.lib.ref_debug.argtypes = [_p, _p, _p, _p, _i64, ctypes.c_longlong, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p]
         n = (ctypes.c_int * 4)()
         self.lib.ref_layout(ctypes.byref(n, 0), ctypes.byref(n, 4), ctypes.byref(n, 8), ctypes.byref(n, 12))
         self.n_levels, self.n_features, self.mlp_width, self.n_fp32_grad_levels = list(n)
@@ -80,10 +80,11 @@ class RefCuda:
         import torch
         n, L, dev = samples.numel(), self.n_levels, samples.device
         out = {'x': torch.zeros(n, 6, 3, device=dev), 'scale': torch.zeros(n, 6, device=dev),
+               'contracted': torch.zeros(n, 6, dtype=torch.int32, device=dev), 'x_check': torch.zeros(n, 6, 3, device=dev),
                'n_groups': torch.zeros(n, L, dtype=torch.int32, device=dev), 'rows': torch.zeros(n, L, 6, 8, dtype=torch.int32, device=dev),
                'weights': torch.zeros(n, L, 6, 8, device=dev)}
         self._check(self.lib.ref_debug(_ptr(origins), _ptr(directions), _ptr(radii), _ptr(tdist), tdist.shape[1] - 1, pattern_seed, _ptr(samples), n,
-                                       _ptr(out['x']), _ptr(out['scale']), _ptr(out['n_groups']), _ptr(out['rows']), _ptr(out['weights']),
-                                       _stream(stream)), 'debug')
+                                       _ptr(out['x']), _ptr(out['scale']), _ptr(out['contracted']), _ptr(out['x_check']), _ptr(out['n_groups']),
+                                       _ptr(out['rows']), _ptr(out['weights']), _stream(stream)), 'debug')
         out['rows'] = out['rows'].to(torch.int64) & 0xFFFFFFFF
         return out

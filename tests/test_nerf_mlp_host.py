@@ -312,3 +312,45 @@ def test_packed_order_is_the_kernels_canonical_layout(rows, k):
             assert position[r * k + c].item() == canonical_offset(r, c, k) // 2
     w = torch.randn(rows, k).bfloat16()
     assert torch.equal(nm.row_major(w.reshape(-1)[order].view(rows, k)), w)
+
+
+def test_tensor_core_forward_wrapper_rejects_mismatched_tensors():
+    """The C ABI of the tensor-core forward sees only pointers and row strides, so the wrapper checks shapes, dtypes and
+    layouts first: every mismatch below raises ValueError before anything reaches the device."""
+    from zipnerf_b200 import capi
+    layout = nm.NerfMlpLayout()
+    params = torch.zeros(layout.numel)
+    layout.initialize(params, torch.Generator().manual_seed(1))
+    packed = nm.pack(layout, params)
+    n = 40
+
+    def good():
+        return {'features': torch.zeros(n, 56, dtype=torch.bfloat16), 'inputs': torch.zeros(n, 96, dtype=torch.bfloat16),
+                'packed': dict(packed), 'outputs': torch.zeros(n, 8, dtype=torch.bfloat16), 'status': torch.zeros(1, dtype=torch.int32)}
+
+    def call(a, require_cuda=False):
+        capi.check_nerf_mlp_forward_tc(a['features'], a['inputs'], a['packed'], a['outputs'], a['status'], require_cuda=require_cuda)
+
+    call(good())  # the shapes nerf_mlp.pack and the kernel agree on
+    with pytest.raises(ValueError):
+        call(good(), require_cuda=True)  # host tensors
+    bad = []
+    for key, value in [('features', torch.zeros(n, 48, dtype=torch.bfloat16)), ('features', torch.zeros(n, 56)),
+                       ('inputs', torch.zeros(n, 64, dtype=torch.bfloat16)), ('inputs', torch.zeros(n + 1, 96, dtype=torch.bfloat16)),
+                       ('outputs', torch.zeros(n, 4, dtype=torch.bfloat16)), ('outputs', torch.zeros(n - 1, 8, dtype=torch.bfloat16)),
+                       ('outputs', torch.zeros(8, n, dtype=torch.bfloat16).t()), ('outputs', torch.zeros(n, 8)),
+                       ('features', torch.zeros(56, n, dtype=torch.bfloat16).t()), ('status', torch.zeros(1, dtype=torch.int64))]:
+        a = good()
+        a[key] = value
+        bad.append(a)
+    for name in packed:
+        for wrong in (packed[name][:-1].clone() if packed[name].dim() == 1 else packed[name][:-1].clone(), packed[name].double()):
+            a = good()
+            a['packed'] = dict(packed) | {name: wrong}
+            bad.append(a)
+    a = good()
+    del a['packed']['rgb']
+    bad.append(a)
+    for a in bad:
+        with pytest.raises(ValueError):
+            call(a)

@@ -83,16 +83,22 @@ def test_forward_bit_exact_with_reference_kernels(capi, cuda_device, name, inter
 @needs_reference
 @pytest.mark.parametrize('name', sorted(VARIANT_OF))
 def test_intermediates_bit_exact_with_reference_device_code(capi, cuda_device, name):
-    """Sample placement, multisample radii, merged corner rows (hash indices) and weights on every sample."""
+    """Sample placement, multisample radii, contraction masks, merged corner rows (hash indices) and weights on every
+    sample."""
     case = CASES[name]
     ref = RefCuda(VARIANT_OF[name])
     ours = capi.CFeaturizer(case['level'], case['sizes'], case['entries'], case['n_features'], case['mlp_width'])
     rays, _, _ = case_tensors(case, cuda_device)
     n_samples = case['tdist'].shape[0] * (case['tdist'].shape[1] - 1)
     samples = torch.arange(n_samples, dtype=torch.int32, device=cuda_device)
-    a = ours.debug(*rays, case['seed'], samples)
-    b = ref.debug(*rays, case['seed'], samples)
-    for key in ['x', 'scale', 'n_groups', 'rows', 'weights']:
+    assert_intermediates_equal(ours.debug(*rays, case['seed'], samples), ref.debug(*rays, case['seed'], samples))
+
+
+def assert_intermediates_equal(a: dict, b: dict) -> None:
+    # the reference harness's contraction flag comes from a restated position p; the contracted position formed again
+    # from that p must be the reference's own x bit for bit, or the flag would not be the reference's
+    np.testing.assert_array_equal(as_bits(b['x_check']), as_bits(b['x']), err_msg='restated reference position')
+    for key in ['x', 'scale', 'contracted', 'n_groups', 'rows', 'weights']:
         np.testing.assert_array_equal(as_bits(a[key]) if a[key].dtype != torch.int64 else a[key].cpu().numpy(),
                                       as_bits(b[key]) if b[key].dtype != torch.int64 else b[key].cpu().numpy(), err_msg=key)
 

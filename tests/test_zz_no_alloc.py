@@ -78,3 +78,20 @@ def test_no_alloc_backward_rejects_batches_beyond_its_workspace(capi, cuda_devic
     small = torch.zeros(8, device=cuda_device)
     with pytest.raises(capi.ZfError, match=f'at most {limit} samples'):
         f.backward_mlp_no_alloc(small, small, small, tdist, 0, small, small, small, small, small, small, small, small, small, small)
+
+
+@pytest.mark.parametrize('n_intervals', [1, 64, 4096])
+def test_no_alloc_backward_rejects_overflowing_ray_counts(capi, cuda_device, n_intervals):
+    """Ray counts whose sample count would overflow 64 bits are rejected by the size check on the host, before any
+    product is formed and before anything is launched (no tensors are needed: the arguments point nowhere)."""
+    import ctypes
+    sizes, entries = td.grid_layout(10, 21, 16, 512)
+    f = capi.CFeaturizer(0, sizes, entries, 1, 64)
+    for n_rays in ((2 ** 63 - 1) // n_intervals, (2 ** 63 - 1) // n_intervals - 1, 2 ** 62 // n_intervals + 3):
+        rays = capi.zf_rays(None, None, None, None, n_rays, n_intervals, 0, 0)
+        a = capi.zf_backward_mlp_args(rays, None, 0, None, 0, None, None, None, 64 * f.n_output_features, None, f.n_rows, None,
+                                      64 * f.n_output_features, None, None, None, None, 0)
+        with pytest.raises(capi.ZfError, match='samples of this featurizer'):
+            capi.check(capi.load().zf_featurize_backward_mlp_no_alloc(f.handle, ctypes.byref(a), None))
+        with pytest.raises(capi.ZfError, match='32-bit indexing'):
+            capi.check(capi.load().zf_featurize_backward_mlp(f.handle, ctypes.byref(a), None))
