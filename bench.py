@@ -629,6 +629,8 @@ def run_b200(args) -> None:
         result['e2e'] = measure_e2e(step, args, world, start_exchange, exchange, barrier)
     if not args.skip_train_step:
         result['train_step'] = measure_train_step(args, world, rank, device, barrier)
+    if not args.skip_render:
+        result['render_frame'] = measure_render(args, world, rank, device, barrier)
     if rank == 0 and not args.skip_rows and world == 1:
         result['rows'] = measure_rows(device)
     if rank == 0 and not args.skip_cpu_baseline and world == 1:
@@ -801,6 +803,39 @@ def measure_nerf_mlp(device, physical: int, iters: int = 10, n: int = 65536 * 32
     return out
 
 
+def measure_render(args, world: int, rank: int, device, barrier, frames: int = 3) -> dict:
+    """Config 3: the inference render of one 1296 x 840 frame (zipnerf_b200/render.py: Morton-ordered pixels, view rays,
+    two proposal forwards writing raw densities, deterministic resampling, the NeRF forward, the NeRF MLP and the final
+    compositing), sharded over the ranks by contiguous Morton ranges with no collective. Timed on the device over
+    `frames` frames after 2 warm-up frames; ms per frame is the max over ranks."""
+    import torch.distributed as dist
+    from zipnerf_b200 import render
+    r = render.FrameRenderer(device, rank=rank, world=world)
+    for _ in range(2):
+        r.render()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(frames):
+        r.render()
+    end.record()
+    barrier()
+    ms = start.elapsed_time(end) / frames
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    n_rays = r.n_pixels
+    out = {'ms_per_frame': ms, 'frames': frames, 'rays_per_frame': n_rays, 'mrays_per_s': n_rays / (ms * 1e-3) / 1e6,
+           'featurized_msamples_per_s': n_rays * sum(render.N_SAMPLES) * N_MULTISAMPLES / (ms * 1e-3) / 1e6,
+           'rays_per_gpu': r.n_rays, 'batch_rays': r.batch_rays,
+           'config': f'config3: 1296 x 840 frame, Morton order, {world} contiguous Morton shard(s), 64 + 64 + 32 intervals, pattern seed -1, '
+                     'interleaved thread mapping, forward only; NeRF MLP through ZipNeRFCudaBackend.NerfMlp.forward (inference)'}
+    del r
+    torch.cuda.empty_cache()
+    return out
+
+
 def measure_train_step(args, world: int, rank: int, device, barrier, steps: int = 10) -> dict:
     """The full training step (zipnerf_b200/train_step.py, the reference model's default grids): every rank trains on
     its own rays (weak scaling), each gradient buffer is averaged over the ranks with NCCL on a communication stream as
@@ -937,6 +972,7 @@ def main() -> None:
     parser.add_argument('--skip-reference-cuda', action='store_true', help="skip the timing of the reference's own CUDA kernels")
     parser.add_argument('--skip-contention', action='store_true', help='skip the config-5 contention timing')
     parser.add_argument('--skip-nerf-mlp', action='store_true', help='skip the timing of the NeRF MLP forward')
+    parser.add_argument('--skip-render', action='store_true', help='skip the timing of the config-3 frame render')
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps
     if args.impl == 'reference':
