@@ -1,21 +1,28 @@
-// fz_nerf_mlp.cu -- the NeRF MLP forward of one 128-sample tile per CTA on the tcgen05 tensor cores (bf16 operands in
-// shared memory, fp32 accumulators in tensor memory), the layer chain of NerfMlp::forward (nerf_mlp.h:35-45):
-//   h  = relu(features @ w_density^T + b_density)      -> the first 64 columns of inputs (global) and of the A tile
-//   v0 = relu(inputs @ w_combined^T)                    inputs = [h | encoded direction | 1], bias in the bias lane
-//   out = inputs @ w_skip^T                             8 outputs, accumulated in tensor memory
-//   v1 = relu(v0 @ w_1^T + b_1), v2 = relu(v1 @ w_2^T + b_2)
-//   out += v2 @ w_rgb^T
-// The activations never leave the SM: each layer's epilogue reads its accumulator rows from tensor memory, applies
-// bias and ReLU and writes bf16 back to shared memory as the next layer's A operand.
+// fz_nerf_mlp.cu -- the NeRF MLP forward on the tcgen05 tensor cores: a persistent kernel, one CTA per SM walking over
+// 128-sample tiles, bf16 operands in shared memory, fp32 accumulators in tensor memory. Per tile it runs the layer
+// chain of NerfMlp::forward (nerf_mlp.h:35-45) on the packed (folded) weights:
+//   L0  h  = relu(features @ w_density^T + b_density)      -> columns 0-63 of the inputs tile (and of the global inputs)
+//   L1  v0 = relu(inputs @ w_combined^T)                    inputs = [h | encoded direction | 1], bias in the bias lane
+//   L2  v1 = relu(v0 @ w_1^T + b_1)
+//   L3  v2 = relu(v1 @ w_2^T + b_2)
+//   L4  out = inputs @ w_skip^T + v2 @ w_rgb^T               8 outputs
+// The activations never leave the SM: each layer's epilogue reads its accumulator rows from tensor memory, applies bias
+// and ReLU and writes bf16 back to shared memory as the next layer's A operand.
 //
-// The weights arrive already in the MMAs' shared-memory order, one bulk copy (cp.async.bulk, no multicast) per tensor
-// on a weight mbarrier; the next layer's copy is issued as soon as a layer's MMAs have finished reading the weight
-// buffer, so it lands while that layer's epilogue runs. MMAs and epilogues of one CTA still run one after another.
+// Warp roles (320 threads): warp 0 issues the MMAs (one thread), warp 1 streams the weights (one thread), warps 2-9 run
+// the epilogues and load the input tiles. Weights arrive by bulk copies (cp.async.bulk, no multicast) of pre-packed
+// stages through a two-slot ring: a 256-wide layer is two N-halves of 128 output rows, so the next half's copy runs
+// while the MMAs of the current half do. Tensor memory holds two 256-column accumulator regions used by alternate
+// layers, and the epilogue warps are split the same way: warps 2-5 drain columns [0, 128) of a layer as soon as its
+// first N-half is done, warps 6-9 columns [128, 256) after the second. Barriers between the roles are mbarriers:
+// full / empty per ring slot, acc_full per epilogue half (tcgen05.commit), epi_done (the next layer's A operand is in
+// shared memory). Every wait is bounded: a wait that runs out raises the CTA's abort flag, which ends every role's
+// loop; the CTA then waits (bounded) for its own MMAs and weight copies in flight, frees its tensor memory and sets
+// *status. A status of 1 leaves this launch's outputs undefined.
 //
 // Shared-memory operands use the canonical K-major layout without swizzle: 8-row x 16-byte core matrices stored
 // contiguously (128 bytes), K-adjacent core matrices 128 bytes apart (leading byte offset), 8-row groups
-// (K / 8) * 128 bytes apart (stride byte offset). Every wait on an mbarrier is bounded; a wait that runs out sets
-// *status and the CTA skips to freeing its tensor memory.
+// (K / 8) * 128 bytes apart (stride byte offset).
 #include "zf_mlp.h"
 #include "fz_status.h"
 
@@ -26,26 +33,49 @@
 namespace zf::nerf_mlp {
 
 constexpr int kTileRows = 128;       // M of every MMA: one accumulator row per tensor-memory lane
-constexpr int kThreads = 128;        // 4 warps: warp w owns tensor-memory lanes 32w .. 32w + 31
 constexpr int kFeatures = 56;        // NeRF features per sample: 10 levels x (4 + 1) = 50, padded to 56
 constexpr int kFeaturesK = 64;       // padded to the MMA K step of 16
 constexpr int kDensity = 64;         // density width = hidden columns of the inputs
 constexpr int kInputs = 96;          // hidden 64 + direction block 32 (its last column the bias lane 1.0)
 constexpr int kView = 256;
+constexpr int kHalf = kView / 2;     // output rows of one N-half of a 256-wide layer
 constexpr int kOutputs = 8;          // raw density, 3 rgb logits, 4 padding
 constexpr int kOutputsN = 16;        // the smallest N of an M = 128 MMA
 constexpr int kMmaK = 16;            // K of one kind::f16 MMA
-constexpr uint32_t kTmemColumns = 512;  // accumulator 0..255, outputs 256..271; allocations are powers of two
-constexpr uint32_t kOutColumn = 256;
-constexpr uint32_t kWaitLimit = 1u << 22;  // try_wait polls; a layer's MMAs take microseconds
+
+// warp roles
+constexpr int kMmaWarp = 0;
+constexpr int kProducerWarp = 1;
+constexpr int kFirstEpilogueWarp = 2;
+constexpr int kEpilogueWarps = 8;    // two per tensor-memory lane quadrant: one per N-half
+constexpr int kEpilogueThreads = 32 * kEpilogueWarps;
+constexpr int kThreads = 32 * (kFirstEpilogueWarp + kEpilogueWarps);
+
+constexpr uint32_t kTmemColumns = 512;   // two accumulator regions of 256 columns
+constexpr uint32_t kRegionColumns = 256;
+constexpr uint32_t kWaitLimit = 1u << 22;  // try_wait polls of one wait; a layer takes microseconds
+
+// the weight stages of one tile, in the order the MMAs consume them
+constexpr int kStagesPerTile = 8;
+constexpr int kRingSlots = 2;
+constexpr int kStageBytes = kHalf * kView * 2;                 // 64 KB: one N-half of a 256 x 256 layer
+constexpr int kSkipBytes = kOutputsN * kInputs * 2;            // skip weights at the start of the last stage
+constexpr int kRgbStageOffset = kSkipBytes;                    // rgb weights behind them
+static_assert(kRgbStageOffset % 16 == 0 && kRgbStageOffset + kOutputsN * kView * 2 <= kStageBytes, "skip and rgb share one stage");
 
 // shared-memory carve-up (bytes)
-constexpr int kActBytes = kTileRows * kView * 2;       // 64 KB: features tile, then v0, v1, v2
-constexpr int kInBytes = kTileRows * kInputs * 2;      // 24 KB: the inputs tile
-constexpr int kWeightBytes = kView * kView * 2;        // 128 KB: one layer's weights (combined and skip together)
-constexpr int kSkipOffset = kView * kInputs * 2;       // skip weights behind the combined weights
-constexpr int kSmemBytes = kActBytes + kInBytes + kWeightBytes + 32;  // + the MMA and weight mbarriers, the tensor-memory slot
-static_assert(kSkipOffset + kOutputsN * kInputs * 2 <= kWeightBytes, "combined and skip weights share one buffer");
+constexpr int kActBytes = kTileRows * kView * 2;               // 64 KB: features tile, then v0, v1, v2
+constexpr int kInBytes = kTileRows * kInputs * 2;              // 24 KB: the inputs tile
+constexpr int kBiasFloats = kDensity + 2 * kView;              // density, view_1 and view_2 biases
+constexpr int kActOffset = 0;
+constexpr int kInOffset = kActOffset + kActBytes;
+constexpr int kRingOffset = kInOffset + kInBytes;
+constexpr int kBiasOffset = kRingOffset + kRingSlots * kStageBytes;
+constexpr int kBarOffset = kBiasOffset + kBiasFloats * 4;
+constexpr int kNumBarriers = 8;                                // full[2], empty[2], acc_full[2], epi_done, drain
+constexpr int kMiscOffset = kBarOffset + kNumBarriers * 8;     // tensor-memory slot, abort flag
+constexpr int kSmemBytes = kMiscOffset + 16;
+static_assert(kBarOffset % 8 == 0, "mbarriers are 8-byte aligned");
 static_assert(kSmemBytes <= 227 * 1024, "one CTA per SM");
 
 // packed weights: bf16 [out x in] with zero padding in the canonical K-major order, fp32 biases
@@ -93,35 +123,54 @@ __device__ __forceinline__ void mma(const uint32_t d_tmem, const uint64_t a, con
         "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
 }
 
-// D[128 x n] (+)= A[128 x k] B[n x k]^T from K-major operands, k / 16 MMAs
-__device__ __forceinline__ void mma_chain(const uint32_t d_tmem, const uint32_t a_address, const uint32_t b_address, const int n, const int k,
-                                          const bool accumulate) {
+// D[128 x n] (+)= A[128 x k] B[n x k]^T from K-major operands stored with a_k_total and b_k_total columns, k / 16 MMAs
+__device__ __forceinline__ void mma_chain(const uint32_t d_tmem, const uint32_t a_address, const int a_k_total, const uint32_t b_address,
+                                          const int b_k_total, const int n, const int k, const bool accumulate) {
     const uint32_t idesc = instr_descriptor(kTileRows, n);
-    const uint32_t stride = static_cast<uint32_t>(k >> 3) * 128;
+    const uint32_t a_stride = static_cast<uint32_t>(a_k_total >> 3) * 128, b_stride = static_cast<uint32_t>(b_k_total >> 3) * 128;
     for (int s = 0; s < k / kMmaK; s++) {
         // one K step covers two core matrices: start at chunk 2s, the second chunk one leading offset further
         const uint32_t step = static_cast<uint32_t>(2 * s) * 128;
-        mma(d_tmem, smem_descriptor(a_address + step, 128, stride), smem_descriptor(b_address + step, 128, stride), idesc,
+        mma(d_tmem, smem_descriptor(a_address + step, 128, a_stride), smem_descriptor(b_address + step, 128, b_stride), idesc,
             (accumulate || s > 0) ? 1u : 0u);
     }
 }
 
+// the mbarrier tracks the completion of every tcgen05 operation this thread has issued so far
 __device__ __forceinline__ void commit(const uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-// bounded wait for the given phase parity; false if the limit ran out
-__device__ __forceinline__ bool wait_phase(const uint32_t bar, const uint32_t parity) {
+__device__ __forceinline__ bool try_wait(const uint32_t bar, const uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// bounded wait for the completion of the phase with the given parity; false if the CTA's abort flag went up or the
+// limit ran out (which raises the flag)
+__device__ __forceinline__ bool wait_phase(const uint32_t bar, const uint32_t parity, volatile int* abort) {
     for (uint32_t i = 0; i < kWaitLimit; i++) {
-        uint32_t done;
-        asm volatile(
-            "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(done)
-            : "r"(bar), "r"(parity)
-            : "memory");
-        if (done) return true;
+        if (try_wait(bar, parity)) return true;
+        if ((i & 63u) == 63u && *abort) return false;
     }
+    *abort = 1;
     return false;
+}
+
+// bounded wait that ignores the abort flag (the teardown's wait for work already in flight)
+__device__ __forceinline__ void drain_phase(const uint32_t bar, const uint32_t parity) {
+    for (uint32_t i = 0; i < kWaitLimit; i++) {
+        if (try_wait(bar, parity)) return;
+    }
+}
+
+__device__ __forceinline__ void arrive(const uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -159,39 +208,83 @@ __device__ __forceinline__ uint32_t pack_bf16x2(const float lo, const float hi) 
     return out;
 }
 
-// the weight mbarrier expects `bytes` more bytes in its current phase (the arrival of its one thread)
+// the mbarrier expects `bytes` more bytes in its current phase (the arrival of its one thread)
 __device__ __forceinline__ void expect_bytes(const uint32_t bar, const uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
-// one bulk copy (no multicast) of a weight stored in the canonical order in global memory into shared memory, completing
-// on the weight mbarrier; addresses 16-byte aligned, bytes a multiple of 16
+// one bulk copy (no multicast) of packed weights from global into shared memory, completing on the mbarrier; addresses
+// 16-byte aligned, bytes a multiple of 16
 __device__ __forceinline__ void bulk_copy(const uint32_t dst, const void* src, const uint32_t bytes, const uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst), "l"(src), "r"(bytes),
                  "r"(bar)
                  : "memory");
 }
 
-// this thread's accumulator row (columns 0 .. width - 1) + bias, ReLU, bf16 into row `row` of a K-major operand
-template <int kWidth>
-__device__ __forceinline__ void relu_epilogue(const uint32_t tmem_row, const float* __restrict__ bias, uint8_t* dst, const int row, const int k_total,
-                                              const int k_first) {
-    for (int c = 0; c < kWidth; c += 32) {
-        float v[32];
-        load_columns(tmem_row + static_cast<uint32_t>(c), v);
-        for (int j = 0; j < 32; j += 8) {
-            uint4 out;
-            uint32_t* words = reinterpret_cast<uint32_t*>(&out);
-            for (int q = 0; q < 4; q++) {
-                float lo = v[j + 2 * q], hi = v[j + 2 * q + 1];
-                if (bias != nullptr) {
-                    lo += __ldg(bias + c + j + 2 * q);
-                    hi += __ldg(bias + c + j + 2 * q + 1);
-                }
-                words[q] = pack_bf16x2(fmaxf(lo, 0.0f), fmaxf(hi, 0.0f));
-            }
-            *reinterpret_cast<uint4*>(dst + canonical_offset(row, k_first + c + j, k_total)) = out;
+// 32 accumulator columns of this thread's row + bias (shared memory, or none), ReLU, as 16 words of bf16 pairs
+__device__ __forceinline__ void relu_pack(const uint32_t taddr, const float* bias, uint32_t* words) {
+    float v[32];
+    load_columns(taddr, v);
+    #pragma unroll
+    for (int q = 0; q < 16; q++) {
+        float lo = v[2 * q], hi = v[2 * q + 1];
+        if (bias != nullptr) {
+            lo += bias[2 * q];
+            hi += bias[2 * q + 1];
         }
+        words[q] = pack_bf16x2(fmaxf(lo, 0.0f), fmaxf(hi, 0.0f));
+    }
+}
+
+// 16 words of bf16 pairs (32 columns) into row `row` of a K-major operand at column k_first (and into global memory at
+// `global_row` when given)
+__device__ __forceinline__ void store_words(const uint32_t* words, uint8_t* dst, const int row, const int k_total, const int k_first,
+                                            uint16_t* global_row) {
+    #pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint4 out = make_uint4(words[4 * j], words[4 * j + 1], words[4 * j + 2], words[4 * j + 3]);
+        *reinterpret_cast<uint4*>(dst + canonical_offset(row, k_first + 8 * j, k_total)) = out;
+        if (global_row != nullptr) *reinterpret_cast<uint4*>(global_row + k_first + 8 * j) = out;
+    }
+}
+
+// the tile's features (56 columns + 8 zero columns) into act and its direction block into columns 64-95 of in (zeros
+// for rows past n), by the epilogue threads
+__device__ __forceinline__ void load_tile_inputs(const uint16_t* __restrict__ features, const int64_t features_stride, const uint16_t* inputs,
+                                                 const int64_t inputs_stride, const int64_t first, const int64_t n, uint8_t* act, uint8_t* in,
+                                                 const int tid) {
+    for (int q = tid; q < kTileRows * (kFeaturesK / 8); q += kEpilogueThreads) {
+        const int r = q / (kFeaturesK / 8), c = q % (kFeaturesK / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (first + r < n && c < kFeatures / 8) v = __ldg(reinterpret_cast<const uint4*>(features + (first + r) * features_stride) + c);
+        *reinterpret_cast<uint4*>(act + canonical_offset(r, 8 * c, kFeaturesK)) = v;
+    }
+    for (int q = tid; q < kTileRows * 4; q += kEpilogueThreads) {
+        const int r = q / 4, c = q % 4;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (first + r < n) v = __ldg(reinterpret_cast<const uint4*>(inputs + (first + r) * inputs_stride + kDensity) + c);
+        *reinterpret_cast<uint4*>(in + canonical_offset(r, kDensity + 8 * c, kInputs)) = v;
+    }
+}
+
+// source and size of weight stage s of a tile (the second part only for the last stage)
+struct Stage {
+    const void* src0;
+    uint32_t bytes0;
+    const void* src1;
+    uint32_t bytes1;
+};
+
+__device__ __forceinline__ Stage weight_stage(const PackedMlp& w, const int s) {
+    switch (s) {
+        case 0: return {w.density, kDensity * kFeaturesK * 2, nullptr, 0};
+        case 1: return {w.combined, kHalf * kInputs * 2, nullptr, 0};
+        case 2: return {w.combined + kHalf * kInputs, kHalf * kInputs * 2, nullptr, 0};
+        case 3: return {w.view_1, kHalf * kView * 2, nullptr, 0};
+        case 4: return {w.view_1 + kHalf * kView, kHalf * kView * 2, nullptr, 0};
+        case 5: return {w.view_2, kHalf * kView * 2, nullptr, 0};
+        case 6: return {w.view_2 + kHalf * kView, kHalf * kView * 2, nullptr, 0};
+        default: return {w.skip, kSkipBytes, w.rgb, kOutputsN * kView * 2};
     }
 }
 
@@ -201,186 +294,235 @@ __global__ void __launch_bounds__(kThreads, 1)
     fz_nerf_mlp_forward_kernel(const uint16_t* __restrict__ features, const int64_t features_stride, uint16_t* __restrict__ inputs,
                                const int64_t inputs_stride, const PackedMlp w, uint16_t* __restrict__ outputs, const int64_t n, int* status) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t* act = smem;
-    uint8_t* in = smem + kActBytes;
-    uint8_t* weights = in + kInBytes;
-    uint64_t* bar = reinterpret_cast<uint64_t*>(weights + kWeightBytes);  // MMA completion
-    uint64_t* wbar = bar + 1;                                                // weight copies landed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 2);
-    const int warp = threadIdx.x / 32;
-    const int row = threadIdx.x;  // accumulator row = tensor-memory lane of this thread
-    const int64_t first = static_cast<int64_t>(blockIdx.x) * kTileRows;
-    const int64_t sample = first + row;
-    const bool valid = sample < n;
-    const uint32_t bar_address = smem_address(bar), wbar_address = smem_address(wbar), weights_address = smem_address(weights);
+    uint8_t* act = smem + kActOffset;
+    uint8_t* in = smem + kInOffset;
+    float* bias = reinterpret_cast<float*>(smem + kBiasOffset);  // density [64], view_1 [256], view_2 [256]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOffset);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kMiscOffset);
+    volatile int* abort = reinterpret_cast<volatile int*>(smem + kMiscOffset + 4);
+    const uint32_t bar0 = smem_address(bars);
+    auto full_bar = [&](const uint32_t slot) { return bar0 + 8u * slot; };
+    auto empty_bar = [&](const uint32_t slot) { return bar0 + 8u * (kRingSlots + slot); };
+    auto acc_bar = [&](const uint32_t half) { return bar0 + 8u * (2 * kRingSlots + half); };
+    const uint32_t epi_bar = bar0 + 8u * (2 * kRingSlots + 2);
+    const uint32_t drain_bar = epi_bar + 8u;
+    const uint32_t ring = smem_address(smem + kRingOffset);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int64_t n_tiles = (n + kTileRows - 1) / kTileRows;
 
-    if (warp == 0) {
+    if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_address(tmem_slot)), "r"(kTmemColumns));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    if (threadIdx.x == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar_address), "r"(1));
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(wbar_address), "r"(1));
+    if (threadIdx.x == 32 * kProducerWarp) {
+        for (int s = 0; s < kRingSlots; s++) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(full_bar(s)), "r"(1));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(empty_bar(s)), "r"(1));
+        }
+        for (int h = 0; h < 2; h++) asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(acc_bar(h)), "r"(1));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(epi_bar), "r"(kEpilogueThreads));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(drain_bar), "r"(1));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        expect_bytes(wbar_address, kDensity * kFeaturesK * 2);
-        bulk_copy(weights_address, w.density, kDensity * kFeaturesK * 2, wbar_address);
+        *abort = 0;
     }
-
-    // features (56 columns + 8 zero columns) into act, the direction block into columns 64-95 of in, density weights
-    for (int q = threadIdx.x; q < kTileRows * (kFeaturesK / 8); q += kThreads) {
-        const int r = q / (kFeaturesK / 8), c = q % (kFeaturesK / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (first + r < n && c < kFeatures / 8) v = __ldg(reinterpret_cast<const uint4*>(features + (first + r) * features_stride) + c);
-        *reinterpret_cast<uint4*>(act + canonical_offset(r, 8 * c, kFeaturesK)) = v;
+    for (int i = threadIdx.x; i < kBiasFloats; i += kThreads) {
+        bias[i] = i < kDensity ? __ldg(w.density_bias + i) : i < kDensity + kView ? __ldg(w.view_1_bias + i - kDensity)
+                                                                                   : __ldg(w.view_2_bias + i - kDensity - kView);
     }
-    for (int q = threadIdx.x; q < kTileRows * 4; q += kThreads) {
-        const int r = q / 4, c = q % 4;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (first + r < n) v = __ldg(reinterpret_cast<const uint4*>(inputs + (first + r) * inputs_stride + kDensity) + c);
-        *reinterpret_cast<uint4*>(in + canonical_offset(r, kDensity + 8 * c, kInputs)) = v;
-    }
-    fence_async_shared();
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tmem_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    uint32_t parity = 0, wparity = 0;
-    bool ok = true;  // the same in every thread: each wait's outcome is combined over the block
-    ok = __syncthreads_and(wait_phase(wbar_address, wparity));
-    wparity ^= 1;
-    if (!ok) goto done;
+    bool ok = true;
+    uint32_t stages_issued = 0;
 
-    // layer 0: h = relu(features @ w_density^T + b_density)
-    if (threadIdx.x == 0) {
-        mma_chain(tmem, smem_address(act), smem_address(weights), kDensity, kFeaturesK, false);
-        commit(bar_address);
-    }
-    ok = __syncthreads_and(wait_phase(bar_address, parity));
-    parity ^= 1;
-    if (!ok) goto done;
-    fence_after_sync();
-    if (threadIdx.x == 0) {  // the weight buffer is free: the next layer's weights arrive during this epilogue
-        expect_bytes(wbar_address, (kView + kOutputsN) * kInputs * 2);
-        bulk_copy(weights_address, w.combined, kView * kInputs * 2, wbar_address);
-        bulk_copy(weights_address + kSkipOffset, w.skip, kOutputsN * kInputs * 2, wbar_address);
-    }
-    relu_epilogue<kDensity>(tmem_row, w.density_bias, in, row, kInputs, 0);
-    if (valid) {  // the hidden layer is part of the inputs the backward reads
-        for (int c = 0; c < kDensity / 8; c++) {
-            *reinterpret_cast<uint4*>(inputs + sample * inputs_stride + 8 * c) = *reinterpret_cast<const uint4*>(in + canonical_offset(row, 8 * c, kInputs));
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            // the weight stages of every tile of this CTA, two slots ahead of the MMAs
+            for (int64_t tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+                for (int s = 0; s < kStagesPerTile; s++) {
+                    const uint32_t slot = stages_issued % kRingSlots;
+                    if (stages_issued >= kRingSlots && !wait_phase(empty_bar(slot), (stages_issued / kRingSlots - 1) & 1u, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    const Stage st = weight_stage(w, s);
+                    expect_bytes(full_bar(slot), st.bytes0 + st.bytes1);
+                    bulk_copy(ring + slot * kStageBytes, st.src0, st.bytes0, full_bar(slot));
+                    if (st.bytes1 != 0) bulk_copy(ring + slot * kStageBytes + kRgbStageOffset, st.src1, st.bytes1, full_bar(slot));
+                    stages_issued++;
+                }
+            }
         }
     }
-    fence_async_shared();
-    fence_before_sync();
-    __syncthreads();
-    fence_after_sync();
-    ok = __syncthreads_and(wait_phase(wbar_address, wparity));
-    wparity ^= 1;
-    if (!ok) goto done;
-
-    // layer 1: v0 = relu(inputs @ w_combined^T); outputs = inputs @ w_skip^T
-    if (threadIdx.x == 0) {
-        mma_chain(tmem, smem_address(in), smem_address(weights), kView, kInputs, false);
-        mma_chain(tmem + kOutColumn, smem_address(in), smem_address(weights + kSkipOffset), kOutputsN, kInputs, false);
-        commit(bar_address);
+    else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            uint32_t stage = 0, layer = 0, epi = 0;
+            // the next weight stage (waits for it to land); its slot's empty barrier is committed by release
+            auto take = [&](uint32_t& address) -> bool {
+                const uint32_t slot = stage % kRingSlots;
+                if (!wait_phase(full_bar(slot), (stage / kRingSlots) & 1u, abort)) return false;
+                address = ring + slot * kStageBytes;
+                return true;
+            };
+            auto release = [&]() {
+                commit(empty_bar(stage % kRingSlots));
+                stage++;
+            };
+            // the epilogue warps have finished the previous layer's A operand (or the tile's inputs)
+            auto inputs_ready = [&]() -> bool {
+                const bool done = wait_phase(epi_bar, epi & 1u, abort);
+                epi++;
+                fence_after_sync();
+                return done;
+            };
+            const uint32_t a_act = smem_address(act), a_in = smem_address(in);
+            for (int64_t tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+                uint32_t b = 0;
+                // L0: h = features @ density^T (N = 64, one chain for both epilogue halves)
+                uint32_t d = tmem + (layer & 1u) * kRegionColumns;
+                if (!(ok = inputs_ready() && take(b))) break;
+                mma_chain(d, a_act, kFeaturesK, b, kFeaturesK, kDensity, kFeaturesK, false);
+                release();
+                commit(acc_bar(0));
+                commit(acc_bar(1));
+                layer++;
+                // L1-L3: 256-wide layers as two N-halves of 128 output rows
+                for (int k = 1; k <= 3 && ok; k++) {
+                    d = tmem + (layer & 1u) * kRegionColumns;
+                    const uint32_t a = k == 1 ? a_in : a_act;
+                    const int a_k = k == 1 ? kInputs : kView;
+                    if (!(ok = inputs_ready())) break;
+                    for (int h = 0; h < 2; h++) {
+                        if (!(ok = take(b))) break;
+                        mma_chain(d + h * kHalf, a, a_k, b, a_k, kHalf, a_k, false);
+                        release();
+                        commit(acc_bar(h));
+                    }
+                    layer++;
+                }
+                if (!ok) break;
+                // L4: out = inputs @ skip^T + v2 @ rgb^T (N = 16)
+                d = tmem + (layer & 1u) * kRegionColumns;
+                if (!(ok = inputs_ready() && take(b))) break;
+                mma_chain(d, a_in, kInputs, b, kInputs, kOutputsN, kInputs, false);
+                mma_chain(d, a_act, kView, b + kRgbStageOffset, kView, kOutputsN, kView, true);
+                release();
+                commit(acc_bar(0));
+                commit(acc_bar(1));
+                layer++;
+            }
+        }
     }
-    ok = __syncthreads_and(wait_phase(bar_address, parity));
-    parity ^= 1;
-    if (!ok) goto done;
-    fence_after_sync();
-    if (threadIdx.x == 0) {
-        expect_bytes(wbar_address, kView * kView * 2);
-        bulk_copy(weights_address, w.view_1, kView * kView * 2, wbar_address);
-    }
-    relu_epilogue<kView>(tmem_row, nullptr, act, row, kView, 0);
-    fence_async_shared();
-    fence_before_sync();
-    __syncthreads();
-    fence_after_sync();
-    ok = __syncthreads_and(wait_phase(wbar_address, wparity));
-    wparity ^= 1;
-    if (!ok) goto done;
-
-    // layer 2: v1 = relu(v0 @ w_1^T + b_1)
-    if (threadIdx.x == 0) {
-        mma_chain(tmem, smem_address(act), smem_address(weights), kView, kView, false);
-        commit(bar_address);
-    }
-    ok = __syncthreads_and(wait_phase(bar_address, parity));
-    parity ^= 1;
-    if (!ok) goto done;
-    fence_after_sync();
-    if (threadIdx.x == 0) {
-        expect_bytes(wbar_address, kView * kView * 2);
-        bulk_copy(weights_address, w.view_2, kView * kView * 2, wbar_address);
-    }
-    relu_epilogue<kView>(tmem_row, w.view_1_bias, act, row, kView, 0);
-    fence_async_shared();
-    fence_before_sync();
-    __syncthreads();
-    fence_after_sync();
-    ok = __syncthreads_and(wait_phase(wbar_address, wparity));
-    wparity ^= 1;
-    if (!ok) goto done;
-
-    // layer 3: v2 = relu(v1 @ w_2^T + b_2)
-    if (threadIdx.x == 0) {
-        mma_chain(tmem, smem_address(act), smem_address(weights), kView, kView, false);
-        commit(bar_address);
-    }
-    ok = __syncthreads_and(wait_phase(bar_address, parity));
-    parity ^= 1;
-    if (!ok) goto done;
-    fence_after_sync();
-    if (threadIdx.x == 0) {
-        expect_bytes(wbar_address, kOutputsN * kView * 2);
-        bulk_copy(weights_address, w.rgb, kOutputsN * kView * 2, wbar_address);
-    }
-    relu_epilogue<kView>(tmem_row, w.view_2_bias, act, row, kView, 0);
-    fence_async_shared();
-    fence_before_sync();
-    __syncthreads();
-    fence_after_sync();
-    ok = __syncthreads_and(wait_phase(wbar_address, wparity));
-    wparity ^= 1;
-    if (!ok) goto done;
-
-    // layer 4: outputs += v2 @ w_rgb^T
-    if (threadIdx.x == 0) {
-        mma_chain(tmem + kOutColumn, smem_address(act), smem_address(weights), kOutputsN, kView, true);
-        commit(bar_address);
-    }
-    ok = __syncthreads_and(wait_phase(bar_address, parity));
-    if (!ok) goto done;
-    fence_after_sync();
-    {
-        float v[8];
-        load_columns8(tmem_row + kOutColumn, v);
-        if (valid) {
-            uint4 out;
-            out.x = pack_bf16x2(v[0], v[1]);
-            out.y = pack_bf16x2(v[2], v[3]);
-            out.z = pack_bf16x2(v[4], v[5]);
-            out.w = pack_bf16x2(v[6], v[7]);
-            *reinterpret_cast<uint4*>(outputs + sample * kOutputs) = out;
+    else {
+        // epilogue warps: half h of every layer's columns, the rows of this warp's tensor-memory lane quadrant
+        const int e = warp - kFirstEpilogueWarp;
+        const int h = e / 4;
+        const int quadrant = warp % 4;
+        const int row = 32 * quadrant + lane;
+        const int tid = threadIdx.x - 32 * kFirstEpilogueWarp;
+        const uint32_t lanes = tmem + (static_cast<uint32_t>(32 * quadrant) << 16);
+        uint32_t layer = 0;
+        // warp-uniform outcome: the tensor-memory loads that follow need every lane of the warp
+        auto accumulator_ready = [&](const int half) -> bool {
+            const bool done = __all_sync(0xFFFFFFFFu, wait_phase(acc_bar(half), layer & 1u, abort));
+            fence_after_sync();
+            return done;
+        };
+        auto publish = [&]() {
+            fence_async_shared();
+            fence_before_sync();
+            arrive(epi_bar);
+        };
+        int64_t tile = blockIdx.x;
+        if (tile < n_tiles) {
+            load_tile_inputs(features, features_stride, inputs, inputs_stride, tile * kTileRows, n, act, in, tid);
+            publish();
+        }
+        for (; tile < n_tiles && ok; tile += gridDim.x) {
+            const int64_t sample = tile * kTileRows + row;
+            const bool valid = sample < n;
+            // E0: h + b_density, ReLU -> inputs columns [32 h, 32 h + 32) (shared and global)
+            if (!(ok = accumulator_ready(h))) break;
+            {
+                uint32_t words[16];
+                relu_pack(lanes + (layer & 1u) * kRegionColumns + 32 * h, bias + 32 * h, words);
+                store_words(words, in, row, kInputs, 32 * h, valid ? inputs + sample * inputs_stride : nullptr);
+            }
+            layer++;
+            publish();
+            // E1-E3: v0 (no bias), v1 (+ b_1), v2 (+ b_2) -> act columns [128 h, 128 h + 128). The MMAs of L2 and L3 read
+            // their A operand from act, so the first half's warps, which start when the layer's first N-half is done,
+            // keep their columns in registers until the second N-half (still reading act) is done too.
+            for (int k = 1; k <= 3 && ok; k++) {
+                if (!(ok = accumulator_ready(h))) break;
+                const float* b = k == 1 ? nullptr : bias + kDensity + (k - 2) * kView + kHalf * h;
+                const uint32_t region = lanes + (layer & 1u) * kRegionColumns + kHalf * h;
+                uint32_t words[kHalf / 2];
+                #pragma unroll
+                for (int c = 0; c < kHalf / 32; c++) relu_pack(region + 32 * c, b != nullptr ? b + 32 * c : nullptr, words + 16 * c);
+                if (h == 0 && k >= 2 && !(ok = accumulator_ready(1))) break;
+                #pragma unroll
+                for (int c = 0; c < kHalf / 32; c++) store_words(words + 16 * c, act, row, kView, kHalf * h + 32 * c, nullptr);
+                layer++;
+                publish();
+            }
+            if (!ok) break;
+            // E4: the outputs (first half's warps), then the next tile's inputs
+            if (!(ok = accumulator_ready(h))) break;
+            if (h == 0) {
+                float v[8];
+                load_columns8(lanes + (layer & 1u) * kRegionColumns, v);
+                if (valid) {
+                    uint4 out;
+                    out.x = pack_bf16x2(v[0], v[1]);
+                    out.y = pack_bf16x2(v[2], v[3]);
+                    out.z = pack_bf16x2(v[4], v[5]);
+                    out.w = pack_bf16x2(v[6], v[7]);
+                    *reinterpret_cast<uint4*>(outputs + sample * kOutputs) = out;
+                }
+            }
+            layer++;
+            if (tile + gridDim.x < n_tiles) {
+                load_tile_inputs(features, features_stride, inputs, inputs_stride, (tile + gridDim.x) * kTileRows, n, act, in, tid);
+                publish();
+            }
         }
     }
 
-done:
-    if (!ok && threadIdx.x == 0) atomicExch(status, kWaitTimeout);
+    // teardown: every role has left its loop; on an abort, the MMAs and weight copies already issued finish before the
+    // tensor memory is freed
     fence_before_sync();
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemColumns));
+    if (threadIdx.x == 32 * kMmaWarp) {
+        commit(drain_bar);
+        drain_phase(drain_bar, 0);
+    }
+    if (threadIdx.x == 32 * kProducerWarp && *abort) {
+        for (uint32_t i = stages_issued > kRingSlots ? stages_issued - kRingSlots : 0; i < stages_issued; i++) {
+            drain_phase(full_bar(i % kRingSlots), (i / kRingSlots) & 1u);
+        }
+    }
+    if (threadIdx.x == 0 && *abort) atomicExch(status, kWaitTimeout);
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    if (warp == kMmaWarp) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemColumns));
 }
 
-// one CTA per 128 samples; features, inputs, outputs and weights 16-byte aligned, row strides multiples of 8 elements
+// one CTA per SM over the 128-sample tiles; features, inputs, outputs and weights 16-byte aligned, row strides multiples
+// of 8 elements
 cudaError_t launch_forward(const uint16_t* features, const int64_t features_stride, uint16_t* inputs, const int64_t inputs_stride, const PackedMlp& w,
                            uint16_t* outputs, const int64_t n, int* status, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
-    const cudaError_t e = cudaFuncSetAttribute(fz_nerf_mlp_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(fz_nerf_mlp_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
-    const unsigned int blocks = static_cast<unsigned int>((n + kTileRows - 1) / kTileRows);
+    int device = 0, n_sms = 0;
+    e = cudaGetDevice(&device);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) return e;
+    const int64_t n_tiles = (n + kTileRows - 1) / kTileRows;
+    const unsigned int blocks = static_cast<unsigned int>(n_tiles < n_sms ? n_tiles : n_sms);
     fz_nerf_mlp_forward_kernel<<<blocks, kThreads, kSmemBytes, stream>>>(features, features_stride, inputs, inputs_stride, w, outputs, n, status);
     return cudaGetLastError();
 }

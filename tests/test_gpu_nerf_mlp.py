@@ -77,11 +77,12 @@ def test_nerf_mlp_parameters_is_the_reference_table():
     assert table[0] == ('density_0.weight', [64, 56], 50) and table[-1] == ('rgb.bias', [3], 0) and len(table) == 14
 
 
-@pytest.mark.parametrize('n', [128, 4133])
+@pytest.mark.parametrize('n', [128, 4133, 57_003])
 def test_tensor_core_forward_matches_the_layer_chain(cuda_device, n):
-    """zf_nerf_mlp_forward_tc (one tcgen05 kernel) against the same packed layer chain computed in fp32 from its bf16
-    operands with the kernel's roundings (bias + ReLU in fp32, then bf16): outputs within 1e-2 (1.7e-3 measured), the
-    hidden layer written into the inputs, zero padding outputs, no timed-out wait. n = 4133 leaves a ragged last tile."""
+    """zf_nerf_mlp_forward_tc (one persistent tcgen05 kernel) against the same packed layer chain computed in fp32 from
+    its bf16 operands with the kernel's roundings (bias + ReLU in fp32, then bf16): outputs within 1e-2 (1.7e-3
+    measured), the hidden layer written into the inputs, zero padding outputs, no timed-out wait. n = 4133 leaves a
+    ragged last tile; n = 57,003 gives every CTA of a B200 several tiles (446 tiles over 148 SMs)."""
     from zipnerf_b200 import capi, nerf_mlp as nm
     layout = nm.NerfMlpLayout()
     gen = torch.Generator().manual_seed(7)
@@ -118,3 +119,32 @@ def test_tensor_core_forward_matches_the_layer_chain(cuda_device, n):
 
     assert torch.isfinite(outputs.float()).all() and not outputs[:, 4:].any()
     assert rel(outputs, expected) < 1e-2 and rel(inputs[:, :64], h) < 1e-2
+
+
+def test_tensor_core_forward_rows_are_independent_of_the_batch(cuda_device):
+    """Each sample's outputs depend on its own row only: the first rows of a batch, run alone, equal the same rows of the
+    whole batch bit for bit (what the sharded render relies on), and a second run of the batch repeats the first."""
+    from zipnerf_b200 import capi, nerf_mlp as nm
+    layout = nm.NerfMlpLayout()
+    gen = torch.Generator().manual_seed(11)
+    params = torch.zeros(layout.numel)
+    layout.initialize(params, gen)
+    packed = {k: v.to(cuda_device) for k, v in nm.pack(layout, params).items()}
+    n = 30_001
+    features = torch.randn(n, 56, generator=gen).bfloat16().to(cuda_device)
+    inputs = torch.zeros(n, 96, dtype=torch.bfloat16, device=cuda_device)
+    inputs[:, 64:91] = (torch.rand(n, 27, generator=gen) * 2 - 1).bfloat16().to(cuda_device)
+    inputs[:, 95] = 1.0
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    whole, again = (torch.empty(n, 8, dtype=torch.bfloat16, device=cuda_device) for _ in range(2))
+    capi.nerf_mlp_forward_tc(features, inputs, packed, whole, status)
+    capi.nerf_mlp_forward_tc(features, inputs, packed, again, status)
+    m = 1_000
+    part_inputs = inputs[:m].clone()
+    part = torch.empty(m, 8, dtype=torch.bfloat16, device=cuda_device)
+    capi.nerf_mlp_forward_tc(features[:m].contiguous(), part_inputs, packed, part, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(whole.view(torch.int16), again.view(torch.int16))
+    assert torch.equal(part.view(torch.int16), whole[:m].view(torch.int16))
+    assert torch.equal(part_inputs.view(torch.int16), inputs[:m].view(torch.int16))

@@ -220,7 +220,7 @@ def mma_operand(image, start: int, leading: int, stride: int, rows: int):
     return out
 
 
-@pytest.mark.parametrize('n,k', [(64, 64), (256, 96), (16, 96), (256, 256), (16, 256)])
+@pytest.mark.parametrize('n,k', [(64, 64), (256, 96), (128, 96), (16, 96), (256, 256), (128, 256), (16, 256)])
 def test_tensor_core_operand_layout_is_consistent(n, k):
     """The kernel's staging (canonical_offset) and its MMA descriptors (start + 256 B per K step, leading offset 128 B,
     stride offset k / 8 * 128 B) address the same elements: emulating the operand reads of the documented canonical
@@ -267,7 +267,7 @@ template <int N> int check_instr() {
     return theirs != ours;
 }
 int main() {
-    int bad = check_instr<16>() + check_instr<64>() + check_instr<256>();
+    int bad = check_instr<16>() + check_instr<64>() + check_instr<128>() + check_instr<256>();
     for (uint32_t address : {0u, 0x4000u, 0x1a300u, 0x36000u}) {
         for (uint32_t k : {64u, 96u, 256u}) {
             cute::UMMA::SmemDescriptor d;
@@ -285,7 +285,7 @@ int main() {
 
 @pytest.mark.skipif(shutil.which('nvcc') is None or _cutlass_include() is None, reason='nvcc or the CUTLASS headers are absent')
 def test_tensor_core_descriptors_match_cutlass(tmp_path):
-    """The kernel's instruction descriptors (bf16 x bf16 -> fp32, M = 128, N = 16 / 64 / 256, K-major) and its
+    """The kernel's instruction descriptors (bf16 x bf16 -> fp32, M = 128, N = 16 / 64 / 128 / 256, K-major) and its
     no-swizzle shared-memory descriptors equal the ones CUTLASS's CuTe sm100 code builds (cute/arch/mma_sm100_desc.hpp:
     make_instr_desc, SmemDescriptor with version 1 as make_umma_desc sets it)."""
     source = tmp_path / 'check.cu'
