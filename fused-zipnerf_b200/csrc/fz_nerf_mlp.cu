@@ -10,19 +10,21 @@
 // and ReLU and writes bf16 back to shared memory as the next layer's A operand.
 //
 // Warp roles (320 threads): warp 0 issues the MMAs (one thread), warp 1 streams the weights (one thread), warps 2-9 run
-// the epilogues and load the input tiles. Weights arrive by bulk copies (cp.async.bulk, no multicast) of pre-packed
-// stages through a two-slot ring: a 256-wide layer is two N-halves of 128 output rows, so the next half's copy runs
-// while the MMAs of the current half do. Tensor memory holds two 256-column accumulator regions used by alternate
-// layers, and the epilogue warps are split the same way: warps 2-5 drain columns [0, 128) of a layer as soon as its
-// first N-half is done, warps 6-9 columns [128, 256) after the second. Barriers between the roles are mbarriers:
-// full / empty per ring slot, acc_full per epilogue half (tcgen05.commit), epi_done (the next layer's A operand is in
-// shared memory). Every wait is bounded: a wait that runs out raises the CTA's abort flag, which ends every role's
-// loop; the CTA then waits (bounded) for its own MMAs and weight copies in flight, frees its tensor memory and sets
-// *status. A status of 1 leaves this launch's outputs undefined.
+// the epilogues and load the input tiles. The weights are packed as K-slices of 64 input columns with all output rows
+// (zipnerf_b200.nerf_mlp.pack), so every MMA runs at the full N of its layer; the slices arrive by bulk copies
+// (cp.async.bulk, no multicast) through a four-slot ring, four slices ahead of the MMAs. Tensor memory holds two
+// 256-column accumulator regions used by alternate layers. An epilogue publishes its layer's activations 64 columns at
+// a time (one mbarrier per 64-column chunk), and the next layer's MMAs over K-slice j start as soon as chunk j is in
+// shared memory, so epilogue and MMAs overlap. The next tile's inputs are loaded into registers while the current
+// tile's layers run and stored to shared memory once its last MMAs are done.
+//
+// Every wait is bounded: a wait that runs out raises the CTA's abort flag, which ends every role's loop; the CTA then
+// waits (bounded) for its own MMAs and weight copies in flight, frees its tensor memory and sets *status. A status of 1
+// leaves this launch's outputs undefined.
 //
 // Shared-memory operands use the canonical K-major layout without swizzle: 8-row x 16-byte core matrices stored
 // contiguously (128 bytes), K-adjacent core matrices 128 bytes apart (leading byte offset), 8-row groups
-// (K / 8) * 128 bytes apart (stride byte offset).
+// (K / 8) * 128 bytes apart (stride byte offset), K the operand's stored width (a weight slice: its own width).
 #include "zf_mlp.h"
 #include "fz_status.h"
 
@@ -38,7 +40,6 @@ constexpr int kFeaturesK = 64;       // padded to the MMA K step of 16
 constexpr int kDensity = 64;         // density width = hidden columns of the inputs
 constexpr int kInputs = 96;          // hidden 64 + direction block 32 (its last column the bias lane 1.0)
 constexpr int kView = 256;
-constexpr int kHalf = kView / 2;     // output rows of one N-half of a 256-wide layer
 constexpr int kOutputs = 8;          // raw density, 3 rgb logits, 4 padding
 constexpr int kOutputsN = 16;        // the smallest N of an M = 128 MMA
 constexpr int kMmaK = 16;            // K of one kind::f16 MMA
@@ -47,7 +48,7 @@ constexpr int kMmaK = 16;            // K of one kind::f16 MMA
 constexpr int kMmaWarp = 0;
 constexpr int kProducerWarp = 1;
 constexpr int kFirstEpilogueWarp = 2;
-constexpr int kEpilogueWarps = 8;    // two per tensor-memory lane quadrant: one per N-half
+constexpr int kEpilogueWarps = 8;    // two per tensor-memory lane quadrant
 constexpr int kEpilogueThreads = 32 * kEpilogueWarps;
 constexpr int kThreads = 32 * (kFirstEpilogueWarp + kEpilogueWarps);
 
@@ -55,10 +56,12 @@ constexpr uint32_t kTmemColumns = 512;   // two accumulator regions of 256 colum
 constexpr uint32_t kRegionColumns = 256;
 constexpr uint32_t kWaitLimit = 1u << 22;  // try_wait polls of one wait; a layer takes microseconds
 
-// the weight stages of one tile, in the order the MMAs consume them
-constexpr int kStagesPerTile = 8;
-constexpr int kRingSlots = 2;
-constexpr int kStageBytes = kHalf * kView * 2;                 // 64 KB: one N-half of a 256 x 256 layer
+// weight stages: K-slices of 64 input columns (the combined layer's last slice 32), all output rows each
+constexpr int kSlice = 64;
+constexpr int kChunks = kView / kSlice;                        // 64-column chunks of a 256-wide activation
+constexpr int kStagesPerTile = 12;                             // density, combined x 2, view_1 x 4, view_2 x 4, skip + rgb
+constexpr int kRingSlots = 4;
+constexpr int kStageBytes = kView * kSlice * 2;                // 32 KB
 constexpr int kSkipBytes = kOutputsN * kInputs * 2;            // skip weights at the start of the last stage
 constexpr int kRgbStageOffset = kSkipBytes;                    // rgb weights behind them
 static_assert(kRgbStageOffset % 16 == 0 && kRgbStageOffset + kOutputsN * kView * 2 <= kStageBytes, "skip and rgb share one stage");
@@ -72,11 +75,17 @@ constexpr int kInOffset = kActOffset + kActBytes;
 constexpr int kRingOffset = kInOffset + kInBytes;
 constexpr int kBiasOffset = kRingOffset + kRingSlots * kStageBytes;
 constexpr int kBarOffset = kBiasOffset + kBiasFloats * 4;
-constexpr int kNumBarriers = 8;                                // full[2], empty[2], acc_full[2], epi_done, drain
+// full[4], empty[4], acc_full, in_ready, h_ready, chunk[4], drain
+constexpr int kNumBarriers = 2 * kRingSlots + 3 + kChunks + 1;
 constexpr int kMiscOffset = kBarOffset + kNumBarriers * 8;     // tensor-memory slot, abort flag
 constexpr int kSmemBytes = kMiscOffset + 16;
 static_assert(kBarOffset % 8 == 0, "mbarriers are 8-byte aligned");
 static_assert(kSmemBytes <= 227 * 1024, "one CTA per SM");
+
+// per-thread share of a tile's inputs: features 128 rows x 8 16-byte words (56 columns + zero padding) and direction
+// blocks 128 rows x 4 words
+constexpr int kInputWords = kTileRows * (kFeaturesK / 8 + 4) / kEpilogueThreads;
+static_assert(kInputWords * kEpilogueThreads == kTileRows * (kFeaturesK / 8 + 4), "the input words divide evenly");
 
 // packed weights: bf16 [out x in] with zero padding in the canonical K-major order, fp32 biases
 struct PackedMlp {
@@ -208,6 +217,13 @@ __device__ __forceinline__ uint32_t pack_bf16x2(const float lo, const float hi) 
     return out;
 }
 
+// round to bf16 pairs with negative values (ReLU) set to zero
+__device__ __forceinline__ uint32_t pack_bf16x2_relu(const float lo, const float hi) {
+    uint32_t out;
+    asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(out) : "f"(hi), "f"(lo));
+    return out;
+}
+
 // the mbarrier expects `bytes` more bytes in its current phase (the arrival of its one thread)
 __device__ __forceinline__ void expect_bytes(const uint32_t bar, const uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
@@ -232,7 +248,7 @@ __device__ __forceinline__ void relu_pack(const uint32_t taddr, const float* bia
             lo += bias[2 * q];
             hi += bias[2 * q + 1];
         }
-        words[q] = pack_bf16x2(fmaxf(lo, 0.0f), fmaxf(hi, 0.0f));
+        words[q] = pack_bf16x2_relu(lo, hi);
     }
 }
 
@@ -248,22 +264,51 @@ __device__ __forceinline__ void store_words(const uint32_t* words, uint8_t* dst,
     }
 }
 
-// the tile's features (56 columns + 8 zero columns) into act and its direction block into columns 64-95 of in (zeros
-// for rows past n), by the epilogue threads
-__device__ __forceinline__ void load_tile_inputs(const uint16_t* __restrict__ features, const int64_t features_stride, const uint16_t* inputs,
-                                                 const int64_t inputs_stride, const int64_t first, const int64_t n, uint8_t* act, uint8_t* in,
-                                                 const int tid) {
-    for (int q = tid; q < kTileRows * (kFeaturesK / 8); q += kEpilogueThreads) {
+// input word i of this epilogue thread (tid) for the tile at `first`: its source in global memory (null for a zero
+// word) and its destination in shared memory (act: features with the K-major layout of 64 columns; in: the direction
+// block, columns 64-95)
+__device__ __forceinline__ void input_word(const int i, const int tid, const uint16_t* __restrict__ features, const int64_t features_stride,
+                                           const uint16_t* inputs, const int64_t inputs_stride, const int64_t first, const int64_t n,
+                                           const uint4*& src, uint32_t& dst_offset, bool& to_act) {
+    const int q = tid + i * kEpilogueThreads;
+    constexpr int kFeatureWords = kTileRows * (kFeaturesK / 8);
+    src = nullptr;
+    if (q < kFeatureWords) {
         const int r = q / (kFeaturesK / 8), c = q % (kFeaturesK / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (first + r < n && c < kFeatures / 8) v = __ldg(reinterpret_cast<const uint4*>(features + (first + r) * features_stride) + c);
-        *reinterpret_cast<uint4*>(act + canonical_offset(r, 8 * c, kFeaturesK)) = v;
+        if (first + r < n && c < kFeatures / 8) src = reinterpret_cast<const uint4*>(features + (first + r) * features_stride) + c;
+        dst_offset = canonical_offset(r, 8 * c, kFeaturesK);
+        to_act = true;
     }
-    for (int q = tid; q < kTileRows * 4; q += kEpilogueThreads) {
-        const int r = q / 4, c = q % 4;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (first + r < n) v = __ldg(reinterpret_cast<const uint4*>(inputs + (first + r) * inputs_stride + kDensity) + c);
-        *reinterpret_cast<uint4*>(in + canonical_offset(r, kDensity + 8 * c, kInputs)) = v;
+    else {
+        const int r = (q - kFeatureWords) / 4, c = (q - kFeatureWords) % 4;
+        if (first + r < n) src = reinterpret_cast<const uint4*>(inputs + (first + r) * inputs_stride + kDensity) + c;
+        dst_offset = canonical_offset(r, kDensity + 8 * c, kInputs);
+        to_act = false;
+    }
+}
+
+// this thread's words of the tile's inputs (zeros for rows past n) into registers
+__device__ __forceinline__ void fetch_inputs(uint4 (&words)[kInputWords], const int tid, const uint16_t* __restrict__ features, const int64_t features_stride,
+                                             const uint16_t* inputs, const int64_t inputs_stride, const int64_t first, const int64_t n) {
+    #pragma unroll
+    for (int i = 0; i < kInputWords; i++) {
+        const uint4* src;
+        uint32_t offset;
+        bool to_act;
+        input_word(i, tid, features, features_stride, inputs, inputs_stride, first, n, src, offset, to_act);
+        words[i] = src != nullptr ? __ldg(src) : make_uint4(0, 0, 0, 0);
+    }
+}
+
+// the fetched words into the features tile (act) and the direction block (in)
+__device__ __forceinline__ void store_inputs(const uint4 (&words)[kInputWords], const int tid, uint8_t* act, uint8_t* in) {
+    #pragma unroll
+    for (int i = 0; i < kInputWords; i++) {
+        const uint4* src;
+        uint32_t offset;
+        bool to_act;
+        input_word(i, tid, nullptr, 0, nullptr, 0, 0, 0, src, offset, to_act);
+        *reinterpret_cast<uint4*>((to_act ? act : in) + offset) = words[i];
     }
 }
 
@@ -276,16 +321,12 @@ struct Stage {
 };
 
 __device__ __forceinline__ Stage weight_stage(const PackedMlp& w, const int s) {
-    switch (s) {
-        case 0: return {w.density, kDensity * kFeaturesK * 2, nullptr, 0};
-        case 1: return {w.combined, kHalf * kInputs * 2, nullptr, 0};
-        case 2: return {w.combined + kHalf * kInputs, kHalf * kInputs * 2, nullptr, 0};
-        case 3: return {w.view_1, kHalf * kView * 2, nullptr, 0};
-        case 4: return {w.view_1 + kHalf * kView, kHalf * kView * 2, nullptr, 0};
-        case 5: return {w.view_2, kHalf * kView * 2, nullptr, 0};
-        case 6: return {w.view_2 + kHalf * kView, kHalf * kView * 2, nullptr, 0};
-        default: return {w.skip, kSkipBytes, w.rgb, kOutputsN * kView * 2};
-    }
+    if (s == 0) return {w.density, kDensity * kFeaturesK * 2, nullptr, 0};
+    if (s == 1) return {w.combined, kView * kSlice * 2, nullptr, 0};
+    if (s == 2) return {w.combined + kView * kSlice, kView * (kInputs - kSlice) * 2, nullptr, 0};
+    if (s < 7) return {w.view_1 + (s - 3) * kView * kSlice, kStageBytes, nullptr, 0};
+    if (s < 11) return {w.view_2 + (s - 7) * kView * kSlice, kStageBytes, nullptr, 0};
+    return {w.skip, kSkipBytes, w.rgb, kOutputsN * kView * 2};
 }
 
 // features [n, 56] bf16 (row stride features_stride), inputs [n, 96] bf16 (row stride inputs_stride; the direction
@@ -303,9 +344,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t bar0 = smem_address(bars);
     auto full_bar = [&](const uint32_t slot) { return bar0 + 8u * slot; };
     auto empty_bar = [&](const uint32_t slot) { return bar0 + 8u * (kRingSlots + slot); };
-    auto acc_bar = [&](const uint32_t half) { return bar0 + 8u * (2 * kRingSlots + half); };
-    const uint32_t epi_bar = bar0 + 8u * (2 * kRingSlots + 2);
-    const uint32_t drain_bar = epi_bar + 8u;
+    const uint32_t acc_bar = bar0 + 8u * (2 * kRingSlots);      // a layer's MMAs are done (tcgen05.commit)
+    const uint32_t in_bar = acc_bar + 8u;                      // the tile's inputs are in shared memory
+    const uint32_t h_bar = in_bar + 8u;                        // the hidden layer h is in the inputs tile
+    auto chunk_bar = [&](const int c) { return h_bar + 8u * (1 + c); };  // 64 columns of the next A operand are written
+    const uint32_t drain_bar = h_bar + 8u * (1 + kChunks);
     const uint32_t ring = smem_address(smem + kRingOffset);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int64_t n_tiles = (n + kTileRows - 1) / kTileRows;
@@ -319,8 +362,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(full_bar(s)), "r"(1));
             asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(empty_bar(s)), "r"(1));
         }
-        for (int h = 0; h < 2; h++) asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(acc_bar(h)), "r"(1));
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(epi_bar), "r"(kEpilogueThreads));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(acc_bar), "r"(1));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(in_bar), "r"(kEpilogueThreads));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(h_bar), "r"(kEpilogueThreads));
+        for (int c = 0; c < kChunks; c++) asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(chunk_bar(c)), "r"(kEpilogueThreads / 2));
         asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(drain_bar), "r"(1));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         *abort = 0;
@@ -338,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == kProducerWarp) {
         if (lane == 0) {
-            // the weight stages of every tile of this CTA, two slots ahead of the MMAs
+            // the weight stages of every tile of this CTA, up to a ring's worth ahead of the MMAs
             for (int64_t tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
                 for (int s = 0; s < kStagesPerTile; s++) {
                     const uint32_t slot = stages_issued % kRingSlots;
@@ -357,8 +402,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     else if (warp == kMmaWarp) {
         if (lane == 0) {
-            uint32_t stage = 0, layer = 0, epi = 0;
-            // the next weight stage (waits for it to land); its slot's empty barrier is committed by release
+            uint32_t stage = 0, layer = 0, inputs_seen = 0, hidden_seen = 0;
+            uint32_t chunks_seen[kChunks] = {0, 0, 0, 0};
+            // the next weight stage (waits for it to land); release() commits its slot's empty barrier
             auto take = [&](uint32_t& address) -> bool {
                 const uint32_t slot = stage % kRingSlots;
                 if (!wait_phase(full_bar(slot), (stage / kRingSlots) & 1u, abort)) return false;
@@ -369,108 +415,132 @@ __global__ void __launch_bounds__(kThreads, 1)
                 commit(empty_bar(stage % kRingSlots));
                 stage++;
             };
-            // the epilogue warps have finished the previous layer's A operand (or the tile's inputs)
-            auto inputs_ready = [&]() -> bool {
-                const bool done = wait_phase(epi_bar, epi & 1u, abort);
-                epi++;
+            // chunk c of the next A operand is in shared memory (the epilogue of the previous layer)
+            auto chunk_ready = [&](const int c) -> bool {
+                const bool done = wait_phase(chunk_bar(c), chunks_seen[c] & 1u, abort);
+                chunks_seen[c]++;
                 fence_after_sync();
                 return done;
             };
             const uint32_t a_act = smem_address(act), a_in = smem_address(in);
             for (int64_t tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
                 uint32_t b = 0;
-                // L0: h = features @ density^T (N = 64, one chain for both epilogue halves)
+                // L0: h = features @ density^T (N = 64)
                 uint32_t d = tmem + (layer & 1u) * kRegionColumns;
-                if (!(ok = inputs_ready() && take(b))) break;
+                ok = wait_phase(in_bar, inputs_seen & 1u, abort);
+                inputs_seen++;
+                fence_after_sync();
+                if (!(ok = ok && take(b))) break;
                 mma_chain(d, a_act, kFeaturesK, b, kFeaturesK, kDensity, kFeaturesK, false);
                 release();
-                commit(acc_bar(0));
-                commit(acc_bar(1));
+                commit(acc_bar);
                 layer++;
-                // L1-L3: 256-wide layers as two N-halves of 128 output rows
-                for (int k = 1; k <= 3 && ok; k++) {
+                // L1: v0 = inputs @ combined^T: K-slice 0 reads h (every epilogue thread has written its part), K-slice 1
+                // the direction block
+                d = tmem + (layer & 1u) * kRegionColumns;
+                ok = wait_phase(h_bar, hidden_seen & 1u, abort);
+                hidden_seen++;
+                fence_after_sync();
+                if (!(ok = ok && take(b))) break;
+                mma_chain(d, a_in, kInputs, b, kSlice, kView, kSlice, false);
+                release();
+                if (!(ok = take(b))) break;
+                mma_chain(d, a_in + (kSlice / 8) * 128, kInputs, b, kInputs - kSlice, kView, kInputs - kSlice, true);
+                release();
+                commit(acc_bar);
+                layer++;
+                // L2, L3: K-slice j of the view layers reads chunk j of the previous activation
+                for (int k = 2; k <= 3 && ok; k++) {
                     d = tmem + (layer & 1u) * kRegionColumns;
-                    const uint32_t a = k == 1 ? a_in : a_act;
-                    const int a_k = k == 1 ? kInputs : kView;
-                    if (!(ok = inputs_ready())) break;
-                    for (int h = 0; h < 2; h++) {
-                        if (!(ok = take(b))) break;
-                        mma_chain(d + h * kHalf, a, a_k, b, a_k, kHalf, a_k, false);
+                    for (int j = 0; j < kChunks; j++) {
+                        if (!(ok = chunk_ready(j) && take(b))) break;
+                        mma_chain(d, a_act + j * (kSlice / 8) * 128, kView, b, kSlice, kView, kSlice, j > 0);
                         release();
-                        commit(acc_bar(h));
                     }
+                    if (!ok) break;
+                    commit(acc_bar);
                     layer++;
                 }
                 if (!ok) break;
-                // L4: out = inputs @ skip^T + v2 @ rgb^T (N = 16)
+                // L4: out = inputs @ skip^T + v2 @ rgb^T (N = 16), after every chunk of v2
                 d = tmem + (layer & 1u) * kRegionColumns;
-                if (!(ok = inputs_ready() && take(b))) break;
+                for (int j = 0; j < kChunks && ok; j++) ok = chunk_ready(j);
+                if (!(ok = ok && take(b))) break;
                 mma_chain(d, a_in, kInputs, b, kInputs, kOutputsN, kInputs, false);
                 mma_chain(d, a_act, kView, b + kRgbStageOffset, kView, kOutputsN, kView, true);
                 release();
-                commit(acc_bar(0));
-                commit(acc_bar(1));
+                commit(acc_bar);
                 layer++;
             }
         }
     }
     else {
-        // epilogue warps: half h of every layer's columns, the rows of this warp's tensor-memory lane quadrant
+        // epilogue warps: the rows of this warp's tensor-memory lane quadrant; 64-column chunks g and g + 2 of each
+        // 256-wide layer (g = 0: warps 2-5, g = 1: warps 6-9), so chunks 0 and 1 are published first
         const int e = warp - kFirstEpilogueWarp;
-        const int h = e / 4;
+        const int g = e / 4;
         const int quadrant = warp % 4;
         const int row = 32 * quadrant + lane;
         const int tid = threadIdx.x - 32 * kFirstEpilogueWarp;
         const uint32_t lanes = tmem + (static_cast<uint32_t>(32 * quadrant) << 16);
         uint32_t layer = 0;
         // warp-uniform outcome: the tensor-memory loads that follow need every lane of the warp
-        auto accumulator_ready = [&](const int half) -> bool {
-            const bool done = __all_sync(0xFFFFFFFFu, wait_phase(acc_bar(half), layer & 1u, abort));
+        auto accumulator_ready = [&]() -> bool {
+            const bool done = __all_sync(0xFFFFFFFFu, wait_phase(acc_bar, layer & 1u, abort));
             fence_after_sync();
             return done;
         };
-        auto publish = [&]() {
+        auto publish = [&](const uint32_t bar) {
             fence_async_shared();
             fence_before_sync();
-            arrive(epi_bar);
+            arrive(bar);
         };
+        // relu of 64 accumulator columns [c0, c0 + 64) + bias into columns c0.. of a K-major operand (and global memory)
+        auto relu64 = [&](const uint32_t region, const float* b, uint8_t* dst, const int k_total, const int c0, uint16_t* global_row) {
+            #pragma unroll 1
+            for (int c = c0; c < c0 + kSlice; c += 32) {
+                uint32_t words[16];
+                relu_pack(region + c, b != nullptr ? b + c : nullptr, words);
+                store_words(words, dst, row, k_total, c, global_row);
+            }
+        };
+        uint4 next[kInputWords];
         int64_t tile = blockIdx.x;
         if (tile < n_tiles) {
-            load_tile_inputs(features, features_stride, inputs, inputs_stride, tile * kTileRows, n, act, in, tid);
-            publish();
+            fetch_inputs(next, tid, features, features_stride, inputs, inputs_stride, tile * kTileRows, n);
+            store_inputs(next, tid, act, in);
+            publish(in_bar);
         }
         for (; tile < n_tiles && ok; tile += gridDim.x) {
             const int64_t sample = tile * kTileRows + row;
             const bool valid = sample < n;
-            // E0: h + b_density, ReLU -> inputs columns [32 h, 32 h + 32) (shared and global)
-            if (!(ok = accumulator_ready(h))) break;
+            const bool more = tile + gridDim.x < n_tiles;
+            // E0: h + b_density, ReLU -> inputs columns [32 g, 32 g + 32) (shared and global)
+            if (!(ok = accumulator_ready())) break;
             {
                 uint32_t words[16];
-                relu_pack(lanes + (layer & 1u) * kRegionColumns + 32 * h, bias + 32 * h, words);
-                store_words(words, in, row, kInputs, 32 * h, valid ? inputs + sample * inputs_stride : nullptr);
+                relu_pack(lanes + (layer & 1u) * kRegionColumns + 32 * g, bias + 32 * g, words);
+                store_words(words, in, row, kInputs, 32 * g, valid ? inputs + sample * inputs_stride : nullptr);
+                publish(h_bar);
             }
             layer++;
-            publish();
-            // E1-E3: v0 (no bias), v1 (+ b_1), v2 (+ b_2) -> act columns [128 h, 128 h + 128). The MMAs of L2 and L3 read
-            // their A operand from act, so the first half's warps, which start when the layer's first N-half is done,
-            // keep their columns in registers until the second N-half (still reading act) is done too.
+            // the next tile's inputs, into registers while this tile's layers run
+            if (more) fetch_inputs(next, tid, features, features_stride, inputs, inputs_stride, (tile + gridDim.x) * kTileRows, n);
+            // E1-E3: v0 (no bias), v1 (+ b_1), v2 (+ b_2) -> act, 64-column chunks g and g + 2
             for (int k = 1; k <= 3 && ok; k++) {
-                if (!(ok = accumulator_ready(h))) break;
-                const float* b = k == 1 ? nullptr : bias + kDensity + (k - 2) * kView + kHalf * h;
-                const uint32_t region = lanes + (layer & 1u) * kRegionColumns + kHalf * h;
-                uint32_t words[kHalf / 2];
-                #pragma unroll
-                for (int c = 0; c < kHalf / 32; c++) relu_pack(region + 32 * c, b != nullptr ? b + 32 * c : nullptr, words + 16 * c);
-                if (h == 0 && k >= 2 && !(ok = accumulator_ready(1))) break;
-                #pragma unroll
-                for (int c = 0; c < kHalf / 32; c++) store_words(words + 16 * c, act, row, kView, kHalf * h + 32 * c, nullptr);
+                if (!(ok = accumulator_ready())) break;
+                const float* b = k == 1 ? nullptr : bias + kDensity + (k - 2) * kView;
+                const uint32_t region = lanes + (layer & 1u) * kRegionColumns;
+                for (int c = g; c < kChunks; c += 2) {
+                    relu64(region, b, act, kView, c * kSlice, nullptr);
+                    publish(chunk_bar(c));
+                }
                 layer++;
-                publish();
             }
             if (!ok) break;
-            // E4: the outputs (first half's warps), then the next tile's inputs
-            if (!(ok = accumulator_ready(h))) break;
-            if (h == 0) {
+            // E4: the outputs (g = 0 warps), then the next tile's inputs
+            if (!(ok = accumulator_ready())) break;
+            if (g == 0) {
                 float v[8];
                 load_columns8(lanes + (layer & 1u) * kRegionColumns, v);
                 if (valid) {
@@ -483,9 +553,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             layer++;
-            if (tile + gridDim.x < n_tiles) {
-                load_tile_inputs(features, features_stride, inputs, inputs_stride, (tile + gridDim.x) * kTileRows, n, act, in, tid);
-                publish();
+            if (more) {
+                store_inputs(next, tid, act, in);
+                publish(in_bar);
             }
         }
     }

@@ -137,23 +137,41 @@ def canonical_order(rows: int, k: int) -> torch.Tensor:
     return (r * k + c).expand(rows // 8, k // 8, 8, 8).reshape(-1)
 
 
-def row_major(weight: torch.Tensor) -> torch.Tensor:
-    """The row-major [rows x k] matrix of a weight stored in `canonical_order` (the inverse permutation)."""
+# K-slice width of each packed weight: the tensor-core kernel streams a layer's weights as consecutive slices of this
+# many input columns (all output rows each), and every slice is one contiguous block in the canonical order
+K_SLICE = {'density': 64, 'combined': 64, 'skip': 96, 'view_1': 64, 'view_2': 64, 'rgb': 256}
+
+
+def sliced_order(rows: int, k: int, k_slice: int) -> torch.Tensor:
+    """Row-major element indices of a [rows x k] weight stored as consecutive K-slices of k_slice columns (the last one
+    narrower when k_slice does not divide k), each slice a [rows x width] block in `canonical_order`."""
+    parts = []
+    for c0 in range(0, k, k_slice):
+        width = min(k_slice, k - c0)
+        local = canonical_order(rows, width)
+        parts.append(local // width * k + c0 + local % width)
+    return torch.cat(parts)
+
+
+def row_major(weight: torch.Tensor, k_slice: int | None = None) -> torch.Tensor:
+    """The row-major [rows x k] matrix of a weight stored in `sliced_order` (k_slice columns per slice; one slice by
+    default), the inverse permutation."""
     rows, k = weight.shape
     out = torch.empty_like(weight).reshape(-1)
-    out[canonical_order(rows, k).to(weight.device)] = weight.reshape(-1)
+    out[sliced_order(rows, k, k_slice or k).to(weight.device)] = weight.reshape(-1)
     return out.view(rows, k)
 
 
 def pack(layout: NerfMlpLayout, params: torch.Tensor) -> dict:
-    """`fold` with the weights rounded to bf16 and stored in the tensor cores' canonical order (`canonical_order`), and
-    fp32 biases: the operands of zf_nerf_mlp_forward_tc."""
+    """`fold` with the weights rounded to bf16 and stored as the tensor-core kernel streams them (`sliced_order` with
+    the K-slices of K_SLICE), and fp32 biases: the operands of zf_nerf_mlp_forward_tc."""
     out = {}
     for name, t in fold(layout, params).items():
         if name.endswith('_bias'):
             out[name] = t.contiguous()
         else:
-            out[name] = t.to(torch.bfloat16).reshape(-1)[canonical_order(*t.shape).to(t.device)].view(t.shape).contiguous()
+            order = sliced_order(*t.shape, K_SLICE[name]).to(t.device)
+            out[name] = t.to(torch.bfloat16).reshape(-1)[order].view(t.shape).contiguous()
     return out
 
 

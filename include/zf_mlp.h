@@ -23,11 +23,12 @@ extern "C" {
 ZF_API int zf_relu_backward_bf16(uint16_t* grad, int64_t grad_stride, const uint16_t* activation, int64_t activation_stride, int64_t n_rows,
                                  int n_cols, float* bias_grad, struct CUstream_st* stream);
 
-/* Packed NeRF MLP weights of zf_nerf_mlp_forward_tc: bf16 [out x in] matrices with zero padding, each stored in the
- * tensor cores' no-swizzle K-major order (8-row x 8-column core matrices of 128 bytes, K-adjacent ones next, then the
- * next 8 rows; zipnerf_b200.nerf_mlp.pack writes it), and fp32 biases; the fold of the reference's parameters
- * (nerf_mlp.cu:186-234: bottleneck folded into the first view layer and the rgb skip columns, biases of the layers
- * that read the inputs in their last column). All 16-byte aligned. */
+/* Packed NeRF MLP weights of zf_nerf_mlp_forward_tc: bf16 [out x in] matrices with zero padding, each stored as
+ * consecutive K-slices (all output rows, 64 input columns each; the combined layer's last slice 32; skip and rgb one
+ * slice), every slice in the tensor cores' no-swizzle K-major order (8-row x 8-column core matrices of 128 bytes,
+ * K-adjacent ones next, then the next 8 rows); zipnerf_b200.nerf_mlp.pack writes it. fp32 biases. The fold of the
+ * reference's parameters (nerf_mlp.cu:186-234: bottleneck folded into the first view layer and the rgb skip columns,
+ * biases of the layers that read the inputs in their last column). All 16-byte aligned. */
 typedef struct zf_nerf_mlp_weights {
     const uint16_t* density;       /* [64, 64]: 56 feature columns, zero padding to the MMA K step */
     const float* density_bias;     /* [64] */
@@ -40,12 +41,14 @@ typedef struct zf_nerf_mlp_weights {
     const uint16_t* rgb;           /* [16, 256]: rows 1-3 the rgb weights, the others zero */
 } zf_nerf_mlp_weights;
 
-/* The inference forward of NerfMlp::forward (nerf_mlp.cu:503-560) for the reference model's widths, one tcgen05 kernel
- * (bf16 operands in shared memory, fp32 accumulators in tensor memory, 128 samples per CTA): features [n, 56] bf16,
+/* The inference forward of NerfMlp::forward (nerf_mlp.cu:503-560) for the reference model's widths, one persistent
+ * tcgen05 kernel (bf16 operands in shared memory, fp32 accumulators in tensor memory, 128-sample tiles, one CTA per
+ * SM; each sample's outputs depend on its own row only): features [n, 56] bf16,
  * inputs [n, 96] bf16 (the direction block in columns 64-95 is read, the hidden layer written to columns 0-63),
  * outputs [n, 8] bf16 (raw density, 3 rgb logits, 4 zeros); row strides in elements, multiples of 8; status: a device
- * int the kernel sets to 1 if one of its bounded waits on the tensor cores ran out. Within bf16 rounding of the
- * reference's cuBLASLt chain. */
+ * int the kernel sets to 1 if one of its bounded waits ran out, which leaves this launch's outputs undefined (the
+ * kernel still waits for its own copies and MMAs in flight and frees its tensor memory before it exits). Within bf16
+ * rounding of the reference's cuBLASLt chain. */
 ZF_API int zf_nerf_mlp_forward_tc(const uint16_t* features, int64_t features_stride, uint16_t* inputs, int64_t inputs_stride,
                                   const zf_nerf_mlp_weights* weights, uint16_t* outputs, int64_t n, int* status, struct CUstream_st* stream);
 

@@ -106,7 +106,7 @@ def test_tensor_core_forward_matches_the_layer_chain(cuda_device, n):
     torch.cuda.synchronize()
     assert int(status.item()) == 0
 
-    w = {k: (v if k.endswith('_bias') else nm.row_major(v)).float() for k, v in packed.items()}
+    w = {k: (v if k.endswith('_bias') else nm.row_major(v, nm.K_SLICE[k])).float() for k, v in packed.items()}
     h = torch.relu(torch.nn.functional.pad(features.float(), (0, 8)) @ w['density'].t() + w['density_bias']).bfloat16().float()
     x = torch.cat([h, inputs[:, 64:].float()], 1)
     v0 = torch.relu(x @ w['combined'].t()).bfloat16().float()

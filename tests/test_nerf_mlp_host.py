@@ -94,7 +94,7 @@ def test_packed_weights_have_the_kernel_shapes_and_padding():
     layout, params, g = random_model(2, torch.float32)
     stored = nm.pack(layout, params)
     # the weights are stored in the tensor cores' order; row_major undoes it, and the values are the fold's in bf16
-    packed = {k: (v if k.endswith('_bias') else nm.row_major(v)) for k, v in stored.items()}
+    packed = {k: (v if k.endswith('_bias') else nm.row_major(v, nm.K_SLICE[k])) for k, v in stored.items()}
     folded = nm.fold(layout, params)
     for k, v in packed.items():
         assert torch.equal(v, folded[k] if k.endswith('_bias') else folded[k].to(torch.bfloat16)), k
@@ -299,19 +299,22 @@ def test_tensor_core_descriptors_match_cutlass(tmp_path):
     assert run.returncode == 0 and '0 mismatches' in run.stdout, run.stdout
 
 
-@pytest.mark.parametrize('rows,k', [(64, 64), (256, 96), (16, 96), (256, 256), (16, 256)])
-def test_packed_order_is_the_kernels_canonical_layout(rows, k):
-    """Element (r, c) of a packed weight sits at the kernel's canonical_offset(r, c, k) / 2, so a single bulk copy lands
-    it where the MMA descriptors read it; row_major inverts the order."""
-    order = nm.canonical_order(rows, k)
+@pytest.mark.parametrize('rows,k,k_slice', [(64, 64, 64), (256, 96, 64), (16, 96, 96), (256, 256, 64), (16, 256, 256)])
+def test_packed_order_is_the_kernels_sliced_canonical_layout(rows, k, k_slice):
+    """Element (r, c) of a packed weight sits in K-slice s = c // k_slice at the slice's start plus the kernel's
+    canonical_offset(r, c - s k_slice, width) / 2, where each slice is rows x width elements; so a single bulk copy
+    lands a slice where the MMA descriptors read it. row_major inverts the order."""
+    order = nm.sliced_order(rows, k, k_slice)
     assert sorted(order.tolist()) == list(range(rows * k))
     position = torch.empty(rows * k, dtype=torch.long)
     position[order] = torch.arange(rows * k)
     for r in range(rows):
         for c in range(0, k, 3):
-            assert position[r * k + c].item() == canonical_offset(r, c, k) // 2
+            s = c // k_slice
+            width = min(k_slice, k - s * k_slice)
+            assert position[r * k + c].item() == rows * s * k_slice + canonical_offset(r, c - s * k_slice, width) // 2
     w = torch.randn(rows, k).bfloat16()
-    assert torch.equal(nm.row_major(w.reshape(-1)[order].view(rows, k)), w)
+    assert torch.equal(nm.row_major(w.reshape(-1)[order].view(rows, k), k_slice), w)
 
 
 def test_tensor_core_forward_wrapper_rejects_mismatched_tensors():
