@@ -9,8 +9,8 @@
 // The activations never leave the SM: each layer's epilogue reads its accumulator rows from tensor memory, applies bias
 // and ReLU and writes bf16 back to shared memory as the next layer's A operand.
 //
-// Warp roles (320 threads): warp 0 issues the MMAs (one thread), warp 1 streams the weights (one thread), warps 2-9 run
-// the epilogues and load the input tiles. The weights are packed as K-slices of 64 input columns with all output rows
+// Warp roles (576 threads): warp 0 issues the MMAs (one thread), warp 1 streams the weights (one thread), warps 2-17 run
+// the epilogues (one warp per tensor-memory lane quadrant and 64-column chunk) and load the input tiles. The weights are packed as K-slices of 64 input columns with all output rows
 // (zipnerf_b200.nerf_mlp.pack), so every MMA runs at the full N of its layer; the slices arrive by bulk copies
 // (cp.async.bulk, no multicast) through a four-slot ring, four slices ahead of the MMAs. Tensor memory holds two
 // 256-column accumulator regions used by alternate layers. An epilogue publishes its layer's activations 64 columns at
@@ -48,7 +48,16 @@ constexpr int kMmaK = 16;            // K of one kind::f16 MMA
 constexpr int kMmaWarp = 0;
 constexpr int kProducerWarp = 1;
 constexpr int kFirstEpilogueWarp = 2;
-constexpr int kEpilogueWarps = 8;    // two per tensor-memory lane quadrant
+// whether one lane per epilogue warp polls the accumulator barrier (the others take its outcome)
+#ifndef ZF_MLP_POLL_LANE0
+#define ZF_MLP_POLL_LANE0 0
+#endif
+#ifndef ZF_MLP_EPILOGUE_WARPS
+#define ZF_MLP_EPILOGUE_WARPS 8
+#endif
+constexpr int kEpilogueWarps = ZF_MLP_EPILOGUE_WARPS;  // 4 x the chunk groups: a group of 4 warps covers the 128 lanes
+constexpr int kChunkGroups = kEpilogueWarps / 4;
+static_assert(kChunkGroups == 1 || kChunkGroups == 2 || kChunkGroups == 4, "each group takes whole 64-column chunks");
 constexpr int kEpilogueThreads = 32 * kEpilogueWarps;
 constexpr int kThreads = 32 * (kFirstEpilogueWarp + kEpilogueWarps);
 
@@ -237,30 +246,58 @@ __device__ __forceinline__ void bulk_copy(const uint32_t dst, const void* src, c
                  : "memory");
 }
 
-// 32 accumulator columns of this thread's row + bias (shared memory, or none), ReLU, as 16 words of bf16 pairs
-__device__ __forceinline__ void relu_pack(const uint32_t taddr, const float* bias, uint32_t* words) {
-    float v[32];
-    load_columns(taddr, v);
-    #pragma unroll
-    for (int q = 0; q < 16; q++) {
-        float lo = v[2 * q], hi = v[2 * q + 1];
-        if (bias != nullptr) {
-            lo += bias[2 * q];
-            hi += bias[2 * q + 1];
-        }
-        words[q] = pack_bf16x2_relu(lo, hi);
+// tcgen05.ld of N (16 or 32) consecutive fp32 accumulator columns of this thread's lane into r (no wait)
+template <int N>
+__device__ __forceinline__ void issue_load(const uint32_t taddr, uint32_t* r) {
+    if constexpr (N == 16) {
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]),
+              "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+            : "r"(taddr));
+    }
+    else {
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, "
+            "%19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]),
+              "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+              "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+              "=r"(r[31])
+            : "r"(taddr));
     }
 }
 
-// 16 words of bf16 pairs (32 columns) into row `row` of a K-major operand at column k_first (and into global memory at
-// `global_row` when given)
-__device__ __forceinline__ void store_words(const uint32_t* words, uint8_t* dst, const int row, const int k_total, const int k_first,
-                                            uint16_t* global_row) {
+// N accumulator columns of this thread's row (N = 16, or a multiple of 32 loaded 32 at a time with one wait) + bias
+// (shared memory, or none), ReLU, bf16, into row `row` of a K-major operand at column k_first (and into global memory
+// at `global_row` when given)
+template <int N>
+__device__ __forceinline__ void relu_columns(const uint32_t taddr, const float* bias, uint8_t* dst, const int row, const int k_total, const int k_first,
+                                             uint16_t* global_row) {
+    uint32_t r[N];
+    if constexpr (N == 16) {
+        issue_load<16>(taddr, r);
+    }
+    else {
+        #pragma unroll
+        for (int c = 0; c < N; c += 32) issue_load<32>(taddr + c, r + c);
+    }
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
     #pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const uint4 out = make_uint4(words[4 * j], words[4 * j + 1], words[4 * j + 2], words[4 * j + 3]);
-        *reinterpret_cast<uint4*>(dst + canonical_offset(row, k_first + 8 * j, k_total)) = out;
-        if (global_row != nullptr) *reinterpret_cast<uint4*>(global_row + k_first + 8 * j) = out;
+    for (int j = 0; j < N; j += 8) {
+        uint32_t words[4];
+        #pragma unroll
+        for (int q = 0; q < 4; q++) {
+            float lo = __uint_as_float(r[j + 2 * q]), hi = __uint_as_float(r[j + 2 * q + 1]);
+            if (bias != nullptr) {
+                lo += bias[j + 2 * q];
+                hi += bias[j + 2 * q + 1];
+            }
+            words[q] = pack_bf16x2_relu(lo, hi);
+        }
+        const uint4 out = make_uint4(words[0], words[1], words[2], words[3]);
+        *reinterpret_cast<uint4*>(dst + canonical_offset(row, k_first + j, k_total)) = out;
+        if (global_row != nullptr) *reinterpret_cast<uint4*>(global_row + k_first + j) = out;
     }
 }
 
@@ -365,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(acc_bar), "r"(1));
         asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(in_bar), "r"(kEpilogueThreads));
         asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(h_bar), "r"(kEpilogueThreads));
-        for (int c = 0; c < kChunks; c++) asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(chunk_bar(c)), "r"(kEpilogueThreads / 2));
+        for (int c = 0; c < kChunks; c++) asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(chunk_bar(c)), "r"(128));
         asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(drain_bar), "r"(1));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         *abort = 0;
@@ -475,10 +512,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
     else {
-        // epilogue warps: the rows of this warp's tensor-memory lane quadrant; 64-column chunks g and g + 2 of each
-        // 256-wide layer (g = 0: warps 2-5, g = 1: warps 6-9), so chunks 0 and 1 are published first
+        // epilogue warps: the rows of this warp's tensor-memory lane quadrant; group c (warps 2 + 4c .. 5 + 4c) takes the
+        // 64-column chunks c, c + groups, ... of each 256-wide layer, so the low chunks are published first
         const int e = warp - kFirstEpilogueWarp;
-        const int g = e / 4;
+        const int c = e / 4;
+        constexpr int kHiddenColumns = kDensity / kChunkGroups;  // this group's columns of h
         const int quadrant = warp % 4;
         const int row = 32 * quadrant + lane;
         const int tid = threadIdx.x - 32 * kFirstEpilogueWarp;
@@ -486,7 +524,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t layer = 0;
         // warp-uniform outcome: the tensor-memory loads that follow need every lane of the warp
         auto accumulator_ready = [&]() -> bool {
+#if ZF_MLP_POLL_LANE0
+            bool done = true;
+            if (lane == 0) done = wait_phase(acc_bar, layer & 1u, abort);
+            done = __shfl_sync(0xFFFFFFFFu, done, 0);
+#else
             const bool done = __all_sync(0xFFFFFFFFu, wait_phase(acc_bar, layer & 1u, abort));
+#endif
             fence_after_sync();
             return done;
         };
@@ -494,15 +538,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             fence_async_shared();
             fence_before_sync();
             arrive(bar);
-        };
-        // relu of 64 accumulator columns [c0, c0 + 64) + bias into columns c0.. of a K-major operand (and global memory)
-        auto relu64 = [&](const uint32_t region, const float* b, uint8_t* dst, const int k_total, const int c0, uint16_t* global_row) {
-            #pragma unroll 1
-            for (int c = c0; c < c0 + kSlice; c += 32) {
-                uint32_t words[16];
-                relu_pack(region + c, b != nullptr ? b + c : nullptr, words);
-                store_words(words, dst, row, k_total, c, global_row);
-            }
         };
         uint4 next[kInputWords];
         int64_t tile = blockIdx.x;
@@ -515,32 +550,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t sample = tile * kTileRows + row;
             const bool valid = sample < n;
             const bool more = tile + gridDim.x < n_tiles;
-            // E0: h + b_density, ReLU -> inputs columns [32 g, 32 g + 32) (shared and global)
+            // E0: h + b_density, ReLU -> this group's columns of h in the inputs (shared and global)
             if (!(ok = accumulator_ready())) break;
-            {
-                uint32_t words[16];
-                relu_pack(lanes + (layer & 1u) * kRegionColumns + 32 * g, bias + 32 * g, words);
-                store_words(words, in, row, kInputs, 32 * g, valid ? inputs + sample * inputs_stride : nullptr);
-                publish(h_bar);
-            }
+            relu_columns<kHiddenColumns>(lanes + (layer & 1u) * kRegionColumns + kHiddenColumns * c, bias + kHiddenColumns * c, in, row, kInputs,
+                                         kHiddenColumns * c, valid ? inputs + sample * inputs_stride : nullptr);
+            publish(h_bar);
             layer++;
             // the next tile's inputs, into registers while this tile's layers run
             if (more) fetch_inputs(next, tid, features, features_stride, inputs, inputs_stride, (tile + gridDim.x) * kTileRows, n);
-            // E1-E3: v0 (no bias), v1 (+ b_1), v2 (+ b_2) -> act, 64-column chunks g and g + 2
+            // E1-E3: v0 (no bias), v1 (+ b_1), v2 (+ b_2) -> act, this group's 64-column chunks
             for (int k = 1; k <= 3 && ok; k++) {
                 if (!(ok = accumulator_ready())) break;
                 const float* b = k == 1 ? nullptr : bias + kDensity + (k - 2) * kView;
-                const uint32_t region = lanes + (layer & 1u) * kRegionColumns;
-                for (int c = g; c < kChunks; c += 2) {
-                    relu64(region, b, act, kView, c * kSlice, nullptr);
-                    publish(chunk_bar(c));
+                for (int j = c; j < kChunks; j += kChunkGroups) {
+                    relu_columns<kSlice>(lanes + (layer & 1u) * kRegionColumns + kSlice * j, b != nullptr ? b + kSlice * j : nullptr, act, row, kView,
+                                         kSlice * j, nullptr);
+                    publish(chunk_bar(j));
                 }
                 layer++;
             }
             if (!ok) break;
-            // E4: the outputs (g = 0 warps), then the next tile's inputs
+            // E4: the outputs (chunk-0 warps), then the next tile's inputs
             if (!(ok = accumulator_ready())) break;
-            if (g == 0) {
+            if (c == 0) {
                 float v[8];
                 load_columns8(lanes + (layer & 1u) * kRegionColumns, v);
                 if (valid) {
