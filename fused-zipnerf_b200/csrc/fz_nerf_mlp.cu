@@ -63,7 +63,10 @@ constexpr int kThreads = 32 * (kFirstEpilogueWarp + kEpilogueWarps);
 
 constexpr uint32_t kTmemColumns = 512;   // two accumulator regions of 256 columns
 constexpr uint32_t kRegionColumns = 256;
-constexpr uint32_t kWaitLimit = 1u << 22;  // try_wait polls of one wait; a layer takes microseconds
+// bounded waits: a waiting thread is suspended in mbarrier.try_wait for up to kSuspendNs at a time (woken when the phase
+// completes), and gives up after kWaitNs in total; a layer takes microseconds
+constexpr uint32_t kSuspendNs = 20000;
+constexpr uint64_t kWaitNs = 2000000000ull;
 
 // weight stages: K-slices of 64 input columns (the combined layer's last slice 32), all output rows each
 constexpr int kSlice = 64;
@@ -159,22 +162,32 @@ __device__ __forceinline__ void commit(const uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
+// whether the phase with the given parity has completed; the thread may be suspended (up to kSuspendNs) until it does
 __device__ __forceinline__ bool try_wait(const uint32_t bar, const uint32_t parity) {
     uint32_t done;
     asm volatile(
-        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(done)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(kSuspendNs)
         : "memory");
     return done != 0;
 }
 
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 // bounded wait for the completion of the phase with the given parity; false if the CTA's abort flag went up or the
-// limit ran out (which raises the flag)
+// time limit ran out (which raises the flag)
 __device__ __forceinline__ bool wait_phase(const uint32_t bar, const uint32_t parity, volatile int* abort) {
-    for (uint32_t i = 0; i < kWaitLimit; i++) {
+    if (try_wait(bar, parity)) return true;
+    const uint64_t start = global_ns();
+    while (true) {
         if (try_wait(bar, parity)) return true;
-        if ((i & 63u) == 63u && *abort) return false;
+        if (*abort) return false;
+        if (global_ns() - start > kWaitNs) break;
     }
     *abort = 1;
     return false;
@@ -182,8 +195,8 @@ __device__ __forceinline__ bool wait_phase(const uint32_t bar, const uint32_t pa
 
 // bounded wait that ignores the abort flag (the teardown's wait for work already in flight)
 __device__ __forceinline__ void drain_phase(const uint32_t bar, const uint32_t parity) {
-    for (uint32_t i = 0; i < kWaitLimit; i++) {
-        if (try_wait(bar, parity)) return;
+    const uint64_t start = global_ns();
+    while (!try_wait(bar, parity) && global_ns() - start <= kWaitNs) {
     }
 }
 
