@@ -875,9 +875,9 @@ def measure_train_step(args, world: int, rank: int, device, barrier, steps: int 
     return {'ms': ms, 'steps': steps, 'rays_per_s': world * args.rays / (ms * 1e-3), 'featurized_msamples_per_s': world * step.samples_per_step / (ms * 1e-3) / 1e6,
             'loss_sums_last_step': losses,
             'config': f'{args.rays} rays per GPU x (64 + 64 + 32) intervals; grids of the reference model (6 and 8 levels x 1 feature, 10 x 4, '
-                      f'scale 2, 2^21); rays from a 185-view 1296 x 840 pool; gradient all-reduce over {world} GPU(s) and Adam; the NeRF MLP as '
-                      'cuBLAS / cuBLASLt bf16 GEMMs with bias-ReLU epilogues and this backend\'s ReLU-backward kernel (a stand-in of the '
-                      'reference cuBLASLt chain)'}
+                      f'scale 2, 2^21); rays from a 185-view 1296 x 840 pool; gradient all-reduce over {world} GPU(s) and Adam; the NeRF MLP '
+                      'with the reference interface: forward on the tcgen05 kernel, backward as cuBLAS bf16 GEMMs with this backend\'s '
+                      'ReLU-backward kernel'}
 
 
 def measure_e2e(step: Step, args, world: int, start_exchange, exchange, barrier) -> dict:

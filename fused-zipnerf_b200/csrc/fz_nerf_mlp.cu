@@ -383,7 +383,8 @@ __device__ __forceinline__ Stage weight_stage(const PackedMlp& w, const int s) {
 // block in columns 64-95 is read, the hidden layer written to columns 0-63), outputs [n, 8] bf16
 __global__ void __launch_bounds__(kThreads, 1)
     fz_nerf_mlp_forward_kernel(const uint16_t* __restrict__ features, const int64_t features_stride, uint16_t* __restrict__ inputs,
-                               const int64_t inputs_stride, const PackedMlp w, uint16_t* __restrict__ outputs, const int64_t n, int* status) {
+                               const int64_t inputs_stride, const PackedMlp w, uint16_t* __restrict__ outputs, uint16_t* __restrict__ activations,
+                               const int64_t n, int* status) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* act = smem + kActOffset;
     uint8_t* in = smem + kInOffset;
@@ -575,9 +576,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int k = 1; k <= 3 && ok; k++) {
                 if (!(ok = accumulator_ready())) break;
                 const float* b = k == 1 ? nullptr : bias + kDensity + (k - 2) * kView;
+                // the training forward also keeps v0, v1, v2 in global memory for the backward
+                uint16_t* kept = activations != nullptr && valid ? activations + (static_cast<int64_t>(k - 1) * n + sample) * kView : nullptr;
                 for (int j = c; j < kChunks; j += kChunkGroups) {
                     relu_columns<kSlice>(lanes + (layer & 1u) * kRegionColumns + kSlice * j, b != nullptr ? b + kSlice * j : nullptr, act, row, kView,
-                                         kSlice * j, nullptr);
+                                         kSlice * j, kept);
                     publish(chunk_bar(j));
                 }
                 layer++;
@@ -628,7 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // one CTA per SM over the 128-sample tiles; features, inputs, outputs and weights 16-byte aligned, row strides multiples
 // of 8 elements
 cudaError_t launch_forward(const uint16_t* features, const int64_t features_stride, uint16_t* inputs, const int64_t inputs_stride, const PackedMlp& w,
-                           uint16_t* outputs, const int64_t n, int* status, cudaStream_t stream) {
+                           uint16_t* outputs, uint16_t* activations, const int64_t n, int* status, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
     cudaError_t e = cudaFuncSetAttribute(fz_nerf_mlp_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
@@ -638,14 +641,16 @@ cudaError_t launch_forward(const uint16_t* features, const int64_t features_stri
     if (e != cudaSuccess) return e;
     const int64_t n_tiles = (n + kTileRows - 1) / kTileRows;
     const unsigned int blocks = static_cast<unsigned int>(n_tiles < n_sms ? n_tiles : n_sms);
-    fz_nerf_mlp_forward_kernel<<<blocks, kThreads, kSmemBytes, stream>>>(features, features_stride, inputs, inputs_stride, w, outputs, n, status);
+    fz_nerf_mlp_forward_kernel<<<blocks, kThreads, kSmemBytes, stream>>>(features, features_stride, inputs, inputs_stride, w, outputs, activations, n,
+                                                                         status);
     return cudaGetLastError();
 }
 
 }  // namespace zf::nerf_mlp
 
 int zf_nerf_mlp_forward_tc(const uint16_t* features, const int64_t features_stride, uint16_t* inputs, const int64_t inputs_stride,
-                           const zf_nerf_mlp_weights* weights, uint16_t* outputs, const int64_t n, int* status, cudaStream_t stream) {
+                           const zf_nerf_mlp_weights* weights, uint16_t* outputs, uint16_t* activations, const int64_t n, int* status,
+                           cudaStream_t stream) {
     using namespace zf::nerf_mlp;
     if (n < 0 || weights == nullptr || status == nullptr) return zf::set_error(ZF_ERROR_INVALID_ARGUMENT, "invalid nerf mlp inputs");
     if (n == 0) return ZF_OK;
@@ -659,6 +664,9 @@ int zf_nerf_mlp_forward_tc(const uint16_t* features, const int64_t features_stri
     }
     const PackedMlp w{weights->density, weights->density_bias, weights->combined, weights->skip, weights->view_1,
                       weights->view_1_bias, weights->view_2, weights->view_2_bias, weights->rgb};
-    const cudaError_t e = launch_forward(features, features_stride, inputs, inputs_stride, w, outputs, n, status, stream);
+    if (activations != nullptr && reinterpret_cast<uintptr_t>(activations) % 16 != 0) {
+        return zf::set_error(ZF_ERROR_INVALID_ARGUMENT, "nerf mlp activations must be 16-byte aligned");
+    }
+    const cudaError_t e = launch_forward(features, features_stride, inputs, inputs_stride, w, outputs, activations, n, status, stream);
     return e == cudaSuccess ? ZF_OK : zf::set_cuda_error(e, "nerf mlp forward");
 }

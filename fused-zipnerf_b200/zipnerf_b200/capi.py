@@ -178,7 +178,7 @@ def load() -> ctypes.CDLL:
     # zf_mlp.h
     lib.zf_relu_backward_bf16.argtypes = [_p, _i64, _p, _i64, _i64, ctypes.c_int, _p, _p]
     lib.zf_relu_backward_bf16.restype = ctypes.c_int
-    lib.zf_nerf_mlp_forward_tc.argtypes = [_p, _i64, _p, _i64, _p, _p, _i64, _p, _p]
+    lib.zf_nerf_mlp_forward_tc.argtypes = [_p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _p]
     lib.zf_nerf_mlp_forward_tc.restype = ctypes.c_int
     _lib = lib
     return lib
@@ -410,7 +410,7 @@ NERF_MLP_PACKED_SHAPES = {'density': ((64, 64), 'bfloat16'), 'density_bias': ((6
                           'view_2': ((256, 256), 'bfloat16'), 'view_2_bias': ((256,), 'float32'), 'rgb': ((16, 256), 'bfloat16')}
 
 
-def check_nerf_mlp_forward_tc(features, inputs, packed: dict, outputs, status, require_cuda: bool = True) -> None:
+def check_nerf_mlp_forward_tc(features, inputs, packed: dict, outputs, status, require_cuda: bool = True, activations=None) -> None:
     """Raises ValueError unless the tensors have the shapes, dtypes and layouts the tensor-core kernel reads and writes
     (the C ABI sees only pointers and row strides, so a wrong shape here would make the kernel read or write out of
     bounds): features [n, >= 56] and inputs [n, >= 96] bf16 CUDA tensors with unit column stride, outputs a contiguous
@@ -438,16 +438,20 @@ def check_nerf_mlp_forward_tc(features, inputs, packed: dict, outputs, status, r
             raise ValueError(f'packed[{name!r}] must be a contiguous {dtype} CUDA tensor of {shape} elements')
     if not isinstance(status, torch.Tensor) or not on_device(status) or status.dtype != torch.int32 or status.numel() < 1:
         raise ValueError('status must be an int32 CUDA tensor')
+    if activations is not None and (not isinstance(activations, torch.Tensor) or not on_device(activations) or activations.dtype != torch.bfloat16
+                                    or tuple(activations.shape) != (3, n, 256) or not activations.is_contiguous()):
+        raise ValueError(f'activations must be None or a contiguous [3, {n}, 256] bf16 tensor')
 
 
-def nerf_mlp_forward_tc(features, inputs, packed: dict, outputs, status, stream=None) -> None:
+def nerf_mlp_forward_tc(features, inputs, packed: dict, outputs, status, activations=None, stream=None) -> None:
     """zf_nerf_mlp_forward_tc: features [n, 56] and inputs [n, 96] bf16, packed as zipnerf_b200.nerf_mlp.pack gives it
-    (the kernel's shapes), outputs [n, 8] bf16, status a device int32 the kernel sets on a timed-out wait. The
-    tensors are checked first (check_nerf_mlp_forward_tc: ValueError on a mismatch)."""
-    check_nerf_mlp_forward_tc(features, inputs, packed, outputs, status)
+    (the kernel's shapes), outputs [n, 8] bf16, status a device int32 the kernel sets on a timed-out wait; activations
+    None (inference) or a contiguous [3, n, 256] bf16 tensor for v0, v1, v2 (training). The tensors are checked first
+    (check_nerf_mlp_forward_tc: ValueError on a mismatch)."""
+    check_nerf_mlp_forward_tc(features, inputs, packed, outputs, status, activations=activations)
     w = zf_nerf_mlp_weights(*[packed[name].data_ptr() for name, _ in zf_nerf_mlp_weights._fields_])
     check(load().zf_nerf_mlp_forward_tc(_ptr(features), features.stride(0), _ptr(inputs), inputs.stride(0), ctypes.byref(w), _ptr(outputs),
-                                        features.shape[0], _ptr(status), _stream(stream)))
+                                        _ptr(activations), features.shape[0], _ptr(status), _stream(stream)))
 
 
 class CAdam:

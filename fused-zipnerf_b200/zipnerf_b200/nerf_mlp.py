@@ -162,17 +162,35 @@ def row_major(weight: torch.Tensor, k_slice: int | None = None) -> torch.Tensor:
     return out.view(rows, k)
 
 
-def pack(layout: NerfMlpLayout, params: torch.Tensor) -> dict:
-    """`fold` with the weights rounded to bf16 and stored as the tensor-core kernel streams them (`sliced_order` with
-    the K-slices of K_SLICE), and fp32 biases: the operands of zf_nerf_mlp_forward_tc."""
+_ORDERS: dict = {}
+
+
+def _device_order(rows: int, k: int, k_slice: int, device) -> torch.Tensor:
+    """sliced_order on the device, computed once per shape and device"""
+    key = (rows, k, k_slice, str(device))
+    if key not in _ORDERS:
+        _ORDERS[key] = sliced_order(rows, k, k_slice).to(device)
+    return _ORDERS[key]
+
+
+def pack_folded(folded: dict) -> dict:
+    """The folded network (`fold` in the kernel's shapes) as the operands of zf_nerf_mlp_forward_tc: the weights
+    rounded to bf16 and stored as the tensor-core kernel streams them (`sliced_order` with the K-slices of K_SLICE),
+    the biases rounded to bf16 but stored as fp32 (the reference adds bf16 biases in its fp32 GEMM epilogues,
+    nerf_mlp.cu:31,355-363)."""
     out = {}
-    for name, t in fold(layout, params).items():
+    for name, t in folded.items():
         if name.endswith('_bias'):
-            out[name] = t.contiguous()
+            out[name] = t.to(torch.bfloat16).float().contiguous()
         else:
-            order = sliced_order(*t.shape, K_SLICE[name]).to(t.device)
+            order = _device_order(*t.shape, K_SLICE[name], t.device)
             out[name] = t.to(torch.bfloat16).reshape(-1)[order].view(t.shape).contiguous()
     return out
+
+
+def pack(layout: NerfMlpLayout, params: torch.Tensor) -> dict:
+    """`fold` in the kernel's shapes, packed as the operands of zf_nerf_mlp_forward_tc (`pack_folded`)."""
+    return pack_folded(fold(layout, params))
 
 
 def folded_forward(packed: dict, features: torch.Tensor, direction_block: torch.Tensor) -> torch.Tensor:
@@ -195,14 +213,19 @@ PACKED_ORDER = ('density', 'density_bias', 'combined', 'skip', 'view_1', 'view_1
 
 class NerfMlp:
     """The reference's `NerfMlp` interface (nerf_mlp.h:47-73: `n_features`, `n_inputs`, `pack`, `forward`,
-    `backward`) over the same folded bf16 layer chain as its cuBLASLt path: bf16 GEMMs with bias + ReLU epilogues
-    (cuBLASLt through torch) and this backend's ReLU backward with the bias gradient (`relu_backward_`, zf_mlp.h).
-    `pack` returns the folded weights and biases as one flat bf16 tensor; the backward's packed-weight gradients go
-    back to the fp32 parameters through autograd of the fold.
+    `backward`). `pack` returns one flat bf16 tensor (its layout private to this class, as the reference's packed
+    buffer is): the folded weights and biases row-major, and, for the reference model's widths, the same fold in the
+    tensor-core kernel's order (`pack`, K-sliced canonical bf16 weights and fp32 biases stored bit for bit).
 
-    `_forward` and `_backward` hold the layer chain for any device with `relu_backward` given (the CPU tests pass a
+    forward: the tcgen05 kernel zf_nerf_mlp_forward_tc (one persistent kernel for all layers; training keeps v0, v1,
+    v2 for the backward), for the reference model's widths; other widths run the folded bf16 layer chain as GEMMs with
+    bias + ReLU epilogues (cuBLASLt through torch). backward: the folded chain's GEMMs (cuBLAS through torch) with this
+    backend's ReLU backward and bias gradient (`relu_backward_`, zf_mlp.h); the packed-weight gradients go back to the
+    fp32 parameters through autograd of the fold.
+
+    `_forward` and `_backward` hold the GEMM layer chain for any device with `relu_backward` given (the CPU tests pass a
     torch restatement of the kernel's contract); the public methods take CUDA tensors only, as the reference's
-    checks (nerf_mlp.cu:286-290,493-496,570-574), and use the CUDA kernel."""
+    checks (nerf_mlp.cu:286-290,493-496,570-574)."""
 
     def __init__(self, n_features: int, density_width: int, bottleneck_width: int, view_width: int, direction_degree: int) -> None:
         self.layout = NerfMlpLayout(n_features, density_width, bottleneck_width, view_width, direction_degree)
@@ -211,7 +234,16 @@ class NerfMlp:
         for name in PACKED_ORDER:
             self._offsets[name] = n
             n += math.prod(self._shapes[name])
+        # the tensor-core section: the kernel's widths only (features padded to 56, 64 / 256 / 256, direction degree 4)
+        self.tensor_cores = (self.layout.n_features == 56 and density_width == 64 and view_width == 256 and self.layout.n_inputs == 96)
+        self._tc_shapes, self._tc_offsets = {}, {}
+        if self.tensor_cores:
+            self._tc_shapes = {name: tuple(t.shape) for name, t in fold(self.layout, torch.zeros(self.layout.numel)).items()}
+            for name in PACKED_ORDER:
+                self._tc_offsets[name] = n
+                n += math.prod(self._tc_shapes[name]) * (2 if name.endswith('_bias') else 1)  # fp32 biases: two bf16 slots
         self.packed_size = n
+        self._status = {}
 
     @property
     def n_features(self) -> int:
@@ -232,11 +264,46 @@ class NerfMlp:
     def _pack(self, params: torch.Tensor) -> torch.Tensor:
         if params.numel() < self.layout.size:
             raise RuntimeError('ZipNeRF: invalid nerf mlp parameters')
-        folded = self._fold(params)
-        return torch.cat([folded[name].reshape(-1) for name in PACKED_ORDER]).to(torch.bfloat16)
+        if not self.tensor_cores:
+            folded = self._fold(params)
+            return torch.cat([folded[name].reshape(-1).to(torch.bfloat16) for name in PACKED_ORDER])
+        # one fold in the kernel's shapes; the row-major section is its leading rows and columns
+        folded = fold(self.layout, params[:self.layout.numel])
+        parts = [folded[name][tuple(slice(0, d) for d in self._shapes[name])].reshape(-1).to(torch.bfloat16) for name in PACKED_ORDER]
+        tc = pack_folded(folded)
+        parts += [tc[name].reshape(-1).view(torch.bfloat16) if name.endswith('_bias') else tc[name].reshape(-1) for name in PACKED_ORDER]
+        return torch.cat(parts)
 
     def _weights(self, packed: torch.Tensor) -> dict:
         return {name: packed[self._offsets[name]:self._offsets[name] + math.prod(self._shapes[name])].view(self._shapes[name]) for name in PACKED_ORDER}
+
+    def _tc_weights(self, packed: torch.Tensor) -> dict:
+        """Views of the tensor-core section: bf16 weights in the kernel's order, fp32 biases."""
+        out = {}
+        for name in PACKED_ORDER:
+            a, shape = self._tc_offsets[name], self._tc_shapes[name]
+            if name.endswith('_bias'):
+                out[name] = packed[a:a + 2 * math.prod(shape)].view(torch.float32)
+            else:
+                out[name] = packed[a:a + math.prod(shape)].view(shape)
+        return out
+
+    def status(self, device) -> torch.Tensor:
+        """The device int32 the tensor-core forward sets to 1 if one of its bounded waits ran out (outputs undefined)."""
+        key = str(device)
+        if key not in self._status:
+            self._status[key] = torch.zeros(1, dtype=torch.int32, device=device)
+        return self._status[key]
+
+    def _forward_tc(self, features: torch.Tensor, inputs: torch.Tensor, packed: torch.Tensor, training: bool):
+        from zipnerf_b200 import capi
+        if features.shape[1] != self.n_features or inputs.shape[1] != self.n_inputs or packed.numel() != self.packed_size:
+            raise RuntimeError('ZipNeRF: invalid nerf mlp inputs')
+        n = features.shape[0]
+        outputs = torch.empty(n, 8, dtype=torch.bfloat16, device=features.device)
+        activations = torch.empty(3, n, self.layout.view_width, dtype=torch.bfloat16, device=features.device) if training else None
+        capi.nerf_mlp_forward_tc(features, inputs, self._tc_weights(packed), outputs, self.status(features.device), activations=activations)
+        return outputs, ([inputs, activations[0], activations[1], activations[2]] if training else [])
 
     def _forward(self, features: torch.Tensor, inputs: torch.Tensor, packed: torch.Tensor, training: bool):
         if features.shape[1] != self.n_features or inputs.shape[1] != self.n_inputs or packed.numel() != self.packed_size:
@@ -260,20 +327,21 @@ class NerfMlp:
         dw = self.layout.density_width
         bias_grads = {name: torch.zeros(self._shapes[name], device=packed.device) for name in ('density_bias', 'view_1_bias', 'view_2_bias')}
         no_bias = bias_grads['density_bias'][:0]
-        g = {'rgb': grad_outputs.t().float() @ v2.float()}
+        # weight gradients as bf16 GEMMs (fp32 accumulation inside, bf16 results, as the reference's cuBLASLt backward)
+        g = {'rgb': (grad_outputs.t() @ v2).float()}
         g_v2 = grad_outputs @ w['rgb']
         relu_backward(g_v2, v2, bias_grads['view_2_bias'])
-        g['view_2'] = g_v2.t().float() @ v1.float()
+        g['view_2'] = (g_v2.t() @ v1).float()
         g_v1 = g_v2 @ w['view_2']
         relu_backward(g_v1, v1, bias_grads['view_1_bias'])
-        g['view_1'] = g_v1.t().float() @ v0.float()
+        g['view_1'] = (g_v1.t() @ v0).float()
         g_v0 = g_v1 @ w['view_1']
         relu_backward(g_v0, v0, no_bias)
-        g['combined'] = g_v0.t().float() @ inputs.float()
-        g['skip'] = grad_outputs.t().float() @ inputs.float()
+        g['combined'] = (g_v0.t() @ inputs).float()
+        g['skip'] = (grad_outputs.t() @ inputs).float()
         g_hidden = torch.addmm(grad_outputs @ w['skip'][:, :dw], g_v0, w['combined'][:, :dw])
         relu_backward(g_hidden, inputs[:, :dw], bias_grads['density_bias'])
-        g['density'] = g_hidden.t().float() @ features.float()
+        g['density'] = (g_hidden.t() @ features).float()
         g.update(bias_grads)
         with torch.enable_grad():
             p = params[:self.layout.numel].detach().float().requires_grad_()
@@ -289,6 +357,8 @@ class NerfMlp:
     def forward(self, features: torch.Tensor, inputs: torch.Tensor, packed: torch.Tensor, training: bool):
         for tensor, name in ((features, 'features'), (inputs, 'inputs'), (packed, 'packed')):
             self._check(tensor, name, torch.bfloat16)
+        if self.tensor_cores:
+            return self._forward_tc(features, inputs, packed, training)
         return self._forward(features, inputs, packed, training)
 
     def backward(self, grad_outputs, features, packed, context, params, grad_params) -> torch.Tensor:

@@ -11,10 +11,10 @@ of 10 levels x 4 features (base resolution 16, per-level scale 2, 2^21 entries),
 intervals per ray, the view-direction encoding of degree 4; the trainer's loss weights and Adam settings
 (Trainer.py:17-57). Data: a synthetic pool of 185 views of 1296 x 840 pixels (uniform-noise colors).
 
-Every kernel of the step is this backend's, except the NeRF MLP's GEMMs: they run as cuBLAS / cuBLASLt bf16 GEMMs
-through torch (the layer shapes of the reference's cuBLASLt chain, nerf_mlp.cu:440-455,503-620, with the forward's bias
-and ReLU in the GEMM epilogues and the backward's ReLU masks and bias gradients in this backend's relu_backward_), a
-stand-in of the same shape and cost, not the reference's numerics.
+The NeRF MLP is this backend's `NerfMlp` with the reference's interface and parameter layout (nerf_mlp.cu:440-620):
+`pack` every step, the forward on the tcgen05 kernel (zf_nerf_mlp_forward_tc, keeping v0-v2 for the backward), the
+backward as the folded chain's bf16 GEMMs (cuBLAS through torch) with this backend's ReLU backward and bias gradient
+and the unfold of the packed-weight gradients into the fp32 parameters.
 """
 from __future__ import annotations
 
@@ -50,76 +50,6 @@ def learning_rate(step: int) -> float:
 def grid_layout(n_levels: int):
     sizes = [16 * 2 ** level for level in range(n_levels)]
     return sizes, [min(s ** 3, 2 ** 21) for s in sizes]
-
-
-class NerfMlp:
-    """The NeRF MLP's layers as bf16 GEMMs (cuBLAS through torch): features [n, 56] -> hidden 64 (ReLU, bias) written
-    into the first 64 columns of the NeRF inputs [n, 96] (the featurizer wrote the encoded direction into the last 32);
-    inputs -> view 256 (ReLU; the bottleneck folded into the first view layer, as the reference packs it) -> 256 (ReLU,
-    bias) -> 256 (ReLU, bias) -> rgb; a skip projection of the inputs gives the raw density and the rgb skip rows.
-    Outputs [n, 8] bf16: raw density, 3 rgb logits, padding. Master parameters are one flat fp32 buffer (as the
-    reference's nerf_mlp_params), cast to bf16 once per step."""
-
-    SHAPES = [('density', (64, 56)), ('density_b', (64,)), ('combined', (256, 96)), ('skip', (8, 96)), ('view_1', (256, 256)), ('view_1_b', (256,)),
-              ('view_2', (256, 256)), ('view_2_b', (256,)), ('rgb', (8, 256))]
-
-    def __init__(self, device, generator: torch.Generator) -> None:
-        self.offsets = {}
-        n = 0
-        for name, shape in self.SHAPES:
-            self.offsets[name] = (n, shape)
-            n += math.prod(shape)
-        self.numel = (n + 3) // 4 * 4
-        self.params = torch.zeros(self.numel, device=device)
-        for name, shape in self.SHAPES:
-            if len(shape) == 2:
-                bound = math.sqrt(6.0 / shape[1])
-                self.view(self.params, name).uniform_(-bound, bound, generator=generator)
-        self.grads = torch.zeros_like(self.params)
-        self.zero_bias = torch.zeros(256, device=device, dtype=torch.bfloat16)
-
-    def view(self, buffer: torch.Tensor, name: str) -> torch.Tensor:
-        offset, shape = self.offsets[name]
-        return buffer[offset:offset + math.prod(shape)].view(shape)
-
-    def forward(self, features: torch.Tensor, inputs: torch.Tensor):
-        # bias + ReLU in the GEMM epilogue (cuBLASLt through torch), as the reference's RELU_BIAS epilogues
-        w = {name: self.view(self.params, name).to(torch.bfloat16) for name, _ in self.SHAPES}
-        inputs[:, :64] = torch._addmm_activation(w['density_b'], features, w['density'].t())
-        v0 = torch._addmm_activation(self.zero_bias, inputs, w['combined'].t())
-        outputs = inputs @ w['skip'].t()
-        v1 = torch._addmm_activation(w['view_1_b'], v0, w['view_1'].t())
-        v2 = torch._addmm_activation(w['view_2_b'], v1, w['view_2'].t())
-        outputs += v2 @ w['rgb'].t()
-        return outputs, (w, features, inputs, v0, v1, v2)
-
-    def backward(self, grad_outputs: torch.Tensor, context) -> torch.Tensor:
-        """Accumulates the parameter gradients (fp32) and returns the feature gradient [n, 56] bf16. The ReLU masks and
-        bias gradients take one pass per layer (relu_backward_, this backend's kernel for the reference's DRELU_BGRAD
-        epilogues)."""
-        import ZipNeRFCudaBackend as backend
-        w, features, inputs, v0, v1, v2 = context
-        g = self.grads
-        empty = g[:0]
-
-        def add(name, value):
-            self.view(g, name).add_(value.float())
-
-        add('rgb', grad_outputs.t() @ v2)
-        g_v2 = grad_outputs @ w['rgb']
-        backend.relu_backward_(g_v2, v2, self.view(g, 'view_2_b'))
-        add('view_2', g_v2.t() @ v1)
-        g_v1 = g_v2 @ w['view_2']
-        backend.relu_backward_(g_v1, v1, self.view(g, 'view_1_b'))
-        add('view_1', g_v1.t() @ v0)
-        g_v0 = g_v1 @ w['view_1']
-        backend.relu_backward_(g_v0, v0, empty)
-        add('combined', g_v0.t() @ inputs)
-        add('skip', grad_outputs.t() @ inputs)
-        g_hidden = torch.addmm(grad_outputs @ w['skip'][:, :64], g_v0, w['combined'][:, :64])
-        backend.relu_backward_(g_hidden, inputs[:, :64], self.view(g, 'density_b'))
-        add('density', g_hidden.t() @ features)
-        return g_hidden @ w['density']
 
 
 @dataclass
@@ -174,15 +104,21 @@ class TrainStep:
             w0.uniform_(-math.sqrt(6 / n_out), math.sqrt(6 / n_out), generator=g)
             w1.uniform_(-math.sqrt(6 / 64), math.sqrt(6 / 64), generator=g)
         self.prop_grads = torch.zeros_like(self.prop_params)
-        self.nerf_mlp = NerfMlp(device, g)
+        # the NeRF MLP: the reference's parameter table (nerf_mlp_parameters of the model's widths, Model.py:96-105),
+        # He-uniform over the fan-in columns, zero biases
+        self.nerf_mlp = backend.NerfMlp(GRID_LEVELS[2] * (GRID_FEATURES[2] + 1), MLP_WIDTH, 256, 256, DEGREE)
+        layout = self.nerf_mlp.layout
+        self.nerf_params = torch.zeros(layout.numel, device=device)
+        layout.initialize(self.nerf_params, g)
+        self.nerf_grads = torch.zeros_like(self.nerf_params)
         # the optimizer over the trainer's buffers (Trainer.py:44-57)
         nerf = self.levels[2]
         sizes, entries = grid_layout(GRID_LEVELS[2])
         n_fp32 = sum(1 for e in entries if e < 2 ** 20)
         split = nerf.featurizer.n_fp32_grad_rows * 4
         params = [self.levels[0].table.view(-1), self.levels[1].table.view(-1), nerf.table.view(-1)[:split], nerf.table.view(-1)[split:],
-                  self.prop_params, self.nerf_mlp.params]
-        grads = [self.levels[0].grad, self.levels[1].grad, nerf.grad, nerf.grad_half, self.prop_grads, self.nerf_mlp.grads]
+                  self.prop_params, self.nerf_params]
+        grads = [self.levels[0].grad, self.levels[1].grad, nerf.grad, nerf.grad_half, self.prop_grads, self.nerf_grads]
         scale = backend.nerf_grid_grad_scale
         offsets = [[int(o) for o in np.cumsum([0] + grid_layout(GRID_LEVELS[0])[1])], [int(o) for o in np.cumsum([0] + grid_layout(GRID_LEVELS[1])[1])],
                    [int(o) * 4 for o in np.cumsum([0] + entries[:n_fp32])], [int(o) * 4 for o in np.cumsum([0] + entries[n_fp32:])], [], []]
@@ -236,15 +172,16 @@ class TrainStep:
         inputs = torch.empty(R * n, 96, device=dev, dtype=torch.bfloat16)
         nerf.featurizer.forward(origins, directions, radii, tdist, seed, False, nerf.table, nerf.magnitudes, empty, empty, empty, empty, empty, empty,
                                 features, encoded, inputs)
-        outputs, context = self.nerf_mlp.forward(features, inputs)
+        packed = self.nerf_mlp.pack(self.nerf_params)
+        outputs, context = self.nerf_mlp.forward(features, inputs, packed, True)
         grad_outputs, proposal_grads, self.loss_sums = b.train_final(
             outputs.view(R, n, 8), sdist, tdist, [q['raw'] for q in proposals], [q['sdist'] for q in proposals], [q['tdist'] for q in proposals],
             [q['weights'] for q in proposals], directions, seed, rgb, LOSS['charbonnier_padding'], [LOSS['interlevel']] * 2, list(LOSS['blurs']),
             LOSS['distortion'], LOSS['distortion_power'], LOSS['distortion_premult'], True)
-        grad_features = self.nerf_mlp.backward(grad_outputs.view(R * n, 8), context)
+        grad_features = self.nerf_mlp.backward(grad_outputs.view(R * n, 8), features, packed, context, self.nerf_params, self.nerf_grads)
         nerf.featurizer.backward(origins, directions, radii, tdist, seed, grad_features, nerf.grad, nerf.grad_half)
         if after_backward is not None:
-            after_backward([nerf.grad, nerf.grad_half, self.nerf_mlp.grads])
+            after_backward([nerf.grad, nerf.grad_half, self.nerf_grads])
         for level in range(2):
             lv, q = self.levels[level], proposals[level]
             gw0, gb0, gw1, gb1 = self.proposal_mlp(self.prop_grads, level)

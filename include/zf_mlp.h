@@ -45,12 +45,15 @@ typedef struct zf_nerf_mlp_weights {
  * tcgen05 kernel (bf16 operands in shared memory, fp32 accumulators in tensor memory, 128-sample tiles, one CTA per
  * SM; each sample's outputs depend on its own row only): features [n, 56] bf16,
  * inputs [n, 96] bf16 (the direction block in columns 64-95 is read, the hidden layer written to columns 0-63),
- * outputs [n, 8] bf16 (raw density, 3 rgb logits, 4 zeros); row strides in elements, multiples of 8; status: a device
+ * outputs [n, 8] bf16 (raw density, 3 rgb logits, 4 zeros); activations: NULL (inference), or [3, n, 256] bf16 that
+ * receives the hidden view-layer activations v0, v1, v2 for the backward (the training forward, as NerfMlp::forward with
+ * training = true keeps them, nerf_mlp.cu:527-560); row strides in elements, multiples of 8; status: a device
  * int the kernel sets to 1 if one of its bounded waits ran out, which leaves this launch's outputs undefined (the
  * kernel still waits for its own copies and MMAs in flight and frees its tensor memory before it exits). Within bf16
  * rounding of the reference's cuBLASLt chain. */
 ZF_API int zf_nerf_mlp_forward_tc(const uint16_t* features, int64_t features_stride, uint16_t* inputs, int64_t inputs_stride,
-                                  const zf_nerf_mlp_weights* weights, uint16_t* outputs, int64_t n, int* status, struct CUstream_st* stream);
+                                  const zf_nerf_mlp_weights* weights, uint16_t* outputs, uint16_t* activations, int64_t n, int* status,
+                                  struct CUstream_st* stream);
 
 #ifdef __cplusplus
 }

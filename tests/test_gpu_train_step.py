@@ -14,7 +14,7 @@ def test_training_steps_run_and_update_the_model(cuda_device):
     from zipnerf_b200 import train_step
     step = train_step.TrainStep(cuda_device, n_rays=4096, pool_views=3)
     tables = [level.table.clone() for level in step.levels]
-    mlp = (step.prop_params.clone(), step.nerf_mlp.params.clone())
+    mlp = (step.prop_params.clone(), step.nerf_params.clone())
     magnitudes = step.magnitudes.clone()
     losses = []
     for iteration in range(3):
@@ -27,7 +27,8 @@ def test_training_steps_run_and_update_the_model(cuda_device):
             assert not buffer.any(), 'the Adam step zeroes every gradient buffer'
     for before, level in zip(tables, step.levels):
         assert torch.isfinite(level.table).all() and not torch.equal(before, level.table)
-    assert not torch.equal(mlp[0], step.prop_params) and not torch.equal(mlp[1], step.nerf_mlp.params)
+    assert not torch.equal(mlp[0], step.prop_params) and not torch.equal(mlp[1], step.nerf_params)
+    assert int(step.nerf_mlp.status(cuda_device).item()) == 0  # no wait of the tensor-core forward ran out
     assert torch.isfinite(step.magnitudes).all() and not torch.equal(magnitudes, step.magnitudes)
     assert float(step.optimizer.regularization()) > 0.0
     # the data term (charbonnier, per ray) is bounded by the colors' range

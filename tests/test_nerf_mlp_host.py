@@ -97,7 +97,7 @@ def test_packed_weights_have_the_kernel_shapes_and_padding():
     packed = {k: (v if k.endswith('_bias') else nm.row_major(v, nm.K_SLICE[k])) for k, v in stored.items()}
     folded = nm.fold(layout, params)
     for k, v in packed.items():
-        assert torch.equal(v, folded[k] if k.endswith('_bias') else folded[k].to(torch.bfloat16)), k
+        assert torch.equal(v, folded[k].to(torch.bfloat16).float() if k.endswith('_bias') else folded[k].to(torch.bfloat16)), k
     shapes = {'density': (64, 64), 'density_bias': (64,), 'combined': (256, 96), 'skip': (16, 96), 'view_1': (256, 256),
               'view_1_bias': (256,), 'view_2': (256, 256), 'view_2_bias': (256,), 'rgb': (16, 256)}
     assert {k: tuple(v.shape) for k, v in packed.items()} == shapes
