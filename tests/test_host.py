@@ -195,12 +195,15 @@ def test_nerf_mlp_forward_validates_before_touching_a_device():
     lib = capi.load()
     fake = 1 << 20  # 16-byte aligned, never dereferenced
     w = capi.zf_nerf_mlp_weights(*([fake] * 9))
-    assert lib.zf_nerf_mlp_forward_tc(fake, 56, fake, 96, ctypes.byref(w), fake, 0, fake, None) == capi.ZF_OK  # nothing to do
-    assert lib.zf_nerf_mlp_forward_tc(fake, 56, fake, 96, None, fake, 4, fake, None) == capi.ZF_ERROR_INVALID_ARGUMENT
+    assert lib.zf_nerf_mlp_forward_tc(fake, 56, fake, 96, ctypes.byref(w), fake, None, 0, fake, None) == capi.ZF_OK  # nothing to do
+    assert lib.zf_nerf_mlp_forward_tc(fake, 56, fake, 96, None, fake, None, 4, fake, None) == capi.ZF_ERROR_INVALID_ARGUMENT
     w.view_1 = fake + 8
-    assert lib.zf_nerf_mlp_forward_tc(fake, 56, fake, 96, ctypes.byref(w), fake, 4, fake, None) == capi.ZF_ERROR_INVALID_ARGUMENT
+    assert lib.zf_nerf_mlp_forward_tc(fake, 56, fake, 96, ctypes.byref(w), fake, None, 4, fake, None) == capi.ZF_ERROR_INVALID_ARGUMENT
     assert b'16-byte aligned' in lib.zf_last_error()
     w.view_1 = fake
+    # the training forward's activations buffer must be 16-byte aligned too
+    assert lib.zf_nerf_mlp_forward_tc(fake, 56, fake, 96, ctypes.byref(w), fake, fake + 2, 4, fake, None) == capi.ZF_ERROR_INVALID_ARGUMENT
+    assert b'activations' in lib.zf_last_error()
     for features_stride, inputs_stride in [(50, 96), (56, 90), (48, 96), (56, 88)]:
-        assert lib.zf_nerf_mlp_forward_tc(fake, features_stride, fake, inputs_stride, ctypes.byref(w), fake, 4, fake, None) == capi.ZF_ERROR_INVALID_ARGUMENT
+        assert lib.zf_nerf_mlp_forward_tc(fake, features_stride, fake, inputs_stride, ctypes.byref(w), fake, None, 4, fake, None) == capi.ZF_ERROR_INVALID_ARGUMENT
         assert b'row strides' in lib.zf_last_error()
