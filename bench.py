@@ -552,12 +552,19 @@ def run_b200(args) -> None:
             from zipnerf_b200 import sharding
             comm.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(comm):
-                sharding.allreduce_gradients(buffers)
+                sharding.allreduce_gradients(buffers, half_wire=args.half_wire)
+
+    tails = []
 
     def exchange():
-        # the step ends when every level's exchange has finished
+        # the step ends when every level's exchange has finished; the events around the wait give the exchange tail
+        # (the time the compute stream idles after its last backward)
         if world > 1:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
             torch.cuda.current_stream().wait_stream(comm)
+            b.record()
+            tails.append((a, b))
 
     def barrier():
         if world > 1:
@@ -588,6 +595,7 @@ def run_b200(args) -> None:
         elapsed_ms = t.item()
     ms_per_step = elapsed_ms / args.steps
     value = step.samples_per_step * world * args.steps / (elapsed_ms / 1e3) / 1e6
+    exchange_tail_ms = statistics.mean(a.elapsed_time(b) for a, b in tails[-args.steps:]) if tails else 0.0
     # per-kernel durations and the roofline of the dominant kernel
     kernel_ms: dict[str, list] = {}
     for i in range(args.steps):
@@ -617,6 +625,10 @@ def run_b200(args) -> None:
               'data': 'synthetic (seeded config 2 shapes; Mip-NeRF 360 unavailable)',
               'config': bench_config(args, world, step.samples_per_step),
               'roofline': roofline, 'kernels': kernels, 'gpu_launches': step.kernel_launches_per_step * args.steps, 'clocks': clocks.summary()}
+    if world > 1:
+        result['exchange'] = {'tail_ms_per_step': exchange_tail_ms, 'half_wire': args.half_wire,
+                              'collectives': 'one coalesced NCCL group per level: NeRF grid (fp32 + fp16 gradients), then each proposal level '
+                                             '(grid + MLP gradients), on a communication stream overlapping the later backwards'}
     if rank == 0 and world == 1 and not args.skip_reference_cuda:
         # baseline legs (test infrastructure, outside the product's timed regions): the reference's own CUDA kernels on
         # this step's inputs, and the config-5 contention case
@@ -850,11 +862,17 @@ def measure_train_step(args, world: int, rank: int, device, barrier, steps: int 
         if world > 1:
             comm.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(comm):
-                sharding.allreduce_gradients([b for b in buffers if b is not None])
+                sharding.allreduce_gradients([b for b in buffers if b is not None], half_wire=args.half_wire)
+
+    tails = []
 
     def exchange():
         if world > 1:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
             torch.cuda.current_stream().wait_stream(comm)
+            b.record()
+            tails.append((a, b))
 
     for i in range(args.warmup):
         step.run(i, after_backward=after_backward, exchange=exchange)
@@ -872,7 +890,8 @@ def measure_train_step(args, world: int, rank: int, device, barrier, steps: int 
         elapsed_ms = t.item()
     ms = elapsed_ms / steps
     losses = step.loss_sums.tolist()
-    return {'ms': ms, 'steps': steps, 'rays_per_s': world * args.rays / (ms * 1e-3), 'featurized_msamples_per_s': world * step.samples_per_step / (ms * 1e-3) / 1e6,
+    tail = statistics.mean(a.elapsed_time(b) for a, b in tails[-steps:]) if tails else 0.0
+    return {'ms': ms, 'steps': steps, 'exchange_tail_ms': tail, 'half_wire': args.half_wire, 'rays_per_s': world * args.rays / (ms * 1e-3), 'featurized_msamples_per_s': world * step.samples_per_step / (ms * 1e-3) / 1e6,
             'loss_sums_last_step': losses,
             'config': f'{args.rays} rays per GPU x (64 + 64 + 32) intervals; grids of the reference model (6 and 8 levels x 1 feature, 10 x 4, '
                       f'scale 2, 2^21); rays from a 185-view 1296 x 840 pool; gradient all-reduce over {world} GPU(s) and Adam; the NeRF MLP '
@@ -973,6 +992,8 @@ def main() -> None:
     parser.add_argument('--skip-contention', action='store_true', help='skip the config-5 contention timing')
     parser.add_argument('--skip-nerf-mlp', action='store_true', help='skip the timing of the NeRF MLP forward')
     parser.add_argument('--skip-render', action='store_true', help='skip the timing of the config-3 frame render')
+    parser.add_argument('--half-wire', choices=['fp16', 'fp32'], default='fp16',
+                        help='wire format of the NeRF grid\'s fp16 gradients in the all-reduce (fp16: pre-divided fp16 sums; fp32: fp32 copies)')
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps
     if args.impl == 'reference':

@@ -25,19 +25,41 @@ def sample_offset(ray_start: int, n_intervals: int) -> int:
     return ray_start * n_intervals
 
 
-def allreduce_gradients(buffers, group=None, average: bool = True) -> None:
-    """Sums (or averages) gradient buffers over the ranks in place. fp16 buffers (the NeRF grid's fine levels, scaled
-    by 2^20) are divided by the world size before the sum when averaging, so that the sum of large per-rank values
-    cannot overflow fp16; fp32 buffers are summed, then divided."""
+def allreduce_gradients(buffers, group=None, average: bool = True, half_wire: str = 'fp16') -> None:
+    """Sums (or averages) gradient buffers over the ranks in place; the buffers of one call go out as one NCCL group
+    (a single coalesced launch) on the NCCL backend. fp32 buffers are summed, then divided. fp16 buffers (the NeRF
+    grid's fine levels, scaled by 2^20) when averaging: half_wire 'fp16' divides them by the world size first and sums
+    in fp16 (the sum of large per-rank values cannot overflow; the partial sums round to fp16, so at 8 ranks a value
+    near 40,000 can come back one fp16 spacing low), 'fp32' sums fp32 copies (twice the bytes on the wire; exact to
+    fp32 before the final rounding)."""
     import torch.distributed as dist
+    if half_wire not in ('fp16', 'fp32'):
+        raise ValueError(f'half_wire must be fp16 or fp32, not {half_wire}')
     world = dist.get_world_size(group)
+    if world == 1 or not buffers:
+        return
+    wire, widened = [], []
     for buffer in buffers:
-        if world == 1:
-            continue
         if average and buffer.dtype == torch.float16:
-            buffer.div_(world)
-            dist.all_reduce(buffer, group=group)
-        else:
-            dist.all_reduce(buffer, group=group)
-            if average:
+            if half_wire == 'fp32':
+                wide = buffer.float()
+                widened.append((buffer, wide))
+                wire.append(wide)
+            else:
                 buffer.div_(world)
+                wire.append(buffer)
+        else:
+            wire.append(buffer)
+    if dist.get_backend(group) == 'nccl' and len(wire) > 1:
+        with dist._coalescing_manager(group, device=wire[0].device):
+            for t in wire:
+                dist.all_reduce(t, group=group)
+    else:
+        for t in wire:
+            dist.all_reduce(t, group=group)
+    if average:
+        for buffer in buffers:
+            if buffer.dtype != torch.float16:
+                buffer.div_(world)
+        for buffer, wide in widened:
+            buffer.copy_(wide.div_(world))

@@ -43,6 +43,9 @@ def _worker(rank: int, world: int, port: int, queue) -> None:
         half = torch.full((4,), 40000.0, dtype=torch.float16)
         single = torch.full((3,), float(rank + 1))
         sharding.allreduce_gradients([half, single])
+        # the fp32 wire for fp16 buffers: the average of equal values is exact
+        half_wide = torch.full((4,), 40000.0 + 32.0 * rank, dtype=torch.float16)
+        sharding.allreduce_gradients([half_wide], half_wire='fp32')
         # featurization gradients of this rank's ray shard with the CPU oracle
         import zf_testdata as td
         from oracle.zf_oracle import GridSpec, Oracle
@@ -55,7 +58,7 @@ def _worker(rank: int, world: int, port: int, queue) -> None:
         g32, g16 = Oracle().backward(grid, *rays, case['seed'], grad)
         g32 = torch.from_numpy(g32.copy())
         sharding.allreduce_gradients([g32], average=False)
-        queue.put((rank, half.tolist(), single.tolist(), g32.numpy()))
+        queue.put((rank, half.tolist(), single.tolist(), g32.numpy(), half_wide.tolist()))
     finally:
         dist.destroy_process_group()
 
@@ -79,7 +82,10 @@ def test_gradient_exchange(world):
     grid = GridSpec(case['level'], case['sizes'], case['entries'], 4, 0)
     full32, _ = Oracle().backward(grid, *(case[k] for k in ('origins', 'directions', 'radii', 'tdist')), case['seed'],
                                   np.ascontiguousarray(case['grad_features']))
-    for rank, half, single, g32 in results:
+    for rank, half, single, g32, half_wide in results:
+        # mean of 40000 + 32 k over k < world, rounded once to fp16 (spacing 32 there)
+        expected = float(torch.tensor(40000.0 + 32.0 * (world - 1) / 2).half())
+        assert half_wide == [expected] * 4, half_wide
         # no overflow; the collective's fp16 partial sums round (spacing 32 above 32768): within one spacing per add
         assert all(abs(h - 40000.0) <= 32.0 * (world - 1) for h in half), f'fp16 average overflowed or drifted: {half}'
         if world == 2:
