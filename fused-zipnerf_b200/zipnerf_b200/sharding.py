@@ -26,8 +26,8 @@ def sample_offset(ray_start: int, n_intervals: int) -> int:
 
 
 def allreduce_gradients(buffers, group=None, average: bool = True, half_wire: str = 'fp16') -> None:
-    """Sums (or averages) gradient buffers over the ranks in place; the buffers of one call go out as one NCCL group
-    (a single coalesced launch) on the NCCL backend. fp32 buffers are summed, then divided. fp16 buffers (the NeRF
+    """Sums (or averages) gradient buffers over the ranks in place; on the NCCL backend the buffers of one call and one
+    dtype go out as one coalesced collective (a single NCCL group). fp32 buffers are summed, then divided. fp16 buffers (the NeRF
     grid's fine levels, scaled by 2^20) when averaging: half_wire 'fp16' divides them by the world size first and sums
     in fp16 (the sum of large per-rank values cannot overflow; the partial sums round to fp16, so at 8 ranks a value
     near 40,000 can come back one fp16 spacing low), 'fp32' sums fp32 copies (twice the bytes on the wire; exact to
@@ -50,13 +50,19 @@ def allreduce_gradients(buffers, group=None, average: bool = True, half_wire: st
                 wire.append(buffer)
         else:
             wire.append(buffer)
-    if dist.get_backend(group) == 'nccl' and len(wire) > 1:
-        with dist._coalescing_manager(group, device=wire[0].device):
-            for t in wire:
+    # one coalesced collective per dtype (a coalesced all-reduce takes tensors of one type), in order of appearance
+    by_dtype: dict = {}
+    for t in wire:
+        by_dtype.setdefault(t.dtype, []).append(t)
+    coalesce = dist.get_backend(group) == 'nccl'  # gloo has no coalesced collectives
+    for tensors in by_dtype.values():
+        if coalesce and len(tensors) > 1:
+            with dist._coalescing_manager(group, device=tensors[0].device):
+                for t in tensors:
+                    dist.all_reduce(t, group=group)
+        else:
+            for t in tensors:
                 dist.all_reduce(t, group=group)
-    else:
-        for t in wire:
-            dist.all_reduce(t, group=group)
     if average:
         for buffer in buffers:
             if buffer.dtype != torch.float16:

@@ -43,9 +43,15 @@ def _worker(rank: int, world: int, port: int, queue) -> None:
         half = torch.full((4,), 40000.0, dtype=torch.float16)
         single = torch.full((3,), float(rank + 1))
         sharding.allreduce_gradients([half, single])
-        # the fp32 wire for fp16 buffers: the average of equal values is exact
+        # the fp32 wire for fp16 buffers: the average of equal values is exact; mixed with fp32 buffers, each dtype is
+        # one coalesced collective
         half_wide = torch.full((4,), 40000.0 + 32.0 * rank, dtype=torch.float16)
-        sharding.allreduce_gradients([half_wide], half_wire='fp32')
+        extra = [torch.full((5,), float(rank)), torch.full((2,), 2.0 * rank)]
+        sharding.allreduce_gradients([extra[0], half_wide, extra[1]], half_wire='fp32')
+        assert extra[0].tolist() == [(world - 1) / 2] * 5 and extra[1].tolist() == [float(world - 1)] * 2
+        mixed = [torch.full((3,), float(rank)), torch.full((4,), 100.0, dtype=torch.float16), torch.full((6,), 1.0)]
+        sharding.allreduce_gradients(mixed)
+        assert mixed[0].tolist() == [(world - 1) / 2] * 3 and mixed[1].tolist() == [100.0] * 4 and mixed[2].tolist() == [1.0] * 6
         # featurization gradients of this rank's ray shard with the CPU oracle
         import zf_testdata as td
         from oracle.zf_oracle import GridSpec, Oracle
