@@ -74,7 +74,7 @@ def build_library(jobs: int | None = None, force: bool = False, subset: set | No
     # the C ABI translation units: featurizer objects, the sampling kernels, the Adam step, the MLP's ReLU backward and
     # tensor-core forward
     abi_objects = []
-    for name in ['fz_capi', 'fz_sampling', 'fz_optim', 'fz_mlp', 'fz_nerf_mlp']:
+    for name in ['fz_capi', 'fz_sampling', 'fz_optim', 'fz_mlp', 'fz_nerf_mlp', 'fz_nerf_mlp_backward']:
         source, obj = CSRC / f'{name}.cu', BUILD / f'{name}.o'
         abi_objects.append(obj)
         if force or _stale(obj, [source, *deps]):

@@ -27,6 +27,7 @@
 // (K / 8) * 128 bytes apart (stride byte offset), K the operand's stored width (a weight slice: its own width).
 #include "zf_mlp.h"
 #include "fz_status.h"
+#include "fz_tcgen05.cuh"
 
 #include <cuda_runtime.h>
 
@@ -34,7 +35,6 @@
 
 namespace zf::nerf_mlp {
 
-constexpr int kTileRows = 128;       // M of every MMA: one accumulator row per tensor-memory lane
 constexpr int kFeatures = 56;        // NeRF features per sample: 10 levels x (4 + 1) = 50, padded to 56
 constexpr int kFeaturesK = 64;       // padded to the MMA K step of 16
 constexpr int kDensity = 64;         // density width = hidden columns of the inputs
@@ -42,7 +42,6 @@ constexpr int kInputs = 96;          // hidden 64 + direction block 32 (its last
 constexpr int kView = 256;
 constexpr int kOutputs = 8;          // raw density, 3 rgb logits, 4 padding
 constexpr int kOutputsN = 16;        // the smallest N of an M = 128 MMA
-constexpr int kMmaK = 16;            // K of one kind::f16 MMA
 
 // warp roles
 constexpr int kMmaWarp = 0;
@@ -63,10 +62,6 @@ constexpr int kThreads = 32 * (kFirstEpilogueWarp + kEpilogueWarps);
 
 constexpr uint32_t kTmemColumns = 512;   // two accumulator regions of 256 columns
 constexpr uint32_t kRegionColumns = 256;
-// bounded waits: a waiting thread is suspended in mbarrier.try_wait for up to kSuspendNs at a time (woken when the phase
-// completes), and gives up after kWaitNs in total; a layer takes microseconds
-constexpr uint32_t kSuspendNs = 20000;
-constexpr uint64_t kWaitNs = 2000000000ull;
 
 // weight stages: K-slices of 64 input columns (the combined layer's last slice 32), all output rows each
 constexpr int kSlice = 64;
@@ -111,175 +106,6 @@ struct PackedMlp {
     const float* view_2_bias;     // [256]
     const uint16_t* rgb;          // [16, 256]: rows 1-3 the rgb weights of v2, the others zero
 };
-
-enum Status : int { kOk = 0, kWaitTimeout = 1 };
-
-__device__ __forceinline__ uint32_t smem_address(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-
-// byte offset of element (row, k) of a K-major operand with k_total columns
-__host__ __device__ __forceinline__ uint32_t canonical_offset(const int row, const int k, const int k_total) {
-    return static_cast<uint32_t>(((row >> 3) * (k_total >> 3) + (k >> 3)) * 128 + (row & 7) * 16 + (k & 7) * 2);
-}
-
-// shared-memory matrix descriptor (tcgen05 format): start, leading and stride byte offsets in 16-byte units, version 1
-// in bits 46-47, base offset 0, no swizzle (layout type 0 in bits 61-63)
-__host__ __device__ __forceinline__ uint64_t smem_descriptor(const uint32_t address, const uint32_t leading_bytes, const uint32_t stride_bytes) {
-    uint64_t d = static_cast<uint64_t>((address & 0x3FFFFu) >> 4);
-    d |= static_cast<uint64_t>((leading_bytes >> 4) & 0x3FFFu) << 16;
-    d |= static_cast<uint64_t>((stride_bytes >> 4) & 0x3FFFu) << 32;
-    d |= static_cast<uint64_t>(1) << 46;
-    return d;
-}
-
-// instruction descriptor of kind::f16: fp32 accumulator (bits 4-5 = 1), bf16 A and B (bits 7-9, 10-12 = 1), both
-// K-major (bits 15, 16 = 0), N / 8 in bits 17-22, M / 16 in bits 24-28
-__host__ __device__ constexpr uint32_t instr_descriptor(const int m, const int n) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma(const uint32_t d_tmem, const uint64_t a, const uint64_t b, const uint32_t idesc, const uint32_t accumulate) {
-    asm volatile(
-        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
-}
-
-// D[128 x n] (+)= A[128 x k] B[n x k]^T from K-major operands stored with a_k_total and b_k_total columns, k / 16 MMAs
-__device__ __forceinline__ void mma_chain(const uint32_t d_tmem, const uint32_t a_address, const int a_k_total, const uint32_t b_address,
-                                          const int b_k_total, const int n, const int k, const bool accumulate) {
-    const uint32_t idesc = instr_descriptor(kTileRows, n);
-    const uint32_t a_stride = static_cast<uint32_t>(a_k_total >> 3) * 128, b_stride = static_cast<uint32_t>(b_k_total >> 3) * 128;
-    for (int s = 0; s < k / kMmaK; s++) {
-        // one K step covers two core matrices: start at chunk 2s, the second chunk one leading offset further
-        const uint32_t step = static_cast<uint32_t>(2 * s) * 128;
-        mma(d_tmem, smem_descriptor(a_address + step, 128, a_stride), smem_descriptor(b_address + step, 128, b_stride), idesc,
-            (accumulate || s > 0) ? 1u : 0u);
-    }
-}
-
-// the mbarrier tracks the completion of every tcgen05 operation this thread has issued so far
-__device__ __forceinline__ void commit(const uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-
-// whether the phase with the given parity has completed; the thread may be suspended (up to kSuspendNs) until it does
-__device__ __forceinline__ bool try_wait(const uint32_t bar, const uint32_t parity) {
-    uint32_t done;
-    asm volatile(
-        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(bar), "r"(parity), "r"(kSuspendNs)
-        : "memory");
-    return done != 0;
-}
-
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-// bounded wait for the completion of the phase with the given parity; false if the CTA's abort flag went up or the
-// time limit ran out (which raises the flag)
-__device__ __forceinline__ bool wait_phase(const uint32_t bar, const uint32_t parity, volatile int* abort) {
-    if (try_wait(bar, parity)) return true;
-    const uint64_t start = global_ns();
-    while (true) {
-        if (try_wait(bar, parity)) return true;
-        if (*abort) return false;
-        if (global_ns() - start > kWaitNs) break;
-    }
-    *abort = 1;
-    return false;
-}
-
-// bounded wait that ignores the abort flag (the teardown's wait for work already in flight)
-__device__ __forceinline__ void drain_phase(const uint32_t bar, const uint32_t parity) {
-    const uint64_t start = global_ns();
-    while (!try_wait(bar, parity) && global_ns() - start <= kWaitNs) {
-    }
-}
-
-__device__ __forceinline__ void arrive(const uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-// generic-proxy shared-memory writes become visible to the tensor cores' reads
-__device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// 32 consecutive fp32 accumulator columns of this thread's lane
-__device__ __forceinline__ void load_columns(const uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, "
-        "%19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]),
-          "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
-          "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
-          "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void load_columns8(const uint32_t taddr, float (&v)[8]) {
-    uint32_t r[8];
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ uint32_t pack_bf16x2(const float lo, const float hi) {
-    uint32_t out;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(out) : "f"(hi), "f"(lo));
-    return out;
-}
-
-// round to bf16 pairs with negative values (ReLU) set to zero
-__device__ __forceinline__ uint32_t pack_bf16x2_relu(const float lo, const float hi) {
-    uint32_t out;
-    asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(out) : "f"(hi), "f"(lo));
-    return out;
-}
-
-// the mbarrier expects `bytes` more bytes in its current phase (the arrival of its one thread)
-__device__ __forceinline__ void expect_bytes(const uint32_t bar, const uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-// one bulk copy (no multicast) of packed weights from global into shared memory, completing on the mbarrier; addresses
-// 16-byte aligned, bytes a multiple of 16
-__device__ __forceinline__ void bulk_copy(const uint32_t dst, const void* src, const uint32_t bytes, const uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst), "l"(src), "r"(bytes),
-                 "r"(bar)
-                 : "memory");
-}
-
-// tcgen05.ld of N (16 or 32) consecutive fp32 accumulator columns of this thread's lane into r (no wait)
-template <int N>
-__device__ __forceinline__ void issue_load(const uint32_t taddr, uint32_t* r) {
-    if constexpr (N == 16) {
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]),
-              "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-            : "r"(taddr));
-    }
-    else {
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, "
-            "%19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]),
-              "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
-              "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
-              "=r"(r[31])
-            : "r"(taddr));
-    }
-}
 
 // N accumulator columns of this thread's row (N = 16, or a multiple of 32 loaded 32 at a time with one wait) + bias
 // (shared memory, or none), ReLU, bf16, into row `row` of a K-major operand at column k_first (and into global memory

@@ -20,7 +20,7 @@ EXPORTED = ['zf_featurizer_create', 'zf_featurizer_destroy', 'zf_featurizer_n_ou
             'zf_check_erf_saturation', 'zf_erf_saturation_threshold', 'zf_last_error', 'zf_grid_max_value', 'zf_nerf_grid_grad_scale',
             'zf_direction_block_width', 'zf_initialize_rays', 'zf_view_rays', 'zf_generate_rays', 'zf_sample_uniforms',
             'zf_composite_and_resample', 'zf_train_final', 'zf_composite_final', 'zf_adam_create', 'zf_adam_destroy', 'zf_adam_step',
-            'zf_adam_state', 'zf_relu_backward_bf16', 'zf_nerf_mlp_forward_tc']
+            'zf_adam_state', 'zf_relu_backward_bf16', 'zf_nerf_mlp_forward_tc', 'zf_nerf_mlp_backward_workspace_size', 'zf_nerf_mlp_backward_tc']
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -104,6 +104,14 @@ class zf_nerf_mlp_weights(ctypes.Structure):
     _fields_ = [(name, _p) for name in ('density', 'density_bias', 'combined', 'skip', 'view_1', 'view_1_bias', 'view_2', 'view_2_bias', 'rgb')]
 
 
+class zf_nerf_mlp_weights_t(ctypes.Structure):
+    _fields_ = [(name, _p) for name in ('rgb_t', 'view_2_t', 'view_1_t', 'combined_t', 'skip_t', 'density_t')]
+
+
+class zf_nerf_mlp_grads(ctypes.Structure):
+    _fields_ = [(name, _p) for name in ('density', 'density_bias', 'combined', 'skip', 'view_1', 'view_1_bias', 'view_2', 'view_2_bias', 'rgb')]
+
+
 class ZfError(RuntimeError):
     def __init__(self, code: int, message: str) -> None:
         super().__init__(message)
@@ -180,6 +188,10 @@ def load() -> ctypes.CDLL:
     lib.zf_relu_backward_bf16.restype = ctypes.c_int
     lib.zf_nerf_mlp_forward_tc.argtypes = [_p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _p]
     lib.zf_nerf_mlp_forward_tc.restype = ctypes.c_int
+    lib.zf_nerf_mlp_backward_workspace_size.argtypes = [_i64]
+    lib.zf_nerf_mlp_backward_workspace_size.restype = _i64
+    lib.zf_nerf_mlp_backward_tc.argtypes = [_p, _p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _p, _i64, _i64, _p, _p]
+    lib.zf_nerf_mlp_backward_tc.restype = ctypes.c_int
     _lib = lib
     return lib
 
@@ -452,6 +464,57 @@ def nerf_mlp_forward_tc(features, inputs, packed: dict, outputs, status, activat
     w = zf_nerf_mlp_weights(*[packed[name].data_ptr() for name, _ in zf_nerf_mlp_weights._fields_])
     check(load().zf_nerf_mlp_forward_tc(_ptr(features), features.stride(0), _ptr(inputs), inputs.stride(0), ctypes.byref(w), _ptr(outputs),
                                         _ptr(activations), features.shape[0], _ptr(status), _stream(stream)))
+
+
+# shapes of the transposed packed weights (zf_nerf_mlp_weights_t) and of the packed-weight gradients (zf_nerf_mlp_grads)
+NERF_MLP_TRANSPOSED_SHAPES = {'rgb_t': (256, 16), 'view_2_t': (256, 256), 'view_1_t': (256, 256), 'combined_t': (96, 256), 'skip_t': (96, 16),
+                              'density_t': (64, 64)}
+NERF_MLP_GRAD_SHAPES = {'density': (64, 64), 'density_bias': (64,), 'combined': (256, 96), 'skip': (16, 96), 'view_1': (256, 256),
+                        'view_1_bias': (256,), 'view_2': (256, 256), 'view_2_bias': (256,), 'rgb': (16, 256)}
+
+
+def check_nerf_mlp_backward_tc(grad_outputs, features, inputs, activations, packed_t: dict, grad_features, grads: dict, workspace, status) -> None:
+    """Raises ValueError unless the tensors have the shapes, dtypes and layouts the tensor-core backward reads and
+    writes (its C ABI sees pointers and row strides only)."""
+    import torch
+
+    def cuda(t, dtype, what):
+        if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != dtype:
+            raise ValueError(f'{what} must be a {dtype} CUDA tensor')
+
+    n = features.shape[0] if isinstance(features, torch.Tensor) and features.dim() == 2 else -1
+    for t, width, what in ((grad_outputs, 8, 'grad_outputs'), (features, 56, 'features'), (inputs, 96, 'inputs'), (grad_features, 56, 'grad_features')):
+        cuda(t, torch.bfloat16, what)
+        if t.dim() != 2 or t.shape[0] != n or t.shape[1] < width or t.stride(1) != 1:
+            raise ValueError(f'{what} must be [{n}, >= {width}] with unit column stride')
+    if not grad_outputs.is_contiguous() or grad_outputs.shape[1] != 8:
+        raise ValueError('grad_outputs must be a contiguous [n, 8] tensor')
+    cuda(activations, torch.bfloat16, 'activations')
+    if tuple(activations.shape) != (3, n, 256) or not activations.is_contiguous():
+        raise ValueError(f'activations must be a contiguous [3, {n}, 256] tensor')
+    for name, shape in NERF_MLP_TRANSPOSED_SHAPES.items():
+        t = packed_t.get(name)
+        cuda(t, torch.bfloat16, f'packed_t[{name!r}]')
+        if tuple(t.shape) != shape or not t.is_contiguous():
+            raise ValueError(f'packed_t[{name!r}] must be a contiguous {shape} tensor')
+    for name, shape in NERF_MLP_GRAD_SHAPES.items():
+        t = grads.get(name)
+        cuda(t, torch.float32, f'grads[{name!r}]')
+        if tuple(t.shape) != shape or not t.is_contiguous():
+            raise ValueError(f'grads[{name!r}] must be a contiguous {shape} tensor')
+    cuda(status, torch.int32, 'status')
+    if not isinstance(workspace, torch.Tensor) or not workspace.is_cuda or workspace.numel() * workspace.element_size() < load().zf_nerf_mlp_backward_workspace_size(n):
+        raise ValueError('workspace must be a CUDA tensor of zf_nerf_mlp_backward_workspace_size(n) bytes')
+
+
+def nerf_mlp_backward_tc(grad_outputs, features, inputs, activations, packed_t: dict, grad_features, grads: dict, workspace, status, stream=None) -> None:
+    """zf_nerf_mlp_backward_tc on PyTorch CUDA tensors (checked first: check_nerf_mlp_backward_tc)."""
+    check_nerf_mlp_backward_tc(grad_outputs, features, inputs, activations, packed_t, grad_features, grads, workspace, status)
+    w = zf_nerf_mlp_weights_t(*[packed_t[name].data_ptr() for name, _ in zf_nerf_mlp_weights_t._fields_])
+    g = zf_nerf_mlp_grads(*[grads[name].data_ptr() for name, _ in zf_nerf_mlp_grads._fields_])
+    check(load().zf_nerf_mlp_backward_tc(_ptr(grad_outputs), _ptr(features), features.stride(0), _ptr(inputs), inputs.stride(0), _ptr(activations),
+                                         ctypes.byref(w), _ptr(grad_features), grad_features.stride(0), ctypes.byref(g), _ptr(workspace),
+                                         workspace.numel() * workspace.element_size(), features.shape[0], _ptr(status), _stream(stream)))
 
 
 class CAdam:

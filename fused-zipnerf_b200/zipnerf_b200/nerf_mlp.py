@@ -193,6 +193,24 @@ def pack(layout: NerfMlpLayout, params: torch.Tensor) -> dict:
     return pack_folded(fold(layout, params))
 
 
+# the transposed weights of the backward's data-gradient chain (B operands [inputs x outputs] of dX = dY W), their
+# K-slice widths over the outputs, and their stored shapes
+K_SLICE_T = {'rgb_t': 16, 'view_2_t': 64, 'view_1_t': 64, 'combined_t': 64, 'skip_t': 16, 'density_t': 64}
+TRANSPOSED_OF = {'rgb_t': 'rgb', 'view_2_t': 'view_2', 'view_1_t': 'view_1', 'combined_t': 'combined', 'skip_t': 'skip', 'density_t': 'density'}
+
+
+def pack_transposed(folded: dict) -> dict:
+    """The folded weights transposed ([inputs x outputs]: rgb_t [256, 16], view_2_t / view_1_t [256, 256], combined_t
+    [96, 256], skip_t [96, 16], density_t [64, 64]), rounded to bf16 and stored as the backward kernel streams them
+    (`sliced_order` with the K-slices of K_SLICE_T): the B operands of zf_nerf_mlp_backward_tc."""
+    out = {}
+    for name, source in TRANSPOSED_OF.items():
+        t = folded[source].t().contiguous()
+        order = _device_order(*t.shape, K_SLICE_T[name], t.device)
+        out[name] = t.to(torch.bfloat16).reshape(-1)[order].view(t.shape).contiguous()
+    return out
+
+
 def folded_forward(packed: dict, features: torch.Tensor, direction_block: torch.Tensor) -> torch.Tensor:
     """The packed network's layer chain as the kernel runs it (in the packed tensors' dtype, fp32 accumulation when
     they are fp32): [n, 8] outputs. The hidden layer h is the first columns of the inputs [h | direction block]."""
@@ -209,6 +227,15 @@ def folded_forward(packed: dict, features: torch.Tensor, direction_block: torch.
 
 
 PACKED_ORDER = ('density', 'density_bias', 'combined', 'skip', 'view_1', 'view_1_bias', 'view_2', 'view_2_bias', 'rgb')
+TRANSPOSED_ORDER = tuple(K_SLICE_T)
+
+
+def _weight_grad(grad: torch.Tensor, activation: torch.Tensor) -> torch.Tensor:
+    """grad^T activation of bf16 operands in fp32 (the reference's weight gradients are fp32 GEMM outputs,
+    nerf_mlp.cu:581-582)."""
+    if grad.is_cuda:
+        return torch.mm(grad.t(), activation, out_dtype=torch.float32)
+    return grad.t().float() @ activation.float()
 
 
 class NerfMlp:
@@ -238,10 +265,16 @@ class NerfMlp:
         self.tensor_cores = (self.layout.n_features == 56 and density_width == 64 and view_width == 256 and self.layout.n_inputs == 96)
         self._tc_shapes, self._tc_offsets = {}, {}
         if self.tensor_cores:
-            self._tc_shapes = {name: tuple(t.shape) for name, t in fold(self.layout, torch.zeros(self.layout.numel)).items()}
+            folded = fold(self.layout, torch.zeros(self.layout.numel))
+            self._tc_shapes = {name: tuple(t.shape) for name, t in folded.items()}
             for name in PACKED_ORDER:
                 self._tc_offsets[name] = n
                 n += math.prod(self._tc_shapes[name]) * (2 if name.endswith('_bias') else 1)  # fp32 biases: two bf16 slots
+            # the transposed weights of the tensor-core backward
+            for name in TRANSPOSED_ORDER:
+                self._tc_shapes[name] = tuple(reversed(self._tc_shapes[TRANSPOSED_OF[name]]))
+                self._tc_offsets[name] = n
+                n += math.prod(self._tc_shapes[name])
         self.packed_size = n
         self._status = {}
 
@@ -272,15 +305,17 @@ class NerfMlp:
         parts = [folded[name][tuple(slice(0, d) for d in self._shapes[name])].reshape(-1).to(torch.bfloat16) for name in PACKED_ORDER]
         tc = pack_folded(folded)
         parts += [tc[name].reshape(-1).view(torch.bfloat16) if name.endswith('_bias') else tc[name].reshape(-1) for name in PACKED_ORDER]
+        transposed = pack_transposed(folded)
+        parts += [transposed[name].reshape(-1) for name in TRANSPOSED_ORDER]
         return torch.cat(parts)
 
     def _weights(self, packed: torch.Tensor) -> dict:
         return {name: packed[self._offsets[name]:self._offsets[name] + math.prod(self._shapes[name])].view(self._shapes[name]) for name in PACKED_ORDER}
 
-    def _tc_weights(self, packed: torch.Tensor) -> dict:
-        """Views of the tensor-core section: bf16 weights in the kernel's order, fp32 biases."""
+    def _tc_weights(self, packed: torch.Tensor, names=PACKED_ORDER) -> dict:
+        """Views of the tensor-core section: bf16 weights in the kernels' order, fp32 biases."""
         out = {}
-        for name in PACKED_ORDER:
+        for name in names:
             a, shape = self._tc_offsets[name], self._tc_shapes[name]
             if name.endswith('_bias'):
                 out[name] = packed[a:a + 2 * math.prod(shape)].view(torch.float32)
@@ -327,21 +362,20 @@ class NerfMlp:
         dw = self.layout.density_width
         bias_grads = {name: torch.zeros(self._shapes[name], device=packed.device) for name in ('density_bias', 'view_1_bias', 'view_2_bias')}
         no_bias = bias_grads['density_bias'][:0]
-        # weight gradients as bf16 GEMMs (fp32 accumulation inside, bf16 results, as the reference's cuBLASLt backward)
-        g = {'rgb': (grad_outputs.t() @ v2).float()}
+        g = {'rgb': _weight_grad(grad_outputs, v2)}
         g_v2 = grad_outputs @ w['rgb']
         relu_backward(g_v2, v2, bias_grads['view_2_bias'])
-        g['view_2'] = (g_v2.t() @ v1).float()
+        g['view_2'] = _weight_grad(g_v2, v1)
         g_v1 = g_v2 @ w['view_2']
         relu_backward(g_v1, v1, bias_grads['view_1_bias'])
-        g['view_1'] = (g_v1.t() @ v0).float()
+        g['view_1'] = _weight_grad(g_v1, v0)
         g_v0 = g_v1 @ w['view_1']
         relu_backward(g_v0, v0, no_bias)
-        g['combined'] = (g_v0.t() @ inputs).float()
-        g['skip'] = (grad_outputs.t() @ inputs).float()
+        g['combined'] = _weight_grad(g_v0, inputs)
+        g['skip'] = _weight_grad(grad_outputs, inputs)
         g_hidden = torch.addmm(grad_outputs @ w['skip'][:, :dw], g_v0, w['combined'][:, :dw])
         relu_backward(g_hidden, inputs[:, :dw], bias_grads['density_bias'])
-        g['density'] = (g_hidden.t() @ features).float()
+        g['density'] = _weight_grad(g_hidden, features)
         g.update(bias_grads)
         with torch.enable_grad():
             p = params[:self.layout.numel].detach().float().requires_grad_()
@@ -361,8 +395,34 @@ class NerfMlp:
             return self._forward_tc(features, inputs, packed, training)
         return self._forward(features, inputs, packed, training)
 
+    def _backward_tc(self, grad_outputs, features, packed, context, params, grad_params) -> torch.Tensor:
+        """The backward on the tensor cores (zf_nerf_mlp_backward_tc: the data-gradient chain and the packed-weight
+        gradients in fp32), then the unfold of the packed-weight gradients into the parameters by autograd of the fold."""
+        from zipnerf_b200 import capi
+        if len(context) != 4 or packed.numel() != self.packed_size:
+            raise RuntimeError('ZipNeRF: invalid nerf mlp backward inputs')
+        inputs, base = context[0], context[1]
+        # the training forward's activations: one [3, n, 256] buffer whose planes are v0, v1, v2
+        activations = base.as_strided((3,) + tuple(base.shape), (base.numel(),) + tuple(base.stride()))
+        if activations[2].data_ptr() != context[3].data_ptr() or activations[1].data_ptr() != context[2].data_ptr():
+            raise RuntimeError('ZipNeRF: nerf mlp backward needs the context of the tensor-core forward')
+        n = features.shape[0]
+        grad_features = torch.empty(n, self.n_features, dtype=torch.bfloat16, device=features.device)
+        grads = {name: torch.zeros(shape, device=features.device) for name, shape in capi.NERF_MLP_GRAD_SHAPES.items()}
+        workspace = torch.empty(max(capi.load().zf_nerf_mlp_backward_workspace_size(n), 16), dtype=torch.uint8, device=features.device)
+        capi.nerf_mlp_backward_tc(grad_outputs, features, inputs, activations, self._tc_weights(packed, TRANSPOSED_ORDER), grad_features, grads,
+                                  workspace, self.status(features.device))
+        with torch.enable_grad():
+            p = params[:self.layout.numel].detach().float().requires_grad_()
+            folded = fold(self.layout, p)
+            (grad,) = torch.autograd.grad([folded[name] for name in PACKED_ORDER], p, [grads[name] for name in PACKED_ORDER])
+        grad_params[:self.layout.numel] += grad.to(grad_params.dtype)
+        return grad_features
+
     def backward(self, grad_outputs, features, packed, context, params, grad_params) -> torch.Tensor:
         import ZipNeRFCudaBackend as backend
         self._check(params, 'params', torch.float32)
         self._check(grad_params, 'grad_params', torch.float32)
+        if self.tensor_cores:
+            return self._backward_tc(grad_outputs, features, packed, context, params, grad_params)
         return self._backward(grad_outputs, features, packed, context, params, grad_params, backend.relu_backward_)

@@ -55,6 +55,49 @@ ZF_API int zf_nerf_mlp_forward_tc(const uint16_t* features, int64_t features_str
                                   const zf_nerf_mlp_weights* weights, uint16_t* outputs, uint16_t* activations, int64_t n, int* status,
                                   struct CUstream_st* stream);
 
+/* Transposed packed NeRF MLP weights of zf_nerf_mlp_backward_tc ([inputs x outputs], the B operands of the data
+ * gradients dX = dY W): bf16, stored as consecutive K-slices of the outputs (16 for rgb_t and skip_t, 64 for the others)
+ * in the no-swizzle K-major order; zipnerf_b200.nerf_mlp.pack_transposed writes them. All 16-byte aligned. */
+typedef struct zf_nerf_mlp_weights_t {
+    const uint16_t* rgb_t;         /* [256, 16] */
+    const uint16_t* view_2_t;      /* [256, 256] */
+    const uint16_t* view_1_t;      /* [256, 256] */
+    const uint16_t* combined_t;    /* [96, 256] */
+    const uint16_t* skip_t;        /* [96, 16] */
+    const uint16_t* density_t;     /* [64, 64] */
+} zf_nerf_mlp_weights_t;
+
+/* fp32 gradients of the packed weights (row-major, the shapes of zf_nerf_mlp_weights), accumulated (+=): density
+ * [64, 64] (the first 56 columns), density_bias [64], combined [256, 96], skip [16, 96] (rows 0-7), view_1 and view_2
+ * [256, 256], view_1_bias and view_2_bias [256], rgb [16, 256] (rows 0-7). */
+typedef struct zf_nerf_mlp_grads {
+    float* density;
+    float* density_bias;
+    float* combined;
+    float* skip;
+    float* view_1;
+    float* view_1_bias;
+    float* view_2;
+    float* view_2_bias;
+    float* rgb;
+} zf_nerf_mlp_grads;
+
+/* Bytes of the backward's workspace for n samples (the masked gradients g_v0, g_v1, g_v2 and g_h in bf16); no
+ * counterpart in the reference, whose NerfMlp::backward allocates its intermediates itself (nerf_mlp.cu:575-582). */
+ZF_API int64_t zf_nerf_mlp_backward_workspace_size(int64_t n);
+
+/* The backward of NerfMlp::backward (nerf_mlp.cu:565-620) on the tcgen05 tensor cores, for the reference model's widths:
+ * grad_outputs [n, 8] bf16 (columns 4-7 zero), features [n, 56] and inputs [n, 96] bf16 of the forward (h in columns
+ * 0-63), activations [3, n, 256] bf16 (v0, v1, v2 kept by the training forward), weights_t the transposed packed
+ * weights; grad_features [n, 56] bf16 out; grads += the gradients of the packed weights (their unfold into the
+ * reference's parameters is the caller's); workspace of zf_nerf_mlp_backward_workspace_size(n) bytes. Two kernels: the
+ * data-gradient chain of each 128-sample tile (masked by the activations' ReLU), then the weight gradients as
+ * split-K GEMMs over the samples with fp32 atomics. status: as zf_nerf_mlp_forward_tc. */
+ZF_API int zf_nerf_mlp_backward_tc(const uint16_t* grad_outputs, const uint16_t* features, int64_t features_stride, const uint16_t* inputs,
+                                   int64_t inputs_stride, const uint16_t* activations, const zf_nerf_mlp_weights_t* weights_t,
+                                   uint16_t* grad_features, int64_t grad_features_stride, const zf_nerf_mlp_grads* grads, void* workspace,
+                                   int64_t workspace_bytes, int64_t n, int* status, struct CUstream_st* stream);
+
 #ifdef __cplusplus
 }
 #endif

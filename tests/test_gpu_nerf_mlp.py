@@ -148,3 +148,46 @@ def test_tensor_core_forward_rows_are_independent_of_the_batch(cuda_device):
     assert torch.equal(whole.view(torch.int16), again.view(torch.int16))
     assert torch.equal(part.view(torch.int16), whole[:m].view(torch.int16))
     assert torch.equal(part_inputs.view(torch.int16), inputs[:m].view(torch.int16))
+
+
+@pytest.mark.parametrize('n', [4133, 57_003])
+def test_tensor_core_backward_matches_the_gemm_chain(cuda_device, n):
+    """NerfMlp.backward on the tensor cores (zf_nerf_mlp_backward_tc: the data-gradient kernel, then the weight-gradient
+    GEMMs over the samples) against the same folded chain as bf16 GEMMs through torch (`_backward`, fp32 weight
+    gradients) on the same forward context: feature and parameter gradients within 1e-2 relative (bf16 intermediate
+    gradients, other summation orders), and no timed-out wait. n = 57,003 gives every CTA several tiles and a ragged
+    last tile."""
+    import ZipNeRFCudaBackend as backend
+    from zipnerf_b200 import nerf_mlp as nm
+    layout = nm.NerfMlpLayout()
+    gen = torch.Generator().manual_seed(n)
+    params = torch.zeros(layout.numel)
+    layout.initialize(params, gen)
+    for name, _, fan_in in layout.parameters:
+        if fan_in == 0:
+            layout.view(params, name).uniform_(-0.3, 0.3, generator=gen)
+    features = torch.zeros(n, 56)
+    features[:, :50] = torch.randn(n, 50, generator=gen)
+    inputs = torch.zeros(n, 96)
+    inputs[:, 64:91] = torch.rand(n, 27, generator=gen) * 2 - 1
+    inputs[:, 95] = 1.0
+    grad_outputs = torch.zeros(n, 8)
+    grad_outputs[:, :4] = torch.randn(n, 4, generator=gen)
+    params, features = params.to(cuda_device), features.bfloat16().to(cuda_device)
+    inputs, grad_outputs = inputs.bfloat16().to(cuda_device), grad_outputs.bfloat16().to(cuda_device)
+    mlp = backend.NerfMlp(50, 64, 256, 256, 4)
+    packed = mlp.pack(params)
+    _, context = mlp.forward(features, inputs, packed, True)
+    grad_tc, grad_chain = torch.zeros_like(params), torch.zeros_like(params)
+    features_tc = mlp.backward(grad_outputs, features, packed, context, params, grad_tc)
+    features_chain = mlp._backward(grad_outputs, features, packed, [t.clone() for t in context], params, grad_chain, backend.relu_backward_)
+    torch.cuda.synchronize()
+    assert int(mlp.status(cuda_device).item()) == 0
+
+    def rel(a, b):
+        return ((a.float() - b.float()).norm() / b.float().norm()).item()
+
+    errors = {name: rel(layout.view(grad_tc, name), layout.view(grad_chain, name)) for name, _, _ in layout.parameters
+              if layout.view(grad_chain, name).abs().max() > 0}
+    errors['features'] = rel(features_tc, features_chain)
+    assert max(errors.values()) < 1e-2, errors

@@ -117,9 +117,10 @@ def test_packed_weights_have_the_kernel_shapes_and_padding():
 
 
 @pytest.mark.skipif(shutil.which('nvcc') is None, reason='nvcc is not on PATH')
-def test_tensor_core_forward_compiles_for_sm100a(tmp_path):
+@pytest.mark.parametrize('source', ['fz_nerf_mlp.cu', 'fz_nerf_mlp_backward.cu'])
+def test_tensor_core_kernels_compile_for_sm100a(tmp_path, source):
     run = subprocess.run(['nvcc', '-gencode', 'arch=compute_100a,code=sm_100a', '-O3', '--use_fast_math', '-std=c++17', '-Xptxas', '-v', '-c',
-                          '-I', str(REPO / 'include'), str(REPO / 'fused-zipnerf_b200' / 'csrc' / 'fz_nerf_mlp.cu'), '-o', str(tmp_path / 'fz_nerf_mlp.o')],
+                          '-I', str(REPO / 'include'), str(REPO / 'fused-zipnerf_b200' / 'csrc' / source), '-o', str(tmp_path / 'kernel.o')],
                          capture_output=True, text=True, timeout=300)
     assert run.returncode == 0, run.stderr[-2000:]
     spills = re.findall(r'(\d+) bytes spill stores, (\d+) bytes spill loads', run.stderr)
@@ -291,6 +292,55 @@ def test_tensor_core_descriptors_match_cutlass(tmp_path):
     source = tmp_path / 'check.cu'
     source.write_text(DESCRIPTOR_CHECK)
     binary = tmp_path / 'check'
+    build = subprocess.run(['nvcc', '-std=c++17', '-gencode', 'arch=compute_100a,code=sm_100a', '-I', str(_cutlass_include()),
+                            '-I', str(REPO / 'fused-zipnerf_b200' / 'csrc'), '-I', str(REPO / 'include'), str(source), '-o', str(binary)],
+                           capture_output=True, text=True, timeout=300)
+    assert build.returncode == 0, build.stderr[-3000:]
+    run = subprocess.run([str(binary)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0 and '0 mismatches' in run.stdout, run.stdout
+
+
+MN_DESCRIPTOR_CHECK = r"""
+#include <cstdio>
+#include <cute/tensor.hpp>
+#include <cute/atom/mma_traits_sm100.hpp>
+#include "fz_tcgen05.cuh"
+using namespace cute;
+// the backward's weight-gradient tiles: a [rows (K) x width (MN)] bf16 tile in the canonical order, element (k, m) at
+// ((k / 8) (width / 8) + m / 8) 64 + (k % 8) 8 + m % 8, read as an MN-major operand
+template <int Width, int Rows> int check_mn() {
+    auto layout = make_layout(make_shape(make_shape(Int<8>{}, Int<Width / 8>{}), make_shape(Int<8>{}, Int<Rows / 8>{})),
+                              make_stride(make_stride(Int<1>{}, Int<64>{}), make_stride(Int<8>{}, Int<Width / 8 * 64>{})));
+    auto tensor = make_tensor(make_smem_ptr(reinterpret_cast<bfloat16_t*>(uintptr_t(0))), layout);
+    const uint64_t theirs = uint64_t(UMMA::make_umma_desc<UMMA::Major::MN>(tensor)) & ~uint64_t(0x3FFF);  // start address: device only
+    const uint64_t ours = zf::nerf_mlp::smem_descriptor(0, Width / 8 * 128, 128);
+    if (theirs != ours) std::printf("MN width %d: cute %llx ours %llx\n", Width, (unsigned long long)theirs, (unsigned long long)ours);
+    return theirs != ours;
+}
+template <int N> int check_instr_mn() {
+    const uint32_t theirs = uint32_t(UMMA::make_instr_desc<bfloat16_t, bfloat16_t, float, 128, N, UMMA::Major::MN, UMMA::Major::MN>());
+    const uint32_t ours = zf::nerf_mlp::instr_descriptor(128, N, true, true);
+    if (theirs != ours) std::printf("instr MN N=%d: cute %08x ours %08x\n", N, theirs, ours);
+    return theirs != ours;
+}
+int main() {
+    int bad = check_mn<256, 64>() + check_mn<128, 64>() + check_mn<16, 64>() + check_mn<96, 64>() + check_mn<64, 64>();
+    bad += check_instr_mn<16>() + check_instr_mn<64>() + check_instr_mn<96>() + check_instr_mn<256>();
+    std::printf("%d mismatches\n", bad);
+    return bad;
+}
+"""
+
+
+@pytest.mark.skipif(shutil.which('nvcc') is None or _cutlass_include() is None, reason='nvcc or the CUTLASS headers are absent')
+def test_weight_gradient_descriptors_match_cutlass(tmp_path):
+    """The backward's weight-gradient GEMMs read their operands MN-major (the samples are K): the shared-memory
+    descriptors of those tiles (leading byte offset = the K-atom stride, stride byte offset = 128) and the MN-major
+    instruction descriptors equal the ones CuTe builds for the same layouts (make_umma_desc<Major::MN>,
+    make_instr_desc with Major::MN)."""
+    source = tmp_path / 'check_mn.cu'
+    source.write_text(MN_DESCRIPTOR_CHECK)
+    binary = tmp_path / 'check_mn'
     build = subprocess.run(['nvcc', '-std=c++17', '-gencode', 'arch=compute_100a,code=sm_100a', '-I', str(_cutlass_include()),
                             '-I', str(REPO / 'fused-zipnerf_b200' / 'csrc'), '-I', str(REPO / 'include'), str(source), '-o', str(binary)],
                            capture_output=True, text=True, timeout=300)
