@@ -20,6 +20,9 @@
 #include "fz_status.h"
 #include "fz_tcgen05.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 namespace zf::nerf_mlp {
 
 namespace bwd {
@@ -78,8 +81,8 @@ struct DataArgs {
     const uint16_t* activations;    // [3, n, 256]: v0, v1, v2
     uint16_t* grad_activations;     // [3, n, 256] out: g_v0, g_v1, g_v2
     uint16_t* grad_hidden;          // [n, 64] out: g_h
-    uint16_t* grad_features;        // [n, features_stride] out: columns 0-55
-    int64_t features_stride;
+    uint16_t* grad_features;        // [n, grad_features_stride] out: columns 0-55
+    int64_t grad_features_stride;
     int64_t n;
 };
 
@@ -97,35 +100,42 @@ __device__ __forceinline__ Stage weight_stage(const PackedMlpT& w, const int s) 
     return {w.density_t, kDensity * kDensity * 2};
 }
 
-// N (32 or 64) accumulator columns of this thread's row, times the ReLU mask of mask_row (bf16 values > 0; none: no
-// mask), rounded to bf16, into row `row` of a K-major operand at column k_first (when dst is given) and into global
-// memory at out_row + k_first (its first out_cols columns, when out_row is given)
+// this thread's mask words (8 bf16 values each) of N columns from k_first of mask_row (zeros without a row)
 template <int N>
-__device__ __forceinline__ void masked_columns(const uint32_t taddr, const uint16_t* mask_row, uint8_t* dst, const int row, const int k_total,
-                                               const int k_first, uint16_t* out_row, const int out_cols) {
-    uint32_t r[N];
-    #pragma unroll
-    for (int c = 0; c < N; c += 32) issue_load<32>(taddr + c, r + c);
-    uint4 m[N / 8];
+__device__ __forceinline__ void fetch_mask(const uint16_t* mask_row, const int k_first, uint4 (&m)[N / 8]) {
     #pragma unroll
     for (int j = 0; j < N / 8; j++) m[j] = mask_row != nullptr ? __ldg(reinterpret_cast<const uint4*>(mask_row + k_first) + j) : make_uint4(0, 0, 0, 0);
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// N (32 or 64) accumulator columns of this thread's row, times the ReLU mask m (bf16 values > 0, fetched by
+// fetch_mask; none when masked is false), rounded to bf16, into row `row` of a K-major operand at column k_first (when
+// dst is given) and into global memory at out_row + k_first (its first out_cols columns, when out_row is given)
+template <int N>
+__device__ __forceinline__ void masked_columns(const uint32_t taddr, const bool masked, const uint4 (&m)[N / 8], uint8_t* dst, const int row,
+                                               const int k_total, const int k_first, uint16_t* out_row, const int out_cols) {
+    // 32 columns per TMEM load: the mask words of the layer after this one are held meanwhile
     #pragma unroll
-    for (int j = 0; j < N / 8; j++) {
-        const uint32_t mw[4] = {m[j].x, m[j].y, m[j].z, m[j].w};
-        uint32_t words[4];
+    for (int c = 0; c < N; c += 32) {
+        uint32_t r[32];
+        issue_load<32>(taddr + c, r);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            float lo = __uint_as_float(r[8 * j + 2 * q]), hi = __uint_as_float(r[8 * j + 2 * q + 1]);
-            if (mask_row != nullptr) {
-                if (!(__uint_as_float(mw[q] << 16) > 0.0f)) lo = 0.0f;
-                if (!(__uint_as_float(mw[q] & 0xFFFF0000u) > 0.0f)) hi = 0.0f;
+        for (int j = c / 8; j < c / 8 + 4; j++) {
+            const uint32_t mw[4] = {m[j].x, m[j].y, m[j].z, m[j].w};
+            uint32_t words[4];
+            #pragma unroll
+            for (int q = 0; q < 4; q++) {
+                float lo = __uint_as_float(r[8 * (j - c / 8) + 2 * q]), hi = __uint_as_float(r[8 * (j - c / 8) + 2 * q + 1]);
+                if (masked) {
+                    if (!(__uint_as_float(mw[q] << 16) > 0.0f)) lo = 0.0f;
+                    if (!(__uint_as_float(mw[q] & 0xFFFF0000u) > 0.0f)) hi = 0.0f;
+                }
+                words[q] = pack_bf16x2(lo, hi);
             }
-            words[q] = pack_bf16x2(lo, hi);
+            const uint4 out = make_uint4(words[0], words[1], words[2], words[3]);
+            if (dst != nullptr) *reinterpret_cast<uint4*>(dst + canonical_offset(row, k_first + 8 * j, k_total)) = out;
+            if (out_row != nullptr && 8 * j < out_cols) *reinterpret_cast<uint4*>(out_row + k_first + 8 * j) = out;
         }
-        const uint4 out = make_uint4(words[0], words[1], words[2], words[3]);
-        if (dst != nullptr) *reinterpret_cast<uint4*>(dst + canonical_offset(row, k_first + 8 * j, k_total)) = out;
-        if (out_row != nullptr && 8 * j < out_cols) *reinterpret_cast<uint4*>(out_row + k_first + 8 * j) = out;
     }
 }
 
@@ -293,41 +303,57 @@ __global__ void __launch_bounds__(kThreads, 1) fz_nerf_mlp_backward_data_kernel(
         auto store_gout = [&](const uint4 v) {
             if (tid < kTileRows) *reinterpret_cast<uint4*>(gout + canonical_offset(tid, 0, kGoutK)) = v;
         };
+        // the mask words of the next epilogue are fetched while the layer before it runs: v2, v1, v0 for chunks g and
+        // g + 2, then h for columns [32 g, 32 g + 32)
+        uint4 masks[2][kSlice / 8];
+        uint4 hidden_mask[4];
+        auto fetch_layer_masks = [&](const int index, const int64_t s) {
+            #pragma unroll
+            for (int i = 0; i < 2; i++) {
+                fetch_mask<kSlice>(s < n ? a.activations + (static_cast<int64_t>(index) * n + s) * kView : nullptr, kSlice * (g + 2 * i), masks[i]);
+            }
+        };
         int64_t tile = blockIdx.x;
         uint4 next = make_uint4(0, 0, 0, 0);
         if (tile < n_tiles) {
             store_gout(fetch_gout(tile));
             publish(in_bar);
+            fetch_layer_masks(2, tile * kTileRows + row);
         }
         for (; tile < n_tiles && ok; tile += gridDim.x) {
             const int64_t sample = tile * kTileRows + row;
             const bool valid = sample < n;
             const bool more = tile + gridDim.x < n_tiles;
             // E0-E2: g_v2, g_v1, g_v0 masked by v2, v1, v0: chunks g and g + 2 -> act and global memory
-            for (int k = 0; k < 3 && ok; k++) {
+            #pragma unroll
+            for (int k = 0; k < 3; k++) {
                 if (!(ok = accumulator_ready())) break;
                 const int index = 2 - k;  // v2, v1, v0
-                const uint16_t* mask = valid ? a.activations + (static_cast<int64_t>(index) * n + sample) * kView : nullptr;
                 uint16_t* out = valid ? a.grad_activations + (static_cast<int64_t>(index) * n + sample) * kView : nullptr;
                 const uint32_t region = lanes + (layer & 1u) * kRegionColumns;
-                for (int j = g; j < kChunks; j += 2) {
-                    masked_columns<kSlice>(region + kSlice * j, mask, act, row, kView, kSlice * j, out, kSlice);
+                #pragma unroll
+                for (int i = 0; i < 2; i++) {
+                    const int j = g + 2 * i;
+                    masked_columns<kSlice>(region + kSlice * j, true, masks[i], act, row, kView, kSlice * j, out, kSlice);
                     publish(chunk_bar(j));
                 }
                 layer++;
+                if (k < 2) fetch_layer_masks(index - 1, sample);
+                else fetch_mask<32>(valid ? a.inputs + sample * a.inputs_stride : nullptr, 32 * g, hidden_mask);
                 if (k == 0 && more) next = fetch_gout(tile + gridDim.x);
             }
             if (!ok) break;
             // E3: g_h = g_in[:, 0:64] masked by h: columns [32 g, 32 g + 32) -> the g_h tile and global memory
             if (!(ok = accumulator_ready())) break;
-            masked_columns<32>(lanes + (layer & 1u) * kRegionColumns + 32 * g, valid ? a.inputs + sample * a.inputs_stride : nullptr, gh, row, kDensity,
-                               32 * g, valid ? a.grad_hidden + sample * kDensity : nullptr, 32);
+            masked_columns<32>(lanes + (layer & 1u) * kRegionColumns + 32 * g, true, hidden_mask, gh, row, kDensity, 32 * g,
+                               valid ? a.grad_hidden + sample * kDensity : nullptr, 32);
             publish(h_bar);
             layer++;
+            if (more) fetch_layer_masks(2, (tile + gridDim.x) * kTileRows + row);
             // E4: g_features, columns [32 g, 32 g + 32) below 56, then the next tile's output gradients
             if (!(ok = accumulator_ready())) break;
-            masked_columns<32>(lanes + (layer & 1u) * kRegionColumns + 32 * g, nullptr, nullptr, row, 0, 32 * g,
-                               valid ? a.grad_features + sample * a.features_stride : nullptr, kFeatures - 32 * g);
+            masked_columns<32>(lanes + (layer & 1u) * kRegionColumns + 32 * g, false, hidden_mask, nullptr, row, 0, 32 * g,
+                               valid ? a.grad_features + sample * a.grad_features_stride : nullptr, kFeatures - 32 * g);
             layer++;
             if (more) {
                 store_gout(next);
@@ -357,23 +383,36 @@ __global__ void __launch_bounds__(kThreads, 1) fz_nerf_mlp_backward_data_kernel(
 // ---------------------------------------------------------------------------------------------------------------------
 // weight gradients: dW[m][k] += sum over samples s of G[s][m] V[s][k], bias[m] += sum over s of G[s][m]
 
-constexpr int kWgradThreads = 256;
-constexpr int kKTile = 64;           // samples per K-tile (4 MMA K steps)
-constexpr int kWgradStages = 3;
+// Persistent CTAs over K-tiles of 32 samples. Warp 0 (one lane) loads each K-tile's G and V with TMA tensor copies
+// (no multicast) into a six-slot ring: operands of 64 or more columns as 64-column boxes with the 128-byte swizzle,
+// the 8-column output gradients as one 16-column box with the 32-byte swizzle, columns past the matrix and rows past n
+// zero-filled. Warp 1 (one lane) issues the MN-major MMAs into tensor memory (two M = 128 halves for m_pad = 256).
+// Warps 2-9 sum the bias columns from the same slots, then move the accumulators to dW with vector fp32 atomics.
+constexpr int kWgradWarps = 10;
+constexpr int kWgradThreads = 32 * kWgradWarps;
+constexpr int kWgradFirstSumWarp = 2;
+constexpr int kKTile = 32;           // samples per K-tile (2 MMA K steps)
+constexpr int kWgradStages = 6;
 constexpr int kWgradMaxM = 256;      // two M = 128 halves
 constexpr int kWgradMaxN = 256;
-constexpr int kWgradStageBytes = kKTile * (kWgradMaxM + kWgradMaxN) * 2;  // 64 KB
-constexpr int kWgradBarOffset = kWgradStages * kWgradStageBytes;
-constexpr int kWgradSmemBytes = kWgradBarOffset + 8 * (kWgradStages + 1) + 16;
+constexpr int kBoxCols = 64;         // columns of a 128-byte-swizzled box
+constexpr int kBoxBytes = kKTile * kBoxCols * 2;     // 4 KB: the MN-atom stride of a tile
+constexpr int kNarrowCols = 16;      // columns of the 32-byte-swizzled box (the output gradients)
+constexpr int kNarrowBytes = kKTile * kNarrowCols * 2;
+constexpr int kWgradStageBytes = kKTile * (kWgradMaxM + kWgradMaxN) * 2;  // 32 KB
+constexpr int kWgradSumOffset = kWgradStages * kWgradStageBytes;           // 8 x 256 fp32 partial bias sums
+constexpr int kWgradBarOffset = kWgradSumOffset + 8 * kWgradMaxM * 4;
+constexpr int kWgradBars = 2 * kWgradStages + 1;                           // full[stages], empty[stages], done
+constexpr int kWgradSmemBytes = 1024 + kWgradBarOffset + 8 * kWgradBars + 16;  // 1024: alignment of the swizzled ring
 static_assert(kWgradSmemBytes <= 227 * 1024, "one CTA per SM");
 
 struct WeightArgs {
-    const uint16_t* g;          // [n, g_stride]: the first m_cols columns are G
-    int64_t g_stride;
-    int m_cols;                 // <= 256
-    const uint16_t* v;          // [n, v_stride]: the first k_cols columns are V
-    int64_t v_stride;
-    int k_cols;                 // <= 256
+    CUtensorMap g_map;          // G [n, m_cols] bf16, 64-column boxes of kKTile rows, 128-byte swizzle
+    CUtensorMap v_map;          // V [n, k_cols] bf16, 64-column boxes (128-byte swizzle) or one 16-column box (32-byte)
+    int m_pad;                  // 128 or 256 (G boxes: m_pad / 64)
+    int k_pad;                  // 16 (one narrow box), 64, 128 or 256 (V boxes: k_pad / 64)
+    int m_cols;                 // <= m_pad
+    int k_cols;                 // <= k_pad
     int64_t n;
     float* dw;                  // dW[m][k] at dw[m * dw_m_stride + k * dw_k_stride] (+=)
     int64_t dw_m_stride;
@@ -381,59 +420,50 @@ struct WeightArgs {
     float* bias;                // bias[m] (+=), or null
 };
 
-// the 16-byte copies of one K-tile of G (m_pad columns) and V (k_pad columns) into a stage, canonical order with
-// the samples as rows; columns and samples past the end are zero-filled
-__device__ __forceinline__ void load_wgrad_tile(const WeightArgs& a, const int m_pad, const int k_pad, const int64_t first, const uint32_t stage_address,
-                                                const int tid) {
-    const int gm = m_pad / 8, vk = k_pad / 8;
-    const int words = kKTile * (gm + vk);
-    for (int q = tid; q < words; q += kWgradThreads) {
-        const bool is_g = q < kKTile * gm;
-        const int local = is_g ? q : q - kKTile * gm;
-        const int per_row = is_g ? gm : vk;
-        const int r = local / per_row, c = local % per_row;
-        const int64_t s = first + r;
-        const int cols = is_g ? a.m_cols : a.k_cols;
-        const bool inside = s < a.n && 8 * c < cols;
-        const uint16_t* src = (is_g ? a.g + (inside ? s : 0) * a.g_stride : a.v + (inside ? s : 0) * a.v_stride) + (inside ? 8 * c : 0);
-        const uint32_t dst = stage_address + (is_g ? 0u : static_cast<uint32_t>(kKTile * m_pad * 2)) + canonical_offset(r, 8 * c, per_row * 8);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(inside ? 16 : 0) : "memory");
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+__device__ __forceinline__ void tma_load_2d(const uint32_t dst, const CUtensorMap* map, const int x, const int y, const uint32_t bar) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+                 : "memory");
 }
 
-// D[128 x n] (+)= A[128 x 16 k-steps] B[n x ...]^T with A and B MN-major: the stored rows are the K dimension (samples)
-// and the 16 bytes of a core-matrix row run along M or N; MN-adjacent core matrices 128 bytes apart, K-adjacent ones
-// (width / 8) * 128 bytes apart
-__device__ __forceinline__ void mma_chain_mn(const uint32_t d_tmem, const uint32_t a_address, const int a_width, const uint32_t b_address,
-                                             const int b_width, const int n, const int k, const bool accumulate) {
-    const uint32_t idesc = instr_descriptor(kTileRows, n, true, true);
-    const uint32_t a_k = static_cast<uint32_t>(a_width >> 3) * 128, b_k = static_cast<uint32_t>(b_width >> 3) * 128;
-    for (int s = 0; s < k / kMmaK; s++) {
-        // one K step of 16 samples covers two K-adjacent core matrices
-        mma(d_tmem, smem_descriptor(a_address + 2 * s * a_k, a_k, 128), smem_descriptor(b_address + 2 * s * b_k, b_k, 128), idesc,
-            (accumulate || s > 0) ? 1u : 0u);
-    }
+__device__ __forceinline__ void red_add_v4(float* address, const float a, const float b, const float c, const float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(address), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
+__device__ __forceinline__ uint64_t wgrad_descriptor(const uint32_t address, const bool narrow) {
+    return narrow ? mn_sw32_descriptor(address) : mn_sw128_descriptor(address, kKTile);
 }
 
 __global__ void __launch_bounds__(kWgradThreads, 1) fz_nerf_mlp_backward_weight_kernel(const __grid_constant__ WeightArgs a, int* status) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWgradBarOffset);  // mma_done[stages], drain
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kWgradBarOffset + 8 * (kWgradStages + 1));
-    volatile int* abort = reinterpret_cast<volatile int*>(smem + kWgradBarOffset + 8 * (kWgradStages + 1) + 4);
-    const uint32_t bar0 = smem_address(bars);
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // the swizzle patterns follow shared-memory address bits: the ring starts on a 1024-byte boundary
+    uint8_t* smem = smem_raw + ((1024u - (smem_address(smem_raw) & 1023u)) & 1023u);
     const uint32_t base = smem_address(smem);
+    const uint32_t bar0 = base + kWgradBarOffset;
+    auto full_bar = [&](const uint32_t i) { return bar0 + 8u * i; };
+    auto empty_bar = [&](const uint32_t i) { return bar0 + 8u * (kWgradStages + i); };
+    const uint32_t done_bar = bar0 + 8u * (2 * kWgradStages);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kWgradBarOffset + 8 * kWgradBars);
+    volatile int* abort = reinterpret_cast<volatile int*>(smem + kWgradBarOffset + 8 * kWgradBars + 4);
+    float* partial = reinterpret_cast<float*>(smem + kWgradSumOffset);
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-    const int m_halves = a.m_cols > 128 ? 2 : 1;
-    const int m_pad = 128 * m_halves;
-    const int k_pad = (a.k_cols + 15) / 16 * 16;
+    const bool narrow = a.k_pad < kBoxCols;
+    const int m_halves = a.m_pad / 128;
+    const int g_boxes = a.m_pad / kBoxCols, v_boxes = narrow ? 1 : a.k_pad / kBoxCols;
+    const uint32_t g_bytes = static_cast<uint32_t>(g_boxes * kBoxBytes);
+    const uint32_t stage_bytes = g_bytes + static_cast<uint32_t>(narrow ? kNarrowBytes : v_boxes * kBoxBytes);
     const int64_t n_tiles = (a.n + kKTile - 1) / kKTile;
+    const int my_tiles = blockIdx.x < n_tiles ? static_cast<int>((n_tiles - 1 - blockIdx.x) / gridDim.x + 1) : 0;
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_address(tmem_slot)), "r"(512));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     if (tid == 32) {
-        for (int s = 0; s <= kWgradStages; s++) asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar0 + 8u * s), "r"(1));
+        for (int i = 0; i < kWgradStages; i++) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(full_bar(i)), "r"(1));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(empty_bar(i)), "r"(1 + kWgradWarps - kWgradFirstSumWarp));
+        }
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(done_bar), "r"(1));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         *abort = 0;
     }
@@ -441,96 +471,156 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fz_nerf_mlp_backward_weight_
     __syncthreads();
     fence_after_sync();
     const uint32_t tmem = *tmem_slot;
-    float column_sum = 0.0f;  // this thread's column of G (tid < m_cols), over this CTA's samples
-    // prologue: the first stages in flight
-    int64_t tile = blockIdx.x;
-    for (int s = 0; s < kWgradStages - 1; s++) {
-        if (tile + s * gridDim.x < n_tiles) load_wgrad_tile(a, m_pad, k_pad, (tile + s * gridDim.x) * kKTile, base + s * kWgradStageBytes, tid);
-        else asm volatile("cp.async.commit_group;" ::: "memory");
-    }
-    uint32_t step = 0;
-    bool ok = true;
-    uint32_t mma_phase[kWgradStages] = {0, 0, 0};
-    for (; tile < n_tiles; tile += gridDim.x, step++) {
-        const uint32_t slot = step % kWgradStages;
-        // the stage that the next load reuses must have been read by its MMAs (issued kWgradStages - 1 steps ago)
-        const int64_t ahead = tile + (kWgradStages - 1) * static_cast<int64_t>(gridDim.x);
-        const uint32_t ahead_slot = (step + kWgradStages - 1) % kWgradStages;
-        if (step >= 1 && ahead < n_tiles) {
-            const bool done = __syncthreads_and(wait_phase(bar0 + 8u * ahead_slot, mma_phase[ahead_slot] & 1u, abort));
-            mma_phase[ahead_slot]++;
-            if (!done) {
-                ok = false;
-                break;
+    if (warp == 0) {
+        // TMA producer
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a.g_map)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a.v_map)) : "memory");
+            int issued = 0;
+            for (int i = 0; i < my_tiles; i++) {
+                const uint32_t slot = i % kWgradStages;
+                if (i >= kWgradStages && !wait_phase(empty_bar(slot), (i / kWgradStages - 1) & 1u, abort)) break;
+                const int y = static_cast<int>((blockIdx.x + static_cast<int64_t>(i) * gridDim.x) * kKTile);
+                const uint32_t stage = base + slot * kWgradStageBytes;
+                expect_bytes(full_bar(slot), stage_bytes);
+                for (int b = 0; b < g_boxes; b++) tma_load_2d(stage + b * kBoxBytes, &a.g_map, b * kBoxCols, y, full_bar(slot));
+                for (int b = 0; b < v_boxes; b++) tma_load_2d(stage + g_bytes + b * kBoxBytes, &a.v_map, b * kBoxCols, y, full_bar(slot));
+                issued = i + 1;
             }
+            // every copy issued has landed before the CTA's shared memory can go to another CTA
+            for (int i = issued > kWgradStages ? issued - kWgradStages : 0; i < issued; i++) drain_phase(full_bar(i % kWgradStages), (i / kWgradStages) & 1u);
         }
-        if (ahead < n_tiles) load_wgrad_tile(a, m_pad, k_pad, ahead * kKTile, base + ahead_slot * kWgradStageBytes, tid);
-        else asm volatile("cp.async.commit_group;" ::: "memory");
-        // this step's stage has landed (all but the newest kWgradStages - 1 groups are complete)
-        asm volatile("cp.async.wait_group %0;" ::"n"(kWgradStages - 1) : "memory");
-        fence_async_shared();
-        __syncthreads();
-        const uint32_t stage = base + slot * kWgradStageBytes;
-        if (tid == 0) {
-            fence_after_sync();
-            const uint32_t b = stage + kKTile * m_pad * 2;
-            for (int h = 0; h < m_halves; h++) {
-                // M-half h of G: its 16 MN core-matrix columns start 16 * 128 bytes further along M
-                mma_chain_mn(tmem + h * k_pad, stage + h * 16 * 128, m_pad, b, k_pad, k_pad, kKTile, step > 0);
+    } else if (warp == 1) {
+        // MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = instr_descriptor(kTileRows, a.k_pad, true, true);
+            for (int i = 0; i < my_tiles; i++) {
+                const uint32_t slot = i % kWgradStages;
+                if (!wait_phase(full_bar(slot), (i / kWgradStages) & 1u, abort)) break;
+                fence_after_sync();
+                const uint32_t stage = base + slot * kWgradStageBytes;
+                for (int h = 0; h < m_halves; h++) {
+                    for (int k = 0; k < kKTile / kMmaK; k++) {
+                        // M-half h: two 64-column atoms further; K step k: two 8-row groups further
+                        const uint32_t a_addr = stage + h * 2 * kBoxBytes + k * 2 * 1024;
+                        const uint32_t b_addr = stage + g_bytes + k * 2 * (narrow ? 256 : 1024);
+                        mma(tmem + h * a.k_pad, wgrad_descriptor(a_addr, false), wgrad_descriptor(b_addr, narrow), idesc, (i > 0 || k > 0) ? 1u : 0u);
+                    }
+                }
+                commit(empty_bar(slot));
             }
-            commit(bar0 + 8u * slot);
+            commit(done_bar);
         }
-        // the bias gradient: this thread's column of the K-tile
-        if (a.bias != nullptr && tid < a.m_cols) {
-            const uint8_t* g_tile = smem + slot * kWgradStageBytes;
-            #pragma unroll 8
-            for (int r = 0; r < kKTile; r++) {
-                const uint16_t bits = *reinterpret_cast<const uint16_t*>(g_tile + canonical_offset(r, tid, m_pad));
-                column_sum += __uint_as_float(static_cast<uint32_t>(bits) << 16);
+    } else {
+        // bias sums: warp w' = warp - 2 takes rows w' + 8 j of each K-tile, lane l the 8 columns of word l (box l / 8,
+        // 16-byte chunk l % 8, stored at chunk (l % 8) ^ w' of its 128-byte row)
+        const int wp = warp - kWgradFirstSumWarp;
+        const bool sums = a.bias != nullptr && 8 * lane < a.m_cols;
+        float column_sum[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        const uint32_t read_offset = (lane / 8) * kBoxBytes + wp * 128 + (((lane % 8) ^ wp) << 4);
+        bool ok = true;
+        for (int i = 0; i < my_tiles; i++) {
+            const uint32_t slot = i % kWgradStages;
+            if (!(ok = wait_phase(full_bar(slot), (i / kWgradStages) & 1u, abort))) break;
+            if (sums) {
+                const uint8_t* tile = smem + slot * kWgradStageBytes + read_offset;
+                #pragma unroll
+                for (int j = 0; j < kKTile / 8; j++) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(tile + j * 1024);
+                    const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+                    #pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        column_sum[2 * q] += __uint_as_float(words[q] << 16);
+                        column_sum[2 * q + 1] += __uint_as_float(words[q] & 0xFFFF0000u);
+                    }
+                }
             }
+            __syncwarp();
+            if (lane == 0) arrive(empty_bar(slot));
         }
-    }
-    // every MMA of this CTA is done, then the accumulators go to dW with fp32 atomics (rows of M-half h: warps
-    // 4h .. 4h + 3, tensor-memory lane quadrant warp % 4)
-    fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {
-        commit(bar0 + 8u * kWgradStages);
-        drain_phase(bar0 + 8u * kWgradStages, 0);
-    }
-    fence_before_sync();
-    __syncthreads();
-    fence_after_sync();
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    if (ok && step > 0) {
-        const int h = warp / 4;
-        const int m = 128 * h + 32 * (warp % 4) + lane;
-        if (h < m_halves) {
-            const uint32_t lanes = tmem + (static_cast<uint32_t>(32 * (warp % 4)) << 16) + h * k_pad;
-            for (int c = 0; c < k_pad; c += 16) {
+        // every MMA is done: the accumulators go to dW (rows 128 h + 32 (warp % 4) + lane; with two M-halves warp pair
+        // p = w' / 4 takes half p, with one both pairs take alternate 16-column chunks)
+        ok = ok && (my_tiles == 0 || wait_phase(done_bar, 0, abort));
+        ok = __all_sync(0xFFFFFFFFu, ok);  // the tensor-memory loads below are warp-collective
+        fence_after_sync();
+        const int pair = wp / 4, quadrant = warp % 4;
+        const int h = m_halves == 2 ? pair : 0;
+        const int m = 128 * h + 32 * quadrant + lane;
+        const bool vector = a.dw_k_stride == 1 && (a.dw_m_stride & 3) == 0 && (reinterpret_cast<uintptr_t>(a.dw) & 15) == 0;
+        if (ok && my_tiles > 0) {
+            const uint32_t lanes = tmem + (static_cast<uint32_t>(32 * quadrant) << 16) + h * a.k_pad;
+            for (int c = (m_halves == 2 ? 0 : 16 * pair); c < a.k_pad; c += (m_halves == 2 ? 16 : 32)) {
                 uint32_t r[16];
                 issue_load<16>(lanes + c, r);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 if (m < a.m_cols) {
+                    float* row = a.dw + m * a.dw_m_stride;
                     #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        const float value = __uint_as_float(r[j]);
-                        if (c + j < a.k_cols && value != 0.0f) atomicAdd(a.dw + m * a.dw_m_stride + (c + j) * a.dw_k_stride, value);
+                    for (int j = 0; j < 16; j += 4) {
+                        if (vector && c + j + 4 <= a.k_cols) {
+                            red_add_v4(row + c + j, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+                        } else {
+                            #pragma unroll
+                            for (int e = 0; e < 4; e++) {
+                                if (c + j + e < a.k_cols) atomicAdd(row + (c + j + e) * a.dw_k_stride, __uint_as_float(r[j + e]));
+                            }
+                        }
                     }
                 }
             }
         }
-        if (a.bias != nullptr && tid < a.m_cols && column_sum != 0.0f) atomicAdd(a.bias + tid, column_sum);
+        // the bias: the 8 row phases' partial sums through shared memory, one atomic per column
+        if (a.bias != nullptr) {
+            #pragma unroll
+            for (int e = 0; e < 8; e++) partial[wp * kWgradMaxM + 8 * lane + e] = column_sum[e];
+            asm volatile("bar.sync 1, %0;" ::"n"(32 * (kWgradWarps - kWgradFirstSumWarp)) : "memory");
+            const int column = tid - 32 * kWgradFirstSumWarp;
+            if (ok && my_tiles > 0 && column < a.m_cols) {
+                float total = 0.0f;
+                #pragma unroll
+                for (int w = 0; w < kWgradWarps - kWgradFirstSumWarp; w++) total += partial[w * kWgradMaxM + column];
+                atomicAdd(a.bias + column, total);
+            }
+        }
     }
-    if (tid == 0 && (*abort || !ok)) atomicExch(status, kWaitTimeout);
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    if (tid == 32 && my_tiles > 0) drain_phase(done_bar, 0);  // no MMA still writes the tensor memory freed below
+    if (tid == 0 && *abort) atomicExch(status, kWaitTimeout);
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
 }
 
-// launches of one backward: the data-gradient kernel, then the weight gradients of every packed weight
-cudaError_t launch_backward(const PackedMlpT& w, const DataArgs& d, const zf_nerf_mlp_grads& grads, const uint16_t* features, int* status,
+// cuTensorMapEncodeTiled from the driver through the runtime (the library links no driver library)
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess) p = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+// the tensor map of a [n, cols] bf16 matrix with row stride `stride` elements, boxes of kKTile rows and 64 (128-byte
+// swizzle) or 16 (32-byte swizzle) columns
+bool encode_operand(CUtensorMap* map, const uint16_t* base, const int cols, const int64_t stride, const int64_t n, const bool narrow) {
+    const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (encode == nullptr) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(n)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride) * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(narrow ? kNarrowCols : kBoxCols), static_cast<cuuint32_t>(kKTile)};
+    const cuuint32_t element_strides[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(base), dims, strides, box, element_strides,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, narrow ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t launch_backward(const PackedMlpT& w, const DataArgs& d, const zf_nerf_mlp_grads& grads, const uint16_t* features,
+                            const int64_t features_stride, int* status,
                             cudaStream_t stream) {
     int device = 0, n_sms = 0;
     cudaError_t e = cudaGetDevice(&device);
@@ -551,18 +641,43 @@ cudaError_t launch_backward(const PackedMlpT& w, const DataArgs& d, const zf_ner
     const uint16_t* v0 = d.activations;
     const uint16_t* v1 = d.activations + n * kView;
     const uint16_t* v2 = d.activations + 2 * n * kView;
-    const WeightArgs launches[] = {
-        // view_2: g_v2^T v1 (+ bias), view_1: g_v1^T v0 (+ bias), combined: g_v0^T inputs (its bias in the bias lane)
-        {g_v2, kView, kView, v1, kView, kView, n, grads.view_2, kView, 1, grads.view_2_bias},
-        {g_v1, kView, kView, v0, kView, kView, n, grads.view_1, kView, 1, grads.view_1_bias},
-        {g_v0, kView, kView, d.inputs, d.inputs_stride, kInputs, n, grads.combined, kInputs, 1, nullptr},
-        // density: g_h^T features (+ bias)
-        {d.grad_hidden, kDensity, kDensity, features, d.features_stride, kFeatures, n, grads.density, kDensity, 1, grads.density_bias},
-        // rgb and skip, transposed (their 8 output rows as N): v2^T g_out into rgb[o][i], inputs^T g_out into skip[o][i]
-        {v2, kView, kView, d.grad_outputs, kOutputs, kOutputs, n, grads.rgb, 1, kView, nullptr},
-        {d.inputs, d.inputs_stride, kInputs, d.grad_outputs, kOutputs, kOutputs, n, grads.skip, 1, kInputs, nullptr},
+    struct Gemm {
+        const uint16_t* g;
+        int64_t g_stride;
+        int m_cols;
+        const uint16_t* v;
+        int64_t v_stride;
+        int k_cols;
+        float* dw;
+        int64_t dw_m_stride, dw_k_stride;
+        float* bias;
     };
-    for (const WeightArgs& a : launches) {
+    const Gemm gemms[] = {
+        // view_2: g_v2^T v1 (+ bias), view_1: g_v1^T v0 (+ bias), combined: g_v0^T inputs (its bias in the bias lane)
+        {g_v2, kView, kView, v1, kView, kView, grads.view_2, kView, 1, grads.view_2_bias},
+        {g_v1, kView, kView, v0, kView, kView, grads.view_1, kView, 1, grads.view_1_bias},
+        {g_v0, kView, kView, d.inputs, d.inputs_stride, kInputs, grads.combined, kInputs, 1, nullptr},
+        // density: g_h^T features (+ bias)
+        {d.grad_hidden, kDensity, kDensity, features, features_stride, kFeatures, grads.density, kDensity, 1, grads.density_bias},
+        // rgb and skip, transposed (their 8 output rows as N): v2^T g_out into rgb[o][i], inputs^T g_out into skip[o][i]
+        {v2, kView, kView, d.grad_outputs, kOutputs, kOutputs, grads.rgb, 1, kView, nullptr},
+        {d.inputs, d.inputs_stride, kInputs, d.grad_outputs, kOutputs, kOutputs, grads.skip, 1, kInputs, nullptr},
+    };
+    for (const Gemm& gemm : gemms) {
+        WeightArgs a{};
+        a.m_pad = gemm.m_cols > 128 ? 256 : 128;
+        a.k_pad = gemm.k_cols <= kNarrowCols ? kNarrowCols : (gemm.k_cols + kBoxCols - 1) / kBoxCols * kBoxCols;
+        a.m_cols = gemm.m_cols;
+        a.k_cols = gemm.k_cols;
+        a.n = n;
+        a.dw = gemm.dw;
+        a.dw_m_stride = gemm.dw_m_stride;
+        a.dw_k_stride = gemm.dw_k_stride;
+        a.bias = gemm.bias;
+        if (!encode_operand(&a.g_map, gemm.g, gemm.m_cols, gemm.g_stride, n, false) ||
+            !encode_operand(&a.v_map, gemm.v, gemm.k_cols, gemm.v_stride, n, a.k_pad == kNarrowCols)) {
+            return cudaErrorInvalidValue;
+        }
         fz_nerf_mlp_backward_weight_kernel<<<grid, kWgradThreads, kWgradSmemBytes, stream>>>(a, status);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
@@ -586,6 +701,8 @@ int zf_nerf_mlp_backward_tc(const uint16_t* grad_outputs, const uint16_t* featur
     using namespace zf::nerf_mlp::bwd;
     if (n < 0 || weights == nullptr || grads == nullptr || status == nullptr) return zf::set_error(ZF_ERROR_INVALID_ARGUMENT, "invalid nerf mlp backward inputs");
     if (n == 0) return ZF_OK;
+    // the weight gradients' tensor copies address samples with 32-bit coordinates
+    if (n > INT32_MAX - 64) return zf::set_error(ZF_ERROR_INVALID_ARGUMENT, "nerf mlp backward: too many samples");
     if (workspace_bytes < zf_nerf_mlp_backward_workspace_size(n)) return zf::set_error(ZF_ERROR_INVALID_ARGUMENT, "nerf mlp backward workspace too small");
     const void* pointers[] = {grad_outputs, features, inputs, activations, grad_features, workspace, weights->rgb_t, weights->view_2_t,
                               weights->view_1_t, weights->combined_t, weights->skip_t, weights->density_t};
@@ -604,6 +721,6 @@ int zf_nerf_mlp_backward_tc(const uint16_t* grad_outputs, const uint16_t* featur
     const PackedMlpT w{weights->rgb_t, weights->view_2_t, weights->view_1_t, weights->combined_t, weights->skip_t, weights->density_t};
     uint16_t* ws = static_cast<uint16_t*>(workspace);
     const DataArgs d{grad_outputs, inputs, inputs_stride, activations, ws, ws + 3 * n * kView, grad_features, grad_features_stride, n};
-    const cudaError_t e = launch_backward(w, d, *grads, features, status, stream);
+    const cudaError_t e = launch_backward(w, d, *grads, features, features_stride, status, stream);
     return e == cudaSuccess ? ZF_OK : zf::set_cuda_error(e, "nerf mlp backward");
 }

@@ -29,14 +29,24 @@ __host__ __device__ __forceinline__ uint32_t canonical_offset(const int row, con
 }
 
 // shared-memory matrix descriptor (tcgen05 format): start, leading and stride byte offsets in 16-byte units, version 1
-// in bits 46-47, base offset 0, no swizzle (layout type 0 in bits 61-63)
-__host__ __device__ __forceinline__ uint64_t smem_descriptor(const uint32_t address, const uint32_t leading_bytes, const uint32_t stride_bytes) {
+// in bits 46-47, base offset 0, the layout type in bits 61-63 (0: no swizzle, 2: 128-byte swizzle, 6: 32-byte swizzle)
+__host__ __device__ __forceinline__ uint64_t smem_descriptor(const uint32_t address, const uint32_t leading_bytes, const uint32_t stride_bytes,
+                                                             const uint32_t layout = 0) {
     uint64_t d = static_cast<uint64_t>((address & 0x3FFFFu) >> 4);
     d |= static_cast<uint64_t>((leading_bytes >> 4) & 0x3FFFu) << 16;
     d |= static_cast<uint64_t>((stride_bytes >> 4) & 0x3FFFu) << 32;
     d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(layout & 7u) << 61;
     return d;
 }
+
+// MN-major tiles of `rows` K rows as TMA writes them: with the 128-byte swizzle, 64-column atoms rows * 128 bytes apart
+// (leading offset) and 8-row K groups 1024 bytes apart (stride offset); with the 32-byte swizzle one 16-column atom,
+// 8-row K groups 256 bytes apart
+__host__ __device__ __forceinline__ uint64_t mn_sw128_descriptor(const uint32_t address, const uint32_t rows) {
+    return smem_descriptor(address, rows * 128, 1024, 2);
+}
+__host__ __device__ __forceinline__ uint64_t mn_sw32_descriptor(const uint32_t address) { return smem_descriptor(address, 0, 256, 6); }
 
 // instruction descriptor of kind::f16: fp32 accumulator (bits 4-5 = 1), bf16 A and B (bits 7-9, 10-12 = 1), A and B
 // K-major (bits 15, 16 = 0) or MN-major (= 1), N / 8 in bits 17-22, M / 16 in bits 24-28

@@ -323,8 +323,27 @@ template <int N> int check_instr_mn() {
     if (theirs != ours) std::printf("instr MN N=%d: cute %08x ours %08x\n", N, theirs, ours);
     return theirs != ours;
 }
+// the TMA-written weight-gradient tiles: K-major tiling of CuTe's MN-major swizzle atoms (8-row K groups adjacent)
+template <class Atom, int Width, int Rows> uint64_t cute_swizzled() {
+    auto layout = tile_to_shape(Atom{}, make_shape(Int<Width>{}, Int<Rows>{}), Step<_2, _1>{});
+    auto tensor = make_tensor(make_smem_ptr(reinterpret_cast<bfloat16_t*>(uintptr_t(0))), layout);
+    return uint64_t(UMMA::make_umma_desc<UMMA::Major::MN>(tensor)) & ~uint64_t(0x3FFF);
+}
+template <int Width, int Rows> int check_sw128() {
+    const uint64_t theirs = cute_swizzled<UMMA::Layout_MN_SW128_Atom<bfloat16_t>, Width, Rows>();
+    const uint64_t ours = zf::nerf_mlp::mn_sw128_descriptor(0, Rows);
+    if (theirs != ours) std::printf("SW128 width %d rows %d: cute %llx ours %llx\n", Width, Rows, (unsigned long long)theirs, (unsigned long long)ours);
+    return theirs != ours;
+}
+int check_sw32() {
+    const uint64_t theirs = cute_swizzled<UMMA::Layout_MN_SW32_Atom<bfloat16_t>, 16, 32>();
+    const uint64_t ours = zf::nerf_mlp::mn_sw32_descriptor(0);
+    if (theirs != ours) std::printf("SW32: cute %llx ours %llx\n", (unsigned long long)theirs, (unsigned long long)ours);
+    return theirs != ours;
+}
 int main() {
     int bad = check_mn<256, 64>() + check_mn<128, 64>() + check_mn<16, 64>() + check_mn<96, 64>() + check_mn<64, 64>();
+    bad += check_sw128<256, 32>() + check_sw128<128, 32>() + check_sw32();
     bad += check_instr_mn<16>() + check_instr_mn<64>() + check_instr_mn<96>() + check_instr_mn<256>();
     std::printf("%d mismatches\n", bad);
     return bad;
@@ -335,9 +354,10 @@ int main() {
 @pytest.mark.skipif(shutil.which('nvcc') is None or _cutlass_include() is None, reason='nvcc or the CUTLASS headers are absent')
 def test_weight_gradient_descriptors_match_cutlass(tmp_path):
     """The backward's weight-gradient GEMMs read their operands MN-major (the samples are K): the shared-memory
-    descriptors of those tiles (leading byte offset = the K-atom stride, stride byte offset = 128) and the MN-major
-    instruction descriptors equal the ones CuTe builds for the same layouts (make_umma_desc<Major::MN>,
-    make_instr_desc with Major::MN)."""
+    descriptors of canonical tiles (leading byte offset = the K-atom stride, stride byte offset = 128), of the
+    TMA-written tiles with the 128-byte swizzle (leading offset = the 64-column atom stride, stride offset = 1024)
+    and the 32-byte swizzle, and the MN-major instruction descriptors equal the ones CuTe builds for the same layouts
+    (make_umma_desc<Major::MN>, make_instr_desc with Major::MN)."""
     source = tmp_path / 'check_mn.cu'
     source.write_text(MN_DESCRIPTOR_CHECK)
     binary = tmp_path / 'check_mn'
