@@ -42,6 +42,10 @@ constexpr int kInputs = 96;          // hidden 64 + direction block 32 (its last
 constexpr int kView = 256;
 constexpr int kOutputs = 8;          // raw density, 3 rgb logits, 4 padding
 constexpr int kOutputsN = 16;        // the smallest N of an M = 128 MMA
+// the training record behind the activations v0, v1, v2 ([3, n, 256] bf16): their ReLU masks, [3, n, 8] words (bit
+// c % 32 of word c / 32: column c positive), then h's, [n, 2] words
+constexpr int kMaskWords = kView / 32;
+constexpr int kHiddenMaskWords = kDensity / 32;
 
 // warp roles
 constexpr int kMmaWarp = 0;
@@ -109,10 +113,12 @@ struct PackedMlp {
 
 // N accumulator columns of this thread's row (N = 16, or a multiple of 32 loaded 32 at a time with one wait) + bias
 // (shared memory, or none), ReLU, bf16, into row `row` of a K-major operand at column k_first (and into global memory
-// at `global_row` when given)
+// at `global_row` when given; and, when mask_words is given, bit c % 32 of word c / 32 set where column c came out
+// positive, N a multiple of 32)
 template <int N>
 __device__ __forceinline__ void relu_columns(const uint32_t taddr, const float* bias, uint8_t* dst, const int row, const int k_total, const int k_first,
-                                             uint16_t* global_row) {
+                                             uint16_t* global_row, uint32_t* mask_words = nullptr) {
+    uint32_t bits[N / 32 > 0 ? N / 32 : 1] = {};
     uint32_t r[N];
     if constexpr (N == 16) {
         issue_load<16>(taddr, r);
@@ -133,10 +139,20 @@ __device__ __forceinline__ void relu_columns(const uint32_t taddr, const float* 
                 hi += bias[j + 2 * q + 1];
             }
             words[q] = pack_bf16x2_relu(lo, hi);
+            if constexpr (N >= 32) {
+                const uint32_t pair = (__uint_as_float(words[q] << 16) > 0.0f ? 1u : 0u) | (__uint_as_float(words[q] & 0xFFFF0000u) > 0.0f ? 2u : 0u);
+                bits[(j + 2 * q) / 32] |= pair << ((j + 2 * q) % 32);
+            }
         }
         const uint4 out = make_uint4(words[0], words[1], words[2], words[3]);
         *reinterpret_cast<uint4*>(dst + canonical_offset(row, k_first + j, k_total)) = out;
         if (global_row != nullptr) *reinterpret_cast<uint4*>(global_row + k_first + j) = out;
+    }
+    if constexpr (N == 32) {
+        if (mask_words != nullptr) *mask_words = bits[0];
+    }
+    else if constexpr (N == 64) {
+        if (mask_words != nullptr) *reinterpret_cast<uint2*>(mask_words) = make_uint2(bits[0], bits[1]);
     }
 }
 
@@ -212,6 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                const int64_t inputs_stride, const PackedMlp w, uint16_t* __restrict__ outputs, uint16_t* __restrict__ activations,
                                const int64_t n, int* status) {
     extern __shared__ __align__(1024) uint8_t smem[];
+    uint32_t* masks = activations != nullptr ? reinterpret_cast<uint32_t*>(activations + 3 * n * kView) : nullptr;
     uint8_t* act = smem + kActOffset;
     uint8_t* in = smem + kInOffset;
     float* bias = reinterpret_cast<float*>(smem + kBiasOffset);  // density [64], view_1 [256], view_2 [256]
@@ -357,6 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int e = warp - kFirstEpilogueWarp;
         const int c = e / 4;
         constexpr int kHiddenColumns = kDensity / kChunkGroups;  // this group's columns of h
+        static_assert(kHiddenColumns == 32, "the training record keeps h's ReLU mask as one word per chunk group (8 epilogue warps)");
         const int quadrant = warp % 4;
         const int row = 32 * quadrant + lane;
         const int tid = threadIdx.x - 32 * kFirstEpilogueWarp;
@@ -393,7 +411,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             // E0: h + b_density, ReLU -> this group's columns of h in the inputs (shared and global)
             if (!(ok = accumulator_ready())) break;
             relu_columns<kHiddenColumns>(lanes + (layer & 1u) * kRegionColumns + kHiddenColumns * c, bias + kHiddenColumns * c, in, row, kInputs,
-                                         kHiddenColumns * c, valid ? inputs + sample * inputs_stride : nullptr);
+                                         kHiddenColumns * c, valid ? inputs + sample * inputs_stride : nullptr,
+                                         masks != nullptr && valid ? masks + 3 * n * kMaskWords + sample * kHiddenMaskWords + c : nullptr);
             publish(h_bar);
             layer++;
             // the next tile's inputs, into registers while this tile's layers run
@@ -404,9 +423,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float* b = k == 1 ? nullptr : bias + kDensity + (k - 2) * kView;
                 // the training forward also keeps v0, v1, v2 in global memory for the backward
                 uint16_t* kept = activations != nullptr && valid ? activations + (static_cast<int64_t>(k - 1) * n + sample) * kView : nullptr;
+                uint32_t* kept_mask = masks != nullptr && valid ? masks + (static_cast<int64_t>(k - 1) * n + sample) * kMaskWords : nullptr;
                 for (int j = c; j < kChunks; j += kChunkGroups) {
                     relu_columns<kSlice>(lanes + (layer & 1u) * kRegionColumns + kSlice * j, b != nullptr ? b + kSlice * j : nullptr, act, row, kView,
-                                         kSlice * j, kept);
+                                         kSlice * j, kept, kept_mask != nullptr ? kept_mask + 2 * j : nullptr);
                     publish(chunk_bar(j));
                 }
                 layer++;
@@ -473,6 +493,11 @@ cudaError_t launch_forward(const uint16_t* features, const int64_t features_stri
 }
 
 }  // namespace zf::nerf_mlp
+
+int64_t zf_nerf_mlp_activations_size(const int64_t n) {
+    using namespace zf::nerf_mlp;
+    return n < 0 ? 0 : n * (3 * kView * 2 + 3 * kMaskWords * 4 + kHiddenMaskWords * 4);
+}
 
 int zf_nerf_mlp_forward_tc(const uint16_t* features, const int64_t features_stride, uint16_t* inputs, const int64_t inputs_stride,
                            const zf_nerf_mlp_weights* weights, uint16_t* outputs, uint16_t* activations, const int64_t n, int* status,

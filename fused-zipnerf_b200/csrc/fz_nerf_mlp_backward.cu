@@ -78,7 +78,8 @@ struct DataArgs {
     const uint16_t* grad_outputs;   // [n, 8]
     const uint16_t* inputs;         // [n, inputs_stride]: h in columns 0-63
     int64_t inputs_stride;
-    const uint16_t* activations;    // [3, n, 256]: v0, v1, v2
+    const uint32_t* masks;          // [3, n, 8]: the ReLU masks of v0, v1, v2 (bit c % 32 of word c / 32)
+    const uint32_t* hidden_masks;   // [n, 2]: h's
     uint16_t* grad_activations;     // [3, n, 256] out: g_v0, g_v1, g_v2
     uint16_t* grad_hidden;          // [n, 64] out: g_h
     uint16_t* grad_features;        // [n, grad_features_stride] out: columns 0-55
@@ -100,35 +101,30 @@ __device__ __forceinline__ Stage weight_stage(const PackedMlpT& w, const int s) 
     return {w.density_t, kDensity * kDensity * 2};
 }
 
-// this thread's mask words (8 bf16 values each) of N columns from k_first of mask_row (zeros without a row)
+// N (32 or 64) accumulator columns of this thread's row, times the ReLU mask bits m (bit c of the 64-bit word: column
+// k_first + c positive; all columns when masked is false), rounded to bf16, into row `row` of a K-major operand at
+// column k_first (when dst is given) and into global memory at out_row + k_first (its first out_cols columns, when
+// out_row is given)
 template <int N>
-__device__ __forceinline__ void fetch_mask(const uint16_t* mask_row, const int k_first, uint4 (&m)[N / 8]) {
-    #pragma unroll
-    for (int j = 0; j < N / 8; j++) m[j] = mask_row != nullptr ? __ldg(reinterpret_cast<const uint4*>(mask_row + k_first) + j) : make_uint4(0, 0, 0, 0);
-}
-
-// N (32 or 64) accumulator columns of this thread's row, times the ReLU mask m (bf16 values > 0, fetched by
-// fetch_mask; none when masked is false), rounded to bf16, into row `row` of a K-major operand at column k_first (when
-// dst is given) and into global memory at out_row + k_first (its first out_cols columns, when out_row is given)
-template <int N>
-__device__ __forceinline__ void masked_columns(const uint32_t taddr, const bool masked, const uint4 (&m)[N / 8], uint8_t* dst, const int row,
+__device__ __forceinline__ void masked_columns(const uint32_t taddr, const bool masked, const uint64_t m, uint8_t* dst, const int row,
                                                const int k_total, const int k_first, uint16_t* out_row, const int out_cols) {
-    // 32 columns per TMEM load: the mask words of the layer after this one are held meanwhile
+    // 32 columns per tensor-memory load
     #pragma unroll
     for (int c = 0; c < N; c += 32) {
         uint32_t r[32];
         issue_load<32>(taddr + c, r);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        const uint32_t bits = static_cast<uint32_t>(m >> c);
         #pragma unroll
         for (int j = c / 8; j < c / 8 + 4; j++) {
-            const uint32_t mw[4] = {m[j].x, m[j].y, m[j].z, m[j].w};
             uint32_t words[4];
             #pragma unroll
             for (int q = 0; q < 4; q++) {
-                float lo = __uint_as_float(r[8 * (j - c / 8) + 2 * q]), hi = __uint_as_float(r[8 * (j - c / 8) + 2 * q + 1]);
+                const int col = 8 * (j - c / 8) + 2 * q;  // within this 32-column load
+                float lo = __uint_as_float(r[col]), hi = __uint_as_float(r[col + 1]);
                 if (masked) {
-                    if (!(__uint_as_float(mw[q] << 16) > 0.0f)) lo = 0.0f;
-                    if (!(__uint_as_float(mw[q] & 0xFFFF0000u) > 0.0f)) hi = 0.0f;
+                    if (!((bits >> col) & 1u)) lo = 0.0f;
+                    if (!((bits >> (col + 1)) & 1u)) hi = 0.0f;
                 }
                 words[q] = pack_bf16x2(lo, hi);
             }
@@ -138,6 +134,29 @@ __device__ __forceinline__ void masked_columns(const uint32_t taddr, const bool 
         }
     }
 }
+
+// this thread's mask bits of one tile: chunks g and g + 2 of v2, v1, v0 (64 bits each), then h's columns [32 g, 32 g + 32)
+struct TileMasks {
+    uint2 v[3][2];
+    uint32_t h;
+};
+
+__device__ __forceinline__ TileMasks fetch_masks(const DataArgs& a, const int64_t sample, const int g) {
+    TileMasks t{};
+    if (sample < a.n) {
+        #pragma unroll
+        for (int k = 0; k < 3; k++) {
+            const int index = 2 - k;  // v2, v1, v0
+            const uint2* row = reinterpret_cast<const uint2*>(a.masks + (static_cast<int64_t>(index) * a.n + sample) * (kView / 32));
+            #pragma unroll
+            for (int i = 0; i < 2; i++) t.v[k][i] = __ldg(row + g + 2 * i);
+        }
+        t.h = __ldg(a.hidden_masks + sample * (kDensity / 32) + g);
+    }
+    return t;
+}
+
+__device__ __forceinline__ uint64_t bits64(const uint2 w) { return static_cast<uint64_t>(w.x) | (static_cast<uint64_t>(w.y) << 32); }
 
 __global__ void __launch_bounds__(kThreads, 1) fz_nerf_mlp_backward_data_kernel(const __grid_constant__ PackedMlpT w, const __grid_constant__ DataArgs a,
                                                                              int* status) {
@@ -303,22 +322,14 @@ __global__ void __launch_bounds__(kThreads, 1) fz_nerf_mlp_backward_data_kernel(
         auto store_gout = [&](const uint4 v) {
             if (tid < kTileRows) *reinterpret_cast<uint4*>(gout + canonical_offset(tid, 0, kGoutK)) = v;
         };
-        // the mask words of the next epilogue are fetched while the layer before it runs: v2, v1, v0 for chunks g and
-        // g + 2, then h for columns [32 g, 32 g + 32)
-        uint4 masks[2][kSlice / 8];
-        uint4 hidden_mask[4];
-        auto fetch_layer_masks = [&](const int index, const int64_t s) {
-            #pragma unroll
-            for (int i = 0; i < 2; i++) {
-                fetch_mask<kSlice>(s < n ? a.activations + (static_cast<int64_t>(index) * n + s) * kView : nullptr, kSlice * (g + 2 * i), masks[i]);
-            }
-        };
+        // the ReLU mask bits of the next tile are fetched while this tile's layers run
         int64_t tile = blockIdx.x;
         uint4 next = make_uint4(0, 0, 0, 0);
+        TileMasks masks{}, next_masks{};
         if (tile < n_tiles) {
             store_gout(fetch_gout(tile));
             publish(in_bar);
-            fetch_layer_masks(2, tile * kTileRows + row);
+            masks = fetch_masks(a, tile * kTileRows + row, g);
         }
         for (; tile < n_tiles && ok; tile += gridDim.x) {
             const int64_t sample = tile * kTileRows + row;
@@ -334,27 +345,28 @@ __global__ void __launch_bounds__(kThreads, 1) fz_nerf_mlp_backward_data_kernel(
                 #pragma unroll
                 for (int i = 0; i < 2; i++) {
                     const int j = g + 2 * i;
-                    masked_columns<kSlice>(region + kSlice * j, true, masks[i], act, row, kView, kSlice * j, out, kSlice);
+                    masked_columns<kSlice>(region + kSlice * j, true, bits64(masks.v[k][i]), act, row, kView, kSlice * j, out, kSlice);
                     publish(chunk_bar(j));
                 }
                 layer++;
-                if (k < 2) fetch_layer_masks(index - 1, sample);
-                else fetch_mask<32>(valid ? a.inputs + sample * a.inputs_stride : nullptr, 32 * g, hidden_mask);
-                if (k == 0 && more) next = fetch_gout(tile + gridDim.x);
+                if (k == 0 && more) {
+                    next = fetch_gout(tile + gridDim.x);
+                    next_masks = fetch_masks(a, (tile + gridDim.x) * kTileRows + row, g);
+                }
             }
             if (!ok) break;
             // E3: g_h = g_in[:, 0:64] masked by h: columns [32 g, 32 g + 32) -> the g_h tile and global memory
             if (!(ok = accumulator_ready())) break;
-            masked_columns<32>(lanes + (layer & 1u) * kRegionColumns + 32 * g, true, hidden_mask, gh, row, kDensity, 32 * g,
+            masked_columns<32>(lanes + (layer & 1u) * kRegionColumns + 32 * g, true, masks.h, gh, row, kDensity, 32 * g,
                                valid ? a.grad_hidden + sample * kDensity : nullptr, 32);
             publish(h_bar);
             layer++;
-            if (more) fetch_layer_masks(2, (tile + gridDim.x) * kTileRows + row);
             // E4: g_features, columns [32 g, 32 g + 32) below 56, then the next tile's output gradients
             if (!(ok = accumulator_ready())) break;
-            masked_columns<32>(lanes + (layer & 1u) * kRegionColumns + 32 * g, false, hidden_mask, nullptr, row, 0, 32 * g,
+            masked_columns<32>(lanes + (layer & 1u) * kRegionColumns + 32 * g, false, 0, nullptr, row, 0, 32 * g,
                                valid ? a.grad_features + sample * a.grad_features_stride : nullptr, kFeatures - 32 * g);
             layer++;
+            masks = next_masks;
             if (more) {
                 store_gout(next);
                 publish(in_bar);
@@ -620,8 +632,7 @@ bool encode_operand(CUtensorMap* map, const uint16_t* base, const int cols, cons
 }
 
 cudaError_t launch_backward(const PackedMlpT& w, const DataArgs& d, const zf_nerf_mlp_grads& grads, const uint16_t* features,
-                            const int64_t features_stride, int* status,
-                            cudaStream_t stream) {
+                            const int64_t features_stride, const uint16_t* activations, int* status, cudaStream_t stream) {
     int device = 0, n_sms = 0;
     cudaError_t e = cudaGetDevice(&device);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, device);
@@ -638,9 +649,9 @@ cudaError_t launch_backward(const PackedMlpT& w, const DataArgs& d, const zf_ner
     const uint16_t* g_v0 = d.grad_activations;
     const uint16_t* g_v1 = d.grad_activations + n * kView;
     const uint16_t* g_v2 = d.grad_activations + 2 * n * kView;
-    const uint16_t* v0 = d.activations;
-    const uint16_t* v1 = d.activations + n * kView;
-    const uint16_t* v2 = d.activations + 2 * n * kView;
+    const uint16_t* v0 = activations;
+    const uint16_t* v1 = activations + n * kView;
+    const uint16_t* v2 = activations + 2 * n * kView;
     struct Gemm {
         const uint16_t* g;
         int64_t g_stride;
@@ -720,7 +731,8 @@ int zf_nerf_mlp_backward_tc(const uint16_t* grad_outputs, const uint16_t* featur
     }
     const PackedMlpT w{weights->rgb_t, weights->view_2_t, weights->view_1_t, weights->combined_t, weights->skip_t, weights->density_t};
     uint16_t* ws = static_cast<uint16_t*>(workspace);
-    const DataArgs d{grad_outputs, inputs, inputs_stride, activations, ws, ws + 3 * n * kView, grad_features, grad_features_stride, n};
-    const cudaError_t e = launch_backward(w, d, *grads, features, features_stride, status, stream);
+    const uint32_t* masks = reinterpret_cast<const uint32_t*>(activations + 3 * n * kView);
+    const DataArgs d{grad_outputs, inputs, inputs_stride, masks, masks + 3 * n * (kView / 32), ws, ws + 3 * n * kView, grad_features, grad_features_stride, n};
+    const cudaError_t e = launch_backward(w, d, *grads, features, features_stride, activations, status, stream);
     return e == cudaSuccess ? ZF_OK : zf::set_cuda_error(e, "nerf mlp backward");
 }

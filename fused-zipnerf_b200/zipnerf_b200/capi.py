@@ -20,7 +20,8 @@ EXPORTED = ['zf_featurizer_create', 'zf_featurizer_destroy', 'zf_featurizer_n_ou
             'zf_check_erf_saturation', 'zf_erf_saturation_threshold', 'zf_last_error', 'zf_grid_max_value', 'zf_nerf_grid_grad_scale',
             'zf_direction_block_width', 'zf_initialize_rays', 'zf_view_rays', 'zf_generate_rays', 'zf_sample_uniforms',
             'zf_composite_and_resample', 'zf_train_final', 'zf_composite_final', 'zf_adam_create', 'zf_adam_destroy', 'zf_adam_step',
-            'zf_adam_state', 'zf_relu_backward_bf16', 'zf_nerf_mlp_forward_tc', 'zf_nerf_mlp_backward_workspace_size', 'zf_nerf_mlp_backward_tc']
+            'zf_adam_state', 'zf_relu_backward_bf16', 'zf_nerf_mlp_activations_size', 'zf_nerf_mlp_forward_tc', 'zf_nerf_mlp_backward_workspace_size',
+            'zf_nerf_mlp_backward_tc']
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -188,6 +189,8 @@ def load() -> ctypes.CDLL:
     lib.zf_relu_backward_bf16.restype = ctypes.c_int
     lib.zf_nerf_mlp_forward_tc.argtypes = [_p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _p]
     lib.zf_nerf_mlp_forward_tc.restype = ctypes.c_int
+    lib.zf_nerf_mlp_activations_size.argtypes = [_i64]
+    lib.zf_nerf_mlp_activations_size.restype = _i64
     lib.zf_nerf_mlp_backward_workspace_size.argtypes = [_i64]
     lib.zf_nerf_mlp_backward_workspace_size.restype = _i64
     lib.zf_nerf_mlp_backward_tc.argtypes = [_p, _p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _p, _i64, _i64, _p, _p]
@@ -422,6 +425,23 @@ NERF_MLP_PACKED_SHAPES = {'density': ((64, 64), 'bfloat16'), 'density_bias': ((6
                           'view_2': ((256, 256), 'bfloat16'), 'view_2_bias': ((256,), 'float32'), 'rgb': ((16, 256), 'bfloat16')}
 
 
+# bytes per sample of the training forward's record (zf_nerf_mlp_activations_size): v0, v1, v2 as [3, n, 256] bf16, their
+# ReLU masks as [3, n, 8] uint32, h's as [n, 2] uint32
+NERF_MLP_RECORD_BYTES_PER_SAMPLE = 3 * 256 * 2 + 3 * 8 * 4 + 2 * 4
+
+
+def nerf_mlp_record_size(n: int) -> int:
+    """Bytes of the training forward's record for n samples (zf_nerf_mlp_activations_size)."""
+    return n * NERF_MLP_RECORD_BYTES_PER_SAMPLE
+
+
+def _check_record(activations, n: int, on_device) -> None:
+    import torch
+    if not isinstance(activations, torch.Tensor) or not on_device(activations) or not activations.is_contiguous() \
+            or activations.numel() * activations.element_size() < nerf_mlp_record_size(n):
+        raise ValueError(f'activations must be a contiguous CUDA tensor of {nerf_mlp_record_size(n)} bytes (the training record of {n} samples)')
+
+
 def check_nerf_mlp_forward_tc(features, inputs, packed: dict, outputs, status, require_cuda: bool = True, activations=None) -> None:
     """Raises ValueError unless the tensors have the shapes, dtypes and layouts the tensor-core kernel reads and writes
     (the C ABI sees only pointers and row strides, so a wrong shape here would make the kernel read or write out of
@@ -450,15 +470,15 @@ def check_nerf_mlp_forward_tc(features, inputs, packed: dict, outputs, status, r
             raise ValueError(f'packed[{name!r}] must be a contiguous {dtype} CUDA tensor of {shape} elements')
     if not isinstance(status, torch.Tensor) or not on_device(status) or status.dtype != torch.int32 or status.numel() < 1:
         raise ValueError('status must be an int32 CUDA tensor')
-    if activations is not None and (not isinstance(activations, torch.Tensor) or not on_device(activations) or activations.dtype != torch.bfloat16
-                                    or tuple(activations.shape) != (3, n, 256) or not activations.is_contiguous()):
-        raise ValueError(f'activations must be None or a contiguous [3, {n}, 256] bf16 tensor')
+    if activations is not None:
+        _check_record(activations, n, on_device)
 
 
 def nerf_mlp_forward_tc(features, inputs, packed: dict, outputs, status, activations=None, stream=None) -> None:
     """zf_nerf_mlp_forward_tc: features [n, 56] and inputs [n, 96] bf16, packed as zipnerf_b200.nerf_mlp.pack gives it
     (the kernel's shapes), outputs [n, 8] bf16, status a device int32 the kernel sets on a timed-out wait; activations
-    None (inference) or a contiguous [3, n, 256] bf16 tensor for v0, v1, v2 (training). The tensors are checked first
+    None (inference) or a contiguous tensor of nerf_mlp_record_size(n) bytes for the training record (v0, v1, v2 as
+    [3, n, 256] bf16 at its start, then the ReLU masks). The tensors are checked first
     (check_nerf_mlp_forward_tc: ValueError on a mismatch)."""
     check_nerf_mlp_forward_tc(features, inputs, packed, outputs, status, activations=activations)
     w = zf_nerf_mlp_weights(*[packed[name].data_ptr() for name, _ in zf_nerf_mlp_weights._fields_])
@@ -489,9 +509,7 @@ def check_nerf_mlp_backward_tc(grad_outputs, features, inputs, activations, pack
             raise ValueError(f'{what} must be [{n}, >= {width}] with unit column stride')
     if not grad_outputs.is_contiguous() or grad_outputs.shape[1] != 8:
         raise ValueError('grad_outputs must be a contiguous [n, 8] tensor')
-    cuda(activations, torch.bfloat16, 'activations')
-    if tuple(activations.shape) != (3, n, 256) or not activations.is_contiguous():
-        raise ValueError(f'activations must be a contiguous [3, {n}, 256] tensor')
+    _check_record(activations, n, lambda t: t.is_cuda)
     for name, shape in NERF_MLP_TRANSPOSED_SHAPES.items():
         t = packed_t.get(name)
         cuda(t, torch.bfloat16, f'packed_t[{name!r}]')

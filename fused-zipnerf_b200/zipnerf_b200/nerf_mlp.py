@@ -336,9 +336,14 @@ class NerfMlp:
             raise RuntimeError('ZipNeRF: invalid nerf mlp inputs')
         n = features.shape[0]
         outputs = torch.empty(n, 8, dtype=torch.bfloat16, device=features.device)
-        activations = torch.empty(3, n, self.layout.view_width, dtype=torch.bfloat16, device=features.device) if training else None
-        capi.nerf_mlp_forward_tc(features, inputs, self._tc_weights(packed), outputs, self.status(features.device), activations=activations)
-        return outputs, ([inputs, activations[0], activations[1], activations[2]] if training else [])
+        if not training:
+            capi.nerf_mlp_forward_tc(features, inputs, self._tc_weights(packed), outputs, self.status(features.device))
+            return outputs, []
+        # the training record: v0, v1, v2 ([3, n, 256] bf16, the context's views), then their ReLU masks for the backward
+        record = torch.empty(capi.nerf_mlp_record_size(n) // 2, dtype=torch.bfloat16, device=features.device)
+        capi.nerf_mlp_forward_tc(features, inputs, self._tc_weights(packed), outputs, self.status(features.device), activations=record)
+        planes = record[:3 * n * self.layout.view_width].view(3, n, self.layout.view_width)
+        return outputs, [inputs, planes[0], planes[1], planes[2]]
 
     def _forward(self, features: torch.Tensor, inputs: torch.Tensor, packed: torch.Tensor, training: bool):
         if features.shape[1] != self.n_features or inputs.shape[1] != self.n_inputs or packed.numel() != self.packed_size:
@@ -402,11 +407,15 @@ class NerfMlp:
         if len(context) != 4 or packed.numel() != self.packed_size:
             raise RuntimeError('ZipNeRF: invalid nerf mlp backward inputs')
         inputs, base = context[0], context[1]
-        # the training forward's activations: one [3, n, 256] buffer whose planes are v0, v1, v2
-        activations = base.as_strided((3,) + tuple(base.shape), (base.numel(),) + tuple(base.stride()))
-        if activations[2].data_ptr() != context[3].data_ptr() or activations[1].data_ptr() != context[2].data_ptr():
-            raise RuntimeError('ZipNeRF: nerf mlp backward needs the context of the tensor-core forward')
         n = features.shape[0]
+        # the training forward's record: v0, v1, v2 are its first three planes, the ReLU masks follow them
+        record_elements = capi.nerf_mlp_record_size(n) // 2
+        plane = base.numel()
+        if (base.dtype != torch.bfloat16 or not base.is_contiguous() or context[2].data_ptr() != base.data_ptr() + 2 * plane
+                or context[3].data_ptr() != base.data_ptr() + 4 * plane
+                or base.untyped_storage().nbytes() < 2 * (base.storage_offset() + record_elements)):
+            raise RuntimeError('ZipNeRF: nerf mlp backward needs the context of the tensor-core forward')
+        activations = base.as_strided((record_elements,), (1,))
         grad_features = torch.empty(n, self.n_features, dtype=torch.bfloat16, device=features.device)
         grads = {name: torch.zeros(shape, device=features.device) for name, shape in capi.NERF_MLP_GRAD_SHAPES.items()}
         workspace = torch.empty(max(capi.load().zf_nerf_mlp_backward_workspace_size(n), 16), dtype=torch.uint8, device=features.device)

@@ -41,13 +41,20 @@ typedef struct zf_nerf_mlp_weights {
     const uint16_t* rgb;           /* [16, 256]: rows 1-3 the rgb weights, the others zero */
 } zf_nerf_mlp_weights;
 
-/* The inference forward of NerfMlp::forward (nerf_mlp.cu:503-560) for the reference model's widths, one persistent
+/* Bytes of the training forward's record for n samples: the hidden view-layer activations v0, v1, v2 ([3, n, 256]
+ * bf16), then their ReLU masks ([3, n, 8] uint32: bit c % 32 of word c / 32 set where column c is positive), then the
+ * hidden layer h's ([n, 2] uint32). No counterpart in the reference, whose training forward keeps v0-v2 in tensors it
+ * allocates (nerf_mlp.cu:527-560). */
+ZF_API int64_t zf_nerf_mlp_activations_size(int64_t n);
+
+/* The forward of NerfMlp::forward (nerf_mlp.cu:503-560) for the reference model's widths, one persistent
  * tcgen05 kernel (bf16 operands in shared memory, fp32 accumulators in tensor memory, 128-sample tiles, one CTA per
  * SM; each sample's outputs depend on its own row only): features [n, 56] bf16,
  * inputs [n, 96] bf16 (the direction block in columns 64-95 is read, the hidden layer written to columns 0-63),
- * outputs [n, 8] bf16 (raw density, 3 rgb logits, 4 zeros); activations: NULL (inference), or [3, n, 256] bf16 that
- * receives the hidden view-layer activations v0, v1, v2 for the backward (the training forward, as NerfMlp::forward with
- * training = true keeps them, nerf_mlp.cu:527-560); row strides in elements, multiples of 8; status: a device
+ * outputs [n, 8] bf16 (raw density, 3 rgb logits, 4 zeros); activations: NULL (inference), or the training record of
+ * zf_nerf_mlp_activations_size(n) bytes, which receives v0, v1, v2 and the ReLU masks for the backward (the training
+ * forward, as NerfMlp::forward with training = true keeps v0-v2, nerf_mlp.cu:527-560); row strides in elements,
+ * multiples of 8; status: a device
  * int the kernel sets to 1 if one of its bounded waits ran out, which leaves this launch's outputs undefined (the
  * kernel still waits for its own copies and MMAs in flight and frees its tensor memory before it exits). Within bf16
  * rounding of the reference's cuBLASLt chain. */
@@ -88,11 +95,12 @@ ZF_API int64_t zf_nerf_mlp_backward_workspace_size(int64_t n);
 
 /* The backward of NerfMlp::backward (nerf_mlp.cu:565-620) on the tcgen05 tensor cores, for the reference model's widths:
  * grad_outputs [n, 8] bf16 (columns 4-7 zero), features [n, 56] and inputs [n, 96] bf16 of the forward (h in columns
- * 0-63), activations [3, n, 256] bf16 (v0, v1, v2 kept by the training forward), weights_t the transposed packed
+ * 0-63), activations the training forward's record (v0, v1, v2 and the ReLU masks), weights_t the transposed packed
  * weights; grad_features [n, 56] bf16 out; grads += the gradients of the packed weights (their unfold into the
- * reference's parameters is the caller's); workspace of zf_nerf_mlp_backward_workspace_size(n) bytes. Two kernels: the
- * data-gradient chain of each 128-sample tile (masked by the activations' ReLU), then the weight gradients as
- * split-K GEMMs over the samples with fp32 atomics. status: as zf_nerf_mlp_forward_tc. */
+ * reference's parameters is the caller's); workspace of zf_nerf_mlp_backward_workspace_size(n) bytes; n < 2^31 - 64.
+ * Seven launches: the data-gradient chain of each 128-sample tile (masked by the record's ReLU masks), then six weight
+ * gradients as split-K GEMMs over the samples (TMA tensor copies of this GPU's memory, no multicast) with fp32 atomics.
+ * status: as zf_nerf_mlp_forward_tc. */
 ZF_API int zf_nerf_mlp_backward_tc(const uint16_t* grad_outputs, const uint16_t* features, int64_t features_stride, const uint16_t* inputs,
                                    int64_t inputs_stride, const uint16_t* activations, const zf_nerf_mlp_weights_t* weights_t,
                                    uint16_t* grad_features, int64_t grad_features_stride, const zf_nerf_mlp_grads* grads, void* workspace,

@@ -191,3 +191,78 @@ def test_tensor_core_backward_matches_the_gemm_chain(cuda_device, n):
               if layout.view(grad_chain, name).abs().max() > 0}
     errors['features'] = rel(features_tc, features_chain)
     assert max(errors.values()) < 1e-2, errors
+
+
+def _backward_case(cuda_device, n, seed):
+    import ZipNeRFCudaBackend as backend
+    from zipnerf_b200 import nerf_mlp as nm
+    layout = nm.NerfMlpLayout()
+    gen = torch.Generator().manual_seed(seed)
+    params = torch.zeros(layout.numel)
+    layout.initialize(params, gen)
+    for name, _, fan_in in layout.parameters:
+        if fan_in == 0:
+            layout.view(params, name).uniform_(-0.3, 0.3, generator=gen)
+    features = torch.zeros(n, 56)
+    features[:, :50] = torch.randn(n, 50, generator=gen)
+    inputs = torch.zeros(n, 96)
+    inputs[:, 64:91] = torch.rand(n, 27, generator=gen) * 2 - 1
+    inputs[:, 95] = 1.0
+    grad_outputs = torch.zeros(n, 8)
+    grad_outputs[:, :4] = torch.randn(n, 4, generator=gen)
+    mlp = backend.NerfMlp(50, 64, 256, 256, 4)
+    params = params.to(cuda_device)
+    return (mlp, layout, params, features.bfloat16().to(cuda_device), inputs.bfloat16().to(cuda_device),
+            grad_outputs.bfloat16().to(cuda_device))
+
+
+def test_training_record_masks_are_the_activations_signs(cuda_device):
+    """The training forward's record holds v0, v1, v2 and, behind them, one bit per column set exactly where the stored
+    bf16 value is positive (bit c % 32 of word c / 32), for v0-v2 and for the hidden layer h the forward writes into
+    inputs[:, 0:64] (n = 5,003: a ragged last tile)."""
+    mlp, _, params, features, inputs, _ = _backward_case(cuda_device, 5_003, 11)
+    n = features.shape[0]
+    packed = mlp.pack(params)
+    _, context = mlp.forward(features, inputs, packed, True)
+    torch.cuda.synchronize()
+    record = context[1].as_strided((3 * n * 256 + 3 * n * 16 + 4 * n,), (1,))
+    words = record[3 * n * 256:].view(torch.int32)
+    bit = torch.arange(32, device=cuda_device)
+
+    def expand(w, columns):
+        return ((w.view(torch.int32).unsqueeze(-1) >> bit) & 1).reshape(n, columns).bool()
+
+    for k in range(3):
+        expected = context[1 + k].float() > 0
+        assert torch.equal(expand(words[k * n * 8:(k + 1) * n * 8].view(n, 8), 256), expected), k
+    assert torch.equal(expand(words[3 * n * 8:].view(n, 2), 64), inputs[:, :64].float() > 0)
+
+
+def test_tensor_core_backward_reads_features_with_their_own_stride(cuda_device):
+    """zf_nerf_mlp_backward_tc takes separate row strides for features and grad_features: features as the first 56
+    columns of a [n, 64] buffer (stride 64) and grad_features as a [n, 72] buffer's give the same gradients bit for bit
+    as the contiguous call."""
+    from zipnerf_b200 import capi
+    mlp, layout, params, features, inputs, grad_outputs = _backward_case(cuda_device, 9_001, 5)
+    n = features.shape[0]
+    packed = mlp.pack(params)
+    _, context = mlp.forward(features, inputs, packed, True)
+    record = context[1].as_strided((capi.nerf_mlp_record_size(n) // 2,), (1,))
+    weights = mlp._tc_weights(packed, ('rgb_t', 'view_2_t', 'view_1_t', 'combined_t', 'skip_t', 'density_t'))
+    workspace = torch.empty(capi.load().zf_nerf_mlp_backward_workspace_size(n), dtype=torch.uint8, device=cuda_device)
+    results = []
+    for feature_width, grad_width in ((56, 56), (64, 72)):
+        wide = torch.zeros(n, feature_width, dtype=torch.bfloat16, device=cuda_device)
+        wide[:, :56] = features
+        grad_features = torch.zeros(n, grad_width, dtype=torch.bfloat16, device=cuda_device)
+        grads = {name: torch.zeros(shape, device=cuda_device) for name, shape in capi.NERF_MLP_GRAD_SHAPES.items()}
+        # one CTA's share of the weight gradients is summed by fp32 atomics in any order: compare up to that
+        capi.nerf_mlp_backward_tc(grad_outputs, wide[:, :56], inputs, record, weights, grad_features[:, :56], grads, workspace,
+                                  mlp.status(cuda_device))
+        torch.cuda.synchronize()
+        results.append((grad_features[:, :56].clone(), grads))
+    assert int(mlp.status(cuda_device).item()) == 0
+    assert torch.equal(results[0][0].view(torch.int16), results[1][0].view(torch.int16))
+    for name in capi.NERF_MLP_GRAD_SHAPES:
+        a, b = results[0][1][name], results[1][1][name]
+        assert ((a - b).norm() <= 1e-5 * b.norm() + 1e-30).item(), name

@@ -207,3 +207,20 @@ def test_nerf_mlp_forward_validates_before_touching_a_device():
     for features_stride, inputs_stride in [(50, 96), (56, 90), (48, 96), (56, 88)]:
         assert lib.zf_nerf_mlp_forward_tc(fake, features_stride, fake, inputs_stride, ctypes.byref(w), fake, None, 4, fake, None) == capi.ZF_ERROR_INVALID_ARGUMENT
         assert b'row strides' in lib.zf_last_error()
+
+
+def test_nerf_mlp_training_record_and_backward_limits():
+    """The training record's size (v0-v2 in bf16, then the ReLU masks as bits) is the same on both sides of the ABI,
+    and the tensor-core backward rejects sample counts its 32-bit tensor-copy coordinates cannot address before it
+    touches a device."""
+    from zipnerf_b200 import capi
+    lib = capi.load()
+    for n in (0, 1, 127, 2_097_152):
+        assert lib.zf_nerf_mlp_activations_size(n) == capi.nerf_mlp_record_size(n) == n * (3 * 512 + 3 * 32 + 8)
+    fake = 1 << 20
+    w = capi.zf_nerf_mlp_weights_t(*([fake] * 6))
+    g = capi.zf_nerf_mlp_grads(*([fake] * 9))
+    n = 2 ** 31
+    assert lib.zf_nerf_mlp_backward_tc(fake, fake, 56, fake, 96, fake, ctypes.byref(w), fake, 56, ctypes.byref(g), fake, 1 << 62, n, fake,
+                                       None) == capi.ZF_ERROR_INVALID_ARGUMENT
+    assert b'too many samples' in lib.zf_last_error()
