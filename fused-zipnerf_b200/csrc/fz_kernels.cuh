@@ -894,12 +894,37 @@ struct BackwardMlpArgs {
 #ifndef ZF_MLP_WARPS
 #define ZF_MLP_WARPS 8
 #endif
+// Paired fp32 arithmetic (sm_100): two lanes' worth of fused multiply-adds or adds in one instruction, each element
+// rounded as the scalar fma.rn / add.rn with flush-to-zero (what __fmaf_rn and __fadd_rn are under --use_fast_math), so
+// a pair of sequential chains gives the scalar chains' results bit for bit.
+__device__ __forceinline__ uint64_t pair_of(const float lo, const float hi) {
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
+}
+__device__ __forceinline__ float2 split_pair(const uint64_t d) {
+    float2 v;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(d));
+    return v;
+}
+__device__ __forceinline__ uint64_t fma_pair(const uint64_t a, const uint64_t b, const uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t add_pair(const uint64_t a, const uint64_t b) {
+    uint64_t d;
+    asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 constexpr int kMlpWarps = ZF_MLP_WARPS;
 constexpr int kMlpBlock = 32 * kMlpWarps;
 __host__ __device__ constexpr int mlp_rows_pad(const int width) { return (width + 3) / 4 * 4; }
 __host__ __device__ constexpr int mlp_block_floats(const int n_out, const int nout_pad, const int width) {
     return mlp_rows_pad(width) * nout_pad + 2 * mlp_rows_pad(width)                  // weights (w0 rows padded to nout_pad), b0, w1
-        + (n_out * (mlp_rows_pad(width) + 1) + 2 * width + 1 + 3) / 4 * 4;           // the block's parameter gradient sums
+        + (n_out * (mlp_rows_pad(width) + 1) + 2 * width + 1 + 3) / 4 * 4            // the block's parameter gradient sums
+        + mlp_rows_pad(width) * nout_pad;                                             // w0 with row pairs interleaved
 }
 __host__ __device__ constexpr int mlp_warp_floats(const int nout_pad, const int width) {
     return 32 * odd_quads(mlp_rows_pad(width)) + 32 * odd_quads(nout_pad) + 32;  // pre-activations, features, upstream gradient
@@ -925,6 +950,9 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
     float* s_acc = s_w1 + w_pad;
     const int acc_stride = w_pad + 1;
     const int acc_b0 = n_out * acc_stride, acc_w1 = acc_b0 + W, acc_b1 = acc_w1 + W, n_acc = acc_b1 + 1;
+    // w0 again with rows 2 k and 2 k + 1 interleaved: element (j, i) at (j / 2) 2 NOUT_PAD + 2 i + j % 2, so one float4
+    // holds two rows' weights of two consecutive inputs (the paired forward recomputation)
+    float* s_w0p = smem + mlp_block_floats(n_out, NOUT_PAD, W) - w_pad * NOUT_PAD;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float* s_pre = smem + mlp_block_floats(n_out, NOUT_PAD, W) + warp * mlp_warp_floats(NOUT_PAD, W);  // [32, ps]
     float* s_feat = s_pre + 32 * ps;           // [32, fs]
@@ -932,7 +960,9 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
     // padding rows (j >= W) and columns (i >= n_out) are zero: their pre-activations are 0 and select no gradient
     for (int i = threadIdx.x; i < w_pad * NOUT_PAD; i += kMlpBlock) {
         const int j = i / NOUT_PAD, c = i - j * NOUT_PAD;
-        s_w0[i] = j < W && c < n_out ? __ldg(a.w0 + j * n_out + c) : 0.0f;
+        const float w = j < W && c < n_out ? __ldg(a.w0 + j * n_out + c) : 0.0f;
+        s_w0[i] = w;
+        s_w0p[(j / 2) * 2 * NOUT_PAD + 2 * c + (j % 2)] = w;
     }
     for (int i = threadIdx.x; i < w_pad; i += kMlpBlock) {
         s_b0[i] = i < W ? __ldg(a.b0 + i) : 0.0f;
@@ -965,51 +995,66 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
         }
         __syncwarp();
 
-        // phase 1, one sample per lane: MLP recomputation and its input gradient (featurize_backward_mlp.cu:82-105)
+        // phase 1, one sample per lane: MLP recomputation and its input gradient (featurize_backward_mlp.cu:82-105), two
+        // hidden units per paired instruction in the recomputation and two inputs per paired instruction in the gradient
+        float grad_f[NOUT_PAD];
         {
-            float f[NOUT_PAD];
+            uint64_t ff[NOUT_PAD];  // (f_i, f_i)
             #pragma unroll
             for (int q = 0; q < NOUT_PAD / 4; q++) {
                 const float4 v = *reinterpret_cast<const float4*>(s_feat + lane * fs + 4 * q);
-                f[4 * q] = v.x;
-                f[4 * q + 1] = v.y;
-                f[4 * q + 2] = v.z;
-                f[4 * q + 3] = v.w;
+                ff[4 * q] = pair_of(v.x, v.x);
+                ff[4 * q + 1] = pair_of(v.y, v.y);
+                ff[4 * q + 2] = pair_of(v.z, v.z);
+                ff[4 * q + 3] = pair_of(v.w, v.w);
             }
             const float g = s_g[lane];
-            float grad_f[NOUT_PAD];
+            uint64_t gf[NOUT_PAD / 2];  // (grad_f_2k, grad_f_2k+1)
             #pragma unroll
-            for (int i = 0; i < NOUT_PAD; i++) grad_f[i] = 0.0f;
+            for (int k = 0; k < NOUT_PAD / 2; k++) gf[k] = pair_of(0.0f, 0.0f);
             for (int j0 = 0; j0 < w_pad; j0 += 4) {
                 float pre[4];
                 #pragma unroll
-                for (int r = 0; r < 4; r++) {
-                    const float4* w = reinterpret_cast<const float4*>(s_w0 + (j0 + r) * NOUT_PAD);
-                    // the forward's accumulation order; the padding columns (zero weight, zero feature) add +0, which
-                    // changes at most the sign of a zero and so neither the ReLU mask nor relu(pre)
-                    float p = s_b0[j0 + r];
+                for (int h = 0; h < 2; h++) {
+                    const int j = j0 + 2 * h;
+                    // rows j and j + 1 in the forward's accumulation order; the padding columns (zero weight, zero
+                    // feature) add +0, which changes at most the sign of a zero and so neither the ReLU mask nor relu(pre)
+                    const float4* wp = reinterpret_cast<const float4*>(s_w0p + (j / 2) * 2 * NOUT_PAD);
+                    uint64_t p = pair_of(s_b0[j], s_b0[j + 1]);
                     #pragma unroll
-                    for (int q = 0; q < NOUT_PAD / 4; q++) {
-                        const float4 wq = w[q];
-                        p = __fmaf_rn(wq.x, f[4 * q], p);
-                        p = __fmaf_rn(wq.y, f[4 * q + 1], p);
-                        p = __fmaf_rn(wq.z, f[4 * q + 2], p);
-                        p = __fmaf_rn(wq.w, f[4 * q + 3], p);
+                    for (int q = 0; q < NOUT_PAD / 2; q++) {
+                        const float4 w2 = wp[q];  // (w[j][2q], w[j+1][2q], w[j][2q+1], w[j+1][2q+1])
+                        p = fma_pair(pair_of(w2.x, w2.y), ff[2 * q], p);
+                        p = fma_pair(pair_of(w2.z, w2.w), ff[2 * q + 1], p);
                     }
-                    pre[r] = p;
+                    const float2 pv = split_pair(p);
+                    pre[2 * h] = pv.x;
+                    pre[2 * h + 1] = pv.y;
                     // branch-free: a zero pre-activation gradient adds +0 (the warp has some positive lane anyway)
-                    const float grad_pre = p > 0.0f ? __fmul_rn(g, s_w1[j0 + r]) : 0.0f;
                     #pragma unroll
-                    for (int q = 0; q < NOUT_PAD / 4; q++) {
-                        const float4 wq = w[q];
-                        grad_f[4 * q] = __fmaf_rn(grad_pre, wq.x, grad_f[4 * q]);
-                        grad_f[4 * q + 1] = __fmaf_rn(grad_pre, wq.y, grad_f[4 * q + 1]);
-                        grad_f[4 * q + 2] = __fmaf_rn(grad_pre, wq.z, grad_f[4 * q + 2]);
-                        grad_f[4 * q + 3] = __fmaf_rn(grad_pre, wq.w, grad_f[4 * q + 3]);
+                    for (int r = 0; r < 2; r++) {
+                        const float pr = r == 0 ? pv.x : pv.y;
+                        const float grad_pre = pr > 0.0f ? __fmul_rn(g, s_w1[j + r]) : 0.0f;
+                        const uint64_t gp = pair_of(grad_pre, grad_pre);
+                        const float4* w = reinterpret_cast<const float4*>(s_w0 + (j + r) * NOUT_PAD);
+                        #pragma unroll
+                        for (int q = 0; q < NOUT_PAD / 4; q++) {
+                            const float4 wq = w[q];
+                            gf[2 * q] = fma_pair(gp, pair_of(wq.x, wq.y), gf[2 * q]);
+                            gf[2 * q + 1] = fma_pair(gp, pair_of(wq.z, wq.w), gf[2 * q + 1]);
+                        }
                     }
                 }
                 *reinterpret_cast<float4*>(s_pre + lane * ps + j0) = make_float4(pre[0], pre[1], pre[2], pre[3]);
             }
+            #pragma unroll
+            for (int k = 0; k < NOUT_PAD / 2; k++) {
+                const float2 v = split_pair(gf[k]);
+                grad_f[2 * k] = v.x;
+                grad_f[2 * k + 1] = v.y;
+            }
+        }
+        {
             // this sample's scaled feature gradient to grad_rows (read by the scatter kernel)
             if (lane < n_rows) {
                 float* out = a.grad_rows + static_cast<size_t>(base + lane) * n_out;
@@ -1037,27 +1082,53 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
         // [pre > 0] g with the features); the tiles of the first columns also sum grad_b0 and grad_w1 of their rows
         for (int tile = lane; tile < n_tiles; tile += 32) {
             const int j0 = (tile / n_itiles) * 4, i0 = (tile % n_itiles) * TI;
-            float sum[4][TI] = {};
-            float sum_b0[4] = {}, sum_w1[4] = {};
+            // paired sums: sum2[r][k] = (sum[r][2k], sum[r][2k+1]), b0s / w1s = rows (0, 1) and (2, 3)
+            uint64_t sum2[4][TI / 2];
+            #pragma unroll
+            for (int r = 0; r < 4; r++) {
+                #pragma unroll
+                for (int k = 0; k < TI / 2; k++) sum2[r][k] = pair_of(0.0f, 0.0f);
+            }
+            uint64_t b0s[2] = {pair_of(0.0f, 0.0f), pair_of(0.0f, 0.0f)}, w1s[2] = {pair_of(0.0f, 0.0f), pair_of(0.0f, 0.0f)};
             for (int s = 0; s < n_rows; s++) {
                 const float4 p = *reinterpret_cast<const float4*>(s_pre + s * ps + j0);
-                float fc[TI];
+                uint64_t fc[TI / 2];
                 #pragma unroll
-                for (int c = 0; c < TI; c += 2) {
-                    const float2 v = *reinterpret_cast<const float2*>(s_feat + s * fs + i0 + c);
-                    fc[c] = v.x;
-                    fc[c + 1] = v.y;
+                for (int k = 0; k < TI / 2; k++) {
+                    const float2 v = *reinterpret_cast<const float2*>(s_feat + s * fs + i0 + 2 * k);
+                    fc[k] = pair_of(v.x, v.y);
                 }
                 const float gs = s_g[s];
                 const float av[4] = {p.x > 0.0f ? gs : 0.0f, p.y > 0.0f ? gs : 0.0f, p.z > 0.0f ? gs : 0.0f, p.w > 0.0f ? gs : 0.0f};
-                const float pr[4] = {p.x, p.y, p.z, p.w};
                 #pragma unroll
                 for (int r = 0; r < 4; r++) {
+                    const uint64_t a2 = pair_of(av[r], av[r]);
                     #pragma unroll
-                    for (int c = 0; c < TI; c++) sum[r][c] = __fmaf_rn(av[r], fc[c], sum[r][c]);
-                    sum_b0[r] = __fadd_rn(sum_b0[r], av[r]);
-                    sum_w1[r] = __fmaf_rn(gs, fmaxf(pr[r], 0.0f), sum_w1[r]);
+                    for (int k = 0; k < TI / 2; k++) sum2[r][k] = fma_pair(a2, fc[k], sum2[r][k]);
                 }
+                const uint64_t g2 = pair_of(gs, gs);
+                b0s[0] = add_pair(b0s[0], pair_of(av[0], av[1]));
+                b0s[1] = add_pair(b0s[1], pair_of(av[2], av[3]));
+                w1s[0] = fma_pair(g2, pair_of(fmaxf(p.x, 0.0f), fmaxf(p.y, 0.0f)), w1s[0]);
+                w1s[1] = fma_pair(g2, pair_of(fmaxf(p.z, 0.0f), fmaxf(p.w, 0.0f)), w1s[1]);
+            }
+            float sum[4][TI], sum_b0[4], sum_w1[4];
+            #pragma unroll
+            for (int r = 0; r < 4; r++) {
+                #pragma unroll
+                for (int k = 0; k < TI / 2; k++) {
+                    const float2 v = split_pair(sum2[r][k]);
+                    sum[r][2 * k] = v.x;
+                    sum[r][2 * k + 1] = v.y;
+                }
+            }
+            #pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const float2 b = split_pair(b0s[h]), w = split_pair(w1s[h]);
+                sum_b0[2 * h] = b.x;
+                sum_b0[2 * h + 1] = b.y;
+                sum_w1[2 * h] = w.x;
+                sum_w1[2 * h + 1] = w.y;
             }
             #pragma unroll
             for (int r = 0; r < 4; r++) {
