@@ -636,7 +636,7 @@ def run_b200(args) -> None:
     if rank == 0 and world == 1 and not args.skip_contention:
         result['contention'] = measure_contention(args, device, physical)
     if rank == 0 and world == 1 and not args.skip_nerf_mlp:
-        result['nerf_mlp'] = measure_nerf_mlp(device, physical)
+        result['nerf_mlp'] = measure_nerf_mlp(device, physical, n=args.nerf_mlp_samples)
     if not args.skip_e2e:
         result['e2e'] = measure_e2e(step, args, world, start_exchange, exchange, barrier)
     if not args.skip_train_step:
@@ -767,10 +767,17 @@ def measure_rows(device, iters: int = 10) -> dict:
 
 
 def measure_nerf_mlp(device, physical: int, iters: int = 10, n: int = 65536 * 32) -> dict:
-    """The NeRF MLP's inference forward over one training step's NeRF level (2,097,152 samples; the reference model's
-    widths, nerf_mlp.cu:440-455): the tcgen05 kernel (zf_nerf_mlp_forward_tc through the C ABI) and the cuBLAS chain of
-    ZipNeRFCudaBackend.NerfMlp, CUDA-event means over `iters` runs after 3 warm-ups, against the measured bf16 peak
-    (burst). Inputs (336 MB) are larger than L2."""
+    """The NeRF MLP over one training step's NeRF level (2,097,152 samples by default; the reference model's widths,
+    nerf_mlp.cu:440-455), CUDA-event means over `iters` runs after 3 warm-ups under the clock sampler:
+
+    * inference forward: the tcgen05 kernel (zf_nerf_mlp_forward_tc through the C ABI) against the folded layer chain
+      as cuBLAS bf16 GEMMs with bias + ReLU epilogues (`NerfMlp._forward`), against the measured bf16 peak (burst);
+    * training iteration (pack, training forward, backward with the packed-weight gradients unfolded into the
+      reference's parameters) through `ZipNeRFCudaBackend.NerfMlp`: the tcgen05 kernels (forward keeping v0-v2 and
+      their ReLU masks, data-gradient chain, TMA-fed weight-gradient GEMMs) against the cuBLAS chain with this
+      backend's ReLU-backward kernel (`_forward` / `_backward`).
+
+    Inputs (336 MB at the default size) are larger than L2."""
     import ZipNeRFCudaBackend as backend
     from zipnerf_b200 import capi, nerf_mlp as nm
     layout = nm.NerfMlpLayout()
@@ -781,11 +788,15 @@ def measure_nerf_mlp(device, physical: int, iters: int = 10, n: int = 65536 * 32
     inputs = torch.zeros(n, 96, dtype=torch.bfloat16, device=device)
     inputs[:, 64:91] = (torch.rand(n, 27, generator=gen) * 2 - 1).bfloat16().to(device)
     inputs[:, 95] = 1.0
+    grad_outputs = torch.zeros(n, 8, dtype=torch.bfloat16, device=device)
+    grad_outputs[:, :4] = torch.randn(n, 4, generator=gen).bfloat16().to(device)
     outputs = torch.empty(n, 8, dtype=torch.bfloat16, device=device)
     status = torch.zeros(1, dtype=torch.int32, device=device)
     packed = {k: v.to(device) for k, v in nm.pack(layout, params).items()}
     mlp = backend.NerfMlp(50, 64, 256, 256, 4)
-    flat = mlp.pack(params.to(device))
+    device_params = params.to(device)
+    grad_params = torch.zeros_like(device_params)
+    flat = mlp.pack(device_params)
     peaks = measured_peaks()
     flop = 2 * nm.MACS_PER_SAMPLE * n
 
@@ -801,17 +812,33 @@ def measure_nerf_mlp(device, physical: int, iters: int = 10, n: int = 65536 * 32
         torch.cuda.synchronize()
         return start.elapsed_time(end) / iters
 
-    out = {'config': f'{n} samples (65,536 rays x 32 intervals); density 64 x 56, combined 256 x 96, skip 8 x 96, view 2 x 256 x 256, rgb 8 x 256; '
-                     'bf16 operands, fp32 accumulation', 'flop_per_sample': 2 * nm.MACS_PER_SAMPLE}
+    def train_tc():
+        p = mlp.pack(device_params)
+        _, context = mlp.forward(features, inputs, p, True)
+        mlp.backward(grad_outputs, features, p, context, device_params, grad_params)
+
+    def train_chain():
+        p = mlp.pack(device_params)
+        _, context = mlp._forward(features, inputs, p, True)
+        mlp._backward(grad_outputs, features, p, context, device_params, grad_params, backend.relu_backward_)
+
+    out = {'config': f'{n} samples; density 64 x 56, combined 256 x 96, skip 8 x 96, view 2 x 256 x 256, rgb 8 x 256; '
+                     'bf16 operands, fp32 accumulation (fp32 weight gradients)', 'flop_per_sample': 2 * nm.MACS_PER_SAMPLE,
+           'training_flop_per_sample': 3 * 2 * nm.MACS_PER_SAMPLE}
     with ClockSampler(physical) as clocks:
         for name, fn in (('tcgen05', lambda: capi.nerf_mlp_forward_tc(features, inputs, packed, outputs, status)),
-                         ('cublas_chain', lambda: mlp.forward(features, inputs, flat, False))):
+                         ('cublas_chain', lambda: mlp._forward(features, inputs, flat, False))):
             ms = time_ms(fn)
             tflops = flop / (ms * 1e-3) / 1e12
             out[name] = {'ms': ms, 'tflops': tflops, 'frac_of_bf16_peak': tflops / peaks['bf16_tflops']}
+        for name, fn in (('training_tcgen05', train_tc), ('training_cublas_chain', train_chain)):
+            ms = time_ms(fn)
+            tflops = 3 * flop / (ms * 1e-3) / 1e12
+            out[name] = {'ms': ms, 'tflops': tflops, 'frac_of_bf16_peak': tflops / peaks['bf16_tflops']}
     out['clocks'] = clocks.summary()
-    out['tcgen05_status'] = int(status.item())
+    out['tcgen05_status'] = int(mlp.status(device).item()) | int(status.item())
     out['ratio'] = out['cublas_chain']['ms'] / out['tcgen05']['ms']
+    out['training_ratio'] = out['training_cublas_chain']['ms'] / out['training_tcgen05']['ms']
     return out
 
 
@@ -895,8 +922,8 @@ def measure_train_step(args, world: int, rank: int, device, barrier, steps: int 
             'loss_sums_last_step': losses,
             'config': f'{args.rays} rays per GPU x (64 + 64 + 32) intervals; grids of the reference model (6 and 8 levels x 1 feature, 10 x 4, '
                       f'scale 2, 2^21); rays from a 185-view 1296 x 840 pool; gradient all-reduce over {world} GPU(s) and Adam; the NeRF MLP '
-                      'with the reference interface: forward on the tcgen05 kernel, backward as cuBLAS bf16 GEMMs with this backend\'s '
-                      'ReLU-backward kernel'}
+                      'with the reference interface on the tcgen05 kernels: forward (keeping v0-v2 and their ReLU masks), data-gradient '
+                      'chain and TMA-fed weight-gradient GEMMs'}
 
 
 def measure_e2e(step: Step, args, world: int, start_exchange, exchange, barrier) -> dict:
@@ -990,7 +1017,8 @@ def main() -> None:
     parser.add_argument('--skip-train-step', action='store_true', help='skip the timing of the full training step')
     parser.add_argument('--skip-reference-cuda', action='store_true', help="skip the timing of the reference's own CUDA kernels")
     parser.add_argument('--skip-contention', action='store_true', help='skip the config-5 contention timing')
-    parser.add_argument('--skip-nerf-mlp', action='store_true', help='skip the timing of the NeRF MLP forward')
+    parser.add_argument('--skip-nerf-mlp', action='store_true', help='skip the timing of the NeRF MLP (inference forward and training iteration)')
+    parser.add_argument('--nerf-mlp-samples', type=int, default=65536 * 32, help='samples of the NeRF MLP timing (one step\'s NeRF level by default)')
     parser.add_argument('--skip-render', action='store_true', help='skip the timing of the config-3 frame render')
     parser.add_argument('--half-wire', choices=['fp16', 'fp32'], default='fp16',
                         help='wire format of the NeRF grid\'s fp16 gradients in the all-reduce (fp16: pre-divided fp16 sums; fp32: fp32 copies)')
