@@ -115,7 +115,7 @@ struct PackedMlp {
 // (shared memory, or none), ReLU, bf16, into row `row` of a K-major operand at column k_first (and into global memory
 // at `global_row` when given; and, when mask_words is given, bit c % 32 of word c / 32 set where column c came out
 // positive, N a multiple of 32)
-template <int N>
+template <int N, bool kMasks = false>
 __device__ __forceinline__ void relu_columns(const uint32_t taddr, const float* bias, uint8_t* dst, const int row, const int k_total, const int k_first,
                                              uint16_t* global_row, uint32_t* mask_words = nullptr) {
     uint32_t bits[N / 32 > 0 ? N / 32 : 1] = {};
@@ -139,7 +139,7 @@ __device__ __forceinline__ void relu_columns(const uint32_t taddr, const float* 
                 hi += bias[j + 2 * q + 1];
             }
             words[q] = pack_bf16x2_relu(lo, hi);
-            if constexpr (N >= 32) {
+            if constexpr (kMasks && N >= 32) {
                 const uint32_t pair = (__uint_as_float(words[q] << 16) > 0.0f ? 1u : 0u) | (__uint_as_float(words[q] & 0xFFFF0000u) > 0.0f ? 2u : 0u);
                 bits[(j + 2 * q) / 32] |= pair << ((j + 2 * q) % 32);
             }
@@ -148,10 +148,10 @@ __device__ __forceinline__ void relu_columns(const uint32_t taddr, const float* 
         *reinterpret_cast<uint4*>(dst + canonical_offset(row, k_first + j, k_total)) = out;
         if (global_row != nullptr) *reinterpret_cast<uint4*>(global_row + k_first + j) = out;
     }
-    if constexpr (N == 32) {
+    if constexpr (kMasks && N == 32) {
         if (mask_words != nullptr) *mask_words = bits[0];
     }
-    else if constexpr (N == 64) {
+    else if constexpr (kMasks && N == 64) {
         if (mask_words != nullptr) *reinterpret_cast<uint2*>(mask_words) = make_uint2(bits[0], bits[1]);
     }
 }
@@ -166,7 +166,9 @@ __device__ __forceinline__ void input_word(const int i, const int tid, const uin
     constexpr int kFeatureWords = kTileRows * (kFeaturesK / 8);
     src = nullptr;
     if (q < kFeatureWords) {
-        const int r = q / (kFeaturesK / 8), c = q % (kFeaturesK / 8);
+        // eight consecutive words: one 16-byte chunk of eight consecutive rows, which is one core matrix (128
+        // contiguous bytes of shared memory, all 32 banks)
+        const int r = (q / (8 * (kFeaturesK / 8))) * 8 + q % 8, c = (q / 8) % (kFeaturesK / 8);
         if (first + r < n && c < kFeatures / 8) src = reinterpret_cast<const uint4*>(features + (first + r) * features_stride) + c;
         dst_offset = canonical_offset(r, 8 * c, kFeaturesK);
         to_act = true;
@@ -223,6 +225,9 @@ __device__ __forceinline__ Stage weight_stage(const PackedMlp& w, const int s) {
 
 // features [n, 56] bf16 (row stride features_stride), inputs [n, 96] bf16 (row stride inputs_stride; the direction
 // block in columns 64-95 is read, the hidden layer written to columns 0-63), outputs [n, 8] bf16
+// kRecord: the training forward, which writes the record (activations non-null); the inference forward compiles
+// without the mask bits' work in its epilogues
+template <bool kRecord>
 __global__ void __launch_bounds__(kThreads, 1)
     fz_nerf_mlp_forward_kernel(const uint16_t* __restrict__ features, const int64_t features_stride, uint16_t* __restrict__ inputs,
                                const int64_t inputs_stride, const PackedMlp w, uint16_t* __restrict__ outputs, uint16_t* __restrict__ activations,
@@ -410,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool more = tile + gridDim.x < n_tiles;
             // E0: h + b_density, ReLU -> this group's columns of h in the inputs (shared and global)
             if (!(ok = accumulator_ready())) break;
-            relu_columns<kHiddenColumns>(lanes + (layer & 1u) * kRegionColumns + kHiddenColumns * c, bias + kHiddenColumns * c, in, row, kInputs,
+            relu_columns<kHiddenColumns, kRecord>(lanes + (layer & 1u) * kRegionColumns + kHiddenColumns * c, bias + kHiddenColumns * c, in, row, kInputs,
                                          kHiddenColumns * c, valid ? inputs + sample * inputs_stride : nullptr,
                                          masks != nullptr && valid ? masks + 3 * n * kMaskWords + sample * kHiddenMaskWords + c : nullptr);
             publish(h_bar);
@@ -425,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint16_t* kept = activations != nullptr && valid ? activations + (static_cast<int64_t>(k - 1) * n + sample) * kView : nullptr;
                 uint32_t* kept_mask = masks != nullptr && valid ? masks + (static_cast<int64_t>(k - 1) * n + sample) * kMaskWords : nullptr;
                 for (int j = c; j < kChunks; j += kChunkGroups) {
-                    relu_columns<kSlice>(lanes + (layer & 1u) * kRegionColumns + kSlice * j, b != nullptr ? b + kSlice * j : nullptr, act, row, kView,
+                    relu_columns<kSlice, kRecord>(lanes + (layer & 1u) * kRegionColumns + kSlice * j, b != nullptr ? b + kSlice * j : nullptr, act, row, kView,
                                          kSlice * j, kept, kept_mask != nullptr ? kept_mask + 2 * j : nullptr);
                     publish(chunk_bar(j));
                 }
@@ -479,7 +484,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 cudaError_t launch_forward(const uint16_t* features, const int64_t features_stride, uint16_t* inputs, const int64_t inputs_stride, const PackedMlp& w,
                            uint16_t* outputs, uint16_t* activations, const int64_t n, int* status, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(fz_nerf_mlp_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    const auto kernel = activations != nullptr ? fz_nerf_mlp_forward_kernel<true> : fz_nerf_mlp_forward_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
     int device = 0, n_sms = 0;
     e = cudaGetDevice(&device);
@@ -487,8 +493,7 @@ cudaError_t launch_forward(const uint16_t* features, const int64_t features_stri
     if (e != cudaSuccess) return e;
     const int64_t n_tiles = (n + kTileRows - 1) / kTileRows;
     const unsigned int blocks = static_cast<unsigned int>(n_tiles < n_sms ? n_tiles : n_sms);
-    fz_nerf_mlp_forward_kernel<<<blocks, kThreads, kSmemBytes, stream>>>(features, features_stride, inputs, inputs_stride, w, outputs, activations, n,
-                                                                         status);
+    kernel<<<blocks, kThreads, kSmemBytes, stream>>>(features, features_stride, inputs, inputs_stride, w, outputs, activations, n, status);
     return cudaGetLastError();
 }
 
