@@ -150,13 +150,13 @@ def test_tensor_core_forward_rows_are_independent_of_the_batch(cuda_device):
     assert torch.equal(part_inputs.view(torch.int16), inputs[:m].view(torch.int16))
 
 
-@pytest.mark.parametrize('n', [4133, 57_003])
+@pytest.mark.parametrize('n', [5, 8, 136, 4133, 57_003])
 def test_tensor_core_backward_matches_the_gemm_chain(cuda_device, n):
     """NerfMlp.backward on the tensor cores (zf_nerf_mlp_backward_tc: the data-gradient kernel, then the weight-gradient
     GEMMs over the samples) against the same folded chain as bf16 GEMMs through torch (`_backward`, fp32 weight
     gradients) on the same forward context: feature and parameter gradients within 1e-2 relative (bf16 intermediate
-    gradients, other summation orders), and no timed-out wait. n = 57,003 gives every CTA several tiles and a ragged
-    last tile."""
+    gradients, other summation orders), and no timed-out wait. n = 5 and 8 are less than one tile, 136 a partial second
+    tile, 4,133 and 57,003 ragged last tiles; 57,003 gives every CTA several tiles."""
     import ZipNeRFCudaBackend as backend
     from zipnerf_b200 import nerf_mlp as nm
     layout = nm.NerfMlpLayout()
