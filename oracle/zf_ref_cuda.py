@@ -2,7 +2,7 @@
 
 oracle/ref_cuda/build.py compiles one library per grid layout (oracle/_ref/cuda/libzfref_<variant>.so) where the
 reference sources exist; the libraries travel to the GPU box with oracle/_ref. The GPU tests use them as the bit-exact
-checker of the product kernels, and tests/bench_vs_reference_cuda.py times them. Takes PyTorch CUDA tensors.
+checker of the product kernels, and bench.py's reference_cuda leg times them. Takes PyTorch CUDA tensors.
 """
 from __future__ import annotations
 

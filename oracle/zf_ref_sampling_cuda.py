@@ -4,7 +4,7 @@ INFRASTRUCTURE ONLY).
 oracle/ref_cuda/build.py compiles B/sampling/src/sampling_api.cu and B/optimizer/src/optimizer_api.cu (unmodified, with
 the launchers of oracle/ref_cuda/ref_sampling.cu) into oracle/_ref/cuda/libzfref_sampling.so, which travels to the GPU
 box with oracle/_ref. The GPU tests use it as the bit-exact checker of the product's sampling and Adam kernels, and
-tests/bench_vs_reference_cuda.py times both. Takes PyTorch CUDA tensors; allocates outputs as the reference's
+bench.py's rows leg times both. Takes PyTorch CUDA tensors; allocates outputs as the reference's
 wrappers do (B/ = ZipNeRFCudaBackend/ZipNeRFCudaBackend/).
 """
 from __future__ import annotations
