@@ -71,10 +71,10 @@ def build_library(jobs: int | None = None, force: bool = False, subset: set | No
             wanted.append(obj)
             if force or _stale(obj, [inst, *deps]):
                 steps.append([NVCC, *NVCC_FLAGS, f'-DZF_INST_F={features}', f'-DZF_INST_PAD={pad}', '-c', str(inst), '-o', str(obj)])
-    # the C ABI translation units: featurizer objects, the sampling kernels, the Adam step, the MLP's ReLU backward and
-    # tensor-core forward
+    # the C ABI translation units: featurizer objects, the sampling kernels, the Adam step, the MLP's ReLU backward, its
+    # tensor-core forward and backward, and its pack and unfold
     abi_objects = []
-    for name in ['fz_capi', 'fz_sampling', 'fz_optim', 'fz_mlp', 'fz_nerf_mlp', 'fz_nerf_mlp_backward']:
+    for name in ['fz_capi', 'fz_sampling', 'fz_optim', 'fz_mlp', 'fz_nerf_mlp', 'fz_nerf_mlp_backward', 'fz_nerf_mlp_pack']:
         source, obj = CSRC / f'{name}.cu', BUILD / f'{name}.o'
         abi_objects.append(obj)
         if force or _stale(obj, [source, *deps]):

@@ -21,7 +21,7 @@ EXPORTED = ['zf_featurizer_create', 'zf_featurizer_destroy', 'zf_featurizer_n_ou
             'zf_direction_block_width', 'zf_initialize_rays', 'zf_view_rays', 'zf_generate_rays', 'zf_sample_uniforms',
             'zf_composite_and_resample', 'zf_train_final', 'zf_composite_final', 'zf_adam_create', 'zf_adam_destroy', 'zf_adam_step',
             'zf_adam_state', 'zf_relu_backward_bf16', 'zf_nerf_mlp_activations_size', 'zf_nerf_mlp_forward_tc', 'zf_nerf_mlp_backward_workspace_size',
-            'zf_nerf_mlp_backward_tc']
+            'zf_nerf_mlp_backward_tc', 'zf_nerf_mlp_parameter_count', 'zf_nerf_mlp_pack', 'zf_nerf_mlp_unfold_grads']
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -113,6 +113,16 @@ class zf_nerf_mlp_grads(ctypes.Structure):
     _fields_ = [(name, _p) for name in ('density', 'density_bias', 'combined', 'skip', 'view_1', 'view_1_bias', 'view_2', 'view_2_bias', 'rgb')]
 
 
+# the targets of zf_nerf_mlp_pack: the row-major section, the tensor-core forward's, the transposed weights
+NERF_MLP_PACK_TARGETS = ('density', 'density_bias', 'combined', 'skip', 'view_1', 'view_1_bias', 'view_2', 'view_2_bias', 'rgb',
+                         'tc_density', 'tc_density_bias', 'tc_combined', 'tc_skip', 'tc_view_1', 'tc_view_1_bias', 'tc_view_2', 'tc_view_2_bias',
+                         'tc_rgb', 'rgb_t', 'view_2_t', 'view_1_t', 'combined_t', 'skip_t', 'density_t')
+
+
+class zf_nerf_mlp_packed(ctypes.Structure):
+    _fields_ = [(name, _p) for name in NERF_MLP_PACK_TARGETS]
+
+
 class ZfError(RuntimeError):
     def __init__(self, code: int, message: str) -> None:
         super().__init__(message)
@@ -195,6 +205,12 @@ def load() -> ctypes.CDLL:
     lib.zf_nerf_mlp_backward_workspace_size.restype = _i64
     lib.zf_nerf_mlp_backward_tc.argtypes = [_p, _p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _p, _i64, _i64, _p, _p]
     lib.zf_nerf_mlp_backward_tc.restype = ctypes.c_int
+    lib.zf_nerf_mlp_parameter_count.argtypes = []
+    lib.zf_nerf_mlp_parameter_count.restype = _i64
+    lib.zf_nerf_mlp_pack.argtypes = [_p, _p, _p]
+    lib.zf_nerf_mlp_pack.restype = ctypes.c_int
+    lib.zf_nerf_mlp_unfold_grads.argtypes = [_p, _p, _p, _p]
+    lib.zf_nerf_mlp_unfold_grads.restype = ctypes.c_int
     _lib = lib
     return lib
 
@@ -533,6 +549,33 @@ def nerf_mlp_backward_tc(grad_outputs, features, inputs, activations, packed_t: 
     check(load().zf_nerf_mlp_backward_tc(_ptr(grad_outputs), _ptr(features), features.stride(0), _ptr(inputs), inputs.stride(0), _ptr(activations),
                                          ctypes.byref(w), _ptr(grad_features), grad_features.stride(0), ctypes.byref(g), _ptr(workspace),
                                          workspace.numel() * workspace.element_size(), features.shape[0], _ptr(status), _stream(stream)))
+
+
+def nerf_mlp_pack(params, targets: dict, stream=None) -> None:
+    """zf_nerf_mlp_pack: the fp32 parameters (a CUDA tensor of at least zf_nerf_mlp_parameter_count() elements) into the
+    given targets, device addresses by NERF_MLP_PACK_TARGETS name (missing names: not written); the caller sizes them
+    (zipnerf_b200.nerf_mlp.NerfMlp lays them out in its packed buffer)."""
+    import torch
+    if not isinstance(params, torch.Tensor) or not params.is_cuda or params.dtype != torch.float32 or params.numel() < load().zf_nerf_mlp_parameter_count():
+        raise ValueError('params must be a float32 CUDA tensor of the reference model widths\' parameter count')
+    out = zf_nerf_mlp_packed(*[targets.get(name) for name in NERF_MLP_PACK_TARGETS])
+    check(load().zf_nerf_mlp_pack(_ptr(params), ctypes.byref(out), _stream(stream)))
+
+
+def nerf_mlp_unfold_grads(params, grads: dict, grad_params, stream=None) -> None:
+    """zf_nerf_mlp_unfold_grads: grad_params (float32, the parameter layout) += the unfold of the packed-weight gradients
+    (fp32 CUDA tensors of NERF_MLP_GRAD_SHAPES)."""
+    import torch
+    n = load().zf_nerf_mlp_parameter_count()
+    for t, what in ((params, 'params'), (grad_params, 'grad_params')):
+        if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != torch.float32 or t.numel() < n or not t.is_contiguous():
+            raise ValueError(f'{what} must be a contiguous float32 CUDA tensor of at least {n} elements')
+    for name, shape in NERF_MLP_GRAD_SHAPES.items():
+        t = grads.get(name)
+        if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != torch.float32 or tuple(t.shape) != shape or not t.is_contiguous():
+            raise ValueError(f'grads[{name!r}] must be a contiguous float32 CUDA tensor of shape {shape}')
+    g = zf_nerf_mlp_grads(*[grads[name].data_ptr() for name, _ in zf_nerf_mlp_grads._fields_])
+    check(load().zf_nerf_mlp_unfold_grads(_ptr(params), ctypes.byref(g), _ptr(grad_params), _stream(stream)))
 
 
 class CAdam:

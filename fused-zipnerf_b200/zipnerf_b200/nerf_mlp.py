@@ -244,11 +244,13 @@ class NerfMlp:
     buffer is): the folded weights and biases row-major, and, for the reference model's widths, the same fold in the
     tensor-core kernel's order (`pack`, K-sliced canonical bf16 weights and fp32 biases stored bit for bit).
 
-    forward: the tcgen05 kernel zf_nerf_mlp_forward_tc (one persistent kernel for all layers; training keeps v0, v1,
-    v2 for the backward), for the reference model's widths; other widths run the folded bf16 layer chain as GEMMs with
-    bias + ReLU epilogues (cuBLASLt through torch). backward: the folded chain's GEMMs (cuBLAS through torch) with this
-    backend's ReLU backward and bias gradient (`relu_backward_`, zf_mlp.h); the packed-weight gradients go back to the
-    fp32 parameters through autograd of the fold.
+    For the reference model's widths every step runs on this backend's kernels (zf_mlp.h): `pack` is one launch of
+    zf_nerf_mlp_pack (the fold in the reference's fp32 order); `forward` the tcgen05 kernel zf_nerf_mlp_forward_tc (one
+    persistent kernel for all layers; training keeps v0, v1, v2 and their ReLU masks for the backward); `backward` the
+    tcgen05 data-gradient and weight-gradient kernels (zf_nerf_mlp_backward_tc), then the unfold of the packed-weight
+    gradients into the fp32 parameters (zf_nerf_mlp_unfold_grads). Other widths run the folded bf16 layer chain as GEMMs
+    with bias + ReLU epilogues (cuBLASLt through torch), this backend's ReLU backward and bias gradient
+    (`relu_backward_`), and the unfold as autograd of the fold.
 
     `_forward` and `_backward` hold the GEMM layer chain for any device with `relu_backward` given (the CPU tests pass a
     torch restatement of the kernel's contract); the public methods take CUDA tensors only, as the reference's
@@ -277,6 +279,17 @@ class NerfMlp:
                 n += math.prod(self._tc_shapes[name])
         self.packed_size = n
         self._status = {}
+        if self.tensor_cores:
+            # zf_nerf_mlp_pack's targets: element offsets in the packed buffer (the row-major section, the tensor-core
+            # forward's, the transposed weights), and the packed-weight gradients as views of one flat fp32 buffer
+            self._pack_targets = {name: self._offsets[name] for name in PACKED_ORDER}
+            self._pack_targets |= {'tc_' + name: self._tc_offsets[name] for name in PACKED_ORDER}
+            self._pack_targets |= {name: self._tc_offsets[name] for name in TRANSPOSED_ORDER}
+            self._grad_offsets, g = {}, 0
+            for name in PACKED_ORDER:
+                self._grad_offsets[name] = g
+                g += math.prod(self._tc_shapes[name])
+            self._grad_numel = g
 
     @property
     def n_features(self) -> int:
@@ -300,7 +313,14 @@ class NerfMlp:
         if not self.tensor_cores:
             folded = self._fold(params)
             return torch.cat([folded[name].reshape(-1).to(torch.bfloat16) for name in PACKED_ORDER])
-        # one fold in the kernel's shapes; the row-major section is its leading rows and columns
+        if params.is_cuda:
+            # one launch: zf_nerf_mlp_pack writes every section of the packed buffer
+            from zipnerf_b200 import capi
+            packed = torch.empty(self.packed_size, dtype=torch.bfloat16, device=params.device)
+            base = packed.data_ptr()
+            capi.nerf_mlp_pack(params, {name: base + 2 * offset for name, offset in self._pack_targets.items()})
+            return packed
+        # on the CPU: one fold in the kernel's shapes; the row-major section is its leading rows and columns
         folded = fold(self.layout, params[:self.layout.numel])
         parts = [folded[name][tuple(slice(0, d) for d in self._shapes[name])].reshape(-1).to(torch.bfloat16) for name in PACKED_ORDER]
         tc = pack_folded(folded)
@@ -402,7 +422,7 @@ class NerfMlp:
 
     def _backward_tc(self, grad_outputs, features, packed, context, params, grad_params) -> torch.Tensor:
         """The backward on the tensor cores (zf_nerf_mlp_backward_tc: the data-gradient chain and the packed-weight
-        gradients in fp32), then the unfold of the packed-weight gradients into the parameters by autograd of the fold."""
+        gradients in fp32), then the unfold of the packed-weight gradients into the parameters (zf_nerf_mlp_unfold_grads)."""
         from zipnerf_b200 import capi
         if len(context) != 4 or packed.numel() != self.packed_size:
             raise RuntimeError('ZipNeRF: invalid nerf mlp backward inputs')
@@ -417,15 +437,14 @@ class NerfMlp:
             raise RuntimeError('ZipNeRF: nerf mlp backward needs the context of the tensor-core forward')
         activations = base.as_strided((record_elements,), (1,))
         grad_features = torch.empty(n, self.n_features, dtype=torch.bfloat16, device=features.device)
-        grads = {name: torch.zeros(shape, device=features.device) for name, shape in capi.NERF_MLP_GRAD_SHAPES.items()}
+        flat = torch.zeros(self._grad_numel, device=features.device)
+        grads = {name: flat[self._grad_offsets[name]:self._grad_offsets[name] + math.prod(shape)].view(shape)
+                 for name, shape in capi.NERF_MLP_GRAD_SHAPES.items()}
         workspace = torch.empty(max(capi.load().zf_nerf_mlp_backward_workspace_size(n), 16), dtype=torch.uint8, device=features.device)
         capi.nerf_mlp_backward_tc(grad_outputs, features, inputs, activations, self._tc_weights(packed, TRANSPOSED_ORDER), grad_features, grads,
                                   workspace, self.status(features.device))
-        with torch.enable_grad():
-            p = params[:self.layout.numel].detach().float().requires_grad_()
-            folded = fold(self.layout, p)
-            (grad,) = torch.autograd.grad([folded[name] for name in PACKED_ORDER], p, [grads[name] for name in PACKED_ORDER])
-        grad_params[:self.layout.numel] += grad.to(grad_params.dtype)
+        # the unfold into the reference's parameters, one launch (zf_nerf_mlp_unfold_grads)
+        capi.nerf_mlp_unfold_grads(params, grads, grad_params)
         return grad_features
 
     def backward(self, grad_outputs, features, packed, context, params, grad_params) -> torch.Tensor:

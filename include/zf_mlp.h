@@ -106,6 +106,54 @@ ZF_API int zf_nerf_mlp_backward_tc(const uint16_t* grad_outputs, const uint16_t*
                                    uint16_t* grad_features, int64_t grad_features_stride, const zf_nerf_mlp_grads* grads, void* workspace,
                                    int64_t workspace_bytes, int64_t n, int* status, struct CUstream_st* stream);
 
+/* Targets of zf_nerf_mlp_pack (any may be NULL: not written), the packed operands of NerfMlp::pack for the reference
+ * model's widths (nerf_mlp.cu:493-501, pack_kernel nerf_mlp.cu:186-234):
+ * - the layer chain's bf16 row-major weights: density [64, 56], density_bias [64], combined [256, 96], skip [8, 96],
+ *   view_1 and view_2 [256, 256], view_1_bias and view_2_bias [256], rgb [8, 256] (the reference's packed tensors);
+ * - the tensor-core forward's operands (zf_nerf_mlp_weights): bf16 weights in its K-slice order (density [64, 64],
+ *   combined [256, 96], skip [16, 96], view_1 and view_2 [256, 256], rgb [16, 256]) and the bf16-rounded biases as fp32;
+ * - the tensor-core backward's transposed operands (zf_nerf_mlp_weights_t). */
+typedef struct zf_nerf_mlp_packed {
+    uint16_t* density;
+    uint16_t* density_bias;
+    uint16_t* combined;
+    uint16_t* skip;
+    uint16_t* view_1;
+    uint16_t* view_1_bias;
+    uint16_t* view_2;
+    uint16_t* view_2_bias;
+    uint16_t* rgb;
+    uint16_t* tc_density;
+    float* tc_density_bias;
+    uint16_t* tc_combined;
+    uint16_t* tc_skip;
+    uint16_t* tc_view_1;
+    float* tc_view_1_bias;
+    uint16_t* tc_view_2;
+    float* tc_view_2_bias;
+    uint16_t* tc_rgb;
+    uint16_t* rgb_t;
+    uint16_t* view_2_t;
+    uint16_t* view_1_t;
+    uint16_t* combined_t;
+    uint16_t* skip_t;
+    uint16_t* density_t;
+} zf_nerf_mlp_packed;
+
+/* Elements of the fp32 parameter buffer of the reference model's widths (nerf_mlp_parameters(50, 64, 256, 256, 4),
+ * nerf_mlp.cu:440-455): 227,556. */
+ZF_API int64_t zf_nerf_mlp_parameter_count(void);
+
+/* NerfMlp::pack (nerf_mlp.cu:493-501) for the reference model's widths, one launch: folds the fp32 parameters (the
+ * bottleneck into the first view layer and the rgb skip rows, the biases of the layers reading the inputs into the bias
+ * lane) with the reference's fp32 multiply-add order and rounds to bf16, writing every given target. */
+ZF_API int zf_nerf_mlp_pack(const float* params, const zf_nerf_mlp_packed* out, struct CUstream_st* stream);
+
+/* The unfold of NerfMlp::backward (unpack_kernel, nerf_mlp.cu:236-284, 616-617) for the reference model's widths, one
+ * launch: grad_params (fp32, the parameter layout) += the chain rule of the fold applied to the packed-weight
+ * gradients of zf_nerf_mlp_backward_tc (fp32; the reference's bias gradients are bf16). */
+ZF_API int zf_nerf_mlp_unfold_grads(const float* params, const zf_nerf_mlp_grads* grads, float* grad_params, struct CUstream_st* stream);
+
 #ifdef __cplusplus
 }
 #endif

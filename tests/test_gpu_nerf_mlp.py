@@ -266,3 +266,45 @@ def test_tensor_core_backward_reads_features_with_their_own_stride(cuda_device):
     for name in capi.NERF_MLP_GRAD_SHAPES:
         a, b = results[0][1][name], results[1][1][name]
         assert ((a - b).norm() <= 1e-5 * b.norm() + 1e-30).item(), name
+
+
+def test_pack_kernel_matches_the_torch_fold(cuda_device):
+    """zf_nerf_mlp_pack (one launch) against the fold computed with torch on the CPU (`NerfMlp.pack` of host
+    parameters): every section of the packed buffer (row-major, the tensor-core forward's K-sliced weights and fp32
+    biases, the transposed weights) holds the same values; the folded columns (fp32 sums over the 256 bottleneck
+    outputs, in another order on each side) may differ by one bf16 step, everything copied is equal bit for bit."""
+    import ZipNeRFCudaBackend as backend
+    mlp, layout, params, _, _, _ = _backward_case(cuda_device, 8, 21)
+    on_device = mlp.pack(params).cpu()
+    on_host = mlp._pack(params.cpu())
+    assert on_device.shape == on_host.shape
+    a, b = on_device.float(), on_host.float()
+    steps = (a - b).abs() / b.abs().clamp_min(1e-30)
+    differing = (a != b)
+    assert float(steps[differing].max()) <= 2 ** -7 if bool(differing.any()) else True
+    # the copied tensors are equal bit for bit: view_1, view_2 and their biases in every section
+    for name in ('view_1', 'view_2', 'view_1_bias', 'view_2_bias'):
+        o, shape = mlp._offsets[name], mlp._shapes[name]
+        size = shape[0] * (shape[1] if len(shape) > 1 else 1)
+        assert torch.equal(on_device[o:o + size].view(torch.int16), on_host[o:o + size].view(torch.int16)), name
+    assert int(differing.sum()) < 0.01 * on_device.numel()
+
+
+def test_unfold_kernel_matches_autograd_of_the_fold(cuda_device):
+    """zf_nerf_mlp_unfold_grads (one launch) against autograd of the fold on random packed-weight gradients: every
+    parameter's gradient within 1e-5 relative (fp32 sums in other orders); it accumulates into the given buffer."""
+    from zipnerf_b200 import capi, nerf_mlp as nm
+    mlp, layout, params, _, _, _ = _backward_case(cuda_device, 8, 22)
+    gen = torch.Generator().manual_seed(5)
+    grads = {name: torch.randn(shape, generator=gen).to(cuda_device) for name, shape in capi.NERF_MLP_GRAD_SHAPES.items()}
+    with torch.enable_grad():
+        p = params.detach().double().requires_grad_()
+        folded = nm.fold(layout, p)
+        (expected,) = torch.autograd.grad([folded[name] for name in nm.PACKED_ORDER], p, [grads[name].double() for name in nm.PACKED_ORDER])
+    start = torch.full_like(params, 0.25)
+    got = start.clone()
+    capi.nerf_mlp_unfold_grads(params, grads, got)
+    torch.cuda.synchronize()
+    for name, _, _ in layout.parameters:
+        e, g = layout.view(expected, name), layout.view(got - start, name).double()
+        assert float((g - e).norm()) <= 1e-5 * float(e.norm()) + 1e-6, name

@@ -184,3 +184,25 @@ def test_whole_path_is_as_close_to_float64_as_the_reference(ref_mlp, cuda_device
     worse = {name: (errors['ours'][name], errors['reference'][name]) for name in truth
              if errors['ours'][name] > 1.25 * errors['reference'][name] + 1e-3}
     assert not worse, worse
+
+
+def test_pack_equals_the_references_bit_for_bit(ref_mlp, cuda_device):
+    """zf_nerf_mlp_pack folds with the reference pack_kernel's fp32 multiply-add order (nerf_mlp.cu:153-234), so the
+    row-major section of this backend's packed buffer equals the reference's packed tensors bit for bit (its segments
+    in the same order, each padded to 128 elements, nerf_mlp.cu:122,471-474), nonzero biases included."""
+    import ZipNeRFCudaBackend as backend
+    from zipnerf_b200 import nerf_mlp as nm
+    layout, params, _, _, _ = _case(cuda_device, 4096)
+    params = params.to(cuda_device)
+    ref, ours = ref_mlp.NerfMlp(50, 64, 256, 256, 4), backend.NerfMlp(50, 64, 256, 256, 4)
+    theirs, mine = ref.pack(params), ours.pack(params)
+    torch.cuda.synchronize()
+    offset = 0
+    for name in nm.PACKED_ORDER:
+        shape = ours._shapes[name]
+        size = shape[0] * (shape[1] if len(shape) > 1 else 1)
+        a = mine[ours._offsets[name]:ours._offsets[name] + size].view(torch.int16)
+        b = theirs[offset:offset + size].view(torch.int16)
+        assert torch.equal(a, b), (name, int((a != b).sum()))
+        offset = (offset + size + 127) // 128 * 128
+    assert offset == theirs.numel()
