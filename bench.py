@@ -96,6 +96,10 @@ class ClockSampler:
                                           '--format=csv,noheader,nounits', '-lms', '200'], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # nvidia-smi's first line can take longer than a short timed region: the region starts after it
+            deadline = time.time() + 5.0
+            while not self.lines and self.proc.poll() is None and time.time() < deadline:
+                time.sleep(0.01)
         except (OSError, ValueError):
             self.proc = None
         return self
@@ -106,6 +110,10 @@ class ClockSampler:
 
     def __exit__(self, *exc) -> None:
         if self.proc is not None:
+            # one more sample after the timed region's last work was queued (nvidia-smi samples every 200 ms)
+            seen, deadline = len(self.lines), time.time() + 1.0
+            while len(self.lines) == seen and self.proc.poll() is None and time.time() < deadline:
+                time.sleep(0.01)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
