@@ -224,3 +224,23 @@ def test_nerf_mlp_training_record_and_backward_limits():
     assert lib.zf_nerf_mlp_backward_tc(fake, fake, 56, fake, 96, fake, ctypes.byref(w), fake, 56, ctypes.byref(g), fake, 1 << 62, n, fake,
                                        None) == capi.ZF_ERROR_INVALID_ARGUMENT
     assert b'too many samples' in lib.zf_last_error()
+
+
+def test_nerf_mlp_pack_and_unfold_validate_before_touching_a_device():
+    """The pack and unfold entry points reject missing pointers and a misaligned fp32 bias target before any launch,
+    and the parameter count they assume is the table's of the reference model's widths."""
+    from zipnerf_b200 import capi, nerf_mlp as nm
+    lib = capi.load()
+    assert lib.zf_nerf_mlp_parameter_count() == nm.NerfMlpLayout().size == 227_556
+    fake = 1 << 20
+    targets = capi.zf_nerf_mlp_packed(*([fake] * len(capi.NERF_MLP_PACK_TARGETS)))
+    assert lib.zf_nerf_mlp_pack(None, ctypes.byref(targets), None) == capi.ZF_ERROR_INVALID_ARGUMENT
+    assert lib.zf_nerf_mlp_pack(fake, None, None) == capi.ZF_ERROR_INVALID_ARGUMENT
+    targets.tc_view_1_bias = fake + 2  # fp32 biases need 4-byte alignment
+    assert lib.zf_nerf_mlp_pack(fake, ctypes.byref(targets), None) == capi.ZF_ERROR_INVALID_ARGUMENT
+    assert b'misaligned' in lib.zf_last_error()
+    grads = capi.zf_nerf_mlp_grads(*([fake] * 9))
+    assert lib.zf_nerf_mlp_unfold_grads(fake, ctypes.byref(grads), None, None) == capi.ZF_ERROR_INVALID_ARGUMENT
+    grads.rgb = None
+    assert lib.zf_nerf_mlp_unfold_grads(fake, ctypes.byref(grads), fake, None) == capi.ZF_ERROR_INVALID_ARGUMENT
+    assert b'gradients must be given' in lib.zf_last_error()
