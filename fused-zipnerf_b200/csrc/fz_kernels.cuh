@@ -920,7 +920,9 @@ __device__ __forceinline__ uint64_t add_pair(const uint64_t a, const uint64_t b)
 
 constexpr int kMlpWarps = ZF_MLP_WARPS;
 constexpr int kMlpBlock = 32 * kMlpWarps;
-__host__ __device__ constexpr int mlp_rows_pad(const int width) { return (width + 3) / 4 * 4; }
+// hidden units padded to whole steps of the recomputation (kMlpChains pairs; zero weights and bias beyond the width)
+constexpr int kMlpChains = 4;
+__host__ __device__ constexpr int mlp_rows_pad(const int width) { return (width + 2 * kMlpChains - 1) / (2 * kMlpChains) * (2 * kMlpChains); }
 __host__ __device__ constexpr int mlp_block_floats(const int n_out, const int nout_pad, const int width) {
     return mlp_rows_pad(width) * nout_pad + 2 * mlp_rows_pad(width)                  // weights (w0 rows padded to nout_pad), b0, w1
         + (n_out * (mlp_rows_pad(width) + 1) + 2 * width + 1 + 3) / 4 * 4            // the block's parameter gradient sums
@@ -1012,40 +1014,48 @@ __global__ void __launch_bounds__(kMlpBlock, ZF_MIN_BLOCKS_BACKWARD_MLP) fz_back
             uint64_t gf[NOUT_PAD / 2];  // (grad_f_2k, grad_f_2k+1)
             #pragma unroll
             for (int k = 0; k < NOUT_PAD / 2; k++) gf[k] = pair_of(0.0f, 0.0f);
-            for (int j0 = 0; j0 < w_pad; j0 += 4) {
-                float pre[4];
+            // kMlpChains pairs of hidden units at a time: their recomputations are independent chains, interleaved
+            for (int j0 = 0; j0 < w_pad; j0 += 2 * kMlpChains) {
+                // rows j0 + 2 h and j0 + 2 h + 1 in the forward's accumulation order; the padding columns (zero weight,
+                // zero feature) add +0, which changes at most the sign of a zero and so neither the ReLU mask nor
+                // relu(pre)
+                uint64_t p[kMlpChains];
                 #pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    const int j = j0 + 2 * h;
-                    // rows j and j + 1 in the forward's accumulation order; the padding columns (zero weight, zero
-                    // feature) add +0, which changes at most the sign of a zero and so neither the ReLU mask nor relu(pre)
-                    const float4* wp = reinterpret_cast<const float4*>(s_w0p + (j / 2) * 2 * NOUT_PAD);
-                    uint64_t p = pair_of(s_b0[j], s_b0[j + 1]);
+                for (int h = 0; h < kMlpChains; h++) p[h] = pair_of(s_b0[j0 + 2 * h], s_b0[j0 + 2 * h + 1]);
+                const float4* wp = reinterpret_cast<const float4*>(s_w0p + (j0 / 2) * 2 * NOUT_PAD);
+                #pragma unroll
+                for (int q = 0; q < NOUT_PAD / 2; q++) {
                     #pragma unroll
-                    for (int q = 0; q < NOUT_PAD / 2; q++) {
-                        const float4 w2 = wp[q];  // (w[j][2q], w[j+1][2q], w[j][2q+1], w[j+1][2q+1])
-                        p = fma_pair(pair_of(w2.x, w2.y), ff[2 * q], p);
-                        p = fma_pair(pair_of(w2.z, w2.w), ff[2 * q + 1], p);
-                    }
-                    const float2 pv = split_pair(p);
-                    pre[2 * h] = pv.x;
-                    pre[2 * h + 1] = pv.y;
-                    // branch-free: a zero pre-activation gradient adds +0 (the warp has some positive lane anyway)
-                    #pragma unroll
-                    for (int r = 0; r < 2; r++) {
-                        const float pr = r == 0 ? pv.x : pv.y;
-                        const float grad_pre = pr > 0.0f ? __fmul_rn(g, s_w1[j + r]) : 0.0f;
-                        const uint64_t gp = pair_of(grad_pre, grad_pre);
-                        const float4* w = reinterpret_cast<const float4*>(s_w0 + (j + r) * NOUT_PAD);
-                        #pragma unroll
-                        for (int q = 0; q < NOUT_PAD / 4; q++) {
-                            const float4 wq = w[q];
-                            gf[2 * q] = fma_pair(gp, pair_of(wq.x, wq.y), gf[2 * q]);
-                            gf[2 * q + 1] = fma_pair(gp, pair_of(wq.z, wq.w), gf[2 * q + 1]);
-                        }
+                    for (int h = 0; h < kMlpChains; h++) {
+                        const float4 w2 = wp[h * NOUT_PAD / 2 + q];  // (w[j][2q], w[j+1][2q], w[j][2q+1], w[j+1][2q+1])
+                        p[h] = fma_pair(pair_of(w2.x, w2.y), ff[2 * q], p[h]);
+                        p[h] = fma_pair(pair_of(w2.z, w2.w), ff[2 * q + 1], p[h]);
                     }
                 }
-                *reinterpret_cast<float4*>(s_pre + lane * ps + j0) = make_float4(pre[0], pre[1], pre[2], pre[3]);
+                float pre[2 * kMlpChains];
+                #pragma unroll
+                for (int h = 0; h < kMlpChains; h++) {
+                    const float2 pv = split_pair(p[h]);
+                    pre[2 * h] = pv.x;
+                    pre[2 * h + 1] = pv.y;
+                }
+                // branch-free: a zero pre-activation gradient adds +0 (the warp has some positive lane anyway)
+                #pragma unroll
+                for (int r = 0; r < 2 * kMlpChains; r++) {
+                    const float grad_pre = pre[r] > 0.0f ? __fmul_rn(g, s_w1[j0 + r]) : 0.0f;
+                    const uint64_t gp = pair_of(grad_pre, grad_pre);
+                    const float4* w = reinterpret_cast<const float4*>(s_w0 + (j0 + r) * NOUT_PAD);
+                    #pragma unroll
+                    for (int q = 0; q < NOUT_PAD / 4; q++) {
+                        const float4 wq = w[q];
+                        gf[2 * q] = fma_pair(gp, pair_of(wq.x, wq.y), gf[2 * q]);
+                        gf[2 * q + 1] = fma_pair(gp, pair_of(wq.z, wq.w), gf[2 * q + 1]);
+                    }
+                }
+                #pragma unroll
+                for (int h = 0; h < kMlpChains / 2; h++) {
+                    *reinterpret_cast<float4*>(s_pre + lane * ps + j0 + 4 * h) = make_float4(pre[4 * h], pre[4 * h + 1], pre[4 * h + 2], pre[4 * h + 3]);
+                }
             }
             #pragma unroll
             for (int k = 0; k < NOUT_PAD / 2; k++) {
