@@ -5,7 +5,9 @@ A step is one training iteration's featurization of config 2 (paper shape): the 
 (64 intervals per ray, fused density MLP, fp32 features) and of the NeRF level (32 intervals, packed bf16 features and
 NeRF-input tail), then the NeRF-level backward (bf16 upstream gradients -> fp32/fp16 grid gradients) and the two
 proposal-level backwards (MLP recomputation, grid and MLP parameter gradients), in the order of the reference's
-Renderer.render_rays_training / Trainer.compute_gradients. Inputs are seeded synthetic data of config 2's shapes (the
+Renderer.render_rays_training / Trainer.compute_gradients. The three backwards are independent once their upstream
+gradients exist (disjoint gradient buffers), so the timed steps run them on three streams, as a training step can; the
+per-kernel times and the roofline come from further steps with the calls in sequence. Inputs are seeded synthetic data of config 2's shapes (the
 reference's Mip-NeRF 360 scenes are not available). With --gpus N (one process per GPU, torchrun), every rank
 featurizes its own 65536 rays (weak scaling) and the grid and MLP gradients are all-reduced over NCCL, the
 data-parallel exchange of a training step.
@@ -180,6 +182,8 @@ class Step:
                            'g16': torch.zeros((sum(self.nerf.entries) - split) * F, device=device, dtype=torch.float16)}
         self.samples_per_step = wl.n_intervals_total * N_MULTISAMPLES
         self.kernel_names = ['forward_proposal', 'forward_proposal', 'forward_nerf', 'backward_nerf', 'backward_proposal', 'backward_proposal']
+        # the streams of the concurrent backwards: NeRF level, proposal level 0, proposal level 1
+        self.backward_streams = [torch.cuda.Stream(device=device) for _ in range(3)]
         self.calls_per_step = len(self.kernel_names)
         # kernel launches of the step's calls (level passes of the NeRF grid, two kernels per proposal backward)
         from zipnerf_b200 import capi
@@ -206,10 +210,12 @@ class Step:
             if po is not None:
                 po['grad_raw'] = next(it)
 
-    def run(self, events=None, after_backward=None) -> None:
+    def run(self, events=None, after_backward=None, concurrent: bool = False) -> None:
         """One step; events (list of (start, end) CUDA event pairs per kernel) are recorded if given;
-        after_backward(buffers) is called with each level's gradient buffers once its backward is enqueued (the
-        data-parallel exchange of those buffers starts there)."""
+        after_backward(buffers) is called with each level's gradient buffers once its backward is enqueued, on that
+        backward's stream (the data-parallel exchange of those buffers starts there). concurrent: the three levels'
+        backwards on three streams after the forwards (not with events: those time each call alone)."""
+        assert not (concurrent and events is not None)
         wl, seed, e = self.wl, self.wl.pattern_seed, self.empty
         rays = (wl.origins, wl.directions, wl.radii)
         k = 0
@@ -229,19 +235,28 @@ class Step:
                    wl.encoded_directions, self.nerf_out['inputs'])
         mark(k, 1)
         k += 1
-        mark(k, 0)
-        fn.backward(*rays, nerf.tdist, seed, self.nerf_out['grad'][:, :fn.n_output_features], self.nerf_grads['g32'], self.nerf_grads['g16'])
-        mark(k, 1)
-        k += 1
-        if after_backward is not None:
-            after_backward([self.nerf_grads['g32'], self.nerf_grads['g16']])
-        for lvl, f, po, pg in zip(self.props, self.featurizers, self.prop_out, self.prop_grads):
+        main = torch.cuda.current_stream()
+        if concurrent:
+            for s in self.backward_streams:
+                s.wait_stream(main)
+        with torch.cuda.stream(self.backward_streams[0] if concurrent else main):
             mark(k, 0)
-            f.backward_mlp(*rays, lvl.tdist, seed, po['features'], po['grad_raw'], *lvl.mlp[:3], pg['table'], pg['w0'], pg['b0'], pg['w1'], pg['b1'])
+            fn.backward(*rays, nerf.tdist, seed, self.nerf_out['grad'][:, :fn.n_output_features], self.nerf_grads['g32'], self.nerf_grads['g16'])
             mark(k, 1)
             k += 1
             if after_backward is not None:
-                after_backward([pg['table'], pg['w0'], pg['b0'], pg['w1'], pg['b1']])
+                after_backward([self.nerf_grads['g32'], self.nerf_grads['g16']])
+        for s, lvl, f, po, pg in zip(self.backward_streams[1:], self.props, self.featurizers, self.prop_out, self.prop_grads):
+            with torch.cuda.stream(s if concurrent else main):
+                mark(k, 0)
+                f.backward_mlp(*rays, lvl.tdist, seed, po['features'], po['grad_raw'], *lvl.mlp[:3], pg['table'], pg['w0'], pg['b0'], pg['w1'], pg['b1'])
+                mark(k, 1)
+                k += 1
+                if after_backward is not None:
+                    after_backward([pg['table'], pg['w0'], pg['b0'], pg['w1'], pg['b1']])
+        if concurrent:
+            for s in self.backward_streams:
+                main.wait_stream(s)
 
     def kernel_bytes(self) -> list:
         out = []
@@ -514,7 +529,9 @@ def bench_config(args, world: int, samples_per_step: int) -> dict:
                         'table 2^21, 16->512, fused MLP 64) and the NeRF level (10x4 features, table 2^21, 16->8192)',
             'rays_per_gpu': args.rays, 'samples_per_step_per_gpu': samples_per_step,
             'parallelism': f'dp{world} (rays sharded, gradients all-reduced)' if world > 1 else 'single GPU',
-            'l2': 'inputs larger than L2 (step working set ~1.8 GB > 126 MB)'}
+            'l2': 'inputs larger than L2 (step working set ~1.8 GB > 126 MB)',
+            'schedule': 'forwards in sequence; the three backwards on three streams (independent given their upstream gradients); '
+                        'per-kernel times from steps with every call in sequence'}
 
 
 def run_reference_arm(args) -> None:
@@ -558,7 +575,7 @@ def run_b200(args) -> None:
         # levels' backwards run (every rank issues the same collectives in the same order)
         if world > 1:
             from zipnerf_b200 import sharding
-            comm.wait_stream(torch.cuda.current_stream())
+            comm.wait_stream(torch.cuda.current_stream())  # the stream of the level's backward
             with torch.cuda.stream(comm):
                 sharding.allreduce_gradients(buffers, half_wire=args.half_wire)
 
@@ -580,7 +597,7 @@ def run_b200(args) -> None:
         torch.cuda.synchronize()
 
     for _ in range(args.warmup):
-        step.run(after_backward=start_exchange)
+        step.run(after_backward=start_exchange, concurrent=True)
         exchange()
     barrier()
     n_k = step.calls_per_step
@@ -592,10 +609,14 @@ def run_b200(args) -> None:
         barrier()
         start.record()
         for i in range(args.steps):
-            step.run(events[i], after_backward=start_exchange)
+            step.run(after_backward=start_exchange, concurrent=True)
             exchange()
         end.record()
         barrier()
+    # the per-kernel times: the same steps with the calls in sequence (no exchange), each call between events
+    for i in range(args.steps):
+        step.run(events[i])
+    barrier()
     elapsed_ms = start.elapsed_time(end)
     if world > 1:
         t = torch.tensor([elapsed_ms], device=device)
@@ -966,7 +987,7 @@ def measure_e2e(step: Step, args, world: int, start_exchange, exchange, barrier)
             k = i % 2
             compute.wait_event(copied[k])
             step.set_inputs(device_sets[k])
-            step.run(after_backward=start_exchange)
+            step.run(after_backward=start_exchange, concurrent=True)
             exchange()
             result_host.copy_(torch.cat(result_dev), non_blocking=True)
             released[k].record(compute)

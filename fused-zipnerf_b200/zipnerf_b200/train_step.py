@@ -12,9 +12,12 @@ intervals per ray, the view-direction encoding of degree 4; the trainer's loss w
 (Trainer.py:17-57). Data: a synthetic pool of 185 views of 1296 x 840 pixels (uniform-noise colors).
 
 The NeRF MLP is this backend's `NerfMlp` with the reference's interface and parameter layout (nerf_mlp.cu:440-620):
-`pack` every step, the forward on the tcgen05 kernel (zf_nerf_mlp_forward_tc, keeping v0-v2 for the backward), the
-backward as the folded chain's bf16 GEMMs (cuBLAS through torch) with this backend's ReLU backward and bias gradient
-and the unfold of the packed-weight gradients into the fp32 parameters.
+`pack` every step (one kernel launch), the forward on the tcgen05 kernel keeping the training record (v0-v2 and one
+ReLU-mask bit per column), the backward on the tcgen05 data-gradient and weight-gradient kernels, and the unfold of the
+packed-weight gradients into the fp32 parameters (one kernel launch).
+
+The two proposal levels' backwards run on their own streams beside the NeRF grid's backward: all three are independent
+once the NeRF MLP's backward has run.
 """
 from __future__ import annotations
 
@@ -125,6 +128,9 @@ class TrainStep:
         self.grad_buffers = grads
         self.optimizer = backend.Adam(params, grads, [1.0, 1.0, scale, scale, 1.0, 1.0], offsets, LOSS['grid_regularization'], backend.grid_max_value,
                                       ADAM['beta1'], ADAM['beta2'], ADAM['eps'], self.magnitudes)
+        # the proposal levels' backwards run on their own streams beside the NeRF grid's backward (their inputs are final
+        # once the final level's kernel has run, and their gradient buffers are disjoint from the NeRF level's)
+        self.backward_streams = [torch.cuda.Stream(device=device) for _ in range(2)]
         self.pool = rows.ray_pool(device, n_views=pool_views)
         self.warp = rows.ray_warp(NEAR, FAR)
         self.loss_sums = None
@@ -137,11 +143,13 @@ class TrainStep:
         b1 = buffer[a + 64 * n_out + 128:a + 64 * n_out + 129]
         return w0, b0, w1, b1
 
-    def run(self, iteration: int, lr: float | None = None, anneal: float | None = None, after_backward=None, exchange=None) -> None:
+    def run(self, iteration: int, lr: float | None = None, anneal: float | None = None, after_backward=None, exchange=None,
+            concurrent: bool = True) -> None:
         """One training iteration (learning rate and resampling anneal from the trainer's schedules unless given).
         after_backward(buffers) is called with each group of gradient buffers as soon as they are final (the NeRF grid,
-        then each proposal level with the MLP buffers last); exchange() is called before the optimizer step (the
-        data-parallel average must have finished)."""
+        then each proposal level with the MLP buffers last), on the stream of the backward that wrote them; exchange() is
+        called before the optimizer step (the data-parallel average must have finished). concurrent=False runs the
+        proposal levels' backwards on this stream after the NeRF grid's."""
         if lr is None:
             lr = learning_rate(iteration)
         if anneal is None:  # schlick_bias(iteration / NUM_ITERATIONS, ANNEAL_SLOPE) (utils.py:30-32, Trainer.py:135-136)
@@ -179,16 +187,26 @@ class TrainStep:
             [q['weights'] for q in proposals], directions, seed, rgb, LOSS['charbonnier_padding'], [LOSS['interlevel']] * 2, list(LOSS['blurs']),
             LOSS['distortion'], LOSS['distortion_power'], LOSS['distortion_premult'], True)
         grad_features = self.nerf_mlp.backward(grad_outputs.view(R * n, 8), features, packed, context, self.nerf_params, self.nerf_grads)
+        # the NeRF grid's backward on this stream, the proposal levels' beside it on theirs (they start after the NeRF
+        # MLP's tensor-core kernels, which hold whole SMs); this stream waits for them before the exchange and Adam, so
+        # the step's temporaries are not reused early
+        main = torch.cuda.current_stream()
+        streams = self.backward_streams if concurrent else [main, main]
+        for s in streams:
+            s.wait_stream(main)
         nerf.featurizer.backward(origins, directions, radii, tdist, seed, grad_features, nerf.grad, nerf.grad_half)
         if after_backward is not None:
             after_backward([nerf.grad, nerf.grad_half, self.nerf_grads])
-        for level in range(2):
+        for level, s in enumerate(streams):
             lv, q = self.levels[level], proposals[level]
             gw0, gb0, gw1, gb1 = self.proposal_mlp(self.prop_grads, level)
-            lv.featurizer.backward_mlp(origins, directions, radii, q['tdist'], seed, q['features'], proposal_grads[level],
-                                       *self.proposal_mlp(self.prop_params, level)[:3], lv.grad, gw0, gb0, gw1.view(-1), gb1)
-            if after_backward is not None:
-                after_backward([lv.grad] + ([self.prop_grads] if level == 1 else []))
+            with torch.cuda.stream(s):
+                lv.featurizer.backward_mlp(origins, directions, radii, q['tdist'], seed, q['features'], proposal_grads[level],
+                                           *self.proposal_mlp(self.prop_params, level)[:3], lv.grad, gw0, gb0, gw1.view(-1), gb1)
+                if after_backward is not None:
+                    after_backward([lv.grad] + ([self.prop_grads] if level == 1 else []))
+        for s in streams:
+            main.wait_stream(s)
         if exchange is not None:
             exchange()
         self.optimizer.step(lr)

@@ -35,6 +35,23 @@ def test_training_steps_run_and_update_the_model(cuda_device):
     assert all(0.0 < float(l[0]) < 2.0 for l in losses)
 
 
+def test_concurrent_backwards_train_like_the_sequential_step(cuda_device):
+    """The proposal levels' backwards on their own streams beside the NeRF grid's backward give the model of the
+    sequential step: two models from the same initial state, trained three steps each way, have the same losses up to
+    the gradient atomics' summation order (a backward that read a buffer before it was written would show here)."""
+    from zipnerf_b200 import train_step
+    losses = []
+    for concurrent in (True, False):
+        step = train_step.TrainStep(cuda_device, n_rays=4096, pool_views=3)
+        out = []
+        for iteration in range(3):
+            step.run(iteration, concurrent=concurrent)
+            out.append(step.loss_sums.clone())
+        torch.cuda.synchronize()
+        losses.append(torch.stack(out).double())
+    torch.testing.assert_close(losses[0], losses[1], rtol=1e-3, atol=1e-7)
+
+
 @pytest.mark.parametrize('cols,act_cols', [(256, 256), (64, 96), (8, 8), (24, 24)])
 def test_relu_backward_matches_torch(cuda_device, cols, act_cols):
     """The masked gradient equals PyTorch's grad * (act > 0) exactly (NaN activations mask); the bias gradient (fp32
