@@ -613,7 +613,12 @@ def run_b200(args) -> None:
             exchange()
         end.record()
         barrier()
-    # the per-kernel times: the same steps with the calls in sequence (no exchange), each call between events
+    # the per-kernel times: the same steps with the calls in sequence (no exchange), each call between events, after
+    # warm-up steps in sequence (the proposal backwards' workspaces come from the caching allocator, whose blocks
+    # belong to the stream they were first used on)
+    for _ in range(args.warmup):
+        step.run()
+    barrier()
     for i in range(args.steps):
         step.run(events[i])
     barrier()
