@@ -587,7 +587,29 @@ __global__ void __launch_bounds__(kBlock, cooperative_forward(F) ? ZF_MIN_BLOCKS
             }
             float raw = __ldg(a.b1);
             if (a.w0_vectors) {
-                for (int j = 0; j < a.mlp_width; j++) {
+                // two hidden units at a time: independent chains in the reference's input order, added to raw in unit
+                // order
+                int j = 0;
+                for (; j + 1 < a.mlp_width; j += 2) {
+                    float pre0 = __ldg(a.b0 + j), pre1 = __ldg(a.b0 + j + 1);
+                    const float4* w = reinterpret_cast<const float4*>(a.w0 + j * n_out);
+                    const float4* v = reinterpret_cast<const float4*>(a.w0 + (j + 1) * n_out);
+                    #pragma unroll
+                    for (int q = 0; q < NOUT_PAD / 4; q++) {
+                        const float4 wq = __ldg(w + q), vq = __ldg(v + q);
+                        pre0 = __fmaf_rn(wq.x, f[4 * q], pre0);
+                        pre1 = __fmaf_rn(vq.x, f[4 * q], pre1);
+                        pre0 = __fmaf_rn(wq.y, f[4 * q + 1], pre0);
+                        pre1 = __fmaf_rn(vq.y, f[4 * q + 1], pre1);
+                        pre0 = __fmaf_rn(wq.z, f[4 * q + 2], pre0);
+                        pre1 = __fmaf_rn(vq.z, f[4 * q + 2], pre1);
+                        pre0 = __fmaf_rn(wq.w, f[4 * q + 3], pre0);
+                        pre1 = __fmaf_rn(vq.w, f[4 * q + 3], pre1);
+                    }
+                    raw = __fmaf_rn(__ldg(a.w1 + j), fmaxf(pre0, 0.0f), raw);
+                    raw = __fmaf_rn(__ldg(a.w1 + j + 1), fmaxf(pre1, 0.0f), raw);
+                }
+                for (; j < a.mlp_width; j++) {
                     float pre = __ldg(a.b0 + j);
                     const float4* w = reinterpret_cast<const float4*>(a.w0 + j * n_out);
                     #pragma unroll
